@@ -1,0 +1,177 @@
+"""Generate the golden fixtures in this directory from the unmodified reference.
+
+Run where the reference tree is mounted (``FSCTEP_REFERENCE_ROOT``, default the
+container's read-only mount); the outputs are committed and the tests read only
+them, so nothing at test time needs the reference.
+
+    python tests/golden/make_golden.py
+
+Fixtures:
+
+* ``ictd_tables.npz`` -- harmonic bases, normalised CG tensors, packed U_g per
+  (l1,l2) group, direction projectors and product_5 factors for lmax 2 and 3,
+  taken from the reference's own functions (``models/ictd_irreps.py``).
+* ``ictd_model_{a,b}.npz`` -- seeded inputs, a seed-perturbed state_dict (fresh
+  models output E = 0, ``mlp.py:126-127``) and the reference's per-graph energy,
+  forces and stress (float64, and float32 for the tolerance budget), computed with
+  ``PureCartesianICTDTransformerLayer`` (``pure_cartesian_ictd_layers_full.py``)
+  and the calculator/trainer conventions (F = -dE/dpos, sigma = (1/V) dE/d eps).
+* ``tp_ops.npz`` -- the ``_C_ictd_tp`` operator family evaluated by the reference's
+  einsum references (``models/ictd_irreps_cuda.py:169-311``) on the shapes of
+  ``test/test_ictd_tp_backend.py``.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+import ref_shims  # noqa: E402
+
+ref_shims.install()
+sys.path.insert(0, ref_shims.REPO_ROOT)
+
+from fsctep_b200 import systems  # noqa: E402
+from fsctep_b200.weights import seeded_state_dict  # noqa: E402
+from oracle import neighbors  # noqa: E402
+
+
+def tables():
+    from molecular_force_field.models import ictd_irreps as R
+
+    out = {}
+    for L in range(0, 5):
+        out[f"basis_{L}"] = R._harmonic_basis_cpu_f64(L).numpy()
+    for lmax in (2, 3):
+        tp = R.HarmonicFullyConnectedTensorProduct(4, 1, 4, lmax, internal_compute_dtype=torch.float64)
+        cg = tp._get_cg_list(torch.device("cpu"), torch.float64)
+        for p, (l1, l2, l3) in enumerate(tp.paths):
+            out[f"L{lmax}_cg_{l1}{l2}{l3}"] = cg[p].numpy()
+        U = tp._get_proj_group_list(torch.device("cpu"), torch.float64)
+        for g, u in zip(tp._groups, U):
+            out[f"L{lmax}_U_{g['l1']}{g['l2']}"] = u.numpy()
+        out[f"L{lmax}_paths"] = np.array(tp.paths, dtype=np.int64)
+        ew = R.HarmonicElementwiseProduct(lmax=lmax, mul=4, irreps_out="0e")
+        out[f"L{lmax}_p5_factors"] = np.array(ew._0e_factors, dtype=np.float64)
+    for l in range(0, 5):
+        out[f"dirproj_{l}"] = R._dir_proj_cpu_f64(l).numpy()
+    g = torch.Generator().manual_seed(7)
+    n = torch.randn(64, 3, generator=g, dtype=torch.float64)
+    n = n / n.norm(dim=1, keepdim=True)
+    out["dir_n"] = n.numpy()
+    for l in range(0, 5):
+        out[f"dir_Y_{l}"] = R.direction_harmonics_fast(n, l).numpy()
+    np.savez_compressed(os.path.join(HERE, "ictd_tables.npz"), **out)
+
+
+def _perturb(model, seed):
+    """Overwrite every parameter from ``fsctep_b200.weights.seeded_state_dict``; the
+    tests rebuild the same tensors from the seed, so only a checksum is stored."""
+    shapes = {k: tuple(v.shape) for k, v in model.state_dict().items()}
+    sd = seeded_state_dict(shapes, seed, torch.float64)
+    model.load_state_dict(sd)
+    return shapes
+
+
+def _ref_efs(model, pos, Z, batch, src, dst, shifts, cell, dtype):
+    model = model.to(dtype)
+    pos = torch.tensor(pos, dtype=dtype, requires_grad=True)
+    cell_t = torch.tensor(cell, dtype=dtype)
+    b = torch.tensor(batch)
+    nb = cell_t.shape[0]
+    strain = torch.zeros(nb, 3, 3, dtype=dtype, requires_grad=True)
+    D = torch.eye(3, dtype=dtype) + 0.5 * (strain + strain.transpose(-1, -2))
+    pos_in = torch.einsum("ni,nij->nj", pos, D[b])
+    cell_in = torch.bmm(cell_t, D)
+    e = model(pos_in, torch.tensor(Z), b, torch.tensor(src), torch.tensor(dst),
+              torch.tensor(shifts, dtype=dtype), cell_in)
+    Eg = torch.zeros(nb, dtype=dtype).index_add(0, b, e.squeeze(-1))
+    gp, gs = torch.autograd.grad(Eg.sum(), [pos, strain])
+    vol = torch.abs(torch.det(cell_t))
+    return {"energy": Eg.detach().numpy(), "forces": (-gp).numpy(),
+            "stress": (gs / vol.view(-1, 1, 1)).numpy(), "atom_energy": e.detach().squeeze(-1).numpy()}
+
+
+def model_case(tag, system, cfg, seed):
+    from molecular_force_field.models.pure_cartesian_ictd_layers_full import PureCartesianICTDTransformerLayer
+
+    torch.set_default_dtype(torch.float64)
+    model = PureCartesianICTDTransformerLayer(
+        max_embed_radius=cfg["max_radius"], main_max_radius=cfg["max_radius"],
+        main_number_of_basis=cfg["number_of_basis"], hidden_dim_conv=cfg["channels"], hidden_dim_sh=32,
+        hidden_dim=64, lmax=cfg["lmax"], num_interaction=cfg["num_interaction"],
+        function_type_main=cfg["function_type"], max_atomvalue=cfg["max_atomvalue"],
+        internal_compute_dtype=torch.float64, device=torch.device("cpu"))
+    shapes = _perturb(model, seed)
+    src, dst, S = neighbors.batched_neighbor_list(system["pos"], system["batch"], system["cell"],
+                                                  cfg["max_radius"], system["pbc"])
+    args = (system["pos"], system["Z"], system["batch"], src, dst, S.astype(np.float64), system["cell"])
+    r64 = _ref_efs(model, *args, torch.float64)
+    sd64 = {k: v.detach().clone() for k, v in model.state_dict().items()}
+    model.internal_compute_dtype = torch.float32
+    for mod in model.modules():
+        if hasattr(mod, "internal_compute_dtype"):
+            mod.internal_compute_dtype = torch.float32
+    torch.set_default_dtype(torch.float32)
+    r32 = _ref_efs(model, *args, torch.float32)
+    torch.set_default_dtype(torch.float64)
+    out = {"pos": system["pos"], "Z": system["Z"], "batch": system["batch"], "cell": system["cell"],
+           "pbc": np.array(system["pbc"]), "edge_src": src.astype(np.int32), "edge_dst": dst.astype(np.int32),
+           "edge_shifts": S.astype(np.int8)}
+    for k, v in cfg.items():
+        out[f"cfg_{k}"] = np.array(v)
+    out["sd_seed"] = np.array(seed)
+    for k, v in sd64.items():
+        out[f"sdshape/{k}"] = np.array(shapes[k], dtype=np.int64)
+        out[f"sdsum/{k}"] = np.array(float(v.double().sum()))
+    for k, v in r64.items():
+        out[f"ref64_{k}"] = v
+    for k, v in r32.items():
+        out[f"ref32_{k}"] = v
+    np.savez_compressed(os.path.join(HERE, f"ictd_model_{tag}.npz"), **out)
+    print(tag, "atoms", system["pos"].shape[0], "edges", src.shape[0], "E", r64["energy"],
+          "max|dE| fp32", np.abs(r64["energy"] - r32["energy"]).max(),
+          "max|dF| fp32", np.abs(r64["forces"] - r32["forces"]).max(), "max|F|", np.abs(r64["forces"]).max())
+
+
+def tp_ops():
+    from molecular_force_field.models import ictd_irreps_cuda as RC
+
+    out = {}
+    g = torch.Generator().manual_seed(100)
+    B, I, m1, m2, P, K, O = 4, 3, 3, 3, 2, 3, 4
+    a = torch.randn(B, I, m1, generator=g, dtype=torch.float64)
+    b = torch.randn(B, 1, m2, generator=g, dtype=torch.float64)
+    U = torch.randn(m1 * m2, P * K, generator=g, dtype=torch.float64)
+    w = torch.randn(P, O, I, generator=g, dtype=torch.float64)
+    gates = torch.randn(B, P, generator=g, dtype=torch.float64)
+    y = RC._project_forward_reference(a, b, U, P)
+    gy = torch.randn(y.shape, generator=g, dtype=torch.float64)
+    ga, gb, gu = RC._project_transpose_reference(gy, a, b, U, need_a=True, need_b=True, need_u=True)
+    mo, _ = RC._mix_forward_reference(y, w, gates)
+    go = torch.randn(mo.shape, generator=g, dtype=torch.float64)
+    my, mw, mg = RC._mix_transpose_reference(go, y, w, gates, need_y=True, need_w=True, need_g=True)
+    for k, v in dict(a=a, b=b, U=U, w=w, gates=gates, y=y, gy=gy, ga=ga, gb=gb, gu=gu, mo=mo, go=go,
+                     my=my, mw=mw, mg=mg).items():
+        out[k] = v.numpy()
+    np.savez_compressed(os.path.join(HERE, "tp_ops.npz"), **out)
+
+
+def main():
+    tables()
+    tp_ops()
+    cfg_a = dict(channels=32, lmax=2, num_interaction=2, number_of_basis=8, max_radius=5.0,
+                 function_type="bessel", max_atomvalue=10)
+    model_case("a", systems.random_frames(n_frames=2, n_atoms=96, box=10.0, seed=11), cfg_a, seed=1)
+    cfg_b = dict(channels=16, lmax=2, num_interaction=3, number_of_basis=8, max_radius=5.0,
+                 function_type="gaussian", max_atomvalue=16)
+    model_case("b", systems.diamond_crystal(n_cells=(2, 2, 2), seed=12), cfg_b, seed=2)
+
+
+if __name__ == "__main__":
+    main()
