@@ -1,0 +1,458 @@
+// pure-cartesian-ictd energy + forces: forward of PureCartesianICTDTransformerLayer
+// (pure_cartesian_ictd_layers_full.py:867-1078) and a hand-written reverse pass that yields
+// dE/dr per edge, forces and the virial without autograd replay.  All buffers come from the
+// caller's workspace; nothing is allocated here.
+#include <algorithm>
+#include <cmath>
+#include <vector>
+
+#include "common.cuh"
+#include "ictd_paths.cuh"
+#include "kernels.cuh"
+
+namespace fsc {
+
+using namespace ictd2;
+
+namespace {
+
+constexpr int64_t kGramChunk = 16384;  // nodes per readout chunk
+constexpr int64_t kMaxGraphs = 4096;   // graphs per call (float64 accumulators in the workspace)
+
+struct Plan {
+  int C, nint, S, nC, D0, nb;
+  int64_t N, E, B, npairs, chunk;
+  int hidden[4];
+  int n_hidden;
+  // workspace
+  int32_t* dst;
+  float* edge_y;
+  float* gates;
+  float* feats[8];
+  float* zbuf;
+  float* scalars;
+  float* p5;
+  float* x0;
+  float* act_pre[4];
+  float* act_post[4];
+  double* energy_d;
+  float* grads[8];
+  float* dscalars;
+  float* dp5;
+  float* dxa;
+  float* dxb;
+  float* dgates;
+  float* dY;
+  float* edge_grad;
+  double* virial_d;
+  double* cellg_d;
+  float* chunkbuf;
+};
+
+int validate(const fsc_ictd_config* cfg) {
+  FSC_REQUIRE(cfg != nullptr, "config is null");
+  if (cfg->lmax != 2) return fail(FSC_ERR_UNSUPPORTED, "ictd engine supports lmax = 2 only");
+  if (cfg->channels != 32 && cfg->channels != 64)
+    return fail(FSC_ERR_UNSUPPORTED, "ictd engine supports channels 32 or 64");
+  if (cfg->num_interaction < 2 || cfg->num_interaction > 8)
+    return fail(FSC_ERR_UNSUPPORTED, "num_interaction must be in [2, 8]");
+  if (cfg->number_of_basis < 1 || cfg->number_of_basis > 16)
+    return fail(FSC_ERR_UNSUPPORTED, "number_of_basis must be in [1, 16]");
+  if (cfg->basis_kind != 0 && cfg->basis_kind != 1)
+    return fail(FSC_ERR_UNSUPPORTED, "radial basis must be gaussian (0) or bessel (1)");
+  if (cfg->output_size != 8) return fail(FSC_ERR_UNSUPPORTED, "output_size must be 8");
+  if (cfg->n_hidden < 1 || cfg->n_hidden > 4) return fail(FSC_ERR_UNSUPPORTED, "MainNet needs 1..4 hidden layers");
+  for (int k = 0; k < cfg->n_hidden; ++k)
+    if (cfg->hidden[k] < 1 || cfg->hidden[k] > 1024) return fail(FSC_ERR_UNSUPPORTED, "MainNet hidden size out of range");
+  if (cfg->invariant_channels < 1) return fail(FSC_ERR_ARGUMENT, "invariant_channels must be >= 1");
+  return FSC_OK;
+}
+
+void layout(Plan& p, Arena& ar, const fsc_ictd_config* cfg, int64_t N, int64_t E) {
+  p.C = cfg->channels;
+  p.nint = cfg->num_interaction;
+  p.S = (p.nint - 1) * cfg->invariant_channels;
+  p.nC = p.C * p.nint;
+  p.D0 = 3 * p.nC + p.S;
+  p.nb = cfg->number_of_basis;
+  p.N = N;
+  p.E = E;
+  p.npairs = (int64_t)p.nC * (p.nC + 1) / 2;
+  p.chunk = std::max<int64_t>(1, std::min<int64_t>(N, kGramChunk));
+  p.n_hidden = cfg->n_hidden;
+  for (int k = 0; k < 4; ++k) p.hidden[k] = k < cfg->n_hidden ? cfg->hidden[k] : 0;
+  int maxw = p.D0;
+  for (int k = 0; k < p.n_hidden; ++k) maxw = std::max(maxw, p.hidden[k]);
+  const int64_t fsz = N * NK * p.C;
+  p.dst = ar.take<int32_t>(E);
+  p.edge_y = ar.take<float>(E * 12);
+  p.gates = ar.take<float>((int64_t)p.nint * E * 12);
+  for (int k = 0; k < p.nint; ++k) p.feats[k] = ar.take<float>(fsz);
+  p.zbuf = ar.take<float>(N * NZ * p.C);
+  p.scalars = ar.take<float>(N * p.S);
+  p.p5 = ar.take<float>(N * p.D0);
+  p.x0 = ar.take<float>(N * p.D0);
+  for (int k = 0; k < p.n_hidden; ++k) {
+    p.act_pre[k] = ar.take<float>(N * p.hidden[k]);
+    p.act_post[k] = ar.take<float>(N * p.hidden[k]);
+  }
+  p.energy_d = ar.take<double>(kMaxGraphs * 19);
+  p.virial_d = p.energy_d ? p.energy_d + kMaxGraphs : nullptr;
+  p.cellg_d = p.energy_d ? p.energy_d + 10 * kMaxGraphs : nullptr;
+  for (int k = 0; k < p.nint; ++k) p.grads[k] = ar.take<float>(fsz);
+  p.dscalars = ar.take<float>(N * p.S);
+  p.dp5 = ar.take<float>(N * p.D0);
+  p.dxa = ar.take<float>(N * maxw);
+  p.dxb = ar.take<float>(N * maxw);
+  p.dgates = ar.take<float>((int64_t)p.nint * E * 12);
+  p.dY = ar.take<float>(E * 12);
+  p.edge_grad = ar.take<float>(E * 3);
+  p.chunkbuf = ar.take<float>(p.chunk * std::max<int64_t>(p.npairs, (int64_t)p.nC * p.nC));
+}
+
+GemmArgs gemm(const float* A, int64_t a_gs, int64_t a_rs, const float* B, int64_t ldb, int b_trans, float* C,
+              int64_t c_gs, int64_t c_rs, int64_t G, int R, int K, int N) {
+  GemmArgs g{};
+  g.A = A; g.a_gs = a_gs; g.a_rs = a_rs;
+  g.B = B; g.ldb = ldb; g.b_trans = b_trans;
+  g.C = C; g.c_gs = c_gs; g.c_rs = c_rs;
+  g.G = G; g.R = R; g.K = K; g.N = N;
+  return g;
+}
+
+__global__ void finalize_kernel(const double* __restrict__ e, const double* __restrict__ v, int64_t B, float* energy,
+                                float* virial) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < B && energy) energy[i] = (float)e[i];
+  if (i < 9 * B && virial) virial[i] = (float)v[i];
+}
+
+struct Ctx {
+  const fsc_ictd_config* cfg;
+  const fsc_ictd_weights* w;
+  const fsc_graph* g;
+  Plan p;
+  cudaStream_t st;
+};
+
+ConvArgs conv_args(const Ctx& c, int layer) {
+  ConvArgs a{};
+  a.N = c.p.N;
+  a.E = c.p.E;
+  a.C = c.p.C;
+  a.row_ptr = c.g->row_ptr;
+  a.src = c.g->src;
+  a.dst = c.p.dst;
+  a.tr_ptr = c.g->tr_ptr;
+  a.tr_eid = c.g->tr_eid;
+  a.species = c.g->species;
+  a.tables = c.w->tables;
+  a.edge_y = c.p.edge_y;
+  a.gates = c.p.gates + (int64_t)layer * c.p.E * 12;
+  return a;
+}
+
+ReadoutArgs readout_args(const Ctx& c) {
+  ReadoutArgs r{};
+  r.N = c.p.N;
+  r.C = c.p.C;
+  r.nint = c.p.nint;
+  r.S = c.p.S;
+  for (int k = 0; k < c.p.nint; ++k) r.feats[k] = c.p.feats[k];
+  r.tables = c.w->tables;
+  r.xmap = c.w->xmap;
+  return r;
+}
+
+RadialW radial(const fsc_ictd_weights* w) {
+  return RadialW{w->rad_w1, w->rad_b1, w->rad_w2, w->rad_b2, w->rad_w3, w->rad_b3};
+}
+
+int forward(Ctx& c) {
+  Plan& p = c.p;
+  const fsc_graph* g = c.g;
+  const fsc_ictd_weights* w = c.w;
+  cudaStream_t st = c.st;
+  const int C = p.C;
+  FSC_TRY(launch_edge_dst(g->row_ptr, p.dst, p.N, st));
+  EdgeFwdArgs ef{};
+  ef.E = p.E; ef.pos = g->pos; ef.src = g->src; ef.dst = p.dst; ef.batch = g->batch; ef.cell = g->cell;
+  ef.shift = g->shift; ef.tables = w->tables; ef.rad = radial(w); ef.nint = p.nint; ef.nb = p.nb;
+  ef.basis_kind = c.cfg->basis_kind; ef.rc = c.cfg->max_radius; ef.edge_y = p.edge_y; ef.gates = p.gates;
+  FSC_TRY(launch_edge_forward(ef, st));
+  FSC_TRY(launch_conv1_forward(conv_args(c, 0), w->ai, w->vsp, p.feats[0], st));
+  for (int k = 1; k < p.nint; ++k) {
+    FSC_TRY(launch_conv2_z(conv_args(c, k), p.feats[k - 1], p.zbuf, st));
+    const float* W = w->mix_fwd + (int64_t)(k - 1) * NP * C * C;
+    int64_t boff = 0;
+    for (int l3 = 0; l3 < 3; ++l3) {
+      GemmArgs ga = gemm(p.zbuf + OFF3(l3) * C, NZ * C, NP3(l3) * C, W + boff, C, 0, p.feats[k] + KB(l3) * C,
+                         NK * C, C, p.N, 2 * l3 + 1, NP3(l3) * C, C);
+      ga.deg_rowptr = g->row_ptr;
+      FSC_TRY(launch_gemm(ga, st));
+      boff += (int64_t)NP3(l3) * C * C;
+    }
+  }
+  // readout scalars: packed Gram x symmetrised W_read
+  ReadoutArgs ra = readout_args(c);
+  FSC_TRY(cudaMemsetAsync(p.scalars, 0, sizeof(float) * p.N * p.S, st) == cudaSuccess ? FSC_OK
+                                                                                         : fail(FSC_ERR_CUDA, "memset"));
+  for (int l = 0; l < 3; ++l) {
+    const float* Wp = w->wread_p + (int64_t)l * p.S * p.npairs;
+    for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
+      const int64_t nn = std::min(p.chunk, p.N - n0);
+      FSC_TRY(launch_gram_pack(ra, l, n0, nn, w->pairs, p.npairs, p.chunkbuf, st));
+      GemmArgs ga = gemm(p.chunkbuf, p.npairs, 0, Wp, p.npairs, 1, p.scalars + n0 * p.S, p.S, 0, nn, 1,
+                         (int)p.npairs, p.S);
+      ga.accumulate = 1;
+      FSC_TRY(launch_gemm(ga, st));
+    }
+  }
+  FSC_TRY(launch_p5_forward(ra, p.scalars, p.p5, st));
+  FSC_TRY(launch_layernorm(p.p5, p.N, p.D0, w->mn_in_g, w->mn_in_b, 0, p.x0, st));
+  const float* xin = p.x0;
+  int din = p.D0;
+  for (int k = 0; k < p.n_hidden; ++k) {
+    GemmArgs ga = gemm(xin, din, 0, w->mn_w[k], din, 1, p.act_pre[k], p.hidden[k], 0, p.N, 1, din, p.hidden[k]);
+    ga.bias = w->mn_b[k];
+    FSC_TRY(launch_gemm(ga, st));
+    FSC_TRY(launch_layernorm(p.act_pre[k], p.N, p.hidden[k], w->mn_g[k], w->mn_beta[k], 1, p.act_post[k], st));
+    xin = p.act_post[k];
+    din = p.hidden[k];
+  }
+  return FSC_OK;
+}
+
+int backward(Ctx& c) {
+  Plan& p = c.p;
+  const fsc_graph* g = c.g;
+  const fsc_ictd_weights* w = c.w;
+  cudaStream_t st = c.st;
+  const int C = p.C;
+  const int H = p.hidden[p.n_hidden - 1];
+  FSC_TRY(launch_energy_seed(p.N, H, w->out_v, g->energy_weight, g->num_local, p.dxa, st));
+  float* dcur = p.dxa;
+  float* dnext = p.dxb;
+  for (int k = p.n_hidden - 1; k >= 0; --k) {
+    const int din = k == 0 ? p.D0 : p.hidden[k - 1];
+    // da_k = LN_bwd(a_k, dx_{k+1}) into dnext, then dx_k = da_k @ W_k into dcur
+    FSC_TRY(launch_layernorm_backward(p.act_pre[k], dcur, p.N, p.hidden[k], w->mn_g[k], w->mn_beta[k], 1, dnext, st));
+    GemmArgs ga = gemm(dnext, p.hidden[k], 0, w->mn_w[k], din, 0, dcur, din, 0, p.N, 1, p.hidden[k], din);
+    FSC_TRY(launch_gemm(ga, st));
+  }
+  FSC_TRY(launch_layernorm_backward(p.p5, dcur, p.N, p.D0, w->mn_in_g, w->mn_in_b, 0, p.dp5, st));
+  ReadoutArgs ra = readout_args(c);
+  FSC_TRY(launch_p5_backward(ra, p.scalars, p.dp5, p.grads, p.dscalars, st));
+  for (int l = 0; l < 3; ++l) {
+    const float* Ws = w->wread_s + (int64_t)l * p.S * p.nC * p.nC;
+    for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
+      const int64_t nn = std::min(p.chunk, p.N - n0);
+      GemmArgs ga = gemm(p.dscalars + n0 * p.S, p.S, 0, Ws, (int64_t)p.nC * p.nC, 0, p.chunkbuf,
+                         (int64_t)p.nC * p.nC, 0, nn, 1, p.S, p.nC * p.nC);
+      FSC_TRY(launch_gemm(ga, st));
+      FSC_TRY(launch_gram_apply(ra, l, n0, nn, p.chunkbuf, p.grads, st));
+    }
+  }
+  if (cudaMemsetAsync(p.dY, 0, sizeof(float) * p.E * 12, st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset dY");
+  for (int k = p.nint - 1; k >= 1; --k) {
+    ConvArgs ca = conv_args(c, k);
+    // dZ = (1/deg) G_k x W   (l3 blocks)
+    const float* Wb = w->mix_bwd + (int64_t)(k - 1) * NP * C * C;
+    int64_t boff = 0;
+    for (int l3 = 0; l3 < 3; ++l3) {
+      GemmArgs ga = gemm(p.grads[k] + KB(l3) * C, NK * C, C, Wb + boff, NP3(l3) * C, 0, p.zbuf + OFF3(l3) * C,
+                         NZ * C, NP3(l3) * C, p.N, 2 * l3 + 1, C, NP3(l3) * C);
+      ga.deg_rowptr = g->row_ptr;
+      FSC_TRY(launch_gemm(ga, st));
+      boff += (int64_t)NP3(l3) * C * C;
+    }
+    FSC_TRY(launch_conv2_q(ca, p.feats[k - 1], p.zbuf, p.dgates + (int64_t)k * p.E * 12, p.dY, st));
+    FSC_TRY(launch_conv2_r(ca, p.grads[k], p.zbuf, st));
+    const float* Wx = w->mix_dx + (int64_t)(k - 1) * NP * C * C;
+    boff = 0;
+    for (int l1 = 0; l1 < 3; ++l1) {
+      GemmArgs ga = gemm(p.zbuf + OFF1(l1) * C, NZ * C, NP1(l1) * C, Wx + boff, C, 0, p.grads[k - 1] + KB(l1) * C,
+                         NK * C, C, p.N, 2 * l1 + 1, NP1(l1) * C, C);
+      ga.accumulate = 1;
+      FSC_TRY(launch_gemm(ga, st));
+      boff += (int64_t)NP1(l1) * C * C;
+    }
+  }
+  FSC_TRY(launch_conv1_backward(conv_args(c, 0), w->ai, w->vsp, p.grads[0], p.dgates, p.dY, st));
+  return FSC_OK;
+}
+
+// Per-graph sums in float64: out[b*W + w] += sum of vals over items of graph b.
+// Items: atoms (W = 1, value e[n], counted when n < limit) or edges (W = 9, r_e (x) g_e).
+template <int W>
+__global__ void graph_reduce_kernel(const float* __restrict__ e, const float* __restrict__ edge_y,
+                                    const float* __restrict__ grad, const int32_t* __restrict__ item_atom,
+                                    const int32_t* __restrict__ batch, int64_t count, int64_t limit,
+                                    double* __restrict__ out, const float* __restrict__ shift) {
+  __shared__ double red[W][8];
+  __shared__ int first_graph;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  double v[W];
+  int gid = -1;
+#pragma unroll
+  for (int w = 0; w < W; ++w) v[w] = 0.0;
+  if (i < count) {
+    const int64_t atom = item_atom ? item_atom[i] : i;
+    gid = batch[atom];
+    if (W == 1) {
+      if (i < limit) v[0] = (double)e[i];
+    } else {
+      const float* r = shift ? shift + 3 * i : edge_y + 12 * i + 9;
+      const float* g = grad + 3 * i;
+#pragma unroll
+      for (int a = 0; a < 3; ++a)
+#pragma unroll
+        for (int b = 0; b < 3; ++b) v[(3 * a + b) % W] = (double)r[a] * (double)g[b];
+    }
+  }
+  if (threadIdx.x == 0) first_graph = gid;
+  __syncthreads();
+  const bool uniform = __syncthreads_and(gid == first_graph || gid < 0);
+  if (!uniform) {
+    if (gid >= 0)
+#pragma unroll
+      for (int w = 0; w < W; ++w) atomicAdd(out + (int64_t)gid * W + w, v[w]);
+    return;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    double t = v[w];
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (lane == 0) red[w][warp] = t;
+  }
+  __syncthreads();
+  if (threadIdx.x < W && first_graph >= 0) {
+    double t = 0.0;
+    for (int k = 0; k < (int)(blockDim.x >> 5); ++k) t += red[threadIdx.x][k];
+    atomicAdd(out + (int64_t)first_graph * W + threadIdx.x, t);
+  }
+}
+
+int prepare(Ctx& c, void* workspace, size_t bytes) {
+  const fsc_graph* g = c.g;
+  FSC_TRY(validate(c.cfg));
+  FSC_REQUIRE(c.w && g, "weights/graph is null");
+  FSC_REQUIRE(g->num_atoms >= 0 && g->num_edges >= 0 && g->num_graphs >= 1, "bad graph sizes");
+  FSC_REQUIRE(g->num_atoms < (int64_t)INT32_MAX && g->num_edges < (int64_t)INT32_MAX,
+              "graph too large for int32 indices");
+  FSC_REQUIRE(g->num_graphs <= kMaxGraphs, "too many graphs per call (max 4096)");
+  FSC_REQUIRE(g->num_local >= 0 && g->num_local <= g->num_atoms, "num_local out of range");
+  Arena ar(workspace, bytes);
+  layout(c.p, ar, c.cfg, g->num_atoms, g->num_edges);
+  if (!ar.ok() || workspace == nullptr)
+    return fail(FSC_ERR_CAPACITY, "workspace too small: need " + std::to_string(ar.off) + " bytes");
+  c.p.B = g->num_graphs;
+  return FSC_OK;
+}
+
+int run_forward(Ctx& c, float* energy, float* atom_energy) {
+  if (cudaMemsetAsync(c.p.energy_d, 0, sizeof(double) * kMaxGraphs * 19, c.st) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "memset accumulators");
+  FSC_TRY(forward(c));
+  const int H = c.p.hidden[c.p.n_hidden - 1];
+  float* ebuf = atom_energy ? atom_energy : c.p.dxb;  // dxb is free until the backward starts
+  FSC_TRY(launch_energy(c.p.act_post[c.p.n_hidden - 1], c.p.N, H, c.w->out_v, c.w->out_c0, c.g->batch,
+                        c.g->num_local, ebuf, nullptr, c.st));
+  if (c.p.N > 0) {
+    graph_reduce_kernel<1><<<(unsigned)ceil_div(c.p.N, 256), 256, 0, c.st>>>(
+        ebuf, nullptr, nullptr, nullptr, c.g->batch, c.p.N, c.g->num_local, c.p.energy_d, nullptr);
+    FSC_TRY(check_launch("graph_reduce_kernel<1>"));
+  }
+  if (energy) {
+    finalize_kernel<<<(unsigned)ceil_div(c.p.B, 256), 256, 0, c.st>>>(c.p.energy_d, nullptr, c.p.B, energy, nullptr);
+    FSC_TRY(check_launch("finalize_kernel"));
+  }
+  return FSC_OK;
+}
+
+int run_backward(Ctx& c, fsc_ictd_outputs* out) {
+  const fsc_graph* g = c.g;
+  FSC_TRY(backward(c));
+  EdgeBwdArgs eb{};
+  eb.E = c.p.E; eb.src = g->src; eb.batch = g->batch; eb.tables = c.w->tables; eb.rad = radial(c.w);
+  eb.nint = c.p.nint; eb.nb = c.p.nb; eb.basis_kind = c.cfg->basis_kind; eb.rc = c.cfg->max_radius;
+  eb.edge_y = c.p.edge_y; eb.dgates = c.p.dgates; eb.dY = c.p.dY;
+  eb.edge_grad = out->edge_grad ? out->edge_grad : c.p.edge_grad;
+  eb.virial = nullptr;
+  FSC_TRY(launch_edge_backward(eb, c.st));
+  if (out->forces) FSC_TRY(launch_forces(g->row_ptr, g->tr_ptr, g->tr_eid, eb.edge_grad, out->forces, c.p.N, c.st));
+  const int64_t nfin = 9 * c.p.B;
+  if (out->virial) {
+    if (cudaMemsetAsync(c.p.virial_d, 0, sizeof(double) * 9 * kMaxGraphs, c.st) != cudaSuccess)
+      return fail(FSC_ERR_CUDA, "memset virial");
+    if (c.p.E > 0) {
+      graph_reduce_kernel<9><<<(unsigned)ceil_div(c.p.E, 256), 256, 0, c.st>>>(
+          nullptr, c.p.edge_y, eb.edge_grad, g->src, g->batch, c.p.E, c.p.E, c.p.virial_d, nullptr);
+      FSC_TRY(check_launch("graph_reduce_kernel<9>"));
+    }
+    finalize_kernel<<<(unsigned)ceil_div(nfin, 256), 256, 0, c.st>>>(c.p.energy_d, c.p.virial_d, c.p.B, nullptr,
+                                                                     out->virial);
+    FSC_TRY(check_launch("finalize_kernel (virial)"));
+  }
+  if (out->cell_grad) {
+    if (cudaMemsetAsync(c.p.cellg_d, 0, sizeof(double) * 9 * kMaxGraphs, c.st) != cudaSuccess)
+      return fail(FSC_ERR_CUDA, "memset cell grad");
+    if (c.p.E > 0) {
+      graph_reduce_kernel<9><<<(unsigned)ceil_div(c.p.E, 256), 256, 0, c.st>>>(
+          nullptr, c.p.edge_y, eb.edge_grad, g->src, g->batch, c.p.E, c.p.E, c.p.cellg_d, g->shift);
+      FSC_TRY(check_launch("graph_reduce_kernel<9> (cell)"));
+    }
+    finalize_kernel<<<(unsigned)ceil_div(nfin, 256), 256, 0, c.st>>>(c.p.energy_d, c.p.cellg_d, c.p.B, nullptr,
+                                                                     out->cell_grad);
+    FSC_TRY(check_launch("finalize_kernel (cell)"));
+  }
+  return FSC_OK;
+}
+
+}  // namespace
+}  // namespace fsc
+
+extern "C" {
+
+size_t fsc_ictd_workspace_bytes(const fsc_ictd_config* cfg, int64_t num_atoms, int64_t num_edges) {
+  if (!cfg || fsc::validate(cfg) != FSC_OK) return 0;
+  fsc::Plan p{};
+  fsc::Arena ar(nullptr, 0);
+  fsc::layout(p, ar, cfg, num_atoms, num_edges);
+  return ar.off;
+}
+
+int fsc_ictd_forward(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g, float* energy,
+                     float* atom_energy, void* workspace, size_t workspace_bytes, void* stream) {
+  fsc::Ctx c{cfg, w, g, fsc::Plan{}, fsc::as_stream(stream)};
+  FSC_TRY(fsc::prepare(c, workspace, workspace_bytes));
+  return fsc::run_forward(c, energy, atom_energy);
+}
+
+int fsc_ictd_backward(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g,
+                      fsc_ictd_outputs* out, void* workspace, size_t workspace_bytes, void* stream) {
+  FSC_REQUIRE(out != nullptr, "outputs required");
+  fsc::Ctx c{cfg, w, g, fsc::Plan{}, fsc::as_stream(stream)};
+  FSC_TRY(fsc::prepare(c, workspace, workspace_bytes));
+  return fsc::run_backward(c, out);
+}
+
+int fsc_ictd_energy_forces(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g,
+                           fsc_ictd_outputs* out, void* workspace, size_t workspace_bytes, void* stream) {
+  FSC_REQUIRE(out && out->forces && out->energy, "outputs (energy, forces) required");
+  fsc::Ctx c{cfg, w, g, fsc::Plan{}, fsc::as_stream(stream)};
+  FSC_TRY(fsc::prepare(c, workspace, workspace_bytes));
+  FSC_TRY(fsc::run_forward(c, out->energy, out->atom_energy));
+  return fsc::run_backward(c, out);
+}
+
+int fsc_ictd_energy(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g, float* energy,
+                    float* atom_energy, void* workspace, size_t workspace_bytes, void* stream) {
+  FSC_REQUIRE(energy, "energy output required");
+  return fsc_ictd_forward(cfg, w, g, energy, atom_energy, workspace, workspace_bytes, stream);
+}
+
+int64_t fsc_ictd_tables_floats(void) { return ictd2::TAB_FLOATS; }
+
+}  // extern "C"

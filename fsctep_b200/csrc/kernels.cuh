@@ -1,0 +1,128 @@
+// Internal kernel-launch interfaces shared by the .cu files (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fsc {
+
+struct RadialW {
+  const float *w1, *b1, *w2, *b2, *w3, *b3;
+};
+
+struct EdgeFwdArgs {
+  int64_t E;
+  const float* pos;
+  const int32_t* src;
+  const int32_t* dst;
+  const int32_t* batch;
+  const float* cell;
+  const float* shift;
+  const float* tables;
+  RadialW rad;
+  int nint, nb, basis_kind;
+  float rc;
+  float* edge_y;   // [E][12]: Y[9], r[3]
+  float* gates;    // [nint][E][12]
+};
+
+struct EdgeBwdArgs {
+  int64_t E;
+  const int32_t* src;
+  const int32_t* batch;
+  const float* tables;
+  RadialW rad;
+  int nint, nb, basis_kind;
+  float rc;
+  const float* edge_y;
+  const float* dgates;   // [nint][E][12]
+  const float* dY;       // [E][12]
+  float* edge_grad;      // [E][3]
+  double* virial;        // [B][9] or null (accumulated)
+};
+
+int launch_edge_forward(const EdgeFwdArgs& a, cudaStream_t st);
+int launch_edge_backward(const EdgeBwdArgs& a, cudaStream_t st);
+int launch_forces(const int32_t* row_ptr, const int32_t* tr_ptr, const int32_t* tr_eid, const float* g,
+                  float* F, int64_t N, cudaStream_t st);
+int launch_edge_dst(const int32_t* row_ptr, int32_t* dst, int64_t N, cudaStream_t st);
+
+struct ConvArgs {
+  int64_t N, E;
+  int C;
+  const int32_t* row_ptr;
+  const int32_t* src;
+  const int32_t* dst;
+  const int32_t* tr_ptr;
+  const int32_t* tr_eid;
+  const int32_t* species;
+  const float* tables;
+  const float* edge_y;   // [E][12]
+  const float* gates;    // [E][12] of this layer
+};
+
+// conv1: f1[n][k][c]
+int launch_conv1_forward(const ConvArgs& a, const float* ai, const float* vsp, float* f1, cudaStream_t st);
+// conv1 backward: dgates (this layer, all 11 written) and dY (+=)
+int launch_conv1_backward(const ConvArgs& a, const float* ai, const float* vsp, const float* G1,
+                          float* dgates, float* dY, cudaStream_t st);
+// conv2 forward: Z[n][35][C] (not yet divided by the degree)
+int launch_conv2_z(const ConvArgs& a, const float* x, float* Z, cudaStream_t st);
+// conv2 backward, src-centric: R[s][35][C] = sum_{e: src=s} sum_k Yt * G[dst]/deg(dst)
+int launch_conv2_r(const ConvArgs& a, const float* G, float* R, cudaStream_t st);
+// conv2 backward, dst-centric: dgates[e][p], dY[e][k] += from x[src] and dZ[dst]
+int launch_conv2_q(const ConvArgs& a, const float* x, const float* dZ, float* dgates, float* dY,
+                   cudaStream_t st);
+
+// Generic fp32 GEMM with two-level row addressing:
+//   row (g, r), g < G, r < R:  A + g*a_gs + r*a_rs (K contiguous), C + g*c_gs + r*c_rs (N contiguous)
+//   B[k][n] = b_trans ? B[n*ldb + k] : B[k*ldb + n]
+//   C = scale_g * (A @ B) + bias  (+ C if accumulate);  scale_g = 1/max(deg,1) from deg_rowptr if set
+struct GemmArgs {
+  const float* A;
+  int64_t a_gs, a_rs;
+  const float* B;
+  int64_t ldb;
+  int b_trans;
+  float* C;
+  int64_t c_gs, c_rs;
+  int64_t G;
+  int R, K, N;
+  const int32_t* deg_rowptr;
+  const float* bias;
+  int accumulate;
+};
+int launch_gemm(const GemmArgs& a, cudaStream_t st);
+
+// Readout (pure_cartesian_ictd_layers_full.py:956-1054)
+struct ReadoutArgs {
+  int64_t N;
+  int C, nint, S;
+  const float* feats[8];       // nint pointers to [N][9][C]
+  const float* tables;
+  const int32_t* xmap;         // [9*nC] Gram operand element -> (layer << 16) | (k*C + c)
+};
+// Packed Gram of component block l for nodes [n0, n0+nn): Gp[n][pair] = sum_m t[c][m] t[d][m]
+int launch_gram_pack(const ReadoutArgs& a, int l, int64_t n0, int64_t nn, const int32_t* pairs, int64_t npairs,
+                     float* Gp, cudaStream_t st);
+// grads[k][n][KB(l)+m][c] += 2 sum_d H[n][c'][d] t[n][d][m] for nodes [n0, n0+nn), H [nn][nC][nC]
+int launch_gram_apply(const ReadoutArgs& a, int l, int64_t n0, int64_t nn, const float* H, float* const* grads,
+                      cudaStream_t st);
+int launch_p5_forward(const ReadoutArgs& a, const float* scalars, float* p5, cudaStream_t st);
+// Writes (not accumulates) grads[k] for all components, and dscalars.
+int launch_p5_backward(const ReadoutArgs& a, const float* scalars, const float* dp5, float* const* grads,
+                       float* dscalars, cudaStream_t st);
+// LayerNorm over the last dim (rows x D), eps 1e-5, optional SiLU after.
+int launch_layernorm(const float* X, int64_t rows, int D, const float* gamma, const float* beta, int silu,
+                     float* Y, cudaStream_t st);
+// Backward: dX = LN_backward(dY * (silu ? silu'(u) : 1)), u = LN(X)
+int launch_layernorm_backward(const float* X, const float* dY, int64_t rows, int D, const float* gamma,
+                              const float* beta, int silu, float* dX, cudaStream_t st);
+// e[n] = x[n] . v + c0;  energy[batch[n]] += e[n] for n < num_local (double accumulate)
+int launch_energy(const float* x, int64_t N, int H, const float* v, float c0, const int32_t* batch,
+                  int64_t num_local, float* atom_energy, double* energy, cudaStream_t st);
+// dx[n] = v * weight[n]  (weight NULL: 1 for n < num_local, else 0)
+int launch_energy_seed(int64_t N, int H, const float* v, const float* weight, int64_t num_local, float* dx,
+                       cudaStream_t st);
+
+}  // namespace fsc

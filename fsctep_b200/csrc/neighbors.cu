@@ -1,0 +1,491 @@
+// Neighbour list with the semantics of radius_graph_pbc_gpu (utils/graph_utils.py:192-258).
+//
+// Edge (src=i, dst=j, S): |(pos[j] + S@cell) - pos[i]| < cutoff, S in {-1,0,1}^3 on periodic axes,
+// no i == j at S == 0.  Float64 arithmetic in a fixed order without FMA contraction
+// (shift_c = (S0*c0c + S1*c1c) + S2*c2c; d_c = (pos[j,c] + shift_c) - pos[i,c];
+//  r2 = (dx*dx + dy*dy) + dz*dz; edge iff r2 < cutoff*cutoff), so the edge set is bit-exact
+// with the CPU oracle.  Output: CSR by dst with rows sorted by (src, sidx),
+// sidx = (S0+1)*9 + (S1+1)*3 + (S2+1).
+//
+// Two searches, identical results:
+//  * all pairs within a frame (any cell shape, any pbc), one thread per dst atom, candidates
+//    visited in (src, sidx) order so rows come out sorted;
+//  * cell list for a periodic orthorhombic frame whose positions lie in [0, L): cells of side
+//    >= cutoff + 1e-6, the 27 neighbour cells of the dst atom's cell are visited with their
+//    wrap count q (S = -q); every (src, S) candidate is met exactly once for any cell count
+//    per axis >= 1; rows are sorted afterwards (warp-per-row rank sort).
+#include <cub/cub.cuh>
+
+#include <algorithm>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace fsc {
+
+namespace {
+
+struct FrameDev {
+  const int64_t* frame_ptr;  // [F+1]
+  const double* cell;        // [F][9]
+  int64_t F;
+};
+
+__device__ __forceinline__ int find_frame(const int64_t* fp, int64_t F, int64_t a) {
+  int64_t lo = 0, hi = F;  // fp[lo] <= a < fp[hi]
+  while (hi - lo > 1) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (fp[mid] <= a) lo = mid;
+    else hi = mid;
+  }
+  return (int)lo;
+}
+
+__device__ __forceinline__ bool within(const double* pj, const double* pi, const double* sv, double r2max) {
+  const double dx = __dadd_rn(__dadd_rn(pj[0], sv[0]), -pi[0]);
+  const double dy = __dadd_rn(__dadd_rn(pj[1], sv[1]), -pi[1]);
+  const double dz = __dadd_rn(__dadd_rn(pj[2], sv[2]), -pi[2]);
+  const double r2 = __dadd_rn(__dadd_rn(__dmul_rn(dx, dx), __dmul_rn(dy, dy)), __dmul_rn(dz, dz));
+  return r2 < r2max;
+}
+
+__device__ __forceinline__ void shift_vec(const double* c, int s0, int s1, int s2, double* sv) {
+#pragma unroll
+  for (int k = 0; k < 3; ++k)
+    sv[k] = __dadd_rn(__dadd_rn(__dmul_rn((double)s0, c[k]), __dmul_rn((double)s1, c[3 + k])),
+                      __dmul_rn((double)s2, c[6 + k]));
+}
+
+// mode 0: count into counts[j]; mode 1: write src/sidx at row_ptr[j]...
+__global__ void brute_kernel(const double* __restrict__ pos, FrameDev fr, int64_t j0, int64_t j1, int p0, int p1,
+                             int p2, double r2max, int mode, int32_t* __restrict__ counts,
+                             const int32_t* __restrict__ row_ptr, int32_t* __restrict__ src,
+                             int8_t* __restrict__ sidx) {
+  const int64_t j = j0 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= j1) return;
+  const int f = find_frame(fr.frame_ptr, fr.F, j);
+  const int64_t a0 = fr.frame_ptr[f], a1 = fr.frame_ptr[f + 1];
+  const double* c = fr.cell + 9 * f;
+  const double pj[3] = {pos[3 * j], pos[3 * j + 1], pos[3 * j + 2]};
+  int32_t n = 0;
+  int64_t out = mode ? row_ptr[j] : 0;
+  for (int64_t i = a0; i < a1; ++i) {
+    const double pi[3] = {pos[3 * i], pos[3 * i + 1], pos[3 * i + 2]};
+    for (int s0 = -p0; s0 <= p0; ++s0)
+      for (int s1 = -p1; s1 <= p1; ++s1)
+        for (int s2 = -p2; s2 <= p2; ++s2) {
+          if (i == j && s0 == 0 && s1 == 0 && s2 == 0) continue;
+          double sv[3];
+          shift_vec(c, s0, s1, s2, sv);
+          if (within(pj, pi, sv, r2max)) {
+            if (mode) {
+              src[out] = (int32_t)i;
+              sidx[out] = (int8_t)((s0 + 1) * 9 + (s1 + 1) * 3 + (s2 + 1));
+              ++out;
+            } else {
+              ++n;
+            }
+          }
+        }
+  }
+  if (!mode) counts[j] = n;
+}
+
+struct CellGrid {
+  int nc[3];
+  double L[3];
+  double inv_cs[3];
+};
+
+__device__ __forceinline__ int cell_coord(double x, double inv_cs, int n) {
+  int c = (int)floor(x * inv_cs);
+  return c < 0 ? 0 : (c >= n ? n - 1 : c);
+}
+
+__global__ void cell_assign_kernel(const double* __restrict__ pos, int64_t a0, int64_t na, CellGrid g,
+                                   int32_t* __restrict__ cell_of, int32_t* __restrict__ cell_count) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= na) return;
+  const int64_t a = a0 + t;
+  const int cx = cell_coord(pos[3 * a], g.inv_cs[0], g.nc[0]);
+  const int cy = cell_coord(pos[3 * a + 1], g.inv_cs[1], g.nc[1]);
+  const int cz = cell_coord(pos[3 * a + 2], g.inv_cs[2], g.nc[2]);
+  const int id = (cx * g.nc[1] + cy) * g.nc[2] + cz;
+  cell_of[t] = id;
+  atomicAdd(cell_count + id, 1);
+}
+
+__global__ void cell_fill_kernel(int64_t a0, int64_t na, const int32_t* __restrict__ cell_of,
+                                 const int32_t* __restrict__ cell_start, int32_t* __restrict__ cursor,
+                                 int32_t* __restrict__ cell_atoms) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= na) return;
+  const int id = cell_of[t];
+  const int slot = atomicAdd(cursor + id, 1);
+  cell_atoms[cell_start[id] + slot] = (int32_t)(a0 + t);
+}
+
+__global__ void cell_search_kernel(const double* __restrict__ pos, int64_t a0, int64_t na, CellGrid g,
+                                   const double* __restrict__ cellm, const int32_t* __restrict__ cell_of,
+                                   const int32_t* __restrict__ cell_start, const int32_t* __restrict__ cell_atoms,
+                                   double r2max, int mode, int32_t* __restrict__ counts,
+                                   const int32_t* __restrict__ row_ptr, int32_t* __restrict__ src,
+                                   int8_t* __restrict__ sidx) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= na) return;
+  const int64_t j = a0 + t;
+  const int id = cell_of[t];
+  const int cz = id % g.nc[2], cy = (id / g.nc[2]) % g.nc[1], cx = id / (g.nc[2] * g.nc[1]);
+  const double pj[3] = {pos[3 * j], pos[3 * j + 1], pos[3 * j + 2]};
+  int32_t n = 0;
+  int64_t out = mode ? row_ptr[j] : 0;
+  for (int dx = -1; dx <= 1; ++dx) {
+    const int ux = cx + dx;
+    const int qx = ux < 0 ? -1 : (ux >= g.nc[0] ? 1 : 0);
+    const int wx = ux - qx * g.nc[0];
+    for (int dy = -1; dy <= 1; ++dy) {
+      const int uy = cy + dy;
+      const int qy = uy < 0 ? -1 : (uy >= g.nc[1] ? 1 : 0);
+      const int wy = uy - qy * g.nc[1];
+      for (int dz = -1; dz <= 1; ++dz) {
+        const int uz = cz + dz;
+        const int qz = uz < 0 ? -1 : (uz >= g.nc[2] ? 1 : 0);
+        const int wz = uz - qz * g.nc[2];
+        const int s0 = -qx, s1 = -qy, s2 = -qz;
+        double sv[3];
+        shift_vec(cellm, s0, s1, s2, sv);
+        const int nid = (wx * g.nc[1] + wy) * g.nc[2] + wz;
+        for (int k = cell_start[nid]; k < cell_start[nid + 1]; ++k) {
+          const int64_t i = cell_atoms[k];
+          if (i == j && s0 == 0 && s1 == 0 && s2 == 0) continue;
+          const double pi[3] = {pos[3 * i], pos[3 * i + 1], pos[3 * i + 2]};
+          if (within(pj, pi, sv, r2max)) {
+            if (mode) {
+              src[out] = (int32_t)i;
+              sidx[out] = (int8_t)((s0 + 1) * 9 + (s1 + 1) * 3 + (s2 + 1));
+              ++out;
+            } else {
+              ++n;
+            }
+          }
+        }
+      }
+    }
+  }
+  if (!mode) counts[j] = n;
+}
+
+// Warp per row: sort (key = src*27 + sidx) ascending by rank counting; rows of any length.
+__global__ void row_sort_kernel(const int32_t* __restrict__ row_ptr, int64_t N, int32_t* __restrict__ src,
+                                int8_t* __restrict__ sidx, int32_t* __restrict__ tmp_src, int8_t* __restrict__ tmp_sidx) {
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (r >= N) return;
+  const int e0 = row_ptr[r], e1 = row_ptr[r + 1];
+  for (int e = e0 + lane; e < e1; e += 32) {
+    const int64_t key = (int64_t)src[e] * 27 + sidx[e];
+    int rank = 0;
+    for (int f = e0; f < e1; ++f) {
+      const int64_t k2 = (int64_t)src[f] * 27 + sidx[f];
+      rank += (k2 < key) ? 1 : 0;
+    }
+    tmp_src[e0 + rank] = src[e];
+    tmp_sidx[e0 + rank] = sidx[e];
+  }
+  __syncwarp();
+  for (int e = e0 + lane; e < e1; e += 32) {
+    src[e] = tmp_src[e];
+    sidx[e] = tmp_sidx[e];
+  }
+}
+
+__global__ void out_of_box_kernel(const double* __restrict__ pos, int64_t a0, int64_t na, double Lx, double Ly,
+                                  double Lz, int32_t* __restrict__ flag) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= na) return;
+  const int64_t a = a0 + t;
+  const double x = pos[3 * a], y = pos[3 * a + 1], z = pos[3 * a + 2];
+  if (!(x >= 0.0 && x < Lx && y >= 0.0 && y < Ly && z >= 0.0 && z < Lz)) atomicOr(flag, 1);
+}
+
+// transpose CSR
+__global__ void tr_count_kernel(const int32_t* __restrict__ src, int64_t E, int32_t* __restrict__ cnt) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e < E) atomicAdd(cnt + src[e], 1);
+}
+__global__ void tr_fill_kernel(const int32_t* __restrict__ src, int64_t E, const int32_t* __restrict__ tr_ptr,
+                               int32_t* __restrict__ cursor, int32_t* __restrict__ tr_eid) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= E) return;
+  const int s = src[e];
+  tr_eid[tr_ptr[s] + atomicAdd(cursor + s, 1)] = (int32_t)e;
+}
+__global__ void tr_sort_kernel(const int32_t* __restrict__ tr_ptr, int64_t N, int32_t* __restrict__ tr_eid,
+                               int32_t* __restrict__ tmp) {
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (r >= N) return;
+  const int e0 = tr_ptr[r], e1 = tr_ptr[r + 1];
+  for (int e = e0 + lane; e < e1; e += 32) {
+    const int key = tr_eid[e];
+    int rank = 0;
+    for (int f = e0; f < e1; ++f) rank += (tr_eid[f] < key) ? 1 : 0;
+    tmp[e0 + rank] = key;
+  }
+  __syncwarp();
+  for (int e = e0 + lane; e < e1; e += 32) tr_eid[e] = tmp[e];
+}
+
+size_t scan_temp_bytes(int64_t n) {
+  size_t bytes = 0;
+  cub::DeviceScan::ExclusiveSum(nullptr, bytes, (int32_t*)nullptr, (int32_t*)nullptr, (int)n);
+  return bytes;
+}
+
+struct NbrWs {
+  int32_t* counts;      // [N+1]
+  int32_t* cell_of;     // [N]
+  int32_t* cell_count;  // [N+2]
+  int32_t* cell_start;  // [N+2]
+  int32_t* cursor;      // [N+2]
+  int32_t* cell_atoms;  // [N]
+  int64_t* frame_ptr;   // [F+1] (F <= N+1)
+  double* cell;         // [F][9]
+  int32_t* flag;        // [4]
+  void* scan_tmp;
+  size_t scan_bytes;
+};
+
+void nbr_layout(NbrWs& w, Arena& ar, int64_t N, int64_t F) {
+  w.counts = ar.take<int32_t>(N + 1);
+  w.cell_of = ar.take<int32_t>(N + 1);
+  w.cell_count = ar.take<int32_t>(N + 2);
+  w.cell_start = ar.take<int32_t>(N + 2);
+  w.cursor = ar.take<int32_t>(N + 2);
+  w.cell_atoms = ar.take<int32_t>(N + 1);
+  w.frame_ptr = ar.take<int64_t>(F + 1);
+  w.cell = ar.take<double>(9 * F + 9);
+  w.flag = ar.take<int32_t>(4);
+  w.scan_bytes = scan_temp_bytes(N + 2);
+  w.scan_tmp = ar.take<char>((int64_t)w.scan_bytes + 16);
+}
+
+bool orthorhombic(const double* c) {
+  return c[1] == 0.0 && c[2] == 0.0 && c[3] == 0.0 && c[5] == 0.0 && c[6] == 0.0 && c[7] == 0.0 && c[0] > 0.0 &&
+         c[4] > 0.0 && c[8] > 0.0;
+}
+
+CellGrid make_grid(const double* c, double cutoff, int64_t natoms) {
+  CellGrid g{};
+  const double L[3] = {c[0], c[4], c[8]};
+  int64_t nc[3];
+  for (int k = 0; k < 3; ++k) nc[k] = std::max<int64_t>(1, (int64_t)std::floor(L[k] / (cutoff + 1e-6)));
+  const int64_t cap = std::max<int64_t>(1, natoms);
+  while (nc[0] * nc[1] * nc[2] > cap) {
+    int k = 0;
+    if (nc[1] > nc[k]) k = 1;
+    if (nc[2] > nc[k]) k = 2;
+    nc[k] -= 1;
+  }
+  for (int k = 0; k < 3; ++k) {
+    g.nc[k] = (int)nc[k];
+    g.L[k] = L[k];
+    g.inv_cs[k] = (double)nc[k] / L[k];
+  }
+  return g;
+}
+
+// Run the search (mode 0 count / 1 fill) over all frames.
+int search(const double* pos, const double* cell_host, const int64_t* fp_host, int64_t F, int64_t N,
+           const int32_t* pbc, double cutoff, int mode, int32_t* counts, const int32_t* row_ptr, int32_t* src,
+           int8_t* sidx, NbrWs& w, cudaStream_t st) {
+  const double r2max = cutoff * cutoff;
+  const bool all_pbc = pbc[0] && pbc[1] && pbc[2];
+  std::vector<int64_t> brute_frames;
+  for (int64_t f = 0; f < F; ++f) {
+    const int64_t a0 = fp_host[f], na = fp_host[f + 1] - fp_host[f];
+    const double* c = cell_host + 9 * f;
+    bool use_cells = all_pbc && orthorhombic(c) && na > 512;
+    if (use_cells) {
+      if (cudaMemsetAsync(w.flag, 0, sizeof(int32_t), st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset flag");
+      out_of_box_kernel<<<(unsigned)ceil_div(na, 256), 256, 0, st>>>(pos, a0, na, c[0], c[4], c[8], w.flag);
+      int32_t flag = 0;
+      if (cudaMemcpyAsync(&flag, w.flag, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+          cudaStreamSynchronize(st) != cudaSuccess)
+        return fail(FSC_ERR_CUDA, "neighbour box check");
+      use_cells = (flag == 0);
+    }
+    if (!use_cells) {
+      brute_frames.push_back(f);
+      continue;
+    }
+    CellGrid g = make_grid(c, cutoff, na);
+    const int64_t ncell = (int64_t)g.nc[0] * g.nc[1] * g.nc[2];
+    if (cudaMemsetAsync(w.cell_count, 0, sizeof(int32_t) * (ncell + 1), st) != cudaSuccess ||
+        cudaMemsetAsync(w.cursor, 0, sizeof(int32_t) * (ncell + 1), st) != cudaSuccess)
+      return fail(FSC_ERR_CUDA, "memset cells");
+    const unsigned blocks = (unsigned)ceil_div(na, 256);
+    cell_assign_kernel<<<blocks, 256, 0, st>>>(pos, a0, na, g, w.cell_of, w.cell_count);
+    size_t sb = w.scan_bytes;
+    if (cub::DeviceScan::ExclusiveSum(w.scan_tmp, sb, w.cell_count, w.cell_start, (int)(ncell + 1), st) !=
+        cudaSuccess)
+      return fail(FSC_ERR_CUDA, "cell scan");
+    cell_fill_kernel<<<blocks, 256, 0, st>>>(a0, na, w.cell_of, w.cell_start, w.cursor, w.cell_atoms);
+    cell_search_kernel<<<blocks, 256, 0, st>>>(pos, a0, na, g, w.cell + 9 * f, w.cell_of, w.cell_start, w.cell_atoms,
+                                               r2max, mode, counts, row_ptr, src, sidx);
+    FSC_TRY(check_launch("cell_search_kernel"));
+  }
+  if (!brute_frames.empty()) {
+    // one launch over all atoms of the brute-force frames (contiguous runs are launched together)
+    size_t k = 0;
+    while (k < brute_frames.size()) {
+      size_t k2 = k + 1;
+      while (k2 < brute_frames.size() && brute_frames[k2] == brute_frames[k2 - 1] + 1) ++k2;
+      const int64_t f0 = brute_frames[k], f1 = brute_frames[k2 - 1] + 1;
+      const int64_t a0 = fp_host[f0], a1 = fp_host[f1];
+      FrameDev fr{w.frame_ptr, w.cell, F};
+      const int64_t na = a1 - a0;
+      if (na > 0) {
+        brute_kernel<<<(unsigned)ceil_div(na, 128), 128, 0, st>>>(pos, fr, a0, a1, pbc[0], pbc[1], pbc[2], r2max,
+                                                                  mode, counts, row_ptr, src, sidx);
+        FSC_TRY(check_launch("brute_kernel"));
+      }
+      k = k2;
+    }
+  }
+  return FSC_OK;
+}
+
+}  // namespace
+}  // namespace fsc
+
+using namespace fsc;
+
+extern "C" {
+
+size_t fsc_neighbor_workspace_bytes(int64_t num_atoms, int64_t num_edges) {
+  NbrWs w{};
+  Arena ar(nullptr, 0);
+  nbr_layout(w, ar, num_atoms, num_atoms + 1);
+  ar.take<int32_t>(num_edges);
+  ar.take<int8_t>(num_edges);
+  return ar.off;
+}
+
+static int nbr_prepare(const double* cell, const int64_t* frame_ptr_host, int64_t F, int64_t N, const int32_t* pbc,
+                       NbrWs& w, void* workspace, size_t bytes, std::vector<double>& cell_host, cudaStream_t st) {
+  FSC_REQUIRE(F >= 1 && N >= 0, "bad frame/atom counts");
+  FSC_REQUIRE(frame_ptr_host && frame_ptr_host[0] == 0 && frame_ptr_host[F] == N, "frame_ptr must span [0, N]");
+  for (int64_t f = 0; f < F; ++f) FSC_REQUIRE(frame_ptr_host[f + 1] >= frame_ptr_host[f], "frame_ptr not monotone");
+  FSC_REQUIRE(F <= N + 1, "more frames than atoms");
+  FSC_REQUIRE(N < (int64_t)1 << 26, "neighbour builder supports < 2^26 atoms");
+  FSC_REQUIRE(pbc != nullptr, "pbc flags required");
+  Arena ar(workspace, bytes);
+  nbr_layout(w, ar, N, F);
+  if (!ar.ok()) return fail(FSC_ERR_CAPACITY, "neighbour workspace too small");
+  cell_host.resize(9 * F);
+  if (cudaMemcpyAsync(cell_host.data(), cell, sizeof(double) * 9 * F, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaMemcpyAsync(w.cell, cell, sizeof(double) * 9 * F, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(w.frame_ptr, frame_ptr_host, sizeof(int64_t) * (F + 1), cudaMemcpyHostToDevice, st) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "neighbour setup copies");
+  return FSC_OK;
+}
+
+int fsc_neighbor_count(const double* pos, const double* cell, const int64_t* frame_ptr_host, int64_t num_frames,
+                       int64_t num_atoms, const int32_t* pbc_host, double cutoff, int32_t* row_ptr,
+                       int64_t* num_edges_host, void* workspace, size_t workspace_bytes, void* stream) {
+  FSC_REQUIRE(num_edges_host && row_ptr, "row_ptr / num_edges output required");
+  FSC_REQUIRE(cutoff > 0.0, "cutoff must be positive");
+  cudaStream_t st = as_stream(stream);
+  NbrWs w{};
+  std::vector<double> cell_host;
+  FSC_TRY(nbr_prepare(cell, frame_ptr_host, num_frames, num_atoms, pbc_host, w, workspace, workspace_bytes, cell_host,
+                      st));
+  const int64_t N = num_atoms;
+  if (cudaMemsetAsync(w.counts, 0, sizeof(int32_t) * (N + 1), st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset");
+  FSC_TRY(search(pos, cell_host.data(), frame_ptr_host, num_frames, N, pbc_host, cutoff, 0, w.counts, nullptr,
+                 nullptr, nullptr, w, st));
+  size_t sb = w.scan_bytes;
+  if (cub::DeviceScan::ExclusiveSum(w.scan_tmp, sb, w.counts, row_ptr, (int)(N + 1), st) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "edge scan");
+  int32_t total = 0;
+  if (cudaMemcpyAsync(&total, row_ptr + N, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "edge count readback");
+  *num_edges_host = total;
+  return FSC_OK;
+}
+
+int fsc_neighbor_fill(const double* pos, const double* cell, const int64_t* frame_ptr_host, int64_t num_frames,
+                      int64_t num_atoms, const int32_t* pbc_host, double cutoff, const int32_t* row_ptr, int32_t* src,
+                      int8_t* sidx, int64_t capacity, void* workspace, size_t workspace_bytes, void* stream) {
+  FSC_REQUIRE(src && sidx && row_ptr, "outputs required");
+  cudaStream_t st = as_stream(stream);
+  NbrWs w{};
+  std::vector<double> cell_host;
+  FSC_TRY(nbr_prepare(cell, frame_ptr_host, num_frames, num_atoms, pbc_host, w, workspace, workspace_bytes, cell_host,
+                      st));
+  const int64_t N = num_atoms;
+  int32_t total = 0;
+  if (cudaMemcpyAsync(&total, row_ptr + N, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "edge count readback");
+  if (total > capacity) return fail(FSC_ERR_CAPACITY, "edge capacity " + std::to_string(capacity) + " < " +
+                                                          std::to_string(total));
+  FSC_TRY(search(pos, cell_host.data(), frame_ptr_host, num_frames, N, pbc_host, cutoff, 1, nullptr, row_ptr, src,
+                 sidx, w, st));
+  // rows from the cell-list search are unordered: sort every row (sorted rows stay as they are)
+  if (total > 0 && N > 0) {
+    Arena ar2(workspace, workspace_bytes);
+    NbrWs dummy{};
+    nbr_layout(dummy, ar2, N, num_frames);
+    int32_t* tmp_src = ar2.take<int32_t>(total);
+    int8_t* tmp_sidx = ar2.take<int8_t>(total);
+    if (!ar2.ok() || !tmp_src)
+      return fail(FSC_ERR_CAPACITY, "neighbour workspace too small for the fill phase; size it with "
+                                    "fsc_neighbor_workspace_bytes(num_atoms, num_edges)");
+    row_sort_kernel<<<(unsigned)ceil_div(N, 8), 256, 0, st>>>(row_ptr, N, src, sidx, tmp_src, tmp_sidx);
+    FSC_TRY(check_launch("row_sort_kernel"));
+  }
+  return FSC_OK;
+}
+
+int fsc_csr_transpose(const int32_t* row_ptr, const int32_t* src, int64_t num_atoms, int64_t num_edges,
+                      int32_t* tr_ptr, int32_t* tr_eid, void* workspace, size_t workspace_bytes, void* stream) {
+  cudaStream_t st = as_stream(stream);
+  const int64_t N = num_atoms, E = num_edges;
+  FSC_REQUIRE(tr_ptr && tr_eid && row_ptr && src, "null pointer");
+  Arena ar(workspace, workspace_bytes);
+  int32_t* cnt = ar.take<int32_t>(N + 1);
+  int32_t* cursor = ar.take<int32_t>(N + 1);
+  int32_t* tmp = ar.take<int32_t>(E + 1);
+  const size_t sbytes = scan_temp_bytes(N + 1);
+  void* stmp = ar.take<char>((int64_t)sbytes + 16);
+  if (!ar.ok() || (workspace == nullptr)) return fail(FSC_ERR_CAPACITY, "transpose workspace too small");
+  if (cudaMemsetAsync(cnt, 0, sizeof(int32_t) * (N + 1), st) != cudaSuccess ||
+      cudaMemsetAsync(cursor, 0, sizeof(int32_t) * (N + 1), st) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "memset");
+  if (E > 0) tr_count_kernel<<<(unsigned)ceil_div(E, 256), 256, 0, st>>>(src, E, cnt);
+  size_t sb = sbytes;
+  if (cub::DeviceScan::ExclusiveSum(stmp, sb, cnt, tr_ptr, (int)(N + 1), st) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "transpose scan");
+  if (E > 0) {
+    tr_fill_kernel<<<(unsigned)ceil_div(E, 256), 256, 0, st>>>(src, E, tr_ptr, cursor, tr_eid);
+    tr_sort_kernel<<<(unsigned)ceil_div(N, 8), 256, 0, st>>>(tr_ptr, N, tr_eid, tmp);
+  }
+  return check_launch("csr_transpose");
+}
+
+size_t fsc_csr_transpose_workspace_bytes(int64_t num_atoms, int64_t num_edges) {
+  Arena ar(nullptr, 0);
+  ar.take<int32_t>(num_atoms + 1);
+  ar.take<int32_t>(num_atoms + 1);
+  ar.take<int32_t>(num_edges + 1);
+  ar.take<char>((int64_t)scan_temp_bytes(num_atoms + 1) + 16);
+  return ar.off;
+}
+
+}  // extern "C"

@@ -1,0 +1,306 @@
+"""pure-cartesian-ictd on B200: weight packing, graph CSR and the native E + F engine.
+
+Host-side mirror of the reference operator surface for this path:
+
+* ``ICTDEngine`` packs a reference-layout ``state_dict`` of
+  ``PureCartesianICTDTransformerLayer`` (``models/pure_cartesian_ictd_layers_full.py``)
+  into the fp32 device layouts of ``include/fsctep_b200.h`` and runs the native
+  forward / hand-written backward (``fsc_ictd_forward`` / ``fsc_ictd_backward``).
+* ``GraphCSR`` turns an edge list ``(edge_src, edge_dst, edge_shifts)`` (any order) into
+  the dst-sorted CSR + transpose CSR the kernels read.
+* ``PureCartesianICTDTransformerLayer`` (in ``fsctep_b200.models``) wraps both behind the
+  reference module's constructor, state_dict keys and ``forward`` signature.
+
+Nothing here computes on the CPU: every numeric step of the path is a kernel in
+``libfsctep_b200.so``; the packing below is a one-time weight transform.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass, field
+from typing import Dict, Optional, Sequence
+
+import torch
+
+from fsctep_b200 import _native as N
+from fsctep_b200 import tables as T
+
+BASIS_KINDS = {"gaussian": 0, "bessel": 1}
+NP = 11
+P3_PATHS = [[0, 4, 9], [1, 3, 6, 8], [2, 5, 7, 10]]   # paths by l3, path order
+P1_PATHS = [[0, 1, 2], [3, 4, 5, 6], [7, 8, 9, 10]]   # paths by l1
+P_L0L = [0, 3, 7]                                      # (l,0,l) paths
+
+
+@dataclass
+class ICTDConfig:
+    channels: int = 64
+    lmax: int = 2
+    num_interaction: int = 3
+    number_of_basis: int = 8
+    max_radius: float = 5.0
+    function_type: str = "gaussian"
+    output_size: int = 8
+    embedding_dim: int = 16
+    max_atomvalue: int = 10
+    invariant_channels: int = 32
+    embed_size: Sequence[int] = field(default_factory=lambda: (128, 128, 128))
+
+    @property
+    def scalar_channels(self):
+        return (self.num_interaction - 1) * self.invariant_channels
+
+    def native(self) -> N.IctdConfig:
+        if self.function_type not in BASIS_KINDS:
+            raise NotImplementedError(f"radial basis {self.function_type!r} is not implemented in the sm_100a kernels "
+                                      f"(supported: {sorted(BASIS_KINDS)})")
+        c = N.IctdConfig(channels=self.channels, lmax=self.lmax, num_interaction=self.num_interaction,
+                         number_of_basis=self.number_of_basis, basis_kind=BASIS_KINDS[self.function_type],
+                         max_radius=float(self.max_radius), num_species=self.max_atomvalue,
+                         output_size=self.output_size, invariant_channels=self.invariant_channels,
+                         n_hidden=len(self.embed_size), n_out=17)
+        for k, h in enumerate(self.embed_size):
+            c.hidden[k] = int(h)
+        return c
+
+
+def gram_xmap(C: int, nint: int):
+    """Storage location of every element of the readout's Gram operand.
+
+    The reference splits the flat concatenation of all layers' features (each in the
+    [l0 (C,1) | l1 (C,3) | l2 (C,5)] layout) into l blocks of nC*(2l+1) elements
+    (``pure_cartesian_ictd_layers_full.py:956-958``), so t_l[c][m] is flat element
+    off_l + c*(2l+1) + m.  Returns, per flat element, (layer << 16) | (k*C + channel) with
+    k = l'*l' + m' the component index in the [N][9][C] feature buffers.
+    """
+    out = []
+    for q in range(9 * C * nint):
+        layer, w = divmod(q, 9 * C)
+        if w < C:
+            l, base = 0, 0
+        elif w < 4 * C:
+            l, base = 1, C
+        else:
+            l, base = 2, 4 * C
+        c, m = divmod(w - base, 2 * l + 1)
+        out.append((layer << 16) | ((l * l + m) * C + c))
+    return out
+
+
+def _silu(x):
+    return x * torch.sigmoid(x)
+
+
+class PackedICTDWeights:
+    """fp32 device tensors in the C-ABI layouts, derived once from a reference state_dict."""
+
+    def __init__(self, sd: Dict[str, torch.Tensor], cfg: ICTDConfig, device):
+        dev = torch.device(device)
+        f64 = lambda k: sd[k].detach().to(device=dev, dtype=torch.float64)  # noqa: E731
+        C_, nint = cfg.channels, cfg.num_interaction
+        keep = {}
+
+        def put(name, t):
+            keep[name] = t.to(device=dev, dtype=torch.float32).contiguous()
+            return keep[name]
+
+        put("tables", torch.from_numpy(T.kernel_tables(cfg.lmax)))
+        # per-species conv1 tables
+        emb = f64("e3_conv_emb.atom_embedding.weight")
+        h = _silu(emb @ f64("e3_conv_emb.atom_mlp.0.weight").T + f64("e3_conv_emb.atom_mlp.0.bias"))
+        ai = h @ f64("e3_conv_emb.atom_mlp.2.weight").T + f64("e3_conv_emb.atom_mlp.2.bias")  # [S, 8]
+        W1 = f64("e3_conv_emb.tp2.weight")  # [P, C, 8, 8]
+        vsp = torch.stack([torch.einsum("oij,sj->sio", W1[p], ai) for p in P_L0L], dim=1)  # [S, 3, 8, C]
+        put("ai", ai)
+        put("vsp", vsp)
+        # radial MLPs: conv1 fc, then fc2_layers.k
+        pref = ["e3_conv_emb.fc"] + [f"fc2_layers.{k}" for k in range(nint - 1)]
+        put("rad_w1", torch.stack([f64(f"{p}.0.weight") for p in pref]))
+        put("rad_b1", torch.stack([f64(f"{p}.0.bias") for p in pref]))
+        put("rad_w2", torch.stack([f64(f"{p}.2.weight") for p in pref]))
+        put("rad_b2", torch.stack([f64(f"{p}.2.bias") for p in pref]))
+        put("rad_w3", torch.stack([f64(f"{p}.4.weight") for p in pref]))
+        put("rad_b3", torch.stack([f64(f"{p}.4.bias") for p in pref]))
+        # channel mixes
+        fwd, bwd, dx = [], [], []
+        for k in range(nint - 1):
+            W = f64(f"tp2_layers.{k}.weight")[..., 0]  # [P, o, i]
+            for group in P3_PATHS:
+                fwd.append(torch.cat([W[p].T for p in group], dim=0).reshape(-1))      # [(rank,i)][o]
+                bwd.append(torch.cat([W[p] for p in group], dim=1).reshape(-1))        # [o][(rank,i)]
+            for group in P1_PATHS:
+                dx.append(torch.cat([W[p] for p in group], dim=0).reshape(-1))         # [(rank,o)][i]
+        put("mix_fwd", torch.cat(fwd))
+        put("mix_bwd", torch.cat(bwd))
+        put("mix_dx", torch.cat(dx))
+        # readout W_read
+        nC = C_ * nint
+        iu = torch.triu_indices(nC, nC, device=dev)
+        wp, ws = [], []
+        for l in range(3):
+            Wr = f64(f"W_read.{l}") / math.sqrt(2 * l + 1)  # [S, nC, nC]
+            Wsym = 0.5 * (Wr + Wr.transpose(1, 2))
+            ws.append(Wsym.reshape(-1))
+            packed = (Wr + Wr.transpose(1, 2))[:, iu[0], iu[1]]
+            diag = iu[0] == iu[1]
+            packed[:, diag] = Wr[:, iu[0][diag], iu[1][diag]]
+            wp.append(packed.reshape(-1))
+        put("wread_p", torch.cat(wp))
+        put("wread_s", torch.cat(ws))
+        keep["pairs"] = (iu[0] | (iu[1] << 16)).to(torch.int32).contiguous()
+        keep["xmap"] = torch.tensor(gram_xmap(C_, nint), dtype=torch.int32, device=dev)
+        # MainNet
+        put("mn_in_g", f64("proj_total.input_norm.weight"))
+        put("mn_in_b", f64("proj_total.input_norm.bias"))
+        for k in range(len(cfg.embed_size)):
+            put(f"mn_w{k}", f64(f"proj_total.layers.{k}.weight"))
+            put(f"mn_b{k}", f64(f"proj_total.layers.{k}.bias"))
+            put(f"mn_g{k}", f64(f"proj_total.layer_norms.{k}.weight"))
+            put(f"mn_beta{k}", f64(f"proj_total.layer_norms.{k}.bias"))
+        wsum = f64("weighted_sum.weights")
+        put("out_v", f64("proj_total.output.weight").T @ wsum)
+        self.out_c0 = float((f64("proj_total.output.bias") * wsum).sum().item())
+        self.tensors = keep
+        s = N.IctdWeights()
+        for name in ("tables", "ai", "vsp", "rad_w1", "rad_b1", "rad_w2", "rad_b2", "rad_w3", "rad_b3",
+                     "mix_fwd", "mix_bwd", "mix_dx", "wread_p", "wread_s", "pairs", "xmap", "mn_in_g", "mn_in_b", "out_v"):
+            setattr(s, name, keep[name].data_ptr())
+        for k in range(len(cfg.embed_size)):
+            s.mn_w[k] = keep[f"mn_w{k}"].data_ptr()
+            s.mn_b[k] = keep[f"mn_b{k}"].data_ptr()
+            s.mn_g[k] = keep[f"mn_g{k}"].data_ptr()
+            s.mn_beta[k] = keep[f"mn_beta{k}"].data_ptr()
+        s.out_c0 = self.out_c0
+        self.struct = s
+
+
+class GraphCSR:
+    """dst-sorted CSR + transpose CSR of an edge list (all int32 on the device).
+
+    ``order`` maps CSR edge slots to the caller's edge indices (stable by dst), so per-edge
+    outputs can be returned in the caller's order.
+    """
+
+    def __init__(self, num_atoms: int, row_ptr, src, shift, tr_ptr, tr_eid, order=None):
+        self.num_atoms = int(num_atoms)
+        self.row_ptr, self.src, self.shift, self.tr_ptr, self.tr_eid = row_ptr, src, shift, tr_ptr, tr_eid
+        self.order = order
+        self.num_edges = int(src.shape[0])
+
+    @staticmethod
+    def transpose(row_ptr, src, num_atoms: int):
+        dev = src.device
+        E = int(src.shape[0])
+        tr_ptr = torch.empty(num_atoms + 1, dtype=torch.int32, device=dev)
+        tr_eid = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
+        L = N.lib()
+        ws_bytes = L.fsc_csr_transpose_workspace_bytes(num_atoms, E)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        N.check(L.fsc_csr_transpose(N.ptr(row_ptr), N.ptr(src), num_atoms, E, N.ptr(tr_ptr), N.ptr(tr_eid),
+                                    N.ptr(ws), ws_bytes, N.stream_ptr(dev)), "fsc_csr_transpose")
+        return tr_ptr, tr_eid[:E]
+
+    @classmethod
+    def from_edges(cls, edge_src, edge_dst, edge_shifts, num_atoms: int):
+        dev = edge_src.device
+        order = torch.argsort(edge_dst, stable=True)
+        dst_sorted = edge_dst[order]
+        counts = torch.bincount(dst_sorted, minlength=num_atoms)
+        row_ptr = torch.zeros(num_atoms + 1, dtype=torch.int32, device=dev)
+        row_ptr[1:] = torch.cumsum(counts, 0).to(torch.int32)
+        src = edge_src[order].to(torch.int32).contiguous()
+        shift = edge_shifts[order].to(torch.float32).contiguous()
+        tr_ptr, tr_eid = cls.transpose(row_ptr, src, num_atoms)
+        return cls(num_atoms, row_ptr, src, shift, tr_ptr, tr_eid, order)
+
+
+class ICTDEngine:
+    """Native energy + forces for one packed model (reused across calls)."""
+
+    def __init__(self, state_dict: Dict[str, torch.Tensor], cfg: ICTDConfig, device="cuda"):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.ncfg = cfg.native()
+        self.weights = PackedICTDWeights(state_dict, cfg, self.device)
+        self._ws = None
+
+    def workspace(self, num_atoms: int, num_edges: int):
+        need = N.lib().fsc_ictd_workspace_bytes(C.byref(self.ncfg), num_atoms, num_edges)
+        if need == 0:
+            N.check(1, "fsc_ictd_workspace_bytes (unsupported configuration)")
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = None
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def _graph(self, pos, species, batch, cell, g: GraphCSR, num_graphs, num_local, energy_weight):
+        s = N.Graph()
+        s.num_atoms = g.num_atoms
+        s.num_local = g.num_atoms if num_local is None else int(num_local)
+        s.num_edges = g.num_edges
+        s.num_graphs = int(num_graphs)
+        s.pos, s.species, s.batch, s.cell = pos.data_ptr(), species.data_ptr(), batch.data_ptr(), cell.data_ptr()
+        s.row_ptr, s.src, s.shift = g.row_ptr.data_ptr(), g.src.data_ptr(), g.shift.data_ptr()
+        s.tr_ptr, s.tr_eid = g.tr_ptr.data_ptr(), g.tr_eid.data_ptr()
+        s.energy_weight = 0 if energy_weight is None else energy_weight.data_ptr()
+        return s
+
+    @staticmethod
+    def _inputs(pos, species, batch, cell):
+        pos = pos.detach().to(torch.float32).contiguous()
+        species = species.to(torch.int32).contiguous()
+        batch = batch.to(torch.int32).contiguous()
+        cell = cell.detach().to(torch.float32).reshape(-1, 3, 3).contiguous()
+        return pos, species, batch, cell
+
+    def forward(self, pos, species, batch, cell, g: GraphCSR, num_local=None):
+        """Per-graph energy (B,) and per-atom energy (N,); intermediates stay in the workspace."""
+        pos, species, batch, cell = self._inputs(pos, species, batch, cell)
+        B = cell.shape[0]
+        ws = self.workspace(g.num_atoms, g.num_edges)
+        energy = torch.empty(B, dtype=torch.float32, device=self.device)
+        atom_e = torch.empty(g.num_atoms, dtype=torch.float32, device=self.device)
+        gs = self._graph(pos, species, batch, cell, g, B, num_local, None)
+        N.check(N.lib().fsc_ictd_forward(C.byref(self.ncfg), C.byref(self.weights.struct), C.byref(gs),
+                                         N.ptr(energy), N.ptr(atom_e), N.ptr(ws), ws.numel(),
+                                         N.stream_ptr(self.device)), "fsc_ictd_forward")
+        self._last = (pos, species, batch, cell, g, num_local)
+        return energy, atom_e
+
+    def backward(self, energy_weight=None, want_virial=True, want_cell_grad=False, want_edge_grad=False):
+        """Reverse pass of the last forward: forces (N,3), virial (B,3,3), dE/dcell, dE/dr."""
+        pos, species, batch, cell, g, num_local = self._last
+        B = cell.shape[0]
+        ws = self.workspace(g.num_atoms, g.num_edges)
+        dev = self.device
+        out = {"forces": torch.empty(g.num_atoms, 3, dtype=torch.float32, device=dev)}
+        if want_virial:
+            out["virial"] = torch.empty(B, 3, 3, dtype=torch.float32, device=dev)
+        if want_cell_grad:
+            out["cell_grad"] = torch.empty(B, 3, 3, dtype=torch.float32, device=dev)
+        if want_edge_grad:
+            out["edge_grad"] = torch.empty(g.num_edges, 3, dtype=torch.float32, device=dev)
+        if energy_weight is not None:
+            energy_weight = energy_weight.detach().to(torch.float32).reshape(-1).contiguous()
+        gs = self._graph(pos, species, batch, cell, g, B, num_local, energy_weight)
+        o = N.IctdOutputs()
+        o.forces = out["forces"].data_ptr()
+        o.virial = out["virial"].data_ptr() if want_virial else 0
+        o.cell_grad = out["cell_grad"].data_ptr() if want_cell_grad else 0
+        o.edge_grad = out["edge_grad"].data_ptr() if want_edge_grad else 0
+        N.check(N.lib().fsc_ictd_backward(C.byref(self.ncfg), C.byref(self.weights.struct), C.byref(gs), C.byref(o),
+                                          N.ptr(ws), ws.numel(), N.stream_ptr(dev)), "fsc_ictd_backward")
+        return out
+
+    def energy_forces(self, pos, species, batch, cell, g: GraphCSR, num_local=None, want_stress=True):
+        energy, atom_e = self.forward(pos, species, batch, cell, g, num_local)
+        out = self.backward(want_virial=want_stress)
+        out["energy"] = energy
+        out["atom_energy"] = atom_e
+        if want_stress:
+            vol = torch.abs(torch.det(self._last[3].double())).clamp(min=1e-10).float()
+            v = out["virial"]
+            out["stress"] = 0.5 * (v + v.transpose(1, 2)) / vol.view(-1, 1, 1)
+        return out

@@ -1,0 +1,198 @@
+"""Drop-in ``PureCartesianICTDTransformerLayer`` (``--tensor-product-mode pure-cartesian-ictd``).
+
+Same constructor arguments, submodule names and ``state_dict`` keys/shapes as the reference
+``models/pure_cartesian_ictd_layers_full.py:476-866``, so a reference checkpoint loads with
+``load_state_dict``.  ``forward`` has the reference signature (``:867-886``) and returns the
+per-atom energy ``(N, 1)``; it is differentiable w.r.t. ``pos`` and ``cell`` through a custom
+autograd function whose backward is the native hand-written reverse pass (forces, and the
+cell gradient that the trainer's strain-based stress needs), so
+``torch.autograd.grad(E, pos)`` works as in ``evaluation/calculator.py:158-159``.
+
+Covered: lmax 2, path policy "full", channels 32/64, gaussian or bessel radial basis,
+no external tensor, no physical-tensor heads, no long-range / spectral modules, no
+``sync_after_scatter`` hook and no ``precomputed_edge_vec``.  Anything else raises
+``NotImplementedError`` (there is no CPU path to fall back to).
+"""
+
+from __future__ import annotations
+
+from typing import Dict, Optional
+
+import torch
+import torch.nn as nn
+
+from fsctep_b200.ictd import ICTDConfig, ICTDEngine, GraphCSR
+from fsctep_b200.tables import paths_full
+
+
+class _TP(nn.Module):
+    def __init__(self, num_paths, mul_out, mul_in1, mul_in2):
+        super().__init__()
+        self.weight = nn.Parameter(torch.randn(num_paths, mul_out, mul_in1, mul_in2) * 0.02)
+        self.num_paths = num_paths
+
+
+def _radial_mlp(nb, num_paths):
+    return nn.Sequential(nn.Linear(nb, 64), nn.SiLU(), nn.Linear(64, 64), nn.SiLU(), nn.Linear(64, num_paths))
+
+
+class _Conv1(nn.Module):
+    def __init__(self, cfg: ICTDConfig, num_paths):
+        super().__init__()
+        self.atom_embedding = nn.Embedding(cfg.max_atomvalue, cfg.embedding_dim)
+        self.atom_mlp = nn.Sequential(nn.Linear(cfg.embedding_dim, 64), nn.SiLU(), nn.Linear(64, cfg.output_size))
+        self.tp2 = _TP(num_paths, cfg.channels, cfg.output_size, cfg.output_size)
+        self.fc = _radial_mlp(cfg.number_of_basis, num_paths)
+
+
+class _MainNet(nn.Module):
+    def __init__(self, input_size, hidden_sizes, output_size):
+        super().__init__()
+        self.layers = nn.ModuleList()
+        self.layer_norms = nn.ModuleList()
+        self.input_norm = nn.LayerNorm(input_size)
+        sizes = [input_size] + list(hidden_sizes)
+        for a, b in zip(sizes[:-1], sizes[1:]):
+            self.layers.append(nn.Linear(a, b))
+            self.layer_norms.append(nn.LayerNorm(b))
+        self.output = nn.Linear(sizes[-1], output_size)
+        self.input_size = input_size
+
+
+class _WeightedSum(nn.Module):
+    def __init__(self, n):
+        super().__init__()
+        self.weights = nn.Parameter(torch.zeros(n))
+
+
+class _NativeEnergy(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, pos, cell, owner, graph, species, batch):
+        eng = owner._engine
+        _, atom_e = eng.forward(pos, species, batch, cell, graph)
+        ctx.owner, ctx.graph, ctx.species, ctx.batch = owner, graph, species, batch
+        ctx.generation = owner._bump()
+        ctx.save_for_backward(pos, cell)
+        ctx.pos_dtype, ctx.cell_dtype = pos.dtype, cell.dtype
+        return atom_e.view(-1, 1).to(pos.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_e):
+        pos, cell = ctx.saved_tensors
+        owner = ctx.owner
+        eng = owner._engine
+        if owner._generation != ctx.generation:  # another forward reused the workspace: recompute
+            eng.forward(pos, ctx.species, ctx.batch, cell, ctx.graph)
+            owner._generation = ctx.generation
+        out = eng.backward(energy_weight=grad_e.reshape(-1), want_virial=False,
+                           want_cell_grad=ctx.needs_input_grad[1])
+        gpos = (-out["forces"]).to(ctx.pos_dtype) if ctx.needs_input_grad[0] else None
+        gcell = out["cell_grad"].to(ctx.cell_dtype).reshape(cell.shape) if ctx.needs_input_grad[1] else None
+        return gpos, gcell, None, None, None, None
+
+
+class PureCartesianICTDTransformerLayer(nn.Module):
+    def __init__(self, max_embed_radius: float, main_max_radius: float, main_number_of_basis: int,
+                 hidden_dim_conv: int, hidden_dim_sh=None, hidden_dim=None, channel_in2: int = 32,
+                 embedding_dim: int = 16, max_atomvalue: int = 10, output_size: int = 8, embed_size=None,
+                 main_hidden_sizes3=None, num_layers: int = 1, num_interaction: int = 2, device=None,
+                 function_type_main: str = "gaussian", lmax: int = 2, ictd_Lmax: int = 6,
+                 ictd_tp_path_policy: str = "full", ictd_tp_max_rank_other=None, max_rank_other: int = 1,
+                 k_policy: str = "k0", internal_compute_dtype=None, ictd_tp_backend: str = "auto",
+                 product5_muls_by_l=None, invariant_channels: int = 32, physical_tensor_outputs=None,
+                 external_tensor_rank=None, external_tensor_irrep=None, external_tensor_parity=None,
+                 external_tensor_specs=None, num_fidelity_levels: int = 0, long_range_mode: str = "none",
+                 feature_spectral_mode: str = "none", **unused):
+        super().__init__()
+        if embed_size is None:
+            embed_size = [128, 128, 128]
+        unsupported = []
+        if ictd_tp_path_policy != "full":
+            unsupported.append(f"ictd_tp_path_policy={ictd_tp_path_policy!r}")
+        if int(lmax) != 2:
+            unsupported.append(f"lmax={lmax}")
+        if product5_muls_by_l is not None:
+            unsupported.append("product5_muls_by_l")
+        if physical_tensor_outputs:
+            unsupported.append("physical_tensor_outputs")
+        if external_tensor_rank is not None or external_tensor_specs:
+            unsupported.append("external tensors")
+        if num_fidelity_levels:
+            unsupported.append("multi-fidelity")
+        if long_range_mode != "none" or feature_spectral_mode != "none":
+            unsupported.append("long-range / spectral modules")
+        if int(num_interaction) < 2:
+            raise ValueError(f"num_interaction must be >= 2, got {num_interaction}")
+        if unsupported:
+            raise NotImplementedError("fsctep_b200 pure-cartesian-ictd does not cover: " + ", ".join(unsupported))
+        self.cfg = ICTDConfig(channels=int(hidden_dim_conv), lmax=int(lmax), num_interaction=int(num_interaction),
+                              number_of_basis=int(main_number_of_basis), max_radius=float(max_embed_radius),
+                              function_type=str(function_type_main), output_size=int(output_size),
+                              embedding_dim=int(embedding_dim), max_atomvalue=int(max_atomvalue),
+                              invariant_channels=int(invariant_channels), embed_size=tuple(embed_size))
+        self.cfg.native()  # validates the radial basis kind
+        self.lmax = int(lmax)
+        self.channels = int(hidden_dim_conv)
+        self.num_interaction = int(num_interaction)
+        self.max_radius = float(max_embed_radius)
+        self.number_of_basis = int(main_number_of_basis)
+        self.function_type = str(function_type_main)
+        self.invariant_channels = int(invariant_channels)
+        P = len(paths_full(self.lmax))
+        C, nint = self.channels, self.num_interaction
+        self.e3_conv_emb = _Conv1(self.cfg, P)
+        self.tp2_layers = nn.ModuleList([_TP(P, C, C, 1) for _ in range(nint - 1)])
+        self.fc2_layers = nn.ModuleList([_radial_mlp(self.number_of_basis, P) for _ in range(nint - 1)])
+        nC = C * nint
+        S = (nint - 1) * self.invariant_channels
+        self.W_read = nn.ParameterList([nn.Parameter(torch.randn(S, nC, nC) * 0.02) for _ in range(self.lmax + 1)])
+        self.readout_linear = nn.Sequential(nn.Linear(S + (self.lmax + 1) * nC, embed_size[0]), nn.SiLU(),
+                                            nn.Linear(embed_size[0], 17))
+        self.weighted_sum = _WeightedSum(17)
+        self.proj_total = _MainNet(nint * (self.lmax + 1) * C + S, embed_size, 17)
+        self._engine: Optional[ICTDEngine] = None
+        self._engine_key = None
+        self._generation = 0
+
+    def _bump(self):
+        self._generation += 1
+        return self._generation
+
+    def _ensure_engine(self, device):
+        key = (str(device),) + tuple((p.data_ptr(), p._version) for p in self.parameters())
+        if self._engine is None or self._engine_key != key:
+            self._engine = ICTDEngine({k: v.detach() for k, v in self.state_dict().items()}, self.cfg, device)
+            self._engine_key = key
+        return self._engine
+
+    def forward(self, pos, A, batch, edge_src, edge_dst, edge_shifts, cell, *, precomputed_edge_vec=None,
+                sync_after_scatter=None, external_tensor=None, external_tensor_blocks=None, fidelity_ids=None,
+                return_physical_tensors: bool = False, return_reciprocal_source: bool = False):
+        if precomputed_edge_vec is not None or sync_after_scatter is not None or external_tensor is not None \
+                or external_tensor_blocks is not None or return_physical_tensors or return_reciprocal_source:
+            raise NotImplementedError("fsctep_b200 pure-cartesian-ictd forward covers (pos, A, batch, edges, cell) "
+                                      "with no optional inputs")
+        if not pos.is_cuda:
+            raise RuntimeError("fsctep_b200 runs on CUDA devices only (no CPU path)")
+        n = pos.shape[0]
+        species = A.long()
+        if n and int(species.max().item()) >= self.cfg.max_atomvalue:
+            raise IndexError("atomic number out of range of atom_embedding (max_atomvalue)")
+        cell = cell.reshape(-1, 3, 3)
+        if n and int(batch.max().item()) >= cell.shape[0]:
+            raise IndexError("batch index out of range of cell")
+        self._ensure_engine(pos.device)
+        graph = GraphCSR.from_edges(edge_src.long(), edge_dst.long(), edge_shifts, n)
+        return _NativeEnergy.apply(pos, cell, self, graph, species, batch)
+
+
+def reference_state_dict_shapes(cfg: ICTDConfig) -> Dict[str, tuple]:
+    """Shapes of the reference state_dict for a config (for seeded synthetic weights)."""
+    with torch.device("meta"):
+        m = PureCartesianICTDTransformerLayer(
+            max_embed_radius=cfg.max_radius, main_max_radius=cfg.max_radius,
+            main_number_of_basis=cfg.number_of_basis, hidden_dim_conv=cfg.channels, lmax=cfg.lmax,
+            num_interaction=cfg.num_interaction, function_type_main=cfg.function_type,
+            max_atomvalue=cfg.max_atomvalue, embedding_dim=cfg.embedding_dim, output_size=cfg.output_size,
+            invariant_channels=cfg.invariant_channels, embed_size=list(cfg.embed_size))
+    return {k: tuple(v.shape) for k, v in m.state_dict().items()}

@@ -1,0 +1,73 @@
+"""GPU neighbour list with the semantics of ``radius_graph_pbc_gpu`` (``utils/graph_utils.py:192-258``).
+
+``build_graph`` runs the native count + fill (cell list for large periodic orthorhombic
+frames, all-pairs otherwise; identical edge sets, float64 distance test in a fixed order)
+and the transpose CSR, returning a ``GraphCSR`` ready for ``ICTDEngine``.
+``radius_graph_pbc`` returns the flat ``(edge_src, edge_dst, edge_shifts)`` triple of the
+reference function (canonical order: dst, then src, then shift).
+"""
+
+from __future__ import annotations
+
+from typing import Sequence
+
+import numpy as np
+import torch
+
+from fsctep_b200 import _native as N
+from fsctep_b200.ictd import GraphCSR
+
+
+def _sidx_to_shift(sidx: torch.Tensor) -> torch.Tensor:
+    s = sidx.to(torch.int32)
+    return torch.stack([s // 9 - 1, (s // 3) % 3 - 1, s % 3 - 1], dim=1)
+
+
+def build_graph(pos: torch.Tensor, cell: torch.Tensor, cutoff: float, frame_ptr: Sequence[int] = None,
+                pbc=(True, True, True)) -> GraphCSR:
+    """pos (N,3) and cell (F,3,3) on the GPU (float64 used for the distance test)."""
+    dev = pos.device
+    pos64 = pos.detach().to(torch.float64).contiguous()
+    cell64 = cell.detach().to(device=dev, dtype=torch.float64).reshape(-1, 3, 3).contiguous()
+    n = int(pos64.shape[0])
+    F = int(cell64.shape[0])
+    if frame_ptr is None:
+        if F != 1:
+            raise ValueError("frame_ptr is required with more than one cell")
+        frame_ptr = [0, n]
+    fp = np.ascontiguousarray(np.asarray(frame_ptr, dtype=np.int64))
+    pbc_h = np.ascontiguousarray(np.asarray([1 if p else 0 for p in pbc], dtype=np.int32))
+    L = N.lib()
+    st = N.stream_ptr(dev)
+    row_ptr = torch.empty(n + 1, dtype=torch.int32, device=dev)
+    ws = torch.empty(L.fsc_neighbor_workspace_bytes(n, 0), dtype=torch.uint8, device=dev)
+    ne = N.I64(0)
+    N.check(L.fsc_neighbor_count(N.ptr(pos64), N.ptr(cell64), fp.ctypes.data_as(N.P), F, n,
+                                 pbc_h.ctypes.data_as(N.P), float(cutoff), N.ptr(row_ptr), N.C.byref(ne),
+                                 N.ptr(ws), ws.numel(), st), "fsc_neighbor_count")
+    E = int(ne.value)
+    src = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
+    sidx = torch.empty(max(E, 1), dtype=torch.int8, device=dev)
+    need = L.fsc_neighbor_workspace_bytes(n, E)
+    if ws.numel() < need:
+        ws = torch.empty(need, dtype=torch.uint8, device=dev)
+    N.check(L.fsc_neighbor_fill(N.ptr(pos64), N.ptr(cell64), fp.ctypes.data_as(N.P), F, n,
+                                pbc_h.ctypes.data_as(N.P), float(cutoff), N.ptr(row_ptr), N.ptr(src), N.ptr(sidx), E,
+                                N.ptr(ws), ws.numel(), st), "fsc_neighbor_fill")
+    src, sidx = src[:E], sidx[:E]
+    shift = _sidx_to_shift(sidx).to(torch.float32).contiguous()
+    tr_ptr, tr_eid = GraphCSR.transpose(row_ptr, src, n)
+    g = GraphCSR(n, row_ptr, src, shift, tr_ptr, tr_eid)
+    g.sidx = sidx
+    return g
+
+
+def radius_graph_pbc(pos: torch.Tensor, r: float, cell: torch.Tensor, pbc=None, frame_ptr=None):
+    """(edge_src, edge_dst, edge_shifts) like the reference, canonical order, int64 / float64."""
+    if pbc is None:
+        pbc = (True, True, True)
+    g = build_graph(pos, cell, r, frame_ptr, pbc)
+    dev = pos.device
+    counts = (g.row_ptr[1:] - g.row_ptr[:-1]).to(torch.int64)
+    dst = torch.repeat_interleave(torch.arange(g.num_atoms, device=dev), counts)
+    return g.src.to(torch.int64), dst, _sidx_to_shift(g.sidx).to(torch.float64)

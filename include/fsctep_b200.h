@@ -1,0 +1,267 @@
+/*
+ * fsctep_b200 -- C ABI of the B200-native (sm_100a) FSCTEP message-passing hot path.
+ *
+ * Everything here takes plain pointers and sizes: no torch types.  All data
+ * pointers are DEVICE pointers unless a comment says otherwise; `stream` is a
+ * cudaStream_t passed as void* (NULL = legacy default stream).  Every function
+ * returns an fsc_status; on failure fsc_last_error() gives a message (per host
+ * thread).  Nothing in this library allocates device memory: callers pass
+ * outputs and workspaces they own (sizes from the *_workspace_bytes queries).
+ *
+ * Reference interfaces replaced (paths inside the Parity-LRX/FSCTEP project):
+ *   - the `_C_ictd_tp` pybind operator family       csrc/ictd_tp.cpp:498-523
+ *   - the per-edge TP layers + autograd force/virial pure_cartesian_ictd_layers_full.py:867-1078,
+ *     evaluation/calculator.py:152-159, training/trainer.py:1213-1310
+ *   - the LibTorch engine E/F/virial call           lammps_user_mfftorch/src/USER-MFFTORCH/
+ *                                                   mff_torch_engine.cpp:740-864 (MFFTorchEngine::compute)
+ *   - the neighbour search                          utils/graph_utils.py:192-258 (radius_graph_pbc_gpu)
+ */
+#ifndef FSCTEP_B200_H
+#define FSCTEP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  FSC_OK = 0,
+  FSC_ERR_ARGUMENT = 1,     /* bad shape / pointer / unsupported size        */
+  FSC_ERR_CUDA = 2,         /* a CUDA runtime call or kernel launch failed   */
+  FSC_ERR_UNSUPPORTED = 3,  /* configuration outside what the kernels cover  */
+  FSC_ERR_CAPACITY = 4      /* an output buffer is too small (see message)   */
+} fsc_status;
+
+typedef enum { FSC_F32 = 0, FSC_F64 = 1 } fsc_dtype;
+
+/* ---- library ------------------------------------------------------------ */
+const char* fsc_last_error(void);
+int fsc_version(void);
+/* 1 when the library was built with its CUDA kernels (always, for this build).
+ * Replaces `_C_ictd_tp.has_cuda()` (csrc/ictd_tp.cpp:516-522). */
+int fsc_has_cuda(void);
+
+/* ---- `_C_ictd_tp` operator family (csrc/ictd_tp.cpp:137-497) -------------
+ * Shapes follow the reference TORCH_CHECKs (csrc/ictd_tp.cpp:78-108):
+ *   a (B, I, m1), b (B, J, m2), u (m1*m2, P*K), y (B, P, K, I*J),
+ *   w (P, O, I*J), gates (B, P), out (B, O, K).  All C-contiguous.
+ * J (mul_in2) may be any value >= 1 (the reference CUDA path needs J == 1).
+ * Outputs are fully overwritten (no accumulation).                           */
+int fsc_project_bucket_forward(int dtype, const void* a, const void* b, const void* u, void* y,
+                               int64_t B, int64_t I, int64_t J, int64_t m1, int64_t m2,
+                               int64_t P, int64_t K, void* stream);        /* ictd_tp.cpp:137 */
+int fsc_project_bucket_transpose_a(int dtype, const void* grad_y, const void* b, const void* u,
+                                   void* grad_a, int64_t B, int64_t I, int64_t J, int64_t m1,
+                                   int64_t m2, int64_t P, int64_t K, void* stream); /* :175 */
+int fsc_project_bucket_transpose_b(int dtype, const void* grad_y, const void* a, const void* u,
+                                   void* grad_b, int64_t B, int64_t I, int64_t J, int64_t m1,
+                                   int64_t m2, int64_t P, int64_t K, void* stream); /* :210 */
+int fsc_project_bucket_transpose_u(int dtype, const void* grad_y, const void* a, const void* b,
+                                   void* grad_u, int64_t B, int64_t I, int64_t J, int64_t m1,
+                                   int64_t m2, int64_t P, int64_t K, void* stream); /* :242 */
+int fsc_mix_bucket_forward(int dtype, const void* y, const void* w, const void* gates, void* out,
+                           int64_t B, int64_t P, int64_t K, int64_t IJ, int64_t O,
+                           void* stream);                                  /* :270 */
+int fsc_mix_bucket_transpose_y(int dtype, const void* grad_out, const void* w, const void* gates,
+                               void* grad_y, int64_t B, int64_t P, int64_t K, int64_t IJ,
+                               int64_t O, void* stream);                   /* :293 */
+int fsc_mix_bucket_transpose_w(int dtype, const void* grad_out, const void* y, const void* gates,
+                               void* grad_w, int64_t B, int64_t P, int64_t K, int64_t IJ,
+                               int64_t O, void* stream);                   /* :322 */
+int fsc_mix_bucket_transpose_g(int dtype, const void* grad_out, const void* y, const void* w,
+                               void* grad_g, int64_t B, int64_t P, int64_t K, int64_t IJ,
+                               int64_t O, void* stream);                   /* :346 */
+/* y-free fused forward of one same-kdim bucket: out = mix(project(a,b,u), w, gates) (:372). */
+int fsc_bucketed_tp_forward(int dtype, const void* a, const void* b, const void* u, const void* w,
+                            const void* gates, void* out, int64_t B, int64_t I, int64_t J,
+                            int64_t m1, int64_t m2, int64_t P, int64_t K, int64_t O, void* stream);
+/* Double-backward fused terms (ictd_tp.cpp:387-495, ictd_tp_cuda.cu:528-534, 780-786):
+ *   grad_h  = PF(gga,b,u) + PF(a,ggb,u) + PF(a,b,ggu)        -> (B,P,K,I*J)
+ *   grad_a2 = PAT(h,ggb,u) + PAT(h,b,ggu)                    -> (B,I,m1)
+ *   grad_b2 = PBT(h,gga,u) + PBT(h,a,ggu)                    -> (B,J,m2)
+ *   grad_u2 = PUT(h,gga,b) + PUT(h,a,ggb)                    -> (m1*m2,P*K)
+ *   grad_g_out = MF(ggy,w,g) + MF(y,ggw,g) + MF(y,w,ggg)     -> (B,O,K)
+ *   grad_y2 = MYT(g_out,ggw,g) + MYT(g_out,w,ggg)            -> (B,P,K,IJ)
+ *   grad_w2 = MWT(g_out,ggy,g) + MWT(g_out,y,ggg)            -> (P,O,IJ)
+ *   grad_g2 = MGT(g_out,ggy,w) + MGT(g_out,y,ggw)            -> (B,P)              */
+int fsc_project_dbl_bwd_grad_h(int dtype, const void* a, const void* gga, const void* b,
+                               const void* ggb, const void* u, const void* ggu, void* out,
+                               int64_t B, int64_t I, int64_t J, int64_t m1, int64_t m2,
+                               int64_t P, int64_t K, void* stream);
+int fsc_project_dbl_bwd_grad_a(int dtype, const void* h, const void* b, const void* ggb,
+                               const void* u, const void* ggu, void* out, int64_t B, int64_t I,
+                               int64_t J, int64_t m1, int64_t m2, int64_t P, int64_t K,
+                               void* stream);
+int fsc_project_dbl_bwd_grad_b(int dtype, const void* h, const void* a, const void* gga,
+                               const void* u, const void* ggu, void* out, int64_t B, int64_t I,
+                               int64_t J, int64_t m1, int64_t m2, int64_t P, int64_t K,
+                               void* stream);
+int fsc_project_dbl_bwd_grad_u(int dtype, const void* h, const void* a, const void* gga,
+                               const void* b, const void* ggb, void* out, int64_t B, int64_t I,
+                               int64_t J, int64_t m1, int64_t m2, int64_t P, int64_t K,
+                               void* stream);
+int fsc_mix_dbl_bwd_grad_g_out(int dtype, const void* y, const void* ggy, const void* w,
+                               const void* ggw, const void* gates, const void* ggg, void* out,
+                               int64_t B, int64_t P, int64_t K, int64_t IJ, int64_t O,
+                               void* stream);
+int fsc_mix_dbl_bwd_grad_y(int dtype, const void* g_out, const void* w, const void* ggw,
+                           const void* gates, const void* ggg, void* out, int64_t B, int64_t P,
+                           int64_t K, int64_t IJ, int64_t O, void* stream);
+int fsc_mix_dbl_bwd_grad_w(int dtype, const void* g_out, const void* y, const void* ggy,
+                           const void* gates, const void* ggg, void* out, int64_t B, int64_t P,
+                           int64_t K, int64_t IJ, int64_t O, void* stream);
+int fsc_mix_dbl_bwd_grad_g(int dtype, const void* g_out, const void* y, const void* ggy,
+                           const void* w, const void* ggw, void* out, int64_t B, int64_t P,
+                           int64_t K, int64_t IJ, int64_t O, void* stream);
+
+/* ---- neighbour list (utils/graph_utils.py:192-258) ------------------------
+ * Edges (src=i, dst=j, S) with |(pos[j] + S@cell) - pos[i]| < cutoff, S in
+ * {-1,0,1}^3 on periodic axes ({0} on open ones), no self pair at S = 0;
+ * float64 arithmetic in the fixed order documented in oracle/neighbors.py.
+ * Output is a CSR by dst: row_ptr[N+1]; per edge src[e] and the packed image
+ * index sidx[e] = (S0+1)*9 + (S1+1)*3 + (S2+1); rows sorted by (src, sidx).
+ * Frames: atoms of frame g are [frame_ptr[g], frame_ptr[g+1]) (host array);
+ * edges never cross frames.  `cell` is [num_frames][3][3] (device), rows =
+ * lattice vectors.  The builder uses a cell list when a frame is periodic and
+ * orthorhombic with all positions inside [0, L), else an all-pairs search.
+ * Two phases: count (fills row_ptr, returns the edge count in *num_edges,
+ * host; workspace >= fsc_neighbor_workspace_bytes(N, 0)) then fill (needs
+ * capacity >= *num_edges and workspace >= fsc_neighbor_workspace_bytes(N, E)).
+ * Both phases synchronise `stream` (the edge count is read back to the host). */
+size_t fsc_neighbor_workspace_bytes(int64_t num_atoms, int64_t num_edges);
+/* pos [N][3] (device), cell [num_frames][3][3] (device); pbc_host[3] (host). */
+int fsc_neighbor_count(const double* pos, const double* cell, const int64_t* frame_ptr_host,
+                       int64_t num_frames, int64_t num_atoms, const int32_t* pbc_host,
+                       double cutoff, int32_t* row_ptr, int64_t* num_edges_host,
+                       void* workspace, size_t workspace_bytes, void* stream);
+int fsc_neighbor_fill(const double* pos, const double* cell, const int64_t* frame_ptr_host,
+                      int64_t num_frames, int64_t num_atoms, const int32_t* pbc_host,
+                      double cutoff, const int32_t* row_ptr, int32_t* src, int8_t* sidx,
+                      int64_t capacity, void* workspace, size_t workspace_bytes, void* stream);
+/* Transpose CSR (edges grouped by src, ascending edge id within a group). */
+size_t fsc_csr_transpose_workspace_bytes(int64_t num_atoms, int64_t num_edges);
+int fsc_csr_transpose(const int32_t* row_ptr, const int32_t* src, int64_t num_atoms,
+                      int64_t num_edges, int32_t* tr_ptr, int32_t* tr_eid, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* ---- pure-cartesian-ictd energy + forces + virial -------------------------
+ * One call = PureCartesianICTDTransformerLayer forward (pure_cartesian_ictd_layers_full.py:
+ * 867-1078) followed by a hand-written backward giving dE/dpos and the per-edge
+ * dE/dr (no autograd replay).  Covers lmax = 2, path_policy "full",
+ * channels 32 or 64, any num_interaction in [2, 8], number_of_basis <= 16,
+ * radial basis gaussian/bessel, MainNet with up to 4 hidden layers, no external
+ * tensor, no physical heads, no long-range module.                           */
+typedef struct {
+  int32_t channels;          /* C (hidden_dim_conv): 32 or 64                    */
+  int32_t lmax;              /* must be 2                                        */
+  int32_t num_interaction;   /* 2..8                                             */
+  int32_t number_of_basis;   /* radial basis size, <= 16                         */
+  int32_t basis_kind;        /* 0 = gaussian, 1 = bessel                         */
+  float max_radius;          /* cutoff of the radial basis                       */
+  int32_t num_species;       /* max_atomvalue (rows of the per-species tables)  */
+  int32_t output_size;       /* conv1 scalar width, must be 8                    */
+  int32_t invariant_channels;/* readout scalar channels per extra interaction   */
+  int32_t n_hidden;          /* MainNet hidden layers, 1..4                      */
+  int32_t hidden[4];         /* MainNet hidden sizes (<= 1024)                   */
+  int32_t n_out;             /* MainNet output width (17)                        */
+} fsc_ictd_config;
+
+/* Packed fp32 device weights.  The host side derives them from the reference
+ * state_dict (key names in comments); layouts are row-major.
+ *   P = 11 paths, nint = num_interaction, nb = number_of_basis, C = channels,
+ *   nC = C*nint, S = (nint-1)*invariant_channels, npairs = nC*(nC+1)/2.   */
+typedef struct {
+  const float* tables;   /* ictd tables, fsc_ictd_tables_floats() floats: Y polynomials,
+                            conv2 CG (115x5), conv1 CG (9x5), product_5 factors (3)       */
+  const float* ai;       /* [num_species][8]   atom_mlp(atom_embedding(Z))                 */
+  const float* vsp;      /* [num_species][3][8][C]  V[s][l][i][o] = sum_j e3_conv_emb.tp2.weight[p(l,0,l),o,i,j]*ai[s,j] */
+  const float* rad_w1;   /* [nint][64][nb]   fc.0 / fc2_layers.k.0 weight                  */
+  const float* rad_b1;   /* [nint][64]                                                      */
+  const float* rad_w2;   /* [nint][64][64]   fc.2 / fc2_layers.k.2                          */
+  const float* rad_b2;   /* [nint][64]                                                      */
+  const float* rad_w3;   /* [nint][11][64]   fc.4 / fc2_layers.k.4                          */
+  const float* rad_b3;   /* [nint][11]                                                      */
+  /* Channel mixes of conv2..N (tp2_layers.k.weight W[p][o][i]), 11*C*C floats per layer,
+   * three blocks per layer for l3 (l1) = 0, 1, 2 holding the paths with that l3 (l1) in
+   * path order (P3 = P1 = {3, 4, 4} paths):                                                 */
+  const float* mix_fwd;  /* [nint-1] x blocks [(rank,i)][o] = W[p_rank][o][i]                */
+  const float* mix_bwd;  /* [nint-1] x blocks [o][(rank,i)] = W[p_rank][o][i]                */
+  const float* mix_dx;   /* [nint-1] x blocks (by l1) [(rank,o)][i] = W[p_rank][o][i]        */
+  const float* wread_p;  /* [3][S][npairs]   W_read.l symmetrised, upper-triangle packed,
+                                             off-diagonal doubled, scaled 1/sqrt(2l+1)    */
+  const float* wread_s;  /* [3][S][nC][nC]   W_read.l symmetrised (W+W^T)/2, scaled 1/sqrt(2l+1) */
+  const int32_t* pairs;  /* [npairs] packed (c | d<<16), c <= d, row-major upper triangle       */
+  /* The Gram invariants read t_l[c][m] = F[off_l + c*(2l+1) + m] from the flat concatenation
+   * F of all layers' features in the reference layout (pure_cartesian_ictd_layers_full.py:
+   * 956-958 splits torch.cat(features) into l blocks of nC*(2l+1)); off_l = 0, nC, 4nC.
+   * xmap[off_l + c*(2l+1) + m] = (layer << 16) | (k*C + channel) locates that element in
+   * the [N][9][C] feature buffers.                                                          */
+  const int32_t* xmap;   /* [9*nC]                                                          */
+  const float* mn_in_g;  /* [D0]  proj_total.input_norm.weight, D0 = 3*nC + S             */
+  const float* mn_in_b;  /* [D0]  proj_total.input_norm.bias                              */
+  const float* mn_w[4];  /* [hidden[k]][in_k]  proj_total.layers.k.weight (as stored)      */
+  const float* mn_b[4];  /* [hidden[k]]        proj_total.layers.k.bias                    */
+  const float* mn_g[4];  /* [hidden[k]]        proj_total.layer_norms.k.weight            */
+  const float* mn_beta[4];/* [hidden[k]]       proj_total.layer_norms.k.bias              */
+  /* proj_total.output followed by weighted_sum collapse to one dot product:
+   *   e = x_last . out_v + out_c0,  out_v = output.weight^T weighted_sum.weights,
+   *   out_c0 = output.bias . weighted_sum.weights                                        */
+  const float* out_v;    /* [hidden[last]]                                                  */
+  float out_c0;
+} fsc_ictd_weights;
+
+/* Number of floats in the `tables` block. */
+int64_t fsc_ictd_tables_floats(void);
+
+typedef struct {
+  int64_t num_atoms;        /* N (owned + ghost)                                     */
+  int64_t num_local;        /* energy = sum over atoms [0, num_local)                */
+  int64_t num_edges;        /* E                                                     */
+  int64_t num_graphs;       /* B                                                     */
+  const float* pos;         /* [N][3]                                                */
+  const int32_t* species;   /* [N] atomic numbers, < num_species                     */
+  const int32_t* batch;     /* [N] graph of each atom                                */
+  const float* cell;        /* [B][3][3] rows = lattice vectors                      */
+  const int32_t* row_ptr;   /* [N+1] CSR by dst                                      */
+  const int32_t* src;       /* [E] edge sources, sorted by dst                       */
+  const float* shift;       /* [E][3] integer image shift S (as float), r = pos[dst]-pos[src]+S@cell[batch[src]] */
+  const int32_t* tr_ptr;    /* [N+1] CSR by src                                      */
+  const int32_t* tr_eid;    /* [E] edge ids grouped by src                           */
+  const float* energy_weight;/* [N] or NULL: backward seed dL/de_n; NULL = 1 for atoms
+                                [0, num_local), 0 for the rest (LAMMPS ghost convention,
+                                mff_torch_engine.cpp:812-820)                           */
+} fsc_graph;
+
+typedef struct {
+  float* energy;            /* [B] per-graph energy (sum of atom energies, local atoms) */
+  float* atom_energy;       /* [N] or NULL                                            */
+  float* forces;            /* [N][3] = -dE/dpos                                      */
+  float* virial;            /* [B][9] or NULL: sum_e r_e (x) dE/dr_e (row-major a,b)  */
+  float* edge_grad;         /* [E][3] or NULL: dE/dr_e per edge (LAMMPS atom virial)  */
+  float* cell_grad;         /* [B][9] or NULL: dE/dcell = sum_e S_e (x) dE/dr_e        */
+} fsc_ictd_outputs;
+
+size_t fsc_ictd_workspace_bytes(const fsc_ictd_config* cfg, int64_t num_atoms, int64_t num_edges);
+int fsc_ictd_energy_forces(const fsc_ictd_config* cfg, const fsc_ictd_weights* w,
+                           const fsc_graph* g, fsc_ictd_outputs* out, void* workspace,
+                           size_t workspace_bytes, void* stream);
+/* The same call split in two: forward leaves its intermediates in `workspace`;
+ * backward (same cfg, weights, graph and workspace, no other call on that workspace
+ * in between) produces the outputs' forces / virial / edge_grad / cell_grad with the
+ * seed graph->energy_weight.  This pair is what an autograd wrapper binds. */
+int fsc_ictd_forward(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g,
+                     float* energy, float* atom_energy, void* workspace, size_t workspace_bytes,
+                     void* stream);
+int fsc_ictd_backward(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g,
+                      fsc_ictd_outputs* out, void* workspace, size_t workspace_bytes, void* stream);
+/* Forward only (per-atom energy), same workspace. */
+int fsc_ictd_energy(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g,
+                    float* energy, float* atom_energy, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FSCTEP_B200_H */

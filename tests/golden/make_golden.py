@@ -168,9 +168,12 @@ def main():
     cfg_a = dict(channels=32, lmax=2, num_interaction=2, number_of_basis=8, max_radius=5.0,
                  function_type="bessel", max_atomvalue=10)
     model_case("a", systems.random_frames(n_frames=2, n_atoms=96, box=10.0, seed=11), cfg_a, seed=1)
-    cfg_b = dict(channels=16, lmax=2, num_interaction=3, number_of_basis=8, max_radius=5.0,
+    cfg_b = dict(channels=32, lmax=2, num_interaction=3, number_of_basis=8, max_radius=5.0,
                  function_type="gaussian", max_atomvalue=16)
     model_case("b", systems.diamond_crystal(n_cells=(2, 2, 2), seed=12), cfg_b, seed=2)
+    cfg_c = dict(channels=64, lmax=2, num_interaction=3, number_of_basis=8, max_radius=5.0,
+                 function_type="gaussian", max_atomvalue=16)
+    model_case("c", systems.diamond_crystal(n_cells=(2, 2, 2), seed=13, sigma=0.15), cfg_c, seed=3)
 
 
 if __name__ == "__main__":

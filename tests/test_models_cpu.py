@@ -1,0 +1,35 @@
+"""Host-side checks of the drop-in module (no GPU): state_dict layout identical to the reference."""
+
+import pytest
+import torch
+
+import golden_io
+from fsctep_b200.ictd import ICTDConfig
+from fsctep_b200.models import PureCartesianICTDTransformerLayer, reference_state_dict_shapes
+
+
+@pytest.mark.parametrize("tag", ["a", "b", "c"])
+def test_state_dict_keys_and_shapes_match_reference(tag):
+    z = golden_io.load(f"ictd_model_{tag}.npz")
+    ref = {k[len("sdshape/"):]: tuple(int(x) for x in z[k]) for k in z.files if k.startswith("sdshape/")}
+    cfg = ICTDConfig(channels=int(z["cfg_channels"]), num_interaction=int(z["cfg_num_interaction"]),
+                     function_type=str(z["cfg_function_type"]), max_atomvalue=int(z["cfg_max_atomvalue"]))
+    assert reference_state_dict_shapes(cfg) == ref
+
+
+def test_loads_reference_state_dict():
+    cfg, sd, _ = golden_io.model_case("a")
+    m = PureCartesianICTDTransformerLayer(max_embed_radius=5.0, main_max_radius=5.0, main_number_of_basis=8,
+                                          hidden_dim_conv=32, num_interaction=2, function_type_main="bessel")
+    m.load_state_dict({k: v.float() for k, v in sd.items()})
+
+
+def test_unsupported_options_raise():
+    with pytest.raises(NotImplementedError):
+        PureCartesianICTDTransformerLayer(5.0, 5.0, 8, 32, external_tensor_rank=1)
+    with pytest.raises(NotImplementedError):
+        PureCartesianICTDTransformerLayer(5.0, 5.0, 8, 32, function_type_main="fourier")
+    m = PureCartesianICTDTransformerLayer(5.0, 5.0, 8, 32)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m(torch.zeros(2, 3), torch.ones(2).long(), torch.zeros(2).long(), torch.zeros(1).long(),
+          torch.ones(1).long(), torch.zeros(1, 3), torch.eye(3)[None])

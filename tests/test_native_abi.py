@@ -1,0 +1,48 @@
+"""CPU-side checks of the C ABI: the library loads and exports every declared entry point."""
+
+import os
+import re
+
+import pytest
+
+from fsctep_b200 import _native as N
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    src = open(os.path.join(ROOT, "include", "fsctep_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(fsc_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_and_binding_agree():
+    assert _declared() == N.exported_symbols()
+
+
+def test_library_exports_every_declared_symbol():
+    lib = N.lib()
+    for name in _declared():
+        assert hasattr(lib, name), name
+
+
+def test_library_queries_without_gpu():
+    lib = N.lib()
+    assert lib.fsc_has_cuda() == 1
+    assert lib.fsc_ictd_tables_floats() == 720
+    assert lib.fsc_neighbor_workspace_bytes(1000, 0) > 0
+
+
+def test_unsupported_config_reports_zero_workspace():
+    import ctypes
+    cfg = N.IctdConfig(channels=48, lmax=2, num_interaction=3, number_of_basis=8, basis_kind=0, max_radius=5.0,
+                       num_species=10, output_size=8, invariant_channels=32, n_hidden=1, n_out=17)
+    cfg.hidden[0] = 128
+    assert N.lib().fsc_ictd_workspace_bytes(ctypes.byref(cfg), 10, 10) == 0
+
+
+def test_argument_errors_are_reported_not_raised_in_c():
+    # a bad dtype is rejected before any device work
+    st = N.lib().fsc_project_bucket_forward(7, None, None, None, None, 1, 1, 1, 1, 1, 1, 1, None)
+    assert st == 1
+    assert b"dtype" in N.lib().fsc_last_error()
