@@ -1,0 +1,339 @@
+"""Benchmark: atom-steps/s of pure-cartesian-ictd energy + forces on B200.
+
+Workload ("si1m"): pure-cartesian-ictd, 3 interaction layers, 64 channels,
+lmax 2, fp32, cutoff 5.0 A, 8 gaussian radial functions (the CLI default basis); a periodic
+diamond-lattice Si crystal of 1,000,000 atoms (50^3 conventional cells x 8 atoms, a = 5.43 A,
+Gaussian displacements sigma = 0.08 A), seeded synthetic positions and seeded random weights.
+One step = one MD-style evaluation: GPU neighbour list (cell list, bit-exact with the
+reference semantics) + forward + hand-written backward (energy, forces).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+
+``--impl reference`` times the reference algorithm's CPU path (the oracle port of the
+reference PyTorch implementation, fp32, all host threads) on a bounded replica of the same
+workload.  Under torchrun (N > 1) every rank runs its own replica of the workload
+(independent systems, no data-path collective); the reported value is the sum over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+WORKLOADS = {
+    "si1m": dict(cells=(50, 50, 50), channels=64, num_interaction=3, Z=14, max_atomvalue=16),
+    "si64k": dict(cells=(20, 20, 20), channels=64, num_interaction=3, Z=14, max_atomvalue=16),
+}
+CPU_SAMPLE_CELLS = (6, 6, 6)  # 1,728-atom replica of the same crystal for the CPU baseline
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def model_cfg(w):
+    from fsctep_b200.ictd import ICTDConfig
+
+    return ICTDConfig(channels=w["channels"], num_interaction=w["num_interaction"], number_of_basis=8,
+                      max_radius=5.0, function_type="gaussian", max_atomvalue=w["max_atomvalue"])
+
+
+def seeded_weights(cfg, seed=2024):
+    from fsctep_b200.models import reference_state_dict_shapes
+    from fsctep_b200.weights import seeded_state_dict
+
+    return seeded_state_dict(reference_state_dict_shapes(cfg), seed)
+
+
+class ClockSampler:
+    """nvidia-smi clocks during the timed region (one GPU)."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(max(smax)), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def algorithmic_work(stage, N, E, cfg):
+    """(flops, bytes) per launch of a stage, from the per-unit figures of the hot path."""
+    C, nint = cfg.channels, cfg.num_interaction
+    nC = C * nint
+    S = (nint - 1) * cfg.invariant_channels
+    npairs = nC * (nC + 1) // 2
+    table = {
+        # packed Gram contraction: 2*S per pair per node, 3 l blocks (+ Gram build)
+        "readout_gram_forward": (N * 3 * (2.0 * S * npairs) + N * 2.0 * npairs * 9, N * 9 * nC * 4.0),
+        "readout_gram_backward": (N * 3 * (2.0 * S * nC * nC) + N * 2.0 * nC * nC * 9, N * 9 * nC * 8.0),
+        # TP contraction: 115 MACs per channel per edge
+        "conv2_edge_forward": (2.0 * E * C * 115, N * 9 * C * 4.0 + N * 35 * C * 4.0 + E * 100.0),
+        "conv2_edge_backward_gates": (2.0 * E * C * 115, N * 9 * C * 4.0 + N * 35 * C * 4.0 + E * 100.0),
+        "conv2_edge_backward_x": (2.0 * E * C * 115, N * 9 * C * 4.0 + N * 35 * C * 4.0 + E * 100.0),
+        "edge_forward": (E * nint * 2.0 * (8 * 64 + 64 * 64 + 64 * 11), E * (12 + 48 + nint * 48.0)),
+        "edge_backward": (E * nint * 4.0 * (8 * 64 + 64 * 64 + 64 * 11), E * (48 + 48 + nint * 48.0 + 12)),
+    }
+    return table.get(stage)
+
+
+def run_native(args, rank, world, device):
+    from fsctep_b200 import _native as NAT
+    from fsctep_b200 import systems
+    from fsctep_b200.ictd import ICTDEngine
+    from fsctep_b200.neighbors import build_graph
+
+    w = WORKLOADS[args.workload]
+    cfg = model_cfg(w)
+    sysd = systems.diamond_crystal(n_cells=w["cells"], seed=1000 + rank, Z=w["Z"])
+    n = sysd["pos"].shape[0]
+    eng = ICTDEngine(seeded_weights(cfg), cfg, device)
+    pos_d = torch.tensor(sysd["pos"], device=device)
+    cell_d = torch.tensor(sysd["cell"], device=device)
+    Z = torch.tensor(sysd["Z"], device=device, dtype=torch.int32)
+    batch = torch.zeros(n, device=device, dtype=torch.int32)
+    pos_h = torch.tensor(sysd["pos"]).pin_memory()
+    forces_h = torch.empty(n, 3, dtype=torch.float32).pin_memory()
+    energy_h = torch.empty(1, dtype=torch.float32).pin_memory()
+
+    def step(pos, cell):
+        g = build_graph(pos, cell, cfg.max_radius)
+        energy, _ = eng.forward(pos, Z, batch, cell, g)
+        out = eng.backward(want_virial=False)
+        return energy, out["forces"], g
+
+    def e2e_step():
+        pos = pos_h.to(device, non_blocking=True)
+        energy, forces, g = step(pos, cell_d)
+        forces_h.copy_(forces, non_blocking=True)
+        energy_h.copy_(energy, non_blocking=True)
+        return g
+
+    for _ in range(args.warmup):
+        _, _, g = step(pos_d, cell_d)
+    torch.cuda.synchronize()
+    E_edges = g.num_edges
+
+    # kernel launches per step (counted once, outside the timed region)
+    ours = None
+    if not args.no_launch_count:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step(pos_d, cell_d)
+            torch.cuda.synchronize()
+        ours = sum(e.count for e in prof.key_averages() if "fsc::" in e.key or "cub::" in e.key)
+
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    NAT.profile_enable(True)
+    stage_ms = {}
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device() if world == 1 else int(os.environ.get("LOCAL_RANK", 0))) as clk:
+        t0.record()
+        for _ in range(args.steps):
+            step(pos_d, cell_d)
+            for name, ms in NAT.profile_read():
+                stage_ms.setdefault(name, []).append(ms)
+        t1.record()
+        torch.cuda.synchronize()
+    NAT.profile_enable(False)
+    ms_total = t0.elapsed_time(t1)
+    if world > 1:
+        torch.distributed.barrier()
+    # end-to-end through the public API with host buffers
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_e2e = e1 and e0.elapsed_time(e1)
+    ms_total_t = torch.tensor([ms_total, ms_e2e], device=device, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(ms_total_t, op=torch.distributed.ReduceOp.MAX)
+    ms_total, ms_e2e = float(ms_total_t[0]), float(ms_total_t[1])
+    return dict(n=n, E=E_edges, ms_step=ms_total / args.steps, ms_e2e=ms_e2e / args.steps, stage_ms=stage_ms,
+                clocks=clk.summary(), launches=None if ours is None else ours * args.steps, cfg=cfg)
+
+
+def cpu_reference(steps, warmup, budget_s=None):
+    """Time the oracle port of the reference CPU path on a bounded replica of the workload."""
+    from fsctep_b200 import systems
+    from oracle import ictd_model as OM
+    from oracle import neighbors as ON
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    w = WORKLOADS["si1m"]
+    cfg = model_cfg(w)
+    sd = {k: v.float() for k, v in seeded_weights(cfg).items()}
+    sysd = systems.diamond_crystal(n_cells=CPU_SAMPLE_CELLS, seed=1000, Z=w["Z"])
+    src, dst, S = ON.neighbor_list(sysd["pos"], sysd["cell"][0], 5.0)
+    args = (torch.tensor(sysd["pos"], dtype=torch.float32), torch.tensor(sysd["Z"]), torch.tensor(sysd["batch"]),
+            torch.tensor(src), torch.tensor(dst), torch.tensor(S, dtype=torch.float32),
+            torch.tensor(sysd["cell"], dtype=torch.float32))
+    ocfg = OM.ICTDConfig(channels=cfg.channels, num_interaction=cfg.num_interaction, function_type="gaussian",
+                         max_atomvalue=cfg.max_atomvalue)
+    tabs = OM._TPTables(2, torch.float32)
+    for _ in range(warmup):
+        OM.energy_forces_stress(sd, ocfg, *args, want_stress=False, tabs=tabs)
+    times = []
+    for _ in range(steps):
+        t = time.perf_counter()
+        OM.energy_forces_stress(sd, ocfg, *args, want_stress=False, tabs=tabs)
+        times.append(time.perf_counter() - t)
+    n = sysd["pos"].shape[0]
+    med = float(np.median(times))
+    return {"value": n / med, "unit": "atom-steps/s", "cores": threads, "kind": "port",
+            "sample": f"{n}-atom diamond replica ({CPU_SAMPLE_CELLS[0]}^3 cells, {len(src)} edges) of the same "
+                      f"model, fp32 PyTorch eager (oracle port of the reference CPU path), energy+forces, "
+                      f"median of {steps} steps after {warmup} warm-up, neighbour list excluded",
+            "seconds_per_step": med}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--workload", default="si1m", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-launch-count", action="store_true", help="skip the torch.profiler launch count (for ncu)")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    metric = "atom-steps/s (E+F)"
+    w = WORKLOADS[args.workload]
+    n_atoms = int(np.prod(w["cells"])) * 8
+    config = {"workload": f"{args.workload}: pure-cartesian-ictd diamond Si {n_atoms} atoms (config 4)",
+              "model": "pure-cartesian-ictd", "channels": w["channels"], "num_interaction": w["num_interaction"],
+              "lmax": 2, "cutoff": 5.0, "radial_basis": "gaussian x8", "atoms_per_gpu": n_atoms,
+              "parallelism": f"replicas{args.gpus}" if args.gpus > 1 else "single",
+              "step": "neighbour list + forward + backward (energy, forces)",
+              "l2": "inputs larger than L2 (features 2.3 GB per layer at 1M atoms)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        r = cpu_reference(max(1, args.steps), max(0, min(args.warmup, 1)))
+        line = {"metric": metric, "value": r["value"], "unit": "atom-steps/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["seconds_per_step"] * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "config": config, "impl": "reference",
+                "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": r["value"], "unit": "atom-steps/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    if world > 1:
+        torch.distributed.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300))
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(device)
+    res = run_native(args, rank, world, device)
+    n, E = res["n"], res["E"]
+    value = n * world / (res["ms_step"] / 1e3)
+    e2e_value = n * world / (res["ms_e2e"] / 1e3)
+    # dominant stage and its roofline
+    stage_avg = {}
+    for name, lst in res["stage_ms"].items():
+        stage_avg[name] = (sum(lst) / args.steps, len(lst) / args.steps)
+    dom = max(stage_avg, key=lambda k: stage_avg[k][0]) if stage_avg else None
+    pk = peaks()
+    roofline = None
+    if dom is not None:
+        per_step_ms, launches = stage_avg[dom]
+        work = algorithmic_work(dom, n, E, res["cfg"])
+        avg_launch_ms = per_step_ms / max(launches, 1)
+        if work is not None:
+            flops, nbytes = work
+            ach = flops / (avg_launch_ms / 1e3) / 1e12
+            roofline = {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": pk["bf16_tflops"],
+                        "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"], "traffic": None,
+                        "peak_source": pk["source"] + " bf16 dense (no fp32/tf32 peak measured)",
+                        "avg_launch_ms": avg_launch_ms,
+                        "algorithmic_bytes_per_launch": nbytes,
+                        "hbm_achieved_gbs": nbytes / (avg_launch_ms / 1e3) / 1e9}
+    line = {"metric": metric, "value": value, "unit": "atom-steps/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": res["ms_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded positions and weights)",
+            "config": config, "edges_per_gpu": E, "roofline": roofline, "clocks": res["clocks"],
+            "gpu_launches": res["launches"],
+            "e2e": {"value": e2e_value, "unit": "atom-steps/s", "h2d_bytes_per_step": n * 3 * 8,
+                    "d2h_bytes_per_step": n * 3 * 4 + 4},
+            "stages_ms": {k: round(v[0], 3) for k, v in sorted(stage_avg.items(), key=lambda kv: -kv[1][0])}}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r = cpu_reference(2, 1)
+        line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -82,6 +82,8 @@ _PROTOS = {
                                    C.c_size_t, P]),
     "fsc_ictd_backward": (C.c_int, [C.POINTER(IctdConfig), C.POINTER(IctdWeights), C.POINTER(Graph),
                                     C.POINTER(IctdOutputs), P, C.c_size_t, P]),
+    "fsc_profile_enable": (None, [C.c_int]),
+    "fsc_profile_read": (C.c_int, [C.POINTER(C.c_char_p), C.POINTER(C.c_float), C.c_int]),
     "fsc_ictd_energy": (C.c_int, [C.POINTER(IctdConfig), C.POINTER(IctdWeights), C.POINTER(Graph), P, P, P,
                                   C.c_size_t, P]),
 }
@@ -124,6 +126,20 @@ def stream_ptr(device=None):
     import torch
 
     return P(torch.cuda.current_stream(device).cuda_stream)
+
+
+def profile_enable(on: bool) -> None:
+    lib().fsc_profile_enable(1 if on else 0)
+
+
+def profile_read(max_stages: int = 64):
+    """[(stage name, ms)] recorded since the last enable/read (synchronises)."""
+    names = (C.c_char_p * max_stages)()
+    ms = (C.c_float * max_stages)()
+    n = lib().fsc_profile_read(names, ms, max_stages)
+    if n < 0:
+        raise NativeError("fsc_profile_read failed")
+    return [(names[i].decode(), float(ms[i])) for i in range(n)]
 
 
 def ptr(t):

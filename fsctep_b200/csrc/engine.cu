@@ -14,6 +14,27 @@ namespace fsc {
 
 using namespace ictd2;
 
+// Optional per-stage CUDA-event timing of the engine (off by default).
+namespace prof {
+constexpr int kMax = 64;
+bool enabled = false;
+int count = 0;
+const char* names[kMax];
+cudaEvent_t events[kMax];
+bool created = false;
+
+void mark(const char* name, cudaStream_t st) {
+  if (!enabled || count >= kMax) return;
+  if (!created) {
+    for (int i = 0; i < kMax; ++i) cudaEventCreate(&events[i]);
+    created = true;
+  }
+  names[count] = name;
+  cudaEventRecord(events[count], st);
+  ++count;
+}
+}  // namespace prof
+
 namespace {
 
 constexpr int64_t kGramChunk = 16384;  // nodes per readout chunk
@@ -174,15 +195,19 @@ int forward(Ctx& c) {
   const fsc_ictd_weights* w = c.w;
   cudaStream_t st = c.st;
   const int C = p.C;
+  prof::mark("begin", st);
   FSC_TRY(launch_edge_dst(g->row_ptr, p.dst, p.N, st));
   EdgeFwdArgs ef{};
   ef.E = p.E; ef.pos = g->pos; ef.src = g->src; ef.dst = p.dst; ef.batch = g->batch; ef.cell = g->cell;
   ef.shift = g->shift; ef.tables = w->tables; ef.rad = radial(w); ef.nint = p.nint; ef.nb = p.nb;
   ef.basis_kind = c.cfg->basis_kind; ef.rc = c.cfg->max_radius; ef.edge_y = p.edge_y; ef.gates = p.gates;
   FSC_TRY(launch_edge_forward(ef, st));
+  prof::mark("edge_forward", st);
   FSC_TRY(launch_conv1_forward(conv_args(c, 0), w->ai, w->vsp, p.feats[0], st));
+  prof::mark("conv1_forward", st);
   for (int k = 1; k < p.nint; ++k) {
     FSC_TRY(launch_conv2_z(conv_args(c, k), p.feats[k - 1], p.zbuf, st));
+    prof::mark("conv2_edge_forward", st);
     const float* W = w->mix_fwd + (int64_t)(k - 1) * NP * C * C;
     int64_t boff = 0;
     for (int l3 = 0; l3 < 3; ++l3) {
@@ -192,6 +217,7 @@ int forward(Ctx& c) {
       FSC_TRY(launch_gemm(ga, st));
       boff += (int64_t)NP3(l3) * C * C;
     }
+    prof::mark("conv2_mix_forward", st);
   }
   // readout scalars: packed Gram x symmetrised W_read
   ReadoutArgs ra = readout_args(c);
@@ -208,6 +234,7 @@ int forward(Ctx& c) {
       FSC_TRY(launch_gemm(ga, st));
     }
   }
+  prof::mark("readout_gram_forward", st);
   FSC_TRY(launch_p5_forward(ra, p.scalars, p.p5, st));
   FSC_TRY(launch_layernorm(p.p5, p.N, p.D0, w->mn_in_g, w->mn_in_b, 0, p.x0, st));
   const float* xin = p.x0;
@@ -220,6 +247,7 @@ int forward(Ctx& c) {
     xin = p.act_post[k];
     din = p.hidden[k];
   }
+  prof::mark("readout_mlp_forward", st);
   return FSC_OK;
 }
 
@@ -243,6 +271,7 @@ int backward(Ctx& c) {
   FSC_TRY(launch_layernorm_backward(p.p5, dcur, p.N, p.D0, w->mn_in_g, w->mn_in_b, 0, p.dp5, st));
   ReadoutArgs ra = readout_args(c);
   FSC_TRY(launch_p5_backward(ra, p.scalars, p.dp5, p.grads, p.dscalars, st));
+  prof::mark("readout_mlp_backward", st);
   for (int l = 0; l < 3; ++l) {
     const float* Ws = w->wread_s + (int64_t)l * p.S * p.nC * p.nC;
     for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
@@ -253,6 +282,7 @@ int backward(Ctx& c) {
       FSC_TRY(launch_gram_apply(ra, l, n0, nn, p.chunkbuf, p.grads, st));
     }
   }
+  prof::mark("readout_gram_backward", st);
   if (cudaMemsetAsync(p.dY, 0, sizeof(float) * p.E * 12, st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset dY");
   for (int k = p.nint - 1; k >= 1; --k) {
     ConvArgs ca = conv_args(c, k);
@@ -266,8 +296,11 @@ int backward(Ctx& c) {
       FSC_TRY(launch_gemm(ga, st));
       boff += (int64_t)NP3(l3) * C * C;
     }
+    prof::mark("conv2_mix_backward_dz", st);
     FSC_TRY(launch_conv2_q(ca, p.feats[k - 1], p.zbuf, p.dgates + (int64_t)k * p.E * 12, p.dY, st));
+    prof::mark("conv2_edge_backward_gates", st);
     FSC_TRY(launch_conv2_r(ca, p.grads[k], p.zbuf, st));
+    prof::mark("conv2_edge_backward_x", st);
     const float* Wx = w->mix_dx + (int64_t)(k - 1) * NP * C * C;
     boff = 0;
     for (int l1 = 0; l1 < 3; ++l1) {
@@ -277,8 +310,10 @@ int backward(Ctx& c) {
       FSC_TRY(launch_gemm(ga, st));
       boff += (int64_t)NP1(l1) * C * C;
     }
+    prof::mark("conv2_mix_backward_dx", st);
   }
   FSC_TRY(launch_conv1_backward(conv_args(c, 0), w->ai, w->vsp, p.grads[0], p.dgates, p.dY, st));
+  prof::mark("conv1_backward", st);
   return FSC_OK;
 }
 
@@ -381,6 +416,7 @@ int run_backward(Ctx& c, fsc_ictd_outputs* out) {
   eb.edge_grad = out->edge_grad ? out->edge_grad : c.p.edge_grad;
   eb.virial = nullptr;
   FSC_TRY(launch_edge_backward(eb, c.st));
+  prof::mark("edge_backward", c.st);
   if (out->forces) FSC_TRY(launch_forces(g->row_ptr, g->tr_ptr, g->tr_eid, eb.edge_grad, out->forces, c.p.N, c.st));
   const int64_t nfin = 9 * c.p.B;
   if (out->virial) {
@@ -407,6 +443,7 @@ int run_backward(Ctx& c, fsc_ictd_outputs* out) {
                                                                      out->cell_grad);
     FSC_TRY(check_launch("finalize_kernel (cell)"));
   }
+  prof::mark("forces_virial", c.st);
   return FSC_OK;
 }
 
@@ -454,5 +491,26 @@ int fsc_ictd_energy(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const
 }
 
 int64_t fsc_ictd_tables_floats(void) { return ictd2::TAB_FLOATS; }
+
+void fsc_profile_enable(int enable) {
+  fsc::prof::enabled = enable != 0;
+  fsc::prof::count = 0;
+}
+
+int fsc_profile_read(const char** names, float* ms, int max_stages) {
+  using namespace fsc::prof;
+  if (count < 2) {
+    count = 0;
+    return 0;
+  }
+  if (cudaEventSynchronize(events[count - 1]) != cudaSuccess) return -1;
+  int n = 0;
+  for (int i = 1; i < count && n < max_stages; ++i, ++n) {
+    names[n] = fsc::prof::names[i];
+    cudaEventElapsedTime(&ms[n], events[i - 1], events[i]);
+  }
+  count = 0;
+  return n;
+}
 
 }  // extern "C"

@@ -261,6 +261,14 @@ int fsc_ictd_energy(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const
                     float* energy, float* atom_energy, void* workspace, size_t workspace_bytes,
                     void* stream);
 
+/* ---- stage timing ------------------------------------------------------
+ * When enabled, the engine records a CUDA event after each stage on its stream;
+ * fsc_profile_read waits for the last one and returns per-stage milliseconds (stage
+ * i spans from mark i-1 to mark i; the same name may repeat, once per layer) and
+ * clears the record.  Process-wide, not thread-safe; meant for benchmarks. */
+void fsc_profile_enable(int enable);
+int fsc_profile_read(const char** names, float* ms, int max_stages);
+
 #ifdef __cplusplus
 }
 #endif
