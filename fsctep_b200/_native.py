@@ -32,7 +32,7 @@ class IctdConfig(C.Structure):
 class IctdWeights(C.Structure):
     _fields_ = [("tables", P), ("ai", P), ("vsp", P), ("rad_w1", P), ("rad_b1", P), ("rad_w2", P),
                 ("rad_b2", P), ("rad_w3", P), ("rad_b3", P), ("mix_fwd", P), ("mix_bwd", P), ("mix_dx", P),
-                ("wread_p", P), ("wread_s", P), ("pairs", P), ("xmap", P), ("mn_in_g", P), ("mn_in_b", P),
+                ("wread_p", P), ("wread_s", P), ("pairs", P), ("xmap", P), ("xinv", P), ("wimg_fwd", P), ("wimg_bwd", P), ("mn_in_g", P), ("mn_in_b", P),
                 ("mn_w", P * 4), ("mn_b", P * 4), ("mn_g", P * 4), ("mn_beta", P * 4), ("out_v", P),
                 ("out_c0", C.c_float)]
 
@@ -82,6 +82,8 @@ _PROTOS = {
                                    C.c_size_t, P]),
     "fsc_ictd_backward": (C.c_int, [C.POINTER(IctdConfig), C.POINTER(IctdWeights), C.POINTER(Graph),
                                     C.POINTER(IctdOutputs), P, C.c_size_t, P]),
+    "fsc_ictd_status": (C.c_int, [C.POINTER(IctdConfig), I64, I64, P, P, C.POINTER(C.c_int)]),
+    "fsc_ictd_set_readout_path": (None, [C.c_int]),
     "fsc_profile_enable": (None, [C.c_int]),
     "fsc_profile_read": (C.c_int, [C.POINTER(C.c_char_p), C.POINTER(C.c_float), C.c_int]),
     "fsc_ictd_energy": (C.c_int, [C.POINTER(IctdConfig), C.POINTER(IctdWeights), C.POINTER(Graph), P, P, P,

@@ -68,7 +68,15 @@ struct Plan {
   double* virial_d;
   double* cellg_d;
   float* chunkbuf;
+  // tensor-core readout
+  bool tc;
+  int64_t n_pad;
+  float* Fg;
+  float* dFg;
+  int* err;
 };
+
+int g_readout_path = 0;  // 0: tensor cores where supported, 1: CUDA cores
 
 int validate(const fsc_ictd_config* cfg) {
   FSC_REQUIRE(cfg != nullptr, "config is null");
@@ -128,7 +136,48 @@ void layout(Plan& p, Arena& ar, const fsc_ictd_config* cfg, int64_t N, int64_t E
   p.dgates = ar.take<float>((int64_t)p.nint * E * 12);
   p.dY = ar.take<float>(E * 12);
   p.edge_grad = ar.take<float>(E * 3);
-  p.chunkbuf = ar.take<float>(p.chunk * std::max<int64_t>(p.npairs, (int64_t)p.nC * p.nC));
+  p.tc = g_readout_path == 0 && readout_tc_supported(p.nC, p.S);
+  p.n_pad = ceil_div(std::max<int64_t>(N, 1), 128) * 128;
+  p.err = ar.take<int>(64);
+  if (p.tc) {
+    p.chunkbuf = nullptr;
+    p.Fg = ar.take<float>((int64_t)9 * p.nC * p.n_pad);
+    p.dFg = ar.take<float>((int64_t)9 * p.nC * p.n_pad);
+  } else {
+    p.Fg = p.dFg = nullptr;
+    p.chunkbuf = ar.take<float>(p.chunk * std::max<int64_t>(p.npairs, (int64_t)p.nC * p.nC));
+  }
+}
+
+FgArgs fg_args(const Plan& p, const fsc_ictd_weights* w) {
+  FgArgs f{};
+  f.N = p.N;
+  f.n_pad = p.n_pad;
+  f.C = p.C;
+  f.nint = p.nint;
+  for (int k = 0; k < p.nint; ++k) {
+    f.feats[k] = p.feats[k];
+    f.grads[k] = p.grads[k];
+  }
+  f.xinv = w->xinv;
+  f.Fg = p.Fg;
+  f.dFg = p.dFg;
+  return f;
+}
+
+ReadoutTcArgs tc_args(const Plan& p, const float* wimg) {
+  ReadoutTcArgs r{};
+  r.N = p.N;
+  r.n_pad = p.n_pad;
+  r.nC = p.nC;
+  r.S = p.S;
+  r.Fg = p.Fg;
+  r.wimg = wimg;
+  r.scalars = p.scalars;
+  r.dscal = p.dscalars;
+  r.dFg = p.dFg;
+  r.err = p.err;
+  return r;
 }
 
 GemmArgs gemm(const float* A, int64_t a_gs, int64_t a_rs, const float* B, int64_t ldb, int b_trans, float* C,
@@ -221,9 +270,13 @@ int forward(Ctx& c) {
   }
   // readout scalars: packed Gram x symmetrised W_read
   ReadoutArgs ra = readout_args(c);
-  FSC_TRY(cudaMemsetAsync(p.scalars, 0, sizeof(float) * p.N * p.S, st) == cudaSuccess ? FSC_OK
-                                                                                         : fail(FSC_ERR_CUDA, "memset"));
-  for (int l = 0; l < 3; ++l) {
+  if (p.tc) {
+    FSC_TRY(launch_fg_gather(fg_args(p, w), st));
+    FSC_TRY(launch_readout_fwd_tc(tc_args(p, w->wimg_fwd), st));
+  }
+  if (!p.tc && cudaMemsetAsync(p.scalars, 0, sizeof(float) * p.N * p.S, st) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "memset scalars");
+  for (int l = 0; l < 3 && !p.tc; ++l) {
     const float* Wp = w->wread_p + (int64_t)l * p.S * p.npairs;
     for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
       const int64_t nn = std::min(p.chunk, p.N - n0);
@@ -272,7 +325,11 @@ int backward(Ctx& c) {
   ReadoutArgs ra = readout_args(c);
   FSC_TRY(launch_p5_backward(ra, p.scalars, p.dp5, p.grads, p.dscalars, st));
   prof::mark("readout_mlp_backward", st);
-  for (int l = 0; l < 3; ++l) {
+  if (p.tc) {
+    FSC_TRY(launch_readout_bwd_tc(tc_args(p, w->wimg_bwd), st));
+    FSC_TRY(launch_fg_scatter_add(fg_args(p, w), st));
+  }
+  for (int l = 0; l < 3 && !p.tc; ++l) {
     const float* Ws = w->wread_s + (int64_t)l * p.S * p.nC * p.nC;
     for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
       const int64_t nn = std::min(p.chunk, p.N - n0);
@@ -387,7 +444,8 @@ int prepare(Ctx& c, void* workspace, size_t bytes) {
 }
 
 int run_forward(Ctx& c, float* energy, float* atom_energy) {
-  if (cudaMemsetAsync(c.p.energy_d, 0, sizeof(double) * kMaxGraphs * 19, c.st) != cudaSuccess)
+  if (cudaMemsetAsync(c.p.energy_d, 0, sizeof(double) * kMaxGraphs * 19, c.st) != cudaSuccess ||
+      cudaMemsetAsync(c.p.err, 0, sizeof(int) * 64, c.st) != cudaSuccess)
     return fail(FSC_ERR_CUDA, "memset accumulators");
   FSC_TRY(forward(c));
   const int H = c.p.hidden[c.p.n_hidden - 1];
@@ -491,6 +549,22 @@ int fsc_ictd_energy(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const
 }
 
 int64_t fsc_ictd_tables_floats(void) { return ictd2::TAB_FLOATS; }
+
+int fsc_ictd_status(const fsc_ictd_config* cfg, int64_t num_atoms, int64_t num_edges, void* workspace,
+                    void* stream, int* status_host) {
+  FSC_REQUIRE(status_host && workspace, "status output and workspace required");
+  FSC_TRY(fsc::validate(cfg));
+  fsc::Plan p{};
+  fsc::Arena ar(workspace, (size_t)-1);
+  fsc::layout(p, ar, cfg, num_atoms, num_edges);
+  cudaStream_t st = fsc::as_stream(stream);
+  if (cudaMemcpyAsync(status_host, p.err, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return fsc::fail(FSC_ERR_CUDA, "status readback");
+  return FSC_OK;
+}
+
+void fsc_ictd_set_readout_path(int path) { fsc::g_readout_path = path; }
 
 void fsc_profile_enable(int enable) {
   fsc::prof::enabled = enable != 0;

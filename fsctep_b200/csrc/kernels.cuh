@@ -112,6 +112,33 @@ int launch_p5_forward(const ReadoutArgs& a, const float* scalars, float* p5, cud
 // Writes (not accumulates) grads[k] for all components, and dscalars.
 int launch_p5_backward(const ReadoutArgs& a, const float* scalars, const float* dp5, float* const* grads,
                        float* dscalars, cudaStream_t st);
+// Tensor-core readout (readout_tc.cu)
+struct ReadoutTcArgs {
+  int64_t N, n_pad;     // nodes, Fg row stride (multiple of 128)
+  int nC, S;
+  const float* Fg;      // [9*nC][n_pad] Gram operand, node innermost
+  const float* wimg;    // pre-formatted W blocks (hi/lo), forward or backward order
+  float* scalars;       // forward output [N][S]
+  const float* dscal;   // backward input [N][S]
+  float* dFg;           // backward output [9*nC][n_pad]
+  int* err;             // first failing wait site (0 = ok)
+};
+bool readout_tc_supported(int nC, int S);
+int64_t readout_tc_blocks(int nC, bool backward);
+int launch_readout_fwd_tc(const ReadoutTcArgs& a, cudaStream_t st);
+int launch_readout_bwd_tc(const ReadoutTcArgs& a, cudaStream_t st);
+struct FgArgs {
+  int64_t N, n_pad;
+  int C, nint;
+  const float* feats[8];
+  float* grads[8];
+  const int32_t* xinv;  // [nint][9*C] storage (layer, k*C + c) -> Gram operand row
+  float* Fg;
+  const float* dFg;
+};
+int launch_fg_gather(const FgArgs& a, cudaStream_t st);
+int launch_fg_scatter_add(const FgArgs& a, cudaStream_t st);
+
 // LayerNorm over the last dim (rows x D), eps 1e-5, optional SiLU after.
 int launch_layernorm(const float* X, int64_t rows, int D, const float* gamma, const float* beta, int silu,
                      float* Y, cudaStream_t st);

@@ -89,6 +89,49 @@ def gram_xmap(C: int, nint: int):
     return out
 
 
+def gram_xinv(C: int, nint: int):
+    """Inverse of gram_xmap: [nint][9*C] storage (layer, k*C + c) -> Gram operand row."""
+    inv = [[0] * (9 * C) for _ in range(nint)]
+    for r, code in enumerate(gram_xmap(C, nint)):
+        inv[code >> 16][code & 0xFFFF] = r
+    return inv
+
+
+def tf32_split(x: torch.Tensor):
+    """fp32 -> (hi, lo): hi keeps the top 19 bits, lo = round_to_nearest_tf32(x - hi)."""
+    x = x.to(torch.float32).contiguous()
+    hi = (x.view(torch.int32) & -8192).view(torch.float32)
+    r = (x - hi).contiguous()
+    lo = ((r.view(torch.int32) + 4096) & -8192).view(torch.float32)
+    return hi, lo
+
+
+def readout_images(W_read, C: int, nint: int):
+    """W_read.l blocks as shared-memory images of the tcgen05 operands (see include/fsctep_b200.h).
+
+    Returns (wimg_fwd, wimg_bwd) as flat fp32 tensors.
+    """
+    nC = C * nint
+    nb = nC // 8
+    fwd, bwd = [], []
+    iu = torch.triu_indices(nb, nb)
+    for l in range(3):
+        Wr = W_read[l].to(torch.float64) / math.sqrt(2 * l + 1)
+        S = Wr.shape[0]
+        Ws = 0.5 * (Wr + Wr.transpose(1, 2))
+        blk = Ws.reshape(S, nb, 8, nb, 8).permute(1, 3, 0, 2, 4).reshape(nb, nb, S, 64)  # [cb][db][o][pair]
+        # forward: cb <= db, x2 off the diagonal, image [pair/4][o][pair%4]
+        f = blk[iu[0], iu[1]] * torch.where(iu[0] == iu[1], 1.0, 2.0).to(blk)[:, None, None]
+        f = f.reshape(-1, S, 16, 4).permute(0, 2, 1, 3)
+        hi, lo = tf32_split(f)
+        fwd.append(torch.stack([hi, lo], dim=1).reshape(-1))
+        # backward: all blocks, image [o/4][pair][o%4] of Ws
+        b = blk.reshape(nb * nb, S, 64).transpose(1, 2).reshape(nb * nb, 64, S // 4, 4).permute(0, 2, 1, 3)
+        hi, lo = tf32_split(b)
+        bwd.append(torch.stack([hi, lo], dim=1).reshape(-1))
+    return torch.cat(fwd), torch.cat(bwd)
+
+
 def _silu(x):
     return x * torch.sigmoid(x)
 
@@ -151,6 +194,14 @@ class PackedICTDWeights:
         put("wread_s", torch.cat(ws))
         keep["pairs"] = (iu[0] | (iu[1] << 16)).to(torch.int32).contiguous()
         keep["xmap"] = torch.tensor(gram_xmap(C_, nint), dtype=torch.int32, device=dev)
+        keep["xinv"] = torch.tensor(gram_xinv(C_, nint), dtype=torch.int32, device=dev).reshape(-1)
+        S = (nint - 1) * cfg.invariant_channels
+        if S in (32, 64) and nC % 8 == 0:
+            wf, wb = readout_images([f64(f"W_read.{l}") for l in range(3)], C_, nint)
+            put("wimg_fwd", wf)
+            put("wimg_bwd", wb)
+        else:
+            keep["wimg_fwd"] = keep["wimg_bwd"] = None
         # MainNet
         put("mn_in_g", f64("proj_total.input_norm.weight"))
         put("mn_in_b", f64("proj_total.input_norm.bias"))
@@ -165,7 +216,7 @@ class PackedICTDWeights:
         self.tensors = keep
         s = N.IctdWeights()
         for name in ("tables", "ai", "vsp", "rad_w1", "rad_b1", "rad_w2", "rad_b2", "rad_w3", "rad_b3",
-                     "mix_fwd", "mix_bwd", "mix_dx", "wread_p", "wread_s", "pairs", "xmap", "mn_in_g", "mn_in_b", "out_v"):
+                     "mix_fwd", "mix_bwd", "mix_dx", "wread_p", "wread_s", "pairs", "xmap", "xinv", "mn_in_g", "mn_in_b", "out_v"):
             setattr(s, name, keep[name].data_ptr())
         for k in range(len(cfg.embed_size)):
             s.mn_w[k] = keep[f"mn_w{k}"].data_ptr()
@@ -173,6 +224,8 @@ class PackedICTDWeights:
             s.mn_g[k] = keep[f"mn_g{k}"].data_ptr()
             s.mn_beta[k] = keep[f"mn_beta{k}"].data_ptr()
         s.out_c0 = self.out_c0
+        s.wimg_fwd = 0 if keep["wimg_fwd"] is None else keep["wimg_fwd"].data_ptr()
+        s.wimg_bwd = 0 if keep["wimg_bwd"] is None else keep["wimg_bwd"].data_ptr()
         self.struct = s
 
 
@@ -293,6 +346,15 @@ class ICTDEngine:
         N.check(N.lib().fsc_ictd_backward(C.byref(self.ncfg), C.byref(self.weights.struct), C.byref(gs), C.byref(o),
                                           N.ptr(ws), ws.numel(), N.stream_ptr(dev)), "fsc_ictd_backward")
         return out
+
+    def status(self) -> int:
+        """Device status word of the last call (0 = ok); synchronises the stream."""
+        pos, species, batch, cell, g, num_local = self._last
+        ws = self.workspace(g.num_atoms, g.num_edges)
+        st = C.c_int(0)
+        N.check(N.lib().fsc_ictd_status(C.byref(self.ncfg), g.num_atoms, g.num_edges, N.ptr(ws),
+                                        N.stream_ptr(self.device), C.byref(st)), "fsc_ictd_status")
+        return int(st.value)
 
     def energy_forces(self, pos, species, batch, cell, g: GraphCSR, num_local=None, want_stress=True):
         energy, atom_e = self.forward(pos, species, batch, cell, g, num_local)

@@ -199,6 +199,15 @@ typedef struct {
    * xmap[off_l + c*(2l+1) + m] = (layer << 16) | (k*C + channel) locates that element in
    * the [N][9][C] feature buffers.                                                          */
   const int32_t* xmap;   /* [9*nC]                                                          */
+  const int32_t* xinv;   /* [nint][9*C] inverse of xmap: storage (layer, k*C+c) -> element   */
+  /* Tensor-core readout: W_read in 8x8 (c, d) blocks, each block pre-formatted as the
+   * shared-memory image of a K-major tf32 MMA operand and split hi/lo for 3xTF32 (hi keeps
+   * the top 19 bits, lo = round_tf32(w - hi)); nb = nC/8.
+   *   wimg_fwd: for l, cb <= db:  [hi|lo][pair/4][o][pair%4] of Ws (x2 off the diagonal)
+   *   wimg_bwd: for l, cb, db:    [hi|lo][o/4][pair][o%4]   of Ws
+   * with pair = 8*(c - 8cb) + (d - 8db) and Ws = (W_read.l + W_read.l^T)/2/sqrt(2l+1).      */
+  const float* wimg_fwd; /* [3*nb*(nb+1)/2][2][16][S][4]                                   */
+  const float* wimg_bwd; /* [3*nb*nb][2][S/4][64][4]                                       */
   const float* mn_in_g;  /* [D0]  proj_total.input_norm.weight, D0 = 3*nC + S             */
   const float* mn_in_b;  /* [D0]  proj_total.input_norm.bias                              */
   const float* mn_w[4];  /* [hidden[k]][in_k]  proj_total.layers.k.weight (as stored)      */
@@ -256,6 +265,12 @@ int fsc_ictd_forward(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, cons
                      void* stream);
 int fsc_ictd_backward(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g,
                       fsc_ictd_outputs* out, void* workspace, size_t workspace_bytes, void* stream);
+/* Device status word of the last call on `workspace` (0 = ok; else the id of a bounded
+ * wait in a tensor-core kernel that timed out).  Synchronises `stream`.  */
+int fsc_ictd_status(const fsc_ictd_config* cfg, int64_t num_atoms, int64_t num_edges, void* workspace,
+                    void* stream, int* status_host);
+/* Readout path: 0 = tensor cores where supported (default), 1 = CUDA-core kernels. */
+void fsc_ictd_set_readout_path(int path);
 /* Forward only (per-atom energy), same workspace. */
 int fsc_ictd_energy(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g,
                     float* energy, float* atom_energy, void* workspace, size_t workspace_bytes,

@@ -14,6 +14,7 @@ def test_energy_forces_stress_match_reference(tag):
     eng, g, (pos, Z, batch, cell), c, _, _ = U.golden_engine(tag)
     out = eng.energy_forces(pos, Z, batch, cell, g)
     torch.cuda.synchronize()
+    assert eng.status() == 0
     E = out["energy"].cpu().numpy()
     F = out["forces"].cpu().numpy()
     S = out["stress"].cpu().numpy()
@@ -42,3 +43,33 @@ def test_energy_weights_ghost_convention():
     ae = full["atom_energy"].double()
     torch.cuda.synchronize()
     assert abs(part["energy"].item() - ae[: n // 2].sum().item()) < 1e-4 * abs(ae[: n // 2].sum().item()) + 1e-5
+
+
+@pytest.mark.parametrize("tag,n_cells", [("c", (5, 5, 3)), ("b", (3, 3, 5))])
+def test_tensor_core_readout_matches_cuda_core_readout(tag, n_cells):
+    """tcgen05 readout (default) vs the CUDA-core readout on several 128-node tiles (partial last tile)."""
+    from fsctep_b200 import _native as NAT
+    from fsctep_b200 import systems
+    from fsctep_b200.neighbors import build_graph
+
+    eng, _, _, c, icfg, sd = U.golden_engine(tag)
+    s = systems.diamond_crystal(n_cells=n_cells, seed=21)
+    dev = torch.device("cuda")
+    pos, cell = torch.tensor(s["pos"], device=dev), torch.tensor(s["cell"], device=dev)
+    g = build_graph(pos, cell, 5.0)
+    Z, b = torch.tensor(s["Z"], device=dev), torch.tensor(s["batch"], device=dev)
+    try:
+        NAT.lib().fsc_ictd_set_readout_path(1)
+        ref = eng.energy_forces(pos, Z, b, cell, g)
+        torch.cuda.synchronize()
+        NAT.lib().fsc_ictd_set_readout_path(0)
+        out = eng.energy_forces(pos, Z, b, cell, g)
+        torch.cuda.synchronize()
+        assert eng.status() == 0
+    finally:
+        NAT.lib().fsc_ictd_set_readout_path(0)
+    assert pos.shape[0] % 128 != 0
+    e, er = out["energy"].double().cpu(), ref["energy"].double().cpu()
+    assert (e - er).abs().max().item() <= 1e-5 * er.abs().max().item(), (e, er)
+    assert U.rel_max(out["forces"].cpu().numpy(), ref["forces"].cpu().numpy()) <= 1e-4
+    assert U.rel_max(out["atom_energy"].cpu().numpy(), ref["atom_energy"].cpu().numpy()) <= 1e-4
