@@ -169,82 +169,107 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_r_kernel(ConvArgs a, co
 }
 
 // ---------------------------------------------------------------- conv2 backward: gates and Y (dst-centric)
-// Q[q] = sum_c x[src][KB(l1)+m1][c] * dZ[dst][zrow(p,kk)][c]  (dZ already carries 1/deg)
-// dgate[p] = sum_{q in p} Q[q] * Yt0[q];   dY[yb(q)+m] += Q[q] * gate[p(q)] * cg2[q][m]
-constexpr int QRED_LD = NQ + 2;  // padded row of the cross-lane reduction buffer
+// One warp per dst node, one lane per incoming edge (rows longer than 32 take several passes).
+// Per edge, over all channels:  Q[q] = sum_c x[src][KB(l1)+m1][c] * dZ[dst][zrow(p,kk)][c]
+// (dZ already carries 1/deg), then
+//   dgate[p]         = sum_{q in p} Q[q] * Yt0[q],     Yt0[q] = sum_m2 CG_p[m1,m2,kk] Y[KB(l2)+m2]
+//   dY[KB(l2)+m2]   += sum_{q in p} Q[q] * gate[p] * CG_p[m1,m2,kk]
+// Every reduction runs inside one thread: no cross-lane traffic.  dZ rows are read as 16-byte
+// vectors that all lanes of the warp share (same node), x rows as 16-byte vectors per lane.
+// Paths with l1 = G: p in [P_LO(G), P_HI(G)), their Q entries [QOFF(P_LO), QOFF(P_HI)).
+__host__ __device__ constexpr int P_LO(int G) { return G == 0 ? 0 : (G == 1 ? 3 : 7); }
+__host__ __device__ constexpr int P_HI(int G) { return G == 0 ? 3 : (G == 1 ? 7 : 11); }
+__host__ __device__ constexpr int Q_END(int G) { return G == 2 ? NQ : QOFF(P_HI(G)); }
+
+template <int G, int C>
+__device__ __forceinline__ void q_group(const float4* __restrict__ x4, const float4* __restrict__ dz4,
+                                        const float* __restrict__ cg2, const float* Y, const float* g, float* dg,
+                                        float* dy) {
+  constexpr int Q0 = QOFF(P_LO(G)), NQG = Q_END(G) - Q0, M1 = 2 * G + 1;
+  float Q[NQG];
+#pragma unroll
+  for (int i = 0; i < NQG; ++i) Q[i] = 0.f;
+#pragma unroll 1
+  for (int c4 = 0; c4 < C / 4; ++c4) {
+    float4 xv[M1];
+#pragma unroll
+    for (int m1 = 0; m1 < M1; ++m1) xv[m1] = x4[(KB(G) + m1) * (C / 4) + c4];
+#pragma unroll
+    for (int p = P_LO(G); p < P_HI(G); ++p)
+#pragma unroll
+      for (int kk = 0; kk < 2 * L3(p) + 1; ++kk) {
+        const float4 d = dz4[zrow(p, kk) * (C / 4) + c4];
+#pragma unroll
+        for (int m1 = 0; m1 < M1; ++m1) {
+          float acc = Q[qidx(p, m1, kk) - Q0];
+          acc = fmaf(xv[m1].x, d.x, acc);
+          acc = fmaf(xv[m1].y, d.y, acc);
+          acc = fmaf(xv[m1].z, d.z, acc);
+          acc = fmaf(xv[m1].w, d.w, acc);
+          Q[qidx(p, m1, kk) - Q0] = acc;
+        }
+      }
+  }
+#pragma unroll
+  for (int p = P_LO(G); p < P_HI(G); ++p)
+#pragma unroll
+    for (int m1 = 0; m1 < M1; ++m1)
+#pragma unroll
+      for (int kk = 0; kk < 2 * L3(p) + 1; ++kk) {
+        const int q = qidx(p, m1, kk);
+        float y0 = 0.f;
+#pragma unroll
+        for (int m2 = 0; m2 < 2 * L2(p) + 1; ++m2) y0 = fmaf(cg2[5 * q + m2], Y[KB(L2(p)) + m2], y0);
+        dg[p] = fmaf(Q[q - Q0], y0, dg[p]);
+        const float qg = Q[q - Q0] * g[p];
+#pragma unroll
+        for (int m2 = 0; m2 < 2 * L2(p) + 1; ++m2)
+          dy[KB(L2(p)) + m2] = fmaf(qg, cg2[5 * q + m2], dy[KB(L2(p)) + m2]);
+      }
+}
+
 template <int CPL>
 __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_q_kernel(ConvArgs a, const float* __restrict__ x,
                                                                   const float* __restrict__ dZ,
                                                                   float* __restrict__ dgates,
                                                                   float* __restrict__ dY) {
   __shared__ float cg2[NQ * 5];
-  __shared__ EdgeBuf bufs[CONV_WARPS];
-  __shared__ float qv[CONV_WARPS][NQ + 1];
-  extern __shared__ float red_dyn[];  // [CONV_WARPS][32 * QRED_LD]
   load_cg2(cg2, a.tables);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n = (int64_t)blockIdx.x * CONV_WARPS + warp;
   if (n >= a.N) return;
-  const int C = 32 * CPL;
-  EdgeBuf& b = bufs[warp];
-  float* rw = red_dyn + warp * 32 * QRED_LD;
-  float dz[NZ][CPL];
-#pragma unroll
-  for (int i = 0; i < NZ; ++i)
-#pragma unroll
-    for (int c = 0; c < CPL; ++c) dz[i][c] = dZ[(n * NZ + i) * C + lane + 32 * c];
+  constexpr int C = 32 * CPL;
   const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
-  for (int e = e0; e < e1; ++e) {
-    const int64_t s = a.src[e];
-    float xv[NK][CPL];
+  const float4* dz4 = reinterpret_cast<const float4*>(dZ + n * NZ * C);
+  for (int base = e0; base < e1; base += 32) {
+    const int e = base + lane;
+    const bool active = e < e1;
+    const int64_t ee = active ? e : e0;
+    const int64_t s = a.src[ee];
+    const float4* x4 = reinterpret_cast<const float4*>(x + s * NK * C);
+    float Y[NK], g[NP], dg[NP], dy[NK];
 #pragma unroll
-    for (int k = 0; k < NK; ++k)
-#pragma unroll
-      for (int c = 0; c < CPL; ++c) xv[k][c] = x[(s * NK + k) * C + lane + 32 * c];
-    build_yt(b, cg2, a.edge_y, a.gates, e, lane, false);  // ungated Yt0
-#pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-      for (int m1 = 0; m1 < 2 * L1(p) + 1; ++m1)
-#pragma unroll
-        for (int kk = 0; kk < 2 * L3(p) + 1; ++kk) {
-          float t = 0.f;
-#pragma unroll
-          for (int c = 0; c < CPL; ++c) t = fmaf(xv[KB(L1(p)) + m1][c], dz[zrow(p, kk)][c], t);
-          rw[lane * QRED_LD + qidx(p, m1, kk)] = t;
-        }
-    __syncwarp();
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int q = lane + 32 * j;
-      if (q < NQ) {
-        float acc = 0.f;
-#pragma unroll 8
-        for (int l = 0; l < 32; ++l) acc += rw[l * QRED_LD + q];
-        qv[warp][q] = acc;
-      }
+    for (int k = 0; k < NK; ++k) {
+      Y[k] = a.edge_y[12 * ee + k];
+      dy[k] = 0.f;
     }
-    __syncwarp();
-    // lanes 0..10: dgate[p]; lanes 11..19: dY[k]
-    if (lane < NP) {
-      const int p = lane;
-      float acc = 0.f;
-      for (int q = 0; q < NQ; ++q)
-        if (c_qtab.path[q] == p) acc = fmaf(qv[warp][q], b.yt[q], acc);
-      dgates[12 * (int64_t)e + p] = acc;
-    } else if (lane < NP + NK) {
-      const int k = lane - NP;
-      float acc = 0.f;
-      for (int q = 0; q < NQ; ++q) {
-        const int m = k - c_qtab.yb[q];
-        if (m >= 0 && m < 5) acc = fmaf(qv[warp][q] * b.g[c_qtab.path[q]], cg2[5 * q + m], acc);
-      }
-      dY[12 * (int64_t)e + k] += acc;
-    } else if (lane == 31) {
-      dgates[12 * (int64_t)e + 11] = 0.f;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+      g[p] = a.gates[12 * ee + p];
+      dg[p] = 0.f;
     }
-    __syncwarp();
+    q_group<0, C>(x4, dz4, cg2, Y, g, dg, dy);
+    q_group<1, C>(x4, dz4, cg2, Y, g, dg, dy);
+    q_group<2, C>(x4, dz4, cg2, Y, g, dg, dy);
+    if (!active) continue;
+    float4* dgo = reinterpret_cast<float4*>(dgates + 12 * (int64_t)e);
+    dgo[0] = make_float4(dg[0], dg[1], dg[2], dg[3]);
+    dgo[1] = make_float4(dg[4], dg[5], dg[6], dg[7]);
+    dgo[2] = make_float4(dg[8], dg[9], dg[10], 0.f);
+    float* dyo = dY + 12 * (int64_t)e;
+#pragma unroll
+    for (int k = 0; k < NK; ++k) dyo[k] += dy[k];
   }
 }
 
@@ -415,19 +440,7 @@ int launch_conv2_r(const ConvArgs& a, const float* G, float* R, cudaStream_t st)
 }
 int launch_conv2_q(const ConvArgs& a, const float* x, const float* dZ, float* dgates, float* dY,
                    cudaStream_t st) {
-  if (a.N == 0) return FSC_OK;
-  const unsigned blocks = (unsigned)ceil_div(a.N, CONV_WARPS);
-  const int sm = CONV_WARPS * 32 * QRED_LD * (int)sizeof(float);
-  if (a.C == 32) {
-    cudaFuncSetAttribute(conv2_q_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-    conv2_q_kernel<1><<<blocks, CONV_WARPS * 32, sm, st>>>(a, x, dZ, dgates, dY);
-  } else if (a.C == 64) {
-    cudaFuncSetAttribute(conv2_q_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-    conv2_q_kernel<2><<<blocks, CONV_WARPS * 32, sm, st>>>(a, x, dZ, dgates, dY);
-  } else {
-    return fail(FSC_ERR_UNSUPPORTED, "ictd conv kernels support channels 32 or 64");
-  }
-  return check_launch("conv2_q_kernel");
+  FSC_CONV_LAUNCH(conv2_q_kernel, a, x, dZ, dgates, dY);
 }
 
 }  // namespace fsc
