@@ -74,6 +74,7 @@ _PROTOS = {
     "fsc_neighbor_fill": (C.c_int, [P, P, P, I64, I64, P, C.c_double, P, P, P, I64, P, C.c_size_t, P]),
     "fsc_csr_transpose_workspace_bytes": (C.c_size_t, [I64, I64]),
     "fsc_csr_transpose": (C.c_int, [P, P, I64, I64, P, P, P, C.c_size_t, P]),
+    "fsc_csr_transpose_static": (C.c_int, [P, P, I64, I64, P, P, P]),
     "fsc_ictd_tables_floats": (I64, []),
     "fsc_ictd_workspace_bytes": (C.c_size_t, [C.POINTER(IctdConfig), I64, I64]),
     "fsc_ictd_energy_forces": (C.c_int, [C.POINTER(IctdConfig), C.POINTER(IctdWeights), C.POINTER(Graph),

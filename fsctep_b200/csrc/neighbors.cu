@@ -17,6 +17,8 @@
 #include <cub/cub.cuh>
 
 #include <algorithm>
+#include <mutex>
+#include <string>
 #include <vector>
 
 #include "common.cuh"
@@ -477,6 +479,55 @@ int fsc_csr_transpose(const int32_t* row_ptr, const int32_t* src, int64_t num_at
     tr_sort_kernel<<<(unsigned)ceil_div(N, 8), 256, 0, st>>>(tr_ptr, N, tr_eid, tmp);
   }
   return check_launch("csr_transpose");
+}
+
+// ---- allocation-free transpose ----------------------------------------------------------
+// For callers that cannot allocate device memory (a CUDA-graph-captured MD step, a host
+// program bound to a fixed memory pool, an FFI binding with no allocator): the scratch lives
+// in a file-scope __device__ array that every GPU loading this library keeps until exit.
+namespace {
+constexpr int64_t kStaticMaxAtoms = 262144;       // rows of the CSR
+constexpr int64_t kStaticMaxEdges = 4194304;      // edges
+constexpr size_t kStaticScanBytes = (1u << 20) + 4096;  // scan temporaries + arena rounding
+constexpr size_t kStaticScratchBytes = sizeof(int32_t) * (2 * (kStaticMaxAtoms + 1) + kStaticMaxEdges + 64) +
+                                       kStaticScanBytes;
+__device__ __align__(256) unsigned char g_transpose_scratch[kStaticScratchBytes];
+
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[64] = {};
+
+// Device address of g_transpose_scratch on the current device (looked up once per device).
+int static_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(FSC_ERR_CUDA, "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_transpose_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(FSC_ERR_CUDA, std::string("cudaGetSymbolAddress(g_transpose_scratch): ") + cudaGetErrorString(e));
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return FSC_OK;
+}
+}  // namespace
+
+int fsc_csr_transpose_static(const int32_t* row_ptr, const int32_t* src, int64_t num_atoms, int64_t num_edges,
+                             int32_t* tr_ptr, int32_t* tr_eid, void* stream) {
+  FSC_REQUIRE(num_atoms >= 0 && num_edges >= 0, "negative size");
+  if (num_atoms > kStaticMaxAtoms || num_edges > kStaticMaxEdges)
+    return fail(FSC_ERR_CAPACITY, "fsc_csr_transpose_static handles at most " + std::to_string(kStaticMaxAtoms) +
+                                      " atoms and " + std::to_string(kStaticMaxEdges) + " edges (got " +
+                                      std::to_string(num_atoms) + ", " + std::to_string(num_edges) +
+                                      "); use fsc_csr_transpose with a caller workspace");
+  if (scan_temp_bytes(num_atoms + 1) + 16 > kStaticScanBytes)
+    return fail(FSC_ERR_CAPACITY, "scan temporaries exceed the static scratch");
+  void* scratch = nullptr;
+  FSC_TRY(static_scratch(&scratch));
+  // Same kernels and layout as fsc_csr_transpose; the counters are cleared on every call.
+  return fsc_csr_transpose(row_ptr, src, num_atoms, num_edges, tr_ptr, tr_eid, scratch, kStaticScratchBytes,
+                           stream);
 }
 
 size_t fsc_csr_transpose_workspace_bytes(int64_t num_atoms, int64_t num_edges) {

@@ -146,6 +146,19 @@ int fsc_csr_transpose(const int32_t* row_ptr, const int32_t* src, int64_t num_at
                       int64_t num_edges, int32_t* tr_ptr, int32_t* tr_eid, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* Allocation-free transpose, for callers that cannot call cudaMalloc (a CUDA-graph-captured
+ * MD step, a host that hands all device memory to a fixed pool, an FFI binding without a
+ * device allocator).  No counterpart in the reference.  Same result as fsc_csr_transpose,
+ * but its scratch is a file-scope __device__ array of this library (about 19 MiB, held on
+ * every GPU that loads the library until exit), so it accepts at most 262,144 atoms and
+ * 4,194,304 edges and returns FSC_ERR_CAPACITY beyond that.  It allocates nothing.  The
+ * first call on a device looks up the array's device address (cudaGetSymbolAddress, once
+ * per device, with that device current); make that first call before any stream capture.
+ * All calls share the one array and it keeps the last call's contents: calls that overlap
+ * on the GPU (different streams, or different host threads on one device) race.        */
+int fsc_csr_transpose_static(const int32_t* row_ptr, const int32_t* src, int64_t num_atoms,
+                             int64_t num_edges, int32_t* tr_ptr, int32_t* tr_eid, void* stream);
+
 /* ---- pure-cartesian-ictd energy + forces + virial -------------------------
  * One call = PureCartesianICTDTransformerLayer forward (pure_cartesian_ictd_layers_full.py:
  * 867-1078) followed by a hand-written backward giving dE/dpos and the per-edge
