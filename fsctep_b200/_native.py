@@ -85,6 +85,7 @@ _PROTOS = {
                                     C.POINTER(IctdOutputs), P, C.c_size_t, P]),
     "fsc_ictd_status": (C.c_int, [C.POINTER(IctdConfig), I64, I64, P, P, C.POINTER(C.c_int)]),
     "fsc_ictd_set_readout_path": (None, [C.c_int]),
+    "fsc_ictd_set_radial_path": (None, [C.c_int]),
     "fsc_profile_enable": (None, [C.c_int]),
     "fsc_profile_read": (C.c_int, [C.POINTER(C.c_char_p), C.POINTER(C.c_float), C.c_int]),
     "fsc_ictd_energy": (C.c_int, [C.POINTER(IctdConfig), C.POINTER(IctdWeights), C.POINTER(Graph), P, P, P,

@@ -70,6 +70,7 @@ struct Plan {
   float* chunkbuf;
   // tensor-core readout
   bool tc;
+  bool rtc;  // radial MLPs on tensor cores
   int64_t n_pad;
   float* Fg;
   float* dFg;
@@ -77,6 +78,7 @@ struct Plan {
 };
 
 int g_readout_path = 0;  // 0: tensor cores where supported, 1: CUDA cores
+int g_radial_path = 0;   // 0: tensor cores where supported, 1: CUDA cores
 
 int validate(const fsc_ictd_config* cfg) {
   FSC_REQUIRE(cfg != nullptr, "config is null");
@@ -137,6 +139,7 @@ void layout(Plan& p, Arena& ar, const fsc_ictd_config* cfg, int64_t N, int64_t E
   p.dY = ar.take<float>(E * 12);
   p.edge_grad = ar.take<float>(E * 3);
   p.tc = g_readout_path == 0 && readout_tc_supported(p.nC, p.S);
+  p.rtc = g_radial_path == 0 && radial_tc_supported(p.nb);
   p.n_pad = ceil_div(std::max<int64_t>(N, 1), 128) * 128;
   p.err = ar.take<int>(64);
   if (p.tc) {
@@ -250,7 +253,15 @@ int forward(Ctx& c) {
   ef.E = p.E; ef.pos = g->pos; ef.src = g->src; ef.dst = p.dst; ef.batch = g->batch; ef.cell = g->cell;
   ef.shift = g->shift; ef.tables = w->tables; ef.rad = radial(w); ef.nint = p.nint; ef.nb = p.nb;
   ef.basis_kind = c.cfg->basis_kind; ef.rc = c.cfg->max_radius; ef.edge_y = p.edge_y; ef.gates = p.gates;
-  FSC_TRY(launch_edge_forward(ef, st));
+  if (p.rtc) {
+    FSC_TRY(launch_edge_geom(ef, st));
+    RadialTcArgs ra{};
+    ra.E = p.E; ra.rad = ef.rad; ra.nint = p.nint; ra.nb = p.nb; ra.basis_kind = ef.basis_kind; ra.rc = ef.rc;
+    ra.tables = w->tables; ra.edge_y = p.edge_y; ra.gates = p.gates; ra.err = p.err;
+    FSC_TRY(launch_radial_fwd_tc(ra, st));
+  } else {
+    FSC_TRY(launch_edge_forward(ef, st));
+  }
   prof::mark("edge_forward", st);
   FSC_TRY(launch_conv1_forward(conv_args(c, 0), w->ai, w->vsp, p.feats[0], st));
   prof::mark("conv1_forward", st);
@@ -473,7 +484,15 @@ int run_backward(Ctx& c, fsc_ictd_outputs* out) {
   eb.edge_y = c.p.edge_y; eb.dgates = c.p.dgates; eb.dY = c.p.dY;
   eb.edge_grad = out->edge_grad ? out->edge_grad : c.p.edge_grad;
   eb.virial = nullptr;
-  FSC_TRY(launch_edge_backward(eb, c.st));
+  if (c.p.rtc) {
+    RadialTcArgs ra{};
+    ra.E = c.p.E; ra.rad = eb.rad; ra.nint = c.p.nint; ra.nb = c.p.nb; ra.basis_kind = eb.basis_kind; ra.rc = eb.rc;
+    ra.tables = c.w->tables; ra.edge_y = c.p.edge_y; ra.dgates = c.p.dgates; ra.dY = c.p.dY;
+    ra.edge_grad = eb.edge_grad; ra.err = c.p.err;
+    FSC_TRY(launch_radial_bwd_tc(ra, c.st));
+  } else {
+    FSC_TRY(launch_edge_backward(eb, c.st));
+  }
   prof::mark("edge_backward", c.st);
   if (out->forces) FSC_TRY(launch_forces(g->row_ptr, g->tr_ptr, g->tr_eid, eb.edge_grad, out->forces, c.p.N, c.st));
   const int64_t nfin = 9 * c.p.B;
@@ -565,6 +584,7 @@ int fsc_ictd_status(const fsc_ictd_config* cfg, int64_t num_atoms, int64_t num_e
 }
 
 void fsc_ictd_set_readout_path(int path) { fsc::g_readout_path = path; }
+void fsc_ictd_set_radial_path(int path) { fsc::g_radial_path = path; }
 
 void fsc_profile_enable(int enable) {
   fsc::prof::enabled = enable != 0;

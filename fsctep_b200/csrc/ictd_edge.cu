@@ -14,6 +14,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "edge_common.cuh"
 #include "ictd_paths.cuh"
 #include "kernels.cuh"
 
@@ -48,31 +49,6 @@ __device__ __forceinline__ void load_radial(RadialSmem& s, const RadialW& W, int
     s.w3t[i] = q < RAD_P ? w3[q * RAD_H + j] : 0.f;
   }
   if (threadIdx.x < 12) s.b3[threadIdx.x] = threadIdx.x < RAD_P ? W.b3[layer * RAD_P + threadIdx.x] : 0.f;
-}
-
-// Radial basis value and derivative (e3nn soft_one_hot_linspace, cutoff=True), times sqrt(nb).
-__device__ __forceinline__ void radial_basis(int kind, int nb, float rc, float x, float* emb, float* demb) {
-  const float scale = sqrtf((float)nb);
-  if (kind == 0) {  // gaussian: exp(-((x - mu_b)/step)^2) / 1.12, mu_b = (b+1) step, step = rc/(nb+1)
-    const float step = rc / (float)(nb + 1);
-    for (int b = 0; b < nb; ++b) {
-      float d = (x - (float)(b + 1) * step) / step;
-      float v = expf(-d * d) * (scale / 1.12f);
-      emb[b] = v;
-      if (demb) demb[b] = v * (-2.f * d / step);
-    }
-  } else {  // bessel: sqrt(2/c) sin(b pi x / c) / x on 0 < x < c
-    const float pre = sqrtf(2.f / rc) * scale;
-    const bool inside = (x > 0.f) && (x / rc < 1.f);
-    for (int b = 0; b < nb; ++b) {
-      float w = (float)(b + 1) * 3.14159265358979323846f / rc;
-      float s, c;
-      sincosf(w * x, &s, &c);
-      float v = inside ? pre * s / x : 0.f;
-      emb[b] = v;
-      if (demb) demb[b] = inside ? pre * (w * c * x - s) / (x * x) : 0.f;
-    }
-  }
 }
 
 // Radial MLP forward for one edge: gates[q] = W3 silu(W2 silu(W1 emb + b1) + b2) + b3.
@@ -159,7 +135,7 @@ __global__ void __launch_bounds__(EDGE_TPB) edge_forward_kernel(EdgeFwdArgs a) {
       }
       const float len = sqrtf(r[0] * r[0] + r[1] * r[1] + r[2] * r[2]);
       float emb[16];
-      radial_basis(a.basis_kind, a.nb, a.rc, len, emb, nullptr);
+      radial_basis<16>(a.basis_kind, a.nb, a.rc, len, emb, nullptr);
       float gates[12];
       radial_mlp(s, a.nb, emb, gates);
       float4* g4 = reinterpret_cast<float4*>(a.gates + ((int64_t)layer * a.E + e) * 12);
@@ -191,7 +167,7 @@ __global__ void __launch_bounds__(EDGE_TPB) edge_backward_kernel(EdgeBwdArgs a) 
       const float* ey = a.edge_y + 12 * e;
       const float len = sqrtf(ey[9] * ey[9] + ey[10] * ey[10] + ey[11] * ey[11]);
       float emb[16], demb[16];
-      radial_basis(a.basis_kind, a.nb, a.rc, len, emb, demb);
+      radial_basis<16>(a.basis_kind, a.nb, a.rc, len, emb, demb);
       float dg[12];
       const float4* dg4 = reinterpret_cast<const float4*>(a.dgates + ((int64_t)layer * a.E + e) * 12);
       {
@@ -251,29 +227,12 @@ __global__ void __launch_bounds__(EDGE_TPB) edge_backward_kernel(EdgeBwdArgs a) 
     if (e >= a.E) continue;
     const float* ey = a.edge_y + 12 * e;
     const float rx = ey[9], ry = ey[10], rz = ey[11];
-    const float len = sqrtf(rx * rx + ry * ry + rz * rz);
-    const float inv = 1.f / fmaxf(len, 1e-8f);
-    const float nx = rx * inv, ny = ry * inv, nz = rz * inv;
-    float gx[ictd2::NMONO], gy[ictd2::NMONO], gz[ictd2::NMONO];
-    ictd2::monomial_grads(nx, ny, nz, gx, gy, gz);
-    const float* dY = a.dY + 12 * e;
-    float dnx = 0.f, dny = 0.f, dnz = 0.f;
+    float dYe[ictd2::NK];
 #pragma unroll
-    for (int m = 0; m < ictd2::NMONO; ++m) {
-      float w = 0.f;
-#pragma unroll
-      for (int k = 0; k < ictd2::NK; ++k) w = fmaf(ypoly[m * ictd2::NK + k], dY[k], w);
-      dnx = fmaf(w, gx[m], dnx);
-      dny = fmaf(w, gy[m], dny);
-      dnz = fmaf(w, gz[m], dnz);
-    }
-    // n = r / max(|r|, 1e-8): dn/dr = (I - n n^T)/|r| (|r| > 1e-8)
-    const float dot = dnx * nx + dny * ny + dnz * nz;
-    const float dl = dlen[t];
-    float g0 = dl * nx + (dnx - dot * nx) * inv;
-    float g1 = dl * ny + (dny - dot * ny) * inv;
-    float g2 = dl * nz + (dnz - dot * nz) * inv;
-    if (!(len > 1e-8f)) { g0 = dl * nx + dnx * inv; g1 = dl * ny + dny * inv; g2 = dl * nz + dnz * inv; }
+    for (int k = 0; k < ictd2::NK; ++k) dYe[k] = a.dY[12 * e + k];
+    float gg3[3];
+    edge_direction_grad(ypoly, rx, ry, rz, dYe, dlen[t], gg3);
+    const float g0 = gg3[0], g1 = gg3[1], g2 = gg3[2];
     a.edge_grad[3 * e + 0] = g0;
     a.edge_grad[3 * e + 1] = g1;
     a.edge_grad[3 * e + 2] = g2;
@@ -311,6 +270,45 @@ __global__ void edge_dst_kernel(const int32_t* __restrict__ row_ptr, int32_t* __
   const int64_t n = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   if (n >= N) return;
   for (int e = row_ptr[n] + (threadIdx.x & 31); e < row_ptr[n + 1]; e += 32) dst[e] = (int32_t)n;
+}
+
+// Edge geometry only: r_e and Y(n_e) into edge_y (the layer-independent part of edge_forward).
+__global__ void __launch_bounds__(256) edge_geom_kernel(EdgeFwdArgs a) {
+  __shared__ float ypoly[ictd2::NMONO * ictd2::NK];
+  for (int i = threadIdx.x; i < ictd2::NMONO * ictd2::NK; i += blockDim.x) ypoly[i] = a.tables[ictd2::TAB_YPOLY + i];
+  __syncthreads();
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= a.E) return;
+  const int i = a.src[e], j = a.dst[e];
+  const float* cell = a.cell + 9 * (int64_t)a.batch[i];
+  const float s0 = a.shift[3 * e + 0], s1 = a.shift[3 * e + 1], s2 = a.shift[3 * e + 2];
+  float y[12];
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    const float sv = s0 * cell[c] + s1 * cell[3 + c] + s2 * cell[6 + c];
+    y[9 + c] = a.pos[3 * (int64_t)j + c] - a.pos[3 * (int64_t)i + c] + sv;
+  }
+  const float len = sqrtf(y[9] * y[9] + y[10] * y[10] + y[11] * y[11]);
+  const float inv = 1.f / fmaxf(len, 1e-8f);
+  float mono[ictd2::NMONO];
+  ictd2::monomials(y[9] * inv, y[10] * inv, y[11] * inv, mono);
+#pragma unroll
+  for (int k = 0; k < ictd2::NK; ++k) {
+    float v = 0.f;
+#pragma unroll
+    for (int m = 0; m < ictd2::NMONO; ++m) v = fmaf(ypoly[m * ictd2::NK + k], mono[m], v);
+    y[k] = v;
+  }
+  float4* out4 = reinterpret_cast<float4*>(a.edge_y + 12 * e);
+  out4[0] = make_float4(y[0], y[1], y[2], y[3]);
+  out4[1] = make_float4(y[4], y[5], y[6], y[7]);
+  out4[2] = make_float4(y[8], y[9], y[10], y[11]);
+}
+
+int launch_edge_geom(const EdgeFwdArgs& a, cudaStream_t st) {
+  if (a.E == 0) return FSC_OK;
+  edge_geom_kernel<<<(unsigned)ceil_div(a.E, 256), 256, 0, st>>>(a);
+  return check_launch("edge_geom_kernel");
 }
 
 int launch_edge_forward(const EdgeFwdArgs& a, cudaStream_t st) {

@@ -42,6 +42,25 @@ struct EdgeBwdArgs {
 };
 
 int launch_edge_forward(const EdgeFwdArgs& a, cudaStream_t st);
+int launch_edge_geom(const EdgeFwdArgs& a, cudaStream_t st);
+
+// Radial MLPs on tcgen05 (radial_tc.cu).
+struct RadialTcArgs {
+  int64_t E;
+  RadialW rad;
+  int nint, nb, basis_kind;
+  float rc;
+  const float* tables;   // ypoly
+  const float* edge_y;   // [E][12]
+  float* gates;          // forward output [nint][E][12]
+  const float* dgates;   // backward input [nint][E][12]
+  const float* dY;       // backward input [E][12]
+  float* edge_grad;      // backward output [E][3]
+  int* err;              // first failing wait site (0 = ok)
+};
+bool radial_tc_supported(int nb);
+int launch_radial_fwd_tc(const RadialTcArgs& a, cudaStream_t st);
+int launch_radial_bwd_tc(const RadialTcArgs& a, cudaStream_t st);
 int launch_edge_backward(const EdgeBwdArgs& a, cudaStream_t st);
 int launch_forces(const int32_t* row_ptr, const int32_t* tr_ptr, const int32_t* tr_eid, const float* g,
                   float* F, int64_t N, cudaStream_t st);

@@ -1,0 +1,534 @@
+// Per-edge radial MLPs of the ictd layers on the 5th-generation tensor cores.
+//
+// Forward, per layer (fc / fc2_layers, pure_cartesian_ictd_layers_full.py:277-283, 693-699):
+//   gates = W3 silu(W2 silu(W1 emb + b1) + b2) + b3,   emb = radial basis of |r_e| (nb <= 16)
+// Backward, per layer (the adjoint autograd replays, evaluation/calculator.py:158-159):
+//   dh2 = W3^T dgates, da2 = dh2 * silu'(a2), dh1 = W2^T da2, da1 = dh1 * silu'(a1),
+//   dE/d|r| += (W1^T da1) . demb/d|r|
+// and, after the last layer, the direction part dE/dY -> dE/dr (edge_grad).
+//
+// One CTA owns a tile of 128 edges (thread = edge = TMEM lane = MMA row) and walks its tiles
+// persistently.  Every matrix product of the MLP is a chain of tcgen05.mma (kind::tf32,
+// M = 128) with the activations as the A operand in TMEM and the layer's weights as B operand
+// images in shared memory.  fp32 accuracy comes from the 3xTF32 split (hi*hi + hi*lo + lo*hi).
+// The element-wise steps (bias, SiLU and its derivative, tf32 split) run on the CUDA cores
+// between the MMA chains, reading the accumulators with tcgen05.ld and writing the next A with
+// tcgen05.st.  Two CTAs share an SM (256 TMEM columns each) so one CTA's element-wise work
+// overlaps the other's MMAs.
+//
+// TMEM columns of a CTA: D0 = [0, 64), D1 = [64, 128), A hi = [128, 192), A lo = [192, 256).
+// Where D1 is free, a K = 64 product is split over two accumulators (D0, D1) and an N = 16
+// product over eight (16 columns each in [0, 128)), summed on the CUDA cores.
+#include "common.cuh"
+#include "edge_common.cuh"
+#include "kernels.cuh"
+#include "tc_common.cuh"
+
+namespace fsc {
+
+namespace {
+
+constexpr int RT = 128;      // edges per tile
+constexpr int RH = 64;       // hidden width (fixed by the reference)
+constexpr int RP = 11;       // gates per layer
+constexpr int RT_PER_SM = 2; // CTAs per SM
+constexpr uint32_t kMinSmem = 80u * 1024u;  // keeps at most two CTAs (512 TMEM columns) per SM
+
+// B-operand image of a row-major N x K matrix for a K-major, no-swizzle descriptor: element
+// (n, k) at float (k/4)*4N + 4n + k%4.  The 8-wide K step j starts at byte 32*N*j; the second
+// 4-wide K half is LBO = 16*N bytes further, the next 8 rows SBO = 128 bytes further.
+__device__ __forceinline__ int bimg(int n, int k, int N) { return (k >> 2) * 4 * N + 4 * n + (k & 3); }
+
+template <int NBP>
+struct FwdImg {
+  static constexpr int W1 = 0;                // [64][NBP]   B[k][b] = W1[k][b]
+  static constexpr int W2 = W1 + RH * NBP;    // [64][64]    B[j][k] = W2[j][k]
+  static constexpr int W3 = W2 + RH * RH;     // [16][64]    B[q][j] = W3[q][j] (q >= 11 zero)
+  static constexpr int SIZE = W3 + 16 * RH;
+};
+
+template <int NBP>
+struct BwdImg {
+  static constexpr int W1 = 0;                // [64][NBP]   B[k][b] = W1[k][b]
+  static constexpr int W3P = W1 + RH * NBP;   // [64][16]    B[j][q] = W3[q][j]
+  static constexpr int W2 = W3P + RH * 16;    // [64][64]    B[j][k] = W2[j][k]
+  static constexpr int W2T = W2 + RH * RH;    // [64][64]    B[k][j] = W2[j][k]
+  static constexpr int W1T = W2T + RH * RH;   // [16][64]    B[b][k] = W1[k][b] (b >= nb zero)
+  static constexpr int SIZE = W1T + 16 * RH;
+};
+
+// Shared memory: hi images, lo images, biases, ypoly, mbarrier, TMEM slot.
+template <int SIZE>
+struct RtSmem {
+  static constexpr uint32_t HI = 0;
+  static constexpr uint32_t LO = 4u * SIZE;
+  static constexpr uint32_t BIAS = 8u * SIZE;                   // b1[64], b2[64], b3[16]
+  static constexpr uint32_t YPOLY = BIAS + 4u * 144;            // [NMONO][NK]
+  static constexpr uint32_t BAR = (YPOLY + 4u * 96 + 15u) & ~15u;
+  static constexpr uint32_t TOTAL_RAW = BAR + 16;
+  static constexpr uint32_t TOTAL = TOTAL_RAW > kMinSmem ? TOTAL_RAW : kMinSmem;
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Writes element (n, k) of a B image, split into tf32 hi and lo.
+__device__ __forceinline__ void put_b(float* hi, float* lo, int off, int N, int n, int k, float v) {
+  uint32_t h, l;
+  tc::split_tf32(v, h, l);
+  hi[off + bimg(n, k, N)] = __uint_as_float(h);
+  lo[off + bimg(n, k, N)] = __uint_as_float(l);
+}
+
+__device__ __forceinline__ void load_bias(float* bias, const RadialW& W, int layer) {
+  for (int i = threadIdx.x; i < 144; i += blockDim.x) {
+    float v;
+    if (i < RH) v = W.b1[layer * RH + i];
+    else if (i < 2 * RH) v = W.b2[layer * RH + i - RH];
+    else v = (i - 2 * RH) < RP ? W.b3[layer * RP + i - 2 * RH] : 0.f;
+    bias[i] = v;
+  }
+}
+
+// D = A x B^T over `ksteps` 8-wide K steps with the 3xTF32 split.  The tensor core truncates
+// every accumulation toward zero, which biases long chains; so the two small cross terms of all
+// K steps are accumulated before the hi*hi terms, and K step j goes to accumulator j % nacc
+// (at column d + (j % nacc) * acc_cols), which the CUDA cores add up with round-to-nearest.
+__device__ __forceinline__ void mma_3xtf32(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo,
+                                           int N, int ksteps, uint32_t idesc, int nacc = 1, uint32_t acc_cols = 0) {
+  for (int j = 0; j < ksteps; ++j) {
+    const uint32_t dj = d + (uint32_t)(j % nacc) * acc_cols;
+    const uint64_t dh = tc::smem_desc_kmajor(b_hi + 32u * N * j, 16u * N, 128);
+    const uint64_t dl = tc::smem_desc_kmajor(b_lo + 32u * N * j, 16u * N, 128);
+    tc::mma_tf32_ts(dj, a_hi + 8u * j, dl, idesc, j >= nacc);
+    tc::mma_tf32_ts(dj, a_lo + 8u * j, dh, idesc, 1);
+  }
+  for (int j = 0; j < ksteps; ++j) {
+    const uint32_t dj = d + (uint32_t)(j % nacc) * acc_cols;
+    const uint64_t dh = tc::smem_desc_kmajor(b_hi + 32u * N * j, 16u * N, 128);
+    tc::mma_tf32_ts(dj, a_hi + 8u * j, dh, idesc, 1);
+  }
+}
+
+// Sum of the eight 16-column accumulators of an N = 16 product at columns [t, t + 128).
+__device__ __forceinline__ void ld_sum16x8(uint32_t t, float* out) {
+#pragma unroll
+  for (int q = 0; q < 16; ++q) out[q] = 0.f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t u[32];
+    tc::tmem_ld32(t + 32u * c, u);
+    tc::tmem_wait_ld();
+#pragma unroll
+    for (int q = 0; q < 16; ++q) out[q] += __uint_as_float(u[q]) + __uint_as_float(u[16 + q]);
+  }
+}
+
+// Splits 32 values into tf32 hi / lo and stores them as 32 A columns at `col`.
+__device__ __forceinline__ void store_a32(uint32_t t_ahi, uint32_t t_alo, uint32_t col, const float* v) {
+  uint32_t hi[32], lo[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) tc::split_tf32(v[i], hi[i], lo[i]);
+  tc::tmem_st32(t_ahi + col, hi);
+  tc::tmem_st32(t_alo + col, lo);
+}
+
+// Hand-off from the CUDA-core phase to the MMA issuer: every thread's tcgen05.st is complete and
+// ordered before the barrier.
+__device__ __forceinline__ void a_ready() {
+  tc::tmem_wait_st();
+  tc::tc_fence_before();
+  __syncthreads();
+}
+
+// Waits for the commit of the last MMA chain (all threads).  Returns false block-uniformly when
+// the wait timed out anywhere in the block.
+__device__ __forceinline__ bool d_ready(uint64_t* bar, uint32_t& phase, int* err, int where) {
+  const bool ok = tc::mbar_wait(bar, phase, err, where);
+  phase ^= 1u;
+  tc::tc_fence_after();
+  return !__syncthreads_or(!ok);
+}
+
+// After a timed-out wait: bounded wait for the chain still committed to `bar` before the TMEM
+// it writes is released.
+__device__ __forceinline__ void drain(uint64_t* bar, uint32_t phase) {
+  for (uint32_t i = 0; i < tc::kSpinLimit; ++i) {
+    if (tc::mbar_try_wait(bar, phase ^ 1u)) return;
+    __nanosleep(64);
+  }
+}
+
+// ------------------------------------------------------------------ forward
+template <int NBP>
+__global__ void __launch_bounds__(RT, RT_PER_SM) radial_fwd_tc_kernel(RadialTcArgs a) {
+  using IM = FwdImg<NBP>;
+  using SM = RtSmem<IM::SIZE>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  float* img_hi = reinterpret_cast<float*>(smem + SM::HI);
+  float* img_lo = reinterpret_cast<float*>(smem + SM::LO);
+  float* bias = reinterpret_cast<float*>(smem + SM::BIAS);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + SM::BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::BAR + 8);
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_slot, 256);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    tc::mbar_init(bar, 1);
+    tc::fence_mbar_init();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const uint32_t tD0 = tbase, tD1 = tbase + 64u, tAhi = tbase + 128u, tAlo = tbase + 192u;
+  const uint32_t s_hi = tc::smem_u32(img_hi), s_lo = tc::smem_u32(img_lo);
+  constexpr uint32_t id64 = tc::idesc_tf32(RT, 64), id16 = tc::idesc_tf32(RT, 16);
+  const int64_t ntiles = (a.E + RT - 1) / RT;
+  uint32_t phase = 0;
+  bool ok = true;
+
+  for (int layer = 0; layer < a.nint && ok; ++layer) {
+    // ---- this layer's weights as B images
+    __syncthreads();
+    const float* w1 = a.rad.w1 + (size_t)layer * RH * a.nb;
+    const float* w2 = a.rad.w2 + (size_t)layer * RH * RH;
+    const float* w3 = a.rad.w3 + (size_t)layer * RP * RH;
+    for (int i = tid; i < RH * NBP; i += RT) {
+      const int k = i / NBP, b = i - k * NBP;
+      put_b(img_hi, img_lo, IM::W1, RH, k, b, b < a.nb ? w1[k * a.nb + b] : 0.f);
+    }
+    for (int i = tid; i < RH * RH; i += RT) put_b(img_hi, img_lo, IM::W2, RH, i >> 6, i & 63, w2[i]);
+    for (int i = tid; i < 16 * RH; i += RT) {
+      const int q = i >> 6, j = i & 63;
+      put_b(img_hi, img_lo, IM::W3, 16, q, j, q < RP ? w3[q * RH + j] : 0.f);
+    }
+    load_bias(bias, a.rad, layer);
+    fence_proxy_async_smem();
+    __syncthreads();
+
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      const int64_t e = tile * RT + tid;
+      const bool valid = e < a.E;
+      // ---- A = emb
+      {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        if (valid) {
+          const float4 ry = reinterpret_cast<const float4*>(a.edge_y + 12 * e)[2];
+          const float len = sqrtf(ry.y * ry.y + ry.z * ry.z + ry.w * ry.w);
+          radial_basis<NBP>(a.basis_kind, a.nb, a.rc, len, v, nullptr);
+        }
+        store_a32(tAhi + lane_off, tAlo + lane_off, 0, v);
+      }
+      a_ready();
+      if (tid == 0) {
+        tc::tc_fence_after();
+        mma_3xtf32(tD0, tAhi, tAlo, s_hi + 4u * IM::W1, s_lo + 4u * IM::W1, 64, NBP / 8, id64);
+        tc::mma_commit(bar);
+      }
+      if (!(ok = d_ready(bar, phase, a.err, 41))) break;
+      // ---- h1 = silu(D0 + b1) -> A ; D0 = h1 W2^T
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t u[32];
+        float v[32];
+        tc::tmem_ld32(tD0 + lane_off + 32u * h, u);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = silu(__uint_as_float(u[i]) + bias[32 * h + i]);
+        store_a32(tAhi + lane_off, tAlo + lane_off, 32u * h, v);
+      }
+      a_ready();
+      if (tid == 0) {
+        tc::tc_fence_after();
+        mma_3xtf32(tD0, tAhi, tAlo, s_hi + 4u * IM::W2, s_lo + 4u * IM::W2, 64, RH / 8, id64, 2, 64);
+        tc::mma_commit(bar);
+      }
+      if (!(ok = d_ready(bar, phase, a.err, 42))) break;
+      // ---- h2 = silu(D0 + D1 + b2) -> A ; D0..D1 = h2 W3^T (eight 16-column accumulators)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t u[32], w[32];
+        float v[32];
+        tc::tmem_ld32(tD0 + lane_off + 32u * h, u);
+        tc::tmem_ld32(tD1 + lane_off + 32u * h, w);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = silu((__uint_as_float(u[i]) + __uint_as_float(w[i])) + bias[RH + 32 * h + i]);
+        store_a32(tAhi + lane_off, tAlo + lane_off, 32u * h, v);
+      }
+      a_ready();
+      if (tid == 0) {
+        tc::tc_fence_after();
+        mma_3xtf32(tD0, tAhi, tAlo, s_hi + 4u * IM::W3, s_lo + 4u * IM::W3, 16, RH / 8, id16, 8, 16);
+        tc::mma_commit(bar);
+      }
+      if (!(ok = d_ready(bar, phase, a.err, 43))) break;
+      // ---- gates = sum of the accumulators + b3
+      {
+        float gs[16];
+        ld_sum16x8(tD0 + lane_off, gs);
+        if (valid) {
+          float g[12];
+#pragma unroll
+          for (int q = 0; q < 12; ++q) g[q] = q < RP ? gs[q] + bias[2 * RH + q] : 0.f;
+          float4* g4 = reinterpret_cast<float4*>(a.gates + ((int64_t)layer * a.E + e) * 12);
+          g4[0] = make_float4(g[0], g[1], g[2], g[3]);
+          g4[1] = make_float4(g[4], g[5], g[6], g[7]);
+          g4[2] = make_float4(g[8], g[9], g[10], 0.f);
+        }
+      }
+      tc::tc_fence_before();  // the next tile's tcgen05.st into A follows this tile's loads
+    }
+  }
+  if (!ok && tid == 0) drain(bar, phase);
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tbase, 256);
+  }
+}
+
+// ------------------------------------------------------------------ backward
+template <int NBP>
+__global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcArgs a) {
+  using IM = BwdImg<NBP>;
+  using SM = RtSmem<IM::SIZE>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  float* img_hi = reinterpret_cast<float*>(smem + SM::HI);
+  float* img_lo = reinterpret_cast<float*>(smem + SM::LO);
+  float* bias = reinterpret_cast<float*>(smem + SM::BIAS);
+  float* ypoly = reinterpret_cast<float*>(smem + SM::YPOLY);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + SM::BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::BAR + 8);
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  for (int i = tid; i < ictd2::NMONO * ictd2::NK; i += RT) ypoly[i] = a.tables[ictd2::TAB_YPOLY + i];
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_slot, 256);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    tc::mbar_init(bar, 1);
+    tc::fence_mbar_init();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const uint32_t tD0 = tbase, tD1 = tbase + 64u, tAhi = tbase + 128u, tAlo = tbase + 192u;
+  const uint32_t s_hi = tc::smem_u32(img_hi), s_lo = tc::smem_u32(img_lo);
+  constexpr uint32_t id64 = tc::idesc_tf32(RT, 64), id16 = tc::idesc_tf32(RT, 16);
+  const int64_t ntiles = (a.E + RT - 1) / RT;
+  uint32_t phase = 0;
+  bool ok = true;
+
+  for (int layer = 0; layer < a.nint && ok; ++layer) {
+    __syncthreads();
+    const float* w1 = a.rad.w1 + (size_t)layer * RH * a.nb;
+    const float* w2 = a.rad.w2 + (size_t)layer * RH * RH;
+    const float* w3 = a.rad.w3 + (size_t)layer * RP * RH;
+    for (int i = tid; i < RH * NBP; i += RT) {
+      const int k = i / NBP, b = i - k * NBP;
+      const float v = b < a.nb ? w1[k * a.nb + b] : 0.f;
+      put_b(img_hi, img_lo, IM::W1, RH, k, b, v);
+    }
+    for (int i = tid; i < RH * 16; i += RT) {  // W1T rows b < 16
+      const int b = i >> 6, k = i & 63;
+      put_b(img_hi, img_lo, IM::W1T, 16, b, k, b < a.nb ? w1[k * a.nb + b] : 0.f);
+    }
+    for (int i = tid; i < RH * RH; i += RT) {
+      const int j = i >> 6, k = i & 63;
+      put_b(img_hi, img_lo, IM::W2, RH, j, k, w2[i]);
+      put_b(img_hi, img_lo, IM::W2T, RH, k, j, w2[i]);
+    }
+    for (int i = tid; i < RH * 16; i += RT) {
+      const int j = i >> 4, q = i & 15;
+      put_b(img_hi, img_lo, IM::W3P, RH, j, q, q < RP ? w3[q * RH + j] : 0.f);
+    }
+    load_bias(bias, a.rad, layer);
+    fence_proxy_async_smem();
+    __syncthreads();
+
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      const int64_t e = tile * RT + tid;
+      const bool valid = e < a.E;
+      float demb[NBP];
+      float ry[3] = {0.f, 0.f, 0.f};
+      // ---- A = [emb (NBP) | dgates (16)] ; D0 = emb W1^T (a1 - b1), D1 = dg W3 (dh2)
+      {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+#pragma unroll
+        for (int b = 0; b < NBP; ++b) demb[b] = 0.f;
+        if (valid) {
+          const float4 r4 = reinterpret_cast<const float4*>(a.edge_y + 12 * e)[2];
+          ry[0] = r4.y; ry[1] = r4.z; ry[2] = r4.w;
+          const float len = sqrtf(r4.y * r4.y + r4.z * r4.z + r4.w * r4.w);
+          radial_basis<NBP>(a.basis_kind, a.nb, a.rc, len, v, demb);
+          const float4* dg4 = reinterpret_cast<const float4*>(a.dgates + ((int64_t)layer * a.E + e) * 12);
+          const float4 g0 = dg4[0], g1 = dg4[1], g2 = dg4[2];
+          v[NBP + 0] = g0.x; v[NBP + 1] = g0.y; v[NBP + 2] = g0.z; v[NBP + 3] = g0.w;
+          v[NBP + 4] = g1.x; v[NBP + 5] = g1.y; v[NBP + 6] = g1.z; v[NBP + 7] = g1.w;
+          v[NBP + 8] = g2.x; v[NBP + 9] = g2.y; v[NBP + 10] = g2.z;
+        }
+        store_a32(tAhi + lane_off, tAlo + lane_off, 0, v);
+      }
+      a_ready();
+      if (tid == 0) {
+        tc::tc_fence_after();
+        mma_3xtf32(tD0, tAhi, tAlo, s_hi + 4u * IM::W1, s_lo + 4u * IM::W1, 64, NBP / 8, id64);
+        mma_3xtf32(tD1, tAhi + NBP, tAlo + NBP, s_hi + 4u * IM::W3P, s_lo + 4u * IM::W3P, 64, 2, id64);
+        tc::mma_commit(bar);
+      }
+      if (!(ok = d_ready(bar, phase, a.err, 51))) break;
+      // ---- h1 = silu(a1) -> A, keep silu'(a1) ; D0 = h1 W2^T (a2 - b2)
+      float sg1[RH];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t u[32];
+        float v[32];
+        tc::tmem_ld32(tD0 + lane_off + 32u * h, u);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float x = __uint_as_float(u[i]) + bias[32 * h + i];
+          v[i] = silu(x);
+          sg1[32 * h + i] = silu_grad(x);
+        }
+        store_a32(tAhi + lane_off, tAlo + lane_off, 32u * h, v);
+      }
+      a_ready();
+      if (tid == 0) {
+        tc::tc_fence_after();
+        mma_3xtf32(tD0, tAhi, tAlo, s_hi + 4u * IM::W2, s_lo + 4u * IM::W2, 64, RH / 8, id64);
+        tc::mma_commit(bar);
+      }
+      if (!(ok = d_ready(bar, phase, a.err, 52))) break;
+      // ---- da2 = dh2 * silu'(a2) -> A ; D0 = da2 W2 (dh1)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t u[32], w[32];
+        float v[32];
+        tc::tmem_ld32(tD0 + lane_off + 32u * h, u);
+        tc::tmem_ld32(tD1 + lane_off + 32u * h, w);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(w[i]) * silu_grad(__uint_as_float(u[i]) + bias[RH + 32 * h + i]);
+        store_a32(tAhi + lane_off, tAlo + lane_off, 32u * h, v);
+      }
+      a_ready();
+      if (tid == 0) {
+        tc::tc_fence_after();
+        mma_3xtf32(tD0, tAhi, tAlo, s_hi + 4u * IM::W2T, s_lo + 4u * IM::W2T, 64, RH / 8, id64, 2, 64);
+        tc::mma_commit(bar);
+      }
+      if (!(ok = d_ready(bar, phase, a.err, 53))) break;
+      // ---- da1 = (D0 + D1) * silu'(a1) -> A ; D0..D1 = da1 W1 (dE/demb, eight accumulators)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t u[32], w[32];
+        float v[32];
+        tc::tmem_ld32(tD0 + lane_off + 32u * h, u);
+        tc::tmem_ld32(tD1 + lane_off + 32u * h, w);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = (__uint_as_float(u[i]) + __uint_as_float(w[i])) * sg1[32 * h + i];
+        store_a32(tAhi + lane_off, tAlo + lane_off, 32u * h, v);
+      }
+      a_ready();
+      if (tid == 0) {
+        tc::tc_fence_after();
+        mma_3xtf32(tD0, tAhi, tAlo, s_hi + 4u * IM::W1T, s_lo + 4u * IM::W1T, 16, RH / 8, id16, 8, 16);
+        tc::mma_commit(bar);
+      }
+      if (!(ok = d_ready(bar, phase, a.err, 54))) break;
+      // ---- dE/d|r| of this layer; the last layer also applies the direction part
+      {
+        float de[16];
+        ld_sum16x8(tD0 + lane_off, de);
+        if (valid) {
+          float dl = 0.f;
+#pragma unroll
+          for (int b = 0; b < NBP; ++b) dl = fmaf(de[b], demb[b], dl);
+          float* eg = a.edge_grad + 3 * e;
+          if (layer > 0) dl += eg[0];
+          if (layer + 1 < a.nint) {
+            eg[0] = dl;
+          } else {
+            float dYe[ictd2::NK], g[3];
+            const float4* d4 = reinterpret_cast<const float4*>(a.dY + 12 * e);
+            const float4 d0 = d4[0], d1 = d4[1], d2 = d4[2];
+            dYe[0] = d0.x; dYe[1] = d0.y; dYe[2] = d0.z; dYe[3] = d0.w;
+            dYe[4] = d1.x; dYe[5] = d1.y; dYe[6] = d1.z; dYe[7] = d1.w; dYe[8] = d2.x;
+            edge_direction_grad(ypoly, ry[0], ry[1], ry[2], dYe, dl, g);
+            eg[0] = g[0]; eg[1] = g[1]; eg[2] = g[2];
+          }
+        }
+      }
+      tc::tc_fence_before();
+    }
+  }
+  if (!ok && tid == 0) drain(bar, phase);
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tbase, 256);
+  }
+}
+
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!cached[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+template <typename K>
+int launch_rt(K kernel, uint32_t smem, const RadialTcArgs& a, cudaStream_t st, const char* name) {
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, std::string(name) + ": cannot set shared memory size");
+  const int64_t ntiles = ceil_div(a.E, RT);
+  const int64_t grid = ntiles < (int64_t)RT_PER_SM * num_sms() ? ntiles : (int64_t)RT_PER_SM * num_sms();
+  kernel<<<(unsigned)grid, RT, smem, st>>>(a);
+  return check_launch(name);
+}
+
+}  // namespace
+
+bool radial_tc_supported(int nb) { return nb >= 1 && nb <= 16; }
+
+int launch_radial_fwd_tc(const RadialTcArgs& a, cudaStream_t st) {
+  if (a.E == 0) return FSC_OK;
+  if (!radial_tc_supported(a.nb)) return fail(FSC_ERR_UNSUPPORTED, "radial_fwd_tc: number_of_basis must be 1..16");
+  if (a.nb <= 8)
+    return launch_rt(radial_fwd_tc_kernel<8>, RtSmem<FwdImg<8>::SIZE>::TOTAL, a, st, "radial_fwd_tc_kernel<8>");
+  return launch_rt(radial_fwd_tc_kernel<16>, RtSmem<FwdImg<16>::SIZE>::TOTAL, a, st, "radial_fwd_tc_kernel<16>");
+}
+
+int launch_radial_bwd_tc(const RadialTcArgs& a, cudaStream_t st) {
+  if (a.E == 0) return FSC_OK;
+  if (!radial_tc_supported(a.nb)) return fail(FSC_ERR_UNSUPPORTED, "radial_bwd_tc: number_of_basis must be 1..16");
+  if (a.nb <= 8)
+    return launch_rt(radial_bwd_tc_kernel<8>, RtSmem<BwdImg<8>::SIZE>::TOTAL, a, st, "radial_bwd_tc_kernel<8>");
+  return launch_rt(radial_bwd_tc_kernel<16>, RtSmem<BwdImg<16>::SIZE>::TOTAL, a, st, "radial_bwd_tc_kernel<16>");
+}
+
+}  // namespace fsc

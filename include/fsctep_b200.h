@@ -284,6 +284,9 @@ int fsc_ictd_status(const fsc_ictd_config* cfg, int64_t num_atoms, int64_t num_e
                     void* stream, int* status_host);
 /* Readout path: 0 = tensor cores where supported (default), 1 = CUDA-core kernels. */
 void fsc_ictd_set_readout_path(int path);
+/* Radial MLP path (per-edge fc / fc2_layers and their backward): 0 = tensor cores where
+ * supported (default; number_of_basis <= 16), 1 = CUDA-core kernels.  Process-wide. */
+void fsc_ictd_set_radial_path(int path);
 /* Forward only (per-atom energy), same workspace. */
 int fsc_ictd_energy(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g,
                     float* energy, float* atom_energy, void* workspace, size_t workspace_bytes,

@@ -73,3 +73,38 @@ def test_tensor_core_readout_matches_cuda_core_readout(tag, n_cells):
     assert (e - er).abs().max().item() <= 1e-5 * er.abs().max().item(), (e, er)
     assert U.rel_max(out["forces"].cpu().numpy(), ref["forces"].cpu().numpy()) <= 1e-4
     assert U.rel_max(out["atom_energy"].cpu().numpy(), ref["atom_energy"].cpu().numpy()) <= 1e-4
+
+
+@pytest.mark.parametrize("nb,kind,n_cells", [(8, "gaussian", (3, 3, 3)), (12, "bessel", (5, 3, 3))])
+def test_tensor_core_radial_matches_cuda_core(nb, kind, n_cells):
+    """tcgen05 radial MLPs (default) vs the CUDA-core ones; nb=12 exercises the 16-wide padded basis."""
+    from fsctep_b200 import _native as NAT
+    from fsctep_b200 import systems
+    from fsctep_b200.ictd import ICTDConfig, ICTDEngine
+    from fsctep_b200.models import reference_state_dict_shapes
+    from fsctep_b200.neighbors import build_graph
+    from fsctep_b200.weights import seeded_state_dict
+
+    cfg = ICTDConfig(channels=32, num_interaction=3, number_of_basis=nb, max_radius=5.0, function_type=kind,
+                     max_atomvalue=16)
+    eng = ICTDEngine(seeded_state_dict(reference_state_dict_shapes(cfg), 5), cfg, "cuda")
+    s = systems.diamond_crystal(n_cells=n_cells, seed=23)
+    dev = torch.device("cuda")
+    pos, cell = torch.tensor(s["pos"], device=dev), torch.tensor(s["cell"], device=dev)
+    g = build_graph(pos, cell, 5.0)
+    assert g.num_edges % 128 != 0
+    Z, b = torch.tensor(s["Z"], device=dev), torch.tensor(s["batch"], device=dev)
+    try:
+        NAT.lib().fsc_ictd_set_radial_path(1)
+        ref = eng.energy_forces(pos, Z, b, cell, g)
+        torch.cuda.synchronize()
+        NAT.lib().fsc_ictd_set_radial_path(0)
+        out = eng.energy_forces(pos, Z, b, cell, g)
+        torch.cuda.synchronize()
+        assert eng.status() == 0
+    finally:
+        NAT.lib().fsc_ictd_set_radial_path(0)
+    e, er = out["energy"].double().cpu(), ref["energy"].double().cpu()
+    assert (e - er).abs().max().item() <= 1e-5 * er.abs().max().item(), (e, er)
+    assert U.rel_max(out["forces"].cpu().numpy(), ref["forces"].cpu().numpy()) <= 1e-4
+    assert U.rel_max(out["stress"].cpu().numpy(), ref["stress"].cpu().numpy()) <= 1e-4
