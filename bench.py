@@ -11,8 +11,11 @@ reference semantics) + forward + hand-written backward (energy, forces).
 
 ``--impl reference`` times the reference algorithm's CPU path (the oracle port of the
 reference PyTorch implementation, fp32, all host threads) on a bounded replica of the same
-workload.  Under torchrun (N > 1) every rank runs its own replica of the workload
-(independent systems, no data-path collective); the reported value is the sum over ranks.
+workload.  Under torchrun (N > 1) the crystal grows with N (weak scaling, 1,000,000 owned atoms
+per GPU) and is cut into a (2, 1, 1) / (2, 2, 1) / (2, 2, 2) grid of blocks, one per rank: each
+step exchanges a 15 A halo of ghost positions, evaluates the owned atoms' energies and forces
+on the local system, returns the ghost forces to their owners and sums the energy
+(fsctep_b200.domain); the reported value is all owned atoms / the slowest rank's time.
 """
 
 from __future__ import annotations
@@ -136,15 +139,20 @@ def algorithmic_work(stage, N, E, cfg):
 
 def run_native(args, rank, world, device):
     from fsctep_b200 import _native as NAT
+    from fsctep_b200 import domain as D
     from fsctep_b200 import systems
     from fsctep_b200.ictd import ICTDEngine
     from fsctep_b200.neighbors import build_graph
 
     w = WORKLOADS[args.workload]
     cfg = model_cfg(w)
-    sysd = systems.diamond_crystal(n_cells=w["cells"], seed=1000 + rank, Z=w["Z"])
-    n = sysd["pos"].shape[0]
     eng = ICTDEngine(seeded_weights(cfg), cfg, device)
+    dims = D.grid_for(world)
+    if world == 1:
+        sysd = systems.diamond_crystal(n_cells=w["cells"], seed=1000 + rank, Z=w["Z"])
+    else:  # this rank's block of a (dims * cells) crystal
+        sysd = systems.diamond_block(D.block_of(rank, dims), dims, n_cells=w["cells"], seed=1000 + rank, Z=w["Z"])
+    n = sysd["pos"].shape[0]
     pos_d = torch.tensor(sysd["pos"], device=device)
     cell_d = torch.tensor(sysd["cell"], device=device)
     Z = torch.tensor(sysd["Z"], device=device, dtype=torch.int32)
@@ -153,23 +161,38 @@ def run_native(args, rank, world, device):
     forces_h = torch.empty(n, 3, dtype=torch.float32).pin_memory()
     energy_h = torch.empty(1, dtype=torch.float32).pin_memory()
 
-    def step(pos, cell):
-        g = build_graph(pos, cell, cfg.max_radius)
-        energy, _ = eng.forward(pos, Z, batch, cell, g)
-        out = eng.backward(want_virial=False)
-        return energy, out["forces"], g
+    if world == 1:
+        def step(pos, cell):
+            g = build_graph(pos, cell, cfg.max_radius)
+            energy, _ = eng.forward(pos, Z, batch, cell, g)
+            out = eng.backward(want_virial=False)
+            return energy, out["forces"], {"edges": g.num_edges, "ghosts": 0}
+    else:
+        dec = D.Decomposition(sysd["cell"][0], dims, cfg.num_interaction * cfg.max_radius)
+        evaluate = D.ictd_evaluator(eng, sysd["cell"][0], cfg.max_radius)
+        info = {}
+
+        def counting_eval(p, s, nl, pbc):
+            out = evaluate(p, s, nl, pbc)
+            info["edges"] = eng._last[4].num_edges
+            return out
+
+        def step(pos, cell):
+            r = D.run_dist(D.decomposed_step(dec, rank, pos, Z, counting_eval))
+            info["ghosts"] = r["num_ghosts"]
+            return r["energy"].reshape(1), r["forces"], dict(info)
 
     def e2e_step():
         pos = pos_h.to(device, non_blocking=True)
         energy, forces, g = step(pos, cell_d)
         forces_h.copy_(forces, non_blocking=True)
-        energy_h.copy_(energy, non_blocking=True)
+        energy_h.copy_(energy.to(torch.float32), non_blocking=True)
         return g
 
     for _ in range(args.warmup):
-        _, _, g = step(pos_d, cell_d)
+        _, _, info = step(pos_d, cell_d)
     torch.cuda.synchronize()
-    E_edges = g.num_edges
+    E_edges = info["edges"]
 
     # kernel launches per step (counted once, outside the timed region)
     ours = None
@@ -215,7 +238,8 @@ def run_native(args, rank, world, device):
         torch.distributed.all_reduce(ms_total_t, op=torch.distributed.ReduceOp.MAX)
     ms_total, ms_e2e = float(ms_total_t[0]), float(ms_total_t[1])
     return dict(n=n, E=E_edges, ms_step=ms_total / args.steps, ms_e2e=ms_e2e / args.steps, stage_ms=stage_ms,
-                clocks=clk.summary(), launches=None if ours is None else ours * args.steps, cfg=cfg)
+                clocks=clk.summary(), launches=None if ours is None else ours * args.steps, cfg=cfg,
+                ghosts=info["ghosts"], dims=dims)
 
 
 def cpu_reference(steps, warmup, budget_s=None):
@@ -254,6 +278,8 @@ def cpu_reference(steps, warmup, budget_s=None):
 
 
 def main():
+    from fsctep_b200.domain import grid_for
+
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -272,7 +298,10 @@ def main():
     config = {"workload": f"{args.workload}: pure-cartesian-ictd diamond Si {n_atoms} atoms (config 4)",
               "model": "pure-cartesian-ictd", "channels": w["channels"], "num_interaction": w["num_interaction"],
               "lmax": 2, "cutoff": 5.0, "radial_basis": "gaussian x8", "atoms_per_gpu": n_atoms,
-              "parallelism": f"replicas{args.gpus}" if args.gpus > 1 else "single",
+              "parallelism": ("spatial%dx%dx%d" % grid_for(args.gpus)) if args.gpus > 1 else "single",
+              "decomposition": ("blocks of a (50 px, 50 py, 50 pz)-cell crystal, halo = num_interaction x cutoff "
+                                "= 15 A of recomputed ghosts, one position halo exchange and one reverse ghost-force "
+                                "exchange per step (NCCL all_to_all), energy all_reduce") if args.gpus > 1 else None,
               "step": "neighbour list + forward + backward (energy, forces)",
               "l2": "inputs larger than L2 (features 2.3 GB per layer at 1M atoms)"}
 
@@ -321,7 +350,8 @@ def main():
     line = {"metric": metric, "value": value, "unit": "atom-steps/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": res["ms_step"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded positions and weights)",
-            "config": config, "edges_per_gpu": E, "roofline": roofline, "clocks": res["clocks"],
+            "config": config, "edges_per_gpu": E, "ghost_atoms_per_gpu": res["ghosts"], "roofline": roofline,
+            "clocks": res["clocks"],
             "gpu_launches": res["launches"],
             "e2e": {"value": e2e_value, "unit": "atom-steps/s", "h2d_bytes_per_step": n * 3 * 8,
                     "d2h_bytes_per_step": n * 3 * 4 + 4},

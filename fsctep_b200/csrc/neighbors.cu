@@ -10,14 +10,19 @@
 // Two searches, identical results:
 //  * all pairs within a frame (any cell shape, any pbc), one thread per dst atom, candidates
 //    visited in (src, sidx) order so rows come out sorted;
-//  * cell list for a periodic orthorhombic frame whose positions lie in [0, L): cells of side
-//    >= cutoff + 1e-6, the 27 neighbour cells of the dst atom's cell are visited with their
-//    wrap count q (S = -q); every (src, S) candidate is met exactly once for any cell count
-//    per axis >= 1; rows are sorted afterwards (warp-per-row rank sort).
+//  * cell list for a frame whose periodic cell vectors are axis-aligned, with positions in
+//    [0, L) along periodic axes and anywhere along open axes (the grid spans the atoms'
+//    bounding box there): cells of side >= cutoff + 1e-6, the 27 neighbour cells of the dst
+//    atom's cell are visited, periodic axes with their wrap count q (S = -q), open axes only
+//    inside the grid (S = 0); every (src, S) candidate is met exactly once for any cell count
+//    per axis >= 1; rows are sorted afterwards (warp-per-row rank sort).  Mixed periodicity is
+//    what a spatial-decomposition rank has: open along the split axes (explicit ghost images),
+//    periodic along the others.
 #include <cub/cub.cuh>
 
 #include <algorithm>
 #include <mutex>
+#include <cstring>
 #include <string>
 #include <vector>
 
@@ -96,12 +101,13 @@ __global__ void brute_kernel(const double* __restrict__ pos, FrameDev fr, int64_
 
 struct CellGrid {
   int nc[3];
-  double L[3];
-  double inv_cs[3];
+  int per[3];        // periodic axis
+  double lo[3];      // grid origin (0 on periodic axes)
+  double inv_cs[3];  // cells per unit length
 };
 
-__device__ __forceinline__ int cell_coord(double x, double inv_cs, int n) {
-  int c = (int)floor(x * inv_cs);
+__device__ __forceinline__ int cell_coord(double x, double lo, double inv_cs, int n) {
+  int c = (int)floor((x - lo) * inv_cs);
   return c < 0 ? 0 : (c >= n ? n - 1 : c);
 }
 
@@ -110,9 +116,9 @@ __global__ void cell_assign_kernel(const double* __restrict__ pos, int64_t a0, i
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= na) return;
   const int64_t a = a0 + t;
-  const int cx = cell_coord(pos[3 * a], g.inv_cs[0], g.nc[0]);
-  const int cy = cell_coord(pos[3 * a + 1], g.inv_cs[1], g.nc[1]);
-  const int cz = cell_coord(pos[3 * a + 2], g.inv_cs[2], g.nc[2]);
+  const int cx = cell_coord(pos[3 * a], g.lo[0], g.inv_cs[0], g.nc[0]);
+  const int cy = cell_coord(pos[3 * a + 1], g.lo[1], g.inv_cs[1], g.nc[1]);
+  const int cz = cell_coord(pos[3 * a + 2], g.lo[2], g.inv_cs[2], g.nc[2]);
   const int id = (cx * g.nc[1] + cy) * g.nc[2] + cz;
   cell_of[t] = id;
   atomicAdd(cell_count + id, 1);
@@ -145,14 +151,17 @@ __global__ void cell_search_kernel(const double* __restrict__ pos, int64_t a0, i
   for (int dx = -1; dx <= 1; ++dx) {
     const int ux = cx + dx;
     const int qx = ux < 0 ? -1 : (ux >= g.nc[0] ? 1 : 0);
+    if (qx != 0 && !g.per[0]) continue;
     const int wx = ux - qx * g.nc[0];
     for (int dy = -1; dy <= 1; ++dy) {
       const int uy = cy + dy;
       const int qy = uy < 0 ? -1 : (uy >= g.nc[1] ? 1 : 0);
+      if (qy != 0 && !g.per[1]) continue;
       const int wy = uy - qy * g.nc[1];
       for (int dz = -1; dz <= 1; ++dz) {
         const int uz = cz + dz;
         const int qz = uz < 0 ? -1 : (uz >= g.nc[2] ? 1 : 0);
+        if (qz != 0 && !g.per[2]) continue;
         const int wz = uz - qz * g.nc[2];
         const int s0 = -qx, s1 = -qy, s2 = -qz;
         double sv[3];
@@ -202,13 +211,65 @@ __global__ void row_sort_kernel(const int32_t* __restrict__ row_ptr, int64_t N, 
   }
 }
 
-__global__ void out_of_box_kernel(const double* __restrict__ pos, int64_t a0, int64_t na, double Lx, double Ly,
-                                  double Lz, int32_t* __restrict__ flag) {
+// Order-preserving int64 key of a double (for atomicMin / atomicMax).
+__device__ __forceinline__ long long dkey(double x) {
+  const long long b = __double_as_longlong(x);
+  return b >= 0 ? b : (b ^ 0x7FFFFFFFFFFFFFFFLL);
+}
+__host__ __device__ inline double dkey_inv(long long k) {
+  const long long b = k >= 0 ? k : (k ^ 0x7FFFFFFFFFFFFFFFLL);
+  double x;
+  memcpy(&x, &b, sizeof(x));
+  return x;
+}
+
+// flag |= 1 if a position is outside [0, L) on a periodic axis or not finite; mm[2k] / mm[2k+1]
+// = min / max keys of coordinate k.
+__global__ void box_kernel(const double* __restrict__ pos, int64_t a0, int64_t na, int p0, int p1, int p2, double L0,
+                           double L1, double L2, int32_t* __restrict__ flag, long long* __restrict__ mm) {
+  __shared__ long long smin[3][8], smax[3][8];
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= na) return;
-  const int64_t a = a0 + t;
-  const double x = pos[3 * a], y = pos[3 * a + 1], z = pos[3 * a + 2];
-  if (!(x >= 0.0 && x < Lx && y >= 0.0 && y < Ly && z >= 0.0 && z < Lz)) atomicOr(flag, 1);
+  const int per[3] = {p0, p1, p2};
+  const double L[3] = {L0, L1, L2};
+  long long kmin[3], kmax[3];
+  bool bad = false;
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    kmin[k] = 0x7FFFFFFFFFFFFFFFLL;
+    kmax[k] = -0x7FFFFFFFFFFFFFFFLL - 1;
+  }
+  if (t < na) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const double x = pos[3 * (a0 + t) + k];
+      if (!isfinite(x) || (per[k] && !(x >= 0.0 && x < L[k]))) bad = true;
+      kmin[k] = kmax[k] = dkey(x);
+    }
+  }
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(flag, 1);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    for (int o = 16; o > 0; o >>= 1) {
+      kmin[k] = min(kmin[k], __shfl_xor_sync(0xffffffffu, kmin[k], o));
+      kmax[k] = max(kmax[k], __shfl_xor_sync(0xffffffffu, kmax[k], o));
+    }
+    if (lane == 0) {
+      smin[k][warp] = kmin[k];
+      smax[k][warp] = kmax[k];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 3) {
+    const int k = threadIdx.x;
+    long long a = smin[k][0], b = smax[k][0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+      a = min(a, smin[k][w]);
+      b = max(b, smax[k][w]);
+    }
+    atomicMin(mm + 2 * k, a);
+    atomicMax(mm + 2 * k + 1, b);
+  }
 }
 
 // transpose CSR
@@ -255,6 +316,7 @@ struct NbrWs {
   int64_t* frame_ptr;   // [F+1] (F <= N+1)
   double* cell;         // [F][9]
   int32_t* flag;        // [4]
+  long long* mm;        // [6] coordinate min / max keys
   void* scan_tmp;
   size_t scan_bytes;
 };
@@ -269,20 +331,31 @@ void nbr_layout(NbrWs& w, Arena& ar, int64_t N, int64_t F) {
   w.frame_ptr = ar.take<int64_t>(F + 1);
   w.cell = ar.take<double>(9 * F + 9);
   w.flag = ar.take<int32_t>(4);
+  w.mm = ar.take<long long>(6);
   w.scan_bytes = scan_temp_bytes(N + 2);
   w.scan_tmp = ar.take<char>((int64_t)w.scan_bytes + 16);
 }
 
-bool orthorhombic(const double* c) {
-  return c[1] == 0.0 && c[2] == 0.0 && c[3] == 0.0 && c[5] == 0.0 && c[6] == 0.0 && c[7] == 0.0 && c[0] > 0.0 &&
-         c[4] > 0.0 && c[8] > 0.0;
+// Periodic cell vectors axis-aligned (the rows of open axes are not used).
+bool aligned_periodic(const double* c, const int32_t* pbc) {
+  for (int k = 0; k < 3; ++k) {
+    if (!pbc[k]) continue;
+    if (!(c[4 * k] > 0.0)) return false;
+    for (int j = 0; j < 3; ++j)
+      if (j != k && c[3 * k + j] != 0.0) return false;
+  }
+  return true;
 }
 
-CellGrid make_grid(const double* c, double cutoff, int64_t natoms) {
+// lo / hi: grid extent per axis ([0, L) on periodic axes, the bounding box on open ones).
+CellGrid make_grid(const int32_t* pbc, const double* lo, const double* hi, double cutoff, int64_t natoms) {
   CellGrid g{};
-  const double L[3] = {c[0], c[4], c[8]};
   int64_t nc[3];
-  for (int k = 0; k < 3; ++k) nc[k] = std::max<int64_t>(1, (int64_t)std::floor(L[k] / (cutoff + 1e-6)));
+  double L[3];
+  for (int k = 0; k < 3; ++k) {
+    L[k] = hi[k] - lo[k];
+    nc[k] = L[k] > 0.0 ? std::max<int64_t>(1, (int64_t)std::floor(L[k] / (cutoff + 1e-6))) : 1;
+  }
   const int64_t cap = std::max<int64_t>(1, natoms);
   while (nc[0] * nc[1] * nc[2] > cap) {
     int k = 0;
@@ -292,8 +365,9 @@ CellGrid make_grid(const double* c, double cutoff, int64_t natoms) {
   }
   for (int k = 0; k < 3; ++k) {
     g.nc[k] = (int)nc[k];
-    g.L[k] = L[k];
-    g.inv_cs[k] = (double)nc[k] / L[k];
+    g.per[k] = pbc[k] ? 1 : 0;
+    g.lo[k] = lo[k];
+    g.inv_cs[k] = L[k] > 0.0 ? (double)nc[k] / L[k] : 0.0;
   }
   return g;
 }
@@ -303,26 +377,38 @@ int search(const double* pos, const double* cell_host, const int64_t* fp_host, i
            const int32_t* pbc, double cutoff, int mode, int32_t* counts, const int32_t* row_ptr, int32_t* src,
            int8_t* sidx, NbrWs& w, cudaStream_t st) {
   const double r2max = cutoff * cutoff;
-  const bool all_pbc = pbc[0] && pbc[1] && pbc[2];
   std::vector<int64_t> brute_frames;
   for (int64_t f = 0; f < F; ++f) {
     const int64_t a0 = fp_host[f], na = fp_host[f + 1] - fp_host[f];
     const double* c = cell_host + 9 * f;
-    bool use_cells = all_pbc && orthorhombic(c) && na > 512;
+    bool use_cells = aligned_periodic(c, pbc) && na > 512;
+    double lo[3] = {0.0, 0.0, 0.0}, hi[3] = {c[0], c[4], c[8]};
     if (use_cells) {
-      if (cudaMemsetAsync(w.flag, 0, sizeof(int32_t), st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset flag");
-      out_of_box_kernel<<<(unsigned)ceil_div(na, 256), 256, 0, st>>>(pos, a0, na, c[0], c[4], c[8], w.flag);
+      const long long init[6] = {0x7FFFFFFFFFFFFFFFLL, -0x7FFFFFFFFFFFFFFFLL - 1, 0x7FFFFFFFFFFFFFFFLL,
+                                 -0x7FFFFFFFFFFFFFFFLL - 1, 0x7FFFFFFFFFFFFFFFLL, -0x7FFFFFFFFFFFFFFFLL - 1};
+      if (cudaMemsetAsync(w.flag, 0, sizeof(int32_t), st) != cudaSuccess ||
+          cudaMemcpyAsync(w.mm, init, sizeof(init), cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return fail(FSC_ERR_CUDA, "box check setup");
+      box_kernel<<<(unsigned)ceil_div(na, 256), 256, 0, st>>>(pos, a0, na, pbc[0], pbc[1], pbc[2], c[0], c[4], c[8],
+                                                              w.flag, w.mm);
       int32_t flag = 0;
+      long long mm[6];
       if (cudaMemcpyAsync(&flag, w.flag, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+          cudaMemcpyAsync(mm, w.mm, sizeof(mm), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
           cudaStreamSynchronize(st) != cudaSuccess)
         return fail(FSC_ERR_CUDA, "neighbour box check");
       use_cells = (flag == 0);
+      for (int k = 0; k < 3; ++k)
+        if (!pbc[k]) {
+          lo[k] = dkey_inv(mm[2 * k]);
+          hi[k] = dkey_inv(mm[2 * k + 1]);
+        }
     }
     if (!use_cells) {
       brute_frames.push_back(f);
       continue;
     }
-    CellGrid g = make_grid(c, cutoff, na);
+    CellGrid g = make_grid(pbc, lo, hi, cutoff, na);
     const int64_t ncell = (int64_t)g.nc[0] * g.nc[1] * g.nc[2];
     if (cudaMemsetAsync(w.cell_count, 0, sizeof(int32_t) * (ncell + 1), st) != cudaSuccess ||
         cudaMemsetAsync(w.cursor, 0, sizeof(int32_t) * (ncell + 1), st) != cudaSuccess)

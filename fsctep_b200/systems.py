@@ -122,6 +122,25 @@ def diamond_crystal(n_cells=(50, 50, 50), a=5.43, sigma=0.08, seed=0, Z=14):
     return _lattice(DIAMOND_BASIS, n_cells, a, sigma, seed, Z)
 
 
+def diamond_block(block, dims, n_cells=(50, 50, 50), a=5.43, sigma=0.08, seed=0, Z=14):
+    """One rank's block of a diamond crystal of dims * n_cells conventional cells (spatial
+    decomposition, weak scaling: n_cells per rank).  Positions are wrapped into the global cell
+    only along unsplit axes (dims == 1); along split axes a displaced atom stays next to its
+    own block.  Returns the block's atoms and the global cell."""
+    rng = np.random.default_rng(seed)
+    nx, ny, nz = n_cells
+    ii, jj, kk = np.meshgrid(np.arange(nx), np.arange(ny), np.arange(nz), indexing="ij")
+    origins = np.stack([ii, jj, kk], axis=-1).reshape(-1, 1, 3).astype(np.float64)
+    origins = origins + (np.asarray(block, dtype=np.float64) * np.asarray(n_cells))[None, None, :]
+    pos = ((origins + np.asarray(DIAMOND_BASIS)[None]) * a).reshape(-1, 3)
+    pos = pos + rng.normal(scale=sigma, size=pos.shape)
+    L = np.asarray(n_cells, dtype=np.float64) * np.asarray(dims) * a
+    for k in range(3):
+        if dims[k] == 1:
+            pos[:, k] = np.mod(pos[:, k], L[k])
+    return _system(pos, np.full(pos.shape[0], Z), np.zeros(pos.shape[0]), np.diag(L)[None])
+
+
 def fcc_crystal(n_cells=(50, 50, 25), a=3.61, sigma=0.1, seed=0, Z=29):
     """FCC lattice; 50x50x25 cells x 4 atoms = 250,000 atoms."""
     return _lattice(FCC_BASIS, n_cells, a, sigma, seed, Z)

@@ -1,0 +1,141 @@
+"""Spatial decomposition host logic on CPU: halo exchange, ghost-force return, energy / virial
+reduction.  A toy two-hop message-passing potential (receptive field 2 * rc, like a 2-layer
+model) is evaluated on the whole periodic system and decomposed over 2, 4 and 8 ranks, in one
+process (run_local) and over real gloo ranks (run_dist)."""
+
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from fsctep_b200 import domain as D
+from fsctep_b200 import systems
+from oracle import neighbors as ON
+
+RC = 4.0  # first two diamond shells (2.35 and 3.84 A)
+NHOP = 2
+
+
+def toy_evaluate(cell):
+    """Evaluator of a 2-hop potential on a local system (owned atoms first)."""
+    cell_t = torch.tensor(cell, dtype=torch.float64)
+
+    def evaluate(pos, species, num_local, pbc):
+        src, dst, S = ON.neighbor_list(pos.detach().numpy(), cell, RC, pbc=pbc)
+        p = pos.detach().clone().requires_grad_(True)
+        src_t, dst_t = torch.tensor(src), torch.tensor(dst)
+        r = p[dst_t] - p[src_t] + torch.tensor(S, dtype=torch.float64) @ cell_t
+        r.retain_grad()
+        d = r.norm(dim=1)
+        phi = (1.0 - d / RC) ** 2
+        w = 1.0 + 0.1 * species.to(torch.float64)
+        n = p.shape[0]
+        m1 = torch.zeros(n, dtype=torch.float64).index_add(0, dst_t, phi * w[src_t])
+        m2 = torch.zeros(n, dtype=torch.float64).index_add(0, dst_t, phi * torch.tanh(0.3 * m1[src_t]))
+        e = 0.01 * m2 ** 2 + 0.5 * m1 + 0.05 * m1 * m2
+        E = e[:num_local].sum()
+        E.backward()
+        return {"energy": E.detach(), "forces": -p.grad, "atom_energy": e.detach(),
+                "virial": (r.detach().T @ r.grad)}
+
+    return evaluate
+
+
+def _system():
+    s = systems.diamond_crystal(n_cells=(4, 4, 4), seed=31)
+    s["Z"] = (np.arange(s["pos"].shape[0]) % 3).astype(np.int64)
+    return s
+
+
+def _reference(s):
+    ev = toy_evaluate(s["cell"][0])
+    pos = torch.tensor(s["pos"], dtype=torch.float64)
+    return ev(pos, torch.tensor(s["Z"]), pos.shape[0], (True, True, True))
+
+
+def _owned(dec, rank, s):
+    frac = s["pos"] @ np.linalg.inv(s["cell"][0])
+    frac = frac - np.floor(frac)
+    b = dec.block_of(rank)
+    m = np.ones(len(frac), dtype=bool)
+    for k in range(3):
+        m &= (np.floor(frac[:, k] * dec.dims[k]).astype(int) == b[k])
+    return np.nonzero(m)[0]
+
+
+def _decomposed_local(s, dims, halo):
+    dec = D.Decomposition(s["cell"][0], dims, halo)
+    ev = toy_evaluate(s["cell"][0])
+    owned = [_owned(dec, r, s) for r in range(dec.world)]
+    gens = [D.decomposed_step(dec, r, torch.tensor(s["pos"][o], dtype=torch.float64), torch.tensor(s["Z"][o]), ev,
+                              want_virial=True) for r, o in enumerate(owned)]
+    res = D.run_local(gens)
+    F = np.zeros_like(s["pos"])
+    for o, r in zip(owned, res):
+        F[o] = r["forces"].numpy()
+    return res, F, owned
+
+
+@pytest.mark.parametrize("dims", [(2, 1, 1), (2, 2, 1), (2, 2, 2), (1, 2, 1)])
+def test_decomposed_matches_single_domain(dims):
+    s = _system()
+    ref = _reference(s)
+    res, F, owned = _decomposed_local(s, dims, NHOP * RC)
+    assert sorted(np.concatenate(owned).tolist()) == list(range(s["pos"].shape[0]))
+    for r in res:
+        assert abs(r["energy"].item() - ref["energy"].item()) <= 1e-10 * abs(ref["energy"].item())
+        np.testing.assert_allclose(r["virial"].numpy(), ref["virial"].numpy(), rtol=1e-9, atol=1e-9)
+    np.testing.assert_allclose(F, ref["forces"].numpy(), rtol=1e-9, atol=1e-10)
+    ae = np.zeros(s["pos"].shape[0])
+    for o, r in zip(owned, res):
+        ae[o] = r["atom_energy"].numpy()
+    np.testing.assert_allclose(ae, ref["atom_energy"].numpy(), rtol=1e-10, atol=1e-12)
+    assert all(r["num_ghosts"] > 0 for r in res)
+
+
+def test_short_halo_is_detected():
+    """A halo shorter than the receptive field changes the energy: the test above has teeth."""
+    s = _system()
+    ref = _reference(s)
+    res, _, _ = _decomposed_local(s, (2, 1, 1), 1.0 * RC)
+    assert abs(res[0]["energy"].item() - ref["energy"].item()) > 1e-6 * abs(ref["energy"].item())
+
+
+def test_grid_for_and_validation():
+    assert D.grid_for(1) == (1, 1, 1) and D.grid_for(2) == (2, 1, 1)
+    assert D.grid_for(4) == (2, 2, 1) and D.grid_for(8) == (2, 2, 2)
+    with pytest.raises(ValueError):
+        D.grid_for(6)
+    with pytest.raises(ValueError):
+        D.Decomposition(np.eye(3) * 10.0, (2, 1, 1), 6.0)  # halo longer than half the cell
+
+
+def _free_port():
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
+def _gloo_rank(rank, world, port, dims):
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        s = _system()
+        ref = _reference(s)
+        dec = D.Decomposition(s["cell"][0], dims, NHOP * RC)
+        o = _owned(dec, rank, s)
+        res = D.run_dist(D.decomposed_step(dec, rank, torch.tensor(s["pos"][o], dtype=torch.float64),
+                                           torch.tensor(s["Z"][o]), toy_evaluate(s["cell"][0]), want_virial=True))
+        assert abs(res["energy"].item() - ref["energy"].item()) <= 1e-10 * abs(ref["energy"].item())
+        np.testing.assert_allclose(res["forces"].numpy(), ref["forces"].numpy()[o], rtol=1e-9, atol=1e-10)
+        np.testing.assert_allclose(res["virial"].numpy(), ref["virial"].numpy(), rtol=1e-9, atol=1e-9)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_two_ranks():
+    import torch.multiprocessing as mp
+
+    mp.spawn(_gloo_rank, args=(2, _free_port(), (2, 1, 1)), nprocs=2, join=True)

@@ -53,3 +53,23 @@ def test_positions_outside_box_fall_back_to_all_pairs():
     s = systems.diamond_crystal(n_cells=(6, 6, 6), seed=7)
     s["pos"] = s["pos"] + np.array([0.5, -0.3, 0.0])  # some atoms leave [0, L)
     _check(s)
+
+
+def test_cell_list_slab_open_z():
+    s = systems.diamond_crystal(n_cells=(6, 6, 6), seed=8)
+    s["pbc"] = (True, True, False)
+    _check(s)
+
+
+def test_cell_list_open_cluster():
+    s = systems.diamond_crystal(n_cells=(6, 6, 5), seed=9)
+    s["pbc"] = (False, False, False)
+    _check(s)
+
+
+def test_cell_list_split_axis_with_ghost_images():
+    """Layout of a spatial-decomposition rank: open along x with atoms outside [0, L), periodic y, z."""
+    s = systems.diamond_crystal(n_cells=(8, 5, 5), seed=10)
+    s["pos"] = s["pos"] + np.array([-7.5, 0.0, 0.0])
+    s["pbc"] = (False, True, True)
+    _check(s)
