@@ -229,6 +229,40 @@ class PackedICTDWeights:
         self.struct = s
 
 
+# Field order of the core.pt weight blob (fsctep::ictd_atom_energy, torch_ops/ictd_op.cpp).
+BLOB_FIELDS = (["tables", "ai", "vsp", "rad_w1", "rad_b1", "rad_w2", "rad_b2", "rad_w3", "rad_b3", "mix_fwd",
+                "mix_bwd", "mix_dx", "wread_p", "wread_s", "pairs", "xmap", "xinv", "wimg_fwd", "wimg_bwd",
+                "mn_in_g", "mn_in_b"] + [f"mn_w{k}" for k in range(4)] + [f"mn_b{k}" for k in range(4)]
+               + [f"mn_g{k}" for k in range(4)] + [f"mn_beta{k}" for k in range(4)] + ["out_v"])
+
+
+def weight_blob(packed: "PackedICTDWeights", cfg: "ICTDConfig"):
+    """One float32 device tensor holding every packed weight array (int32 arrays bit-cast), each
+    field 256-byte aligned, plus the integer / float configuration lists of the core.pt op."""
+    parts, offs, cur = [], [], 0
+    for name in BLOB_FIELDS:
+        t = packed.tensors.get(name)
+        if t is None:
+            offs.append(-1)
+            continue
+        flat = t.reshape(-1)
+        flat = flat.view(torch.float32) if flat.dtype == torch.int32 else flat.to(torch.float32)
+        pad = (-cur) % 64
+        if pad:
+            parts.append(torch.zeros(pad, dtype=torch.float32, device=flat.device))
+            cur += pad
+        offs.append(cur)
+        parts.append(flat)
+        cur += flat.numel()
+    blob = torch.cat(parts).contiguous()
+    nc = cfg.native()
+    icfg = [nc.channels, nc.lmax, nc.num_interaction, nc.number_of_basis, nc.basis_kind, nc.num_species,
+            nc.output_size, nc.invariant_channels, nc.n_hidden] + [int(nc.hidden[k]) for k in range(4)] + \
+           [nc.n_out] + offs
+    fcfg = [float(cfg.max_radius), float(packed.out_c0)]
+    return blob, icfg, fcfg
+
+
 class GraphCSR:
     """dst-sorted CSR + transpose CSR of an edge list (all int32 on the device).
 

@@ -16,6 +16,10 @@ Fixtures:
   forces and stress (float64, and float32 for the tolerance budget), computed with
   ``PureCartesianICTDTransformerLayer`` (``pure_cartesian_ictd_layers_full.py``)
   and the calculator/trainer conventions (F = -dE/dpos, sigma = (1/V) dE/d eps).
+* ``ictd_o3_{a,b}.npz`` -- the same for ``PureCartesianICTDO3TransformerLayer``
+  (``pure_cartesian_ictd_layers_o3.py``) with active irreps 0e,1e,1o,2e, an external 1o field
+  drawn from N(0, 0.05) per graph and dipole (1o) + polarizability (0e, 2e) heads on batches
+  of non-periodic molecules: energies, forces, per-atom energies and the heads' outputs.
 * ``tp_ops.npz`` -- the ``_C_ictd_tp`` operator family evaluated by the reference's
   einsum references (``models/ictd_irreps_cuda.py:169-311``) on the shapes of
   ``test/test_ictd_tp_backend.py``.
@@ -139,6 +143,53 @@ def model_case(tag, system, cfg, seed):
           "max|dF| fp32", np.abs(r64["forces"] - r32["forces"]).max(), "max|F|", np.abs(r64["forces"]).max())
 
 
+O3_HEADS = {"dipole": {"irreps": ["1o"], "reduce": "sum"}, "polarizability": {"ls": [0, 2], "reduce": "sum"}}
+
+
+def o3_case(tag, system, cfg, seed, field_seed):
+    from molecular_force_field.models.pure_cartesian_ictd_layers_o3 import PureCartesianICTDO3TransformerLayer
+
+    torch.set_default_dtype(torch.float64)
+    model = PureCartesianICTDO3TransformerLayer(
+        max_embed_radius=cfg["max_radius"], main_max_radius=cfg["max_radius"],
+        main_number_of_basis=cfg["number_of_basis"], hidden_dim_conv=cfg["channels"], hidden_dim_sh=32,
+        hidden_dim=64, lmax=cfg["lmax"], num_interaction=cfg["num_interaction"],
+        function_type_main=cfg["function_type"], max_atomvalue=cfg["max_atomvalue"],
+        internal_compute_dtype=torch.float64, device=torch.device("cpu"),
+        external_tensor_rank=1, external_tensor_irrep="1o", physical_tensor_outputs=O3_HEADS,
+        o3_active_irreps=["0e", "1e", "1o", "2e"])
+    shapes = _perturb(model, seed)
+    B = system["cell"].shape[0]
+    field = np.random.default_rng(field_seed).normal(scale=0.05, size=(B, 3))
+    src, dst, S = neighbors.batched_neighbor_list(system["pos"], system["batch"], system["cell"],
+                                                  cfg["max_radius"], system["pbc"])
+    pos = torch.tensor(system["pos"], requires_grad=True)
+    b = torch.tensor(system["batch"])
+    e, phys = model(pos, torch.tensor(system["Z"]), b, torch.tensor(src), torch.tensor(dst),
+                    torch.tensor(S.astype(np.float64)), torch.tensor(system["cell"]),
+                    external_tensor=torch.tensor(field), return_physical_tensors=True)
+    Eg = torch.zeros(B, dtype=torch.float64).index_add(0, b, e.squeeze(-1))
+    (gp,) = torch.autograd.grad(Eg.sum(), [pos])
+    out = {"pos": system["pos"], "Z": system["Z"], "batch": system["batch"], "cell": system["cell"],
+           "pbc": np.array(system["pbc"]), "edge_src": src.astype(np.int32), "edge_dst": dst.astype(np.int32),
+           "edge_shifts": S.astype(np.int8), "field": field}
+    for k, v in cfg.items():
+        out[f"cfg_{k}"] = np.array(v)
+    out["sd_seed"] = np.array(seed)
+    for k, v in model.state_dict().items():
+        out[f"sdshape/{k}"] = np.array(shapes[k], dtype=np.int64)
+        out[f"sdsum/{k}"] = np.array(float(v.double().sum()))
+    out["ref64_energy"] = Eg.detach().numpy()
+    out["ref64_forces"] = (-gp).numpy()
+    out["ref64_atom_energy"] = e.detach().squeeze(-1).numpy()
+    out["ref64_dipole"] = phys["dipole"][1].detach().numpy()
+    out["ref64_polar0"] = phys["polarizability"][0].detach().numpy()
+    out["ref64_polar2"] = phys["polarizability"][2].detach().numpy()
+    np.savez_compressed(os.path.join(HERE, f"ictd_o3_{tag}.npz"), **out)
+    print("o3", tag, "atoms", system["pos"].shape[0], "edges", src.shape[0], "E", out["ref64_energy"][:3],
+          "dipole", out["ref64_dipole"].reshape(B, -1)[0])
+
+
 def tp_ops():
     from molecular_force_field.models import ictd_irreps_cuda as RC
 
@@ -174,7 +225,19 @@ def main():
     cfg_c = dict(channels=64, lmax=2, num_interaction=3, number_of_basis=8, max_radius=5.0,
                  function_type="gaussian", max_atomvalue=16)
     model_case("c", systems.diamond_crystal(n_cells=(2, 2, 2), seed=13, sigma=0.15), cfg_c, seed=3)
+    o3()
+
+
+def o3():
+    cfg = dict(channels=32, lmax=2, num_interaction=3, number_of_basis=8, max_radius=5.0,
+               function_type="gaussian", max_atomvalue=10)
+    o3_case("a", systems.organic_molecules(n_mol=6, seed=14), cfg, seed=4, field_seed=15)
+    cfg64 = dict(cfg, channels=64, function_type="bessel")
+    o3_case("b", systems.organic_molecules(n_mol=4, seed=16), cfg64, seed=5, field_seed=17)
 
 
 if __name__ == "__main__":
-    main()
+    if len(sys.argv) > 1 and sys.argv[1] == "o3":
+        o3()
+    else:
+        main()

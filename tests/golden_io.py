@@ -16,8 +16,8 @@ def load(name):
     return np.load(os.path.join(GOLDEN, name), allow_pickle=False)
 
 
-def model_case(tag, dtype=torch.float64):
-    z = load(f"ictd_model_{tag}.npz")
+def model_case(tag, dtype=torch.float64, prefix="ictd_model"):
+    z = load(f"{prefix}_{tag}.npz")
     shapes = {k[len("sdshape/"):]: tuple(int(x) for x in z[k]) for k in z.files if k.startswith("sdshape/")}
     sd = seeded_state_dict(shapes, int(z["sd_seed"]), torch.float64)
     for k, v in sd.items():
@@ -29,3 +29,8 @@ def model_case(tag, dtype=torch.float64):
     cfg = {k[4:]: z[k].item() for k in z.files if k.startswith("cfg_")}
     case = {k: z[k] for k in z.files if not (k.startswith("sd") or k.startswith("cfg_"))}
     return cfg, sd, case
+
+
+def o3_case(tag, dtype=torch.float64):
+    """(cfg, state_dict, case) of an ``ictd_o3_<tag>.npz`` fixture."""
+    return model_case(tag, dtype, prefix="ictd_o3")
