@@ -26,7 +26,7 @@ FSC_F32, FSC_F64 = 0, 1
 class IctdConfig(C.Structure):
     _fields_ = [("channels", I32), ("lmax", I32), ("num_interaction", I32), ("number_of_basis", I32),
                 ("basis_kind", I32), ("max_radius", C.c_float), ("num_species", I32), ("output_size", I32),
-                ("invariant_channels", I32), ("n_hidden", I32), ("hidden", I32 * 4), ("n_out", I32)]
+                ("invariant_channels", I32), ("n_hidden", I32), ("hidden", I32 * 4), ("n_out", I32), ("o3", I32)]
 
 
 class IctdWeights(C.Structure):
@@ -40,7 +40,7 @@ class IctdWeights(C.Structure):
 class Graph(C.Structure):
     _fields_ = [("num_atoms", I64), ("num_local", I64), ("num_edges", I64), ("num_graphs", I64), ("pos", P),
                 ("species", P), ("batch", P), ("cell", P), ("row_ptr", P), ("src", P), ("shift", P),
-                ("tr_ptr", P), ("tr_eid", P), ("energy_weight", P)]
+                ("tr_ptr", P), ("tr_eid", P), ("energy_weight", P), ("field", P)]
 
 
 class IctdOutputs(C.Structure):
@@ -85,6 +85,7 @@ _PROTOS = {
                                     C.POINTER(IctdOutputs), P, C.c_size_t, P]),
     "fsc_ictd_status": (C.c_int, [C.POINTER(IctdConfig), I64, I64, P, P, C.POINTER(C.c_int)]),
     "fsc_ictd_set_readout_path": (None, [C.c_int]),
+    "fsc_ictd_heads": (C.c_int, [P, P, P, C.c_int, P, P, P, P, C.c_size_t, P]),
     "fsc_ictd_set_radial_path": (None, [C.c_int]),
     "fsc_profile_enable": (None, [C.c_int]),
     "fsc_profile_read": (C.c_int, [C.POINTER(C.c_char_p), C.POINTER(C.c_float), C.c_int]),

@@ -42,6 +42,10 @@ constexpr int64_t kMaxGraphs = 4096;   // graphs per call (float64 accumulators 
 
 struct Plan {
   int C, nint, S, nC, D0, nb;
+  int o3;                   // parity-keyed model: 4 Gram blocks, zero 1e slot in the MainNet input
+  int ngram;                // Gram blocks of the readout (3, or 4 with o3)
+  int goff[4], gl[4];       // block offset in the flat split (units of nC) and its l
+  int64_t nrows;            // Gram operand rows: nC * sum_b (2 l_b + 1)
   int64_t N, E, B, npairs, chunk;
   int hidden[4];
   int n_hidden;
@@ -68,6 +72,7 @@ struct Plan {
   double* virial_d;
   double* cellg_d;
   float* chunkbuf;
+  double* heads_d;          // [4][kMaxGraphs][5] physical-tensor head accumulators
   // tensor-core readout
   bool tc;
   bool rtc;  // radial MLPs on tensor cores
@@ -104,7 +109,19 @@ void layout(Plan& p, Arena& ar, const fsc_ictd_config* cfg, int64_t N, int64_t E
   p.nint = cfg->num_interaction;
   p.S = (p.nint - 1) * cfg->invariant_channels;
   p.nC = p.C * p.nint;
-  p.D0 = 3 * p.nC + p.S;
+  p.o3 = cfg->o3 ? 1 : 0;
+  p.ngram = p.o3 ? 4 : 3;
+  {
+    const int ls[4] = {0, 1, p.o3 ? 1 : 2, 2};
+    int off = 0;
+    for (int b = 0; b < p.ngram; ++b) {
+      p.gl[b] = ls[b];
+      p.goff[b] = off * p.nC;
+      off += 2 * ls[b] + 1;
+    }
+    p.nrows = (int64_t)off * p.nC;
+  }
+  p.D0 = p.ngram * p.nC + p.S;
   p.nb = cfg->number_of_basis;
   p.N = N;
   p.E = E;
@@ -138,14 +155,15 @@ void layout(Plan& p, Arena& ar, const fsc_ictd_config* cfg, int64_t N, int64_t E
   p.dgates = ar.take<float>((int64_t)p.nint * E * 12);
   p.dY = ar.take<float>(E * 12);
   p.edge_grad = ar.take<float>(E * 3);
+  p.heads_d = ar.take<double>(4 * kMaxGraphs * 5);
   p.tc = g_readout_path == 0 && readout_tc_supported(p.nC, p.S);
   p.rtc = g_radial_path == 0 && radial_tc_supported(p.nb);
   p.n_pad = ceil_div(std::max<int64_t>(N, 1), 128) * 128;
   p.err = ar.take<int>(64);
   if (p.tc) {
     p.chunkbuf = nullptr;
-    p.Fg = ar.take<float>((int64_t)9 * p.nC * p.n_pad);
-    p.dFg = ar.take<float>((int64_t)9 * p.nC * p.n_pad);
+    p.Fg = ar.take<float>(p.nrows * p.n_pad);
+    p.dFg = ar.take<float>(p.nrows * p.n_pad);
   } else {
     p.Fg = p.dFg = nullptr;
     p.chunkbuf = ar.take<float>(p.chunk * std::max<int64_t>(p.npairs, (int64_t)p.nC * p.nC));
@@ -165,6 +183,7 @@ FgArgs fg_args(const Plan& p, const fsc_ictd_weights* w) {
   f.xinv = w->xinv;
   f.Fg = p.Fg;
   f.dFg = p.dFg;
+  f.nrows = p.nrows;
   return f;
 }
 
@@ -180,6 +199,11 @@ ReadoutTcArgs tc_args(const Plan& p, const float* wimg) {
   r.dscal = p.dscalars;
   r.dFg = p.dFg;
   r.err = p.err;
+  r.ngram = p.ngram;
+  for (int b = 0; b < 4; ++b) {
+    r.goff[b] = p.goff[b];
+    r.gl[b] = p.gl[b];
+  }
   return r;
 }
 
@@ -222,6 +246,8 @@ ConvArgs conv_args(const Ctx& c, int layer) {
   a.tables = c.w->tables;
   a.edge_y = c.p.edge_y;
   a.gates = c.p.gates + (int64_t)layer * c.p.E * 12;
+  a.field = c.g->field;
+  a.batch = c.g->batch;
   return a;
 }
 
@@ -234,6 +260,12 @@ ReadoutArgs readout_args(const Ctx& c) {
   for (int k = 0; k < c.p.nint; ++k) r.feats[k] = c.p.feats[k];
   r.tables = c.w->tables;
   r.xmap = c.w->xmap;
+  r.o3 = c.p.o3;
+  r.ngram = c.p.ngram;
+  for (int b = 0; b < 4; ++b) {
+    r.goff[b] = c.p.goff[b];
+    r.gl[b] = c.p.gl[b];
+  }
   return r;
 }
 
@@ -282,16 +314,19 @@ int forward(Ctx& c) {
   // readout scalars: packed Gram x symmetrised W_read
   ReadoutArgs ra = readout_args(c);
   if (p.tc) {
+    // o3: the Gram operand rows of the (zero) 1e block have no storage and stay zero
+    if (p.o3 && cudaMemsetAsync(p.Fg, 0, sizeof(float) * p.nrows * p.n_pad, st) != cudaSuccess)
+      return fail(FSC_ERR_CUDA, "memset Fg");
     FSC_TRY(launch_fg_gather(fg_args(p, w), st));
     FSC_TRY(launch_readout_fwd_tc(tc_args(p, w->wimg_fwd), st));
   }
   if (!p.tc && cudaMemsetAsync(p.scalars, 0, sizeof(float) * p.N * p.S, st) != cudaSuccess)
     return fail(FSC_ERR_CUDA, "memset scalars");
-  for (int l = 0; l < 3 && !p.tc; ++l) {
-    const float* Wp = w->wread_p + (int64_t)l * p.S * p.npairs;
+  for (int b = 0; b < p.ngram && !p.tc; ++b) {
+    const float* Wp = w->wread_p + (int64_t)b * p.S * p.npairs;
     for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
       const int64_t nn = std::min(p.chunk, p.N - n0);
-      FSC_TRY(launch_gram_pack(ra, l, n0, nn, w->pairs, p.npairs, p.chunkbuf, st));
+      FSC_TRY(launch_gram_pack(ra, b, n0, nn, w->pairs, p.npairs, p.chunkbuf, st));
       GemmArgs ga = gemm(p.chunkbuf, p.npairs, 0, Wp, p.npairs, 1, p.scalars + n0 * p.S, p.S, 0, nn, 1,
                          (int)p.npairs, p.S);
       ga.accumulate = 1;
@@ -340,14 +375,14 @@ int backward(Ctx& c) {
     FSC_TRY(launch_readout_bwd_tc(tc_args(p, w->wimg_bwd), st));
     FSC_TRY(launch_fg_scatter_add(fg_args(p, w), st));
   }
-  for (int l = 0; l < 3 && !p.tc; ++l) {
-    const float* Ws = w->wread_s + (int64_t)l * p.S * p.nC * p.nC;
+  for (int b = 0; b < p.ngram && !p.tc; ++b) {
+    const float* Ws = w->wread_s + (int64_t)b * p.S * p.nC * p.nC;
     for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
       const int64_t nn = std::min(p.chunk, p.N - n0);
       GemmArgs ga = gemm(p.dscalars + n0 * p.S, p.S, 0, Ws, (int64_t)p.nC * p.nC, 0, p.chunkbuf,
                          (int64_t)p.nC * p.nC, 0, nn, 1, p.S, p.nC * p.nC);
       FSC_TRY(launch_gemm(ga, st));
-      FSC_TRY(launch_gram_apply(ra, l, n0, nn, p.chunkbuf, p.grads, st));
+      FSC_TRY(launch_gram_apply(ra, b, n0, nn, p.chunkbuf, p.grads, st));
     }
   }
   prof::mark("readout_gram_backward", st);
@@ -565,6 +600,19 @@ int fsc_ictd_energy(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const
                     float* atom_energy, void* workspace, size_t workspace_bytes, void* stream) {
   FSC_REQUIRE(energy, "energy output required");
   return fsc_ictd_forward(cfg, w, g, energy, atom_energy, workspace, workspace_bytes, stream);
+}
+
+int fsc_ictd_heads(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g, int nheads,
+                   const int32_t* block_host, const float* weights, float* out, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  FSC_REQUIRE(nheads >= 1 && nheads <= 4, "1..4 heads");
+  FSC_REQUIRE(block_host && weights && out, "head blocks, weights and output required");
+  fsc::Ctx c{cfg, w, g, fsc::Plan{}, fsc::as_stream(stream)};
+  FSC_TRY(fsc::prepare(c, workspace, workspace_bytes));
+  for (int h = 0; h < nheads; ++h)
+    FSC_REQUIRE(block_host[h] >= 0 && block_host[h] < c.p.ngram, "head block index out of range");
+  return fsc::launch_heads(fsc::readout_args(c), g->batch, nheads, block_host, weights, c.p.heads_d, out,
+                           g->num_graphs, c.st);
 }
 
 int64_t fsc_ictd_tables_floats(void) { return ictd2::TAB_FLOATS; }

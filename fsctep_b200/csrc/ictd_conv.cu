@@ -274,6 +274,20 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_q_kernel(ConvArgs a, co
 }
 
 // ---------------------------------------------------------------- conv1 forward
+// Direction harmonics of conv1's first operand Ai[src] (x) Y_l; an external field adds the
+// graph's l = 1 vector (pure_cartesian_ictd_layers_o3.py:466-502: f_in[1o] += scale t Ai[src]).
+__device__ __forceinline__ void load_conv1_y(const ConvArgs& a, int64_t e, int64_t s, float* yv) {
+  const float* y = a.edge_y + 12 * e;
+#pragma unroll
+  for (int k = 0; k < NK; ++k) yv[k] = y[k];
+  if (a.field) {
+    const float* f = a.field + 3 * (int64_t)a.batch[s];
+    yv[1] += f[0];
+    yv[2] += f[1];
+    yv[3] += f[2];
+  }
+}
+
 template <int CPL>
 __global__ void __launch_bounds__(CONV_WARPS * 32) conv1_forward_kernel(ConvArgs a, const float* __restrict__ ai,
                                                                         const float* __restrict__ vsp,
@@ -291,7 +305,8 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv1_forward_kernel(ConvArgs
   const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
   for (int e = e0; e < e1; ++e) {
     const int64_t s = a.src[e];
-    const float* y = a.edge_y + 12 * (int64_t)e;
+    float yv[NK];
+    load_conv1_y(a, e, s, yv);
     const float* g = a.gates + 12 * (int64_t)e;
     const float* A = ai + 8 * (int64_t)a.species[s];
 #pragma unroll
@@ -302,7 +317,7 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv1_forward_kernel(ConvArgs
         const int l = kidx == 0 ? 0 : (kidx < 4 ? 1 : 2);
         float y1 = 0.f;
 #pragma unroll
-        for (int m = 0; m < 5; ++m) y1 = fmaf(cg1[5 * kidx + m], y[KB(l) + m], y1);
+        for (int m = 0; m < 5; ++m) y1 = fmaf(cg1[5 * kidx + m], yv[KB(l) + m], y1);
         S[j] = fmaf(g[P1PATH(l)] * y1, A[i], S[j]);
       }
     }
@@ -377,7 +392,8 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv1_backward_kernel(ConvArg
   __syncwarp();
   for (int e = e0 + lane; e < e1; e += 32) {
     const int64_t s = a.src[e];
-    const float* y = a.edge_y + 12 * (int64_t)e;
+    float yv[NK];
+    load_conv1_y(a, e, s, yv);
     const float* g = a.gates + 12 * (int64_t)e;
     const float* A = ai + 8 * (int64_t)a.species[s];
     float Av[8];
@@ -395,7 +411,7 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv1_backward_kernel(ConvArg
       for (int i = 0; i < 8; ++i) t = fmaf(ds[warp][kidx * 8 + i], Av[i], t);
       float y1 = 0.f;
 #pragma unroll
-      for (int m = 0; m < 5; ++m) y1 = fmaf(cg1[5 * kidx + m], y[KB(l) + m], y1);
+      for (int m = 0; m < 5; ++m) y1 = fmaf(cg1[5 * kidx + m], yv[KB(l) + m], y1);
       dgl[l] = fmaf(t, y1, dgl[l]);
       const float dy1 = t * g[P1PATH(l)];
 #pragma unroll

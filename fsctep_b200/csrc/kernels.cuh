@@ -78,6 +78,8 @@ struct ConvArgs {
   const float* tables;
   const float* edge_y;   // [E][12]
   const float* gates;    // [E][12] of this layer
+  const float* field;    // [B][3] or null: added to the l = 1 harmonic in conv1
+  const int32_t* batch;  // [N] graph of each atom (for field)
 };
 
 // conv1: f1[n][k][c]
@@ -119,14 +121,21 @@ struct ReadoutArgs {
   int C, nint, S;
   const float* feats[8];       // nint pointers to [N][9][C]
   const float* tables;
-  const int32_t* xmap;         // [9*nC] Gram operand element -> (layer << 16) | (k*C + c)
+  const int32_t* xmap;         // [nrows] Gram operand element -> (layer << 16) | (k*C + c), -1 = zero
+  int o3;                      // MainNet input has a zero 1e slot after [0e | scalars]
+  int ngram;                   // Gram blocks
+  int goff[4], gl[4];          // block offsets (elements) and l
 };
-// Packed Gram of component block l for nodes [n0, n0+nn): Gp[n][pair] = sum_m t[c][m] t[d][m]
-int launch_gram_pack(const ReadoutArgs& a, int l, int64_t n0, int64_t nn, const int32_t* pairs, int64_t npairs,
+// Packed Gram of Gram block b for nodes [n0, n0+nn): Gp[n][pair] = sum_m t[c][m] t[d][m]
+int launch_gram_pack(const ReadoutArgs& a, int b, int64_t n0, int64_t nn, const int32_t* pairs, int64_t npairs,
                      float* Gp, cudaStream_t st);
-// grads[k][n][KB(l)+m][c] += 2 sum_d H[n][c'][d] t[n][d][m] for nodes [n0, n0+nn), H [nn][nC][nC]
-int launch_gram_apply(const ReadoutArgs& a, int l, int64_t n0, int64_t nn, const float* H, float* const* grads,
+// grads at t_b[n][c'][m] += 2 sum_d H[n][c'][d] t_b[n][d][m] for nodes [n0, n0+nn), H [nn][nC][nC]
+int launch_gram_apply(const ReadoutArgs& a, int b, int64_t n0, int64_t nn, const float* H, float* const* grads,
                       cudaStream_t st);
+// Physical-tensor heads: out[h][graph][m] = sum_n sum_c w[h][c] t_{block[h]}[n][c][m]; acc: double
+// scratch [nheads][4096][5] (graphs < 4096); blocks: host array of <= 4 block indices; w on the device.
+int launch_heads(const ReadoutArgs& a, const int32_t* batch, int nheads, const int32_t* blocks, const float* w,
+                 double* acc, float* out, int64_t B, cudaStream_t st);
 int launch_p5_forward(const ReadoutArgs& a, const float* scalars, float* p5, cudaStream_t st);
 // Writes (not accumulates) grads[k] for all components, and dscalars.
 int launch_p5_backward(const ReadoutArgs& a, const float* scalars, const float* dp5, float* const* grads,
@@ -141,9 +150,11 @@ struct ReadoutTcArgs {
   const float* dscal;   // backward input [N][S]
   float* dFg;           // backward output [9*nC][n_pad]
   int* err;             // first failing wait site (0 = ok)
+  int ngram;            // Gram blocks (rows of block b start at goff[b], m-width 2 gl[b] + 1)
+  int goff[4], gl[4];
 };
 bool readout_tc_supported(int nC, int S);
-int64_t readout_tc_blocks(int nC, bool backward);
+int64_t readout_tc_blocks(int nC, int ngram, bool backward);
 int launch_readout_fwd_tc(const ReadoutTcArgs& a, cudaStream_t st);
 int launch_readout_bwd_tc(const ReadoutTcArgs& a, cudaStream_t st);
 struct FgArgs {
@@ -154,6 +165,7 @@ struct FgArgs {
   const int32_t* xinv;  // [nint][9*C] storage (layer, k*C + c) -> Gram operand row
   float* Fg;
   const float* dFg;
+  int64_t nrows;        // Gram operand rows
 };
 int launch_fg_gather(const FgArgs& a, cudaStream_t st);
 int launch_fg_scatter_add(const FgArgs& a, cudaStream_t st);

@@ -24,16 +24,27 @@ __device__ __forceinline__ const float* feat_row(const ReadoutArgs& a, int64_t n
   return a.feats[k] + (n * NK + comp) * a.C;
 }
 
-// Gram operand t_l[c'][m] = flat element off_l + c'*(2l+1) + m of the layer concatenation (see xmap).
-__device__ __forceinline__ int64_t xoff(const ReadoutArgs& a, int l, int cprime, int m, int& layer) {
-  const int nC = a.C * a.nint;
-  const int off = l == 0 ? 0 : (l == 1 ? nC : 4 * nC);
-  const int32_t code = a.xmap[off + cprime * (2 * l + 1) + m];
+// Gram operand t_b[c'][m] = flat element goff[b] + c'*(2l+1) + m of the layer concatenation (see
+// xmap); returns its offset in feats[layer] relative to the node's row, or -1 for an element
+// with no storage (the zero 1e block of the o3 model).
+__device__ __forceinline__ int64_t xoff(const ReadoutArgs& a, int b, int cprime, int m, int& layer) {
+  const int l = a.gl[b];
+  const int32_t code = a.xmap[a.goff[b] + cprime * (2 * l + 1) + m];
+  if (code < 0) {
+    layer = 0;
+    return -1;
+  }
   layer = code >> 16;
   return code & 0xffff;
 }
 
-__global__ void gram_pack_kernel(ReadoutArgs a, int l, int64_t n0, int64_t nn, const int32_t* __restrict__ pairs,
+__device__ __forceinline__ float xval(const ReadoutArgs& a, int b, int cprime, int m, int64_t base) {
+  int layer;
+  const int64_t o = xoff(a, b, cprime, m, layer);
+  return o < 0 ? 0.f : a.feats[layer][base + o];
+}
+
+__global__ void gram_pack_kernel(ReadoutArgs a, int b, int64_t n0, int64_t nn, const int32_t* __restrict__ pairs,
                                  int64_t npairs, float* __restrict__ Gp) {
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= nn * npairs) return;
@@ -42,17 +53,14 @@ __global__ void gram_pack_kernel(ReadoutArgs a, int l, int64_t n0, int64_t nn, c
   const int32_t pr = pairs[j];
   const int cp = pr & 0xffff, dp = pr >> 16;
   const int64_t base = n * NK * a.C;
+  const int l = a.gl[b];
   float acc = 0.f;
-  for (int m = 0; m < 2 * l + 1; ++m) {
-    int lc, ld;
-    const int64_t oc = xoff(a, l, cp, m, lc), od = xoff(a, l, dp, m, ld);
-    acc = fmaf(a.feats[lc][base + oc], a.feats[ld][base + od], acc);
-  }
+  for (int m = 0; m < 2 * l + 1; ++m) acc = fmaf(xval(a, b, cp, m, base), xval(a, b, dp, m, base), acc);
   Gp[idx] = acc;
 }
 
-// grads at t_l[c'][m] += 2 sum_d H[n][c'][d] t_l[d][m]
-__global__ void gram_apply_kernel(ReadoutArgs a, GradPtrs g, int l, int64_t n0, int64_t nn,
+// grads at t_b[c'][m] += 2 sum_d H[n][c'][d] t_b[d][m]
+__global__ void gram_apply_kernel(ReadoutArgs a, GradPtrs g, int b, int64_t n0, int64_t nn,
                                   const float* __restrict__ H) {
   const int nC = a.C * a.nint;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -61,28 +69,67 @@ __global__ void gram_apply_kernel(ReadoutArgs a, GradPtrs g, int l, int64_t n0, 
   const int cp = (int)(idx - nl * nC);
   const int64_t n = n0 + nl;
   const int64_t base = n * NK * a.C;
+  const int l = a.gl[b];
   const float* h = H + (nl * nC + cp) * (int64_t)nC;
   float acc[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
   for (int d = 0; d < nC; ++d) {
     const float hv = h[d];
 #pragma unroll
     for (int m = 0; m < 5; ++m)
-      if (m < 2 * l + 1) {
-        int ld;
-        const int64_t od = xoff(a, l, d, m, ld);
-        acc[m] = fmaf(hv, a.feats[ld][base + od], acc[m]);
-      }
+      if (m < 2 * l + 1) acc[m] = fmaf(hv, xval(a, b, d, m, base), acc[m]);
   }
   for (int m = 0; m < 2 * l + 1; ++m) {
     int lc;
-    const int64_t oc = xoff(a, l, cp, m, lc);
-    g.p[lc][base + oc] += 2.f * acc[m];
+    const int64_t oc = xoff(a, b, cp, m, lc);
+    if (oc >= 0) g.p[lc][base + oc] += 2.f * acc[m];
   }
 }
 
+// Physical-tensor heads: out[h][graph][m] = sum_n sum_c w[h][c] t_{blocks[h]}[n][c][m] (m < 5).
+// One warp per (node, head): lanes split the channels, one double atomic per component.
+struct HeadBlocks {
+  int b[4];
+};
+
+__global__ void heads_kernel(ReadoutArgs a, const int32_t* __restrict__ batch, int nheads, HeadBlocks blocks,
+                             const float* __restrict__ w, double* __restrict__ acc) {
+  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (wid >= a.N * nheads) return;
+  const int64_t n = wid / nheads;
+  const int h = (int)(wid - n * nheads);
+  const int b = blocks.b[h];
+  const int l = a.gl[b];
+  const int nC = a.C * a.nint;
+  const int64_t base = n * NK * a.C;
+  float v[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int c = lane; c < nC; c += 32) {
+    const float wc = w[(int64_t)h * nC + c];
+#pragma unroll
+    for (int m = 0; m < 5; ++m)
+      if (m < 2 * l + 1) v[m] = fmaf(wc, xval(a, b, c, m, base), v[m]);
+  }
+#pragma unroll
+  for (int m = 0; m < 5; ++m) v[m] = warp_sum(v[m]);
+  if (lane == 0) {
+    double* o = acc + ((int64_t)h * 4096 + batch[n]) * 5;
+    for (int m = 0; m < 2 * l + 1; ++m) atomicAdd(o + m, (double)v[m]);
+  }
+}
+
+__global__ void heads_finalize_kernel(const double* __restrict__ acc, int nheads, int64_t B, float* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nheads * B * 5) return;
+  const int64_t h = i / (B * 5), r = i - h * B * 5;
+  out[i] = (float)acc[h * 4096 * 5 + r];
+}
+
+// MainNet input [0e | scalars | (o3: zero 1e) | 1 | 2] (product_5 of the concatenated per-layer
+// features, pure_cartesian_ictd_layers_o3.py:1046-1057 for o3).
 __global__ void p5_forward_kernel(ReadoutArgs a, const float* __restrict__ scalars, float* __restrict__ p5) {
   const int nC = a.C * a.nint;
-  const int D0 = 3 * nC + a.S;
+  const int z = a.o3 ? nC : 0;
+  const int D0 = 3 * nC + a.S + z;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= a.N * D0) return;
   const int64_t n = idx / D0;
@@ -96,9 +143,11 @@ __global__ void p5_forward_kernel(ReadoutArgs a, const float* __restrict__ scala
   } else if (j < nC + a.S) {
     const float s = scalars[n * a.S + (j - nC)];
     v = f[0] * s * s;
+  } else if (j < nC + a.S + z) {
+    v = 0.f;
   } else {
-    const int l = j < 2 * nC + a.S ? 1 : 2;
-    const int cp = j - (nC + a.S) - (l - 1) * nC;
+    const int l = j < 2 * nC + a.S + z ? 1 : 2;
+    const int cp = j - (nC + a.S + z) - (l - 1) * nC;
     const int k = cp / a.C, c = cp - k * a.C;
     const float* r = a.feats[k] + (n * NK + KB(l)) * a.C + c;
     float acc = 0.f;
@@ -111,7 +160,8 @@ __global__ void p5_forward_kernel(ReadoutArgs a, const float* __restrict__ scala
 __global__ void p5_backward_kernel(ReadoutArgs a, GradPtrs g, const float* __restrict__ scalars,
                                    const float* __restrict__ dp5, float* __restrict__ dscalars) {
   const int nC = a.C * a.nint;
-  const int D0 = 3 * nC + a.S;
+  const int z = a.o3 ? nC : 0;
+  const int D0 = 3 * nC + a.S + z;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= a.N * D0) return;
   const int64_t n = idx / D0;
@@ -125,9 +175,11 @@ __global__ void p5_backward_kernel(ReadoutArgs a, GradPtrs g, const float* __res
   } else if (j < nC + a.S) {
     const int o = j - nC;
     dscalars[n * a.S + o] = 2.f * f[0] * scalars[n * a.S + o] * d;
+  } else if (j < nC + a.S + z) {
+    // zero 1e slot: no input depends on it
   } else {
-    const int l = j < 2 * nC + a.S ? 1 : 2;
-    const int cp = j - (nC + a.S) - (l - 1) * nC;
+    const int l = j < 2 * nC + a.S + z ? 1 : 2;
+    const int cp = j - (nC + a.S + z) - (l - 1) * nC;
     const int k = cp / a.C, c = cp - k * a.C;
     for (int m = 0; m < 2 * l + 1; ++m) {
       const int64_t off = (n * NK + KB(l) + m) * a.C + c;
@@ -228,6 +280,20 @@ static GradPtrs to_ptrs(float* const* g, int nint) {
   return p;
 }
 
+int launch_heads(const ReadoutArgs& a, const int32_t* batch, int nheads, const int32_t* blocks, const float* w,
+                 double* acc, float* out, int64_t B, cudaStream_t st) {
+  if (cudaMemsetAsync(acc, 0, sizeof(double) * nheads * 4096 * 5, st) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "memset heads");
+  if (a.N > 0) {
+    HeadBlocks hb{};
+    for (int h = 0; h < nheads && h < 4; ++h) hb.b[h] = blocks[h];
+    heads_kernel<<<(unsigned)ceil_div(a.N * nheads, 8), 256, 0, st>>>(a, batch, nheads, hb, w, acc);
+    FSC_TRY(check_launch("heads_kernel"));
+  }
+  heads_finalize_kernel<<<(unsigned)ceil_div((int64_t)nheads * B * 5, 256), 256, 0, st>>>(acc, nheads, B, out);
+  return check_launch("heads_finalize_kernel");
+}
+
 int launch_gram_pack(const ReadoutArgs& a, int l, int64_t n0, int64_t nn, const int32_t* pairs, int64_t npairs,
                      float* Gp, cudaStream_t st) {
   const int64_t total = nn * npairs;
@@ -245,7 +311,7 @@ int launch_gram_apply(const ReadoutArgs& a, int l, int64_t n0, int64_t nn, const
 }
 
 int launch_p5_forward(const ReadoutArgs& a, const float* scalars, float* p5, cudaStream_t st) {
-  const int64_t total = a.N * (3 * a.C * a.nint + a.S);
+  const int64_t total = a.N * ((a.o3 ? 4 : 3) * a.C * a.nint + a.S);
   if (total == 0) return FSC_OK;
   p5_forward_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(a, scalars, p5);
   return check_launch("p5_forward_kernel");
@@ -253,7 +319,7 @@ int launch_p5_forward(const ReadoutArgs& a, const float* scalars, float* p5, cud
 
 int launch_p5_backward(const ReadoutArgs& a, const float* scalars, const float* dp5, float* const* grads,
                        float* dscalars, cudaStream_t st) {
-  const int64_t total = a.N * (3 * a.C * a.nint + a.S);
+  const int64_t total = a.N * ((a.o3 ? 4 : 3) * a.C * a.nint + a.S);
   if (total == 0) return FSC_OK;
   p5_backward_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(a, to_ptrs(grads, a.nint), scalars, dp5,
                                                                        dscalars);

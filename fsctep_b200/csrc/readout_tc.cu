@@ -33,7 +33,6 @@ constexpr int NGEN_WARPS = 8;
 constexpr int THREADS = (NGEN_WARPS + 2) * 32;  // + MMA warp + TMA warp
 constexpr int NSTB = 3;
 
-__device__ __forceinline__ int l_offset(int l, int nC) { return l == 0 ? 0 : (l == 1 ? nC : 4 * nC); }
 
 template <int S>
 struct Smem {
@@ -65,7 +64,7 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nC = a.nC, nb = nC / 8;
   const int64_t n0 = (int64_t)blockIdx.x * TILE;
-  const int nblk = 3 * nb * (nb + 1) / 2;
+  const int nblk = a.ngram * nb * (nb + 1) / 2;
 
   if (warp == NGEN_WARPS) {
     tc::tmem_alloc(tmem_slot, 512);
@@ -122,8 +121,8 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
       if (lane == 0) tc::mbar_arrive(d_empty + dst);
     };
     int s = 0;
-    for (int l = 0; l < 3 && ok; ++l) {
-      const int M = 2 * l + 1, off = l_offset(l, nC);
+    for (int b = 0; b < a.ngram && ok; ++b) {
+      const int M = 2 * a.gl[b] + 1, off = a.goff[b];
       for (int cb = 0; cb < nb && ok; ++cb) {
         float tcv[4][5];
 #pragma unroll
@@ -231,7 +230,7 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nC = a.nC, nb = nC / 8;
   const int64_t n0 = (int64_t)blockIdx.x * TILE;
-  const int nblk = 3 * nb * nb;
+  const int nblk = a.ngram * nb * nb;
 
   if (warp == NGEN_WARPS) {
     tc::tmem_alloc(tmem_slot, 256);
@@ -281,8 +280,8 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
     float* dFg = a.dFg + n;
     int s = 0;
     bool ok = true;
-    for (int l = 0; l < 3 && ok; ++l) {
-      const int M = 2 * l + 1, off = l_offset(l, nC);
+    for (int b = 0; b < a.ngram && ok; ++b) {
+      const int M = 2 * a.gl[b] + 1, off = a.goff[b];
       for (int cb = 0; cb < nb && ok; ++cb) {
         float acc[4][5];
 #pragma unroll
@@ -430,13 +429,14 @@ int launch_bwd(const ReadoutTcArgs& a, cudaStream_t st) {
 
 bool readout_tc_supported(int nC, int S) { return (S == 32 || S == 64) && nC % 8 == 0 && nC <= 512; }
 
-int64_t readout_tc_blocks(int nC, bool backward) {
+int64_t readout_tc_blocks(int nC, int ngram, bool backward) {
   const int64_t nb = nC / 8;
-  return backward ? 3 * nb * nb : 3 * nb * (nb + 1) / 2;
+  return backward ? ngram * nb * nb : ngram * nb * (nb + 1) / 2;
 }
 
 int launch_readout_fwd_tc(const ReadoutTcArgs& a, cudaStream_t st) {
   if (a.N == 0) return FSC_OK;
+  if (a.ngram < 1 || a.ngram > 4) return fail(FSC_ERR_ARGUMENT, "readout: 1..4 Gram blocks");
   if (a.S == 64) return launch_fwd<64>(a, st);
   if (a.S == 32) return launch_fwd<32>(a, st);
   return fail(FSC_ERR_UNSUPPORTED, "tensor-core readout needs S in {32, 64}");
@@ -444,6 +444,7 @@ int launch_readout_fwd_tc(const ReadoutTcArgs& a, cudaStream_t st) {
 
 int launch_readout_bwd_tc(const ReadoutTcArgs& a, cudaStream_t st) {
   if (a.N == 0) return FSC_OK;
+  if (a.ngram < 1 || a.ngram > 4) return fail(FSC_ERR_ARGUMENT, "readout: 1..4 Gram blocks");
   if (a.S == 64) return launch_bwd<64>(a, st);
   if (a.S == 32) return launch_bwd<32>(a, st);
   return fail(FSC_ERR_UNSUPPORTED, "tensor-core readout needs S in {32, 64}");

@@ -32,6 +32,13 @@ NP = 11
 P3_PATHS = [[0, 4, 9], [1, 3, 6, 8], [2, 5, 7, 10]]   # paths by l3, path order
 P1_PATHS = [[0, 1, 2], [3, 4, 5, 6], [7, 8, 9, 10]]   # paths by l1
 P_L0L = [0, 3, 7]                                      # (l,0,l) paths
+# pure-cartesian-ictd-o3 (active irreps 0e, 1e, 1o, 2e; pure_cartesian_ictd_layers_o3.py): index in
+# its 17-path list (ictd_irreps.py:1356-1366) of each SO(3) path above, carried by the
+# canonical-parity blocks 0e, 1o, 2e.  The 1e block only couples to itself and starts at zero.
+O3_ACTIVE = ["0e", "1e", "1o", "2e"]
+O3_L = [0, 1, 1, 2]
+SO3_TO_O3 = [0, 2, 3, 8, 9, 10, 11, 12, 14, 15, 16]
+O3_HEAD_BLOCKS = {("dipole", 1): 2, ("polarizability", 0): 0, ("polarizability", 2): 3}
 
 
 @dataclass
@@ -47,6 +54,7 @@ class ICTDConfig:
     max_atomvalue: int = 10
     invariant_channels: int = 32
     embed_size: Sequence[int] = field(default_factory=lambda: (128, 128, 128))
+    o3: bool = False  # pure-cartesian-ictd-o3 with active irreps 0e,1e,1o,2e
 
     @property
     def scalar_channels(self):
@@ -60,40 +68,48 @@ class ICTDConfig:
                          number_of_basis=self.number_of_basis, basis_kind=BASIS_KINDS[self.function_type],
                          max_radius=float(self.max_radius), num_species=self.max_atomvalue,
                          output_size=self.output_size, invariant_channels=self.invariant_channels,
-                         n_hidden=len(self.embed_size), n_out=17)
+                         n_hidden=len(self.embed_size), n_out=17, o3=1 if self.o3 else 0)
         for k, h in enumerate(self.embed_size):
             c.hidden[k] = int(h)
         return c
 
 
-def gram_xmap(C: int, nint: int):
+def gram_xmap(C: int, nint: int, o3: bool = False):
     """Storage location of every element of the readout's Gram operand.
 
-    The reference splits the flat concatenation of all layers' features (each in the
-    [l0 (C,1) | l1 (C,3) | l2 (C,5)] layout) into l blocks of nC*(2l+1) elements
-    (``pure_cartesian_ictd_layers_full.py:956-958``), so t_l[c][m] is flat element
-    off_l + c*(2l+1) + m.  Returns, per flat element, (layer << 16) | (k*C + channel) with
-    k = l'*l' + m' the component index in the [N][9][C] feature buffers.
+    The reference splits the flat concatenation of all layers' features into blocks of
+    nC*(2l+1) elements (``pure_cartesian_ictd_layers_full.py:956-958``; the o3 model the same way
+    over its 0e,1e,1o,2e blocks, ``pure_cartesian_ictd_layers_o3.py:976``), so element m of
+    channel c of block b is flat element off_b + c*(2l_b+1) + m, with each layer's features
+    laid out [l0 (C,1) | l1 (C,3) | l2 (C,5)] (o3: [0e | 1e | 1o | 2e]).  Returns, per flat
+    element, (layer << 16) | (k*C + channel) with k = l*l + m the component index in the
+    [N][9][C] feature buffers, or -1 for the o3 model's 1e block (identically zero, no storage).
     """
+    if o3:
+        blocks = [(0, 0), (None, 1), (1, 1), (2, 2)]  # (storage l or None, l) per block
+    else:
+        blocks = [(0, 0), (1, 1), (2, 2)]
+    per_layer = sum(C * (2 * l + 1) for _, l in blocks)
     out = []
-    for q in range(9 * C * nint):
-        layer, w = divmod(q, 9 * C)
-        if w < C:
-            l, base = 0, 0
-        elif w < 4 * C:
-            l, base = 1, C
-        else:
-            l, base = 2, 4 * C
+    for q in range(per_layer * nint):
+        layer, w = divmod(q, per_layer)
+        base = 0
+        for sl, l in blocks:
+            width = C * (2 * l + 1)
+            if w < base + width:
+                break
+            base += width
         c, m = divmod(w - base, 2 * l + 1)
-        out.append((layer << 16) | ((l * l + m) * C + c))
+        out.append(-1 if sl is None else (layer << 16) | ((sl * sl + m) * C + c))
     return out
 
 
-def gram_xinv(C: int, nint: int):
+def gram_xinv(C: int, nint: int, o3: bool = False):
     """Inverse of gram_xmap: [nint][9*C] storage (layer, k*C + c) -> Gram operand row."""
     inv = [[0] * (9 * C) for _ in range(nint)]
-    for r, code in enumerate(gram_xmap(C, nint)):
-        inv[code >> 16][code & 0xFFFF] = r
+    for r, code in enumerate(gram_xmap(C, nint, o3)):
+        if code >= 0:
+            inv[code >> 16][code & 0xFFFF] = r
     return inv
 
 
@@ -106,17 +122,16 @@ def tf32_split(x: torch.Tensor):
     return hi, lo
 
 
-def readout_images(W_read, C: int, nint: int):
-    """W_read.l blocks as shared-memory images of the tcgen05 operands (see include/fsctep_b200.h).
-
-    Returns (wimg_fwd, wimg_bwd) as flat fp32 tensors.
+def readout_images(W_read, C: int, nint: int, ls=(0, 1, 2)):
+    """W_read blocks (Gram block b has l = ls[b]) as shared-memory images of the tcgen05 operands
+    (see include/fsctep_b200.h).  Returns (wimg_fwd, wimg_bwd) as flat fp32 tensors.
     """
     nC = C * nint
     nb = nC // 8
     fwd, bwd = [], []
     iu = torch.triu_indices(nb, nb)
-    for l in range(3):
-        Wr = W_read[l].to(torch.float64) / math.sqrt(2 * l + 1)
+    for W_b, l in zip(W_read, ls):
+        Wr = W_b.to(torch.float64) / math.sqrt(2 * l + 1)
         S = Wr.shape[0]
         Ws = 0.5 * (Wr + Wr.transpose(1, 2))
         blk = Ws.reshape(S, nb, 8, nb, 8).permute(1, 3, 0, 2, 4).reshape(nb, nb, S, 64)  # [cb][db][o][pair]
@@ -149,12 +164,15 @@ class PackedICTDWeights:
             keep[name] = t.to(device=dev, dtype=torch.float32).contiguous()
             return keep[name]
 
+        o3 = bool(cfg.o3)
+        # o3 checkpoints have 17 paths; the SO(3) path p is the o3 path SO3_TO_O3[p]
+        psel = (lambda t: t[SO3_TO_O3]) if o3 else (lambda t: t)  # noqa: E731
         put("tables", torch.from_numpy(T.kernel_tables(cfg.lmax)))
         # per-species conv1 tables
         emb = f64("e3_conv_emb.atom_embedding.weight")
         h = _silu(emb @ f64("e3_conv_emb.atom_mlp.0.weight").T + f64("e3_conv_emb.atom_mlp.0.bias"))
         ai = h @ f64("e3_conv_emb.atom_mlp.2.weight").T + f64("e3_conv_emb.atom_mlp.2.bias")  # [S, 8]
-        W1 = f64("e3_conv_emb.tp2.weight")  # [P, C, 8, 8]
+        W1 = psel(f64("e3_conv_emb.tp2.weight"))  # [P, C, 8, 8]
         vsp = torch.stack([torch.einsum("oij,sj->sio", W1[p], ai) for p in P_L0L], dim=1)  # [S, 3, 8, C]
         put("ai", ai)
         put("vsp", vsp)
@@ -164,12 +182,12 @@ class PackedICTDWeights:
         put("rad_b1", torch.stack([f64(f"{p}.0.bias") for p in pref]))
         put("rad_w2", torch.stack([f64(f"{p}.2.weight") for p in pref]))
         put("rad_b2", torch.stack([f64(f"{p}.2.bias") for p in pref]))
-        put("rad_w3", torch.stack([f64(f"{p}.4.weight") for p in pref]))
-        put("rad_b3", torch.stack([f64(f"{p}.4.bias") for p in pref]))
+        put("rad_w3", torch.stack([psel(f64(f"{p}.4.weight")) for p in pref]))
+        put("rad_b3", torch.stack([psel(f64(f"{p}.4.bias")) for p in pref]))
         # channel mixes
         fwd, bwd, dx = [], [], []
         for k in range(nint - 1):
-            W = f64(f"tp2_layers.{k}.weight")[..., 0]  # [P, o, i]
+            W = psel(f64(f"tp2_layers.{k}.weight"))[..., 0]  # [P, o, i]
             for group in P3_PATHS:
                 fwd.append(torch.cat([W[p].T for p in group], dim=0).reshape(-1))      # [(rank,i)][o]
                 bwd.append(torch.cat([W[p] for p in group], dim=1).reshape(-1))        # [o][(rank,i)]
@@ -178,12 +196,16 @@ class PackedICTDWeights:
         put("mix_fwd", torch.cat(fwd))
         put("mix_bwd", torch.cat(bwd))
         put("mix_dx", torch.cat(dx))
-        # readout W_read
+        # readout W_read, one block per Gram block (l = 0, 1, 2; o3: 0e, 1e, 1o, 2e)
         nC = C_ * nint
+        if o3:
+            wkeys, ls = [f"W_read.{k}" for k in O3_ACTIVE], O3_L
+        else:
+            wkeys, ls = [f"W_read.{l}" for l in range(3)], [0, 1, 2]
         iu = torch.triu_indices(nC, nC, device=dev)
         wp, ws = [], []
-        for l in range(3):
-            Wr = f64(f"W_read.{l}") / math.sqrt(2 * l + 1)  # [S, nC, nC]
+        for key, l in zip(wkeys, ls):
+            Wr = f64(key) / math.sqrt(2 * l + 1)  # [S, nC, nC]
             Wsym = 0.5 * (Wr + Wr.transpose(1, 2))
             ws.append(Wsym.reshape(-1))
             packed = (Wr + Wr.transpose(1, 2))[:, iu[0], iu[1]]
@@ -193,15 +215,26 @@ class PackedICTDWeights:
         put("wread_p", torch.cat(wp))
         put("wread_s", torch.cat(ws))
         keep["pairs"] = (iu[0] | (iu[1] << 16)).to(torch.int32).contiguous()
-        keep["xmap"] = torch.tensor(gram_xmap(C_, nint), dtype=torch.int32, device=dev)
-        keep["xinv"] = torch.tensor(gram_xinv(C_, nint), dtype=torch.int32, device=dev).reshape(-1)
+        keep["xmap"] = torch.tensor(gram_xmap(C_, nint, o3), dtype=torch.int32, device=dev)
+        keep["xinv"] = torch.tensor(gram_xinv(C_, nint, o3), dtype=torch.int32, device=dev).reshape(-1)
         S = (nint - 1) * cfg.invariant_channels
         if S in (32, 64) and nC % 8 == 0:
-            wf, wb = readout_images([f64(f"W_read.{l}") for l in range(3)], C_, nint)
+            wf, wb = readout_images([f64(k) for k in wkeys], C_, nint, ls)
             put("wimg_fwd", wf)
             put("wimg_bwd", wb)
         else:
             keep["wimg_fwd"] = keep["wimg_bwd"] = None
+        # o3: external-field scale of the 1o block and the physical-tensor heads
+        self.field_scale = float(sd["e3_conv_emb.external_tensor_scale_by_irrep"][2]) if o3 and \
+            "e3_conv_emb.external_tensor_scale_by_irrep" in sd else 0.0
+        self.heads = []  # (name, l, Gram block)
+        hw = []
+        for (name, l), blk in O3_HEAD_BLOCKS.items():
+            key = f"physical_tensor_heads.{name}.{l}.weight"
+            if o3 and key in sd:
+                self.heads.append((name, l, blk))
+                hw.append(f64(key).reshape(-1))
+        keep["heads_w"] = torch.stack(hw).to(torch.float32).contiguous() if hw else None
         # MainNet
         put("mn_in_g", f64("proj_total.input_norm.weight"))
         put("mn_in_b", f64("proj_total.input_norm.bias"))
@@ -258,7 +291,7 @@ def weight_blob(packed: "PackedICTDWeights", cfg: "ICTDConfig"):
     nc = cfg.native()
     icfg = [nc.channels, nc.lmax, nc.num_interaction, nc.number_of_basis, nc.basis_kind, nc.num_species,
             nc.output_size, nc.invariant_channels, nc.n_hidden] + [int(nc.hidden[k]) for k in range(4)] + \
-           [nc.n_out] + offs
+           [nc.n_out, nc.o3] + offs
     fcfg = [float(cfg.max_radius), float(packed.out_c0)]
     return blob, icfg, fcfg
 
@@ -322,7 +355,7 @@ class ICTDEngine:
             self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
         return self._ws
 
-    def _graph(self, pos, species, batch, cell, g: GraphCSR, num_graphs, num_local, energy_weight):
+    def _graph(self, pos, species, batch, cell, g: GraphCSR, num_graphs, num_local, energy_weight, field=None):
         s = N.Graph()
         s.num_atoms = g.num_atoms
         s.num_local = g.num_atoms if num_local is None else int(num_local)
@@ -332,7 +365,22 @@ class ICTDEngine:
         s.row_ptr, s.src, s.shift = g.row_ptr.data_ptr(), g.src.data_ptr(), g.shift.data_ptr()
         s.tr_ptr, s.tr_eid = g.tr_ptr.data_ptr(), g.tr_eid.data_ptr()
         s.energy_weight = 0 if energy_weight is None else energy_weight.data_ptr()
+        s.field = 0 if field is None else field.data_ptr()
         return s
+
+    def _field(self, field, B):
+        """(B, 3) Cartesian external field -> the conv1 l = 1 term (o3 model), or None."""
+        if field is None:
+            return None
+        if not self.cfg.o3:
+            raise ValueError("an external field needs the o3 model (ICTDConfig(o3=True))")
+        f = torch.as_tensor(field, device=self.device, dtype=torch.float64).reshape(-1, 3)
+        if f.shape[0] == 1 and B > 1:
+            f = f.expand(B, 3)
+        if f.shape[0] != B:
+            raise ValueError(f"field must have one vector per graph ({B}), got {tuple(f.shape)}")
+        M = T.field_l1_map().to(device=self.device)
+        return (self.weights.field_scale * (f @ M.T)).to(torch.float32).contiguous()
 
     @staticmethod
     def _inputs(pos, species, batch, cell):
@@ -342,19 +390,42 @@ class ICTDEngine:
         cell = cell.detach().to(torch.float32).reshape(-1, 3, 3).contiguous()
         return pos, species, batch, cell
 
-    def forward(self, pos, species, batch, cell, g: GraphCSR, num_local=None):
-        """Per-graph energy (B,) and per-atom energy (N,); intermediates stay in the workspace."""
+    def forward(self, pos, species, batch, cell, g: GraphCSR, num_local=None, field=None):
+        """Per-graph energy (B,) and per-atom energy (N,); intermediates stay in the workspace.
+        ``field`` (B, 3): external 1o field of the o3 model (one Cartesian vector per graph)."""
         pos, species, batch, cell = self._inputs(pos, species, batch, cell)
         B = cell.shape[0]
         ws = self.workspace(g.num_atoms, g.num_edges)
         energy = torch.empty(B, dtype=torch.float32, device=self.device)
         atom_e = torch.empty(g.num_atoms, dtype=torch.float32, device=self.device)
-        gs = self._graph(pos, species, batch, cell, g, B, num_local, None)
+        fdev = self._field(field, B)
+        gs = self._graph(pos, species, batch, cell, g, B, num_local, None, fdev)
         N.check(N.lib().fsc_ictd_forward(C.byref(self.ncfg), C.byref(self.weights.struct), C.byref(gs),
                                          N.ptr(energy), N.ptr(atom_e), N.ptr(ws), ws.numel(),
                                          N.stream_ptr(self.device)), "fsc_ictd_forward")
         self._last = (pos, species, batch, cell, g, num_local)
+        self._field_dev = fdev
         return energy, atom_e
+
+    def heads(self):
+        """Physical-tensor heads of the last forward (o3 model): {name: {l: (B, 1, 2l+1)}}."""
+        w = self.weights
+        if not w.heads:
+            return {}
+        pos, species, batch, cell, g, num_local = self._last
+        B = cell.shape[0]
+        ws = self.workspace(g.num_atoms, g.num_edges)
+        nh = len(w.heads)
+        out = torch.empty(nh, B, 5, dtype=torch.float32, device=self.device)
+        blocks = (C.c_int32 * nh)(*[blk for _, _, blk in w.heads])
+        gs = self._graph(pos, species, batch, cell, g, B, num_local, None, self._field_dev)
+        N.check(N.lib().fsc_ictd_heads(C.byref(self.ncfg), C.byref(w.struct), C.byref(gs), nh,
+                                       C.cast(blocks, N.P), N.ptr(w.tensors["heads_w"]), N.ptr(out), N.ptr(ws),
+                                       ws.numel(), N.stream_ptr(self.device)), "fsc_ictd_heads")
+        res = {}
+        for h, (name, l, _) in enumerate(w.heads):
+            res.setdefault(name, {})[l] = out[h, :, : 2 * l + 1].reshape(B, 1, 2 * l + 1)
+        return res
 
     def backward(self, energy_weight=None, want_virial=True, want_cell_grad=False, want_edge_grad=False):
         """Reverse pass of the last forward: forces (N,3), virial (B,3,3), dE/dcell, dE/dr."""
@@ -371,7 +442,7 @@ class ICTDEngine:
             out["edge_grad"] = torch.empty(g.num_edges, 3, dtype=torch.float32, device=dev)
         if energy_weight is not None:
             energy_weight = energy_weight.detach().to(torch.float32).reshape(-1).contiguous()
-        gs = self._graph(pos, species, batch, cell, g, B, num_local, energy_weight)
+        gs = self._graph(pos, species, batch, cell, g, B, num_local, energy_weight, getattr(self, "_field_dev", None))
         o = N.IctdOutputs()
         o.forces = out["forces"].data_ptr()
         o.virial = out["virial"].data_ptr() if want_virial else 0
@@ -390,8 +461,8 @@ class ICTDEngine:
                                         N.stream_ptr(self.device), C.byref(st)), "fsc_ictd_status")
         return int(st.value)
 
-    def energy_forces(self, pos, species, batch, cell, g: GraphCSR, num_local=None, want_stress=True):
-        energy, atom_e = self.forward(pos, species, batch, cell, g, num_local)
+    def energy_forces(self, pos, species, batch, cell, g: GraphCSR, num_local=None, want_stress=True, field=None):
+        energy, atom_e = self.forward(pos, species, batch, cell, g, num_local, field)
         out = self.backward(want_virial=want_stress)
         out["energy"] = energy
         out["atom_energy"] = atom_e

@@ -102,6 +102,17 @@ def _projector(L: int, l: int) -> torch.Tensor:
     return torch.linalg.solve(V.T @ G @ V, V.T @ G).contiguous()
 
 
+def field_l1_map() -> torch.Tensor:
+    """(3, 3) M with t = M @ v: a Cartesian vector's ICTD l = 1 components (its monomial
+    coefficients in ``counts_list(1)`` order projected with P_{1->1}), the embedding of a rank-1
+    external tensor (pure_cartesian_ictd_layers.py:155-340)."""
+    axis = [0 if a else (1 if b else 2) for (a, b, c) in counts_list(1)]
+    sel = torch.zeros(3, 3, dtype=torch.float64)
+    for d, ax in enumerate(axis):
+        sel[d, ax] = 1.0
+    return _projector(1, 1) @ sel
+
+
 @lru_cache(maxsize=None)
 def cg(l1: int, l2: int, l3: int) -> torch.Tensor:
     """Normalised ("component") coupling tensor C[m1, m2, m3]."""

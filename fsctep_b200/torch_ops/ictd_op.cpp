@@ -30,10 +30,10 @@ using torch::autograd::AutogradContext;
 using torch::autograd::variable_list;
 
 // icfg: channels, lmax, num_interaction, number_of_basis, basis_kind, num_species, output_size,
-//       invariant_channels, n_hidden, hidden[4], n_out, then one element offset into the blob per
+//       invariant_channels, n_hidden, hidden[4], n_out, o3, then one element offset into the blob per
 //       weight field in the order of kFields (-1 = absent).
 // fcfg: max_radius, out_c0.
-constexpr int kCfgInts = 14;
+constexpr int kCfgInts = 15;
 constexpr int kFields = 38;
 
 struct Packed {
@@ -59,6 +59,7 @@ Packed unpack(const at::Tensor& blob, c10::IntArrayRef ic, c10::ArrayRef<double>
   p.cfg.n_hidden = (int32_t)ic[8];
   for (int k = 0; k < 4; ++k) p.cfg.hidden[k] = (int32_t)ic[9 + k];
   p.cfg.n_out = (int32_t)ic[13];
+  p.cfg.o3 = (int32_t)ic[14];
   p.cfg.max_radius = (float)fc[0];
   const float* base = blob.data_ptr<float>();
   const int64_t n = blob.numel();

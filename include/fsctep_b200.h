@@ -179,6 +179,11 @@ typedef struct {
   int32_t n_hidden;          /* MainNet hidden layers, 1..4                      */
   int32_t hidden[4];         /* MainNet hidden sizes (<= 1024)                   */
   int32_t n_out;             /* MainNet output width (17)                        */
+  int32_t o3;                /* 0 = pure-cartesian-ictd; 1 = pure-cartesian-ictd-o3 with
+                                active irreps 0e,1e,1o,2e (pure_cartesian_ictd_layers_o3.py):
+                                the canonical-parity blocks 0e,1o,2e carry the 11 SO(3) paths
+                                of its 17, 1e has no source without a 1e input and stays zero;
+                                readout over 4 Gram blocks, MainNet input 4*nC + S          */
 } fsc_ictd_config;
 
 /* Packed fp32 device weights.  The host side derives them from the reference
@@ -254,6 +259,10 @@ typedef struct {
   const float* energy_weight;/* [N] or NULL: backward seed dL/de_n; NULL = 1 for atoms
                                 [0, num_local), 0 for the rest (LAMMPS ghost convention,
                                 mff_torch_engine.cpp:812-820)                           */
+  const float* field;       /* [B][3] or NULL: per-graph vector added to the l = 1 direction
+                                harmonic of conv1 (external 1o field of the o3 model: the
+                                field's ICTD l = 1 components times external_tensor_scale,
+                                pure_cartesian_ictd_layers_o3.py:466-502)               */
 } fsc_graph;
 
 typedef struct {
@@ -287,6 +296,15 @@ void fsc_ictd_set_readout_path(int path);
 /* Radial MLP path (per-edge fc / fc2_layers and their backward): 0 = tensor cores where
  * supported (default; number_of_basis <= 16), 1 = CUDA-core kernels.  Process-wide. */
 void fsc_ictd_set_radial_path(int path);
+/* Physical-tensor heads of the o3 model (pure_cartesian_ictd_layers_o3.py:1010-1044), from the
+ * features left in the workspace by the last fsc_ictd_forward on it: for head h,
+ *   out[h][b][m] = sum_{n in graph b} sum_c weights[h][c] * t_{block[h]}[n][c][m],  m < 2l+1,
+ * t_block = Gram operand block (0e, 1e, 1o, 2e for o3; l = 0, 1, 2 otherwise) of the readout's
+ * flat split of the concatenated features, c < nC.  weights [nheads][nC], out [nheads][B][5]
+ * (entries m >= 2l+1 are set to 0).  block_host: host array of nheads block indices. */
+int fsc_ictd_heads(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g, int nheads,
+                   const int32_t* block_host, const float* weights, float* out, void* workspace,
+                   size_t workspace_bytes, void* stream);
 /* Forward only (per-atom energy), same workspace. */
 int fsc_ictd_energy(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g,
                     float* energy, float* atom_energy, void* workspace, size_t workspace_bytes,

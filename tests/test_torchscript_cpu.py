@@ -28,4 +28,4 @@ def test_cpu_tensors_are_rejected():
     z = torch.zeros(2, 3)
     with pytest.raises((RuntimeError, NotImplementedError)):
         torch.ops.fsctep.ictd_atom_energy(z, torch.zeros(2, dtype=torch.long), torch.zeros(2, dtype=torch.long),
-                                          torch.zeros(2, dtype=torch.long), torch.zeros(4), [0] * 52, [5.0, 0.0])
+                                          torch.zeros(2, dtype=torch.long), torch.zeros(4), [0] * 53, [5.0, 0.0])
