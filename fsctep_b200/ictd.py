@@ -35,10 +35,12 @@ P_L0L = [0, 3, 7]                                      # (l,0,l) paths
 # pure-cartesian-ictd-o3 (active irreps 0e, 1e, 1o, 2e; pure_cartesian_ictd_layers_o3.py): index in
 # its 17-path list (ictd_irreps.py:1356-1366) of each SO(3) path above, carried by the
 # canonical-parity blocks 0e, 1o, 2e.  The 1e block only couples to itself and starts at zero.
-O3_ACTIVE = ["0e", "1e", "1o", "2e"]
-O3_L = [0, 1, 1, 2]
+# With active irreps 0e,1o,2e (the "auto" preset) the o3 path list is the SO(3) one, in order.
 SO3_TO_O3 = [0, 2, 3, 8, 9, 10, 11, 12, 14, 15, 16]
-O3_HEAD_BLOCKS = {("dipole", 1): 2, ("polarizability", 0): 0, ("polarizability", 2): 3}
+
+
+def o3_num_paths(irreps) -> int:
+    return 17 if "1e" in irreps else 11
 
 
 @dataclass
@@ -54,7 +56,8 @@ class ICTDConfig:
     max_atomvalue: int = 10
     invariant_channels: int = 32
     embed_size: Sequence[int] = field(default_factory=lambda: (128, 128, 128))
-    o3: bool = False  # pure-cartesian-ictd-o3 with active irreps 0e,1e,1o,2e
+    o3: bool = False  # pure-cartesian-ictd-o3 (parity-keyed irreps, external field, tensor heads)
+    o3_irreps: Sequence[str] = ("0e", "1e", "1o", "2e")  # active irreps of the o3 model
 
     @property
     def scalar_channels(self):
@@ -68,7 +71,8 @@ class ICTDConfig:
                          number_of_basis=self.number_of_basis, basis_kind=BASIS_KINDS[self.function_type],
                          max_radius=float(self.max_radius), num_species=self.max_atomvalue,
                          output_size=self.output_size, invariant_channels=self.invariant_channels,
-                         n_hidden=len(self.embed_size), n_out=17, o3=1 if self.o3 else 0)
+                         n_hidden=len(self.embed_size), n_out=17,
+                         o3=1 if (self.o3 and "1e" in self.o3_irreps) else 0)
         for k, h in enumerate(self.embed_size):
             c.hidden[k] = int(h)
         return c
@@ -165,8 +169,9 @@ class PackedICTDWeights:
             return keep[name]
 
         o3 = bool(cfg.o3)
-        # o3 checkpoints have 17 paths; the SO(3) path p is the o3 path SO3_TO_O3[p]
-        psel = (lambda t: t[SO3_TO_O3]) if o3 else (lambda t: t)  # noqa: E731
+        irreps = tuple(cfg.o3_irreps) if o3 else ()
+        four = "1e" in irreps  # 0e,1e,1o,2e: 17 paths, the SO(3) path p is o3 path SO3_TO_O3[p]
+        psel = (lambda t: t[SO3_TO_O3]) if four else (lambda t: t)  # noqa: E731
         put("tables", torch.from_numpy(T.kernel_tables(cfg.lmax)))
         # per-species conv1 tables
         emb = f64("e3_conv_emb.atom_embedding.weight")
@@ -199,7 +204,7 @@ class PackedICTDWeights:
         # readout W_read, one block per Gram block (l = 0, 1, 2; o3: 0e, 1e, 1o, 2e)
         nC = C_ * nint
         if o3:
-            wkeys, ls = [f"W_read.{k}" for k in O3_ACTIVE], O3_L
+            wkeys, ls = [f"W_read.{k}" for k in irreps], [int(k[0]) for k in irreps]
         else:
             wkeys, ls = [f"W_read.{l}" for l in range(3)], [0, 1, 2]
         iu = torch.triu_indices(nC, nC, device=dev)
@@ -215,8 +220,8 @@ class PackedICTDWeights:
         put("wread_p", torch.cat(wp))
         put("wread_s", torch.cat(ws))
         keep["pairs"] = (iu[0] | (iu[1] << 16)).to(torch.int32).contiguous()
-        keep["xmap"] = torch.tensor(gram_xmap(C_, nint, o3), dtype=torch.int32, device=dev)
-        keep["xinv"] = torch.tensor(gram_xinv(C_, nint, o3), dtype=torch.int32, device=dev).reshape(-1)
+        keep["xmap"] = torch.tensor(gram_xmap(C_, nint, four), dtype=torch.int32, device=dev)
+        keep["xinv"] = torch.tensor(gram_xinv(C_, nint, four), dtype=torch.int32, device=dev).reshape(-1)
         S = (nint - 1) * cfg.invariant_channels
         if S in (32, 64) and nC % 8 == 0:
             wf, wb = readout_images([f64(k) for k in wkeys], C_, nint, ls)
@@ -224,15 +229,17 @@ class PackedICTDWeights:
             put("wimg_bwd", wb)
         else:
             keep["wimg_fwd"] = keep["wimg_bwd"] = None
-        # o3: external-field scale of the 1o block and the physical-tensor heads
-        self.field_scale = float(sd["e3_conv_emb.external_tensor_scale_by_irrep"][2]) if o3 and \
-            "e3_conv_emb.external_tensor_scale_by_irrep" in sd else 0.0
+        # o3: external-field scale of the 1o block and the physical-tensor heads (canonical parity
+        # of each head's l), in state_dict order
+        skey = "e3_conv_emb.external_tensor_scale_by_irrep"
+        self.field_scale = float(sd[skey][irreps.index("1o")]) if o3 and skey in sd else 0.0
         self.heads = []  # (name, l, Gram block)
         hw = []
-        for (name, l), blk in O3_HEAD_BLOCKS.items():
-            key = f"physical_tensor_heads.{name}.{l}.weight"
-            if o3 and key in sd:
-                self.heads.append((name, l, blk))
+        for key in sd:
+            parts = key.split(".")
+            if o3 and len(parts) == 4 and parts[0] == "physical_tensor_heads" and parts[3] == "weight":
+                l = int(parts[2])
+                self.heads.append((parts[1], l, irreps.index(f"{l}{'e' if l % 2 == 0 else 'o'}")))
                 hw.append(f64(key).reshape(-1))
         keep["heads_w"] = torch.stack(hw).to(torch.float32).contiguous() if hw else None
         # MainNet

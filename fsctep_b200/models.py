@@ -67,10 +67,10 @@ class _WeightedSum(nn.Module):
 
 class _NativeEnergy(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, pos, cell, owner, graph, species, batch):
+    def forward(ctx, pos, cell, owner, graph, species, batch, field=None):
         eng = owner._engine
-        _, atom_e = eng.forward(pos, species, batch, cell, graph)
-        ctx.owner, ctx.graph, ctx.species, ctx.batch = owner, graph, species, batch
+        _, atom_e = eng.forward(pos, species, batch, cell, graph, field=field)
+        ctx.owner, ctx.graph, ctx.species, ctx.batch, ctx.field = owner, graph, species, batch, field
         ctx.generation = owner._bump()
         ctx.save_for_backward(pos, cell)
         ctx.pos_dtype, ctx.cell_dtype = pos.dtype, cell.dtype
@@ -82,13 +82,13 @@ class _NativeEnergy(torch.autograd.Function):
         owner = ctx.owner
         eng = owner._engine
         if owner._generation != ctx.generation:  # another forward reused the workspace: recompute
-            eng.forward(pos, ctx.species, ctx.batch, cell, ctx.graph)
+            eng.forward(pos, ctx.species, ctx.batch, cell, ctx.graph, field=ctx.field)
             owner._generation = ctx.generation
         out = eng.backward(energy_weight=grad_e.reshape(-1), want_virial=False,
                            want_cell_grad=ctx.needs_input_grad[1])
         gpos = (-out["forces"]).to(ctx.pos_dtype) if ctx.needs_input_grad[0] else None
         gcell = out["cell_grad"].to(ctx.cell_dtype).reshape(cell.shape) if ctx.needs_input_grad[1] else None
-        return gpos, gcell, None, None, None, None
+        return gpos, gcell, None, None, None, None, None
 
 
 class PureCartesianICTDTransformerLayer(nn.Module):
@@ -184,6 +184,142 @@ class PureCartesianICTDTransformerLayer(nn.Module):
         self._ensure_engine(pos.device)
         graph = GraphCSR.from_edges(edge_src.long(), edge_dst.long(), edge_shifts, n)
         return _NativeEnergy.apply(pos, cell, self, graph, species, batch)
+
+
+_O3_IRREPS = {("0e", "1o", "2e"), ("0e", "1e", "1o", "2e")}
+
+
+def _irrep_letter(l: int, p: int) -> str:
+    return f"{l}{'e' if p > 0 else 'o'}"
+
+
+class PureCartesianICTDO3TransformerLayer(nn.Module):
+    """Drop-in for ``PureCartesianICTDO3TransformerLayer`` (``--tensor-product-mode
+    pure-cartesian-ictd-o3``, ``models/pure_cartesian_ictd_layers_o3.py:535-1074``).
+
+    Same constructor, parameter names and shapes, and forward signature.  Covered: lmax 2, active
+    irreps 0e,1o,2e (preset "auto") or 0e,1e,1o,2e, an optional rank-1 external field (1o, one
+    vector per graph or one for all), dipole / polarizability-style heads (bias-free linear maps of
+    the readout blocks, reduce "sum").  The energy is differentiable in ``pos`` and ``cell``
+    through the native reverse pass; the physical-tensor outputs are returned without a graph."""
+
+    def __init__(self, max_embed_radius: float, main_max_radius: float, main_number_of_basis: int,
+                 hidden_dim_conv: int, hidden_dim_sh=None, hidden_dim=None, channel_in2: int = 32,
+                 embedding_dim: int = 16, max_atomvalue: int = 10, output_size: int = 8, embed_size=None,
+                 main_hidden_sizes3=None, num_layers: int = 1, num_interaction: int = 2, device=None,
+                 function_type_main: str = "gaussian", lmax: int = 2, ictd_tp_path_policy: str = "full",
+                 ictd_tp_max_rank_other=None, internal_compute_dtype=None, ictd_tp_backend: str = "auto",
+                 invariant_channels: int = 32, physical_tensor_outputs=None, external_tensor_rank=None,
+                 external_tensor_irrep=None, external_tensor_parity=None, external_tensor_specs=None,
+                 o3_irrep_preset: str = "auto", o3_active_irreps=None, num_fidelity_levels: int = 0,
+                 long_range_mode: str = "none", feature_spectral_mode: str = "none",
+                 external_tensor_scale_init: float = 0.0, **unused):
+        super().__init__()
+        if embed_size is None:
+            embed_size = [128, 128, 128]
+        unsupported = []
+        if ictd_tp_path_policy != "full" or int(lmax) != 2:
+            unsupported.append("lmax != 2 or a path policy other than 'full'")
+        if external_tensor_specs or (external_tensor_rank is not None and int(external_tensor_rank) != 1):
+            unsupported.append("external tensors other than one rank-1 field")
+        if external_tensor_rank is not None and external_tensor_irrep not in (None, "1o") and \
+                external_tensor_parity not in (None, "o", -1):
+            unsupported.append("a 1e external field")
+        if num_fidelity_levels or long_range_mode != "none" or feature_spectral_mode != "none":
+            unsupported.append("multi-fidelity / long-range / spectral modules")
+        if o3_active_irreps is not None:
+            irreps = tuple(sorted({str(x).strip() for x in o3_active_irreps} | {"0e"},
+                                  key=lambda t: (int(t[0]), t[1] == "o")))
+        elif str(o3_irrep_preset).lower() in ("auto", "minimal"):
+            irreps = ("0e", "1o", "2e")
+        else:
+            irreps = ()
+        if irreps not in _O3_IRREPS:
+            unsupported.append(f"active irreps {irreps or o3_irrep_preset!r}")
+        heads = {}
+        for name, spec in (physical_tensor_outputs or {}).items():
+            if str(spec.get("reduce", "sum")).lower() != "sum" or spec.get("channels_out", 1) != 1:
+                unsupported.append(f"physical tensor head {name!r} (reduce 'sum', channels_out 1 only)")
+                continue
+            if spec.get("irreps") is not None:
+                ir = [str(x) for x in spec["irreps"]]
+            else:
+                ir = [_irrep_letter(int(l), 1 if int(l) % 2 == 0 else -1) for l in spec.get("ls", [])]
+            if any(x not in irreps for x in ir):
+                unsupported.append(f"physical tensor head {name!r} on inactive irreps")
+            heads[name] = ir
+        if unsupported:
+            raise NotImplementedError("fsctep_b200 pure-cartesian-ictd-o3 does not cover: " + ", ".join(unsupported))
+        if int(num_interaction) < 2:
+            raise ValueError(f"num_interaction must be >= 2, got {num_interaction}")
+        self.irreps = irreps
+        self.cfg = ICTDConfig(channels=int(hidden_dim_conv), lmax=2, num_interaction=int(num_interaction),
+                              number_of_basis=int(main_number_of_basis), max_radius=float(max_embed_radius),
+                              function_type=str(function_type_main), output_size=int(output_size),
+                              embedding_dim=int(embedding_dim), max_atomvalue=int(max_atomvalue),
+                              invariant_channels=int(invariant_channels), embed_size=tuple(embed_size),
+                              o3=True, o3_irreps=irreps)
+        self.cfg.native()
+        C, nint = int(hidden_dim_conv), int(num_interaction)
+        from fsctep_b200.ictd import o3_num_paths
+
+        P = o3_num_paths(irreps)
+        self.channels, self.num_interaction = C, nint
+        self.e3_conv_emb = _Conv1(self.cfg, P)
+        if external_tensor_rank is not None:
+            self.e3_conv_emb.external_tensor_scale_by_irrep = nn.Parameter(
+                torch.full((len(irreps),), float(external_tensor_scale_init)))
+        self.external_tensor_rank = external_tensor_rank
+        self.tp2_layers = nn.ModuleList([_TP(P, C, C, 1) for _ in range(nint - 1)])
+        self.fc2_layers = nn.ModuleList([_radial_mlp(int(main_number_of_basis), P) for _ in range(nint - 1)])
+        nC = C * nint
+        S = (nint - 1) * int(invariant_channels)
+        self.W_read = nn.ParameterDict({k: nn.Parameter(torch.randn(S, nC, nC) * 0.02) for k in irreps})
+        self.readout_linear = nn.Sequential(nn.Linear(S + nC * len(irreps), embed_size[0]), nn.SiLU(),
+                                            nn.Linear(embed_size[0], 17))
+        self.weighted_sum = _WeightedSum(17)
+        self.proj_total = _MainNet(nint * C * len(irreps) + S, embed_size, 17)
+        self._head_spec = heads
+        if heads:
+            self.physical_tensor_heads = nn.ModuleDict({
+                name: nn.ModuleDict({ir[0]: nn.Linear(nC, 1, bias=False) for ir in irs})
+                for name, irs in heads.items()})
+        else:
+            self.physical_tensor_heads = None
+        self._engine: Optional[ICTDEngine] = None
+        self._engine_key = None
+        self._generation = 0
+
+    _bump = PureCartesianICTDTransformerLayer._bump
+    _ensure_engine = PureCartesianICTDTransformerLayer._ensure_engine
+
+    def forward(self, pos, A, batch, edge_src, edge_dst, edge_shifts, cell, *, precomputed_edge_vec=None,
+                sync_after_scatter=None, external_tensor=None, fidelity_ids=None,
+                return_physical_tensors: bool = False, return_reciprocal_source: bool = False):
+        if precomputed_edge_vec is not None or sync_after_scatter is not None or return_reciprocal_source \
+                or fidelity_ids is not None:
+            raise NotImplementedError("fsctep_b200 pure-cartesian-ictd-o3 forward: optional inputs other than "
+                                      "external_tensor / return_physical_tensors are not covered")
+        if not pos.is_cuda:
+            raise RuntimeError("fsctep_b200 runs on CUDA devices only (no CPU path)")
+        n = pos.shape[0]
+        species = A.long()
+        if n and int(species.max().item()) >= self.cfg.max_atomvalue:
+            raise IndexError("atomic number out of range of atom_embedding (max_atomvalue)")
+        cell = cell.reshape(-1, 3, 3)
+        field = None
+        if external_tensor is not None:
+            if self.external_tensor_rank is None:
+                raise ValueError("external_tensor given but the model has no external tensor input")
+            field = external_tensor.detach().reshape(-1, 3)
+        eng = self._ensure_engine(pos.device)
+        graph = GraphCSR.from_edges(edge_src.long(), edge_dst.long(), edge_shifts, n)
+        e = _NativeEnergy.apply(pos, cell, self, graph, species, batch, field)
+        if not return_physical_tensors:
+            return e
+        if self.physical_tensor_heads is None:
+            raise ValueError("return_physical_tensors=True but physical_tensor_outputs was not set in __init__")
+        return e, eng.heads()
 
 
 def reference_state_dict_shapes(cfg: ICTDConfig) -> Dict[str, tuple]:

@@ -54,3 +54,29 @@ def test_edge_order_does_not_matter():
     e2 = m(pos, Z, b, *[a[perm].to(dev) for a in args], cell.float())
     torch.cuda.synchronize()
     assert (e1 - e2).abs().max().item() < 1e-5 * e1.abs().max().item()
+
+
+@pytest.mark.parametrize("tag", ["a", "b"])
+def test_o3_module_matches_reference(tag):
+    """Drop-in o3 module with a reference checkpoint: energy, autograd forces and heads."""
+    from test_models_cpu import _o3_module
+
+    cfg, sd, c = golden_io.o3_case(tag)
+    m = _o3_module(cfg, device="cpu")
+    m.load_state_dict({k: v.float() for k, v in sd.items()})
+    m = m.cuda()
+    dev = torch.device("cuda")
+    pos = torch.tensor(c["pos"], device=dev, dtype=torch.float32).requires_grad_(True)
+    b = torch.tensor(c["batch"], device=dev)
+    e, phys = m(pos, torch.tensor(c["Z"], device=dev), b, torch.tensor(c["edge_src"], device=dev),
+                torch.tensor(c["edge_dst"], device=dev), torch.tensor(c["edge_shifts"], device=dev).float(),
+                torch.tensor(c["cell"], device=dev).float(), external_tensor=torch.tensor(c["field"], device=dev),
+                return_physical_tensors=True)
+    B = c["cell"].shape[0]
+    Eg = torch.zeros(B, device=dev, dtype=e.dtype).index_add(0, b, e.view(-1))
+    (g,) = torch.autograd.grad(Eg.sum(), [pos])
+    E = Eg.detach().double().cpu().numpy()
+    assert np.all(np.abs(E - c["ref64_energy"]) <= U.E_RTOL * np.abs(c["ref64_energy"]).max())
+    assert U.rel_max(-g.cpu().numpy(), c["ref64_forces"]) <= U.F_RTOL
+    assert U.rel_max(phys["dipole"][1].cpu().numpy(), c["ref64_dipole"]) <= 1e-5
+    assert U.rel_max(phys["polarizability"][2].cpu().numpy(), c["ref64_polar2"]) <= 1e-5

@@ -33,3 +33,36 @@ def test_unsupported_options_raise():
     with pytest.raises(RuntimeError, match="CUDA"):
         m(torch.zeros(2, 3), torch.ones(2).long(), torch.zeros(2).long(), torch.zeros(1).long(),
           torch.ones(1).long(), torch.zeros(1, 3), torch.eye(3)[None])
+
+
+def _o3_module(cfg, device="meta"):
+    from fsctep_b200.models import PureCartesianICTDO3TransformerLayer
+
+    heads = {"dipole": {"irreps": ["1o"], "reduce": "sum"}, "polarizability": {"ls": [0, 2], "reduce": "sum"}}
+    with torch.device(device):
+        return PureCartesianICTDO3TransformerLayer(
+            max_embed_radius=float(cfg["max_radius"]), main_max_radius=float(cfg["max_radius"]),
+            main_number_of_basis=int(cfg["number_of_basis"]), hidden_dim_conv=int(cfg["channels"]),
+            hidden_dim_sh=32, hidden_dim=64, lmax=2, num_interaction=int(cfg["num_interaction"]),
+            function_type_main=str(cfg["function_type"]), max_atomvalue=int(cfg["max_atomvalue"]),
+            external_tensor_rank=1, external_tensor_irrep="1o", physical_tensor_outputs=heads,
+            o3_active_irreps=["0e", "1e", "1o", "2e"])
+
+
+@pytest.mark.parametrize("tag", ["a", "b"])
+def test_o3_module_state_dict_matches_reference(tag):
+    z = golden_io.load(f"ictd_o3_{tag}.npz")
+    ref = {k[len("sdshape/"):]: tuple(int(x) for x in z[k]) for k in z.files if k.startswith("sdshape/")}
+    cfg = {k[4:]: z[k].item() for k in z.files if k.startswith("cfg_")}
+    m = _o3_module(cfg)
+    mine = {k: tuple(v.shape) for k, v in m.state_dict().items()}
+    assert mine == ref
+
+
+def test_o3_module_rejects_uncovered_options():
+    from fsctep_b200.models import PureCartesianICTDO3TransformerLayer
+
+    with pytest.raises(NotImplementedError):
+        PureCartesianICTDO3TransformerLayer(5.0, 5.0, 8, 32, o3_irrep_preset="full")
+    with pytest.raises(NotImplementedError):
+        PureCartesianICTDO3TransformerLayer(5.0, 5.0, 8, 32, external_tensor_rank=2)
