@@ -20,6 +20,9 @@ Fixtures:
   (``pure_cartesian_ictd_layers_o3.py``) with active irreps 0e,1e,1o,2e, an external 1o field
   drawn from N(0, 0.05) per graph and dipole (1o) + polarizability (0e, 2e) heads on batches
   of non-periodic molecules: energies, forces, per-atom energies and the heads' outputs.
+* ``sparse_{a,b}.npz`` -- the same for ``PureCartesianSparseTransformerLayer``
+  (``pure_cartesian_sparse_layers.py``; max_rank_other 1, k_policy k0): a config-2-like water box
+  (Lmax 2) and a config-5-like FCC crystal (Lmax 3, with stress).
 * ``tp_ops.npz`` -- the ``_C_ictd_tp`` operator family evaluated by the reference's
   einsum references (``models/ictd_irreps_cuda.py:169-311``) on the shapes of
   ``test/test_ictd_tp_backend.py``.
@@ -190,6 +193,45 @@ def o3_case(tag, system, cfg, seed, field_seed):
           "dipole", out["ref64_dipole"].reshape(B, -1)[0])
 
 
+def sparse_case(tag, system, cfg, seed):
+    from molecular_force_field.models.pure_cartesian_sparse_layers import PureCartesianSparseTransformerLayer
+
+    torch.set_default_dtype(torch.float64)
+    model = PureCartesianSparseTransformerLayer(
+        max_embed_radius=cfg["max_radius"], main_max_radius=cfg["max_radius"],
+        main_number_of_basis=cfg["number_of_basis"], hidden_dim_conv=cfg["channels"], hidden_dim_sh=32,
+        hidden_dim=64, lmax=cfg["lmax"], num_interaction=cfg["num_interaction"],
+        function_type_main=cfg["function_type"], max_atomvalue=cfg["max_atomvalue"], device=torch.device("cpu"))
+    shapes = _perturb(model, seed)
+    src, dst, S = neighbors.batched_neighbor_list(system["pos"], system["batch"], system["cell"],
+                                                  cfg["max_radius"], system["pbc"])
+    args = (system["pos"], system["Z"], system["batch"], src, dst, S.astype(np.float64), system["cell"])
+    r64 = _ref_efs(model, *args, torch.float64)
+    out = {"pos": system["pos"], "Z": system["Z"], "batch": system["batch"], "cell": system["cell"],
+           "pbc": np.array(system["pbc"]), "edge_src": src.astype(np.int32), "edge_dst": dst.astype(np.int32),
+           "edge_shifts": S.astype(np.int8)}
+    for k, v in cfg.items():
+        out[f"cfg_{k}"] = np.array(v)
+    out["sd_seed"] = np.array(seed)
+    for k, v in model.state_dict().items():
+        out[f"sdshape/{k}"] = np.array(shapes[k], dtype=np.int64)
+        out[f"sdsum/{k}"] = np.array(float(v.double().sum()))
+    for k, v in r64.items():
+        out[f"ref64_{k}"] = v
+    np.savez_compressed(os.path.join(HERE, f"sparse_{tag}.npz"), **out)
+    print("sparse", tag, "atoms", system["pos"].shape[0], "edges", src.shape[0], "E", r64["energy"],
+          "max|F|", np.abs(r64["forces"]).max())
+
+
+def sparse():
+    cfg2 = dict(channels=32, lmax=2, num_interaction=3, number_of_basis=8, max_radius=5.0,
+                function_type="gaussian", max_atomvalue=10)
+    sparse_case("a", systems.water_box(n_side=4, box=12.4, seed=18), cfg2, seed=6)
+    cfg5 = dict(channels=32, lmax=3, num_interaction=3, number_of_basis=8, max_radius=5.0,
+                function_type="gaussian", max_atomvalue=30)
+    sparse_case("b", systems.fcc_crystal(n_cells=(3, 3, 3), seed=19), cfg5, seed=7)
+
+
 def tp_ops():
     from molecular_force_field.models import ictd_irreps_cuda as RC
 
@@ -226,6 +268,7 @@ def main():
                  function_type="gaussian", max_atomvalue=16)
     model_case("c", systems.diamond_crystal(n_cells=(2, 2, 2), seed=13, sigma=0.15), cfg_c, seed=3)
     o3()
+    sparse()
 
 
 def o3():
@@ -239,5 +282,7 @@ def o3():
 if __name__ == "__main__":
     if len(sys.argv) > 1 and sys.argv[1] == "o3":
         o3()
+    elif len(sys.argv) > 1 and sys.argv[1] == "sparse":
+        sparse()
     else:
         main()
