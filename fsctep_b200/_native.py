@@ -37,6 +37,19 @@ class IctdWeights(C.Structure):
                 ("out_c0", C.c_float)]
 
 
+class SparseConfig(C.Structure):
+    _fields_ = [("channels", I32), ("lmax", I32), ("num_interaction", I32), ("number_of_basis", I32),
+                ("basis_kind", I32), ("max_radius", C.c_float), ("num_species", I32), ("invariant_channels", I32),
+                ("n_hidden", I32), ("hidden", I32 * 4), ("n_out", I32)]
+
+
+class SparseWeights(C.Structure):
+    _fields_ = [("rad_w1", P), ("rad_b1", P), ("rad_w2", P), ("rad_b2", P), ("pair_k", P), ("mix", P),
+                ("mixT", P), ("wread_p", P), ("wread_s", P), ("pairs", P), ("mn_in_g", P), ("mn_in_b", P),
+                ("mn_w", P * 4), ("mn_b", P * 4), ("mn_g", P * 4), ("mn_beta", P * 4), ("out_v", P),
+                ("out_c0", C.c_float)]
+
+
 class Graph(C.Structure):
     _fields_ = [("num_atoms", I64), ("num_local", I64), ("num_edges", I64), ("num_graphs", I64), ("pos", P),
                 ("species", P), ("batch", P), ("cell", P), ("row_ptr", P), ("src", P), ("shift", P),
@@ -85,6 +98,12 @@ _PROTOS = {
                                     C.POINTER(IctdOutputs), P, C.c_size_t, P]),
     "fsc_ictd_status": (C.c_int, [C.POINTER(IctdConfig), I64, I64, P, P, C.POINTER(C.c_int)]),
     "fsc_ictd_set_readout_path": (None, [C.c_int]),
+    "fsc_sparse_workspace_bytes": (C.c_size_t, [C.POINTER(SparseConfig), I64, I64]),
+    "fsc_sparse_forward": (C.c_int, [C.POINTER(SparseConfig), C.POINTER(SparseWeights), C.POINTER(Graph), P, P, P,
+                                     C.c_size_t, P]),
+    "fsc_sparse_backward": (C.c_int, [C.POINTER(SparseConfig), C.POINTER(SparseWeights), C.POINTER(Graph),
+                                      C.POINTER(IctdOutputs), P, C.c_size_t, P]),
+    "fsc_sparse_status": (C.c_int, [C.POINTER(SparseConfig), I64, I64, P, P, C.POINTER(C.c_int)]),
     "fsc_ictd_heads": (C.c_int, [P, P, P, C.c_int, P, P, P, P, C.c_size_t, P]),
     "fsc_ictd_set_radial_path": (None, [C.c_int]),
     "fsc_profile_enable": (None, [C.c_int]),

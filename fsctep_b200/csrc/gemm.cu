@@ -65,10 +65,10 @@ __global__ void __launch_bounds__(256) gemm_kernel(GemmArgs a) {
     const int64_t row = row0 + ty * 4 + i;
     if (row >= M) continue;
     const int64_t g = row / a.R, r = row % a.R;
-    float scale = 1.f;
+    float scale = a.alpha != 0.f ? a.alpha : 1.f;
     if (a.deg_rowptr) {
       const int d = a.deg_rowptr[g + 1] - a.deg_rowptr[g];
-      scale = 1.f / (float)(d > 1 ? d : 1);
+      scale *= 1.f / (float)(d > 1 ? d : 1);
     }
     float* cptr = a.C + g * a.c_gs + r * a.c_rs;
 #pragma unroll

@@ -57,6 +57,8 @@ struct RadialTcArgs {
   const float* dY;       // backward input [E][12]
   float* edge_grad;      // backward output [E][3]
   int* err;              // first failing wait site (0 = ok)
+  float* hout;           // forward: non-null -> write h2 [nint][E][64] instead of gates
+  const float* hout_grad;// backward: non-null -> dE/dh2 [nint][E][64]; dE/d|r| summed into edge_grad[e][0]
 };
 bool radial_tc_supported(int nb);
 int launch_radial_fwd_tc(const RadialTcArgs& a, cudaStream_t st);
@@ -112,6 +114,7 @@ struct GemmArgs {
   const int32_t* deg_rowptr;
   const float* bias;
   int accumulate;
+  float alpha;  // extra scale of the product (0 means 1)
 };
 int launch_gemm(const GemmArgs& a, cudaStream_t st);
 
@@ -182,5 +185,10 @@ int launch_energy(const float* x, int64_t N, int H, const float* v, float c0, co
 // dx[n] = v * weight[n]  (weight NULL: 1 for n < num_local, else 0)
 int launch_energy_seed(int64_t N, int H, const float* v, const float* weight, int64_t num_local, float* dx,
                        cudaStream_t st);
+
+// Optional per-stage CUDA-event timing (engine.cu).
+namespace prof {
+void mark(const char* name, cudaStream_t st);
+}
 
 }  // namespace fsc

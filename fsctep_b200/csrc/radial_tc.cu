@@ -86,7 +86,7 @@ __device__ __forceinline__ void load_bias(float* bias, const RadialW& W, int lay
     float v;
     if (i < RH) v = W.b1[layer * RH + i];
     else if (i < 2 * RH) v = W.b2[layer * RH + i - RH];
-    else v = (i - 2 * RH) < RP ? W.b3[layer * RP + i - 2 * RH] : 0.f;
+    else v = ((i - 2 * RH) < RP && W.b3) ? W.b3[layer * RP + i - 2 * RH] : 0.f;
     bias[i] = v;
   }
 }
@@ -161,7 +161,9 @@ __device__ __forceinline__ void drain(uint64_t* bar, uint32_t phase) {
 }
 
 // ------------------------------------------------------------------ forward
-template <int NBP>
+// HOUT: stop after the second hidden layer and write h2 = silu(W2 h1 + b2) ([nint][E][64]) for
+// callers that fold the last linear layer into their own contraction (pure-cartesian-sparse).
+template <int NBP, bool HOUT>
 __global__ void __launch_bounds__(RT, RT_PER_SM) radial_fwd_tc_kernel(RadialTcArgs a) {
   using IM = FwdImg<NBP>;
   using SM = RtSmem<IM::SIZE>;
@@ -204,9 +206,11 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_fwd_tc_kernel(RadialTcAr
       put_b(img_hi, img_lo, IM::W1, RH, k, b, b < a.nb ? w1[k * a.nb + b] : 0.f);
     }
     for (int i = tid; i < RH * RH; i += RT) put_b(img_hi, img_lo, IM::W2, RH, i >> 6, i & 63, w2[i]);
-    for (int i = tid; i < 16 * RH; i += RT) {
-      const int q = i >> 6, j = i & 63;
-      put_b(img_hi, img_lo, IM::W3, 16, q, j, q < RP ? w3[q * RH + j] : 0.f);
+    if (!HOUT) {
+      for (int i = tid; i < 16 * RH; i += RT) {
+        const int q = i >> 6, j = i & 63;
+        put_b(img_hi, img_lo, IM::W3, 16, q, j, q < RP ? w3[q * RH + j] : 0.f);
+      }
     }
     load_bias(bias, a.rad, layer);
     fence_proxy_async_smem();
@@ -262,7 +266,19 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_fwd_tc_kernel(RadialTcAr
         tc::tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = silu((__uint_as_float(u[i]) + __uint_as_float(w[i])) + bias[RH + 32 * h + i]);
-        store_a32(tAhi + lane_off, tAlo + lane_off, 32u * h, v);
+        if (HOUT) {
+          if (valid) {
+            float4* o = reinterpret_cast<float4*>(a.hout + ((int64_t)layer * a.E + e) * RH + 32 * h);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          }
+        } else {
+          store_a32(tAhi + lane_off, tAlo + lane_off, 32u * h, v);
+        }
+      }
+      if (HOUT) {
+        tc::tc_fence_before();
+        continue;
       }
       a_ready();
       if (tid == 0) {
@@ -298,7 +314,9 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_fwd_tc_kernel(RadialTcAr
 }
 
 // ------------------------------------------------------------------ backward
-template <int NBP>
+// HOUT: dE/dh2 comes from hout_grad ([nint][E][64]) instead of the gates, and every layer only
+// accumulates dE/d|r| into edge_grad[e][0] (the caller adds the direction part).
+template <int NBP, bool HOUT>
 __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcArgs a) {
   using IM = BwdImg<NBP>;
   using SM = RtSmem<IM::SIZE>;
@@ -311,7 +329,8 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcAr
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::BAR + 8);
 
   const int tid = threadIdx.x, warp = tid >> 5;
-  for (int i = tid; i < ictd2::NMONO * ictd2::NK; i += RT) ypoly[i] = a.tables[ictd2::TAB_YPOLY + i];
+  if (!HOUT)
+    for (int i = tid; i < ictd2::NMONO * ictd2::NK; i += RT) ypoly[i] = a.tables[ictd2::TAB_YPOLY + i];
   if (warp == 0) {
     tc::tmem_alloc(tmem_slot, 256);
     tc::tmem_relinquish();
@@ -351,9 +370,11 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcAr
       put_b(img_hi, img_lo, IM::W2, RH, j, k, w2[i]);
       put_b(img_hi, img_lo, IM::W2T, RH, k, j, w2[i]);
     }
-    for (int i = tid; i < RH * 16; i += RT) {
-      const int j = i >> 4, q = i & 15;
-      put_b(img_hi, img_lo, IM::W3P, RH, j, q, q < RP ? w3[q * RH + j] : 0.f);
+    if (!HOUT) {
+      for (int i = tid; i < RH * 16; i += RT) {
+        const int j = i >> 4, q = i & 15;
+        put_b(img_hi, img_lo, IM::W3P, RH, j, q, q < RP ? w3[q * RH + j] : 0.f);
+      }
     }
     load_bias(bias, a.rad, layer);
     fence_proxy_async_smem();
@@ -376,11 +397,13 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcAr
           ry[0] = r4.y; ry[1] = r4.z; ry[2] = r4.w;
           const float len = sqrtf(r4.y * r4.y + r4.z * r4.z + r4.w * r4.w);
           radial_basis<NBP>(a.basis_kind, a.nb, a.rc, len, v, demb);
-          const float4* dg4 = reinterpret_cast<const float4*>(a.dgates + ((int64_t)layer * a.E + e) * 12);
-          const float4 g0 = dg4[0], g1 = dg4[1], g2 = dg4[2];
-          v[NBP + 0] = g0.x; v[NBP + 1] = g0.y; v[NBP + 2] = g0.z; v[NBP + 3] = g0.w;
-          v[NBP + 4] = g1.x; v[NBP + 5] = g1.y; v[NBP + 6] = g1.z; v[NBP + 7] = g1.w;
-          v[NBP + 8] = g2.x; v[NBP + 9] = g2.y; v[NBP + 10] = g2.z;
+          if (!HOUT) {
+            const float4* dg4 = reinterpret_cast<const float4*>(a.dgates + ((int64_t)layer * a.E + e) * 12);
+            const float4 g0 = dg4[0], g1 = dg4[1], g2 = dg4[2];
+            v[NBP + 0] = g0.x; v[NBP + 1] = g0.y; v[NBP + 2] = g0.z; v[NBP + 3] = g0.w;
+            v[NBP + 4] = g1.x; v[NBP + 5] = g1.y; v[NBP + 6] = g1.z; v[NBP + 7] = g1.w;
+            v[NBP + 8] = g2.x; v[NBP + 9] = g2.y; v[NBP + 10] = g2.z;
+          }
         }
         store_a32(tAhi + lane_off, tAlo + lane_off, 0, v);
       }
@@ -388,7 +411,8 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcAr
       if (tid == 0) {
         tc::tc_fence_after();
         mma_3xtf32(tD0, tAhi, tAlo, s_hi + 4u * IM::W1, s_lo + 4u * IM::W1, 64, NBP / 8, id64);
-        mma_3xtf32(tD1, tAhi + NBP, tAlo + NBP, s_hi + 4u * IM::W3P, s_lo + 4u * IM::W3P, 64, 2, id64);
+        if (!HOUT)
+          mma_3xtf32(tD1, tAhi + NBP, tAlo + NBP, s_hi + 4u * IM::W3P, s_lo + 4u * IM::W3P, 64, 2, id64);
         tc::mma_commit(bar);
       }
       if (!(ok = d_ready(bar, phase, a.err, 51))) break;
@@ -421,8 +445,17 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcAr
         uint32_t u[32], w[32];
         float v[32];
         tc::tmem_ld32(tD0 + lane_off + 32u * h, u);
-        tc::tmem_ld32(tD1 + lane_off + 32u * h, w);
+        if (!HOUT) tc::tmem_ld32(tD1 + lane_off + 32u * h, w);
         tc::tmem_wait_ld();
+        if (HOUT) {
+          const float4* g4 = reinterpret_cast<const float4*>(a.hout_grad + ((int64_t)layer * a.E + e) * RH + 32 * h);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 t = valid ? g4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            w[4 * i] = __float_as_uint(t.x); w[4 * i + 1] = __float_as_uint(t.y);
+            w[4 * i + 2] = __float_as_uint(t.z); w[4 * i + 3] = __float_as_uint(t.w);
+          }
+        }
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(w[i]) * silu_grad(__uint_as_float(u[i]) + bias[RH + 32 * h + i]);
         store_a32(tAhi + lane_off, tAlo + lane_off, 32u * h, v);
@@ -463,7 +496,7 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcAr
           for (int b = 0; b < NBP; ++b) dl = fmaf(de[b], demb[b], dl);
           float* eg = a.edge_grad + 3 * e;
           if (layer > 0) dl += eg[0];
-          if (layer + 1 < a.nint) {
+          if (HOUT || layer + 1 < a.nint) {
             eg[0] = dl;
           } else {
             float dYe[ictd2::NK], g[3];
@@ -518,17 +551,29 @@ bool radial_tc_supported(int nb) { return nb >= 1 && nb <= 16; }
 int launch_radial_fwd_tc(const RadialTcArgs& a, cudaStream_t st) {
   if (a.E == 0) return FSC_OK;
   if (!radial_tc_supported(a.nb)) return fail(FSC_ERR_UNSUPPORTED, "radial_fwd_tc: number_of_basis must be 1..16");
+  if (a.hout) {
+    if (a.nb <= 8)
+      return launch_rt(radial_fwd_tc_kernel<8, true>, RtSmem<FwdImg<8>::SIZE>::TOTAL, a, st, "radial_fwd_tc_kernel<8,h>");
+    return launch_rt(radial_fwd_tc_kernel<16, true>, RtSmem<FwdImg<16>::SIZE>::TOTAL, a, st,
+                     "radial_fwd_tc_kernel<16,h>");
+  }
   if (a.nb <= 8)
-    return launch_rt(radial_fwd_tc_kernel<8>, RtSmem<FwdImg<8>::SIZE>::TOTAL, a, st, "radial_fwd_tc_kernel<8>");
-  return launch_rt(radial_fwd_tc_kernel<16>, RtSmem<FwdImg<16>::SIZE>::TOTAL, a, st, "radial_fwd_tc_kernel<16>");
+    return launch_rt(radial_fwd_tc_kernel<8, false>, RtSmem<FwdImg<8>::SIZE>::TOTAL, a, st, "radial_fwd_tc_kernel<8>");
+  return launch_rt(radial_fwd_tc_kernel<16, false>, RtSmem<FwdImg<16>::SIZE>::TOTAL, a, st, "radial_fwd_tc_kernel<16>");
 }
 
 int launch_radial_bwd_tc(const RadialTcArgs& a, cudaStream_t st) {
   if (a.E == 0) return FSC_OK;
   if (!radial_tc_supported(a.nb)) return fail(FSC_ERR_UNSUPPORTED, "radial_bwd_tc: number_of_basis must be 1..16");
+  if (a.hout_grad) {
+    if (a.nb <= 8)
+      return launch_rt(radial_bwd_tc_kernel<8, true>, RtSmem<BwdImg<8>::SIZE>::TOTAL, a, st, "radial_bwd_tc_kernel<8,h>");
+    return launch_rt(radial_bwd_tc_kernel<16, true>, RtSmem<BwdImg<16>::SIZE>::TOTAL, a, st,
+                     "radial_bwd_tc_kernel<16,h>");
+  }
   if (a.nb <= 8)
-    return launch_rt(radial_bwd_tc_kernel<8>, RtSmem<BwdImg<8>::SIZE>::TOTAL, a, st, "radial_bwd_tc_kernel<8>");
-  return launch_rt(radial_bwd_tc_kernel<16>, RtSmem<BwdImg<16>::SIZE>::TOTAL, a, st, "radial_bwd_tc_kernel<16>");
+    return launch_rt(radial_bwd_tc_kernel<8, false>, RtSmem<BwdImg<8>::SIZE>::TOTAL, a, st, "radial_bwd_tc_kernel<8>");
+  return launch_rt(radial_bwd_tc_kernel<16, false>, RtSmem<BwdImg<16>::SIZE>::TOTAL, a, st, "radial_bwd_tc_kernel<16>");
 }
 
 }  // namespace fsc

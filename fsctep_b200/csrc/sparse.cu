@@ -1,0 +1,995 @@
+// pure-cartesian-sparse energy + forces (models/pure_cartesian_sparse_layers.py:459-855,
+// PureCartesianTensorProductO3Sparse with max_rank_other = 1, k_policy = "k0", no epsilon,
+// pseudotensors identically zero: models/pure_cartesian.py:736-929).
+//
+// Node features are true Cartesian tensors f[n][comp][c], comp = roff(L) + row-major index of the
+// rank-L tensor (R = sum_L 3^L components).  Every tensor-product path p = (L1, L2, Lout = L1+L2)
+// is an outer product: message_p[e][(i, j)][a] = x1[src][roff(L1)+i][a] * n_e^{(x)L2}[j].
+//
+// The reference forms per-edge channel-mixing weights W_e = fc.4(h2_e), P*C*C1*C2 floats per edge
+// (14.7 GB per layer at config 2), and contracts them with the messages.  Here fc.4 is applied
+// after aggregation instead:
+//   conv2:  out[n][Lout comp][c] = (1/avg) sum_{p(Lout), j, a} W[(p, c, a), j] Z_p[n][comp][j][a],
+//           Z_p[n][comp][j][a] = sum_{e -> n} h2'_e[j] message_p[e][comp][a],  h2' = [h2, 1]
+//   (one per-node aggregation kernel + one GEMM per Lout); conv1 folds fc.4 and the atom
+//   features of both ends into per-species-pair tables.  The reverse pass mirrors it: a GEMM
+//   gives dZ, one kernel per edge yields dE/dh2', dE/dn^{(x)L} and the feature gradient of the
+//   source, and the radial MLP backward (radial_tc.cu) turns dE/dh2 into dE/d|r|.
+#include <algorithm>
+#include <cmath>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace fsc {
+namespace sp {
+
+constexpr int J = 65;          // radial hidden width + the bias row
+constexpr int RH = 64;
+constexpr int MAXR = 40;       // components up to rank 3
+constexpr int MAXROWS = 144;   // sum over paths of 3^Lout (142 at lmax 3)
+constexpr int64_t kMaxGraphs = 4096;
+constexpr int64_t kZBudgetFloats = (int64_t)1 << 30;  // aggregation buffer, 4 GB
+constexpr int64_t kGramChunk = 16384;
+
+__host__ __device__ constexpr int pow3(int L) { return L == 0 ? 1 : 3 * pow3(L - 1); }
+__host__ __device__ constexpr int roff(int L) { return (pow3(L) - 1) / 2; }
+
+// conv2 aggregation rows (built on the host).  Row order: Lout, then the component of the
+// rank-Lout output, then the rank q of the path among those with that Lout.
+struct Rows {
+  int nrows, npaths, R, lmax;
+  unsigned char c1[MAXROWS];  // x1 component of the row
+  unsigned char c2[MAXROWS];  // n^{(x)L2} component of the row
+  unsigned char rlist[MAXROWS];
+  short c1off[MAXR + 1];      // rows with x1 component c1: rlist[c1off[c1] .. c1off[c1+1])
+  int zoff[4], npl[4];        // first row and number of paths of each Lout
+  int p1[4];                  // conv1: path index of (L, 0, L)
+};
+
+Rows make_rows(int lmax) {
+  Rows r{};
+  r.lmax = lmax;
+  r.R = roff(lmax + 1);
+  std::vector<int> L1s, L2s, Ls;
+  for (int L1 = 0; L1 <= lmax; ++L1)
+    for (int L2 = 0; L2 <= lmax; ++L2)
+      if (std::min(L1, L2) <= 1 && L1 + L2 <= lmax) {
+        if (L2 == 0) r.p1[L1] = (int)L1s.size();
+        L1s.push_back(L1);
+        L2s.push_back(L2);
+        Ls.push_back(L1 + L2);
+      }
+  r.npaths = (int)L1s.size();
+  int row = 0;
+  std::vector<int> c1v, c2v;
+  for (int Lo = 0; Lo <= lmax; ++Lo) {
+    std::vector<int> ps;
+    for (int p = 0; p < r.npaths; ++p)
+      if (Ls[p] == Lo) ps.push_back(p);
+    r.zoff[Lo] = row;
+    r.npl[Lo] = (int)ps.size();
+    for (int k = 0; k < pow3(Lo); ++k)
+      for (int p : ps) {
+        const int L2 = L2s[p], L1 = L1s[p];
+        const int i = k / pow3(L2), j = k % pow3(L2);
+        c1v.push_back(roff(L1) + i);
+        c2v.push_back(roff(L2) + j);
+        ++row;
+      }
+  }
+  r.nrows = row;
+  for (int q = 0; q < row; ++q) {
+    r.c1[q] = (unsigned char)c1v[q];
+    r.c2[q] = (unsigned char)c2v[q];
+  }
+  int pos = 0;
+  for (int c = 0; c < r.R; ++c) {
+    r.c1off[c] = (short)pos;
+    for (int q = 0; q < row; ++q)
+      if (c1v[q] == c) r.rlist[pos++] = (unsigned char)q;
+  }
+  r.c1off[r.R] = (short)pos;
+  return r;
+}
+
+// n^{(x)L} for L <= lmax, row-major, out[roff(L) + idx]
+__device__ __forceinline__ void npow_all(int lmax, float x, float y, float z, float* out) {
+  const float n[3] = {x, y, z};
+  out[0] = 1.f;
+  out[1] = x; out[2] = y; out[3] = z;
+  if (lmax >= 2)
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+      for (int j = 0; j < 3; ++j) out[4 + 3 * i + j] = n[i] * n[j];
+  if (lmax >= 3)
+#pragma unroll
+    for (int i = 0; i < 9; ++i)
+#pragma unroll
+      for (int k = 0; k < 3; ++k) out[13 + 3 * i + k] = out[4 + i] * n[k];
+}
+
+// dE/dn from dE/d(n^{(x)L})
+__device__ __forceinline__ void npow_grad(int lmax, const float* n, const float* d, float* dn) {
+  dn[0] = d[1]; dn[1] = d[2]; dn[2] = d[3];
+  if (lmax >= 2)
+    for (int i = 0; i < 3; ++i)
+      for (int j = 0; j < 3; ++j) {
+        const float g = d[4 + 3 * i + j];
+        dn[i] += g * n[j];
+        dn[j] += g * n[i];
+      }
+  if (lmax >= 3)
+    for (int i = 0; i < 3; ++i)
+      for (int j = 0; j < 3; ++j)
+        for (int k = 0; k < 3; ++k) {
+          const float g = d[13 + 9 * i + 3 * j + k];
+          dn[i] += g * n[j] * n[k];
+          dn[j] += g * n[i] * n[k];
+          dn[k] += g * n[i] * n[j];
+        }
+}
+
+struct GradList {
+  float* p[8];
+};
+
+struct Args {
+  int64_t N, E;
+  int C, R, lmax, S_species;
+  const int32_t* row_ptr;
+  const int32_t* src;
+  const int32_t* dst;
+  const int32_t* species;
+  const float* edge_y;  // [E][12]: n (0..2), |r| (3), r (9..11)
+};
+
+// ---------------------------------------------------------------- geometry
+__global__ void geom_kernel(int64_t E, const float* __restrict__ pos, const int32_t* __restrict__ src,
+                            const int32_t* __restrict__ dst, const int32_t* __restrict__ batch,
+                            const float* __restrict__ cell, const float* __restrict__ shift, float* __restrict__ ey) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= E) return;
+  const int i = src[e], j = dst[e];
+  const float* c = cell + 9 * (int64_t)batch[i];
+  const float s0 = shift[3 * e], s1 = shift[3 * e + 1], s2 = shift[3 * e + 2];
+  float r[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) r[k] = pos[3 * (int64_t)j + k] - pos[3 * (int64_t)i + k] + (s0 * c[k] + s1 * c[3 + k] + s2 * c[6 + k]);
+  const float len = sqrtf(r[0] * r[0] + r[1] * r[1] + r[2] * r[2]);
+  const float inv = 1.f / fmaxf(len, 1e-8f);
+  float* o = ey + 12 * e;
+  o[0] = r[0] * inv; o[1] = r[1] * inv; o[2] = r[2] * inv; o[3] = len;
+  o[4] = o[5] = o[6] = o[7] = o[8] = 0.f;
+  o[9] = r[0]; o[10] = r[1]; o[11] = r[2];
+}
+
+// ---------------------------------------------------------------- conv1
+// Warp per receiving node, lanes over channels: f1[n][comp][c] = (1/deg) sum_e g_L(e)[c] n^{(x)L}[comp],
+// g_L[c] = sum_j h2'_e[j] K[s_src][s_n][L][j][c].
+template <int CPL>
+__global__ void __launch_bounds__(256) conv1_fwd_kernel(Args a, const float* __restrict__ K, const float* __restrict__ h2,
+                                                        float* __restrict__ f1) {
+  __shared__ float hs[8][J + 3];
+  __shared__ float np[8][MAXR];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t n = (int64_t)blockIdx.x * 8 + warp;
+  if (n >= a.N) return;
+  const int C = 32 * CPL, R = a.R;
+  float acc[MAXR][CPL];
+#pragma unroll
+  for (int q = 0; q < MAXR; ++q)
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) acc[q][i] = 0.f;
+  const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
+  const int sn = a.species[n];
+  for (int e = e0; e < e1; ++e) {
+    const int s = a.src[e];
+    const float* kt = K + ((int64_t)a.species[s] * a.S_species + sn) * (a.lmax + 1) * J * C;
+    hs[warp][lane] = h2[(int64_t)e * RH + lane];
+    hs[warp][lane + 32] = h2[(int64_t)e * RH + lane + 32];
+    if (lane == 0) {
+      hs[warp][64] = 1.f;
+      const float* y = a.edge_y + 12 * (int64_t)e;
+      npow_all(a.lmax, y[0], y[1], y[2], np[warp]);
+    }
+    __syncwarp();
+    for (int L = 0; L <= a.lmax; ++L) {
+      float g[CPL];
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) g[i] = 0.f;
+      const float* kl = kt + (int64_t)L * J * C;
+      for (int j = 0; j < J; ++j) {
+        const float h = hs[warp][j];
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) g[i] = fmaf(h, kl[j * C + lane + 32 * i], g[i]);
+      }
+      for (int q = roff(L); q < roff(L + 1); ++q) {
+        const float v = np[warp][q];
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) acc[q][i] = fmaf(g[i], v, acc[q][i]);
+      }
+    }
+    __syncwarp();
+  }
+  const int deg = e1 - e0;
+  const float inv = 1.f / (float)(deg > 1 ? deg : 1);
+  for (int q = 0; q < R; ++q)
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) f1[(n * R + q) * C + lane + 32 * i] = acc[q][i] * inv;
+}
+
+// conv1 backward: per edge dE/dh2 (layer 0) and dE/dn^{(x)L} (accumulated), from G1 = dE/df1.
+template <int CPL>
+__global__ void __launch_bounds__(256) conv1_bwd_kernel(Args a, const float* __restrict__ K, const float* __restrict__ h2,
+                                                        const float* __restrict__ G1, float* __restrict__ dh2,
+                                                        float* __restrict__ dnp) {
+  __shared__ float hs[8][J + 3];
+  __shared__ float np[8][MAXR];
+  __shared__ float dg[8][4][128];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t n = (int64_t)blockIdx.x * 8 + warp;
+  if (n >= a.N) return;
+  const int C = 32 * CPL, R = a.R;
+  const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
+  const int deg = e1 - e0;
+  const float inv = 1.f / (float)(deg > 1 ? deg : 1);
+  const int sn = a.species[n];
+  for (int e = e0; e < e1; ++e) {
+    const int s = a.src[e];
+    const float* kt = K + ((int64_t)a.species[s] * a.S_species + sn) * (a.lmax + 1) * J * C;
+    hs[warp][lane] = h2[(int64_t)e * RH + lane];
+    hs[warp][lane + 32] = h2[(int64_t)e * RH + lane + 32];
+    if (lane == 0) {
+      hs[warp][64] = 1.f;
+      const float* y = a.edge_y + 12 * (int64_t)e;
+      npow_all(a.lmax, y[0], y[1], y[2], np[warp]);
+    }
+    __syncwarp();
+    float dnl[MAXR];
+    for (int L = 0; L <= a.lmax; ++L) {
+      float g[CPL], d[CPL];
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) g[i] = d[i] = 0.f;
+      const float* kl = kt + (int64_t)L * J * C;
+      for (int j = 0; j < J; ++j) {
+        const float h = hs[warp][j];
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) g[i] = fmaf(h, kl[j * C + lane + 32 * i], g[i]);
+      }
+      for (int q = roff(L); q < roff(L + 1); ++q) {
+        const float v = np[warp][q];
+        float t = 0.f;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+          const float gv = G1[(n * R + q) * C + lane + 32 * i] * inv;
+          d[i] = fmaf(gv, v, d[i]);
+          t = fmaf(gv, g[i], t);
+        }
+        dnl[q] = warp_sum(t);
+      }
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) dg[warp][L][lane + 32 * i] = d[i];
+    }
+    __syncwarp();
+    // dh2'[j] = sum_L sum_c dg_L[c] K[L][j][c], lanes over j
+    for (int j = lane; j < RH; j += 32) {
+      float t = 0.f;
+      for (int L = 0; L <= a.lmax; ++L) {
+        const float* kr = kt + ((int64_t)L * J + j) * C;
+        for (int c = 0; c < C; ++c) t = fmaf(dg[warp][L][c], kr[c], t);
+      }
+      dh2[(int64_t)e * RH + j] = t;
+    }
+    if (lane == 0)
+      for (int q = 0; q < R; ++q) dnp[(int64_t)e * MAXR + q] += dnl[q];
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------- conv2 forward aggregation
+// Block per receiving node; thread item (row r, channel a) with 65 accumulators over j:
+// Z[n][r][j][a] = sum_e h2'_e[j] x1[src_e][c1(r)][a] n_e^{(x)L2}[c2(r)].
+constexpr int ZEB = 32;  // edges staged per batch
+
+__global__ void __launch_bounds__(256) z_kernel(Args a, Rows rows, const float* __restrict__ x,
+                                                const float* __restrict__ h2, int64_t n0, float* __restrict__ Z) {
+  __shared__ __align__(16) float hs[ZEB][RH];
+  __shared__ float np[ZEB][MAXR];
+  __shared__ int srcs[ZEB];
+  const int64_t n = n0 + blockIdx.x;
+  const int C = a.C, R = a.R;
+  const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
+  const int items = rows.nrows * C;
+  float* zn = Z + (int64_t)blockIdx.x * rows.nrows * J * C;
+  for (int base = 0; base < items; base += blockDim.x) {
+    const int item = base + threadIdx.x;
+    const bool valid = item < items;
+    const int r = valid ? item / C : 0, ch = valid ? item - r * C : 0;
+    const int c1 = rows.c1[r], c2 = rows.c2[r];
+    float acc[RH];
+#pragma unroll
+    for (int j = 0; j < RH; ++j) acc[j] = 0.f;
+    float accb = 0.f;
+    for (int eb = e0; eb < e1; eb += ZEB) {
+      const int ne = min(ZEB, e1 - eb);
+      __syncthreads();
+      for (int t = threadIdx.x; t < ne * RH; t += blockDim.x) hs[t / RH][t % RH] = h2[(int64_t)(eb + t / RH) * RH + t % RH];
+      if (threadIdx.x < ne) {
+        const int e = eb + threadIdx.x;
+        srcs[threadIdx.x] = a.src[e];
+        const float* y = a.edge_y + 12 * (int64_t)e;
+        npow_all(a.lmax, y[0], y[1], y[2], np[threadIdx.x]);
+      }
+      __syncthreads();
+      if (valid) {
+        for (int k = 0; k < ne; ++k) {
+          const float m = x[((int64_t)srcs[k] * R + c1) * C + ch] * np[k][c2];
+          const float4* h4 = reinterpret_cast<const float4*>(hs[k]);
+#pragma unroll
+          for (int j4 = 0; j4 < RH / 4; ++j4) {
+            const float4 h = h4[j4];
+            acc[4 * j4] = fmaf(h.x, m, acc[4 * j4]);
+            acc[4 * j4 + 1] = fmaf(h.y, m, acc[4 * j4 + 1]);
+            acc[4 * j4 + 2] = fmaf(h.z, m, acc[4 * j4 + 2]);
+            acc[4 * j4 + 3] = fmaf(h.w, m, acc[4 * j4 + 3]);
+          }
+          accb += m;
+        }
+      }
+    }
+    if (valid) {
+      float* zr = zn + (int64_t)r * J * C + ch;
+#pragma unroll
+      for (int j = 0; j < RH; ++j) zr[(int64_t)j * C] = acc[j];
+      zr[(int64_t)RH * C] = accb;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- conv2 backward
+// Block per edge (edges of the receiving nodes [n0, n0 + nc)); thread item (c1, a) over the rows
+// that read x1 component c1:
+//   dm   = sum_j dZ[n][r][j][a] h2'[j]
+//   dE/dx1[src][c1][a]      += sum_r dm * n^{(x)L2}[c2(r)]          (atomic: sources are shared)
+//   dE/dn^{(x)L2}[c2(r)]    += sum_a dm * x1[src][c1][a]
+//   dE/dh2'[j]              += dZ[n][r][j][a] * x1[src][c1][a] * n^{(x)L2}[c2(r)]
+__global__ void __launch_bounds__(256) conv2_bwd_kernel(Args a, Rows rows, const float* __restrict__ x,
+                                                        const float* __restrict__ h2, const float* __restrict__ dZ,
+                                                        int64_t e_begin, int64_t n0, float* __restrict__ gx,
+                                                        float* __restrict__ dh2, float* __restrict__ dnp) {
+  __shared__ __align__(16) float hs[J + 3];
+  __shared__ float np[MAXR];
+  __shared__ float sdn[MAXR];
+  __shared__ float red[8][RH];
+  const int64_t e = e_begin + blockIdx.x;
+  const int n = a.dst[e], s = a.src[e];
+  const int C = a.C, R = a.R;
+  if (threadIdx.x < RH) hs[threadIdx.x] = h2[e * RH + threadIdx.x];
+  if (threadIdx.x == 0) {
+    hs[RH] = 1.f;
+    const float* y = a.edge_y + 12 * e;
+    npow_all(a.lmax, y[0], y[1], y[2], np);
+  }
+  if (threadIdx.x < MAXR) sdn[threadIdx.x] = 0.f;
+  __syncthreads();
+  const float* dzn = dZ + (int64_t)(n - n0) * rows.nrows * J * C;
+  float acch[RH];
+#pragma unroll
+  for (int j = 0; j < RH; ++j) acch[j] = 0.f;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int items = R * C;
+  for (int base = 0; base < items; base += blockDim.x) {
+    const int item = base + threadIdx.x;
+    const bool valid = item < items;
+    const int c1 = valid ? item / C : 0, ch = valid ? item - c1 * C : 0;
+    const float xv = valid ? x[((int64_t)s * R + c1) * C + ch] : 0.f;
+    float gsum = 0.f;
+    // rows of this c1 (warp-uniform when C is a multiple of 32)
+    const int r0 = rows.c1off[c1], r1 = rows.c1off[c1 + 1];
+    for (int rr = r0; rr < r1; ++rr) {
+      const int r = rows.rlist[rr], c2 = rows.c2[r];
+      const float npv = np[c2];
+      const float m = xv * npv;
+      const float* dz = dzn + (int64_t)r * J * C + ch;
+      float dm = 0.f;
+      if (valid) {
+#pragma unroll
+        for (int j = 0; j < RH; ++j) {
+          const float v = dz[(int64_t)j * C];
+          dm = fmaf(v, hs[j], dm);
+          acch[j] = fmaf(v, m, acch[j]);
+        }
+        dm = fmaf(dz[(int64_t)RH * C], 1.f, dm);
+      }
+      gsum = fmaf(dm, npv, gsum);
+      const float t = warp_sum(dm * xv);
+      if (lane == 0) atomicAdd(&sdn[c2], t);
+    }
+    if (valid && gsum != 0.f) atomicAdd(gx + ((int64_t)s * R + c1) * C + ch, gsum);
+  }
+  // block reduction of dE/dh2
+#pragma unroll
+  for (int j = 0; j < RH; ++j) {
+    const float t = warp_sum(acch[j]);
+    if (lane == 0) red[warp][j] = t;
+  }
+  __syncthreads();
+  if (threadIdx.x < RH) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w][threadIdx.x];
+    dh2[e * RH + threadIdx.x] = t;
+  }
+  if (threadIdx.x < R) dnp[e * MAXR + threadIdx.x] += sdn[threadIdx.x];
+}
+
+// ---------------------------------------------------------------- edge gradient
+// g_e = dE/d|r| n + (I - n n^T) / |r| dE/dn,  dE/dn from dE/dn^{(x)L}; dE/d|r| in g_e[0] on entry.
+__global__ void edge_grad_kernel(int64_t E, int lmax, const float* __restrict__ ey, const float* __restrict__ dnp,
+                                 float* __restrict__ g) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= E) return;
+  const float* y = ey + 12 * e;
+  const float n[3] = {y[0], y[1], y[2]};
+  const float len = y[3];
+  float d[MAXR];
+  for (int q = 0; q < MAXR; ++q) d[q] = dnp[e * MAXR + q];
+  float dn[3];
+  npow_grad(lmax, n, d, dn);
+  const float dl = g[3 * e];
+  const float inv = 1.f / fmaxf(len, 1e-8f);
+  const float dot = dn[0] * n[0] + dn[1] * n[1] + dn[2] * n[2];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) g[3 * e + k] = dl * n[k] + (len > 1e-8f ? (dn[k] - dot * n[k]) : dn[k]) * inv;
+}
+
+// ---------------------------------------------------------------- readout
+// t_L[c'][m] = feats[c' / C][n][roff(L) + m][c' % C]; Gram over m < 3^L.
+struct RdArgs {
+  int64_t N;
+  int C, R, nint, S;
+  const float* feats[8];
+};
+
+__global__ void gram_pack_kernel(RdArgs a, int L, int64_t n0, int64_t nn, const int32_t* __restrict__ pairs,
+                                 int64_t npairs, float* __restrict__ Gp) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= nn * npairs) return;
+  const int64_t nl = idx / npairs, j = idx - nl * npairs;
+  const int64_t n = n0 + nl;
+  const int32_t pr = pairs[j];
+  const int cp = pr & 0xffff, dp = pr >> 16;
+  const int kc = cp / a.C, c = cp - kc * a.C, kd = dp / a.C, d = dp - kd * a.C;
+  const float* fc = a.feats[kc] + (n * a.R + roff(L)) * a.C + c;
+  const float* fd = a.feats[kd] + (n * a.R + roff(L)) * a.C + d;
+  float acc = 0.f;
+  for (int m = 0; m < pow3(L); ++m) acc = fmaf(fc[m * a.C], fd[m * a.C], acc);
+  Gp[idx] = acc;
+}
+
+// grads at t_L[c'][m] += 2 sum_d H[n][c'][d] t_L[d][m]
+__global__ void gram_apply_kernel(RdArgs a, GradList g, int L, int64_t n0, int64_t nn, const float* __restrict__ H) {
+  const int nC = a.C * a.nint;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= nn * nC) return;
+  const int64_t nl = idx / nC;
+  const int cp = (int)(idx - nl * nC);
+  const int64_t n = n0 + nl;
+  const int M = pow3(L);
+  const float* h = H + (nl * nC + cp) * (int64_t)nC;
+  float acc[27];
+  for (int m = 0; m < M; ++m) acc[m] = 0.f;
+  for (int d = 0; d < nC; ++d) {
+    const float hv = h[d];
+    const int kd = d / a.C, dd = d - kd * a.C;
+    const float* fd = a.feats[kd] + (n * a.R + roff(L)) * a.C + dd;
+    for (int m = 0; m < M; ++m) acc[m] = fmaf(hv, fd[m * a.C], acc[m]);
+  }
+  const int kc = cp / a.C, c = cp - kc * a.C;
+  float* gp = g.p[kc] + (n * a.R + roff(L)) * a.C + c;
+  for (int m = 0; m < M; ++m) gp[m * a.C] += 2.f * acc[m];
+}
+
+// MainNet input [layer k: L = 0..lmax: C] x nint | scalars^2 (S)
+__global__ void p5_fwd_kernel(RdArgs a, int lmax, const float* __restrict__ scal, float* __restrict__ p5) {
+  const int W = a.C * (lmax + 1);
+  const int D0 = a.nint * W + a.S;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= a.N * D0) return;
+  const int64_t n = idx / D0;
+  const int j = (int)(idx - n * D0);
+  float v;
+  if (j < a.nint * W) {
+    const int k = j / W, w = j - k * W, L = w / a.C, c = w - L * a.C;
+    const float* f = a.feats[k] + (n * a.R + roff(L)) * a.C + c;
+    float acc = 0.f;
+    for (int m = 0; m < pow3(L); ++m) acc = fmaf(f[m * a.C], f[m * a.C], acc);
+    v = acc * rsqrtf((float)pow3(L));
+  } else {
+    const float s = scal[n * a.S + (j - a.nint * W)];
+    v = s * s;
+  }
+  p5[idx] = v;
+}
+
+__global__ void p5_bwd_kernel(RdArgs a, GradList g, int lmax, const float* __restrict__ scal,
+                              const float* __restrict__ dp5, float* __restrict__ dscal) {
+  const int W = a.C * (lmax + 1);
+  const int D0 = a.nint * W + a.S;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= a.N * D0) return;
+  const int64_t n = idx / D0;
+  const int j = (int)(idx - n * D0);
+  const float d = dp5[idx];
+  if (j < a.nint * W) {
+    const int k = j / W, w = j - k * W, L = w / a.C, c = w - L * a.C;
+    const int64_t off = (n * a.R + roff(L)) * a.C + c;
+    const float sc = 2.f * rsqrtf((float)pow3(L)) * d;
+    for (int m = 0; m < pow3(L); ++m) g.p[k][off + m * a.C] = sc * a.feats[k][off + m * a.C];
+  } else {
+    const int o = j - a.nint * W;
+    dscal[n * a.S + o] = 2.f * scal[n * a.S + o] * d;
+  }
+}
+
+// per-graph sums of r (x) g (virial) or S (x) g (cell gradient), double atomics
+__global__ void edge_reduce_kernel(int64_t E, const float* __restrict__ ey, const float* __restrict__ shift,
+                                   const float* __restrict__ g, const int32_t* __restrict__ src,
+                                   const int32_t* __restrict__ batch, int use_shift, double* __restrict__ out) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= E) return;
+  const float* r = use_shift ? shift + 3 * e : ey + 12 * e + 9;
+  double* o = out + 9 * (int64_t)batch[src[e]];
+  for (int p = 0; p < 3; ++p)
+    for (int q = 0; q < 3; ++q) atomicAdd(o + 3 * p + q, (double)r[p] * (double)g[3 * e + q]);
+}
+
+__global__ void energy_reduce_kernel(int64_t N, int64_t nlocal, const float* __restrict__ ae,
+                                     const int32_t* __restrict__ batch, double* __restrict__ out) {
+  const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= nlocal || n >= N) return;
+  atomicAdd(out + batch[n], (double)ae[n]);
+}
+
+__global__ void to_float_kernel(const double* __restrict__ in, int64_t n, float* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = (float)in[i];
+}
+
+// ---------------------------------------------------------------- plan
+struct Plan {
+  int C, R, lmax, nint, S, nC, D0, nb, n_hidden, hidden[4];
+  int64_t N, E, B, npairs, chunk, gchunk, zstride;
+  Rows rows;
+  int32_t* dst;
+  float* edge_y;
+  float* h2;
+  float* feats[8];
+  float* zbuf;
+  float* scalars;
+  float* p5;
+  float* x0;
+  float* act_pre[4];
+  float* act_post[4];
+  double* acc_d;  // energy [4096] | virial [4096][9] | cell grad [4096][9]
+  float* grads[8];
+  float* dscalars;
+  float* dp5;
+  float* dxa;
+  float* dxb;
+  float* dh2;
+  float* dnp;
+  float* edge_grad;
+  float* gbuf;
+  int* err;
+};
+
+int validate(const fsc_sparse_config* cfg) {
+  FSC_REQUIRE(cfg != nullptr, "config is null");
+  if (cfg->lmax != 2 && cfg->lmax != 3) return fail(FSC_ERR_UNSUPPORTED, "sparse engine supports lmax 2 or 3");
+  if (cfg->channels != 32 && cfg->channels != 64 && cfg->channels != 128)
+    return fail(FSC_ERR_UNSUPPORTED, "sparse engine supports channels 32, 64 or 128");
+  if (cfg->num_interaction < 2 || cfg->num_interaction > 8) return fail(FSC_ERR_UNSUPPORTED, "num_interaction in [2, 8]");
+  if (cfg->number_of_basis < 1 || cfg->number_of_basis > 16) return fail(FSC_ERR_UNSUPPORTED, "number_of_basis in [1, 16]");
+  if (cfg->basis_kind != 0 && cfg->basis_kind != 1) return fail(FSC_ERR_UNSUPPORTED, "gaussian or bessel basis");
+  if (cfg->n_hidden < 1 || cfg->n_hidden > 4) return fail(FSC_ERR_UNSUPPORTED, "MainNet needs 1..4 hidden layers");
+  if (cfg->num_species < 1 || cfg->num_species > 128) return fail(FSC_ERR_UNSUPPORTED, "num_species in [1, 128]");
+  if (cfg->invariant_channels < 1) return fail(FSC_ERR_ARGUMENT, "invariant_channels must be >= 1");
+  if (cfg->channels * cfg->num_interaction > 65535) return fail(FSC_ERR_UNSUPPORTED, "too many channels");
+  return FSC_OK;
+}
+
+void layout(Plan& p, Arena& ar, const fsc_sparse_config* cfg, int64_t N, int64_t E) {
+  p.C = cfg->channels;
+  p.lmax = cfg->lmax;
+  p.R = roff(p.lmax + 1);
+  p.nint = cfg->num_interaction;
+  p.S = (p.nint - 1) * cfg->invariant_channels;
+  p.nC = p.C * p.nint;
+  p.D0 = p.nint * p.C * (p.lmax + 1) + p.S;
+  p.nb = cfg->number_of_basis;
+  p.n_hidden = cfg->n_hidden;
+  for (int k = 0; k < 4; ++k) p.hidden[k] = k < p.n_hidden ? cfg->hidden[k] : 0;
+  p.N = N;
+  p.E = E;
+  p.rows = make_rows(p.lmax);
+  p.zstride = (int64_t)p.rows.nrows * J * p.C;
+  p.chunk = std::max<int64_t>(1, std::min<int64_t>(std::max<int64_t>(N, 1), kZBudgetFloats / p.zstride));
+  p.npairs = (int64_t)p.nC * (p.nC + 1) / 2;
+  p.gchunk = std::max<int64_t>(1, std::min<int64_t>(N, kGramChunk));
+  int maxw = p.D0;
+  for (int k = 0; k < p.n_hidden; ++k) maxw = std::max(maxw, p.hidden[k]);
+  const int64_t fsz = N * p.R * p.C;
+  p.dst = ar.take<int32_t>(E);
+  p.edge_y = ar.take<float>(E * 12);
+  p.h2 = ar.take<float>((int64_t)p.nint * E * RH);
+  for (int k = 0; k < p.nint; ++k) p.feats[k] = ar.take<float>(fsz);
+  p.zbuf = ar.take<float>(p.chunk * p.zstride);
+  p.scalars = ar.take<float>(N * p.S);
+  p.p5 = ar.take<float>(N * p.D0);
+  p.x0 = ar.take<float>(N * p.D0);
+  for (int k = 0; k < p.n_hidden; ++k) {
+    p.act_pre[k] = ar.take<float>(N * p.hidden[k]);
+    p.act_post[k] = ar.take<float>(N * p.hidden[k]);
+  }
+  p.acc_d = ar.take<double>(kMaxGraphs * 19);
+  for (int k = 0; k < p.nint; ++k) p.grads[k] = ar.take<float>(fsz);
+  p.dscalars = ar.take<float>(N * p.S);
+  p.dp5 = ar.take<float>(N * p.D0);
+  p.dxa = ar.take<float>(N * maxw);
+  p.dxb = ar.take<float>(N * maxw);
+  p.dh2 = ar.take<float>((int64_t)p.nint * E * RH);
+  p.dnp = ar.take<float>(E * MAXR);
+  p.edge_grad = ar.take<float>(E * 3);
+  p.gbuf = ar.take<float>(p.gchunk * std::max<int64_t>(p.npairs, (int64_t)p.nC * p.nC));
+  p.err = ar.take<int>(64);
+}
+
+struct Ctx {
+  const fsc_sparse_config* cfg;
+  const fsc_sparse_weights* w;
+  const fsc_graph* g;
+  Plan p;
+  cudaStream_t st;
+};
+
+Args args(const Ctx& c) {
+  Args a{};
+  a.N = c.p.N;
+  a.E = c.p.E;
+  a.C = c.p.C;
+  a.R = c.p.R;
+  a.lmax = c.p.lmax;
+  a.S_species = c.cfg->num_species;
+  a.row_ptr = c.g->row_ptr;
+  a.src = c.g->src;
+  a.dst = c.p.dst;
+  a.species = c.g->species;
+  a.edge_y = c.p.edge_y;
+  return a;
+}
+
+RdArgs rd_args(const Plan& p) {
+  RdArgs r{};
+  r.N = p.N;
+  r.C = p.C;
+  r.R = p.R;
+  r.nint = p.nint;
+  r.S = p.S;
+  for (int k = 0; k < p.nint; ++k) r.feats[k] = p.feats[k];
+  return r;
+}
+
+RadialW radial(const fsc_sparse_weights* w) {
+  RadialW r{};
+  r.w1 = w->rad_w1;
+  r.b1 = w->rad_b1;
+  r.w2 = w->rad_w2;
+  r.b2 = w->rad_b2;
+  r.w3 = nullptr;
+  r.b3 = nullptr;
+  return r;
+}
+
+GemmArgs gemm(const float* A, int64_t a_gs, int64_t a_rs, const float* B, int64_t ldb, int b_trans, float* C,
+              int64_t c_gs, int64_t c_rs, int64_t G, int R, int K, int N) {
+  GemmArgs g{};
+  g.A = A; g.a_gs = a_gs; g.a_rs = a_rs;
+  g.B = B; g.ldb = ldb; g.b_trans = b_trans;
+  g.C = C; g.c_gs = c_gs; g.c_rs = c_rs;
+  g.G = G; g.R = R; g.K = K; g.N = N;
+  return g;
+}
+
+// offset (floats) of layer k's mix block of rank Lout
+int64_t mix_offset(const Plan& p, int k, int Lout) {
+  int64_t per_layer = 0;
+  for (int L = 0; L <= p.lmax; ++L) per_layer += (int64_t)p.rows.npl[L] * J * p.C * p.C;
+  int64_t off = (int64_t)(k - 1) * per_layer;
+  for (int L = 0; L < Lout; ++L) off += (int64_t)p.rows.npl[L] * J * p.C * p.C;
+  return off;
+}
+
+template <typename F>
+int by_cpl(int C, F f) {
+  if (C == 32) return f(std::integral_constant<int, 1>{});
+  if (C == 64) return f(std::integral_constant<int, 2>{});
+  return f(std::integral_constant<int, 4>{});
+}
+
+int forward(Ctx& c) {
+  Plan& p = c.p;
+  const fsc_graph* g = c.g;
+  const fsc_sparse_weights* w = c.w;
+  cudaStream_t st = c.st;
+  FSC_TRY(launch_edge_dst(g->row_ptr, p.dst, p.N, st));
+  if (p.E > 0) {
+    geom_kernel<<<(unsigned)ceil_div(p.E, 256), 256, 0, st>>>(p.E, g->pos, g->src, p.dst, g->batch, g->cell, g->shift,
+                                                             p.edge_y);
+    FSC_TRY(check_launch("sparse geom_kernel"));
+  }
+  RadialTcArgs ra{};
+  ra.E = p.E; ra.rad = radial(w); ra.nint = p.nint; ra.nb = p.nb; ra.basis_kind = c.cfg->basis_kind;
+  ra.rc = c.cfg->max_radius; ra.edge_y = p.edge_y; ra.err = p.err; ra.hout = p.h2;
+  FSC_TRY(launch_radial_fwd_tc(ra, st));
+  prof::mark("sparse_radial_forward", st);
+  Args a = args(c);
+  if (p.N > 0) {
+    FSC_TRY(by_cpl(p.C, [&](auto cpl) {
+      conv1_fwd_kernel<decltype(cpl)::value><<<(unsigned)ceil_div(p.N, 8), 256, 0, st>>>(a, w->pair_k, p.h2, p.feats[0]);
+      return check_launch("sparse conv1_fwd_kernel");
+    }));
+  }
+  prof::mark("sparse_conv1_forward", st);
+  const float avg = (float)std::max(1e-8, (double)p.E / (double)std::max<int64_t>(p.N, 1));
+  for (int k = 1; k < p.nint; ++k) {
+    for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
+      const int64_t nc = std::min(p.chunk, p.N - n0);
+      z_kernel<<<(unsigned)nc, 256, 0, st>>>(a, p.rows, p.feats[k - 1], p.h2 + (int64_t)k * p.E * RH, n0, p.zbuf);
+      FSC_TRY(check_launch("sparse z_kernel"));
+      for (int Lo = 0; Lo <= p.lmax; ++Lo) {
+        const int K = p.rows.npl[Lo] * J * p.C;
+        GemmArgs ga = gemm(p.zbuf + (int64_t)p.rows.zoff[Lo] * J * p.C, p.zstride, K, w->mix + mix_offset(p, k, Lo),
+                           p.C, 0, p.feats[k] + (n0 * p.R + roff(Lo)) * p.C, (int64_t)p.R * p.C, p.C, nc, pow3(Lo),
+                           K, p.C);
+        ga.alpha = 1.f / avg;
+        FSC_TRY(launch_gemm(ga, st));
+      }
+    }
+    prof::mark("sparse_conv2_forward", st);
+  }
+  // readout: bilinear invariants of the channel concatenation, 0e products, MainNet
+  RdArgs rd = rd_args(p);
+  if (cudaMemsetAsync(p.scalars, 0, sizeof(float) * p.N * p.S, st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset");
+  for (int L = 0; L <= p.lmax; ++L) {
+    const float* Wp = w->wread_p + (int64_t)L * p.S * p.npairs;
+    for (int64_t n0 = 0; n0 < p.N; n0 += p.gchunk) {
+      const int64_t nn = std::min(p.gchunk, p.N - n0);
+      gram_pack_kernel<<<(unsigned)ceil_div(nn * p.npairs, 256), 256, 0, st>>>(rd, L, n0, nn, w->pairs, p.npairs,
+                                                                               p.gbuf);
+      FSC_TRY(check_launch("sparse gram_pack_kernel"));
+      GemmArgs ga = gemm(p.gbuf, p.npairs, 0, Wp, p.npairs, 1, p.scalars + n0 * p.S, p.S, 0, nn, 1, (int)p.npairs, p.S);
+      ga.accumulate = 1;
+      FSC_TRY(launch_gemm(ga, st));
+    }
+  }
+  prof::mark("sparse_readout_gram_forward", st);
+  if (p.N > 0) {
+    p5_fwd_kernel<<<(unsigned)ceil_div(p.N * p.D0, 256), 256, 0, st>>>(rd, p.lmax, p.scalars, p.p5);
+    FSC_TRY(check_launch("sparse p5_fwd_kernel"));
+  }
+  FSC_TRY(launch_layernorm(p.p5, p.N, p.D0, w->mn_in_g, w->mn_in_b, 0, p.x0, st));
+  const float* xin = p.x0;
+  int din = p.D0;
+  for (int k = 0; k < p.n_hidden; ++k) {
+    GemmArgs ga = gemm(xin, din, 0, w->mn_w[k], din, 1, p.act_pre[k], p.hidden[k], 0, p.N, 1, din, p.hidden[k]);
+    ga.bias = w->mn_b[k];
+    FSC_TRY(launch_gemm(ga, st));
+    FSC_TRY(launch_layernorm(p.act_pre[k], p.N, p.hidden[k], w->mn_g[k], w->mn_beta[k], 1, p.act_post[k], st));
+    xin = p.act_post[k];
+    din = p.hidden[k];
+  }
+  prof::mark("sparse_readout_mlp_forward", st);
+  return FSC_OK;
+}
+
+int backward(Ctx& c) {
+  Plan& p = c.p;
+  const fsc_graph* g = c.g;
+  const fsc_sparse_weights* w = c.w;
+  cudaStream_t st = c.st;
+  const int H = p.hidden[p.n_hidden - 1];
+  FSC_TRY(launch_energy_seed(p.N, H, w->out_v, g->energy_weight, g->num_local, p.dxa, st));
+  float* dcur = p.dxa;
+  float* dnext = p.dxb;
+  for (int k = p.n_hidden - 1; k >= 0; --k) {
+    const int din = k == 0 ? p.D0 : p.hidden[k - 1];
+    FSC_TRY(launch_layernorm_backward(p.act_pre[k], dcur, p.N, p.hidden[k], w->mn_g[k], w->mn_beta[k], 1, dnext, st));
+    GemmArgs ga = gemm(dnext, p.hidden[k], 0, w->mn_w[k], din, 0, dcur, din, 0, p.N, 1, p.hidden[k], din);
+    FSC_TRY(launch_gemm(ga, st));
+  }
+  FSC_TRY(launch_layernorm_backward(p.p5, dcur, p.N, p.D0, w->mn_in_g, w->mn_in_b, 0, p.dp5, st));
+  RdArgs rd = rd_args(p);
+  GradList gl{};
+  for (int k = 0; k < p.nint; ++k) gl.p[k] = p.grads[k];
+  if (p.N > 0) {
+    p5_bwd_kernel<<<(unsigned)ceil_div(p.N * p.D0, 256), 256, 0, st>>>(rd, gl, p.lmax, p.scalars, p.dp5, p.dscalars);
+    FSC_TRY(check_launch("sparse p5_bwd_kernel"));
+  }
+  prof::mark("sparse_readout_mlp_backward", st);
+  for (int L = 0; L <= p.lmax; ++L) {
+    const float* Ws = w->wread_s + (int64_t)L * p.S * p.nC * p.nC;
+    for (int64_t n0 = 0; n0 < p.N; n0 += p.gchunk) {
+      const int64_t nn = std::min(p.gchunk, p.N - n0);
+      GemmArgs ga = gemm(p.dscalars + n0 * p.S, p.S, 0, Ws, (int64_t)p.nC * p.nC, 0, p.gbuf, (int64_t)p.nC * p.nC, 0,
+                         nn, 1, p.S, p.nC * p.nC);
+      FSC_TRY(launch_gemm(ga, st));
+      gram_apply_kernel<<<(unsigned)ceil_div(nn * p.nC, 128), 128, 0, st>>>(rd, gl, L, n0, nn, p.gbuf);
+      FSC_TRY(check_launch("sparse gram_apply_kernel"));
+    }
+  }
+  prof::mark("sparse_readout_gram_backward", st);
+  if (cudaMemsetAsync(p.dnp, 0, sizeof(float) * p.E * MAXR, st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset");
+  Args a = args(c);
+  const float avg = (float)std::max(1e-8, (double)p.E / (double)std::max<int64_t>(p.N, 1));
+  std::vector<int32_t> rp;
+  if (p.chunk < p.N) {  // chunk edge ranges need the row pointers on the host
+    rp.resize(p.N + 1);
+    if (cudaMemcpyAsync(rp.data(), g->row_ptr, sizeof(int32_t) * (p.N + 1), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+      return fail(FSC_ERR_CUDA, "row_ptr readback");
+  }
+  for (int k = p.nint - 1; k >= 1; --k) {
+    for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
+      const int64_t nc = std::min(p.chunk, p.N - n0);
+      for (int Lo = 0; Lo <= p.lmax; ++Lo) {
+        const int K = p.rows.npl[Lo] * J * p.C;
+        GemmArgs ga = gemm(p.grads[k] + (n0 * p.R + roff(Lo)) * p.C, (int64_t)p.R * p.C, p.C,
+                           w->mixT + mix_offset(p, k, Lo), K, 0, p.zbuf + (int64_t)p.rows.zoff[Lo] * J * p.C,
+                           p.zstride, K, nc, pow3(Lo), p.C, K);
+        ga.alpha = 1.f / avg;
+        FSC_TRY(launch_gemm(ga, st));
+      }
+      const int64_t e_lo = rp.empty() ? 0 : rp[n0], e_hi = rp.empty() ? p.E : rp[n0 + nc];
+      if (e_hi > e_lo) {
+        conv2_bwd_kernel<<<(unsigned)(e_hi - e_lo), 256, 0, st>>>(a, p.rows, p.feats[k - 1],
+                                                                   p.h2 + (int64_t)k * p.E * RH, p.zbuf, e_lo, n0,
+                                                                   p.grads[k - 1], p.dh2 + (int64_t)k * p.E * RH, p.dnp);
+        FSC_TRY(check_launch("sparse conv2_bwd_kernel"));
+      }
+    }
+    prof::mark("sparse_conv2_backward", st);
+  }
+  if (p.N > 0) {
+    FSC_TRY(by_cpl(p.C, [&](auto cpl) {
+      conv1_bwd_kernel<decltype(cpl)::value><<<(unsigned)ceil_div(p.N, 8), 256, 0, st>>>(a, w->pair_k, p.h2, p.grads[0],
+                                                                                         p.dh2, p.dnp);
+      return check_launch("sparse conv1_bwd_kernel");
+    }));
+  }
+  prof::mark("sparse_conv1_backward", st);
+  return FSC_OK;
+}
+
+int prepare(Ctx& c, void* workspace, size_t bytes) {
+  const fsc_graph* g = c.g;
+  FSC_TRY(validate(c.cfg));
+  FSC_REQUIRE(c.w && g, "weights/graph is null");
+  FSC_REQUIRE(g->num_atoms >= 0 && g->num_edges >= 0 && g->num_graphs >= 1, "bad graph sizes");
+  FSC_REQUIRE(g->num_atoms < (int64_t)INT32_MAX && g->num_edges < (int64_t)INT32_MAX, "graph too large");
+  FSC_REQUIRE(g->num_graphs <= kMaxGraphs, "too many graphs per call (max 4096)");
+  FSC_REQUIRE(g->num_local >= 0 && g->num_local <= g->num_atoms, "num_local out of range");
+  Arena ar(workspace, bytes);
+  layout(c.p, ar, c.cfg, g->num_atoms, g->num_edges);
+  if (!ar.ok() || workspace == nullptr)
+    return fail(FSC_ERR_CAPACITY, "workspace too small: need " + std::to_string(ar.off) + " bytes");
+  c.p.B = g->num_graphs;
+  return FSC_OK;
+}
+
+int run_forward(Ctx& c, float* energy, float* atom_energy) {
+  Plan& p = c.p;
+  if (cudaMemsetAsync(p.acc_d, 0, sizeof(double) * kMaxGraphs * 19, c.st) != cudaSuccess ||
+      cudaMemsetAsync(p.err, 0, sizeof(int) * 64, c.st) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "memset accumulators");
+  FSC_TRY(forward(c));
+  const int H = p.hidden[p.n_hidden - 1];
+  float* ebuf = atom_energy ? atom_energy : p.dxb;
+  FSC_TRY(launch_energy(p.act_post[p.n_hidden - 1], p.N, H, c.w->out_v, c.w->out_c0, c.g->batch, c.g->num_local, ebuf,
+                        nullptr, c.st));
+  if (p.N > 0) {
+    energy_reduce_kernel<<<(unsigned)ceil_div(p.N, 256), 256, 0, c.st>>>(p.N, c.g->num_local, ebuf, c.g->batch, p.acc_d);
+    FSC_TRY(check_launch("sparse energy_reduce_kernel"));
+  }
+  if (energy) {
+    to_float_kernel<<<(unsigned)ceil_div(p.B, 256), 256, 0, c.st>>>(p.acc_d, p.B, energy);
+    FSC_TRY(check_launch("sparse to_float_kernel"));
+  }
+  return FSC_OK;
+}
+
+int run_backward(Ctx& c, fsc_ictd_outputs* out) {
+  Plan& p = c.p;
+  const fsc_graph* g = c.g;
+  FSC_TRY(backward(c));
+  float* eg = out->edge_grad ? out->edge_grad : p.edge_grad;
+  RadialTcArgs ra{};
+  ra.E = p.E; ra.rad = radial(c.w); ra.nint = p.nint; ra.nb = p.nb; ra.basis_kind = c.cfg->basis_kind;
+  ra.rc = c.cfg->max_radius; ra.edge_y = p.edge_y; ra.err = p.err; ra.edge_grad = eg; ra.hout_grad = p.dh2;
+  FSC_TRY(launch_radial_bwd_tc(ra, c.st));
+  if (p.E > 0) {
+    edge_grad_kernel<<<(unsigned)ceil_div(p.E, 256), 256, 0, c.st>>>(p.E, p.lmax, p.edge_y, p.dnp, eg);
+    FSC_TRY(check_launch("sparse edge_grad_kernel"));
+  }
+  prof::mark("sparse_edge_backward", c.st);
+  if (out->forces) FSC_TRY(launch_forces(g->row_ptr, g->tr_ptr, g->tr_eid, eg, out->forces, p.N, c.st));
+  double* vir = p.acc_d + kMaxGraphs;
+  double* cg = p.acc_d + 10 * kMaxGraphs;
+  if (out->virial) {
+    if (cudaMemsetAsync(vir, 0, sizeof(double) * 9 * kMaxGraphs, c.st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset");
+    if (p.E > 0)
+      edge_reduce_kernel<<<(unsigned)ceil_div(p.E, 256), 256, 0, c.st>>>(p.E, p.edge_y, g->shift, eg, g->src, g->batch,
+                                                                        0, vir);
+    to_float_kernel<<<(unsigned)ceil_div(9 * p.B, 256), 256, 0, c.st>>>(vir, 9 * p.B, out->virial);
+    FSC_TRY(check_launch("sparse virial"));
+  }
+  if (out->cell_grad) {
+    if (cudaMemsetAsync(cg, 0, sizeof(double) * 9 * kMaxGraphs, c.st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset");
+    if (p.E > 0)
+      edge_reduce_kernel<<<(unsigned)ceil_div(p.E, 256), 256, 0, c.st>>>(p.E, p.edge_y, g->shift, eg, g->src, g->batch,
+                                                                        1, cg);
+    to_float_kernel<<<(unsigned)ceil_div(9 * p.B, 256), 256, 0, c.st>>>(cg, 9 * p.B, out->cell_grad);
+    FSC_TRY(check_launch("sparse cell grad"));
+  }
+  prof::mark("sparse_forces_virial", c.st);
+  return FSC_OK;
+}
+
+}  // namespace sp
+}  // namespace fsc
+
+using namespace fsc;
+
+extern "C" {
+
+size_t fsc_sparse_workspace_bytes(const fsc_sparse_config* cfg, int64_t num_atoms, int64_t num_edges) {
+  if (!cfg || sp::validate(cfg) != FSC_OK) return 0;
+  sp::Plan p{};
+  Arena ar(nullptr, 0);
+  sp::layout(p, ar, cfg, num_atoms, num_edges);
+  return ar.off;
+}
+
+int fsc_sparse_forward(const fsc_sparse_config* cfg, const fsc_sparse_weights* w, const fsc_graph* g, float* energy,
+                       float* atom_energy, void* workspace, size_t workspace_bytes, void* stream) {
+  sp::Ctx c{cfg, w, g, sp::Plan{}, as_stream(stream)};
+  FSC_TRY(sp::prepare(c, workspace, workspace_bytes));
+  return sp::run_forward(c, energy, atom_energy);
+}
+
+int fsc_sparse_backward(const fsc_sparse_config* cfg, const fsc_sparse_weights* w, const fsc_graph* g,
+                        fsc_ictd_outputs* out, void* workspace, size_t workspace_bytes, void* stream) {
+  FSC_REQUIRE(out != nullptr, "outputs required");
+  sp::Ctx c{cfg, w, g, sp::Plan{}, as_stream(stream)};
+  FSC_TRY(sp::prepare(c, workspace, workspace_bytes));
+  return sp::run_backward(c, out);
+}
+
+int fsc_sparse_status(const fsc_sparse_config* cfg, int64_t num_atoms, int64_t num_edges, void* workspace, void* stream,
+                      int* status_host) {
+  FSC_REQUIRE(status_host && workspace, "status output and workspace required");
+  FSC_TRY(sp::validate(cfg));
+  sp::Plan p{};
+  Arena ar(workspace, (size_t)-1);
+  sp::layout(p, ar, cfg, num_atoms, num_edges);
+  cudaStream_t st = as_stream(stream);
+  if (cudaMemcpyAsync(status_host, p.err, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "status readback");
+  return FSC_OK;
+}
+
+}  // extern "C"

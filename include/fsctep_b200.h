@@ -310,6 +310,65 @@ int fsc_ictd_energy(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const
                     float* energy, float* atom_energy, void* workspace, size_t workspace_bytes,
                     void* stream);
 
+/* ---- pure-cartesian-sparse model ------------------------------------------------
+ * PureCartesianSparseTransformerLayer (models/pure_cartesian_sparse_layers.py:459-855) with
+ * max_rank_other = 1, k_policy = "k0", no epsilon paths: node features are true Cartesian
+ * tensors of rank L <= lmax (3^L components per channel; the pseudotensor half is identically
+ * zero), every tensor-product path (L1, L2 -> L1 + L2, min(L1, L2) <= 1) is an outer product,
+ * and the per-edge channel-mixing weights come from the radial MLP (fc.4 of each layer).
+ * The engine never forms those per-edge weights: conv1 uses per-species-pair tables, conv2
+ * aggregates h2 (x) message per receiving node and applies fc.4 as one GEMM.
+ * Same graph (fsc_graph) and outputs (fsc_ictd_outputs) as the ictd engine; field unused. */
+typedef struct {
+  int32_t channels;          /* C: 32, 64 or 128                                  */
+  int32_t lmax;              /* 2 or 3                                            */
+  int32_t num_interaction;   /* 2..8                                              */
+  int32_t number_of_basis;   /* <= 16                                             */
+  int32_t basis_kind;        /* 0 = gaussian, 1 = bessel                          */
+  float max_radius;
+  int32_t num_species;       /* max_atomvalue                                     */
+  int32_t invariant_channels;
+  int32_t n_hidden;
+  int32_t hidden[4];
+  int32_t n_out;             /* 17                                                */
+} fsc_sparse_config;
+
+/* Packed fp32 device weights (host derives them from the reference state_dict):
+ *   R = sum_{L<=lmax} 3^L components, P paths in the reference order, J = 65 (64 hidden + 1). */
+typedef struct {
+  const float* rad_w1;   /* [nint][64][nb]  e3_conv_layers.k.fc.0.weight (k = 0 is e3_conv_emb.fc) */
+  const float* rad_b1;   /* [nint][64]                                                         */
+  const float* rad_w2;   /* [nint][64][64]  fc.2                                               */
+  const float* rad_b2;   /* [nint][64]                                                         */
+  /* conv1, paths (L, 0, L): K[ss][sd][L][j][c] = sum_{a,b} W_fc4[(p_L*C + c)*64 + a*8 + b][j] ai[ss][a] ai[sd][b]
+   * (j = 64: the fc.4 bias), ai = atom_mlp(atom_embedding) per species                         */
+  const float* pair_k;   /* [S][S][lmax+1][J][C]                                               */
+  /* conv2 layer k (k = 1..nint-1), per output rank Lout, the paths with that Lout in order
+   * (rank q): mix[k-1][Lout][(q, j, a)][c] = W_fc4[(p_q*C + c)*C + a][j] (j = 64: bias), and
+   * mixT[k-1][Lout][c][(q, j, a)] its transpose.                                               */
+  const float* mix;
+  const float* mixT;
+  const float* wread_p;  /* [lmax+1][S][npairs] product_3.W.L symmetrised, packed, / sqrt(3^L)  */
+  const float* wread_s;  /* [lmax+1][S][nC][nC] product_3.W.L symmetrised / sqrt(3^L)           */
+  const int32_t* pairs;  /* [npairs] (c | d << 16), c <= d                                        */
+  const float* mn_in_g;
+  const float* mn_in_b;
+  const float* mn_w[4];
+  const float* mn_b[4];
+  const float* mn_g[4];
+  const float* mn_beta[4];
+  const float* out_v;
+  float out_c0;
+} fsc_sparse_weights;
+
+size_t fsc_sparse_workspace_bytes(const fsc_sparse_config* cfg, int64_t num_atoms, int64_t num_edges);
+int fsc_sparse_forward(const fsc_sparse_config* cfg, const fsc_sparse_weights* w, const fsc_graph* g,
+                       float* energy, float* atom_energy, void* workspace, size_t workspace_bytes, void* stream);
+int fsc_sparse_backward(const fsc_sparse_config* cfg, const fsc_sparse_weights* w, const fsc_graph* g,
+                        fsc_ictd_outputs* out, void* workspace, size_t workspace_bytes, void* stream);
+int fsc_sparse_status(const fsc_sparse_config* cfg, int64_t num_atoms, int64_t num_edges, void* workspace,
+                      void* stream, int* status_host);
+
 /* ---- stage timing ------------------------------------------------------
  * When enabled, the engine records a CUDA event after each stage on its stream;
  * fsc_profile_read waits for the last one and returns per-stage milliseconds (stage
