@@ -322,6 +322,138 @@ class PureCartesianICTDO3TransformerLayer(nn.Module):
         return e, eng.heads()
 
 
+class _SparseConv1(nn.Module):
+    def __init__(self, cfg, P):
+        super().__init__()
+        self.atom_embedding = nn.Embedding(cfg.max_atomvalue, cfg.embedding_dim)
+        self.atom_mlp = nn.Sequential(nn.Linear(cfg.embedding_dim, 64), nn.SiLU(), nn.Linear(64, cfg.output_size))
+        self.fc = _radial_mlp(cfg.number_of_basis, P * cfg.channels * cfg.output_size * cfg.output_size)
+
+
+class _SparseConv2(nn.Module):
+    def __init__(self, cfg, P):
+        super().__init__()
+        self.fc = _radial_mlp(cfg.number_of_basis, P * cfg.channels * cfg.channels)
+
+
+class _Bilinear(nn.Module):
+    def __init__(self, channels, out_channels, lmax):
+        super().__init__()
+        self.W = nn.ParameterList([nn.Parameter(torch.randn(out_channels, channels, channels) * 0.02)
+                                   for _ in range(lmax + 1)])
+
+
+class _SparseEnergy(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, pos, cell, owner, graph, species, batch):
+        eng = owner._engine
+        _, atom_e = eng.forward(pos, species, batch, cell, graph)
+        ctx.owner, ctx.graph, ctx.species, ctx.batch = owner, graph, species, batch
+        ctx.generation = owner._bump()
+        ctx.save_for_backward(pos, cell)
+        ctx.pos_dtype, ctx.cell_dtype = pos.dtype, cell.dtype
+        return atom_e.view(-1, 1).to(pos.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_e):
+        pos, cell = ctx.saved_tensors
+        owner = ctx.owner
+        eng = owner._engine
+        if owner._generation != ctx.generation:
+            eng.forward(pos, ctx.species, ctx.batch, cell, ctx.graph)
+            owner._generation = ctx.generation
+        out = eng.backward(energy_weight=grad_e.reshape(-1), want_virial=False,
+                           want_cell_grad=ctx.needs_input_grad[1])
+        gpos = (-out["forces"]).to(ctx.pos_dtype) if ctx.needs_input_grad[0] else None
+        gcell = out["cell_grad"].to(ctx.cell_dtype).reshape(cell.shape) if ctx.needs_input_grad[1] else None
+        return gpos, gcell, None, None, None, None
+
+
+class PureCartesianSparseTransformerLayer(nn.Module):
+    """Drop-in for ``PureCartesianSparseTransformerLayer`` (``--tensor-product-mode
+    pure-cartesian-sparse``, ``models/pure_cartesian_sparse_layers.py:459-855``).
+
+    Same constructor, parameter names (``e3_conv_emb`` is ``e3_conv_layers[0]``, as in the
+    reference) and forward signature; per-atom energy (N, 1) differentiable in ``pos`` and
+    ``cell`` through the native reverse pass.  Covered: lmax 2 or 3, channels 32/64/128,
+    max_rank_other 1, k_policy "k0", no external tensors / heads / long-range / fidelity."""
+
+    def __init__(self, max_embed_radius: float, main_max_radius: float, main_number_of_basis: int,
+                 hidden_dim_conv: int, hidden_dim_sh=None, hidden_dim=None, channel_in2: int = 32,
+                 embedding_dim: int = 16, max_atomvalue: int = 10, output_size: int = 8, invariant_channels: int = 32,
+                 embed_size=None, main_hidden_sizes3=None, num_layers: int = 1, num_interaction: int = 2, device=None,
+                 function_type_main: str = "gaussian", lmax: int = 2, max_rank_other: int = 1, k_policy: str = "k0",
+                 long_range_mode: str = "none", feature_spectral_mode: str = "none", physical_tensor_outputs=None,
+                 external_tensor_rank=None, external_tensor_specs=None, num_fidelity_levels: int = 0, **unused):
+        super().__init__()
+        from fsctep_b200.sparse import SparseConfig, sparse_paths
+
+        if embed_size is None:
+            embed_size = [128, 128, 128]
+        unsupported = []
+        if int(max_rank_other) != 1 or str(k_policy) != "k0":
+            unsupported.append(f"max_rank_other={max_rank_other}, k_policy={k_policy!r}")
+        if int(lmax) not in (2, 3):
+            unsupported.append(f"lmax={lmax}")
+        if int(hidden_dim_conv) not in (32, 64, 128):
+            unsupported.append(f"channels={hidden_dim_conv}")
+        if physical_tensor_outputs or external_tensor_rank is not None or external_tensor_specs or num_fidelity_levels:
+            unsupported.append("physical-tensor heads / external tensors / multi-fidelity")
+        if long_range_mode != "none" or feature_spectral_mode != "none":
+            unsupported.append("long-range / spectral modules")
+        if unsupported:
+            raise NotImplementedError("fsctep_b200 pure-cartesian-sparse does not cover: " + ", ".join(unsupported))
+        if int(num_interaction) < 2:
+            raise ValueError(f"num_interaction must be >= 2, got {num_interaction}")
+        self.cfg = SparseConfig(channels=int(hidden_dim_conv), lmax=int(lmax), num_interaction=int(num_interaction),
+                                number_of_basis=int(main_number_of_basis), max_radius=float(max_embed_radius),
+                                function_type=str(function_type_main), output_size=int(output_size),
+                                embedding_dim=int(embedding_dim), max_atomvalue=int(max_atomvalue),
+                                invariant_channels=int(invariant_channels), embed_size=tuple(embed_size))
+        self.cfg.native()
+        C, nint, L = self.cfg.channels, self.cfg.num_interaction, self.cfg.lmax
+        P = len(sparse_paths(L))
+        self.channels, self.num_interaction, self.Lmax = C, nint, L
+        self.e3_conv_layers = nn.ModuleList([_SparseConv1(self.cfg, P)] +
+                                            [_SparseConv2(self.cfg, P) for _ in range(1, nint)])
+        self.e3_conv_emb = self.e3_conv_layers[0]
+        S = (nint - 1) * int(invariant_channels)
+        self.product_3 = _Bilinear(C * nint, S, L)
+        self.proj_total = _MainNet(nint * C * (L + 1) + S, embed_size, 17)
+        self.weighted_sum = _WeightedSum(17)
+        self._engine = None
+        self._engine_key = None
+        self._generation = 0
+
+    _bump = PureCartesianICTDTransformerLayer._bump
+
+    def _ensure_engine(self, device):
+        from fsctep_b200.sparse import SparseEngine
+
+        key = (str(device),) + tuple((p.data_ptr(), p._version) for p in self.parameters())
+        if self._engine is None or self._engine_key != key:
+            self._engine = SparseEngine({k: v.detach() for k, v in self.state_dict().items()}, self.cfg, device)
+            self._engine_key = key
+        return self._engine
+
+    def forward(self, pos, A, batch, edge_src, edge_dst, edge_shifts, cell, *, precomputed_edge_vec=None,
+                external_tensor=None, fidelity_ids=None, return_physical_tensors: bool = False,
+                return_reciprocal_source: bool = False, **_unused):
+        if precomputed_edge_vec is not None or external_tensor is not None or fidelity_ids is not None \
+                or return_physical_tensors or return_reciprocal_source:
+            raise NotImplementedError("fsctep_b200 pure-cartesian-sparse forward covers (pos, A, batch, edges, cell)")
+        if not pos.is_cuda:
+            raise RuntimeError("fsctep_b200 runs on CUDA devices only (no CPU path)")
+        n = pos.shape[0]
+        species = A.long()
+        if n and int(species.max().item()) >= self.cfg.max_atomvalue:
+            raise IndexError("atomic number out of range of atom_embedding (max_atomvalue)")
+        cell = cell.reshape(-1, 3, 3)
+        self._ensure_engine(pos.device)
+        graph = GraphCSR.from_edges(edge_src.long(), edge_dst.long(), edge_shifts, n)
+        return _SparseEnergy.apply(pos, cell, self, graph, species, batch)
+
+
 def reference_state_dict_shapes(cfg: ICTDConfig) -> Dict[str, tuple]:
     """Shapes of the reference state_dict for a config (for seeded synthetic weights)."""
     with torch.device("meta"):

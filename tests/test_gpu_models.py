@@ -80,3 +80,23 @@ def test_o3_module_matches_reference(tag):
     assert U.rel_max(-g.cpu().numpy(), c["ref64_forces"]) <= U.F_RTOL
     assert U.rel_max(phys["dipole"][1].cpu().numpy(), c["ref64_dipole"]) <= 1e-5
     assert U.rel_max(phys["polarizability"][2].cpu().numpy(), c["ref64_polar2"]) <= 1e-5
+
+
+@pytest.mark.parametrize("tag", ["a", "b"])
+def test_sparse_module_matches_reference(tag):
+    from test_models_cpu import _sparse_module
+
+    cfg, sd, c = golden_io.sparse_case(tag)
+    m = _sparse_module(cfg, device="cpu")
+    m.load_state_dict({k: v.float() for k, v in sd.items()})
+    m = m.cuda()
+    dev = torch.device("cuda")
+    pos = torch.tensor(c["pos"], device=dev, dtype=torch.float32).requires_grad_(True)
+    b = torch.tensor(c["batch"], device=dev)
+    e = m(pos, torch.tensor(c["Z"], device=dev), b, torch.tensor(c["edge_src"], device=dev),
+          torch.tensor(c["edge_dst"], device=dev), torch.tensor(c["edge_shifts"], device=dev).float(),
+          torch.tensor(c["cell"], device=dev).float())
+    (g,) = torch.autograd.grad(e.sum(), [pos])
+    E = e.sum().item()
+    assert abs(E - c["ref64_energy"].sum()) <= U.E_RTOL * abs(c["ref64_energy"].sum())
+    assert U.rel_max(-g.cpu().numpy(), c["ref64_forces"]) <= U.F_RTOL

@@ -66,3 +66,23 @@ def test_o3_module_rejects_uncovered_options():
         PureCartesianICTDO3TransformerLayer(5.0, 5.0, 8, 32, o3_irrep_preset="full")
     with pytest.raises(NotImplementedError):
         PureCartesianICTDO3TransformerLayer(5.0, 5.0, 8, 32, external_tensor_rank=2)
+
+
+def _sparse_module(cfg, device="meta"):
+    from fsctep_b200.models import PureCartesianSparseTransformerLayer
+
+    with torch.device(device):
+        return PureCartesianSparseTransformerLayer(
+            max_embed_radius=float(cfg["max_radius"]), main_max_radius=float(cfg["max_radius"]),
+            main_number_of_basis=int(cfg["number_of_basis"]), hidden_dim_conv=int(cfg["channels"]),
+            hidden_dim_sh=32, hidden_dim=64, lmax=int(cfg["lmax"]), num_interaction=int(cfg["num_interaction"]),
+            function_type_main=str(cfg["function_type"]), max_atomvalue=int(cfg["max_atomvalue"]))
+
+
+@pytest.mark.parametrize("tag", ["a", "b"])
+def test_sparse_module_state_dict_matches_reference(tag):
+    z = golden_io.load(f"sparse_{tag}.npz")
+    ref = {k[len("sdshape/"):]: tuple(int(x) for x in z[k]) for k in z.files if k.startswith("sdshape/")}
+    cfg = {k[4:]: z[k].item() for k in z.files if k.startswith("cfg_")}
+    mine = {k: tuple(v.shape) for k, v in _sparse_module(cfg).state_dict().items()}
+    assert mine == ref
