@@ -13,8 +13,8 @@
 //           Z_p[n][comp][j][a] = sum_{e -> n} h2'_e[j] message_p[e][comp][a],  h2' = [h2, 1]
 //   (one per-node aggregation kernel + one GEMM per Lout); conv1 folds fc.4 and the atom
 //   features of both ends into per-species-pair tables.  The reverse pass mirrors it: a GEMM
-//   gives dZ, one kernel per edge yields dE/dh2', dE/dn^{(x)L} and the feature gradient of the
-//   source, and the radial MLP backward (radial_tc.cu) turns dE/dh2 into dE/d|r|.
+//   gives dZ, two kernels per receiving node yield dE/dh2', dE/dn^{(x)L} and the feature gradient
+//   of the sources, and the radial MLP backward (radial_tc.cu) turns dE/dh2 into dE/d|r|.
 #include <algorithm>
 #include <cmath>
 #include <string>
@@ -351,79 +351,154 @@ __global__ void __launch_bounds__(256) z_kernel(Args a, Rows rows, const float* 
 }
 
 // ---------------------------------------------------------------- conv2 backward
-// Block per edge (edges of the receiving nodes [n0, n0 + nc)); thread item (c1, a) over the rows
-// that read x1 component c1:
-//   dm   = sum_j dZ[n][r][j][a] h2'[j]
-//   dE/dx1[src][c1][a]      += sum_r dm * n^{(x)L2}[c2(r)]          (atomic: sources are shared)
-//   dE/dn^{(x)L2}[c2(r)]    += sum_a dm * x1[src][c1][a]
-//   dE/dh2'[j]              += dZ[n][r][j][a] * x1[src][c1][a] * n^{(x)L2}[c2(r)]
-__global__ void __launch_bounds__(256) conv2_bwd_kernel(Args a, Rows rows, const float* __restrict__ x,
-                                                        const float* __restrict__ h2, const float* __restrict__ dZ,
-                                                        int64_t e_begin, int64_t n0, float* __restrict__ gx,
-                                                        float* __restrict__ dh2, float* __restrict__ dnp) {
-  __shared__ __align__(16) float hs[J + 3];
-  __shared__ float np[MAXR];
-  __shared__ float sdn[MAXR];
-  __shared__ float red[8][RH];
-  const int64_t e = e_begin + blockIdx.x;
-  const int n = a.dst[e], s = a.src[e];
+// Both kernels take one receiving node per block and read its dZ block once.
+// dm_kernel: thread = column (row r, channel a) holding dZ[n][r][:][a] in registers; per edge
+//   dm = sum_j dZ[n][r][j][a] h2'_e[j]
+//   dE/dx1[src][c1(r)][a]   += dm * n^{(x)L2}[c2(r)]     (atomic: sources are shared)
+//   dE/dn^{(x)L2}[c2(r)]    += sum_a dm * x1[src][c1(r)][a]
+__global__ void __launch_bounds__(256) bwd_dm_kernel(Args a, Rows rows, const float* __restrict__ x,
+                                                     const float* __restrict__ h2, const float* __restrict__ dZ,
+                                                     int64_t n0, float* __restrict__ gx, float* __restrict__ dnp) {
+  __shared__ __align__(16) float hs[ZEB][RH];
+  __shared__ float np[ZEB][MAXR];
+  __shared__ float sdn[ZEB][MAXR];
+  __shared__ int srcs[ZEB];
+  const int64_t n = n0 + blockIdx.x;
   const int C = a.C, R = a.R;
-  if (threadIdx.x < RH) hs[threadIdx.x] = h2[e * RH + threadIdx.x];
-  if (threadIdx.x == 0) {
-    hs[RH] = 1.f;
-    const float* y = a.edge_y + 12 * e;
-    npow_all(a.lmax, y[0], y[1], y[2], np);
-  }
-  if (threadIdx.x < MAXR) sdn[threadIdx.x] = 0.f;
-  __syncthreads();
-  const float* dzn = dZ + (int64_t)(n - n0) * rows.nrows * J * C;
-  float acch[RH];
+  const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
+  const int cols = rows.nrows * C;
+  const int lane = threadIdx.x & 31;
+  const float* dzn = dZ + (int64_t)blockIdx.x * rows.nrows * J * C;
+  for (int base = 0; base < cols; base += blockDim.x) {
+    const int col = base + threadIdx.x;
+    const bool valid = col < cols;  // warp-uniform: cols and blockDim are multiples of 32
+    const int r = valid ? col / C : 0, ch = valid ? col - r * C : 0;
+    const int c1 = rows.c1[r], c2 = rows.c2[r];
+    float dz[RH];
+    float dzb = 0.f;
+    if (valid) {
+      const float* zc = dzn + (int64_t)r * J * C + ch;
 #pragma unroll
-  for (int j = 0; j < RH; ++j) acch[j] = 0.f;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int items = R * C;
-  for (int base = 0; base < items; base += blockDim.x) {
-    const int item = base + threadIdx.x;
-    const bool valid = item < items;
-    const int c1 = valid ? item / C : 0, ch = valid ? item - c1 * C : 0;
-    const float xv = valid ? x[((int64_t)s * R + c1) * C + ch] : 0.f;
-    float gsum = 0.f;
-    // rows of this c1 (warp-uniform when C is a multiple of 32)
-    const int r0 = rows.c1off[c1], r1 = rows.c1off[c1 + 1];
-    for (int rr = r0; rr < r1; ++rr) {
-      const int r = rows.rlist[rr], c2 = rows.c2[r];
-      const float npv = np[c2];
-      const float m = xv * npv;
-      const float* dz = dzn + (int64_t)r * J * C + ch;
-      float dm = 0.f;
-      if (valid) {
+      for (int j = 0; j < RH; ++j) dz[j] = zc[(int64_t)j * C];
+      dzb = zc[(int64_t)RH * C];
+    } else {
 #pragma unroll
-        for (int j = 0; j < RH; ++j) {
-          const float v = dz[(int64_t)j * C];
-          dm = fmaf(v, hs[j], dm);
-          acch[j] = fmaf(v, m, acch[j]);
-        }
-        dm = fmaf(dz[(int64_t)RH * C], 1.f, dm);
-      }
-      gsum = fmaf(dm, npv, gsum);
-      const float t = warp_sum(dm * xv);
-      if (lane == 0) atomicAdd(&sdn[c2], t);
+      for (int j = 0; j < RH; ++j) dz[j] = 0.f;
     }
-    if (valid && gsum != 0.f) atomicAdd(gx + ((int64_t)s * R + c1) * C + ch, gsum);
-  }
-  // block reduction of dE/dh2
+    for (int eb = e0; eb < e1; eb += ZEB) {
+      const int ne = min(ZEB, e1 - eb);
+      __syncthreads();
+      for (int t = threadIdx.x; t < ne * RH; t += blockDim.x) hs[t / RH][t % RH] = h2[(int64_t)(eb + t / RH) * RH + t % RH];
+      for (int t = threadIdx.x; t < ZEB * MAXR; t += blockDim.x) sdn[t / MAXR][t % MAXR] = 0.f;
+      if (threadIdx.x < ne) {
+        const int e = eb + threadIdx.x;
+        srcs[threadIdx.x] = a.src[e];
+        const float* y = a.edge_y + 12 * (int64_t)e;
+        npow_all(a.lmax, y[0], y[1], y[2], np[threadIdx.x]);
+      }
+      __syncthreads();
+      if (valid) {
+        for (int k = 0; k < ne; ++k) {
+          const float4* h4 = reinterpret_cast<const float4*>(hs[k]);
+          float d0 = dzb, d1 = 0.f, d2 = 0.f, d3 = 0.f;
 #pragma unroll
-  for (int j = 0; j < RH; ++j) {
-    const float t = warp_sum(acch[j]);
-    if (lane == 0) red[warp][j] = t;
+          for (int j4 = 0; j4 < RH / 4; ++j4) {
+            const float4 h = h4[j4];
+            d0 = fmaf(dz[4 * j4], h.x, d0);
+            d1 = fmaf(dz[4 * j4 + 1], h.y, d1);
+            d2 = fmaf(dz[4 * j4 + 2], h.z, d2);
+            d3 = fmaf(dz[4 * j4 + 3], h.w, d3);
+          }
+          const float dm = (d0 + d1) + (d2 + d3);
+          const int s = srcs[k];
+          const float xv = x[((int64_t)s * R + c1) * C + ch];
+          atomicAdd(gx + ((int64_t)s * R + c1) * C + ch, dm * np[k][c2]);
+          const float t = warp_sum(dm * xv);
+          if (lane == 0) atomicAdd(&sdn[k][c2], t);
+        }
+      }
+      __syncthreads();
+      for (int t = threadIdx.x; t < ne * R; t += blockDim.x) {
+        const int k = t / R, c = t - k * R;
+        dnp[(int64_t)(eb + k) * MAXR + c] += sdn[k][c];
+      }
+    }
   }
-  __syncthreads();
-  if (threadIdx.x < RH) {
-    float t = 0.f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w][threadIdx.x];
-    dh2[e * RH + threadIdx.x] = t;
+}
+
+// dh_kernel: dE/dh2_e[j] = sum_{(r, a)} dZ[n][r][j][a] * x1[src_e][c1(r)][a] * n_e^{(x)L2}[c2(r)],
+// a (edges x columns) . (columns x 64) product tiled through shared memory (64 edges x 64 j per
+// pass, 32 columns per step, 4 x 4 outputs per thread).
+constexpr int DH_E = 64, DH_K = 32;
+
+__global__ void __launch_bounds__(256) bwd_dh_kernel(Args a, Rows rows, const float* __restrict__ x,
+                                                     const float* __restrict__ dZ, int64_t n0, float* __restrict__ dh2) {
+  __shared__ float zt[DH_K][RH + 4];
+  __shared__ float mt[DH_E][DH_K + 1];
+  __shared__ float np[DH_E][MAXR];
+  __shared__ int srcs[DH_E];
+  const int64_t n = n0 + blockIdx.x;
+  const int C = a.C, R = a.R;
+  const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
+  const int cols = rows.nrows * C;
+  const float* dzn = dZ + (int64_t)blockIdx.x * rows.nrows * J * C;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  for (int eb = e0; eb < e1; eb += DH_E) {
+    const int ne = min(DH_E, e1 - eb);
+    __syncthreads();
+    if (threadIdx.x < ne) {
+      const int e = eb + threadIdx.x;
+      srcs[threadIdx.x] = a.src[e];
+      const float* y = a.edge_y + 12 * (int64_t)e;
+      npow_all(a.lmax, y[0], y[1], y[2], np[threadIdx.x]);
+    }
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int col0 = 0; col0 < cols; col0 += DH_K) {
+      __syncthreads();
+      // dZ tile: zt[c][j] = dZ[n][r][j][a], (r, a) = column col0 + c
+      for (int t = threadIdx.x; t < DH_K * RH; t += blockDim.x) {
+        const int c = t % DH_K, j = t / DH_K;
+        const int col = col0 + c;
+        const int r = col / C, ch = col - r * C;
+        zt[c][j] = dzn[((int64_t)r * J + j) * C + ch];
+      }
+      // message tile: mt[e][c] = x1[src_e][c1(r)][a] * n_e^{(x)L2}[c2(r)]
+      for (int t = threadIdx.x; t < DH_E * DH_K; t += blockDim.x) {
+        const int c = t % DH_K, k = t / DH_K;
+        float v = 0.f;
+        if (k < ne) {
+          const int col = col0 + c;
+          const int r = col / C, ch = col - r * C;
+          v = x[((int64_t)srcs[k] * R + rows.c1[r]) * C + ch] * np[k][rows.c2[r]];
+        }
+        mt[k][c] = v;
+      }
+      __syncthreads();
+#pragma unroll 8
+      for (int c = 0; c < DH_K; ++c) {
+        float av[4], bv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) av[i] = mt[ty * 4 + i][c];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) bv[j] = zt[c][tx * 4 + j];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int k = ty * 4 + i;
+      if (k < ne)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dh2[(int64_t)(eb + k) * RH + tx * 4 + j] = acc[i][j];
+    }
   }
-  if (threadIdx.x < R) dnp[e * MAXR + threadIdx.x] += sdn[threadIdx.x];
 }
 
 // ---------------------------------------------------------------- edge gradient
@@ -835,13 +910,6 @@ int backward(Ctx& c) {
   if (cudaMemsetAsync(p.dnp, 0, sizeof(float) * p.E * MAXR, st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset");
   Args a = args(c);
   const float avg = (float)std::max(1e-8, (double)p.E / (double)std::max<int64_t>(p.N, 1));
-  std::vector<int32_t> rp;
-  if (p.chunk < p.N) {  // chunk edge ranges need the row pointers on the host
-    rp.resize(p.N + 1);
-    if (cudaMemcpyAsync(rp.data(), g->row_ptr, sizeof(int32_t) * (p.N + 1), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-        cudaStreamSynchronize(st) != cudaSuccess)
-      return fail(FSC_ERR_CUDA, "row_ptr readback");
-  }
   for (int k = p.nint - 1; k >= 1; --k) {
     for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
       const int64_t nc = std::min(p.chunk, p.N - n0);
@@ -853,13 +921,12 @@ int backward(Ctx& c) {
         ga.alpha = 1.f / avg;
         FSC_TRY(launch_gemm(ga, st));
       }
-      const int64_t e_lo = rp.empty() ? 0 : rp[n0], e_hi = rp.empty() ? p.E : rp[n0 + nc];
-      if (e_hi > e_lo) {
-        conv2_bwd_kernel<<<(unsigned)(e_hi - e_lo), 256, 0, st>>>(a, p.rows, p.feats[k - 1],
-                                                                   p.h2 + (int64_t)k * p.E * RH, p.zbuf, e_lo, n0,
-                                                                   p.grads[k - 1], p.dh2 + (int64_t)k * p.E * RH, p.dnp);
-        FSC_TRY(check_launch("sparse conv2_bwd_kernel"));
-      }
+      bwd_dm_kernel<<<(unsigned)nc, 256, 0, st>>>(a, p.rows, p.feats[k - 1], p.h2 + (int64_t)k * p.E * RH, p.zbuf,
+                                                   n0, p.grads[k - 1], p.dnp);
+      FSC_TRY(check_launch("sparse bwd_dm_kernel"));
+      bwd_dh_kernel<<<(unsigned)nc, 256, 0, st>>>(a, p.rows, p.feats[k - 1], p.zbuf, n0,
+                                                   p.dh2 + (int64_t)k * p.E * RH);
+      FSC_TRY(check_launch("sparse bwd_dh_kernel"));
     }
     prof::mark("sparse_conv2_backward", st);
   }
