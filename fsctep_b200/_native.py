@@ -53,7 +53,7 @@ class SparseWeights(C.Structure):
 class Graph(C.Structure):
     _fields_ = [("num_atoms", I64), ("num_local", I64), ("num_edges", I64), ("num_graphs", I64), ("pos", P),
                 ("species", P), ("batch", P), ("cell", P), ("row_ptr", P), ("src", P), ("shift", P),
-                ("tr_ptr", P), ("tr_eid", P), ("energy_weight", P), ("field", P)]
+                ("tr_ptr", P), ("tr_eid", P), ("energy_weight", P), ("field", P), ("layer_atoms", P)]
 
 
 class IctdOutputs(C.Structure):

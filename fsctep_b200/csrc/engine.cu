@@ -47,6 +47,8 @@ struct Plan {
   int goff[4], gl[4];       // block offset in the flat split (units of nC) and its l
   int64_t nrows;            // Gram operand rows: nC * sum_b (2 l_b + 1)
   int64_t N, E, B, npairs, chunk;
+  int64_t nk[8];            // receiving atoms evaluated per interaction layer (graph layer_atoms)
+  int64_t nro;              // atoms of the readout: nk[nint - 1]
   int hidden[4];
   int n_hidden;
   // workspace
@@ -172,7 +174,7 @@ void layout(Plan& p, Arena& ar, const fsc_ictd_config* cfg, int64_t N, int64_t E
 
 FgArgs fg_args(const Plan& p, const fsc_ictd_weights* w) {
   FgArgs f{};
-  f.N = p.N;
+  f.N = p.nro;
   f.n_pad = p.n_pad;
   f.C = p.C;
   f.nint = p.nint;
@@ -189,7 +191,7 @@ FgArgs fg_args(const Plan& p, const fsc_ictd_weights* w) {
 
 ReadoutTcArgs tc_args(const Plan& p, const float* wimg) {
   ReadoutTcArgs r{};
-  r.N = p.N;
+  r.N = p.nro;
   r.n_pad = p.n_pad;
   r.nC = p.nC;
   r.S = p.S;
@@ -248,12 +250,17 @@ ConvArgs conv_args(const Ctx& c, int layer) {
   a.gates = c.p.gates + (int64_t)layer * c.p.E * 12;
   a.field = c.g->field;
   a.batch = c.g->batch;
+  a.N = c.p.nk[layer];
+  a.n_active = c.p.nk[layer];
+  a.dst_limit = c.p.nk[layer];
+  a.src_limit = layer > 0 ? c.p.nk[layer - 1] : c.p.N;
+  a.err = c.p.err;
   return a;
 }
 
 ReadoutArgs readout_args(const Ctx& c) {
   ReadoutArgs r{};
-  r.N = c.p.N;
+  r.N = c.p.nro;
   r.C = c.p.C;
   r.nint = c.p.nint;
   r.S = c.p.S;
@@ -304,7 +311,7 @@ int forward(Ctx& c) {
     int64_t boff = 0;
     for (int l3 = 0; l3 < 3; ++l3) {
       GemmArgs ga = gemm(p.zbuf + OFF3(l3) * C, NZ * C, NP3(l3) * C, W + boff, C, 0, p.feats[k] + KB(l3) * C,
-                         NK * C, C, p.N, 2 * l3 + 1, NP3(l3) * C, C);
+                         NK * C, C, p.nk[k], 2 * l3 + 1, NP3(l3) * C, C);
       ga.deg_rowptr = g->row_ptr;
       FSC_TRY(launch_gemm(ga, st));
       boff += (int64_t)NP3(l3) * C * C;
@@ -320,12 +327,12 @@ int forward(Ctx& c) {
     FSC_TRY(launch_fg_gather(fg_args(p, w), st));
     FSC_TRY(launch_readout_fwd_tc(tc_args(p, w->wimg_fwd), st));
   }
-  if (!p.tc && cudaMemsetAsync(p.scalars, 0, sizeof(float) * p.N * p.S, st) != cudaSuccess)
+  if (!p.tc && cudaMemsetAsync(p.scalars, 0, sizeof(float) * p.nro * p.S, st) != cudaSuccess)
     return fail(FSC_ERR_CUDA, "memset scalars");
   for (int b = 0; b < p.ngram && !p.tc; ++b) {
     const float* Wp = w->wread_p + (int64_t)b * p.S * p.npairs;
-    for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
-      const int64_t nn = std::min(p.chunk, p.N - n0);
+    for (int64_t n0 = 0; n0 < p.nro; n0 += p.chunk) {
+      const int64_t nn = std::min(p.chunk, p.nro - n0);
       FSC_TRY(launch_gram_pack(ra, b, n0, nn, w->pairs, p.npairs, p.chunkbuf, st));
       GemmArgs ga = gemm(p.chunkbuf, p.npairs, 0, Wp, p.npairs, 1, p.scalars + n0 * p.S, p.S, 0, nn, 1,
                          (int)p.npairs, p.S);
@@ -335,14 +342,14 @@ int forward(Ctx& c) {
   }
   prof::mark("readout_gram_forward", st);
   FSC_TRY(launch_p5_forward(ra, p.scalars, p.p5, st));
-  FSC_TRY(launch_layernorm(p.p5, p.N, p.D0, w->mn_in_g, w->mn_in_b, 0, p.x0, st));
+  FSC_TRY(launch_layernorm(p.p5, p.nro, p.D0, w->mn_in_g, w->mn_in_b, 0, p.x0, st));
   const float* xin = p.x0;
   int din = p.D0;
   for (int k = 0; k < p.n_hidden; ++k) {
-    GemmArgs ga = gemm(xin, din, 0, w->mn_w[k], din, 1, p.act_pre[k], p.hidden[k], 0, p.N, 1, din, p.hidden[k]);
+    GemmArgs ga = gemm(xin, din, 0, w->mn_w[k], din, 1, p.act_pre[k], p.hidden[k], 0, p.nro, 1, din, p.hidden[k]);
     ga.bias = w->mn_b[k];
     FSC_TRY(launch_gemm(ga, st));
-    FSC_TRY(launch_layernorm(p.act_pre[k], p.N, p.hidden[k], w->mn_g[k], w->mn_beta[k], 1, p.act_post[k], st));
+    FSC_TRY(launch_layernorm(p.act_pre[k], p.nro, p.hidden[k], w->mn_g[k], w->mn_beta[k], 1, p.act_post[k], st));
     xin = p.act_post[k];
     din = p.hidden[k];
   }
@@ -357,17 +364,17 @@ int backward(Ctx& c) {
   cudaStream_t st = c.st;
   const int C = p.C;
   const int H = p.hidden[p.n_hidden - 1];
-  FSC_TRY(launch_energy_seed(p.N, H, w->out_v, g->energy_weight, g->num_local, p.dxa, st));
+  FSC_TRY(launch_energy_seed(p.nro, H, w->out_v, g->energy_weight, g->num_local, p.dxa, st));
   float* dcur = p.dxa;
   float* dnext = p.dxb;
   for (int k = p.n_hidden - 1; k >= 0; --k) {
     const int din = k == 0 ? p.D0 : p.hidden[k - 1];
     // da_k = LN_bwd(a_k, dx_{k+1}) into dnext, then dx_k = da_k @ W_k into dcur
-    FSC_TRY(launch_layernorm_backward(p.act_pre[k], dcur, p.N, p.hidden[k], w->mn_g[k], w->mn_beta[k], 1, dnext, st));
-    GemmArgs ga = gemm(dnext, p.hidden[k], 0, w->mn_w[k], din, 0, dcur, din, 0, p.N, 1, p.hidden[k], din);
+    FSC_TRY(launch_layernorm_backward(p.act_pre[k], dcur, p.nro, p.hidden[k], w->mn_g[k], w->mn_beta[k], 1, dnext, st));
+    GemmArgs ga = gemm(dnext, p.hidden[k], 0, w->mn_w[k], din, 0, dcur, din, 0, p.nro, 1, p.hidden[k], din);
     FSC_TRY(launch_gemm(ga, st));
   }
-  FSC_TRY(launch_layernorm_backward(p.p5, dcur, p.N, p.D0, w->mn_in_g, w->mn_in_b, 0, p.dp5, st));
+  FSC_TRY(launch_layernorm_backward(p.p5, dcur, p.nro, p.D0, w->mn_in_g, w->mn_in_b, 0, p.dp5, st));
   ReadoutArgs ra = readout_args(c);
   FSC_TRY(launch_p5_backward(ra, p.scalars, p.dp5, p.grads, p.dscalars, st));
   prof::mark("readout_mlp_backward", st);
@@ -377,8 +384,8 @@ int backward(Ctx& c) {
   }
   for (int b = 0; b < p.ngram && !p.tc; ++b) {
     const float* Ws = w->wread_s + (int64_t)b * p.S * p.nC * p.nC;
-    for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
-      const int64_t nn = std::min(p.chunk, p.N - n0);
+    for (int64_t n0 = 0; n0 < p.nro; n0 += p.chunk) {
+      const int64_t nn = std::min(p.chunk, p.nro - n0);
       GemmArgs ga = gemm(p.dscalars + n0 * p.S, p.S, 0, Ws, (int64_t)p.nC * p.nC, 0, p.chunkbuf,
                          (int64_t)p.nC * p.nC, 0, nn, 1, p.S, p.nC * p.nC);
       FSC_TRY(launch_gemm(ga, st));
@@ -386,6 +393,11 @@ int backward(Ctx& c) {
     }
   }
   prof::mark("readout_gram_backward", st);
+  // the readout only seeded atoms [0, nro): the rest of each evaluated layer starts at zero
+  for (int k = 0; k + 1 < p.nint; ++k)
+    if (p.nk[k] > p.nro &&
+        cudaMemsetAsync(p.grads[k] + p.nro * NK * C, 0, sizeof(float) * (p.nk[k] - p.nro) * NK * C, st) != cudaSuccess)
+      return fail(FSC_ERR_CUDA, "memset grads");
   if (cudaMemsetAsync(p.dY, 0, sizeof(float) * p.E * 12, st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset dY");
   for (int k = p.nint - 1; k >= 1; --k) {
     ConvArgs ca = conv_args(c, k);
@@ -394,28 +406,34 @@ int backward(Ctx& c) {
     int64_t boff = 0;
     for (int l3 = 0; l3 < 3; ++l3) {
       GemmArgs ga = gemm(p.grads[k] + KB(l3) * C, NK * C, C, Wb + boff, NP3(l3) * C, 0, p.zbuf + OFF3(l3) * C,
-                         NZ * C, NP3(l3) * C, p.N, 2 * l3 + 1, C, NP3(l3) * C);
+                         NZ * C, NP3(l3) * C, p.nk[k], 2 * l3 + 1, C, NP3(l3) * C);
       ga.deg_rowptr = g->row_ptr;
       FSC_TRY(launch_gemm(ga, st));
       boff += (int64_t)NP3(l3) * C * C;
     }
     prof::mark("conv2_mix_backward_dz", st);
-    FSC_TRY(launch_conv2_q(ca, p.feats[k - 1], p.zbuf, p.dgates + (int64_t)k * p.E * 12, p.dY, st));
+    ConvArgs cq = ca;
+    cq.N = p.N;  // every receiver: the ones not evaluated zero their gate gradients
+    FSC_TRY(launch_conv2_q(cq, p.feats[k - 1], p.zbuf, p.dgates + (int64_t)k * p.E * 12, p.dY, st));
     prof::mark("conv2_edge_backward_gates", st);
-    FSC_TRY(launch_conv2_r(ca, p.grads[k], p.zbuf, st));
+    ConvArgs cr = ca;
+    cr.N = p.nk[k - 1];  // senders whose layer k-1 features were evaluated
+    FSC_TRY(launch_conv2_r(cr, p.grads[k], p.zbuf, st));
     prof::mark("conv2_edge_backward_x", st);
     const float* Wx = w->mix_dx + (int64_t)(k - 1) * NP * C * C;
     boff = 0;
     for (int l1 = 0; l1 < 3; ++l1) {
       GemmArgs ga = gemm(p.zbuf + OFF1(l1) * C, NZ * C, NP1(l1) * C, Wx + boff, C, 0, p.grads[k - 1] + KB(l1) * C,
-                         NK * C, C, p.N, 2 * l1 + 1, NP1(l1) * C, C);
+                         NK * C, C, p.nk[k - 1], 2 * l1 + 1, NP1(l1) * C, C);
       ga.accumulate = 1;
       FSC_TRY(launch_gemm(ga, st));
       boff += (int64_t)NP1(l1) * C * C;
     }
     prof::mark("conv2_mix_backward_dx", st);
   }
-  FSC_TRY(launch_conv1_backward(conv_args(c, 0), w->ai, w->vsp, p.grads[0], p.dgates, p.dY, st));
+  ConvArgs c1 = conv_args(c, 0);
+  c1.N = p.N;
+  FSC_TRY(launch_conv1_backward(c1, w->ai, w->vsp, p.grads[0], p.dgates, p.dY, st));
   prof::mark("conv1_backward", st);
   return FSC_OK;
 }
@@ -486,6 +504,16 @@ int prepare(Ctx& c, void* workspace, size_t bytes) {
   if (!ar.ok() || workspace == nullptr)
     return fail(FSC_ERR_CAPACITY, "workspace too small: need " + std::to_string(ar.off) + " bytes");
   c.p.B = g->num_graphs;
+  Plan& p = c.p;
+  for (int k = 0; k < p.nint; ++k) {
+    const int64_t v = g->layer_atoms ? g->layer_atoms[k] : g->num_atoms;
+    FSC_REQUIRE(v >= 0 && v <= g->num_atoms && (k == 0 || v <= p.nk[k - 1]),
+                "layer_atoms must be non-increasing and within [0, num_atoms]");
+    p.nk[k] = v;
+  }
+  p.nro = p.nk[p.nint - 1];
+  FSC_REQUIRE(g->energy_weight || p.nro >= g->num_local, "layer_atoms[last] must be >= num_local");
+  p.n_pad = ceil_div(std::max<int64_t>(p.nro, 1), 128) * 128;  // Fg stride of this call (<= allocated)
   return FSC_OK;
 }
 
@@ -496,11 +524,14 @@ int run_forward(Ctx& c, float* energy, float* atom_energy) {
   FSC_TRY(forward(c));
   const int H = c.p.hidden[c.p.n_hidden - 1];
   float* ebuf = atom_energy ? atom_energy : c.p.dxb;  // dxb is free until the backward starts
-  FSC_TRY(launch_energy(c.p.act_post[c.p.n_hidden - 1], c.p.N, H, c.w->out_v, c.w->out_c0, c.g->batch,
+  FSC_TRY(launch_energy(c.p.act_post[c.p.n_hidden - 1], c.p.nro, H, c.w->out_v, c.w->out_c0, c.g->batch,
                         c.g->num_local, ebuf, nullptr, c.st));
-  if (c.p.N > 0) {
-    graph_reduce_kernel<1><<<(unsigned)ceil_div(c.p.N, 256), 256, 0, c.st>>>(
-        ebuf, nullptr, nullptr, nullptr, c.g->batch, c.p.N, c.g->num_local, c.p.energy_d, nullptr);
+  if (atom_energy && c.p.N > c.p.nro &&
+      cudaMemsetAsync(atom_energy + c.p.nro, 0, sizeof(float) * (c.p.N - c.p.nro), c.st) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "memset atom_energy");
+  if (c.p.nro > 0) {
+    graph_reduce_kernel<1><<<(unsigned)ceil_div(c.p.nro, 256), 256, 0, c.st>>>(
+        ebuf, nullptr, nullptr, nullptr, c.g->batch, c.p.nro, c.g->num_local, c.p.energy_d, nullptr);
     FSC_TRY(check_launch("graph_reduce_kernel<1>"));
   }
   if (energy) {

@@ -96,6 +96,10 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_z_kernel(ConvArgs a, co
   const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
   for (int e = e0; e < e1; ++e) {
     const int64_t s = a.src[e];
+    if (s >= a.src_limit) {  // sender outside the previous layer's evaluated atoms
+      if (lane == 0) atomicCAS(a.err, 0, 70);
+      continue;
+    }
     float xv[NK][CPL];
 #pragma unroll
     for (int k = 0; k < NK; ++k)
@@ -142,6 +146,7 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_r_kernel(ConvArgs a, co
   for (int t = t0; t < t1; ++t) {
     const int64_t e = a.tr_eid[t];
     const int64_t d = a.dst[e];
+    if (d >= a.dst_limit) continue;  // receiver not evaluated in this layer: no gradient
     const int deg = a.row_ptr[d + 1] - a.row_ptr[d];
     const float inv = 1.f / (float)(deg > 1 ? deg : 1);
     float gv[NK][CPL];
@@ -241,6 +246,13 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_q_kernel(ConvArgs a, co
   if (n >= a.N) return;
   constexpr int C = 32 * CPL;
   const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
+  if (n >= a.n_active) {  // receiver not evaluated in this layer: its edges' gate gradients are 0
+    for (int e = e0 + lane; e < e1; e += 32) {
+      float4* dgo = reinterpret_cast<float4*>(dgates + 12 * (int64_t)e);
+      dgo[0] = dgo[1] = dgo[2] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    return;
+  }
   const float4* dz4 = reinterpret_cast<const float4*>(dZ + n * NZ * C);
   for (int base = e0; base < e1; base += 32) {
     const int e = base + lane;
@@ -369,6 +381,12 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv1_backward_kernel(ConvArg
   if (n >= a.N) return;
   const int C = 32 * CPL;
   const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
+  if (n >= a.n_active) {  // receiver not evaluated: zero gate gradients, no direction gradient
+    for (int e = e0 + lane; e < e1; e += 32)
+#pragma unroll
+      for (int p = 0; p < 12; ++p) dgates[12 * (int64_t)e + p] = 0.f;
+    return;
+  }
   const int deg = e1 - e0;
   const float inv = 1.f / (float)(deg > 1 ? deg : 1);
   const float* V = vsp + (int64_t)a.species[n] * 3 * 8 * C;

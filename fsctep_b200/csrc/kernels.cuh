@@ -82,6 +82,11 @@ struct ConvArgs {
   const float* gates;    // [E][12] of this layer
   const float* field;    // [B][3] or null: added to the l = 1 harmonic in conv1
   const int32_t* batch;  // [N] graph of each atom (for field)
+  // Receptive-field restriction (all default to "no restriction" when left at 0 / null):
+  int64_t n_active;      // conv1_backward / conv2_q: nodes in [n_active, N) only zero their dgates
+  int64_t dst_limit;     // conv2_r: edges whose dst >= dst_limit carry no gradient
+  int64_t src_limit;     // conv2_z: an edge whose src >= src_limit is skipped and flags err (70)
+  int* err;
 };
 
 // conv1: f1[n][k][c]

@@ -949,6 +949,7 @@ int prepare(Ctx& c, void* workspace, size_t bytes) {
   FSC_REQUIRE(g->num_atoms < (int64_t)INT32_MAX && g->num_edges < (int64_t)INT32_MAX, "graph too large");
   FSC_REQUIRE(g->num_graphs <= kMaxGraphs, "too many graphs per call (max 4096)");
   FSC_REQUIRE(g->num_local >= 0 && g->num_local <= g->num_atoms, "num_local out of range");
+  if (g->layer_atoms) return fail(FSC_ERR_UNSUPPORTED, "layer_atoms is supported by the ictd engine only");
   Arena ar(workspace, bytes);
   layout(c.p, ar, c.cfg, g->num_atoms, g->num_edges);
   if (!ar.ok() || workspace == nullptr)

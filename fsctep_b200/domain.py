@@ -307,25 +307,86 @@ def decomposed_step(dec: Decomposition, rank: int, pos: torch.Tensor, species: t
     return res
 
 
-def ictd_evaluator(engine, cell, cutoff: float, want_virial: bool = False) -> Evaluator:
+SHELL_MARGIN = 1e-3  # relative: covers float32 rounding of edge lengths at ~1000 A coordinates
+
+
+def layer_shells(pos: torch.Tensor, num_local: int, split: Sequence[bool], cutoff: float, num_interaction: int):
+    """Receptive-field order of a local system [owned | ghosts] for the engine's ``layer_atoms``.
+
+    ``d(x)`` = Euclidean distance of ``x`` from the owned atoms' bounding box along the split
+    axes (the others are periodic in the local system), ``shell(x) = ceil(d / w)`` with
+    ``w = cutoff (1 + SHELL_MARGIN)``.  An edge is shorter than the cutoff, so the sender of a
+    receiver in shell ``s`` lies in shell ``<= s + 1`` even after float32 rounding of the edge
+    length.  Owned energies need layer k (conv1 = 0) only on shells ``<= nint - 1 - k`` and
+    positions only on shells ``<= nint``; every sender that an evaluated receiver reads was
+    evaluated one layer earlier.
+
+    Returns ``(perm, layer_atoms)``: ``perm`` indexes ``pos`` — owned atoms first in their order,
+    then the ghosts of shells ``<= nint`` stably sorted by shell (farther ghosts are dropped) —
+    and ``layer_atoms[k]`` = number of leading atoms of ``perm`` in shells ``<= nint - 1 - k``."""
+    n = int(pos.shape[0])
+    dev = pos.device
+    nint = int(num_interaction)
+    own = torch.arange(num_local, device=dev)
+    if n == num_local or num_local == 0:
+        return torch.arange(n, device=dev), [n] * nint
+    p = pos.to(torch.float64)
+    lo = p[:num_local].min(0).values
+    hi = p[:num_local].max(0).values
+    g = p[num_local:]
+    over = torch.clamp(torch.maximum(lo - g, g - hi), min=0.0)
+    over = over * torch.tensor([1.0 if s else 0.0 for s in split], dtype=torch.float64, device=dev)
+    d = torch.linalg.vector_norm(over, dim=1)
+    w = float(cutoff) * (1.0 + SHELL_MARGIN)
+    shell = torch.ceil(d / w).to(torch.int64)
+    keep = (shell <= nint).nonzero().squeeze(1)
+    order = torch.sort(shell[keep], stable=True)
+    ghosts = keep[order.indices] + num_local
+    perm = torch.cat([own, ghosts])
+    counts = torch.bincount(order.values, minlength=nint + 1)[: nint + 1]
+    cum = (num_local + torch.cumsum(counts, 0)).tolist()   # atoms in shells <= s
+    return perm, [int(cum[nint - 1 - k]) for k in range(nint)]
+
+
+def ictd_evaluator(engine, cell, cutoff: float, want_virial: bool = False, restrict_layers: bool = True) -> Evaluator:
     """Evaluator of :func:`decomposed_step` backed by the native engine (one GPU per rank):
     GPU cell-list neighbour list of the local system, forward with ``num_local`` (owned atoms),
-    reverse pass for the forces (and the virial)."""
+    reverse pass for the forces (and the virial).
+
+    With ``restrict_layers`` the ghosts are ordered by distance shell (:func:`layer_shells`) and
+    the engine evaluates interaction layer k only on the receivers within ``nint - 1 - k`` shells
+    of the owned atoms (the readout on owned atoms only); ghosts beyond ``nint`` shells are not
+    used.  The owned energies and all forces are unchanged (the dropped work only fed ghost
+    energies, which carry no weight)."""
     from .neighbors import build_graph
 
     dev = engine.device
     cell_t = torch.as_tensor(np.asarray(cell), dtype=torch.float64, device=dev).reshape(1, 3, 3)
+    nint = engine.cfg.num_interaction
     batch_cache = {}
 
     def evaluate(pos, species, num_local, pbc):
+        n_all = int(pos.shape[0])
+        layers = None
+        if restrict_layers:
+            perm, layers = layer_shells(pos, num_local, [not p for p in pbc], cutoff, nint)
+            pos, species = pos[perm], species[perm]
         g = build_graph(pos, cell_t, cutoff, pbc=pbc)
         n = int(pos.shape[0])
         if n not in batch_cache:
             batch_cache.clear()
             batch_cache[n] = torch.zeros(n, dtype=torch.int32, device=dev)
-        energy, atom_e = engine.forward(pos, species, batch_cache[n], cell_t, g, num_local=num_local)
+        energy, atom_e = engine.forward(pos, species, batch_cache[n], cell_t, g, num_local=num_local,
+                                        layer_atoms=layers)
         out = engine.backward(want_virial=want_virial)
-        res = {"energy": energy[0], "forces": out["forces"], "atom_energy": atom_e}
+        forces = out["forces"]
+        if restrict_layers:
+            full_f = torch.zeros(n_all, 3, dtype=forces.dtype, device=dev)
+            full_f[perm] = forces
+            full_e = torch.zeros(n_all, dtype=atom_e.dtype, device=dev)
+            full_e[perm] = atom_e
+            forces, atom_e = full_f, full_e
+        res = {"energy": energy[0], "forces": forces, "atom_energy": atom_e}
         if want_virial:
             res["virial"] = out["virial"][0]
         return res

@@ -362,7 +362,8 @@ class ICTDEngine:
             self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
         return self._ws
 
-    def _graph(self, pos, species, batch, cell, g: GraphCSR, num_graphs, num_local, energy_weight, field=None):
+    def _graph(self, pos, species, batch, cell, g: GraphCSR, num_graphs, num_local, energy_weight, field=None,
+               layer_atoms=None):
         s = N.Graph()
         s.num_atoms = g.num_atoms
         s.num_local = g.num_atoms if num_local is None else int(num_local)
@@ -373,6 +374,14 @@ class ICTDEngine:
         s.tr_ptr, s.tr_eid = g.tr_ptr.data_ptr(), g.tr_eid.data_ptr()
         s.energy_weight = 0 if energy_weight is None else energy_weight.data_ptr()
         s.field = 0 if field is None else field.data_ptr()
+        if layer_atoms is None:
+            s.layer_atoms = 0
+        else:
+            vals = [int(v) for v in layer_atoms]
+            if len(vals) != self.cfg.num_interaction:
+                raise ValueError(f"layer_atoms needs {self.cfg.num_interaction} entries, got {len(vals)}")
+            self._layer_arr = (C.c_int64 * len(vals))(*vals)  # host array, alive until the next call
+            s.layer_atoms = C.cast(self._layer_arr, N.P)
         return s
 
     def _field(self, field, B):
@@ -397,20 +406,23 @@ class ICTDEngine:
         cell = cell.detach().to(torch.float32).reshape(-1, 3, 3).contiguous()
         return pos, species, batch, cell
 
-    def forward(self, pos, species, batch, cell, g: GraphCSR, num_local=None, field=None):
+    def forward(self, pos, species, batch, cell, g: GraphCSR, num_local=None, field=None, layer_atoms=None):
         """Per-graph energy (B,) and per-atom energy (N,); intermediates stay in the workspace.
-        ``field`` (B, 3): external 1o field of the o3 model (one Cartesian vector per graph)."""
+        ``field`` (B, 3): external 1o field of the o3 model (one Cartesian vector per graph).
+        ``layer_atoms`` (num_interaction ints): receptive-field restriction of a decomposition rank
+        (layer k evaluated for receiving atoms ``[0, layer_atoms[k])``; see :func:`layer_shells`)."""
         pos, species, batch, cell = self._inputs(pos, species, batch, cell)
         B = cell.shape[0]
         ws = self.workspace(g.num_atoms, g.num_edges)
         energy = torch.empty(B, dtype=torch.float32, device=self.device)
         atom_e = torch.empty(g.num_atoms, dtype=torch.float32, device=self.device)
         fdev = self._field(field, B)
-        gs = self._graph(pos, species, batch, cell, g, B, num_local, None, fdev)
+        gs = self._graph(pos, species, batch, cell, g, B, num_local, None, fdev, layer_atoms)
         N.check(N.lib().fsc_ictd_forward(C.byref(self.ncfg), C.byref(self.weights.struct), C.byref(gs),
                                          N.ptr(energy), N.ptr(atom_e), N.ptr(ws), ws.numel(),
                                          N.stream_ptr(self.device)), "fsc_ictd_forward")
         self._last = (pos, species, batch, cell, g, num_local)
+        self._last_layers = layer_atoms
         self._field_dev = fdev
         return energy, atom_e
 
@@ -425,7 +437,7 @@ class ICTDEngine:
         nh = len(w.heads)
         out = torch.empty(nh, B, 5, dtype=torch.float32, device=self.device)
         blocks = (C.c_int32 * nh)(*[blk for _, _, blk in w.heads])
-        gs = self._graph(pos, species, batch, cell, g, B, num_local, None, self._field_dev)
+        gs = self._graph(pos, species, batch, cell, g, B, num_local, None, self._field_dev, self._last_layers)
         N.check(N.lib().fsc_ictd_heads(C.byref(self.ncfg), C.byref(w.struct), C.byref(gs), nh,
                                        C.cast(blocks, N.P), N.ptr(w.tensors["heads_w"]), N.ptr(out), N.ptr(ws),
                                        ws.numel(), N.stream_ptr(self.device)), "fsc_ictd_heads")
@@ -449,7 +461,8 @@ class ICTDEngine:
             out["edge_grad"] = torch.empty(g.num_edges, 3, dtype=torch.float32, device=dev)
         if energy_weight is not None:
             energy_weight = energy_weight.detach().to(torch.float32).reshape(-1).contiguous()
-        gs = self._graph(pos, species, batch, cell, g, B, num_local, energy_weight, getattr(self, "_field_dev", None))
+        gs = self._graph(pos, species, batch, cell, g, B, num_local, energy_weight, getattr(self, "_field_dev", None),
+                         getattr(self, "_last_layers", None))
         o = N.IctdOutputs()
         o.forces = out["forces"].data_ptr()
         o.virial = out["virial"].data_ptr() if want_virial else 0

@@ -263,6 +263,15 @@ typedef struct {
                                 harmonic of conv1 (external 1o field of the o3 model: the
                                 field's ICTD l = 1 components times external_tensor_scale,
                                 pure_cartesian_ictd_layers_o3.py:466-502)               */
+  const int64_t* layer_atoms;/* HOST [num_interaction] or NULL (= all atoms).  Receptive-field
+                                restriction of a spatial-decomposition rank: interaction layer k
+                                (conv1 = 0) is evaluated for receiving atoms [0, layer_atoms[k])
+                                and the readout for atoms [0, layer_atoms[last]).  Non-increasing,
+                                layer_atoms[last] >= num_local, and every edge whose dst is below
+                                layer_atoms[k] (k >= 1) has src below layer_atoms[k-1] (atoms
+                                ordered by distance shell from the owned region); a violated edge
+                                sets status 70 and is skipped.  Atoms past layer_atoms[last] get
+                                atom_energy 0 and no backward seed.  ictd engine only.       */
 } fsc_graph;
 
 typedef struct {

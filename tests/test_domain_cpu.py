@@ -17,11 +17,21 @@ RC = 4.0  # first two diamond shells (2.35 and 3.84 A)
 NHOP = 2
 
 
-def toy_evaluate(cell):
-    """Evaluator of a 2-hop potential on a local system (owned atoms first)."""
+def toy_evaluate(cell, restrict=False):
+    """Evaluator of a 2-hop potential on a local system (owned atoms first).
+
+    ``restrict`` evaluates it the way the engine does with ``layer_atoms``: ghosts reordered by
+    distance shell (:func:`domain.layer_shells`), hop k only for receivers below
+    ``layer_atoms[k]``, atom energies only below ``layer_atoms[-1]``; the contract that every
+    evaluated receiver reads only senders evaluated one hop earlier is asserted."""
     cell_t = torch.tensor(cell, dtype=torch.float64)
 
     def evaluate(pos, species, num_local, pbc):
+        n_all = pos.shape[0]
+        perm = None
+        if restrict:
+            perm, L = D.layer_shells(pos, num_local, [not q for q in pbc], RC, NHOP)
+            pos, species = pos[perm], species[perm]
         src, dst, S = ON.neighbor_list(pos.detach().numpy(), cell, RC, pbc=pbc)
         p = pos.detach().clone().requires_grad_(True)
         src_t, dst_t = torch.tensor(src), torch.tensor(dst)
@@ -32,12 +42,25 @@ def toy_evaluate(cell):
         w = 1.0 + 0.1 * species.to(torch.float64)
         n = p.shape[0]
         m1 = torch.zeros(n, dtype=torch.float64).index_add(0, dst_t, phi * w[src_t])
-        m2 = torch.zeros(n, dtype=torch.float64).index_add(0, dst_t, phi * torch.tanh(0.3 * m1[src_t]))
+        if restrict:
+            assert bool((src_t[dst_t < L[1]] < L[0]).all())  # hop-2 receivers read hop-1 senders only
+            m1 = torch.zeros(n, dtype=torch.float64).index_add(
+                0, dst_t[dst_t < L[0]], (phi * w[src_t])[dst_t < L[0]])
+            on2 = dst_t < L[1]
+            m2 = torch.zeros(n, dtype=torch.float64).index_add(
+                0, dst_t[on2], (phi * torch.tanh(0.3 * m1[src_t]))[on2])
+        else:
+            m2 = torch.zeros(n, dtype=torch.float64).index_add(0, dst_t, phi * torch.tanh(0.3 * m1[src_t]))
         e = 0.01 * m2 ** 2 + 0.5 * m1 + 0.05 * m1 * m2
+        if restrict:
+            e = torch.where(torch.arange(n) < L[-1], e, torch.zeros_like(e))
         E = e[:num_local].sum()
         E.backward()
-        return {"energy": E.detach(), "forces": -p.grad, "atom_energy": e.detach(),
-                "virial": (r.detach().T @ r.grad)}
+        forces, ae = -p.grad, e.detach()
+        if restrict:
+            forces = torch.zeros(n_all, 3, dtype=torch.float64).index_copy(0, perm, forces)
+            ae = torch.zeros(n_all, dtype=torch.float64).index_copy(0, perm, ae)
+        return {"energy": E.detach(), "forces": forces, "atom_energy": ae, "virial": (r.detach().T @ r.grad)}
 
     return evaluate
 
@@ -64,9 +87,9 @@ def _owned(dec, rank, s):
     return np.nonzero(m)[0]
 
 
-def _decomposed_local(s, dims, halo):
+def _decomposed_local(s, dims, halo, restrict=False):
     dec = D.Decomposition(s["cell"][0], dims, halo)
-    ev = toy_evaluate(s["cell"][0])
+    ev = toy_evaluate(s["cell"][0], restrict)
     owned = [_owned(dec, r, s) for r in range(dec.world)]
     gens = [D.decomposed_step(dec, r, torch.tensor(s["pos"][o], dtype=torch.float64), torch.tensor(s["Z"][o]), ev,
                               want_virial=True) for r, o in enumerate(owned)]
@@ -77,11 +100,12 @@ def _decomposed_local(s, dims, halo):
     return res, F, owned
 
 
+@pytest.mark.parametrize("restrict", [False, True])
 @pytest.mark.parametrize("dims", [(2, 1, 1), (2, 2, 1), (2, 2, 2), (1, 2, 1)])
-def test_decomposed_matches_single_domain(dims):
+def test_decomposed_matches_single_domain(dims, restrict):
     s = _system()
     ref = _reference(s)
-    res, F, owned = _decomposed_local(s, dims, NHOP * RC)
+    res, F, owned = _decomposed_local(s, dims, NHOP * RC, restrict)
     assert sorted(np.concatenate(owned).tolist()) == list(range(s["pos"].shape[0]))
     for r in res:
         assert abs(r["energy"].item() - ref["energy"].item()) <= 1e-10 * abs(ref["energy"].item())
@@ -100,6 +124,23 @@ def test_short_halo_is_detected():
     ref = _reference(s)
     res, _, _ = _decomposed_local(s, (2, 1, 1), 1.0 * RC)
     assert abs(res[0]["energy"].item() - ref["energy"].item()) > 1e-6 * abs(ref["energy"].item())
+
+
+def test_layer_shells_order_and_counts():
+    """Owned atoms keep their order in front; ghosts follow by shell; counts are per shell."""
+    g = torch.Generator().manual_seed(3)
+    own = torch.rand(50, 3, generator=g, dtype=torch.float64) * 10.0
+    ghosts = torch.tensor([[12.0, 5, 5], [-0.5, 5, 5], [5, 5, 20.5], [23.0, 5, 5], [5, -9.5, 5], [10.0, 5, 5]],
+                          dtype=torch.float64)
+    lo, hi = own.min(0).values, own.max(0).values
+    pos = torch.cat([own, ghosts])
+    perm, L = D.layer_shells(pos, 50, (True, True, False), 5.0, 3)
+    d = [max(float(lo[0] - x[0]), float(x[0] - hi[0]), float(lo[1] - x[1]), float(x[1] - hi[1]), 0.0)
+         for x in ghosts]  # single-axis overshoots here; z is unsplit (distance 0 along it)
+    shells = [int(np.ceil(v / (5.0 * (1 + D.SHELL_MARGIN)))) for v in d]
+    keep = sorted([i for i in range(6) if shells[i] <= 3], key=lambda i: shells[i])
+    assert perm.tolist() == list(range(50)) + [50 + i for i in keep]
+    assert L == [50 + sum(sh <= 3 - 1 - k for sh in shells) for k in range(3)]
 
 
 def test_grid_for_and_validation():

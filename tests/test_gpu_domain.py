@@ -7,6 +7,7 @@ import pytest
 import torch
 
 import gpu_util as U
+from fsctep_b200 import _native as NAT
 from fsctep_b200 import domain as D
 from fsctep_b200 import systems
 from fsctep_b200.ictd import ICTDConfig, ICTDEngine
@@ -27,8 +28,11 @@ def _owned(dec, rank, pos, cell):
     return np.nonzero(m)[0]
 
 
+@pytest.mark.parametrize("restrict", [False, True])
 @pytest.mark.parametrize("dims", [(2, 1, 1), (2, 2, 2)])
-def test_decomposed_engine_matches_single_domain(dims):
+def test_decomposed_engine_matches_single_domain(dims, restrict):
+    """``restrict``: the engine evaluates layer k only within nint - 1 - k shells of the owned
+    atoms (graph layer_atoms); the result must not change."""
     cfg = ICTDConfig(channels=32, num_interaction=3, number_of_basis=8, max_radius=5.0, function_type="gaussian",
                      max_atomvalue=16)
     eng = ICTDEngine(seeded_state_dict(reference_state_dict_shapes(cfg), 7), cfg, "cuda")
@@ -44,7 +48,13 @@ def test_decomposed_engine_matches_single_domain(dims):
 
     c0 = s["cell"][0]
     dec = D.Decomposition(c0, dims, cfg.num_interaction * cfg.max_radius)
-    ev = D.ictd_evaluator(eng, c0, cfg.max_radius, want_virial=True)
+    ev0 = D.ictd_evaluator(eng, c0, cfg.max_radius, want_virial=True, restrict_layers=restrict)
+
+    def ev(*a):
+        out = ev0(*a)
+        assert eng.status() == 0  # no receiver read a sender outside the previous layer's atoms
+        return out
+
     owned = [_owned(dec, r, s["pos"], c0) for r in range(dec.world)]
     gens = [D.decomposed_step(dec, r, pos[torch.tensor(o, device=dev)], Z[torch.tensor(o, device=dev)], ev,
                               want_virial=True) for r, o in enumerate(owned)]
@@ -58,3 +68,23 @@ def test_decomposed_engine_matches_single_domain(dims):
         assert U.rel_max(r["virial"].cpu().numpy(), ref_v) <= 1e-4
     assert U.rel_max(F, ref_f) <= 1e-4, U.rel_max(F, ref_f)
     assert all(r["num_ghosts"] > 0 for r in res)
+
+
+def test_layer_atoms_contract_violation_is_reported():
+    """A layer_atoms that cuts through the receptive field (layer 1 evaluated on atoms whose
+    senders layer 0 skipped) is reported as status 70, not read from stale memory."""
+    cfg = ICTDConfig(channels=32, num_interaction=3, number_of_basis=8, max_radius=5.0, function_type="gaussian",
+                     max_atomvalue=16)
+    eng = ICTDEngine(seeded_state_dict(reference_state_dict_shapes(cfg), 7), cfg, "cuda")
+    s = systems.diamond_crystal(n_cells=(4, 4, 4), seed=5)
+    dev = torch.device("cuda")
+    pos, cell = torch.tensor(s["pos"], device=dev), torch.tensor(s["cell"], device=dev)
+    Z = torch.tensor(s["Z"], device=dev, dtype=torch.int32)
+    g = build_graph(pos, cell, 5.0)
+    n = int(pos.shape[0])
+    eng.forward(pos, Z, torch.zeros_like(Z), cell, g, num_local=8, layer_atoms=[n, n, n])
+    assert eng.status() == 0
+    eng.forward(pos, Z, torch.zeros_like(Z), cell, g, num_local=8, layer_atoms=[16, 16, 8])
+    assert eng.status() == 70
+    with pytest.raises(NAT.NativeError):
+        eng.forward(pos, Z, torch.zeros_like(Z), cell, g, num_local=8, layer_atoms=[16, 32, 8])  # increasing
