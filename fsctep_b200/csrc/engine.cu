@@ -193,6 +193,7 @@ ReadoutTcArgs tc_args(const Plan& p, const float* wimg) {
   ReadoutTcArgs r{};
   r.N = p.nro;
   r.n_pad = p.n_pad;
+  r.nrows = p.nrows;
   r.nC = p.nC;
   r.S = p.S;
   r.Fg = p.Fg;

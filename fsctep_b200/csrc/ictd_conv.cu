@@ -27,7 +27,16 @@ using namespace ictd2;
 struct QTab {
   int8_t path[NQ];
   int8_t yb[NQ];
+  uint8_t qpad[NQ];  // position of q in the padded per-edge layout (QPOFF blocks)
 };
+
+// Per-edge coupled harmonics are stored with every path's block padded to a multiple of 4
+// entries (offsets QPOFF), so a path's weights are read as 16-byte shared-memory vectors.
+__host__ __device__ constexpr int QPOFF(int p) {
+  constexpr int t[NP] = {0, 4, 8, 16, 28, 32, 48, 60, 88, 104, 112};
+  return t[p];
+}
+constexpr int NQP = 140;
 
 constexpr QTab make_qtab() {
   QTab t{};
@@ -37,6 +46,7 @@ constexpr QTab make_qtab() {
         const int q = qidx(p, m1, kk);
         t.path[q] = (int8_t)p;
         t.yb[q] = (int8_t)KB(L2(p));
+        t.qpad[q] = (uint8_t)(QPOFF(p) + m1 * (2 * L3(p) + 1) + kk);
       }
   return t;
 }
@@ -45,37 +55,124 @@ __constant__ QTab c_qtab = make_qtab();
 
 constexpr int CONV_WARPS = 4;
 
-struct EdgeBuf {
-  float y[12];
-  float g[12];
-  float yt[NQ + 1];
+struct __align__(16) EdgeBuf {
+  float yt[NQP];
+  float yg[24];  // Y (12) then gates (12) of the edge
 };
 
-// Warp-cooperative: load Y and gates of edge e and build Yt (gated when `gated`).
-__device__ __forceinline__ void build_yt(EdgeBuf& b, const float* __restrict__ cg2, const float* __restrict__ edge_y,
-                                         const float* __restrict__ gates, int64_t e, int lane, bool gated) {
-  if (lane < 12) b.y[lane] = edge_y[12 * e + lane];
-  else if (lane < 24) b.g[lane - 12] = gates[12 * e + lane - 12];
+// The Yt entries a lane builds are q = lane + 32 j (j < 4).  Their Y offset and path (byte j of
+// `info` = yb | path << 4) and padded position (byte j of `pad`) live in two registers, read once
+// per warp: per-lane indices into __constant__ memory serialise, which made the indexed-constant
+// path the limiter of the edge loops.
+struct LaneQ {
+  uint32_t info, pad;
+};
+__device__ __forceinline__ LaneQ lane_q(int lane) {
+  LaneQ r{0u, 0u};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int q = lane + 32 * j;
+    if (q < NQ) {
+      const int p = c_qtab.path[q];
+      r.info |= (uint32_t)(c_qtab.yb[q] | (p << 4)) << (8 * j);
+      r.pad |= (uint32_t)(c_qtab.qpad[q]) << (8 * j);
+    }
+  }
+  return r;
+}
+
+// This lane's share of edge e's Y and gates (lanes 0-11: Y, 12-23: gates).
+__device__ __forceinline__ float load_yg(const ConvArgs& a, int64_t e, int lane) {
+  return lane < 12 ? a.edge_y[12 * e + lane] : (lane < 24 ? a.gates[12 * e + lane - 12] : 0.f);
+}
+
+// Warp-cooperative: Yt[q] = gate[p(q)] * sum_m cg2[q][m] Y[yb(q) + m] into b.yt (padded layout).
+__device__ __forceinline__ void build_yt(EdgeBuf& b, const float* __restrict__ cg2, float yg, int lane, LaneQ lq) {
+  if (lane < 24) b.yg[lane] = yg;
   __syncwarp();
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int q = lane + 32 * j;
     if (q < NQ) {
-      const int yb = c_qtab.yb[q];
+      const uint32_t t = lq.info >> (8 * j);
+      const int yb = (int)(t & 15u);
       float v = 0.f;
 #pragma unroll
-      for (int m = 0; m < 5; ++m) v = fmaf(cg2[5 * q + m], b.y[yb + m], v);
-      b.yt[q] = gated ? v * b.g[c_qtab.path[q]] : v;
+      for (int m = 0; m < 5; ++m) v = fmaf(cg2[5 * q + m], b.yg[yb + m], v);
+      b.yt[(lq.pad >> (8 * j)) & 255u] = v * b.yg[12 + ((t >> 4) & 15u)];
     }
   }
   __syncwarp();
+}
+
+// Path p's (2 l1 + 1) x (2 l3 + 1) weights (m1-major) from the padded Yt into registers.
+template <int P>
+__device__ __forceinline__ void path_weights(const EdgeBuf& b, float* w) {
+  constexpr int n = (2 * L1(P) + 1) * (2 * L3(P) + 1);
+  const float4* v4 = reinterpret_cast<const float4*>(b.yt + QPOFF(P));
+#pragma unroll
+  for (int i = 0; i < (n + 3) / 4; ++i) {
+    const float4 v = v4[i];
+    w[4 * i] = v.x;
+    w[4 * i + 1] = v.y;
+    w[4 * i + 2] = v.z;
+    w[4 * i + 3] = v.w;
+  }
 }
 
 __device__ __forceinline__ void load_cg2(float* cg2, const float* tables) {
   for (int i = threadIdx.x; i < NQ * 5; i += blockDim.x) cg2[i] = tables[TAB_CG2 + i];
 }
 
+template <int P, int CPL>
+__device__ __forceinline__ void z_path(const EdgeBuf& b, const float (&xv)[NK][CPL], float (&z)[NZ][CPL]) {
+  float w[28];
+  path_weights<P>(b, w);
+  constexpr int n3 = 2 * L3(P) + 1;
+#pragma unroll
+  for (int m1 = 0; m1 < 2 * L1(P) + 1; ++m1)
+#pragma unroll
+    for (int kk = 0; kk < n3; ++kk)
+#pragma unroll
+      for (int c = 0; c < CPL; ++c)
+        z[zrow(P, kk)][c] = fmaf(xv[KB(L1(P)) + m1][c], w[m1 * n3 + kk], z[zrow(P, kk)][c]);
+}
+
+template <int P, int CPL>
+__device__ __forceinline__ void r_path(const EdgeBuf& b, const float (&gv)[NK][CPL], float (&r)[NZ][CPL]) {
+  float w[28];
+  path_weights<P>(b, w);
+  constexpr int n3 = 2 * L3(P) + 1;
+#pragma unroll
+  for (int m1 = 0; m1 < 2 * L1(P) + 1; ++m1)
+#pragma unroll
+    for (int kk = 0; kk < n3; ++kk)
+#pragma unroll
+      for (int c = 0; c < CPL; ++c)
+        r[rrow(P, m1)][c] = fmaf(gv[KB(L3(P)) + kk][c], w[m1 * n3 + kk], r[rrow(P, m1)][c]);
+}
+
+template <int CPL, template <int, int> class F, typename... T>
+__device__ __forceinline__ void all_paths(T&... t) {
+  F<0, CPL>::run(t...); F<1, CPL>::run(t...); F<2, CPL>::run(t...); F<3, CPL>::run(t...);
+  F<4, CPL>::run(t...); F<5, CPL>::run(t...); F<6, CPL>::run(t...); F<7, CPL>::run(t...);
+  F<8, CPL>::run(t...); F<9, CPL>::run(t...); F<10, CPL>::run(t...);
+}
+template <int P, int CPL>
+struct ZPath {
+  __device__ __forceinline__ static void run(const EdgeBuf& b, const float (&xv)[NK][CPL], float (&z)[NZ][CPL]) {
+    z_path<P, CPL>(b, xv, z);
+  }
+};
+template <int P, int CPL>
+struct RPath {
+  __device__ __forceinline__ static void run(const EdgeBuf& b, const float (&gv)[NK][CPL], float (&r)[NZ][CPL]) {
+    r_path<P, CPL>(b, gv, r);
+  }
+};
+
 // ---------------------------------------------------------------- conv2 forward: Z
+// The next edge's sender row, Y and gates are loaded while the current edge is contracted.
 template <int CPL>
 __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_z_kernel(ConvArgs a, const float* __restrict__ x,
                                                                   float* __restrict__ Z) {
@@ -86,37 +183,45 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_z_kernel(ConvArgs a, co
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n = (int64_t)blockIdx.x * CONV_WARPS + warp;
   if (n >= a.N) return;
-  const int C = 32 * CPL;
+  constexpr int C = 32 * CPL;
   EdgeBuf& b = bufs[warp];
+  const LaneQ lq = lane_q(lane);
   float z[NZ][CPL];
 #pragma unroll
   for (int r = 0; r < NZ; ++r)
 #pragma unroll
     for (int c = 0; c < CPL; ++c) z[r][c] = 0.f;
   const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
-  for (int e = e0; e < e1; ++e) {
+  // a sender outside the previous layer's evaluated atoms is skipped and flagged
+  auto fetch = [&](int e, float (&xd)[NK][CPL], float& yg) -> bool {
     const int64_t s = a.src[e];
-    if (s >= a.src_limit) {  // sender outside the previous layer's evaluated atoms
-      if (lane == 0) atomicCAS(a.err, 0, 70);
-      continue;
-    }
-    float xv[NK][CPL];
+    yg = load_yg(a, e, lane);
+    const bool ok = s < a.src_limit;
 #pragma unroll
     for (int k = 0; k < NK; ++k)
 #pragma unroll
-      for (int c = 0; c < CPL; ++c) xv[k][c] = x[(s * NK + k) * C + lane + 32 * c];
-    build_yt(b, cg2, a.edge_y, a.gates, e, lane, true);
+      for (int c = 0; c < CPL; ++c) xd[k][c] = ok ? x[(s * NK + k) * C + lane + 32 * c] : 0.f;
+    return ok;
+  };
+  float xv[NK][CPL], yg = 0.f;
+  bool ok = e0 < e1 ? fetch(e0, xv, yg) : true;
+  for (int e = e0; e < e1; ++e) {
+    float xn[NK][CPL], ygn = 0.f;
+    bool okn = true;
+    if (e + 1 < e1) okn = fetch(e + 1, xn, ygn);
+    if (ok) {
+      build_yt(b, cg2, yg, lane, lq);
+      all_paths<CPL, ZPath>(b, xv, z);
+      __syncwarp();
+    } else if (lane == 0) {
+      atomicCAS(a.err, 0, 70);
+    }
 #pragma unroll
-    for (int p = 0; p < NP; ++p)
+    for (int k = 0; k < NK; ++k)
 #pragma unroll
-      for (int m1 = 0; m1 < 2 * L1(p) + 1; ++m1)
-#pragma unroll
-        for (int kk = 0; kk < 2 * L3(p) + 1; ++kk) {
-          const float w = b.yt[qidx(p, m1, kk)];
-#pragma unroll
-          for (int c = 0; c < CPL; ++c) z[zrow(p, kk)][c] = fmaf(xv[KB(L1(p)) + m1][c], w, z[zrow(p, kk)][c]);
-        }
-    __syncwarp();
+      for (int c = 0; c < CPL; ++c) xv[k][c] = xn[k][c];
+    yg = ygn;
+    ok = okn;
   }
 #pragma unroll
   for (int r = 0; r < NZ; ++r)
@@ -135,37 +240,46 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_r_kernel(ConvArgs a, co
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t s = (int64_t)blockIdx.x * CONV_WARPS + warp;
   if (s >= a.N) return;
-  const int C = 32 * CPL;
+  constexpr int C = 32 * CPL;
   EdgeBuf& b = bufs[warp];
+  const LaneQ lq = lane_q(lane);
   float r[NZ][CPL];
 #pragma unroll
   for (int i = 0; i < NZ; ++i)
 #pragma unroll
     for (int c = 0; c < CPL; ++c) r[i][c] = 0.f;
   const int t0 = a.tr_ptr[s], t1 = a.tr_ptr[s + 1];
-  for (int t = t0; t < t1; ++t) {
+  // a receiver not evaluated in this layer carries no gradient
+  auto fetch = [&](int t, float (&gd)[NK][CPL], float& yg) -> bool {
     const int64_t e = a.tr_eid[t];
     const int64_t d = a.dst[e];
-    if (d >= a.dst_limit) continue;  // receiver not evaluated in this layer: no gradient
-    const int deg = a.row_ptr[d + 1] - a.row_ptr[d];
+    yg = load_yg(a, e, lane);
+    const bool on = d < a.dst_limit;
+    const int deg = on ? a.row_ptr[d + 1] - a.row_ptr[d] : 1;
     const float inv = 1.f / (float)(deg > 1 ? deg : 1);
-    float gv[NK][CPL];
 #pragma unroll
     for (int k = 0; k < NK; ++k)
 #pragma unroll
-      for (int c = 0; c < CPL; ++c) gv[k][c] = G[(d * NK + k) * C + lane + 32 * c] * inv;
-    build_yt(b, cg2, a.edge_y, a.gates, e, lane, true);
+      for (int c = 0; c < CPL; ++c) gd[k][c] = on ? G[(d * NK + k) * C + lane + 32 * c] * inv : 0.f;
+    return on;
+  };
+  float gv[NK][CPL], yg = 0.f;
+  bool on = t0 < t1 ? fetch(t0, gv, yg) : false;
+  for (int t = t0; t < t1; ++t) {
+    float gn[NK][CPL], ygn = 0.f;
+    bool onn = false;
+    if (t + 1 < t1) onn = fetch(t + 1, gn, ygn);
+    if (on) {
+      build_yt(b, cg2, yg, lane, lq);
+      all_paths<CPL, RPath>(b, gv, r);
+      __syncwarp();
+    }
 #pragma unroll
-    for (int p = 0; p < NP; ++p)
+    for (int k = 0; k < NK; ++k)
 #pragma unroll
-      for (int m1 = 0; m1 < 2 * L1(p) + 1; ++m1)
-#pragma unroll
-        for (int kk = 0; kk < 2 * L3(p) + 1; ++kk) {
-          const float w = b.yt[qidx(p, m1, kk)];
-#pragma unroll
-          for (int c = 0; c < CPL; ++c) r[rrow(p, m1)][c] = fmaf(gv[KB(L3(p)) + kk][c], w, r[rrow(p, m1)][c]);
-        }
-    __syncwarp();
+      for (int c = 0; c < CPL; ++c) gv[k][c] = gn[k][c];
+    yg = ygn;
+    on = onn;
   }
 #pragma unroll
   for (int i = 0; i < NZ; ++i)

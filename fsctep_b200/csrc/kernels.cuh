@@ -149,14 +149,18 @@ int launch_p5_forward(const ReadoutArgs& a, const float* scalars, float* p5, cud
 int launch_p5_backward(const ReadoutArgs& a, const float* scalars, const float* dp5, float* const* grads,
                        float* dscalars, cudaStream_t st);
 // Tensor-core readout (readout_tc.cu)
+// Fg / dFg (Gram operand and its gradient) are tile-blocked: node n, row r at
+//   (n / 128) * nrows * 128 + r * 128 + n % 128,
+// so one tile's rows are 512-byte lines at compile-time-friendly offsets.
 struct ReadoutTcArgs {
-  int64_t N, n_pad;     // nodes, Fg row stride (multiple of 128)
+  int64_t N, n_pad;     // nodes, padded node count (multiple of 128)
   int nC, S;
-  const float* Fg;      // [9*nC][n_pad] Gram operand, node innermost
+  int64_t nrows;        // Gram operand rows per node
+  const float* Fg;      // [n_pad / 128][nrows][128] Gram operand
   const float* wimg;    // pre-formatted W blocks (hi/lo), forward or backward order
   float* scalars;       // forward output [N][S]
   const float* dscal;   // backward input [N][S]
-  float* dFg;           // backward output [9*nC][n_pad]
+  float* dFg;           // backward output, layout of Fg
   int* err;             // first failing wait site (0 = ok)
   int ngram;            // Gram blocks (rows of block b start at goff[b], m-width 2 gl[b] + 1)
   int goff[4], gl[4];

@@ -154,10 +154,9 @@ __device__ __forceinline__ bool d_ready(uint64_t* bar, uint32_t& phase, int* err
 // After a timed-out wait: bounded wait for the chain still committed to `bar` before the TMEM
 // it writes is released.
 __device__ __forceinline__ void drain(uint64_t* bar, uint32_t phase) {
-  for (uint32_t i = 0; i < tc::kSpinLimit; ++i) {
-    if (tc::mbar_try_wait(bar, phase ^ 1u)) return;
-    __nanosleep(64);
-  }
+  const long long t0 = clock64();
+  while (!tc::mbar_try_wait(bar, phase ^ 1u))
+    if (clock64() - t0 > tc::kWaitCycles) return;
 }
 
 // ------------------------------------------------------------------ forward

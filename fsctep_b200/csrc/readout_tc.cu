@@ -17,9 +17,12 @@
 // through mbarriers with bounded waits.  fp32 accuracy comes from the 3xTF32 split
 // (hi*hi + hi*lo + lo*hi; the W split is precomputed on the host).
 //
-// t is read from Fg, a node-innermost copy of the Gram operand (Fg[row][n], row = l-offset +
-// c*(2l+1) + m, rows in the order of the reference's flat split; built by fg_gather_kernel),
-// so that one warp's 32 nodes read one 128-byte line per (c, m).
+// t is read from Fg, a tile-blocked copy of the Gram operand (node n, row r at
+// (n / 128) * nrows * 128 + r * 128 + n % 128, rows in the order of the reference's flat split,
+// row = l-offset + c*(2l+1) + m; built by fg_gather_kernel): one warp's 32 nodes read one
+// 128-byte line per (c, m), at offsets that are immediates once the block is fixed.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "tc_common.cuh"
@@ -29,42 +32,104 @@ namespace fsc {
 namespace {
 
 constexpr int TILE = 128;
-constexpr int NGEN_WARPS = 8;
-constexpr int THREADS = (NGEN_WARPS + 2) * 32;  // + MMA warp + TMA warp
-constexpr int NSTB = 3;
-
+constexpr int NGEN_WARPS = 16;  // 4 per TMEM lane quadrant
+constexpr int THREADS = (NGEN_WARPS + 2) * 32;  // + MMA warp + producer (bulk copy) warp
+constexpr int NSTB = 3;                          // W block ring
+constexpr int NSTT = 4;                          // d-row chunk ring
+constexpr int NSTC = 2;                          // c-row chunk ring (forward)
+constexpr uint32_t TBYTES = 40u * TILE * 4u;     // one chunk: 8 rows x (2l+1 <= 5) x 128 nodes
+constexpr int NSD = 4;                           // TMEM accumulator slots (MMA runs NSD - 1 blocks ahead)
 
 template <int S>
 struct Smem {
   static constexpr uint32_t BBYTES = 512u * S;  // one W block, hi + lo
-  static constexpr uint32_t BAR_OFF = NSTB * BBYTES;
-  static constexpr uint32_t TOTAL = BAR_OFF + 256;
-  // the forward allocates all 512 TMEM columns: keep it at one CTA per SM through shared memory
-  static constexpr uint32_t TOTAL_FWD = TOTAL > 120u * 1024u ? TOTAL : 120u * 1024u;
+  static constexpr uint32_t T_OFF = NSTB * BBYTES;
+  static constexpr uint32_t C_OFF = T_OFF + NSTT * TBYTES;
+  static constexpr uint32_t BAR_FWD = C_OFF + NSTC * TBYTES;
+  static constexpr uint32_t TOTAL_FWD = BAR_FWD + 256;
 };
 
+// Backward: the MMA forms H for two d-blocks at once (N = 128 pairs runs the tensor core at its
+// full rate; N = 64 reaches ~70 %), so its rings hold W block pairs and 16-row t chunks.
+constexpr int NSTB2 = 2, NSTT2 = 2, NSD2 = 3;
+constexpr uint32_t TBYTES2 = 2 * TBYTES;
+template <int S>
+struct SmemBwd {
+  static constexpr uint32_t BBYTES = 1024u * S;  // two W blocks (128 pairs), hi + lo
+  static constexpr uint32_t T_OFF = NSTB2 * BBYTES;
+  static constexpr uint32_t BAR = T_OFF + NSTT2 * TBYTES2;
+  static constexpr uint32_t TOTAL = BAR + 256;
+};
+
+// Ring-slot wait: slot k % n of use k waits for phase (k / n) & 1 of its barrier.
+__device__ __forceinline__ bool ring_full(uint64_t* bars, int k, int n, int* err, int where) {
+  return tc::mbar_wait(bars + k % n, (k / n) & 1, err, where);
+}
+// A producer's use k of a ring slot first waits for the consumers of use k - n.
+__device__ __forceinline__ bool ring_empty(uint64_t* bars, int k, int n, int* err, int where) {
+  return k < n || tc::mbar_wait(bars + k % n, ((k / n) - 1) & 1, err, where);
+}
+
+// Bulk copy of one chunk (or W block) into a ring slot with its byte count on the slot's barrier.
+__device__ __forceinline__ void put(uint8_t* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  tc::mbar_arrive_expect_tx(bar, bytes);
+  tc::bulk_g2s(dst, src, bytes, bar);
+}
+
+// Every CTA walks the Gram-block rows (b, cb) starting at its own row (and wrapping), so that at
+// any moment the CTAs stream different W blocks: all CTAs reading the same 32 KB block at once
+// would queue on the few L2 slices that hold it.
+struct RowOrder {
+  int rows, r0, nb;
+  __device__ RowOrder(int ngram, int nb_) : rows(ngram * nb_), r0(0), nb(nb_) {
+    r0 = (int)(blockIdx.x % (unsigned)rows);
+  }
+  __device__ __forceinline__ void at(int i, int& b, int& cb) const {
+    const int r = (i + r0) % rows;
+    b = r / nb;
+    cb = r - b * nb;
+  }
+};
+// Index of forward W block (b, cb, db >= cb) in the image (rows of nb - cb blocks).
+__device__ __forceinline__ int fwd_block(int b, int cb, int db, int nb) {
+  return b * (nb * (nb + 1) / 2) + cb * nb - cb * (cb - 1) / 2 + (db - cb);
+}
+
 // ------------------------------------------------------------------ forward
-// Each 64-pair block is accumulated fresh in one of two TMEM accumulators (24 MMAs) and added to
-// per-thread fp32 registers (round-to-nearest) by the generator warps, so the tensor core never
-// carries a long accumulation chain.
+// Roles (one CTA = 128 nodes = the 128 TMEM lanes / MMA rows):
+//  * producer warp: for every block s (Gram block b, c-block cb <= d-block db) bulk-copies the W
+//    block s and the d-block's 8 (2l+1) t rows (one contiguous chunk of the tile-blocked Fg), and
+//    once per (b, cb) the c-block's rows, into shared-memory rings;
+//  * 16 generator warps: thread = node (TMEM lane) and quarter qq of the d-rows; builds its 16
+//    pairs (c, d = 2qq + dd) of the Gram block from shared memory, splits them (3xTF32) into TMEM
+//    and adds output columns [16qq, 16qq + 16) of the previous block's fresh 24-MMA accumulator to
+//    fp32 registers (round-to-nearest), so the tensor core never carries a long accumulation chain;
+//  * MMA warp: 24 tcgen05.mma (A = Gram block in TMEM, B = W block in shared memory) per block.
 template <int S>
 __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   using SM = Smem<S>;
   uint8_t* sB = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::BAR_OFF);
+  const float* sT = reinterpret_cast<const float*>(smem + SM::T_OFF);
+  const float* sC = reinterpret_cast<const float*>(smem + SM::C_OFF);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::BAR_FWD);
   uint64_t* full_B = bars;        // [3]
   uint64_t* empty_B = bars + 3;   // [3]
-  uint64_t* full_A = bars + 6;    // [2]
-  uint64_t* empty_A = bars + 8;   // [2]
-  uint64_t* d_full = bars + 10;   // [2]
-  uint64_t* d_empty = bars + 12;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* full_T = bars + 6;    // [4]
+  uint64_t* empty_T = bars + 10;  // [4]
+  uint64_t* full_C = bars + 14;   // [2]
+  uint64_t* empty_C = bars + 16;  // [2]
+  uint64_t* full_A = bars + 18;   // [2]
+  uint64_t* empty_A = bars + 20;  // [2]
+  uint64_t* d_full = bars + 22;   // [NSD]
+  uint64_t* d_empty = bars + 26;  // [NSD]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 30);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nC = a.nC, nb = nC / 8;
+  const int nb = a.nC / 8;
   const int64_t n0 = (int64_t)blockIdx.x * TILE;
   const int nblk = a.ngram * nb * (nb + 1) / 2;
+  const float* Ftile = a.Fg + (int64_t)blockIdx.x * a.nrows * TILE;
 
   if (warp == NGEN_WARPS) {
     tc::tmem_alloc(tmem_slot, 512);
@@ -75,9 +140,17 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
       tc::mbar_init(full_B + i, 1);
       tc::mbar_init(empty_B + i, 1);
     }
+    for (int i = 0; i < NSTT; ++i) {
+      tc::mbar_init(full_T + i, 1);
+      tc::mbar_init(empty_T + i, NGEN_WARPS);
+    }
     for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(full_C + i, 1);
+      tc::mbar_init(empty_C + i, NGEN_WARPS);
       tc::mbar_init(full_A + i, NGEN_WARPS);
       tc::mbar_init(empty_A + i, 1);
+    }
+    for (int i = 0; i < NSD; ++i) {
       tc::mbar_init(d_full + i, 1);
       tc::mbar_init(d_empty + i, NGEN_WARPS);
     }
@@ -87,86 +160,111 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  auto tD = [&](int st) { return tbase + 64u * st; };                              // cols [0, 128)
-  auto tA = [&](int st, int lo) { return tbase + 128u + 128u * st + 64u * lo; };  // cols [128, 384)
+  auto tD = [&](int st) { return tbase + 64u * st; };                              // cols [0, 256)
+  auto tA = [&](int st, int lo) { return tbase + 256u + 128u * st + 64u * lo; };  // cols [256, 512)
 
   if (warp < NGEN_WARPS) {
     // ---------------- Gram generators + block accumulation
-    const int q4 = warp & 3, h = warp >> 2;
+    const int q4 = warp & 3, qq = warp >> 2;
     const int row = q4 * 32 + lane;
-    const int64_t n = n0 + row;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    const bool has_cols = 32 * h < S;  // this warp half owns output columns [32h, 32h+32)
-    const float* Fg = a.Fg + n;
-    float acc[32];
+    const bool has_cols = 16 * qq < S;  // this warp owns output columns [16qq, 16qq+16)
+    float acc[16];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
     bool ok = true;
+    int s = 0, rr = 0;
     auto flush = [&](int t) {
-      const int dst = t & 1;
-      if (!tc::mbar_wait(d_full + dst, (t >> 1) & 1, a.err, 16)) {
+      const int dst = t % NSD;
+      if (!ring_full(d_full, t, NSD, a.err, 16)) {
         ok = false;
         return;
       }
       tc::tc_fence_after();
       if (has_cols) {
-        uint32_t v[32];
-        tc::tmem_ld32(tD(dst) + lane_off + 32u * h, v);
+        uint32_t v[16];
+        tc::tmem_ld16(tD(dst) + lane_off + 16u * qq, v);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] += __uint_as_float(v[i]);
+        for (int i = 0; i < 16; ++i) acc[i] += __uint_as_float(v[i]);
       }
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(d_empty + dst);
     };
-    int s = 0;
-    for (int b = 0; b < a.ngram && ok; ++b) {
-      const int M = 2 * a.gl[b] + 1, off = a.goff[b];
-      for (int cb = 0; cb < nb && ok; ++cb) {
-        float tcv[4][5];
+    // one Gram block row (b, cb): c-rows from the C ring (held for the row), d-rows of every
+    // db >= cb from the T ring
+    auto gen_row = [&](auto mconst, int cb) {
+      constexpr int M = decltype(mconst)::value;
+      if (!ring_full(full_C, rr, NSTC, a.err, 12)) {
+        ok = false;
+        return;
+      }
+      const float* pc = sC + (rr % NSTC) * (TBYTES / 4) + row;
+      for (int db = cb; db < nb; ++db, ++s) {
+        if (!ring_full(full_T, s, NSTT, a.err, 10)) {
+          ok = false;
+          return;
+        }
+        float tdv[2][M];
+        const float* pt = sT + (s % NSTT) * (TBYTES / 4) + 2 * qq * M * TILE + row;
 #pragma unroll
-        for (int cq = 0; cq < 4; ++cq)
+        for (int dd = 0; dd < 2; ++dd)
 #pragma unroll
-          for (int m = 0; m < 5; ++m)
-            tcv[cq][m] = m < M ? Fg[(int64_t)(off + (8 * cb + 4 * h + cq) * M + m) * a.n_pad] : 0.f;
-        for (int db = cb; db < nb && ok; ++db, ++s) {
-          float tdv[8][5];
+          for (int m = 0; m < M; ++m) tdv[dd][m] = pt[(dd * M + m) * TILE];
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(empty_T + s % NSTT);
+        const int st = s & 1;
+        if (s >= 2 && !tc::mbar_wait(empty_A + st, ((s >> 1) - 1) & 1, a.err, 11)) {
+          ok = false;
+          return;
+        }
+        // pairs (c, d = 2qq + dd) -> A column 16qq + 2c + dd (the forward W images use this order)
+        uint32_t hi[16], lo[16];
 #pragma unroll
-          for (int dq = 0; dq < 8; ++dq)
+        for (int c = 0; c < 8; ++c) {
+          float tc_[M];
 #pragma unroll
-            for (int m = 0; m < 5; ++m)
-              tdv[dq][m] = m < M ? Fg[(int64_t)(off + (8 * db + dq) * M + m) * a.n_pad] : 0.f;
-          const int st = s & 1;
-          if (s >= 2 && !tc::mbar_wait(empty_A + st, ((s >> 1) - 1) & 1, a.err, 11)) {
-            ok = false;
-            break;
+          for (int m = 0; m < M; ++m) tc_[m] = pc[(c * M + m) * TILE];
+#pragma unroll
+          for (int dd = 0; dd < 2; ++dd) {
+            float g = 0.f;
+#pragma unroll
+            for (int m = 0; m < M; ++m) g = fmaf(tc_[m], tdv[dd][m], g);
+            tc::split_tf32(g, hi[2 * c + dd], lo[2 * c + dd]);
           }
-          uint32_t hi[32], lo[32];
-#pragma unroll
-          for (int cq = 0; cq < 4; ++cq)
-#pragma unroll
-            for (int dq = 0; dq < 8; ++dq) {
-              float g = 0.f;
-#pragma unroll
-              for (int m = 0; m < 5; ++m) g = fmaf(tcv[cq][m], tdv[dq][m], g);
-              tc::split_tf32(g, hi[cq * 8 + dq], lo[cq * 8 + dq]);
-            }
-          tc::tmem_st32(tA(st, 0) + lane_off + 32u * h, hi);
-          tc::tmem_st32(tA(st, 1) + lane_off + 32u * h, lo);
-          tc::tmem_wait_st();
-          tc::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(full_A + st);
-          if (s >= 1) flush(s - 1);
+        }
+        tc::tmem_st16(tA(st, 0) + lane_off + 16u * qq, hi);
+        tc::tmem_st16(tA(st, 1) + lane_off + 16u * qq, lo);
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(full_A + st);
+        if (s >= 2) {  // two blocks behind: that chain has long finished
+          flush(s - 2);
+          if (!ok) return;
         }
       }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(empty_C + rr % NSTC);
+      ++rr;
+    };
+    const RowOrder order(a.ngram, nb);
+    for (int i = 0; i < order.rows && ok; ++i) {
+      int b, cb;
+      order.at(i, b, cb);
+      const int M = 2 * a.gl[b] + 1;
+      if (M == 1) gen_row(std::integral_constant<int, 1>{}, cb);
+      else if (M == 3) gen_row(std::integral_constant<int, 3>{}, cb);
+      else gen_row(std::integral_constant<int, 5>{}, cb);
     }
-    if (ok) flush(nblk - 1);
+    for (int t = nblk - 2; t < nblk && ok; ++t)
+      if (t >= 0) flush(t);
+    const int64_t n = n0 + row;
     if (ok && has_cols && n < a.N) {
-      float4* out = reinterpret_cast<float4*>(a.scalars + n * S + 32 * h);
+      float4* out = reinterpret_cast<float4*>(a.scalars + n * S + 16 * qq);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) out[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+      for (int i = 0; i < 4; ++i) out[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
     }
   } else if (warp == NGEN_WARPS) {
     // ---------------- MMA issuer
@@ -174,34 +272,48 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
       constexpr uint32_t idesc = tc::idesc_tf32(TILE, S);
       const uint32_t sB0 = tc::smem_u32(sB);
       for (int s = 0; s < nblk; ++s) {
-        const int bst = s % NSTB, ast = s & 1;
+        const int bst = s % NSTB, ast = s & 1, dst = s % NSD;
         if (!tc::mbar_wait(full_B + bst, (s / NSTB) & 1, a.err, 13)) break;
         if (!tc::mbar_wait(full_A + ast, (s >> 1) & 1, a.err, 14)) break;
-        if (s >= 2 && !tc::mbar_wait(d_empty + ast, ((s >> 1) - 1) & 1, a.err, 17)) break;
+        if (!ring_empty(d_empty, s, NSD, a.err, 17)) break;
         tc::tc_fence_after();
         const uint32_t bhi = sB0 + bst * SM::BBYTES, blo = bhi + SM::BBYTES / 2;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint64_t dh = tc::smem_desc_kmajor(bhi + j * 2 * 16 * S, 16 * S, 128);
           const uint64_t dl = tc::smem_desc_kmajor(blo + j * 2 * 16 * S, 16 * S, 128);
-          tc::mma_tf32_ts(tD(ast), tA(ast, 0) + 8 * j, dh, idesc, j != 0);
-          tc::mma_tf32_ts(tD(ast), tA(ast, 0) + 8 * j, dl, idesc, 1);
-          tc::mma_tf32_ts(tD(ast), tA(ast, 1) + 8 * j, dh, idesc, 1);
+          tc::mma_tf32_ts(tD(dst), tA(ast, 0) + 8 * j, dh, idesc, j != 0);
+          tc::mma_tf32_ts(tD(dst), tA(ast, 0) + 8 * j, dl, idesc, 1);
+          tc::mma_tf32_ts(tD(dst), tA(ast, 1) + 8 * j, dh, idesc, 1);
         }
         tc::mma_commit(empty_A + ast);
         tc::mma_commit(empty_B + bst);
-        tc::mma_commit(d_full + ast);
+        tc::mma_commit(d_full + dst);
       }
     }
   } else {
-    // ---------------- W block producer (bulk TMA)
+    // ---------------- producer: W blocks, d-row and c-row chunks (bulk copies)
     if (lane == 0) {
-      const uint8_t* src = reinterpret_cast<const uint8_t*>(a.wimg);
-      for (int s = 0; s < nblk; ++s) {
-        const int bst = s % NSTB;
-        if (s >= NSTB && !tc::mbar_wait(empty_B + bst, ((s / NSTB) - 1) & 1, a.err, 15)) break;
-        tc::mbar_arrive_expect_tx(full_B + bst, SM::BBYTES);
-        tc::bulk_g2s(sB + bst * SM::BBYTES, src + (size_t)s * SM::BBYTES, SM::BBYTES, full_B + bst);
+      const uint8_t* wsrc = reinterpret_cast<const uint8_t*>(a.wimg);
+      uint8_t* tring = smem + SM::T_OFF;
+      uint8_t* cring = smem + SM::C_OFF;
+      int s = 0;
+      bool ok = true;
+      const RowOrder order(a.ngram, nb);
+      for (int rr = 0; rr < order.rows && ok; ++rr) {
+        int b, cb;
+        order.at(rr, b, cb);
+        const int M = 2 * a.gl[b] + 1, off = a.goff[b];
+        const uint32_t cbytes = 8u * M * TILE * 4u;
+        if (!(ok = ring_empty(empty_C, rr, NSTC, a.err, 18))) break;
+        put(cring + (rr % NSTC) * TBYTES, Ftile + (int64_t)(off + 8 * cb * M) * TILE, cbytes, full_C + rr % NSTC);
+        for (int db = cb; db < nb; ++db, ++s) {
+          if (!(ok = ring_empty(empty_T, s, NSTT, a.err, 19))) break;
+          put(tring + (s % NSTT) * TBYTES, Ftile + (int64_t)(off + 8 * db * M) * TILE, cbytes, full_T + s % NSTT);
+          if (!(ok = ring_empty(empty_B, s, NSTB, a.err, 15))) break;
+          const size_t wb = (size_t)fwd_block(b, cb, db, nb);
+          put(sB + (s % NSTB) * SM::BBYTES, wsrc + wb * SM::BBYTES, SM::BBYTES, full_B + s % NSTB);
+        }
       }
     }
   }
@@ -214,34 +326,47 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
 }
 
 // ------------------------------------------------------------------ backward
+// Roles: the MMA warp forms each 128 x 64 block of H (A = ds split in TMEM, B = W block in shared
+// memory) into one of two TMEM accumulators; the producer streams W blocks and the d-block's t
+// rows; 16 epilogue warps (thread = node, quarter qq of the c-rows: c = 2qq, 2qq + 1) contract
+// the other accumulator with t from shared memory: dt[c][m] += 2 sum_d H[c][d] t[d][m] over all
+// d-blocks of a row.
 template <int S>
 __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  using SM = Smem<S>;
+  using SM = SmemBwd<S>;
   uint8_t* sB = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::BAR_OFF);
-  uint64_t* full_B = bars;       // [3]
-  uint64_t* empty_B = bars + 3;  // [3]
-  uint64_t* d_full = bars + 6;   // [2]
-  uint64_t* d_empty = bars + 8;  // [2]
-  uint64_t* a_ready = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  const float* sT = reinterpret_cast<const float*>(smem + SM::T_OFF);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::BAR);
+  uint64_t* full_B = bars;        // [NSTB2]
+  uint64_t* empty_B = bars + 2;   // [NSTB2]
+  uint64_t* full_T = bars + 4;    // [NSTT2]
+  uint64_t* empty_T = bars + 6;   // [NSTT2]
+  uint64_t* d_full = bars + 8;    // [NSD2]
+  uint64_t* d_empty = bars + 11;  // [NSD2]
+  uint64_t* a_ready = bars + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nC = a.nC, nb = nC / 8;
+  const int nb = a.nC / 8, np = nb / 2;  // d-block pairs per row
   const int64_t n0 = (int64_t)blockIdx.x * TILE;
-  const int nblk = a.ngram * nb * nb;
+  const int ngrp = a.ngram * nb * np;
+  const float* Ftile = a.Fg + (int64_t)blockIdx.x * a.nrows * TILE;
 
   if (warp == NGEN_WARPS) {
-    tc::tmem_alloc(tmem_slot, 256);
+    tc::tmem_alloc(tmem_slot, 512);
     tc::tmem_relinquish();
   }
   if (threadIdx.x == 0) {
-    for (int i = 0; i < NSTB; ++i) {
+    for (int i = 0; i < NSTB2; ++i) {
       tc::mbar_init(full_B + i, 1);
       tc::mbar_init(empty_B + i, 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NSTT2; ++i) {
+      tc::mbar_init(full_T + i, 1);
+      tc::mbar_init(empty_T + i, NGEN_WARPS);
+    }
+    for (int i = 0; i < NSD2; ++i) {
       tc::mbar_init(d_full + i, 1);
       tc::mbar_init(d_empty + i, NGEN_WARPS);
     }
@@ -253,93 +378,106 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   const uint32_t tAhi = tbase, tAlo = tbase + 64u;                  // ds split, cols [0, 128)
-  auto tD = [&](int st) { return tbase + 128u + 64u * st; };         // H blocks, cols [128, 256)
+  auto tD = [&](int st) { return tbase + 128u + 128u * st; };        // H block pairs, cols [128, 512)
 
   if (warp < NGEN_WARPS) {
-    const int q4 = warp & 3, h = warp >> 2;
+    const int q4 = warp & 3, qq = warp >> 2;
     const int row = q4 * 32 + lane;
     const int64_t n = n0 + row;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    // A operand: ds (128 x S), split into hi / lo; warp half h stores columns [32h, 32h+32)
-    if (32 * h < S) {
-      uint32_t hi[32], lo[32];
+    // A operand: ds (128 x S), split into hi / lo; warp quarter qq stores columns [16qq, 16qq+16)
+    if (16 * qq < S) {
+      uint32_t hi[16], lo[16];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float v = n < a.N ? a.dscal[n * S + 32 * h + i] : 0.f;
+      for (int i = 0; i < 16; ++i) {
+        const float v = n < a.N ? a.dscal[n * S + 16 * qq + i] : 0.f;
         tc::split_tf32(v, hi[i], lo[i]);
       }
-      tc::tmem_st32(tAhi + lane_off + 32u * h, hi);
-      tc::tmem_st32(tAlo + lane_off + 32u * h, lo);
+      tc::tmem_st16(tAhi + lane_off + 16u * qq, hi);
+      tc::tmem_st16(tAlo + lane_off + 16u * qq, lo);
       tc::tmem_wait_st();
     }
     tc::tc_fence_before();
     __syncwarp();
     if (lane == 0) tc::mbar_arrive(a_ready);
-    // epilogue over blocks
-    const float* Fg = a.Fg + n;
-    float* dFg = a.dFg + n;
+    // epilogue over block pairs
+    float* dFt = a.dFg + (int64_t)blockIdx.x * a.nrows * TILE + row;
     int s = 0;
     bool ok = true;
-    for (int b = 0; b < a.ngram && ok; ++b) {
-      const int M = 2 * a.gl[b] + 1, off = a.goff[b];
-      for (int cb = 0; cb < nb && ok; ++cb) {
-        float acc[4][5];
+    auto epi_row = [&](auto mconst, int off, int cb) {
+      constexpr int M = decltype(mconst)::value;
+      float acc[2][M];
 #pragma unroll
-        for (int cq = 0; cq < 4; ++cq)
+      for (int cq = 0; cq < 2; ++cq)
 #pragma unroll
-          for (int m = 0; m < 5; ++m) acc[cq][m] = 0.f;
-        for (int db = 0; db < nb; ++db, ++s) {
-          float tdv[8][5];
-#pragma unroll
-          for (int dq = 0; dq < 8; ++dq)
-#pragma unroll
-            for (int m = 0; m < 5; ++m)
-              tdv[dq][m] = m < M ? Fg[(int64_t)(off + (8 * db + dq) * M + m) * a.n_pad] : 0.f;
-          const int st = s & 1;
-          if (!tc::mbar_wait(d_full + st, (s >> 1) & 1, a.err, 21)) {
-            ok = false;
-            break;
-          }
-          tc::tc_fence_after();
-          uint32_t hv[32];
-          tc::tmem_ld32(tD(st) + lane_off + 32u * h, hv);
-          tc::tmem_wait_ld();
-          tc::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(d_empty + st);
-#pragma unroll
-          for (int cq = 0; cq < 4; ++cq)
-#pragma unroll
-            for (int dq = 0; dq < 8; ++dq) {
-              const float hcd = __uint_as_float(hv[cq * 8 + dq]);
-#pragma unroll
-              for (int m = 0; m < 5; ++m) acc[cq][m] = fmaf(hcd, tdv[dq][m], acc[cq][m]);
-            }
+        for (int m = 0; m < M; ++m) acc[cq][m] = 0.f;
+      for (int dp = 0; dp < np; ++dp, ++s) {
+        if (!ring_full(full_T, s, NSTT2, a.err, 20)) {
+          ok = false;
+          return;
         }
-        if (!ok) break;
+        const int st = s % NSD2;
+        if (!ring_full(d_full, s, NSD2, a.err, 21)) {
+          ok = false;
+          return;
+        }
+        tc::tc_fence_after();
+        // H[c = 2qq + cq][d] of the pair's first / second d-block at columns 16qq + 8cq + dq / + 64
+        uint32_t hv[2][16];
+        tc::tmem_ld16(tD(st) + lane_off + 16u * qq, hv[0]);
+        tc::tmem_ld16(tD(st) + lane_off + 64u + 16u * qq, hv[1]);
+        const float* pt = sT + (s % NSTT2) * (TBYTES2 / 4) + row;
 #pragma unroll
-        for (int cq = 0; cq < 4; ++cq)
+        for (int dq = 0; dq < 16; ++dq) {
+          float td[M];
 #pragma unroll
-          for (int m = 0; m < 5; ++m)
-            if (m < M) dFg[(int64_t)(off + (8 * cb + 4 * h + cq) * M + m) * a.n_pad] = 2.f * acc[cq][m];
+          for (int m = 0; m < M; ++m) td[m] = pt[(dq * M + m) * TILE];
+          if (dq == 0) tc::tmem_wait_ld();
+#pragma unroll
+          for (int cq = 0; cq < 2; ++cq) {
+            const float hcd = __uint_as_float(hv[dq >> 3][cq * 8 + (dq & 7)]);
+#pragma unroll
+            for (int m = 0; m < M; ++m) acc[cq][m] = fmaf(hcd, td[m], acc[cq][m]);
+          }
+        }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          tc::mbar_arrive(d_empty + st);
+          tc::mbar_arrive(empty_T + s % NSTT2);
+        }
       }
+      float* pd = dFt + (int64_t)(off + (8 * cb + 2 * qq) * M) * TILE;
+#pragma unroll
+      for (int cq = 0; cq < 2; ++cq)
+#pragma unroll
+        for (int m = 0; m < M; ++m) pd[(cq * M + m) * TILE] = 2.f * acc[cq][m];
+    };
+    const RowOrder order(a.ngram, nb);
+    for (int i = 0; i < order.rows && ok; ++i) {
+      int b, cb;
+      order.at(i, b, cb);
+      const int M = 2 * a.gl[b] + 1, off = a.goff[b];
+      if (M == 1) epi_row(std::integral_constant<int, 1>{}, off, cb);
+      else if (M == 3) epi_row(std::integral_constant<int, 3>{}, off, cb);
+      else epi_row(std::integral_constant<int, 5>{}, off, cb);
     }
   } else if (warp == NGEN_WARPS) {
     if (lane == 0) {
-      constexpr uint32_t idesc = tc::idesc_tf32(TILE, 64);
+      constexpr uint32_t idesc = tc::idesc_tf32(TILE, 128);
       const uint32_t sB0 = tc::smem_u32(sB);
       bool ok = tc::mbar_wait(a_ready, 0, a.err, 22);
       tc::tc_fence_after();
-      for (int s = 0; s < nblk && ok; ++s) {
-        const int bst = s % NSTB, dst = s & 1;
-        if (!tc::mbar_wait(full_B + bst, (s / NSTB) & 1, a.err, 23)) break;
-        if (s >= 2 && !tc::mbar_wait(d_empty + dst, ((s >> 1) - 1) & 1, a.err, 24)) break;
+      for (int s = 0; s < ngrp && ok; ++s) {
+        const int bst = s % NSTB2, dst = s % NSD2;
+        if (!ring_full(full_B, s, NSTB2, a.err, 23)) break;
+        if (!ring_empty(d_empty, s, NSD2, a.err, 24)) break;
         tc::tc_fence_after();
         const uint32_t bhi = sB0 + bst * SM::BBYTES, blo = bhi + SM::BBYTES / 2;
 #pragma unroll
         for (int j = 0; j < S / 8; ++j) {
-          const uint64_t dh = tc::smem_desc_kmajor(bhi + j * 2 * 16 * 64, 16 * 64, 128);
-          const uint64_t dl = tc::smem_desc_kmajor(blo + j * 2 * 16 * 64, 16 * 64, 128);
+          const uint64_t dh = tc::smem_desc_kmajor(bhi + j * 2 * 16 * 128, 16 * 128, 128);
+          const uint64_t dl = tc::smem_desc_kmajor(blo + j * 2 * 16 * 128, 16 * 128, 128);
           tc::mma_tf32_ts(tD(dst), tAhi + 8 * j, dh, idesc, j != 0);
           tc::mma_tf32_ts(tD(dst), tAhi + 8 * j, dl, idesc, 1);
           tc::mma_tf32_ts(tD(dst), tAlo + 8 * j, dh, idesc, 1);
@@ -349,13 +487,25 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
       }
     }
   } else {
+    // ---------------- producer: W block pairs and 16-row t chunks
     if (lane == 0) {
-      const uint8_t* src = reinterpret_cast<const uint8_t*>(a.wimg);
-      for (int s = 0; s < nblk; ++s) {
-        const int bst = s % NSTB;
-        if (s >= NSTB && !tc::mbar_wait(empty_B + bst, ((s / NSTB) - 1) & 1, a.err, 25)) break;
-        tc::mbar_arrive_expect_tx(full_B + bst, SM::BBYTES);
-        tc::bulk_g2s(sB + bst * SM::BBYTES, src + (size_t)s * SM::BBYTES, SM::BBYTES, full_B + bst);
+      const uint8_t* wsrc = reinterpret_cast<const uint8_t*>(a.wimg);
+      uint8_t* tring = smem + SM::T_OFF;
+      int s = 0;
+      bool ok = true;
+      const RowOrder order(a.ngram, nb);
+      for (int rr = 0; rr < order.rows && ok; ++rr) {
+        int b, cb;
+        order.at(rr, b, cb);
+        const int M = 2 * a.gl[b] + 1, off = a.goff[b];
+        const uint32_t cbytes = 16u * M * TILE * 4u;
+        for (int dp = 0; dp < np; ++dp, ++s) {
+          if (!(ok = ring_empty(empty_T, s, NSTT2, a.err, 26))) break;
+          put(tring + (s % NSTT2) * TBYTES2, Ftile + (int64_t)(off + 16 * dp * M) * TILE, cbytes, full_T + s % NSTT2);
+          if (!(ok = ring_empty(empty_B, s, NSTB2, a.err, 25))) break;
+          const size_t wg = (size_t)(b * nb + cb) * np + dp;
+          put(sB + (s % NSTB2) * SM::BBYTES, wsrc + wg * SM::BBYTES, SM::BBYTES, full_B + s % NSTB2);
+        }
       }
     }
   }
@@ -363,13 +513,17 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
   __syncthreads();
   if (warp == NGEN_WARPS) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tbase, 256);
+    tc::tmem_dealloc(tbase, 512);
   }
 }
 
 // ------------------------------------------------------------------ Fg gather / scatter
 // Fg[r][n] = feats[layer(r)][n][kc(r)] via xinv (storage -> row); tile of 32 nodes x one layer.
 constexpr int FG_NODES = 32;
+
+__device__ __forceinline__ int64_t fg_index(int64_t r, int64_t n, int64_t nrows) {
+  return (n / TILE) * nrows * TILE + r * TILE + (n % TILE);
+}
 
 __global__ void fg_gather_kernel(FgArgs a) {
   extern __shared__ float tile[];  // [FG_NODES][9C + 1]
@@ -386,7 +540,7 @@ __global__ void fg_gather_kernel(FgArgs a) {
   const int32_t* inv = a.xinv + (int64_t)layer * W;
   for (int i = threadIdx.x; i < FG_NODES * W; i += blockDim.x) {
     const int kc = i / FG_NODES, nl = i - kc * FG_NODES;
-    a.Fg[(int64_t)inv[kc] * a.n_pad + n0 + nl] = tile[nl * (W + 1) + kc];
+    a.Fg[fg_index(inv[kc], n0 + nl, a.nrows)] = tile[nl * (W + 1) + kc];
   }
 }
 
@@ -399,7 +553,7 @@ __global__ void fg_scatter_add_kernel(FgArgs a) {
   const int32_t* inv = a.xinv + (int64_t)layer * W;
   for (int i = threadIdx.x; i < FG_NODES * W; i += blockDim.x) {
     const int kc = i / FG_NODES, nl = i - kc * FG_NODES;
-    tile[nl * (W + 1) + kc] = a.dFg[(int64_t)inv[kc] * a.n_pad + n0 + nl];
+    tile[nl * (W + 1) + kc] = a.dFg[fg_index(inv[kc], n0 + nl, a.nrows)];
   }
   __syncthreads();
   float* dst = a.grads[layer];
@@ -419,7 +573,7 @@ int launch_fwd(const ReadoutTcArgs& a, cudaStream_t st) {
 }
 template <int S>
 int launch_bwd(const ReadoutTcArgs& a, cudaStream_t st) {
-  const int sm = Smem<S>::TOTAL;
+  const int sm = SmemBwd<S>::TOTAL;
   cudaFuncSetAttribute(readout_bwd_tc_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
   readout_bwd_tc_kernel<S><<<(unsigned)ceil_div(a.N, TILE), THREADS, sm, st>>>(a);
   return check_launch("readout_bwd_tc_kernel");

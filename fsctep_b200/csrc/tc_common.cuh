@@ -1,5 +1,5 @@
 // Thin wrappers over the sm_100a PTX used by the tensor-core kernels (tcgen05, TMEM, mbarrier,
-// bulk async copies).  Every wait is bounded: after kSpinLimit polls it records `where` in the
+// bulk async copies).  Every wait is bounded: after ~1 s of polling it records `where` in the
 // kernel's error word and returns false, so a broken pipeline ends the kernel with an error
 // status instead of hanging the GPU.
 #pragma once
@@ -10,7 +10,7 @@
 namespace fsc {
 namespace tc {
 
-constexpr uint32_t kSpinLimit = 1u << 26;  // ~0.1-1 s of polling
+constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at the B200 boost clock
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -46,11 +46,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait; on timeout writes `where` into *err (first writer wins) and returns false.
+// try_wait itself parks the thread in hardware until the phase completes or a short time limit
+// passes, so the loop wakes as soon as the barrier flips (a software sleep between polls would
+// add its whole granularity to every pipeline hand-off).  Bounded by ~kWaitCycles SM clocks.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int where) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (i > 64) __nanosleep(32);
-    if ((i & 1023) == 1023 && *(volatile int*)err != 0) return false;  // another role gave up
+    if ((i & 255) == 0) {
+      if (*(volatile int*)err != 0) return false;  // another role gave up
+      if (clock64() - t0 > kWaitCycles) break;
+    }
   }
   atomicCAS(err, 0, where);
   return false;
@@ -116,6 +123,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* v) {
         "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
         "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
         "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr)
       : "memory");
 }

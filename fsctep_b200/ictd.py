@@ -139,13 +139,17 @@ def readout_images(W_read, C: int, nint: int, ls=(0, 1, 2)):
         S = Wr.shape[0]
         Ws = 0.5 * (Wr + Wr.transpose(1, 2))
         blk = Ws.reshape(S, nb, 8, nb, 8).permute(1, 3, 0, 2, 4).reshape(nb, nb, S, 64)  # [cb][db][o][pair]
-        # forward: cb <= db, x2 off the diagonal, image [pair/4][o][pair%4]
+        # forward: cb <= db, x2 off the diagonal, pairs reordered (c, d = 2qq + dd) -> 16qq + 2c + dd
+        # (the generator thread of quarter qq owns d-rows 2qq, 2qq+1), image [pair/4][o][pair%4]
         f = blk[iu[0], iu[1]] * torch.where(iu[0] == iu[1], 1.0, 2.0).to(blk)[:, None, None]
+        f = f.reshape(-1, S, 8, 4, 2).permute(0, 1, 3, 2, 4).reshape(-1, S, 64)
         f = f.reshape(-1, S, 16, 4).permute(0, 2, 1, 3)
         hi, lo = tf32_split(f)
         fwd.append(torch.stack([hi, lo], dim=1).reshape(-1))
-        # backward: all blocks, image [o/4][pair][o%4] of Ws
-        b = blk.reshape(nb * nb, S, 64).transpose(1, 2).reshape(nb * nb, 64, S // 4, 4).permute(0, 2, 1, 3)
+        # backward: all blocks in pairs of d-blocks (db even, db + 1) -> N = 128 pairs per MMA,
+        # image [o/4][pair of the two blocks][o%4] of Ws
+        b = blk.reshape(nb, nb // 2, 2, S, 64).permute(0, 1, 3, 2, 4).reshape(nb * nb // 2, S, 128)
+        b = b.transpose(1, 2).reshape(nb * nb // 2, 128, S // 4, 4).permute(0, 2, 1, 3)
         hi, lo = tf32_split(b)
         bwd.append(torch.stack([hi, lo], dim=1).reshape(-1))
     return torch.cat(fwd), torch.cat(bwd)
