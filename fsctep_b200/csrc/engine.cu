@@ -81,6 +81,7 @@ struct Plan {
   int64_t n_pad;
   float* Fg;
   float* dFg;
+  float* gmax;
   int* err;
 };
 
@@ -166,8 +167,9 @@ void layout(Plan& p, Arena& ar, const fsc_ictd_config* cfg, int64_t N, int64_t E
     p.chunkbuf = nullptr;
     p.Fg = ar.take<float>(p.nrows * p.n_pad);
     p.dFg = ar.take<float>(p.nrows * p.n_pad);
+    p.gmax = ar.take<float>(4 * p.n_pad);
   } else {
-    p.Fg = p.dFg = nullptr;
+    p.Fg = p.dFg = p.gmax = nullptr;
     p.chunkbuf = ar.take<float>(p.chunk * std::max<int64_t>(p.npairs, (int64_t)p.nC * p.nC));
   }
 }
@@ -185,6 +187,10 @@ FgArgs fg_args(const Plan& p, const fsc_ictd_weights* w) {
   f.xinv = w->xinv;
   f.Fg = p.Fg;
   f.dFg = p.dFg;
+  f.gmax = p.gmax;
+  for (int l = 0; l < 3; ++l) f.lblock[l] = -1;
+  for (int b = 0; b < p.ngram; ++b)
+    if (!(p.o3 && b == 1)) f.lblock[p.gl[b]] = b;  // o3: block 1 is the zero 1e block
   f.nrows = p.nrows;
   return f;
 }
@@ -197,6 +203,7 @@ ReadoutTcArgs tc_args(const Plan& p, const float* wimg) {
   r.nC = p.nC;
   r.S = p.S;
   r.Fg = p.Fg;
+  r.gmax = p.gmax;
   r.wimg = wimg;
   r.scalars = p.scalars;
   r.dscal = p.dscalars;
@@ -325,6 +332,8 @@ int forward(Ctx& c) {
     // o3: the Gram operand rows of the (zero) 1e block have no storage and stay zero
     if (p.o3 && cudaMemsetAsync(p.Fg, 0, sizeof(float) * p.nrows * p.n_pad, st) != cudaSuccess)
       return fail(FSC_ERR_CUDA, "memset Fg");
+    if (cudaMemsetAsync(p.gmax, 0, sizeof(float) * p.ngram * p.n_pad, st) != cudaSuccess)
+      return fail(FSC_ERR_CUDA, "memset gmax");
     FSC_TRY(launch_fg_gather(fg_args(p, w), st));
     FSC_TRY(launch_readout_fwd_tc(tc_args(p, w->wimg_fwd), st));
   }

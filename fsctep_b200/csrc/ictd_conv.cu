@@ -124,6 +124,19 @@ __device__ __forceinline__ void load_cg2(float* cg2, const float* tables) {
   for (int i = threadIdx.x; i < NQ * 5; i += blockDim.x) cg2[i] = tables[TAB_CG2 + i];
 }
 
+// acc[c] += x[c] * w over this lane's channels; two channels go through one packed fp32 FMA.
+template <int CPL>
+__device__ __forceinline__ void fma_ch(const float (&x)[CPL], float w, float (&acc)[CPL]) {
+  if constexpr (CPL == 2) {
+    const float2 t = __ffma2_rn(make_float2(x[0], x[1]), make_float2(w, w), make_float2(acc[0], acc[1]));
+    acc[0] = t.x;
+    acc[1] = t.y;
+  } else {
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) acc[c] = fmaf(x[c], w, acc[c]);
+  }
+}
+
 template <int P, int CPL>
 __device__ __forceinline__ void z_path(const EdgeBuf& b, const float (&xv)[NK][CPL], float (&z)[NZ][CPL]) {
   float w[28];
@@ -132,10 +145,7 @@ __device__ __forceinline__ void z_path(const EdgeBuf& b, const float (&xv)[NK][C
 #pragma unroll
   for (int m1 = 0; m1 < 2 * L1(P) + 1; ++m1)
 #pragma unroll
-    for (int kk = 0; kk < n3; ++kk)
-#pragma unroll
-      for (int c = 0; c < CPL; ++c)
-        z[zrow(P, kk)][c] = fmaf(xv[KB(L1(P)) + m1][c], w[m1 * n3 + kk], z[zrow(P, kk)][c]);
+    for (int kk = 0; kk < n3; ++kk) fma_ch<CPL>(xv[KB(L1(P)) + m1], w[m1 * n3 + kk], z[zrow(P, kk)]);
 }
 
 template <int P, int CPL>
@@ -146,10 +156,7 @@ __device__ __forceinline__ void r_path(const EdgeBuf& b, const float (&gv)[NK][C
 #pragma unroll
   for (int m1 = 0; m1 < 2 * L1(P) + 1; ++m1)
 #pragma unroll
-    for (int kk = 0; kk < n3; ++kk)
-#pragma unroll
-      for (int c = 0; c < CPL; ++c)
-        r[rrow(P, m1)][c] = fmaf(gv[KB(L3(P)) + kk][c], w[m1 * n3 + kk], r[rrow(P, m1)][c]);
+    for (int kk = 0; kk < n3; ++kk) fma_ch<CPL>(gv[KB(L3(P)) + kk], w[m1 * n3 + kk], r[rrow(P, m1)]);
 }
 
 template <int CPL, template <int, int> class F, typename... T>

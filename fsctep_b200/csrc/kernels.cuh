@@ -161,6 +161,7 @@ struct ReadoutTcArgs {
   float* scalars;       // forward output [N][S]
   const float* dscal;   // backward input [N][S]
   float* dFg;           // backward output, layout of Fg
+  const float* gmax;    // [ngram][n_pad] max_c |t_c|^2 per node and Gram block (fp16 range scaling)
   int* err;             // first failing wait site (0 = ok)
   int ngram;            // Gram blocks (rows of block b start at goff[b], m-width 2 gl[b] + 1)
   int goff[4], gl[4];
@@ -178,6 +179,8 @@ struct FgArgs {
   float* Fg;
   const float* dFg;
   int64_t nrows;        // Gram operand rows
+  float* gmax;          // gather: [ngram][n_pad] max over c of sum_m t[c][m]^2 (zeroed by the caller)
+  int lblock[3];        // Gram block of the features with l = 0, 1, 2 (-1: none)
 };
 int launch_fg_gather(const FgArgs& a, cudaStream_t st);
 int launch_fg_scatter_add(const FgArgs& a, cudaStream_t st);

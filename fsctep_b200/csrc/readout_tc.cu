@@ -5,22 +5,26 @@
 // (pure_cartesian_ictd_layers_full.py:990-1000 and its adjoint; Ws = (W_read + W_read^T)/2/sqrt(2l+1)).
 //
 // The (c, d) plane is cut into 8x8 blocks of 64 pairs.  One CTA owns 128 nodes (= the 128 TMEM
-// lanes / MMA rows):
-//  * forward, per block (c-block <= d-block): 8 generator warps build the 128 x 64 Gram block
-//    on CUDA cores straight into TMEM (thread = node = TMEM lane) and an elected thread issues
-//    tcgen05.mma with A from TMEM and the pre-formatted W block (doubled off the diagonal) from
-//    shared memory, accumulating the 128 x S scalars in TMEM;
-//  * backward, per block (all c-, d-blocks): tcgen05.mma forms the 128 x 64 block of H from ds
-//    (in TMEM) and the W block (shared memory) into one of two TMEM accumulators while the 8
-//    epilogue warps contract the other with t on CUDA cores.
-// W blocks are streamed by 1-D bulk TMA into a 3-stage shared-memory ring; all hand-offs go
-// through mbarriers with bounded waits.  fp32 accuracy comes from the 3xTF32 split
-// (hi*hi + hi*lo + lo*hi; the W split is precomputed on the host).
+// lanes / MMA rows) and has a producer warp (bulk copies of W blocks and of the t rows a block
+// needs into shared-memory rings), an MMA warp and 16 generator / epilogue warps:
+//  * forward, per block (c-block <= d-block): the generator warps build the 128 x 64 Gram block on
+//    CUDA cores from shared memory straight into TMEM and the MMA warp multiplies it with the W
+//    block (doubled off the diagonal) into one of four TMEM accumulators, which the generators
+//    add to fp32 registers a few blocks later;
+//  * backward, per pair of d-blocks: the MMA warp forms the 128 x 128 block of H from ds (TMEM)
+//    and two W blocks (N = 128 runs the tensor core at full rate) while the epilogue warps
+//    contract an earlier one with t.
+// Precision: the MMAs are kind::f16 on a two-term split, hi = fp16(x s), lo = fp16(x s - hi),
+// summing hi*hi + hi*lo + lo*hi (~22 significant bits, like 3xTF32, at twice the K per
+// instruction).  s is a power of two per node (from the Gram bound max_c |t_c|^2, or max |ds|)
+// and per W image (host), so the range fits fp16 and unscaling is exact.  Products accumulate in
+// fp32; every block is a fresh 12-MMA chain and the block sums are added in fp32 registers.
+// All hand-offs go through mbarriers with bounded waits.
 //
 // t is read from Fg, a tile-blocked copy of the Gram operand (node n, row r at
 // (n / 128) * nrows * 128 + r * 128 + n % 128, rows in the order of the reference's flat split,
-// row = l-offset + c*(2l+1) + m; built by fg_gather_kernel): one warp's 32 nodes read one
-// 128-byte line per (c, m), at offsets that are immediates once the block is fixed.
+// row = l-offset + c*(2l+1) + m; built by fg_gather_kernel): the rows one block needs are one
+// contiguous chunk, moved by a single bulk copy.
 #include <type_traits>
 
 #include "common.cuh"
@@ -40,9 +44,13 @@ constexpr int NSTC = 2;                          // c-row chunk ring (forward)
 constexpr uint32_t TBYTES = 40u * TILE * 4u;     // one chunk: 8 rows x (2l+1 <= 5) x 128 nodes
 constexpr int NSD = 4;                           // TMEM accumulator slots (MMA runs NSD - 1 blocks ahead)
 
+// W images: a 64-byte header (float 0 = inverse of the power-of-two range scale applied to W),
+// then fp16 hi / lo planes per block.
+constexpr uint32_t WHEADER = 64u;
+
 template <int S>
 struct Smem {
-  static constexpr uint32_t BBYTES = 512u * S;  // one W block, hi + lo
+  static constexpr uint32_t BBYTES = 256u * S;  // one W block (64 pairs x S), fp16 hi + lo
   static constexpr uint32_t T_OFF = NSTB * BBYTES;
   static constexpr uint32_t C_OFF = T_OFF + NSTT * TBYTES;
   static constexpr uint32_t BAR_FWD = C_OFF + NSTC * TBYTES;
@@ -55,7 +63,7 @@ constexpr int NSTB2 = 2, NSTT2 = 2, NSD2 = 3;
 constexpr uint32_t TBYTES2 = 2 * TBYTES;
 template <int S>
 struct SmemBwd {
-  static constexpr uint32_t BBYTES = 1024u * S;  // two W blocks (128 pairs), hi + lo
+  static constexpr uint32_t BBYTES = 512u * S;  // two W blocks (128 pairs x S), fp16 hi + lo
   static constexpr uint32_t T_OFF = NSTB2 * BBYTES;
   static constexpr uint32_t BAR = T_OFF + NSTT2 * TBYTES2;
   static constexpr uint32_t TOTAL = BAR + 256;
@@ -101,10 +109,13 @@ __device__ __forceinline__ int fwd_block(int b, int cb, int db, int nb) {
 //    block s and the d-block's 8 (2l+1) t rows (one contiguous chunk of the tile-blocked Fg), and
 //    once per (b, cb) the c-block's rows, into shared-memory rings;
 //  * 16 generator warps: thread = node (TMEM lane) and quarter qq of the d-rows; builds its 16
-//    pairs (c, d = 2qq + dd) of the Gram block from shared memory, splits them (3xTF32) into TMEM
-//    and adds output columns [16qq, 16qq + 16) of the previous block's fresh 24-MMA accumulator to
-//    fp32 registers (round-to-nearest), so the tensor core never carries a long accumulation chain;
-//  * MMA warp: 24 tcgen05.mma (A = Gram block in TMEM, B = W block in shared memory) per block.
+//    pairs (c, d = 2qq + dd) of the Gram block from shared memory, scales them by the node's
+//    power-of-two range factor (from gmax) and splits them into fp16 hi + lo in TMEM; adds output
+//    columns [16qq, 16qq + 16) of an earlier block's fresh 12-MMA accumulator, unscaled (exact
+//    powers of two), to fp32 registers, so the tensor core never carries a long accumulation chain;
+//  * MMA warp: 12 tcgen05.mma kind::f16 (hi*hi + hi*lo + lo*hi over 4 K=16 steps; A = Gram block
+//    in TMEM, B = W block in shared memory) per block.  kind::f16 moves K = 16 per instruction,
+//    twice the K of kind::tf32 at the same instruction cost, with the same ~22-bit products.
 template <int S>
 __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -160,8 +171,9 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  auto tD = [&](int st) { return tbase + 64u * st; };                              // cols [0, 256)
-  auto tA = [&](int st, int lo) { return tbase + 256u + 128u * st + 64u * lo; };  // cols [256, 512)
+  auto tD = [&](int st) { return tbase + 64u * st; };                             // cols [0, 256)
+  auto tA = [&](int st, int lo) { return tbase + 256u + 64u * st + 32u * lo; };  // cols [256, 384)
+  const float w_inv = a.wimg[0];
 
   if (warp < NGEN_WARPS) {
     // ---------------- Gram generators + block accumulation
@@ -174,6 +186,10 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
     for (int i = 0; i < 16; ++i) acc[i] = 0.f;
     bool ok = true;
     int s = 0, rr = 0;
+    const int64_t n = n0 + row;
+    // unscale factor of the rows in flight: rows start at blocks r_start[0] > [1] > [2]
+    int r_start[3] = {0, 0, 0};
+    float r_inv[3] = {1.f, 1.f, 1.f};
     auto flush = [&](int t) {
       const int dst = t % NSD;
       if (!ring_full(d_full, t, NSD, a.err, 16)) {
@@ -182,11 +198,12 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
       }
       tc::tc_fence_after();
       if (has_cols) {
+        const float inv = t >= r_start[0] ? r_inv[0] : (t >= r_start[1] ? r_inv[1] : r_inv[2]);
         uint32_t v[16];
         tc::tmem_ld16(tD(dst) + lane_off + 16u * qq, v);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] += __uint_as_float(v[i]);
+        for (int i = 0; i < 16; ++i) acc[i] = fmaf(__uint_as_float(v[i]), inv, acc[i]);
       }
       tc::tc_fence_before();
       __syncwarp();
@@ -194,8 +211,15 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
     };
     // one Gram block row (b, cb): c-rows from the C ring (held for the row), d-rows of every
     // db >= cb from the T ring
-    auto gen_row = [&](auto mconst, int cb) {
+    auto gen_row = [&](auto mconst, int b, int cb) {
       constexpr int M = decltype(mconst)::value;
+      const float scale = tc::f16_range_scale(a.gmax[(int64_t)b * a.n_pad + n]);
+      r_start[2] = r_start[1];
+      r_inv[2] = r_inv[1];
+      r_start[1] = r_start[0];
+      r_inv[1] = r_inv[0];
+      r_start[0] = s;
+      r_inv[0] = w_inv / scale;
       if (!ring_full(full_C, rr, NSTC, a.err, 12)) {
         ok = false;
         return;
@@ -219,23 +243,24 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
           ok = false;
           return;
         }
-        // pairs (c, d = 2qq + dd) -> A column 16qq + 2c + dd (the forward W images use this order)
-        uint32_t hi[16], lo[16];
+        // pairs (c, d = 2qq + dd) -> A element 16qq + 2c + dd (the forward W images use this
+        // order), fp16 packed two per TMEM column: column 8qq + c
+        uint32_t hi[8], lo[8];
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           float tc_[M];
 #pragma unroll
           for (int m = 0; m < M; ++m) tc_[m] = pc[(c * M + m) * TILE];
+          float g0 = 0.f, g1 = 0.f;
 #pragma unroll
-          for (int dd = 0; dd < 2; ++dd) {
-            float g = 0.f;
-#pragma unroll
-            for (int m = 0; m < M; ++m) g = fmaf(tc_[m], tdv[dd][m], g);
-            tc::split_tf32(g, hi[2 * c + dd], lo[2 * c + dd]);
+          for (int m = 0; m < M; ++m) {
+            g0 = fmaf(tc_[m], tdv[0][m], g0);
+            g1 = fmaf(tc_[m], tdv[1][m], g1);
           }
+          tc::split_f16x2(g0 * scale, g1 * scale, hi[c], lo[c]);
         }
-        tc::tmem_st16(tA(st, 0) + lane_off + 16u * qq, hi);
-        tc::tmem_st16(tA(st, 1) + lane_off + 16u * qq, lo);
+        tc::tmem_st8(tA(st, 0) + lane_off + 8u * qq, hi);
+        tc::tmem_st8(tA(st, 1) + lane_off + 8u * qq, lo);
         tc::tmem_wait_st();
         tc::tc_fence_before();
         __syncwarp();
@@ -254,13 +279,12 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
       int b, cb;
       order.at(i, b, cb);
       const int M = 2 * a.gl[b] + 1;
-      if (M == 1) gen_row(std::integral_constant<int, 1>{}, cb);
-      else if (M == 3) gen_row(std::integral_constant<int, 3>{}, cb);
-      else gen_row(std::integral_constant<int, 5>{}, cb);
+      if (M == 1) gen_row(std::integral_constant<int, 1>{}, b, cb);
+      else if (M == 3) gen_row(std::integral_constant<int, 3>{}, b, cb);
+      else gen_row(std::integral_constant<int, 5>{}, b, cb);
     }
     for (int t = nblk - 2; t < nblk && ok; ++t)
       if (t >= 0) flush(t);
-    const int64_t n = n0 + row;
     if (ok && has_cols && n < a.N) {
       float4* out = reinterpret_cast<float4*>(a.scalars + n * S + 16 * qq);
 #pragma unroll
@@ -269,7 +293,7 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
   } else if (warp == NGEN_WARPS) {
     // ---------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = tc::idesc_tf32(TILE, S);
+      constexpr uint32_t idesc = tc::idesc_f16(TILE, S);
       const uint32_t sB0 = tc::smem_u32(sB);
       for (int s = 0; s < nblk; ++s) {
         const int bst = s % NSTB, ast = s & 1, dst = s % NSD;
@@ -279,12 +303,12 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
         tc::tc_fence_after();
         const uint32_t bhi = sB0 + bst * SM::BBYTES, blo = bhi + SM::BBYTES / 2;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < 4; ++j) {  // K = 16 pairs per step: 8 packed columns of A
           const uint64_t dh = tc::smem_desc_kmajor(bhi + j * 2 * 16 * S, 16 * S, 128);
           const uint64_t dl = tc::smem_desc_kmajor(blo + j * 2 * 16 * S, 16 * S, 128);
-          tc::mma_tf32_ts(tD(dst), tA(ast, 0) + 8 * j, dh, idesc, j != 0);
-          tc::mma_tf32_ts(tD(dst), tA(ast, 0) + 8 * j, dl, idesc, 1);
-          tc::mma_tf32_ts(tD(dst), tA(ast, 1) + 8 * j, dh, idesc, 1);
+          tc::mma_f16_ts(tD(dst), tA(ast, 0) + 8 * j, dh, idesc, j != 0);
+          tc::mma_f16_ts(tD(dst), tA(ast, 0) + 8 * j, dl, idesc, 1);
+          tc::mma_f16_ts(tD(dst), tA(ast, 1) + 8 * j, dh, idesc, 1);
         }
         tc::mma_commit(empty_A + ast);
         tc::mma_commit(empty_B + bst);
@@ -294,7 +318,7 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
   } else {
     // ---------------- producer: W blocks, d-row and c-row chunks (bulk copies)
     if (lane == 0) {
-      const uint8_t* wsrc = reinterpret_cast<const uint8_t*>(a.wimg);
+      const uint8_t* wsrc = reinterpret_cast<const uint8_t*>(a.wimg) + WHEADER;
       uint8_t* tring = smem + SM::T_OFF;
       uint8_t* cring = smem + SM::C_OFF;
       int s = 0;
@@ -326,8 +350,9 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
 }
 
 // ------------------------------------------------------------------ backward
-// Roles: the MMA warp forms each 128 x 64 block of H (A = ds split in TMEM, B = W block in shared
-// memory) into one of two TMEM accumulators; the producer streams W blocks and the d-block's t
+// Roles: the MMA warp forms H for two d-blocks at a time (A = ds, range-scaled and split into
+// fp16 hi / lo in TMEM, B = the W block pair in shared memory; 3 x S/16 kind::f16 MMAs) into one of
+// three TMEM accumulators; the producer streams W blocks and the d-block's t
 // rows; 16 epilogue warps (thread = node, quarter qq of the c-rows: c = 2qq, 2qq + 1) contract
 // the other accumulator with t from shared memory: dt[c][m] += 2 sum_d H[c][d] t[d][m] over all
 // d-blocks of a row.
@@ -377,24 +402,35 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t tAhi = tbase, tAlo = tbase + 64u;                  // ds split, cols [0, 128)
+  const uint32_t tAhi = tbase, tAlo = tbase + 32u;                   // ds fp16 split, cols [0, 64)
   auto tD = [&](int st) { return tbase + 128u + 128u * st; };        // H block pairs, cols [128, 512)
+  const float w_inv = a.wimg[0];
+  __shared__ float dmax[4][TILE];
 
   if (warp < NGEN_WARPS) {
     const int q4 = warp & 3, qq = warp >> 2;
     const int row = q4 * 32 + lane;
     const int64_t n = n0 + row;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    // A operand: ds (128 x S), split into hi / lo; warp quarter qq stores columns [16qq, 16qq+16)
-    if (16 * qq < S) {
-      uint32_t hi[16], lo[16];
+    // A operand: ds (128 x S) times the node's power-of-two range factor, split into fp16
+    // hi / lo; warp quarter qq holds elements [16qq, 16qq+16) = packed columns [8qq, 8qq+8)
+    float dv[16];
+    float vmax = 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float v = n < a.N ? a.dscal[n * S + 16 * qq + i] : 0.f;
-        tc::split_tf32(v, hi[i], lo[i]);
-      }
-      tc::tmem_st16(tAhi + lane_off + 16u * qq, hi);
-      tc::tmem_st16(tAlo + lane_off + 16u * qq, lo);
+    for (int i = 0; i < 16; ++i) {
+      dv[i] = (16 * qq < S && n < a.N) ? a.dscal[n * S + 16 * qq + i] : 0.f;
+      vmax = fmaxf(vmax, fabsf(dv[i]));
+    }
+    dmax[qq][row] = vmax;
+    asm volatile("bar.sync 1, %0;" ::"n"(NGEN_WARPS * 32) : "memory");  // generator warps only
+    const float scale = tc::f16_range_scale(fmaxf(fmaxf(dmax[0][row], dmax[1][row]), fmaxf(dmax[2][row], dmax[3][row])));
+    const float unscale = 2.f * w_inv / scale;  // dt = 2 H t; H carries scale / w_inv
+    if (16 * qq < S) {
+      uint32_t hi[8], lo[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) tc::split_f16x2(dv[2 * i] * scale, dv[2 * i + 1] * scale, hi[i], lo[i]);
+      tc::tmem_st8(tAhi + lane_off + 8u * qq, hi);
+      tc::tmem_st8(tAlo + lane_off + 8u * qq, lo);
       tc::tmem_wait_st();
     }
     tc::tc_fence_before();
@@ -451,7 +487,7 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
 #pragma unroll
       for (int cq = 0; cq < 2; ++cq)
 #pragma unroll
-        for (int m = 0; m < M; ++m) pd[(cq * M + m) * TILE] = 2.f * acc[cq][m];
+        for (int m = 0; m < M; ++m) pd[(cq * M + m) * TILE] = unscale * acc[cq][m];
     };
     const RowOrder order(a.ngram, nb);
     for (int i = 0; i < order.rows && ok; ++i) {
@@ -464,7 +500,7 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
     }
   } else if (warp == NGEN_WARPS) {
     if (lane == 0) {
-      constexpr uint32_t idesc = tc::idesc_tf32(TILE, 128);
+      constexpr uint32_t idesc = tc::idesc_f16(TILE, 128);
       const uint32_t sB0 = tc::smem_u32(sB);
       bool ok = tc::mbar_wait(a_ready, 0, a.err, 22);
       tc::tc_fence_after();
@@ -475,12 +511,12 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
         tc::tc_fence_after();
         const uint32_t bhi = sB0 + bst * SM::BBYTES, blo = bhi + SM::BBYTES / 2;
 #pragma unroll
-        for (int j = 0; j < S / 8; ++j) {
+        for (int j = 0; j < S / 16; ++j) {  // K = 16 outputs per step: 8 packed columns of A
           const uint64_t dh = tc::smem_desc_kmajor(bhi + j * 2 * 16 * 128, 16 * 128, 128);
           const uint64_t dl = tc::smem_desc_kmajor(blo + j * 2 * 16 * 128, 16 * 128, 128);
-          tc::mma_tf32_ts(tD(dst), tAhi + 8 * j, dh, idesc, j != 0);
-          tc::mma_tf32_ts(tD(dst), tAhi + 8 * j, dl, idesc, 1);
-          tc::mma_tf32_ts(tD(dst), tAlo + 8 * j, dh, idesc, 1);
+          tc::mma_f16_ts(tD(dst), tAhi + 8 * j, dh, idesc, j != 0);
+          tc::mma_f16_ts(tD(dst), tAhi + 8 * j, dl, idesc, 1);
+          tc::mma_f16_ts(tD(dst), tAlo + 8 * j, dh, idesc, 1);
         }
         tc::mma_commit(empty_B + bst);
         tc::mma_commit(d_full + dst);
@@ -489,7 +525,7 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
   } else {
     // ---------------- producer: W block pairs and 16-row t chunks
     if (lane == 0) {
-      const uint8_t* wsrc = reinterpret_cast<const uint8_t*>(a.wimg);
+      const uint8_t* wsrc = reinterpret_cast<const uint8_t*>(a.wimg) + WHEADER;
       uint8_t* tring = smem + SM::T_OFF;
       int s = 0;
       bool ok = true;
@@ -525,18 +561,42 @@ __device__ __forceinline__ int64_t fg_index(int64_t r, int64_t n, int64_t nrows)
   return (n / TILE) * nrows * TILE + r * TILE + (n % TILE);
 }
 
+// Also: gmax[block(l)][n] = max over this layer's channels c of sum_m t[l][c][m]^2 (atomic max
+// over layers; non-negative floats order like their bit patterns), the range bound of the
+// fp16 split of node n's Gram values (|G_cd| <= max_c |t_c|^2).
 __global__ void fg_gather_kernel(FgArgs a) {
   extern __shared__ float tile[];  // [FG_NODES][9C + 1]
+  __shared__ unsigned int nmax[3][FG_NODES];
   const int layer = blockIdx.y;
   const int W = 9 * a.C;
   const int64_t n0 = (int64_t)blockIdx.x * FG_NODES;
   const float* src = a.feats[layer];
+  if (threadIdx.x < 3 * FG_NODES) (&nmax[0][0])[threadIdx.x] = 0u;
   for (int i = threadIdx.x; i < FG_NODES * W; i += blockDim.x) {
     const int nl = i / W, kc = i - nl * W;
     const int64_t n = n0 + nl;
     tile[nl * (W + 1) + kc] = n < a.N ? src[n * W + kc] : 0.f;
   }
   __syncthreads();
+  for (int i = threadIdx.x; i < FG_NODES * a.C; i += blockDim.x) {
+    const int nl = i / a.C, c = i - nl * a.C;
+    const float* t = tile + nl * (W + 1) + c;
+    float s0 = t[0] * t[0], s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int k = 1; k < 4; ++k) s1 = fmaf(t[k * a.C], t[k * a.C], s1);
+#pragma unroll
+    for (int k = 4; k < 9; ++k) s2 = fmaf(t[k * a.C], t[k * a.C], s2);
+    atomicMax(&nmax[0][nl], __float_as_uint(s0));
+    atomicMax(&nmax[1][nl], __float_as_uint(s1));
+    atomicMax(&nmax[2][nl], __float_as_uint(s2));
+  }
+  __syncthreads();
+  if (threadIdx.x < 3 * FG_NODES) {
+    const int l = threadIdx.x / FG_NODES, nl = threadIdx.x - l * FG_NODES;
+    const int b = a.lblock[l];
+    if (b >= 0 && n0 + nl < a.n_pad)
+      atomicMax(reinterpret_cast<unsigned int*>(a.gmax) + (int64_t)b * a.n_pad + n0 + nl, nmax[l][nl]);
+  }
   const int32_t* inv = a.xinv + (int64_t)layer * W;
   for (int i = threadIdx.x; i < FG_NODES * W; i += blockDim.x) {
     const int kc = i / FG_NODES, nl = i - kc * FG_NODES;

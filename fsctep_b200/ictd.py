@@ -117,18 +117,25 @@ def gram_xinv(C: int, nint: int, o3: bool = False):
     return inv
 
 
-def tf32_split(x: torch.Tensor):
-    """fp32 -> (hi, lo): hi keeps the top 19 bits, lo = round_to_nearest_tf32(x - hi)."""
-    x = x.to(torch.float32).contiguous()
-    hi = (x.view(torch.int32) & -8192).view(torch.float32)
-    r = (x - hi).contiguous()
-    lo = ((r.view(torch.int32) + 4096) & -8192).view(torch.float32)
-    return hi, lo
+def f16_image(x: torch.Tensor) -> torch.Tensor:
+    """float64 operand image [blocks][...] -> float32 tensor holding a 64-byte header (element 0 =
+    1/scale) and, per block, the fp16 hi plane then the fp16 lo plane of scale * x, where scale is
+    the power of two that brings max |x| to at most 2^14 (hi = fp16(x s), lo = fp16(x s - hi))."""
+    m = float(x.abs().max().item()) if x.numel() else 0.0
+    scale = 2.0 ** (14 - math.ceil(math.log2(m))) if m > 0 else 1.0
+    xs = x * scale
+    hi = xs.to(torch.float16)
+    lo = (xs - hi.to(torch.float64)).to(torch.float16)
+    planes = torch.stack([hi, lo], dim=1).reshape(-1).contiguous()
+    header = torch.zeros(16, dtype=torch.float32, device=x.device)
+    header[0] = 1.0 / scale
+    return torch.cat([header, planes.view(torch.float32)])
 
 
 def readout_images(W_read, C: int, nint: int, ls=(0, 1, 2)):
-    """W_read blocks (Gram block b has l = ls[b]) as shared-memory images of the tcgen05 operands
-    (see include/fsctep_b200.h).  Returns (wimg_fwd, wimg_bwd) as flat fp32 tensors.
+    """W_read blocks (Gram block b has l = ls[b]) as shared-memory images of the tcgen05 kind::f16
+    operands (see include/fsctep_b200.h).  Returns (wimg_fwd, wimg_bwd), each a header + fp16 planes
+    (:func:`f16_image`) in a float32 tensor.
     """
     nC = C * nint
     nb = nC // 8
@@ -140,19 +147,15 @@ def readout_images(W_read, C: int, nint: int, ls=(0, 1, 2)):
         Ws = 0.5 * (Wr + Wr.transpose(1, 2))
         blk = Ws.reshape(S, nb, 8, nb, 8).permute(1, 3, 0, 2, 4).reshape(nb, nb, S, 64)  # [cb][db][o][pair]
         # forward: cb <= db, x2 off the diagonal, pairs reordered (c, d = 2qq + dd) -> 16qq + 2c + dd
-        # (the generator thread of quarter qq owns d-rows 2qq, 2qq+1), image [pair/4][o][pair%4]
+        # (the generator thread of quarter qq owns d-rows 2qq, 2qq+1); B = [k/8][o][k%8], K = pairs
         f = blk[iu[0], iu[1]] * torch.where(iu[0] == iu[1], 1.0, 2.0).to(blk)[:, None, None]
         f = f.reshape(-1, S, 8, 4, 2).permute(0, 1, 3, 2, 4).reshape(-1, S, 64)
-        f = f.reshape(-1, S, 16, 4).permute(0, 2, 1, 3)
-        hi, lo = tf32_split(f)
-        fwd.append(torch.stack([hi, lo], dim=1).reshape(-1))
+        fwd.append(f.reshape(-1, S, 8, 8).permute(0, 2, 1, 3))
         # backward: all blocks in pairs of d-blocks (db even, db + 1) -> N = 128 pairs per MMA,
-        # image [o/4][pair of the two blocks][o%4] of Ws
+        # B = [o/8][pair of the two blocks][o%8], K = outputs o
         b = blk.reshape(nb, nb // 2, 2, S, 64).permute(0, 1, 3, 2, 4).reshape(nb * nb // 2, S, 128)
-        b = b.transpose(1, 2).reshape(nb * nb // 2, 128, S // 4, 4).permute(0, 2, 1, 3)
-        hi, lo = tf32_split(b)
-        bwd.append(torch.stack([hi, lo], dim=1).reshape(-1))
-    return torch.cat(fwd), torch.cat(bwd)
+        bwd.append(b.reshape(-1, S // 8, 8, 128).permute(0, 1, 3, 2))
+    return f16_image(torch.cat(fwd)), f16_image(torch.cat(bwd))
 
 
 def _silu(x):

@@ -218,14 +218,16 @@ typedef struct {
    * the [N][9][C] feature buffers.                                                          */
   const int32_t* xmap;   /* [9*nC]                                                          */
   const int32_t* xinv;   /* [nint][9*C] inverse of xmap: storage (layer, k*C+c) -> element   */
-  /* Tensor-core readout: W_read in 8x8 (c, d) blocks, each block pre-formatted as the
-   * shared-memory image of a K-major tf32 MMA operand and split hi/lo for 3xTF32 (hi keeps
-   * the top 19 bits, lo = round_tf32(w - hi)); nb = nC/8.
-   *   wimg_fwd: for l, cb <= db:  [hi|lo][pair/4][o][pair%4] of Ws (x2 off the diagonal)
-   *   wimg_bwd: for l, cb, db:    [hi|lo][o/4][pair][o%4]   of Ws
-   * with pair = 8*(c - 8cb) + (d - 8db) and Ws = (W_read.l + W_read.l^T)/2/sqrt(2l+1).      */
-  const float* wimg_fwd; /* [3*nb*(nb+1)/2][2][16][S][4]                                   */
-  const float* wimg_bwd; /* [3*nb*nb][2][S/4][64][4]                                       */
+  /* Tensor-core readout: W_read in 8x8 (c, d) blocks as shared-memory images of K-major fp16
+   * tcgen05 (kind::f16) operands.  Each image starts with a 64-byte header whose first float is
+   * 1/s, s = the power of two bringing max |W| in the image to <= 2^14; then per block the fp16
+   * hi plane and lo plane of s*W (hi = fp16(s w), lo = fp16(s w - hi)).  nb = nC/8,
+   * pair = (c - 8cb, d - 8db), Ws = (W_read.l + W_read.l^T)/2/sqrt(2l+1):
+   *   wimg_fwd: for l, cb <= db:  [k/8][o][k%8], K = 64 pairs ordered (d/2, c, d%2), Ws x2 off
+   *             the diagonal block
+   *   wimg_bwd: for l, cb, db pairs (db even, db+1):  [o/8][n][o%8], n = 64 (db odd) + 8c + d  */
+  const float* wimg_fwd; /* header + [3*nb*(nb+1)/2][2][8][S][8] fp16                         */
+  const float* wimg_bwd; /* header + [3*nb*nb/2][2][S/8][128][8] fp16                         */
   const float* mn_in_g;  /* [D0]  proj_total.input_norm.weight, D0 = 3*nC + S             */
   const float* mn_in_b;  /* [D0]  proj_total.input_norm.bias                              */
   const float* mn_w[4];  /* [hidden[k]][in_k]  proj_total.layers.k.weight (as stored)      */
