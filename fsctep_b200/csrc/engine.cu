@@ -83,10 +83,18 @@ struct Plan {
   float* dFg;
   float* gmax;
   int* err;
+  // tensor-core GEMM operand images of the weights (null: CUDA-core GEMM)
+  bool gtc;
+  float* img_fwd[8][3];     // conv2 layer k, l3
+  float* img_dz[8][3];
+  float* img_dx[8][3];      // by l1
+  float* img_mnf[4];
+  float* img_mnb[4];
 };
 
 int g_readout_path = 0;  // 0: tensor cores where supported, 1: CUDA cores
 int g_radial_path = 0;   // 0: tensor cores where supported, 1: CUDA cores
+int g_gemm_path = 0;     // 0: tensor cores where supported, 1: CUDA cores
 
 int validate(const fsc_ictd_config* cfg) {
   FSC_REQUIRE(cfg != nullptr, "config is null");
@@ -160,6 +168,25 @@ void layout(Plan& p, Arena& ar, const fsc_ictd_config* cfg, int64_t N, int64_t E
   p.edge_grad = ar.take<float>(E * 3);
   p.heads_d = ar.take<double>(4 * kMaxGraphs * 5);
   p.tc = g_readout_path == 0 && readout_tc_supported(p.nC, p.S);
+  p.gtc = g_gemm_path == 0;
+  for (int k = 0; k < 8; ++k)
+    for (int l = 0; l < 3; ++l) p.img_fwd[k][l] = p.img_dz[k][l] = p.img_dx[k][l] = nullptr;
+  for (int k = 0; k < 4; ++k) p.img_mnf[k] = p.img_mnb[k] = nullptr;
+  if (p.gtc) {
+    const int C = p.C;
+    for (int k = 1; k < p.nint; ++k)
+      for (int l = 0; l < 3; ++l) {
+        p.img_fwd[k][l] = ar.take<float>(gemm_image_floats(NP3(l) * C, C));
+        p.img_dz[k][l] = ar.take<float>(gemm_image_floats(C, NP3(l) * C));
+        p.img_dx[k][l] = ar.take<float>(gemm_image_floats(NP1(l) * C, C));
+      }
+    int din = p.D0;
+    for (int k = 0; k < p.n_hidden; ++k) {
+      p.img_mnf[k] = ar.take<float>(gemm_image_floats(din, p.hidden[k]));
+      p.img_mnb[k] = ar.take<float>(gemm_image_floats(p.hidden[k], din));
+      din = p.hidden[k];
+    }
+  }
   p.rtc = g_radial_path == 0 && radial_tc_supported(p.nb);
   p.n_pad = ceil_div(std::max<int64_t>(N, 1), 128) * 128;
   p.err = ar.take<int>(64);
@@ -188,9 +215,8 @@ FgArgs fg_args(const Plan& p, const fsc_ictd_weights* w) {
   f.Fg = p.Fg;
   f.dFg = p.dFg;
   f.gmax = p.gmax;
-  for (int l = 0; l < 3; ++l) f.lblock[l] = -1;
-  for (int b = 0; b < p.ngram; ++b)
-    if (!(p.o3 && b == 1)) f.lblock[p.gl[b]] = b;  // o3: block 1 is the zero 1e block
+  f.ngram = p.ngram;
+  for (int b = 0; b < 4; ++b) f.goff[b] = p.goff[b];
   f.nrows = p.nrows;
   return f;
 }
@@ -225,6 +251,54 @@ GemmArgs gemm(const float* A, int64_t a_gs, int64_t a_rs, const float* B, int64_
   g.C = C; g.c_gs = c_gs; g.c_rs = c_rs;
   g.G = G; g.R = R; g.K = K; g.N = N;
   return g;
+}
+
+// GEMM on the tensor cores when an image exists and the shape qualifies, else on CUDA cores.
+int run_gemm(const GemmArgs& g, const float* img, int* err, cudaStream_t st) {
+  if (img && gemm_tc_supported(g)) return launch_gemm_tc(g, img, err, st);
+  return launch_gemm(g, st);
+}
+
+// Block offset of l-block l inside one layer's mix weights (3, 4, 4 paths of C x C).
+inline int64_t mix_boff(int l, int C) { return (int64_t)(l == 0 ? 0 : (l == 1 ? 3 : 7)) * C * C; }
+
+// Builds every weight image the tensor-core GEMMs of this call read.
+int build_gemm_images(const Plan& p, const fsc_ictd_weights* w, cudaStream_t st) {
+  if (!p.gtc) return FSC_OK;
+  GemmImageJobs jobs{};
+  int n = 0;
+  auto add = [&](const float* B, int64_t ldb, int trans, int K, int N, float* out) -> int {
+    GemmImageJob& j = jobs.job[n++];
+    j.B = B;
+    j.ldb = ldb;
+    j.b_trans = trans;
+    j.K = K;
+    j.N = N;
+    j.NT = gemm_tc_nt(N);
+    j.ntiles = (int)ceil_div(N, j.NT);
+    j.out = out;
+    if (n == kMaxImageJobs) {
+      FSC_TRY(launch_gemm_images(jobs, n, st));
+      n = 0;
+    }
+    return FSC_OK;
+  };
+  const int C = p.C;
+  for (int k = 1; k < p.nint; ++k) {
+    const int64_t lo = (int64_t)(k - 1) * NP * C * C;
+    for (int l = 0; l < 3; ++l) {
+      FSC_TRY(add(w->mix_fwd + lo + mix_boff(l, C), C, 0, NP3(l) * C, C, p.img_fwd[k][l]));
+      FSC_TRY(add(w->mix_bwd + lo + mix_boff(l, C), NP3(l) * C, 0, C, NP3(l) * C, p.img_dz[k][l]));
+      FSC_TRY(add(w->mix_dx + lo + mix_boff(l, C), C, 0, NP1(l) * C, C, p.img_dx[k][l]));
+    }
+  }
+  int din = p.D0;
+  for (int k = 0; k < p.n_hidden; ++k) {
+    FSC_TRY(add(w->mn_w[k], din, 1, din, p.hidden[k], p.img_mnf[k]));
+    FSC_TRY(add(w->mn_w[k], din, 0, p.hidden[k], din, p.img_mnb[k]));
+    din = p.hidden[k];
+  }
+  return launch_gemm_images(jobs, n, st);
 }
 
 __global__ void finalize_kernel(const double* __restrict__ e, const double* __restrict__ v, int64_t B, float* energy,
@@ -295,6 +369,7 @@ int forward(Ctx& c) {
   cudaStream_t st = c.st;
   const int C = p.C;
   prof::mark("begin", st);
+  FSC_TRY(build_gemm_images(p, w, st));
   FSC_TRY(launch_edge_dst(g->row_ptr, p.dst, p.N, st));
   EdgeFwdArgs ef{};
   ef.E = p.E; ef.pos = g->pos; ef.src = g->src; ef.dst = p.dst; ef.batch = g->batch; ef.cell = g->cell;
@@ -321,7 +396,7 @@ int forward(Ctx& c) {
       GemmArgs ga = gemm(p.zbuf + OFF3(l3) * C, NZ * C, NP3(l3) * C, W + boff, C, 0, p.feats[k] + KB(l3) * C,
                          NK * C, C, p.nk[k], 2 * l3 + 1, NP3(l3) * C, C);
       ga.deg_rowptr = g->row_ptr;
-      FSC_TRY(launch_gemm(ga, st));
+      FSC_TRY(run_gemm(ga, p.img_fwd[k][l3], p.err, st));
       boff += (int64_t)NP3(l3) * C * C;
     }
     prof::mark("conv2_mix_forward", st);
@@ -358,7 +433,7 @@ int forward(Ctx& c) {
   for (int k = 0; k < p.n_hidden; ++k) {
     GemmArgs ga = gemm(xin, din, 0, w->mn_w[k], din, 1, p.act_pre[k], p.hidden[k], 0, p.nro, 1, din, p.hidden[k]);
     ga.bias = w->mn_b[k];
-    FSC_TRY(launch_gemm(ga, st));
+    FSC_TRY(run_gemm(ga, p.img_mnf[k], p.err, st));
     FSC_TRY(launch_layernorm(p.act_pre[k], p.nro, p.hidden[k], w->mn_g[k], w->mn_beta[k], 1, p.act_post[k], st));
     xin = p.act_post[k];
     din = p.hidden[k];
@@ -382,7 +457,7 @@ int backward(Ctx& c) {
     // da_k = LN_bwd(a_k, dx_{k+1}) into dnext, then dx_k = da_k @ W_k into dcur
     FSC_TRY(launch_layernorm_backward(p.act_pre[k], dcur, p.nro, p.hidden[k], w->mn_g[k], w->mn_beta[k], 1, dnext, st));
     GemmArgs ga = gemm(dnext, p.hidden[k], 0, w->mn_w[k], din, 0, dcur, din, 0, p.nro, 1, p.hidden[k], din);
-    FSC_TRY(launch_gemm(ga, st));
+    FSC_TRY(run_gemm(ga, p.img_mnb[k], p.err, st));
   }
   FSC_TRY(launch_layernorm_backward(p.p5, dcur, p.nro, p.D0, w->mn_in_g, w->mn_in_b, 0, p.dp5, st));
   ReadoutArgs ra = readout_args(c);
@@ -418,7 +493,7 @@ int backward(Ctx& c) {
       GemmArgs ga = gemm(p.grads[k] + KB(l3) * C, NK * C, C, Wb + boff, NP3(l3) * C, 0, p.zbuf + OFF3(l3) * C,
                          NZ * C, NP3(l3) * C, p.nk[k], 2 * l3 + 1, C, NP3(l3) * C);
       ga.deg_rowptr = g->row_ptr;
-      FSC_TRY(launch_gemm(ga, st));
+      FSC_TRY(run_gemm(ga, p.img_dz[k][l3], p.err, st));
       boff += (int64_t)NP3(l3) * C * C;
     }
     prof::mark("conv2_mix_backward_dz", st);
@@ -436,7 +511,7 @@ int backward(Ctx& c) {
       GemmArgs ga = gemm(p.zbuf + OFF1(l1) * C, NZ * C, NP1(l1) * C, Wx + boff, C, 0, p.grads[k - 1] + KB(l1) * C,
                          NK * C, C, p.nk[k - 1], 2 * l1 + 1, NP1(l1) * C, C);
       ga.accumulate = 1;
-      FSC_TRY(launch_gemm(ga, st));
+      FSC_TRY(run_gemm(ga, p.img_dx[k][l1], p.err, st));
       boff += (int64_t)NP1(l1) * C * C;
     }
     prof::mark("conv2_mix_backward_dx", st);
@@ -674,6 +749,7 @@ int fsc_ictd_status(const fsc_ictd_config* cfg, int64_t num_atoms, int64_t num_e
 
 void fsc_ictd_set_readout_path(int path) { fsc::g_readout_path = path; }
 void fsc_ictd_set_radial_path(int path) { fsc::g_radial_path = path; }
+void fsc_ictd_set_gemm_path(int path) { fsc::g_gemm_path = path; }
 
 void fsc_profile_enable(int enable) {
   fsc::prof::enabled = enable != 0;

@@ -1,0 +1,365 @@
+// Channel-mixing and MainNet GEMMs on the 5th-generation tensor cores (TMA, tcgen05, TMEM).
+//
+//   C[row, n] (+)= scale(row) * sum_k A[row, k] B[k, n] (+ bias[n]),  rows (g, r): g < G, r < R,
+//   A row (g, r) at A + g*a_gs + r*a_rs (K contiguous), C row at C + g*c_gs + r*c_rs.
+//
+// One CTA = 128 rows (the TMEM lanes; Gb = 128 / R whole row groups) x NT output columns.
+//  * producer warp: per K-chunk of 32, one 3-D TMA load of the A tile (dims K, R, G: the two-level
+//    row addressing needs no copy; 128-byte swizzle, so each row is one swizzle row) and one bulk
+//    copy of the B chunk from a pre-formatted image, into a shared-memory ring;
+//  * 4 math warps: split the staged A in place into tf32 hi (top 19 bits) and write lo =
+//    round_tf32(a - hi) to a second buffer of the same layout (elementwise, so the swizzle needs
+//    no decoding); after the last chunk they read the accumulators and write C;
+//  * MMA warp: per chunk 4 K-steps x (hi*hi, hi*lo, lo*hi) kind::tf32 MMAs (A and B from shared
+//    memory) into accumulator chunk % NACC, so no accumulator carries a long chain; the epilogue
+//    sums the NACC accumulators in fp32.
+// B images (hi / lo planes, K-major, no swizzle) are built from the weights by gemm_image_kernel.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "tc_common.cuh"
+
+namespace fsc {
+
+namespace {
+
+constexpr int KC = 32;                      // K per chunk: one 128-byte row per A row
+constexpr int MT = 128;                     // rows per tile
+constexpr uint32_t ABYTES = MT * KC * 4u;   // 16 KB
+constexpr int GT_THREADS = 6 * 32;          // 4 math warps, producer warp, MMA warp
+
+template <int NT>
+struct GCfg {
+  static constexpr int NACC = NT <= 64 ? 4 : 2;
+  static constexpr int NST = 2;
+  static constexpr uint32_t BBYTES = 2u * KC * NT * 4u;  // hi + lo planes of one chunk
+  static constexpr uint32_t ALO_OFF = NST * ABYTES;
+  static constexpr uint32_t B_OFF = 2 * NST * ABYTES;
+  static constexpr uint32_t BAR_OFF = B_OFF + NST * BBYTES;
+  static constexpr uint32_t TOTAL = BAR_OFF + 128 + 1024;  // + slack for 1024-byte alignment
+  static constexpr uint32_t TCOLS = NT * NACC <= 256 ? 256 : 512;
+};
+
+// K-major, 128-byte swizzle smem descriptor: 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;                 // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;       // stride byte offset
+  d |= (uint64_t)1 << 46;                 // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                 // layout: 128-byte swizzle
+  return d;
+}
+
+__device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(tc::smem_u32(smem_dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(tc::smem_u32(bar))
+      : "memory");
+}
+
+struct GemmTcArgs {
+  const float* bimg;       // [ntiles][K/KC][2][KC/4][NT][4]
+  int K, N;
+  int64_t G;
+  int R, Gb;
+  uint32_t abox;           // bytes of one A box: KC * R * Gb * 4
+  float* C;
+  int64_t c_gs, c_rs;
+  const int32_t* deg_rowptr;
+  const float* bias;
+  int accumulate;
+  float alpha;
+  int* err;
+};
+
+template <int NT>
+__global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, GemmTcArgs a) {
+  using CF = GCfg<NT>;
+  constexpr int NST = CF::NST, NACC = CF::NACC;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sAlo = smem + CF::ALO_OFF;
+  uint8_t* sB = smem + CF::B_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + CF::BAR_OFF);
+  uint64_t* full = bars;                  // [NST] TMA + bulk bytes landed
+  uint64_t* lo_ready = bars + NST;        // [NST] math warps split the chunk
+  uint64_t* empty = bars + 2 * NST;       // [NST] MMAs done with the stage
+  uint64_t* d_ready = bars + 3 * NST;     // all MMAs done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * NST + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nchunks = a.K / KC;
+  const int64_t g0 = (int64_t)blockIdx.x * a.Gb;
+
+  if (warp == 4) {
+    tc::tmem_alloc(tmem_slot, CF::TCOLS);
+    tc::tmem_relinquish();
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NST; ++i) {
+      tc::mbar_init(full + i, 1);
+      tc::mbar_init(lo_ready + i, 4);
+      tc::mbar_init(empty + i, 1);
+    }
+    tc::mbar_init(d_ready, 1);
+    tc::fence_mbar_init();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp < 4) {
+    // ---------------- split A into tf32 hi (in place) and lo, per chunk
+    bool ok = true;
+    for (int c = 0; c < nchunks && ok; ++c) {
+      const int st = c % NST;
+      if (!(ok = tc::mbar_wait(full + st, (c / NST) & 1, a.err, 81))) break;
+      float4* pa = reinterpret_cast<float4*>(sA + st * ABYTES);
+      float4* pl = reinterpret_cast<float4*>(sAlo + st * ABYTES);
+#pragma unroll
+      for (int i = 0; i < (int)(ABYTES / 16) / MT; ++i) {
+        const int idx = threadIdx.x + MT * i;
+        float4 v = pa[idx];
+        uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
+        tc::split_tf32(v.x, h0, l0);
+        tc::split_tf32(v.y, h1, l1);
+        tc::split_tf32(v.z, h2, l2);
+        tc::split_tf32(v.w, h3, l3);
+        pa[idx] = make_float4(__uint_as_float(h0), __uint_as_float(h1), __uint_as_float(h2), __uint_as_float(h3));
+        pl[idx] = make_float4(__uint_as_float(l0), __uint_as_float(l1), __uint_as_float(l2), __uint_as_float(l3));
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(lo_ready + st);
+    }
+    // ---------------- epilogue: thread = tile row = TMEM lane
+    if (ok) ok = tc::mbar_wait(d_ready, 0, a.err, 82);
+    tc::tc_fence_after();
+    const int t = warp * 32 + lane;
+    const int64_t g = g0 + t / a.R;
+    const int r = t % a.R;
+    const bool valid = ok && t < a.R * a.Gb && g < a.G;
+    float scale = a.alpha != 0.f ? a.alpha : 1.f;
+    if (valid && a.deg_rowptr) {
+      const int d = a.deg_rowptr[g + 1] - a.deg_rowptr[g];
+      scale *= 1.f / (float)(d > 1 ? d : 1);
+    }
+    float* crow = valid ? a.C + g * a.c_gs + r * a.c_rs : nullptr;
+    const int n0 = blockIdx.y * NT;
+    const int nacc = nchunks < NACC ? nchunks : NACC;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+#pragma unroll 1
+    for (int cb = 0; cb < NT / 16; ++cb) {
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = 0.f;
+      for (int q = 0; q < nacc; ++q) {
+        uint32_t u[16];
+        tc::tmem_ld16(tbase + (uint32_t)(q * NT) + lane_off + 16u * cb, u);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] += __uint_as_float(u[i]);
+      }
+      const int nc = n0 + 16 * cb;
+      if (crow && nc < a.N) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          v[i] *= scale;
+          if (a.bias && nc + i < a.N) v[i] += a.bias[nc + i];
+        }
+        float* cp = crow + nc;
+        if (nc + 16 <= a.N && (reinterpret_cast<uintptr_t>(cp) & 15) == 0) {
+          float4* c4 = reinterpret_cast<float4*>(cp);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float4 o = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            if (a.accumulate) {
+              const float4 p = c4[i];
+              o.x += p.x;
+              o.y += p.y;
+              o.z += p.z;
+              o.w += p.w;
+            }
+            c4[i] = o;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (nc + i < a.N) cp[i] = a.accumulate ? cp[i] + v[i] : v[i];
+        }
+      }
+    }
+  } else if (warp == 4) {
+    // ---------------- producer
+    if (lane == 0) {
+      const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(a.bimg) + (size_t)blockIdx.y * nchunks * CF::BBYTES;
+      for (int c = 0; c < nchunks; ++c) {
+        const int st = c % NST;
+        if (c >= NST && !tc::mbar_wait(empty + st, ((c / NST) - 1) & 1, a.err, 83)) break;
+        tc::mbar_arrive_expect_tx(full + st, a.abox + CF::BBYTES);
+        tma_load_3d(sA + st * ABYTES, &tmA, c * KC, 0, (int)g0, full + st);
+        tc::bulk_g2s(sB + st * CF::BBYTES, bsrc + (size_t)c * CF::BBYTES, CF::BBYTES, full + st);
+      }
+    }
+  } else {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_tf32(MT, NT);
+      const uint32_t a0 = tc::smem_u32(sA), l0 = tc::smem_u32(sAlo), b0 = tc::smem_u32(sB);
+      bool ok = true;
+      for (int c = 0; c < nchunks; ++c) {
+        const int st = c % NST;
+        if (!(ok = tc::mbar_wait(lo_ready + st, (c / NST) & 1, a.err, 84))) break;
+        tc::tc_fence_after();
+        const uint32_t d = tbase + (uint32_t)((c % NACC) * NT);
+#pragma unroll
+        for (int j = 0; j < KC / 8; ++j) {
+          const uint64_t ah = desc_sw128(a0 + st * ABYTES + 32 * j);
+          const uint64_t al = desc_sw128(l0 + st * ABYTES + 32 * j);
+          const uint32_t bh_addr = b0 + st * CF::BBYTES + j * 2 * 16 * NT;
+          const uint64_t bh = tc::smem_desc_kmajor(bh_addr, 16 * NT, 128);
+          const uint64_t bl = tc::smem_desc_kmajor(bh_addr + CF::BBYTES / 2, 16 * NT, 128);
+          mma_tf32_ss(d, ah, bh, idesc, (c >= NACC || j > 0) ? 1u : 0u);
+          mma_tf32_ss(d, ah, bl, idesc, 1u);
+          mma_tf32_ss(d, al, bh, idesc, 1u);
+        }
+        tc::mma_commit(empty + st);
+      }
+      tc::mma_commit(d_ready);  // also when a wait failed: whatever was issued completes first
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    // the MMA warp commits d_ready on every path: wait (bounded) until no MMA still writes TMEM
+    if (lane == 0) tc::mbar_wait(d_ready, 0, a.err, 85);
+    __syncwarp();
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tbase, CF::TCOLS);
+  }
+}
+
+// B image: element (k, n) of B[k][n] (b_trans: B[n*ldb + k]) at
+//   [n / NT][k / KC][hi|lo][(k % KC) / 4][n % NT][k % 4], zero for n >= N.
+__global__ void gemm_image_kernel(GemmImageJobs jobs) {
+  const GemmImageJob& j = jobs.job[blockIdx.y];
+  const int64_t total = (int64_t)j.K * j.ntiles * j.NT;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int k = (int)(i % j.K);
+    const int64_t n = i / j.K;  // padded column
+    float x = 0.f;
+    if (n < j.N) x = j.b_trans ? j.B[n * j.ldb + k] : j.B[(int64_t)k * j.ldb + n];
+    uint32_t hi, lo;
+    tc::split_tf32(x, hi, lo);
+    const int64_t tile = n / j.NT, nl = n % j.NT;
+    const int64_t nch = j.K / KC;
+    const int64_t base = ((tile * nch + k / KC) * 2) * (KC * j.NT) + ((k % KC) / 4) * (4 * j.NT) + nl * 4 + (k % 4);
+    j.out[base] = __uint_as_float(hi);
+    j.out[base + KC * j.NT] = __uint_as_float(lo);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+template <int NT>
+int launch_nt(const GemmArgs& g, const CUtensorMap& map, GemmTcArgs t, cudaStream_t st) {
+  const int sm = (int)GCfg<NT>::TOTAL;
+  cudaFuncSetAttribute(gemm_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  dim3 grid((unsigned)ceil_div(g.G, (int64_t)t.Gb), (unsigned)ceil_div(g.N, NT));
+  gemm_tc_kernel<NT><<<grid, GT_THREADS, sm, st>>>(map, t);
+  return check_launch("gemm_tc_kernel");
+}
+
+}  // namespace
+
+int gemm_tc_nt(int N) { return N <= 64 ? 64 : (N <= 128 ? 128 : (N <= 192 ? 192 : (N <= 256 ? 256 : 128))); }
+
+bool gemm_tc_supported(const GemmArgs& g) {
+  if (g.K % KC || g.K <= 0 || g.R < 1 || g.R > MT || g.N <= 0) return false;
+  const auto a = reinterpret_cast<uintptr_t>(g.A);
+  if (a % 16 || (g.a_rs * 4) % 16 || (g.a_gs * 4) % 16) return false;
+  if (g.R > 1 && g.a_rs < g.K) return false;
+  return encode_fn() != nullptr;
+}
+
+int64_t gemm_image_floats(int K, int N) {
+  const int NT = gemm_tc_nt(N);
+  return (int64_t)ceil_div(N, NT) * NT * K * 2;
+}
+
+int launch_gemm_images(const GemmImageJobs& jobs, int njobs, cudaStream_t st) {
+  if (njobs <= 0) return FSC_OK;
+  if (njobs > kMaxImageJobs) return fail(FSC_ERR_ARGUMENT, "too many GEMM image jobs");
+  gemm_image_kernel<<<dim3(64, (unsigned)njobs), 256, 0, st>>>(jobs);
+  return check_launch("gemm_image_kernel");
+}
+
+int launch_gemm_tc(const GemmArgs& g, const float* bimg, int* err, cudaStream_t st) {
+  const int64_t M = g.G * (int64_t)g.R;
+  if (M == 0 || g.N == 0) return FSC_OK;
+  if (!gemm_tc_supported(g)) return fail(FSC_ERR_UNSUPPORTED, "gemm_tc: unsupported shape or alignment");
+  const int NT = gemm_tc_nt(g.N);
+  GemmTcArgs t{};
+  t.bimg = bimg;
+  t.K = g.K;
+  t.N = g.N;
+  t.G = g.G;
+  t.R = g.R;
+  t.Gb = MT / g.R;
+  t.abox = (uint32_t)(KC * g.R * t.Gb * 4);
+  t.C = g.C;
+  t.c_gs = g.c_gs;
+  t.c_rs = g.c_rs;
+  t.deg_rowptr = g.deg_rowptr;
+  t.bias = g.bias;
+  t.accumulate = g.accumulate;
+  t.alpha = g.alpha;
+  t.err = err;
+  // A as a 3-D tensor (K, R, G) with byte strides a_rs*4, a_gs*4
+  CUtensorMap map;
+  const cuuint64_t dims[3] = {(cuuint64_t)g.K, (cuuint64_t)g.R, (cuuint64_t)g.G};
+  const cuuint64_t strides[2] = {(cuuint64_t)(g.R > 1 ? g.a_rs : g.K) * 4, (cuuint64_t)g.a_gs * 4};
+  const cuuint32_t box[3] = {(cuuint32_t)KC, (cuuint32_t)g.R, (cuuint32_t)t.Gb};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult rc = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(g.A), dims, strides,
+                                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (rc != CUDA_SUCCESS) return fail(FSC_ERR_CUDA, "cuTensorMapEncodeTiled failed for a GEMM operand");
+  switch (NT) {
+    case 64: return launch_nt<64>(g, map, t, st);
+    case 128: return launch_nt<128>(g, map, t, st);
+    case 192: return launch_nt<192>(g, map, t, st);
+    default: return launch_nt<256>(g, map, t, st);
+  }
+}
+
+}  // namespace fsc

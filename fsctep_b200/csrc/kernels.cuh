@@ -123,6 +123,25 @@ struct GemmArgs {
 };
 int launch_gemm(const GemmArgs& a, cudaStream_t st);
 
+// The same GEMM on tcgen05 (gemm_tc.cu): A staged by TMA (two-level rows as a 3-D tensor map),
+// B from a pre-formatted hi/lo image (gemm_image_kernel), 3xTF32.  Needs K % 32 == 0, A and its
+// row strides 16-byte aligned, rows of one group contiguous (a_rs >= K) when R > 1.
+bool gemm_tc_supported(const GemmArgs& a);
+int gemm_tc_nt(int N);
+int64_t gemm_image_floats(int K, int N);
+int launch_gemm_tc(const GemmArgs& a, const float* bimg, int* err, cudaStream_t st);
+constexpr int kMaxImageJobs = 32;
+struct GemmImageJob {
+  const float* B;     // logical B[k][n] = b_trans ? B[n*ldb + k] : B[k*ldb + n]
+  int64_t ldb;
+  int b_trans, K, N, NT, ntiles;
+  float* out;         // gemm_image_floats(K, N) floats
+};
+struct GemmImageJobs {
+  GemmImageJob job[kMaxImageJobs];
+};
+int launch_gemm_images(const GemmImageJobs& jobs, int njobs, cudaStream_t st);
+
 // Readout (pure_cartesian_ictd_layers_full.py:956-1054)
 struct ReadoutArgs {
   int64_t N;
@@ -161,7 +180,7 @@ struct ReadoutTcArgs {
   float* scalars;       // forward output [N][S]
   const float* dscal;   // backward input [N][S]
   float* dFg;           // backward output, layout of Fg
-  const float* gmax;    // [ngram][n_pad] max_c |t_c|^2 per node and Gram block (fp16 range scaling)
+  const float* gmax;    // [ngram][n_pad] max t^2 per node over each Gram block's rows (fp16 range scaling)
   int* err;             // first failing wait site (0 = ok)
   int ngram;            // Gram blocks (rows of block b start at goff[b], m-width 2 gl[b] + 1)
   int goff[4], gl[4];
@@ -179,8 +198,9 @@ struct FgArgs {
   float* Fg;
   const float* dFg;
   int64_t nrows;        // Gram operand rows
-  float* gmax;          // gather: [ngram][n_pad] max over c of sum_m t[c][m]^2 (zeroed by the caller)
-  int lblock[3];        // Gram block of the features with l = 0, 1, 2 (-1: none)
+  float* gmax;          // gather: [ngram][n_pad] max t^2 over the rows of each Gram block (zeroed by the caller)
+  int ngram;
+  int goff[4];          // first row of each Gram block
 };
 int launch_fg_gather(const FgArgs& a, cudaStream_t st);
 int launch_fg_scatter_add(const FgArgs& a, cudaStream_t st);

@@ -16,7 +16,7 @@
 //    contract an earlier one with t.
 // Precision: the MMAs are kind::f16 on a two-term split, hi = fp16(x s), lo = fp16(x s - hi),
 // summing hi*hi + hi*lo + lo*hi (~22 significant bits, like 3xTF32, at twice the K per
-// instruction).  s is a power of two per node (from the Gram bound max_c |t_c|^2, or max |ds|)
+// instruction).  s is a power of two per node (from the Gram bound (2l+1) max t^2, or max |ds|)
 // and per W image (host), so the range fits fp16 and unscaling is exact.  Products accumulate in
 // fp32; every block is a fresh 12-MMA chain and the block sums are added in fp32 registers.
 // All hand-offs go through mbarriers with bounded waits.
@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
     // db >= cb from the T ring
     auto gen_row = [&](auto mconst, int b, int cb) {
       constexpr int M = decltype(mconst)::value;
-      const float scale = tc::f16_range_scale(a.gmax[(int64_t)b * a.n_pad + n]);
+      const float scale = tc::f16_range_scale((float)M * a.gmax[(int64_t)b * a.n_pad + n]);
       r_start[2] = r_start[1];
       r_inv[2] = r_inv[1];
       r_start[1] = r_start[0];
@@ -561,46 +561,39 @@ __device__ __forceinline__ int64_t fg_index(int64_t r, int64_t n, int64_t nrows)
   return (n / TILE) * nrows * TILE + r * TILE + (n % TILE);
 }
 
-// Also: gmax[block(l)][n] = max over this layer's channels c of sum_m t[l][c][m]^2 (atomic max
-// over layers; non-negative floats order like their bit patterns), the range bound of the
-// fp16 split of node n's Gram values (|G_cd| <= max_c |t_c|^2).
+// Also: gmax[b][n] = max of t^2 over the Gram operand rows of block b (atomic max over the
+// layers' CTAs; non-negative floats order like their bit patterns).  The rows of a block are the
+// reference's flat split of the concatenated features, so t_b[c][m] is an arbitrary feature
+// element; |G_cd| = |sum_m t_cm t_dm| <= (2l+1) gmax bounds the fp16 split's range.
 __global__ void fg_gather_kernel(FgArgs a) {
   extern __shared__ float tile[];  // [FG_NODES][9C + 1]
-  __shared__ unsigned int nmax[3][FG_NODES];
+  __shared__ unsigned int nmax[4][FG_NODES];
   const int layer = blockIdx.y;
   const int W = 9 * a.C;
   const int64_t n0 = (int64_t)blockIdx.x * FG_NODES;
   const float* src = a.feats[layer];
-  if (threadIdx.x < 3 * FG_NODES) (&nmax[0][0])[threadIdx.x] = 0u;
+  if (threadIdx.x < 4 * FG_NODES) (&nmax[0][0])[threadIdx.x] = 0u;
   for (int i = threadIdx.x; i < FG_NODES * W; i += blockDim.x) {
     const int nl = i / W, kc = i - nl * W;
     const int64_t n = n0 + nl;
     tile[nl * (W + 1) + kc] = n < a.N ? src[n * W + kc] : 0.f;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < FG_NODES * a.C; i += blockDim.x) {
-    const int nl = i / a.C, c = i - nl * a.C;
-    const float* t = tile + nl * (W + 1) + c;
-    float s0 = t[0] * t[0], s1 = 0.f, s2 = 0.f;
-#pragma unroll
-    for (int k = 1; k < 4; ++k) s1 = fmaf(t[k * a.C], t[k * a.C], s1);
-#pragma unroll
-    for (int k = 4; k < 9; ++k) s2 = fmaf(t[k * a.C], t[k * a.C], s2);
-    atomicMax(&nmax[0][nl], __float_as_uint(s0));
-    atomicMax(&nmax[1][nl], __float_as_uint(s1));
-    atomicMax(&nmax[2][nl], __float_as_uint(s2));
-  }
-  __syncthreads();
-  if (threadIdx.x < 3 * FG_NODES) {
-    const int l = threadIdx.x / FG_NODES, nl = threadIdx.x - l * FG_NODES;
-    const int b = a.lblock[l];
-    if (b >= 0 && n0 + nl < a.n_pad)
-      atomicMax(reinterpret_cast<unsigned int*>(a.gmax) + (int64_t)b * a.n_pad + n0 + nl, nmax[l][nl]);
-  }
   const int32_t* inv = a.xinv + (int64_t)layer * W;
   for (int i = threadIdx.x; i < FG_NODES * W; i += blockDim.x) {
     const int kc = i / FG_NODES, nl = i - kc * FG_NODES;
-    a.Fg[fg_index(inv[kc], n0 + nl, a.nrows)] = tile[nl * (W + 1) + kc];
+    const int r = inv[kc];
+    const float v = tile[nl * (W + 1) + kc];
+    a.Fg[fg_index(r, n0 + nl, a.nrows)] = v;
+    int b = 0;
+    while (b + 1 < a.ngram && r >= a.goff[b + 1]) ++b;
+    atomicMax(&nmax[b][nl], __float_as_uint(v * v));
+  }
+  __syncthreads();
+  if (threadIdx.x < 4 * FG_NODES) {
+    const int b = threadIdx.x / FG_NODES, nl = threadIdx.x - b * FG_NODES;
+    if (b < a.ngram && n0 + nl < a.n_pad)
+      atomicMax(reinterpret_cast<unsigned int*>(a.gmax) + (int64_t)b * a.n_pad + n0 + nl, nmax[b][nl]);
   }
 }
 

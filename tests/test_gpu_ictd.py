@@ -108,3 +108,40 @@ def test_tensor_core_radial_matches_cuda_core(nb, kind, n_cells):
     assert (e - er).abs().max().item() <= 1e-5 * er.abs().max().item(), (e, er)
     assert U.rel_max(out["forces"].cpu().numpy(), ref["forces"].cpu().numpy()) <= 1e-4
     assert U.rel_max(out["stress"].cpu().numpy(), ref["stress"].cpu().numpy()) <= 1e-4
+
+
+@pytest.mark.parametrize("channels,n_cells", [(64, (5, 3, 3)), (32, (3, 3, 5))])
+def test_tensor_core_gemms_match_cuda_core(channels, n_cells):
+    """tcgen05 channel-mixing / MainNet GEMMs (default) vs the CUDA-core GEMM: node counts that
+    leave partial 128-row tiles for every component count R (1, 3, 5), and N < tile width (C = 32)."""
+    from fsctep_b200 import _native as NAT
+    from fsctep_b200 import systems
+    from fsctep_b200.ictd import ICTDConfig, ICTDEngine
+    from fsctep_b200.models import reference_state_dict_shapes
+    from fsctep_b200.neighbors import build_graph
+    from fsctep_b200.weights import seeded_state_dict
+
+    cfg = ICTDConfig(channels=channels, num_interaction=3, number_of_basis=8, max_radius=5.0,
+                     function_type="gaussian", max_atomvalue=16)
+    eng = ICTDEngine(seeded_state_dict(reference_state_dict_shapes(cfg), 9), cfg, "cuda")
+    s = systems.diamond_crystal(n_cells=n_cells, seed=27)
+    dev = torch.device("cuda")
+    pos, cell = torch.tensor(s["pos"], device=dev), torch.tensor(s["cell"], device=dev)
+    g = build_graph(pos, cell, 5.0)
+    Z, b = torch.tensor(s["Z"], device=dev), torch.tensor(s["batch"], device=dev)
+    assert pos.shape[0] % 125 and pos.shape[0] % 126 and pos.shape[0] % 128
+    try:
+        NAT.lib().fsc_ictd_set_gemm_path(1)
+        ref = eng.energy_forces(pos, Z, b, cell, g)
+        torch.cuda.synchronize()
+        NAT.lib().fsc_ictd_set_gemm_path(0)
+        out = eng.energy_forces(pos, Z, b, cell, g)
+        torch.cuda.synchronize()
+        assert eng.status() == 0
+    finally:
+        NAT.lib().fsc_ictd_set_gemm_path(0)
+    e, er = out["energy"].double().cpu(), ref["energy"].double().cpu()
+    assert (e - er).abs().max().item() <= 1e-5 * er.abs().max().item(), (e, er)
+    assert U.rel_max(out["forces"].cpu().numpy(), ref["forces"].cpu().numpy()) <= 1e-4
+    assert U.rel_max(out["atom_energy"].cpu().numpy(), ref["atom_energy"].cpu().numpy()) <= 1e-4
+    assert U.rel_max(out["stress"].cpu().numpy(), ref["stress"].cpu().numpy()) <= 1e-4
