@@ -410,6 +410,7 @@ int forward(Ctx& c) {
     if (cudaMemsetAsync(p.gmax, 0, sizeof(float) * p.ngram * p.n_pad, st) != cudaSuccess)
       return fail(FSC_ERR_CUDA, "memset gmax");
     FSC_TRY(launch_fg_gather(fg_args(p, w), st));
+    prof::mark("readout_gather", st);
     FSC_TRY(launch_readout_fwd_tc(tc_args(p, w->wimg_fwd), st));
   }
   if (!p.tc && cudaMemsetAsync(p.scalars, 0, sizeof(float) * p.nro * p.S, st) != cudaSuccess)
@@ -465,6 +466,7 @@ int backward(Ctx& c) {
   prof::mark("readout_mlp_backward", st);
   if (p.tc) {
     FSC_TRY(launch_readout_bwd_tc(tc_args(p, w->wimg_bwd), st));
+    prof::mark("readout_gram_backward", st);
     FSC_TRY(launch_fg_scatter_add(fg_args(p, w), st));
   }
   for (int b = 0; b < p.ngram && !p.tc; ++b) {
@@ -477,7 +479,7 @@ int backward(Ctx& c) {
       FSC_TRY(launch_gram_apply(ra, b, n0, nn, p.chunkbuf, p.grads, st));
     }
   }
-  prof::mark("readout_gram_backward", st);
+  prof::mark(p.tc ? "readout_scatter" : "readout_gram_backward", st);
   // the readout only seeded atoms [0, nro): the rest of each evaluated layer starts at zero
   for (int k = 0; k + 1 < p.nint; ++k)
     if (p.nk[k] > p.nro &&

@@ -108,8 +108,9 @@ __device__ __forceinline__ int fwd_block(int b, int cb, int db, int nb) {
 //  * producer warp: for every block s (Gram block b, c-block cb <= d-block db) bulk-copies the W
 //    block s and the d-block's 8 (2l+1) t rows (one contiguous chunk of the tile-blocked Fg), and
 //    once per (b, cb) the c-block's rows, into shared-memory rings;
-//  * 16 generator warps: thread = node (TMEM lane) and quarter qq of the d-rows; builds its 16
-//    pairs (c, d = 2qq + dd) of the Gram block from shared memory, scales them by the node's
+//  * 16 generator warps: thread = node (TMEM lane) and quarter qq of the block: c-rows
+//    4(qq & 1) + ci (held in registers for the whole block row), d-rows 4(qq >> 1) + di; builds
+//    its 16 pairs of the Gram block (packed fp32 FMAs), scales them by the node's
 //    power-of-two range factor (from gmax) and splits them into fp16 hi + lo in TMEM; adds output
 //    columns [16qq, 16qq + 16) of an earlier block's fresh 12-MMA accumulator, unscaled (exact
 //    powers of two), to fp32 registers, so the tensor core never carries a long accumulation chain;
@@ -224,18 +225,28 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
         ok = false;
         return;
       }
-      const float* pc = sC + (rr % NSTC) * (TBYTES / 4) + row;
+      float tcv[4][M];
+      {
+        const float* pc = sC + (rr % NSTC) * (TBYTES / 4) + 4 * (qq & 1) * M * TILE + row;
+#pragma unroll
+        for (int ci = 0; ci < 4; ++ci)
+#pragma unroll
+          for (int m = 0; m < M; ++m) tcv[ci][m] = pc[(ci * M + m) * TILE];
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(empty_C + rr % NSTC);
+      ++rr;
       for (int db = cb; db < nb; ++db, ++s) {
         if (!ring_full(full_T, s, NSTT, a.err, 10)) {
           ok = false;
           return;
         }
-        float tdv[2][M];
-        const float* pt = sT + (s % NSTT) * (TBYTES / 4) + 2 * qq * M * TILE + row;
+        float tdv[4][M];
+        const float* pt = sT + (s % NSTT) * (TBYTES / 4) + 4 * (qq >> 1) * M * TILE + row;
 #pragma unroll
-        for (int dd = 0; dd < 2; ++dd)
+        for (int di = 0; di < 4; ++di)
 #pragma unroll
-          for (int m = 0; m < M; ++m) tdv[dd][m] = pt[(dd * M + m) * TILE];
+          for (int m = 0; m < M; ++m) tdv[di][m] = pt[(di * M + m) * TILE];
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(empty_T + s % NSTT);
         const int st = s & 1;
@@ -243,22 +254,19 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
           ok = false;
           return;
         }
-        // pairs (c, d = 2qq + dd) -> A element 16qq + 2c + dd (the forward W images use this
-        // order), fp16 packed two per TMEM column: column 8qq + c
+        // pairs (c = 4(qq&1) + ci, d = 4(qq>>1) + di) -> A element 16qq + 4ci + di (the forward W
+        // images use this order), fp16 packed two per TMEM column: column 8qq + 2ci + di/2
         uint32_t hi[8], lo[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float tc_[M];
+        for (int ci = 0; ci < 4; ++ci)
 #pragma unroll
-          for (int m = 0; m < M; ++m) tc_[m] = pc[(c * M + m) * TILE];
-          float g0 = 0.f, g1 = 0.f;
+          for (int dp = 0; dp < 2; ++dp) {
+            float2 g = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int m = 0; m < M; ++m) {
-            g0 = fmaf(tc_[m], tdv[0][m], g0);
-            g1 = fmaf(tc_[m], tdv[1][m], g1);
+            for (int m = 0; m < M; ++m)
+              g = __ffma2_rn(make_float2(tcv[ci][m], tcv[ci][m]), make_float2(tdv[2 * dp][m], tdv[2 * dp + 1][m]), g);
+            tc::split_f16x2(g.x * scale, g.y * scale, hi[2 * ci + dp], lo[2 * ci + dp]);
           }
-          tc::split_f16x2(g0 * scale, g1 * scale, hi[c], lo[c]);
-        }
         tc::tmem_st8(tA(st, 0) + lane_off + 8u * qq, hi);
         tc::tmem_st8(tA(st, 1) + lane_off + 8u * qq, lo);
         tc::tmem_wait_st();
@@ -270,9 +278,6 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
           if (!ok) return;
         }
       }
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(empty_C + rr % NSTC);
-      ++rr;
     };
     const RowOrder order(a.ngram, nb);
     for (int i = 0; i < order.rows && ok; ++i) {
@@ -469,11 +474,12 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
 #pragma unroll
           for (int m = 0; m < M; ++m) td[m] = pt[(dq * M + m) * TILE];
           if (dq == 0) tc::tmem_wait_ld();
+          const float2 h2 = make_float2(__uint_as_float(hv[dq >> 3][dq & 7]), __uint_as_float(hv[dq >> 3][8 + (dq & 7)]));
 #pragma unroll
-          for (int cq = 0; cq < 2; ++cq) {
-            const float hcd = __uint_as_float(hv[dq >> 3][cq * 8 + (dq & 7)]);
-#pragma unroll
-            for (int m = 0; m < M; ++m) acc[cq][m] = fmaf(hcd, td[m], acc[cq][m]);
+          for (int m = 0; m < M; ++m) {
+            const float2 t2 = __ffma2_rn(h2, make_float2(td[m], td[m]), make_float2(acc[0][m], acc[1][m]));
+            acc[0][m] = t2.x;
+            acc[1][m] = t2.y;
           }
         }
         tc::tc_fence_before();
@@ -557,63 +563,111 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
 // Fg[r][n] = feats[layer(r)][n][kc(r)] via xinv (storage -> row); tile of 32 nodes x one layer.
 constexpr int FG_NODES = 32;
 
-__device__ __forceinline__ int64_t fg_index(int64_t r, int64_t n, int64_t nrows) {
-  return (n / TILE) * nrows * TILE + r * TILE + (n % TILE);
-}
 
 // Also: gmax[b][n] = max of t^2 over the Gram operand rows of block b (atomic max over the
 // layers' CTAs; non-negative floats order like their bit patterns).  The rows of a block are the
 // reference's flat split of the concatenated features, so t_b[c][m] is an arbitrary feature
 // element; |G_cd| = |sum_m t_cm t_dm| <= (2l+1) gmax bounds the fp16 split's range.
-__global__ void fg_gather_kernel(FgArgs a) {
-  extern __shared__ float tile[];  // [FG_NODES][9C + 1]
+// Both passes keep several 16-byte loads per thread in flight (memory bound transposes).
+template <int C>
+__global__ void __launch_bounds__(256) fg_gather_kernel(FgArgs a) {
+  constexpr int W = 9 * C, W4 = W / 4, TS = W + 1, ROUND = 6;
+  constexpr int PER = FG_NODES * W4 / 256;  // float4 loads per thread
+  extern __shared__ float tile[];  // [FG_NODES][TS], then xinv of this layer [W]
+  int* sinv = reinterpret_cast<int*>(tile + FG_NODES * TS);
   __shared__ unsigned int nmax[4][FG_NODES];
-  const int layer = blockIdx.y;
-  const int W = 9 * a.C;
+  const int layer = blockIdx.y, tid = threadIdx.x;
   const int64_t n0 = (int64_t)blockIdx.x * FG_NODES;
-  const float* src = a.feats[layer];
-  if (threadIdx.x < 4 * FG_NODES) (&nmax[0][0])[threadIdx.x] = 0u;
-  for (int i = threadIdx.x; i < FG_NODES * W; i += blockDim.x) {
-    const int nl = i / W, kc = i - nl * W;
-    const int64_t n = n0 + nl;
-    tile[nl * (W + 1) + kc] = n < a.N ? src[n * W + kc] : 0.f;
+  const float4* src4 = reinterpret_cast<const float4*>(a.feats[layer]);
+  if (tid < 4 * FG_NODES) (&nmax[0][0])[tid] = 0u;
+  for (int i = tid; i < W; i += 256) sinv[i] = a.xinv[(int64_t)layer * W + i];
+#pragma unroll
+  for (int j0 = 0; j0 < PER; j0 += ROUND) {
+    float4 v[ROUND];
+#pragma unroll
+    for (int j = 0; j < ROUND; ++j) {
+      const int i = tid + 256 * (j0 + j), nl = i / W4, k4 = i - nl * W4;
+      v[j] = (j0 + j < PER && n0 + nl < a.N) ? src4[(n0 + nl) * W4 + k4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < ROUND; ++j) {
+      if (j0 + j >= PER) break;
+      const int i = tid + 256 * (j0 + j), nl = i / W4, k4 = i - nl * W4;
+      float* t = tile + nl * TS + 4 * k4;
+      t[0] = v[j].x;
+      t[1] = v[j].y;
+      t[2] = v[j].z;
+      t[3] = v[j].w;
+    }
   }
   __syncthreads();
-  const int32_t* inv = a.xinv + (int64_t)layer * W;
-  for (int i = threadIdx.x; i < FG_NODES * W; i += blockDim.x) {
-    const int kc = i / FG_NODES, nl = i - kc * FG_NODES;
-    const int r = inv[kc];
-    const float v = tile[nl * (W + 1) + kc];
-    a.Fg[fg_index(r, n0 + nl, a.nrows)] = v;
-    int b = 0;
-    while (b + 1 < a.ngram && r >= a.goff[b + 1]) ++b;
-    atomicMax(&nmax[b][nl], __float_as_uint(v * v));
+  // thread = one node (nl) and every 8th storage column; a warp writes one 128-byte row segment
+  const int nl = tid & (FG_NODES - 1);
+  const int64_t n = n0 + nl;
+  float* fg = a.Fg + (n / TILE) * a.nrows * TILE + (n % TILE);
+  float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
+#pragma unroll 8
+  for (int kc = tid >> 5; kc < W; kc += 8) {
+    const int r = sinv[kc];
+    const float v = tile[nl * TS + kc];
+    fg[(int64_t)r * TILE] = v;
+    const float q = v * v;
+    if (r < a.goff[1] || a.ngram == 1) m0 = fmaxf(m0, q);
+    else if (r < a.goff[2] || a.ngram == 2) m1 = fmaxf(m1, q);
+    else if (r < a.goff[3] || a.ngram == 3) m2 = fmaxf(m2, q);
+    else m3 = fmaxf(m3, q);
   }
+  atomicMax(&nmax[0][nl], __float_as_uint(m0));
+  atomicMax(&nmax[1][nl], __float_as_uint(m1));
+  atomicMax(&nmax[2][nl], __float_as_uint(m2));
+  atomicMax(&nmax[3][nl], __float_as_uint(m3));
   __syncthreads();
-  if (threadIdx.x < 4 * FG_NODES) {
-    const int b = threadIdx.x / FG_NODES, nl = threadIdx.x - b * FG_NODES;
-    if (b < a.ngram && n0 + nl < a.n_pad)
-      atomicMax(reinterpret_cast<unsigned int*>(a.gmax) + (int64_t)b * a.n_pad + n0 + nl, nmax[b][nl]);
+  if (tid < 4 * FG_NODES) {
+    const int b = tid / FG_NODES, l = tid - b * FG_NODES;
+    if (b < a.ngram && n0 + l < a.n_pad)
+      atomicMax(reinterpret_cast<unsigned int*>(a.gmax) + (int64_t)b * a.n_pad + n0 + l, nmax[b][l]);
   }
 }
 
 // grads[layer][n][kc] += dFg[r(kc)][n]
-__global__ void fg_scatter_add_kernel(FgArgs a) {
+template <int C>
+__global__ void __launch_bounds__(256) fg_scatter_add_kernel(FgArgs a) {
+  constexpr int W = 9 * C, W4 = W / 4, TS = W + 1, ROUND = 6;
+  constexpr int PER = FG_NODES * W4 / 256;
   extern __shared__ float tile[];
-  const int layer = blockIdx.y;
-  const int W = 9 * a.C;
+  int* sinv = reinterpret_cast<int*>(tile + FG_NODES * TS);
+  const int layer = blockIdx.y, tid = threadIdx.x;
   const int64_t n0 = (int64_t)blockIdx.x * FG_NODES;
-  const int32_t* inv = a.xinv + (int64_t)layer * W;
-  for (int i = threadIdx.x; i < FG_NODES * W; i += blockDim.x) {
-    const int kc = i / FG_NODES, nl = i - kc * FG_NODES;
-    tile[nl * (W + 1) + kc] = a.dFg[fg_index(inv[kc], n0 + nl, a.nrows)];
+  for (int i = tid; i < W; i += 256) sinv[i] = a.xinv[(int64_t)layer * W + i];
+  __syncthreads();
+  {
+    const int nl = tid & (FG_NODES - 1);
+    const int64_t n = n0 + nl;
+    const float* fg = a.dFg + (n / TILE) * a.nrows * TILE + (n % TILE);
+#pragma unroll 8
+    for (int kc = tid >> 5; kc < W; kc += 8) tile[nl * TS + kc] = fg[(int64_t)sinv[kc] * TILE];
   }
   __syncthreads();
-  float* dst = a.grads[layer];
-  for (int i = threadIdx.x; i < FG_NODES * W; i += blockDim.x) {
-    const int nl = i / W, kc = i - nl * W;
-    const int64_t n = n0 + nl;
-    if (n < a.N) dst[n * W + kc] += tile[nl * (W + 1) + kc];
+  float4* dst4 = reinterpret_cast<float4*>(a.grads[layer]);
+#pragma unroll
+  for (int j0 = 0; j0 < PER; j0 += ROUND) {
+    float4 g[ROUND];
+#pragma unroll
+    for (int j = 0; j < ROUND; ++j) {
+      const int i = tid + 256 * (j0 + j), nl = i / W4, k4 = i - nl * W4;
+      if (j0 + j < PER && n0 + nl < a.N) g[j] = dst4[(n0 + nl) * W4 + k4];
+    }
+#pragma unroll
+    for (int j = 0; j < ROUND; ++j) {
+      const int i = tid + 256 * (j0 + j), nl = i / W4, k4 = i - nl * W4;
+      if (j0 + j >= PER || n0 + nl >= a.N) continue;
+      const float* t = tile + nl * TS + 4 * k4;
+      g[j].x += t[0];
+      g[j].y += t[1];
+      g[j].z += t[2];
+      g[j].w += t[3];
+      dst4[(n0 + nl) * W4 + k4] = g[j];
+    }
   }
 }
 
@@ -659,19 +713,31 @@ int launch_readout_bwd_tc(const ReadoutTcArgs& a, cudaStream_t st) {
 
 int launch_fg_gather(const FgArgs& a, cudaStream_t st) {
   if (a.N == 0) return FSC_OK;
-  const int sm = FG_NODES * (9 * a.C + 1) * (int)sizeof(float);
-  cudaFuncSetAttribute(fg_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  if (a.C != 32 && a.C != 64) return fail(FSC_ERR_UNSUPPORTED, "fg_gather: C must be 32 or 64");
+  const int sm = (FG_NODES * (9 * a.C + 1) + 9 * a.C) * (int)sizeof(float);
   dim3 grid((unsigned)ceil_div(a.n_pad, FG_NODES), (unsigned)a.nint);
-  fg_gather_kernel<<<grid, 256, sm, st>>>(a);
+  if (a.C == 64) {
+    cudaFuncSetAttribute(fg_gather_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    fg_gather_kernel<64><<<grid, 256, sm, st>>>(a);
+  } else {
+    cudaFuncSetAttribute(fg_gather_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    fg_gather_kernel<32><<<grid, 256, sm, st>>>(a);
+  }
   return check_launch("fg_gather_kernel");
 }
 
 int launch_fg_scatter_add(const FgArgs& a, cudaStream_t st) {
   if (a.N == 0) return FSC_OK;
-  const int sm = FG_NODES * (9 * a.C + 1) * (int)sizeof(float);
-  cudaFuncSetAttribute(fg_scatter_add_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  if (a.C != 32 && a.C != 64) return fail(FSC_ERR_UNSUPPORTED, "fg_scatter_add: C must be 32 or 64");
+  const int sm = (FG_NODES * (9 * a.C + 1) + 9 * a.C) * (int)sizeof(float);
   dim3 grid((unsigned)ceil_div(a.n_pad, FG_NODES), (unsigned)a.nint);
-  fg_scatter_add_kernel<<<grid, 256, sm, st>>>(a);
+  if (a.C == 64) {
+    cudaFuncSetAttribute(fg_scatter_add_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    fg_scatter_add_kernel<64><<<grid, 256, sm, st>>>(a);
+  } else {
+    cudaFuncSetAttribute(fg_scatter_add_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    fg_scatter_add_kernel<32><<<grid, 256, sm, st>>>(a);
+  }
   return check_launch("fg_scatter_add_kernel");
 }
 

@@ -146,10 +146,11 @@ def readout_images(W_read, C: int, nint: int, ls=(0, 1, 2)):
         S = Wr.shape[0]
         Ws = 0.5 * (Wr + Wr.transpose(1, 2))
         blk = Ws.reshape(S, nb, 8, nb, 8).permute(1, 3, 0, 2, 4).reshape(nb, nb, S, 64)  # [cb][db][o][pair]
-        # forward: cb <= db, x2 off the diagonal, pairs reordered (c, d = 2qq + dd) -> 16qq + 2c + dd
-        # (the generator thread of quarter qq owns d-rows 2qq, 2qq+1); B = [k/8][o][k%8], K = pairs
+        # forward: cb <= db, x2 off the diagonal, pairs reordered (c = 4ch + ci, d = 4dh + di) ->
+        # 16qq + 4ci + di with qq = ch + 2dh (the generator thread of quarter qq owns those c and d
+        # rows); B = [k/8][o][k%8], K = pairs
         f = blk[iu[0], iu[1]] * torch.where(iu[0] == iu[1], 1.0, 2.0).to(blk)[:, None, None]
-        f = f.reshape(-1, S, 8, 4, 2).permute(0, 1, 3, 2, 4).reshape(-1, S, 64)
+        f = f.reshape(-1, S, 2, 4, 2, 4).permute(0, 1, 4, 2, 3, 5).reshape(-1, S, 64)
         fwd.append(f.reshape(-1, S, 8, 8).permute(0, 2, 1, 3))
         # backward: all blocks in pairs of d-blocks (db even, db + 1) -> N = 128 pairs per MMA,
         # B = [o/8][pair of the two blocks][o%8], K = outputs o
