@@ -53,6 +53,8 @@ struct Plan {
   int n_hidden;
   // workspace
   int32_t* dst;
+  int32_t* tr_dst;
+  float* invdeg;
   float* edge_y;
   float* gates;
   float* feats[8];
@@ -144,6 +146,8 @@ void layout(Plan& p, Arena& ar, const fsc_ictd_config* cfg, int64_t N, int64_t E
   for (int k = 0; k < p.n_hidden; ++k) maxw = std::max(maxw, p.hidden[k]);
   const int64_t fsz = N * NK * p.C;
   p.dst = ar.take<int32_t>(E);
+  p.tr_dst = ar.take<int32_t>(E);
+  p.invdeg = ar.take<float>(N);
   p.edge_y = ar.take<float>(E * 12);
   p.gates = ar.take<float>((int64_t)p.nint * E * 12);
   for (int k = 0; k < p.nint; ++k) p.feats[k] = ar.take<float>(fsz);
@@ -337,6 +341,8 @@ ConvArgs conv_args(const Ctx& c, int layer) {
   a.dst_limit = c.p.nk[layer];
   a.src_limit = layer > 0 ? c.p.nk[layer - 1] : c.p.N;
   a.err = c.p.err;
+  a.tr_dst = c.p.tr_dst;
+  a.invdeg = c.p.invdeg;
   return a;
 }
 
@@ -371,6 +377,7 @@ int forward(Ctx& c) {
   prof::mark("begin", st);
   FSC_TRY(build_gemm_images(p, w, st));
   FSC_TRY(launch_edge_dst(g->row_ptr, p.dst, p.N, st));
+  FSC_TRY(launch_transpose_aux(g->row_ptr, p.dst, g->tr_eid, p.N, p.E, p.tr_dst, p.invdeg, st));
   EdgeFwdArgs ef{};
   ef.E = p.E; ef.pos = g->pos; ef.src = g->src; ef.dst = p.dst; ef.batch = g->batch; ef.cell = g->cell;
   ef.shift = g->shift; ef.tables = w->tables; ef.rad = radial(w); ef.nint = p.nint; ef.nb = p.nb;

@@ -181,7 +181,7 @@ struct RPath {
 // ---------------------------------------------------------------- conv2 forward: Z
 // The next edge's sender row, Y and gates are loaded while the current edge is contracted.
 template <int CPL>
-__global__ void __launch_bounds__(CONV_WARPS * 32) conv2_z_kernel(ConvArgs a, const float* __restrict__ x,
+__global__ void __launch_bounds__(CONV_WARPS * 32, 4) conv2_z_kernel(ConvArgs a, const float* __restrict__ x,
                                                                   float* __restrict__ Z) {
   __shared__ float cg2[NQ * 5];
   __shared__ EdgeBuf bufs[CONV_WARPS];
@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_z_kernel(ConvArgs a, co
 
 // ---------------------------------------------------------------- conv2 backward: R (src-centric)
 template <int CPL>
-__global__ void __launch_bounds__(CONV_WARPS * 32) conv2_r_kernel(ConvArgs a, const float* __restrict__ G,
+__global__ void __launch_bounds__(CONV_WARPS * 32, 4) conv2_r_kernel(ConvArgs a, const float* __restrict__ G,
                                                                   float* __restrict__ R) {
   __shared__ float cg2[NQ * 5];
   __shared__ EdgeBuf bufs[CONV_WARPS];
@@ -259,11 +259,10 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_r_kernel(ConvArgs a, co
   // a receiver not evaluated in this layer carries no gradient
   auto fetch = [&](int t, float (&gd)[NK][CPL], float& yg) -> bool {
     const int64_t e = a.tr_eid[t];
-    const int64_t d = a.dst[e];
+    const int64_t d = a.tr_dst[t];  // precomputed: no dependent index chain through dst[e]
     yg = load_yg(a, e, lane);
     const bool on = d < a.dst_limit;
-    const int deg = on ? a.row_ptr[d + 1] - a.row_ptr[d] : 1;
-    const float inv = 1.f / (float)(deg > 1 ? deg : 1);
+    const float inv = on ? a.invdeg[d] : 0.f;
 #pragma unroll
     for (int k = 0; k < NK; ++k)
 #pragma unroll

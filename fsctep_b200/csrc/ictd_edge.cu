@@ -341,6 +341,26 @@ int launch_forces(const int32_t* row_ptr, const int32_t* tr_ptr, const int32_t* 
   return check_launch("forces_kernel");
 }
 
+// Per transposed-CSR slot t: the receiver of edge tr_eid[t]; per node: 1 / max(in-degree, 1).
+__global__ void transpose_aux_kernel(const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ dst,
+                                     const int32_t* __restrict__ tr_eid, int64_t N, int64_t E,
+                                     int32_t* __restrict__ tr_dst, float* __restrict__ invdeg) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < E) tr_dst[i] = dst[tr_eid[i]];
+  if (i < N) {
+    const int d = row_ptr[i + 1] - row_ptr[i];
+    invdeg[i] = 1.f / (float)(d > 1 ? d : 1);
+  }
+}
+
+int launch_transpose_aux(const int32_t* row_ptr, const int32_t* dst, const int32_t* tr_eid, int64_t N, int64_t E,
+                         int32_t* tr_dst, float* invdeg, cudaStream_t st) {
+  const int64_t n = E > N ? E : N;
+  if (n == 0) return FSC_OK;
+  transpose_aux_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(row_ptr, dst, tr_eid, N, E, tr_dst, invdeg);
+  return check_launch("transpose_aux_kernel");
+}
+
 int launch_edge_dst(const int32_t* row_ptr, int32_t* dst, int64_t N, cudaStream_t st) {
   if (N == 0) return FSC_OK;
   edge_dst_kernel<<<(unsigned)ceil_div(N, 8), 256, 0, st>>>(row_ptr, dst, N);

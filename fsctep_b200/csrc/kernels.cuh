@@ -67,6 +67,8 @@ int launch_edge_backward(const EdgeBwdArgs& a, cudaStream_t st);
 int launch_forces(const int32_t* row_ptr, const int32_t* tr_ptr, const int32_t* tr_eid, const float* g,
                   float* F, int64_t N, cudaStream_t st);
 int launch_edge_dst(const int32_t* row_ptr, int32_t* dst, int64_t N, cudaStream_t st);
+int launch_transpose_aux(const int32_t* row_ptr, const int32_t* dst, const int32_t* tr_eid, int64_t N, int64_t E,
+                         int32_t* tr_dst, float* invdeg, cudaStream_t st);
 
 struct ConvArgs {
   int64_t N, E;
@@ -87,6 +89,8 @@ struct ConvArgs {
   int64_t dst_limit;     // conv2_r: edges whose dst >= dst_limit carry no gradient
   int64_t src_limit;     // conv2_z: an edge whose src >= src_limit is skipped and flags err (70)
   int* err;
+  const int32_t* tr_dst; // [E] receiver of edge tr_eid[t] (conv2_r)
+  const float* invdeg;   // [N] 1 / max(in-degree, 1) (conv2_r)
 };
 
 // conv1: f1[n][k][c]
