@@ -181,7 +181,7 @@ struct RPath {
 // ---------------------------------------------------------------- conv2 forward: Z
 // The next edge's sender row, Y and gates are loaded while the current edge is contracted.
 template <int CPL>
-__global__ void __launch_bounds__(CONV_WARPS * 32, 4) conv2_z_kernel(ConvArgs a, const float* __restrict__ x,
+__global__ void __launch_bounds__(CONV_WARPS * 32) conv2_z_kernel(ConvArgs a, const float* __restrict__ x,
                                                                   float* __restrict__ Z) {
   __shared__ float cg2[NQ * 5];
   __shared__ EdgeBuf bufs[CONV_WARPS];
@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(CONV_WARPS * 32, 4) conv2_z_kernel(ConvArgs a,
 
 // ---------------------------------------------------------------- conv2 backward: R (src-centric)
 template <int CPL>
-__global__ void __launch_bounds__(CONV_WARPS * 32, 4) conv2_r_kernel(ConvArgs a, const float* __restrict__ G,
+__global__ void __launch_bounds__(CONV_WARPS * 32) conv2_r_kernel(ConvArgs a, const float* __restrict__ G,
                                                                   float* __restrict__ R) {
   __shared__ float cg2[NQ * 5];
   __shared__ EdgeBuf bufs[CONV_WARPS];
