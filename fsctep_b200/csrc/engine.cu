@@ -257,52 +257,29 @@ GemmArgs gemm(const float* A, int64_t a_gs, int64_t a_rs, const float* B, int64_
   return g;
 }
 
-// GEMM on the tensor cores when an image exists and the shape qualifies, else on CUDA cores.
-int run_gemm(const GemmArgs& g, const float* img, int* err, cudaStream_t st) {
-  if (img && gemm_tc_supported(g)) return launch_gemm_tc(g, img, err, st);
-  return launch_gemm(g, st);
-}
-
 // Block offset of l-block l inside one layer's mix weights (3, 4, 4 paths of C x C).
 inline int64_t mix_boff(int l, int C) { return (int64_t)(l == 0 ? 0 : (l == 1 ? 3 : 7)) * C * C; }
 
 // Builds every weight image the tensor-core GEMMs of this call read.
 int build_gemm_images(const Plan& p, const fsc_ictd_weights* w, cudaStream_t st) {
   if (!p.gtc) return FSC_OK;
-  GemmImageJobs jobs{};
-  int n = 0;
-  auto add = [&](const float* B, int64_t ldb, int trans, int K, int N, float* out) -> int {
-    GemmImageJob& j = jobs.job[n++];
-    j.B = B;
-    j.ldb = ldb;
-    j.b_trans = trans;
-    j.K = K;
-    j.N = N;
-    j.NT = gemm_tc_nt(N);
-    j.ntiles = (int)ceil_div(N, j.NT);
-    j.out = out;
-    if (n == kMaxImageJobs) {
-      FSC_TRY(launch_gemm_images(jobs, n, st));
-      n = 0;
-    }
-    return FSC_OK;
-  };
+  GemmImageBatch jobs;
   const int C = p.C;
   for (int k = 1; k < p.nint; ++k) {
     const int64_t lo = (int64_t)(k - 1) * NP * C * C;
     for (int l = 0; l < 3; ++l) {
-      FSC_TRY(add(w->mix_fwd + lo + mix_boff(l, C), C, 0, NP3(l) * C, C, p.img_fwd[k][l]));
-      FSC_TRY(add(w->mix_bwd + lo + mix_boff(l, C), NP3(l) * C, 0, C, NP3(l) * C, p.img_dz[k][l]));
-      FSC_TRY(add(w->mix_dx + lo + mix_boff(l, C), C, 0, NP1(l) * C, C, p.img_dx[k][l]));
+      FSC_TRY(jobs.add(w->mix_fwd + lo + mix_boff(l, C), C, 0, NP3(l) * C, C, p.img_fwd[k][l], st));
+      FSC_TRY(jobs.add(w->mix_bwd + lo + mix_boff(l, C), NP3(l) * C, 0, C, NP3(l) * C, p.img_dz[k][l], st));
+      FSC_TRY(jobs.add(w->mix_dx + lo + mix_boff(l, C), C, 0, NP1(l) * C, C, p.img_dx[k][l], st));
     }
   }
   int din = p.D0;
   for (int k = 0; k < p.n_hidden; ++k) {
-    FSC_TRY(add(w->mn_w[k], din, 1, din, p.hidden[k], p.img_mnf[k]));
-    FSC_TRY(add(w->mn_w[k], din, 0, p.hidden[k], din, p.img_mnb[k]));
+    FSC_TRY(jobs.add(w->mn_w[k], din, 1, din, p.hidden[k], p.img_mnf[k], st));
+    FSC_TRY(jobs.add(w->mn_w[k], din, 0, p.hidden[k], din, p.img_mnb[k], st));
     din = p.hidden[k];
   }
-  return launch_gemm_images(jobs, n, st);
+  return jobs.flush(st);
 }
 
 __global__ void finalize_kernel(const double* __restrict__ e, const double* __restrict__ v, int64_t B, float* energy,
@@ -685,6 +662,9 @@ int run_backward(Ctx& c, fsc_ictd_outputs* out) {
 }
 
 }  // namespace
+
+int gemm_path() { return g_gemm_path; }
+
 }  // namespace fsc
 
 extern "C" {

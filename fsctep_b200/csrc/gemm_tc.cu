@@ -32,9 +32,15 @@ constexpr int MT = 128;                     // rows per tile
 constexpr uint32_t ABYTES = MT * KC * 4u;   // 16 KB
 constexpr int GT_THREADS = 6 * 32;          // 4 math warps, producer warp, MMA warp
 
+// NT <= 128 (FLUSH): every group of GC K-chunks (24 MMAs) accumulates into a fresh one of two TMEM
+// slots, which the math warps add to fp32 registers (tensor-core accumulation truncates, so long
+// chains over large K would bias the result).  Wider tiles (only used with K <= 128 here) rotate
+// the chunks over NACC accumulators summed in the epilogue.
 template <int NT>
 struct GCfg {
-  static constexpr int NACC = NT <= 64 ? 4 : 2;
+  static constexpr bool FLUSH = NT <= 128;
+  static constexpr int GC = 2;
+  static constexpr int NACC = FLUSH ? 2 : 2;
   static constexpr int NST = 2;
   static constexpr uint32_t BBYTES = 2u * KC * NT * 4u;  // hi + lo planes of one chunk
   static constexpr uint32_t ALO_OFF = NST * ABYTES;
@@ -102,10 +108,12 @@ __global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_consta
   uint64_t* lo_ready = bars + NST;        // [NST] math warps split the chunk
   uint64_t* empty = bars + 2 * NST;       // [NST] MMAs done with the stage
   uint64_t* d_ready = bars + 3 * NST;     // all MMAs done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * NST + 1);
+  uint64_t* grp_full = bars + 3 * NST + 1;   // [2] FLUSH: a group's MMAs done
+  uint64_t* grp_empty = bars + 3 * NST + 3;  // [2] FLUSH: math warps read the slot
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * NST + 5);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nchunks = a.K / KC;
+  const int nchunks = (a.K + KC - 1) / KC;  // a K tail reads TMA zero fill and zero image rows
   const int64_t g0 = (int64_t)blockIdx.x * a.Gb;
 
   if (warp == 4) {
@@ -119,16 +127,41 @@ __global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_consta
       tc::mbar_init(empty + i, 1);
     }
     tc::mbar_init(d_ready, 1);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(grp_full + i, 1);
+      tc::mbar_init(grp_empty + i, 4);
+    }
     tc::fence_mbar_init();
   }
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  const int ngroups = (nchunks + CF::GC - 1) / CF::GC;
 
   if (warp < 4) {
     // ---------------- split A into tf32 hi (in place) and lo, per chunk
     bool ok = true;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    float sum[CF::FLUSH ? NT : 1];
+#pragma unroll
+    for (int i = 0; i < (CF::FLUSH ? NT : 1); ++i) sum[i] = 0.f;
+    auto flush = [&](int g) {  // FLUSH: add group g's slot to the fp32 sums and free it
+      const int slot = g & 1;
+      if (!(ok = tc::mbar_wait(grp_full + slot, (g >> 1) & 1, a.err, 86))) return;
+      tc::tc_fence_after();
+#pragma unroll
+      for (int cb = 0; cb < (CF::FLUSH ? NT / 16 : 0); ++cb) {
+        uint32_t u[16];
+        tc::tmem_ld16(tbase + (uint32_t)(slot * NT) + lane_off + 16u * cb, u);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sum[16 * cb + i] += __uint_as_float(u[i]);
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(grp_empty + slot);
+    };
     for (int c = 0; c < nchunks && ok; ++c) {
       const int st = c % NST;
       if (!(ok = tc::mbar_wait(full + st, (c / NST) & 1, a.err, 81))) break;
@@ -149,7 +182,9 @@ __global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_consta
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(lo_ready + st);
+      if (CF::FLUSH && (c % CF::GC == CF::GC - 1 || c == nchunks - 1) && c / CF::GC >= 1) flush(c / CF::GC - 1);
     }
+    if (CF::FLUSH && ok) flush(ngroups - 1);
     // ---------------- epilogue: thread = tile row = TMEM lane
     if (ok) ok = tc::mbar_wait(d_ready, 0, a.err, 82);
     tc::tc_fence_after();
@@ -165,18 +200,22 @@ __global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_consta
     float* crow = valid ? a.C + g * a.c_gs + r * a.c_rs : nullptr;
     const int n0 = blockIdx.y * NT;
     const int nacc = nchunks < NACC ? nchunks : NACC;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-#pragma unroll 1
+#pragma unroll
     for (int cb = 0; cb < NT / 16; ++cb) {
       float v[16];
+      if (CF::FLUSH) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = 0.f;
-      for (int q = 0; q < nacc; ++q) {
-        uint32_t u[16];
-        tc::tmem_ld16(tbase + (uint32_t)(q * NT) + lane_off + 16u * cb, u);
-        tc::tmem_wait_ld();
+        for (int i = 0; i < 16; ++i) v[i] = sum[(CF::FLUSH ? 16 * cb + i : 0)];
+      } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] += __uint_as_float(u[i]);
+        for (int i = 0; i < 16; ++i) v[i] = 0.f;
+        for (int q = 0; q < nacc; ++q) {
+          uint32_t u[16];
+          tc::tmem_ld16(tbase + (uint32_t)(q * NT) + lane_off + 16u * cb, u);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] += __uint_as_float(u[i]);
+        }
       }
       const int nc = n0 + 16 * cb;
       if (crow && nc < a.N) {
@@ -228,8 +267,12 @@ __global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_consta
       for (int c = 0; c < nchunks; ++c) {
         const int st = c % NST;
         if (!(ok = tc::mbar_wait(lo_ready + st, (c / NST) & 1, a.err, 84))) break;
+        const int g = c / CF::GC;
+        const bool first = CF::FLUSH ? c % CF::GC == 0 : c < NACC;
+        if (CF::FLUSH && first && g >= 2 && !(ok = tc::mbar_wait(grp_empty + (g & 1), ((g >> 1) - 1) & 1, a.err, 87)))
+          break;
         tc::tc_fence_after();
-        const uint32_t d = tbase + (uint32_t)((c % NACC) * NT);
+        const uint32_t d = tbase + (uint32_t)((CF::FLUSH ? (g & 1) : (c % NACC)) * NT);
 #pragma unroll
         for (int j = 0; j < KC / 8; ++j) {
           const uint64_t ah = desc_sw128(a0 + st * ABYTES + 32 * j);
@@ -237,11 +280,12 @@ __global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_consta
           const uint32_t bh_addr = b0 + st * CF::BBYTES + j * 2 * 16 * NT;
           const uint64_t bh = tc::smem_desc_kmajor(bh_addr, 16 * NT, 128);
           const uint64_t bl = tc::smem_desc_kmajor(bh_addr + CF::BBYTES / 2, 16 * NT, 128);
-          mma_tf32_ss(d, ah, bh, idesc, (c >= NACC || j > 0) ? 1u : 0u);
+          mma_tf32_ss(d, ah, bh, idesc, (!first || j > 0) ? 1u : 0u);
           mma_tf32_ss(d, ah, bl, idesc, 1u);
           mma_tf32_ss(d, al, bh, idesc, 1u);
         }
         tc::mma_commit(empty + st);
+        if (CF::FLUSH && (c % CF::GC == CF::GC - 1 || c == nchunks - 1)) tc::mma_commit(grp_full + (g & 1));
       }
       tc::mma_commit(d_ready);  // also when a wait failed: whatever was issued completes first
     }
@@ -258,19 +302,21 @@ __global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_consta
 }
 
 // B image: element (k, n) of B[k][n] (b_trans: B[n*ldb + k]) at
-//   [n / NT][k / KC][hi|lo][(k % KC) / 4][n % NT][k % 4], zero for n >= N.
+//   [n / NT][k / KC][hi|lo][(k % KC) / 4][n % NT][k % 4], zero for n >= N or k >= K (K padded to
+//   whole chunks).
 __global__ void gemm_image_kernel(GemmImageJobs jobs) {
   const GemmImageJob& j = jobs.job[blockIdx.y];
-  const int64_t total = (int64_t)j.K * j.ntiles * j.NT;
+  const int Kp = (j.K + KC - 1) / KC * KC;
+  const int64_t total = (int64_t)Kp * j.ntiles * j.NT;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int k = (int)(i % j.K);
-    const int64_t n = i / j.K;  // padded column
+    const int k = (int)(i % Kp);
+    const int64_t n = i / Kp;  // padded column
     float x = 0.f;
-    if (n < j.N) x = j.b_trans ? j.B[n * j.ldb + k] : j.B[(int64_t)k * j.ldb + n];
+    if (n < j.N && k < j.K) x = j.b_trans ? j.B[n * j.ldb + k] : j.B[(int64_t)k * j.ldb + n];
     uint32_t hi, lo;
     tc::split_tf32(x, hi, lo);
     const int64_t tile = n / j.NT, nl = n % j.NT;
-    const int64_t nch = j.K / KC;
+    const int64_t nch = Kp / KC;
     const int64_t base = ((tile * nch + k / KC) * 2) * (KC * j.NT) + ((k % KC) / 4) * (4 * j.NT) + nl * 4 + (k % 4);
     j.out[base] = __uint_as_float(hi);
     j.out[base + KC * j.NT] = __uint_as_float(lo);
@@ -304,7 +350,7 @@ int launch_nt(const GemmArgs& g, const CUtensorMap& map, GemmTcArgs t, cudaStrea
 int gemm_tc_nt(int N) { return N <= 64 ? 64 : (N <= 128 ? 128 : (N <= 192 ? 192 : (N <= 256 ? 256 : 128))); }
 
 bool gemm_tc_supported(const GemmArgs& g) {
-  if (g.K % KC || g.K <= 0 || g.R < 1 || g.R > MT || g.N <= 0) return false;
+  if (g.K % 4 || g.K <= 0 || g.R < 1 || g.R > MT || g.N <= 0) return false;
   const auto a = reinterpret_cast<uintptr_t>(g.A);
   if (a % 16 || (g.a_rs * 4) % 16 || (g.a_gs * 4) % 16) return false;
   if (g.R > 1 && g.a_rs < g.K) return false;
@@ -313,7 +359,7 @@ bool gemm_tc_supported(const GemmArgs& g) {
 
 int64_t gemm_image_floats(int K, int N) {
   const int NT = gemm_tc_nt(N);
-  return (int64_t)ceil_div(N, NT) * NT * K * 2;
+  return (int64_t)ceil_div(N, NT) * NT * ((K + KC - 1) / KC * KC) * 2;
 }
 
 int launch_gemm_images(const GemmImageJobs& jobs, int njobs, cudaStream_t st) {
@@ -321,6 +367,30 @@ int launch_gemm_images(const GemmImageJobs& jobs, int njobs, cudaStream_t st) {
   if (njobs > kMaxImageJobs) return fail(FSC_ERR_ARGUMENT, "too many GEMM image jobs");
   gemm_image_kernel<<<dim3(64, (unsigned)njobs), 256, 0, st>>>(jobs);
   return check_launch("gemm_image_kernel");
+}
+
+int GemmImageBatch::add(const float* B, int64_t ldb, int b_trans, int K, int N, float* out, cudaStream_t st) {
+  GemmImageJob& j = jobs.job[n++];
+  j.B = B;
+  j.ldb = ldb;
+  j.b_trans = b_trans;
+  j.K = K;
+  j.N = N;
+  j.NT = gemm_tc_nt(N);
+  j.ntiles = (int)ceil_div(N, j.NT);
+  j.out = out;
+  return n == kMaxImageJobs ? flush(st) : FSC_OK;
+}
+
+int GemmImageBatch::flush(cudaStream_t st) {
+  const int m = n;
+  n = 0;
+  return launch_gemm_images(jobs, m, st);
+}
+
+int run_gemm(const GemmArgs& g, const float* img, int* err, cudaStream_t st) {
+  if (img && gemm_tc_supported(g)) return launch_gemm_tc(g, img, err, st);
+  return launch_gemm(g, st);
 }
 
 int launch_gemm_tc(const GemmArgs& g, const float* bimg, int* err, cudaStream_t st) {

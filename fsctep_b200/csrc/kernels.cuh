@@ -128,7 +128,7 @@ struct GemmArgs {
 int launch_gemm(const GemmArgs& a, cudaStream_t st);
 
 // The same GEMM on tcgen05 (gemm_tc.cu): A staged by TMA (two-level rows as a 3-D tensor map),
-// B from a pre-formatted hi/lo image (gemm_image_kernel), 3xTF32.  Needs K % 32 == 0, A and its
+// B from a pre-formatted hi/lo image (gemm_image_kernel), 3xTF32.  Needs K % 4 == 0, A and its
 // row strides 16-byte aligned, rows of one group contiguous (a_rs >= K) when R > 1.
 bool gemm_tc_supported(const GemmArgs& a);
 int gemm_tc_nt(int N);
@@ -145,6 +145,17 @@ struct GemmImageJobs {
   GemmImageJob job[kMaxImageJobs];
 };
 int launch_gemm_images(const GemmImageJobs& jobs, int njobs, cudaStream_t st);
+// Collects image jobs and launches them in batches of kMaxImageJobs.
+struct GemmImageBatch {
+  GemmImageJobs jobs{};
+  int n = 0;
+  int add(const float* B, int64_t ldb, int b_trans, int K, int N, float* out, cudaStream_t st);
+  int flush(cudaStream_t st);
+};
+// Tensor-core GEMM when an image is given and the shape qualifies, else the CUDA-core kernel.
+int run_gemm(const GemmArgs& a, const float* img, int* err, cudaStream_t st);
+// Process-wide GEMM path (fsc_ictd_set_gemm_path): 0 = tensor cores where supported.
+int gemm_path();
 
 // Readout (pure_cartesian_ictd_layers_full.py:956-1054)
 struct ReadoutArgs {

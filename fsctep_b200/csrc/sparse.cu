@@ -660,6 +660,14 @@ struct Plan {
   float* edge_grad;
   float* gbuf;
   int* err;
+  // tensor-core GEMM operand images of the weights (null: CUDA-core GEMM)
+  bool gtc;
+  float* img_mix[8][4];    // conv2 layer k, Lout: fc.4 regrouped, forward
+  float* img_mixT[8][4];   // its transpose (backward dZ)
+  float* img_gf[4];        // packed Gram x W_read (forward), per L
+  float* img_gb[4];        // ds x W_read (backward), per L
+  float* img_mnf[4];
+  float* img_mnb[4];
 };
 
 int validate(const fsc_sparse_config* cfg) {
@@ -721,6 +729,28 @@ void layout(Plan& p, Arena& ar, const fsc_sparse_config* cfg, int64_t N, int64_t
   p.edge_grad = ar.take<float>(E * 3);
   p.gbuf = ar.take<float>(p.gchunk * std::max<int64_t>(p.npairs, (int64_t)p.nC * p.nC));
   p.err = ar.take<int>(64);
+  p.gtc = gemm_path() == 0;
+  for (int k = 0; k < 8; ++k)
+    for (int L = 0; L < 4; ++L) p.img_mix[k][L] = p.img_mixT[k][L] = nullptr;
+  for (int k = 0; k < 4; ++k) p.img_gf[k] = p.img_gb[k] = p.img_mnf[k] = p.img_mnb[k] = nullptr;
+  if (p.gtc) {
+    for (int k = 1; k < p.nint; ++k)
+      for (int L = 0; L <= p.lmax; ++L) {
+        const int K = p.rows.npl[L] * J * p.C;
+        p.img_mix[k][L] = ar.take<float>(gemm_image_floats(K, p.C));
+        p.img_mixT[k][L] = ar.take<float>(gemm_image_floats(p.C, K));
+      }
+    for (int L = 0; L <= p.lmax; ++L) {
+      p.img_gf[L] = ar.take<float>(gemm_image_floats((int)p.npairs, p.S));
+      p.img_gb[L] = ar.take<float>(gemm_image_floats(p.S, p.nC * p.nC));
+    }
+    int din = p.D0;
+    for (int k = 0; k < p.n_hidden; ++k) {
+      p.img_mnf[k] = ar.take<float>(gemm_image_floats(din, p.hidden[k]));
+      p.img_mnb[k] = ar.take<float>(gemm_image_floats(p.hidden[k], din));
+      din = p.hidden[k];
+    }
+  }
 }
 
 struct Ctx {
@@ -780,6 +810,32 @@ GemmArgs gemm(const float* A, int64_t a_gs, int64_t a_rs, const float* B, int64_
 }
 
 // offset (floats) of layer k's mix block of rank Lout
+int64_t mix_offset(const Plan& p, int k, int Lout);
+
+// Builds every weight image the tensor-core GEMMs of this call read.
+int build_gemm_images(const Plan& p, const fsc_sparse_weights* w, cudaStream_t st) {
+  if (!p.gtc) return FSC_OK;
+  GemmImageBatch jobs;
+  for (int k = 1; k < p.nint; ++k)
+    for (int L = 0; L <= p.lmax; ++L) {
+      const int K = p.rows.npl[L] * J * p.C;
+      FSC_TRY(jobs.add(w->mix + mix_offset(p, k, L), p.C, 0, K, p.C, p.img_mix[k][L], st));
+      FSC_TRY(jobs.add(w->mixT + mix_offset(p, k, L), K, 0, p.C, K, p.img_mixT[k][L], st));
+    }
+  for (int L = 0; L <= p.lmax; ++L) {
+    FSC_TRY(jobs.add(w->wread_p + (int64_t)L * p.S * p.npairs, p.npairs, 1, (int)p.npairs, p.S, p.img_gf[L], st));
+    FSC_TRY(jobs.add(w->wread_s + (int64_t)L * p.S * p.nC * p.nC, (int64_t)p.nC * p.nC, 0, p.S, p.nC * p.nC,
+                     p.img_gb[L], st));
+  }
+  int din = p.D0;
+  for (int k = 0; k < p.n_hidden; ++k) {
+    FSC_TRY(jobs.add(w->mn_w[k], din, 1, din, p.hidden[k], p.img_mnf[k], st));
+    FSC_TRY(jobs.add(w->mn_w[k], din, 0, p.hidden[k], din, p.img_mnb[k], st));
+    din = p.hidden[k];
+  }
+  return jobs.flush(st);
+}
+
 int64_t mix_offset(const Plan& p, int k, int Lout) {
   int64_t per_layer = 0;
   for (int L = 0; L <= p.lmax; ++L) per_layer += (int64_t)p.rows.npl[L] * J * p.C * p.C;
@@ -800,6 +856,7 @@ int forward(Ctx& c) {
   const fsc_graph* g = c.g;
   const fsc_sparse_weights* w = c.w;
   cudaStream_t st = c.st;
+  FSC_TRY(build_gemm_images(p, w, st));
   FSC_TRY(launch_edge_dst(g->row_ptr, p.dst, p.N, st));
   if (p.E > 0) {
     geom_kernel<<<(unsigned)ceil_div(p.E, 256), 256, 0, st>>>(p.E, g->pos, g->src, p.dst, g->batch, g->cell, g->shift,
@@ -831,7 +888,7 @@ int forward(Ctx& c) {
                            p.C, 0, p.feats[k] + (n0 * p.R + roff(Lo)) * p.C, (int64_t)p.R * p.C, p.C, nc, pow3(Lo),
                            K, p.C);
         ga.alpha = 1.f / avg;
-        FSC_TRY(launch_gemm(ga, st));
+        FSC_TRY(run_gemm(ga, p.img_mix[k][Lo], p.err, st));
       }
     }
     prof::mark("sparse_conv2_forward", st);
@@ -848,7 +905,7 @@ int forward(Ctx& c) {
       FSC_TRY(check_launch("sparse gram_pack_kernel"));
       GemmArgs ga = gemm(p.gbuf, p.npairs, 0, Wp, p.npairs, 1, p.scalars + n0 * p.S, p.S, 0, nn, 1, (int)p.npairs, p.S);
       ga.accumulate = 1;
-      FSC_TRY(launch_gemm(ga, st));
+      FSC_TRY(run_gemm(ga, p.img_gf[L], p.err, st));
     }
   }
   prof::mark("sparse_readout_gram_forward", st);
@@ -862,7 +919,7 @@ int forward(Ctx& c) {
   for (int k = 0; k < p.n_hidden; ++k) {
     GemmArgs ga = gemm(xin, din, 0, w->mn_w[k], din, 1, p.act_pre[k], p.hidden[k], 0, p.N, 1, din, p.hidden[k]);
     ga.bias = w->mn_b[k];
-    FSC_TRY(launch_gemm(ga, st));
+    FSC_TRY(run_gemm(ga, p.img_mnf[k], p.err, st));
     FSC_TRY(launch_layernorm(p.act_pre[k], p.N, p.hidden[k], w->mn_g[k], w->mn_beta[k], 1, p.act_post[k], st));
     xin = p.act_post[k];
     din = p.hidden[k];
@@ -884,7 +941,7 @@ int backward(Ctx& c) {
     const int din = k == 0 ? p.D0 : p.hidden[k - 1];
     FSC_TRY(launch_layernorm_backward(p.act_pre[k], dcur, p.N, p.hidden[k], w->mn_g[k], w->mn_beta[k], 1, dnext, st));
     GemmArgs ga = gemm(dnext, p.hidden[k], 0, w->mn_w[k], din, 0, dcur, din, 0, p.N, 1, p.hidden[k], din);
-    FSC_TRY(launch_gemm(ga, st));
+    FSC_TRY(run_gemm(ga, p.img_mnb[k], p.err, st));
   }
   FSC_TRY(launch_layernorm_backward(p.p5, dcur, p.N, p.D0, w->mn_in_g, w->mn_in_b, 0, p.dp5, st));
   RdArgs rd = rd_args(p);
@@ -901,7 +958,7 @@ int backward(Ctx& c) {
       const int64_t nn = std::min(p.gchunk, p.N - n0);
       GemmArgs ga = gemm(p.dscalars + n0 * p.S, p.S, 0, Ws, (int64_t)p.nC * p.nC, 0, p.gbuf, (int64_t)p.nC * p.nC, 0,
                          nn, 1, p.S, p.nC * p.nC);
-      FSC_TRY(launch_gemm(ga, st));
+      FSC_TRY(run_gemm(ga, p.img_gb[L], p.err, st));
       gram_apply_kernel<<<(unsigned)ceil_div(nn * p.nC, 128), 128, 0, st>>>(rd, gl, L, n0, nn, p.gbuf);
       FSC_TRY(check_launch("sparse gram_apply_kernel"));
     }
@@ -919,7 +976,7 @@ int backward(Ctx& c) {
                            w->mixT + mix_offset(p, k, Lo), K, 0, p.zbuf + (int64_t)p.rows.zoff[Lo] * J * p.C,
                            p.zstride, K, nc, pow3(Lo), p.C, K);
         ga.alpha = 1.f / avg;
-        FSC_TRY(launch_gemm(ga, st));
+        FSC_TRY(run_gemm(ga, p.img_mixT[k][Lo], p.err, st));
       }
       bwd_dm_kernel<<<(unsigned)nc, 256, 0, st>>>(a, p.rows, p.feats[k - 1], p.h2 + (int64_t)k * p.E * RH, p.zbuf,
                                                    n0, p.grads[k - 1], p.dnp);

@@ -208,14 +208,15 @@ __device__ __forceinline__ float f16_range_scale(float bound) {
   return __uint_as_float((uint32_t)(e + 127) << 23);
 }
 
-// tf32 split: hi keeps the top 19 bits (exactly representable), lo = round_tf32(x - hi).
+// tf32 split: hi = round_tf32(x) (exactly representable, |x - hi| <= 2^-11 |x|),
+// lo = round_tf32(x - hi); hi*hi + hi*lo + lo*hi then misses at most ~2^-22 of each product.
 __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
-  const uint32_t xb = __float_as_uint(x);
-  hi = xb & 0xFFFFE000u;
-  const float r = x - __uint_as_float(hi);
-  uint32_t rl;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(rl) : "f"(r));
-  lo = rl;
+  uint32_t h, l;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+  const float r = x - __uint_as_float(h);
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(r));
+  hi = h;
+  lo = l;
 }
 
 }  // namespace tc
