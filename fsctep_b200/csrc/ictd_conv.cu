@@ -299,41 +299,86 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_r_kernel(ConvArgs a, co
 // (dZ already carries 1/deg), then
 //   dgate[p]         = sum_{q in p} Q[q] * Yt0[q],     Yt0[q] = sum_m2 CG_p[m1,m2,kk] Y[KB(l2)+m2]
 //   dY[KB(l2)+m2]   += sum_{q in p} Q[q] * gate[p] * CG_p[m1,m2,kk]
-// Every reduction runs inside one thread: no cross-lane traffic.  dZ rows are read as 16-byte
-// vectors that all lanes of the warp share (same node), x rows as 16-byte vectors per lane.
-// Paths with l1 = G: p in [P_LO(G), P_HI(G)), their Q entries [QOFF(P_LO), QOFF(P_HI)).
-__host__ __device__ constexpr int P_LO(int G) { return G == 0 ? 0 : (G == 1 ? 3 : 7); }
-__host__ __device__ constexpr int P_HI(int G) { return G == 0 ? 3 : (G == 1 ? 7 : 11); }
-__host__ __device__ constexpr int Q_END(int G) { return G == 2 ? NQ : QOFF(P_HI(G)); }
+// Every reduction runs inside one thread: no cross-lane traffic.  The sender rows of the warp's 32
+// edges are staged in shared memory one (l1 group, 16-channel chunk) at a time by coalesced
+// 16-byte asynchronous copies (four lanes per 64-byte row chunk), and each lane then reads its own
+// edge's rows from there; dZ rows are 16-byte vectors that all lanes share (same node).
+constexpr int QCH = 16;                       // channels per staged chunk
+constexpr int QES = 4 * 5 + 1;                // float4 slots per edge in a chunk (odd: no bank conflicts)
+constexpr int QZR = 14;                       // dZ rows of the largest l1 group
+constexpr int QBUF_F4 = 32 * QES + 4 * QZR;   // per warp: sender rows, then dZ rows
+constexpr int QTAB_F4 = (NQ * 5 + 3) / 4 + 9; // cg2, then the dZ row list of every group (35 ints)
+constexpr uint32_t QSMEM = 16u * (QTAB_F4 + CONV_WARPS * QBUF_F4);
+
+// Local index of (p, kk) among the dZ rows of p's l1 group: rows are listed path by path.
+__host__ __device__ constexpr int zlocal(int p, int kk) {
+  int j = 0;
+  for (int pp = P_LO(L1(p)); pp < p; ++pp) j += 2 * L3(pp) + 1;
+  return j + kk;
+}
+__host__ __device__ constexpr int zcount(int G) { return zlocal(P_HI(G) - 1, 2 * L3(P_HI(G) - 1)) + 1; }
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 template <int G, int C>
-__device__ __forceinline__ void q_group(const float4* __restrict__ x4, const float4* __restrict__ dz4,
-                                        const float* __restrict__ cg2, const float* Y, const float* g, float* dg,
-                                        float* dy) {
-  constexpr int Q0 = QOFF(P_LO(G)), NQG = Q_END(G) - Q0, M1 = 2 * G + 1;
+__device__ __forceinline__ void q_group(float4* __restrict__ buf, const int* __restrict__ zlist,
+                                        const float* __restrict__ x, int64_t src_row, const float* __restrict__ dzn,
+                                        const float* __restrict__ cg2, const float4* __restrict__ ey4,
+                                        const float4* __restrict__ eg4, float* dg, float* dy) {
+  constexpr int Q0 = QOFF(P_LO(G)), NQG = Q_END(G) - Q0, M1 = 2 * G + 1, NZG = zcount(G);
+  static_assert(NZG <= QZR, "dZ row buffer");
+  const int lane = threadIdx.x & 31;
+  float4* zb = buf + 32 * QES;
   float Q[NQG];
 #pragma unroll
   for (int i = 0; i < NQG; ++i) Q[i] = 0.f;
 #pragma unroll 1
-  for (int c4 = 0; c4 < C / 4; ++c4) {
-    float4 xv[M1];
+  for (int cc = 0; cc < C / QCH; ++cc) {
+    __syncwarp();  // every lane is done reading the previous chunk
+    // 32 edges x M1 rows x 4 float4: lane copies slots f = lane + 32 i, f = (e, m1, c4)
+#pragma unroll 1
+    for (int i = 0; i < 4 * M1; ++i) {
+      const int f = lane + 32 * i, e = f / (4 * M1), r = f - e * (4 * M1);
+      const int64_t row = __shfl_sync(0xffffffffu, src_row, e);
+      cp_async16(buf + e * QES + r, x + (row + KB(G) + (r >> 2)) * C + cc * QCH + 4 * (r & 3));
+    }
+    for (int f = lane; f < 4 * NZG; f += 32)
+      cp_async16(zb + f, dzn + zlist[f >> 2] * C + cc * QCH + 4 * (f & 3));
+    cp_async_wait_all();
+    __syncwarp();
+#pragma unroll 1
+    for (int c4 = 0; c4 < QCH / 4; ++c4) {
+      float4 xv[M1];
 #pragma unroll
-    for (int m1 = 0; m1 < M1; ++m1) xv[m1] = x4[(KB(G) + m1) * (C / 4) + c4];
+      for (int m1 = 0; m1 < M1; ++m1) xv[m1] = buf[lane * QES + 4 * m1 + c4];
 #pragma unroll
-    for (int p = P_LO(G); p < P_HI(G); ++p)
+      for (int p = P_LO(G); p < P_HI(G); ++p)
 #pragma unroll
-      for (int kk = 0; kk < 2 * L3(p) + 1; ++kk) {
-        const float4 d = dz4[zrow(p, kk) * (C / 4) + c4];
+        for (int kk = 0; kk < 2 * L3(p) + 1; ++kk) {
+          const float4 d = zb[4 * zlocal(p, kk) + c4];
 #pragma unroll
-        for (int m1 = 0; m1 < M1; ++m1) {
-          float acc = Q[qidx(p, m1, kk) - Q0];
-          acc = fmaf(xv[m1].x, d.x, acc);
-          acc = fmaf(xv[m1].y, d.y, acc);
-          acc = fmaf(xv[m1].z, d.z, acc);
-          acc = fmaf(xv[m1].w, d.w, acc);
-          Q[qidx(p, m1, kk) - Q0] = acc;
+          for (int m1 = 0; m1 < M1; ++m1) {
+            float acc = Q[qidx(p, m1, kk) - Q0];
+            acc = fmaf(xv[m1].x, d.x, acc);
+            acc = fmaf(xv[m1].y, d.y, acc);
+            acc = fmaf(xv[m1].z, d.z, acc);
+            acc = fmaf(xv[m1].w, d.w, acc);
+            Q[qidx(p, m1, kk) - Q0] = acc;
+          }
         }
-      }
+    }
+  }
+  float Y[12], g[12];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const float4 u = ey4[i], v = eg4[i];
+    Y[4 * i] = u.x; Y[4 * i + 1] = u.y; Y[4 * i + 2] = u.z; Y[4 * i + 3] = u.w;
+    g[4 * i] = v.x; g[4 * i + 1] = v.y; g[4 * i + 2] = v.z; g[4 * i + 3] = v.w;
   }
 #pragma unroll
   for (int p = P_LO(G); p < P_HI(G); ++p)
@@ -354,17 +399,24 @@ __device__ __forceinline__ void q_group(const float4* __restrict__ x4, const flo
 }
 
 template <int CPL>
-__global__ void __launch_bounds__(CONV_WARPS * 32) conv2_q_kernel(ConvArgs a, const float* __restrict__ x,
-                                                                  const float* __restrict__ dZ,
-                                                                  float* __restrict__ dgates,
-                                                                  float* __restrict__ dY) {
-  __shared__ float cg2[NQ * 5];
+__global__ void __launch_bounds__(CONV_WARPS * 32, 3) conv2_q_kernel(ConvArgs a, const float* __restrict__ x,
+                                                                     const float* __restrict__ dZ,
+                                                                     float* __restrict__ dgates,
+                                                                     float* __restrict__ dY) {
+  extern __shared__ float4 qsmem[];
+  float* cg2 = reinterpret_cast<float*>(qsmem);
+  int* zlist = reinterpret_cast<int*>(qsmem + (NQ * 5 + 3) / 4);  // group G's rows at zlocal order
   load_cg2(cg2, a.tables);
+  if (threadIdx.x < NP) {
+    const int p = threadIdx.x, base = p < P_HI(0) ? 0 : (p < P_HI(1) ? zcount(0) : zcount(0) + zcount(1));
+    for (int kk = 0; kk < 2 * L3(p) + 1; ++kk) zlist[base + zlocal(p, kk)] = zrow(p, kk);
+  }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n = (int64_t)blockIdx.x * CONV_WARPS + warp;
   if (n >= a.N) return;
   constexpr int C = 32 * CPL;
+  float4* buf = qsmem + QTAB_F4 + warp * QBUF_F4;
   const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
   if (n >= a.n_active) {  // receiver not evaluated in this layer: its edges' gate gradients are 0
     for (int e = e0 + lane; e < e1; e += 32) {
@@ -373,27 +425,22 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_q_kernel(ConvArgs a, co
     }
     return;
   }
-  const float4* dz4 = reinterpret_cast<const float4*>(dZ + n * NZ * C);
+  const float* dzn = dZ + n * NZ * C;
   for (int base = e0; base < e1; base += 32) {
     const int e = base + lane;
     const bool active = e < e1;
     const int64_t ee = active ? e : e0;
-    const int64_t s = a.src[ee];
-    const float4* x4 = reinterpret_cast<const float4*>(x + s * NK * C);
-    float Y[NK], g[NP], dg[NP], dy[NK];
+    const int64_t src_row = (int64_t)a.src[ee] * NK;
+    const float4* ey4 = reinterpret_cast<const float4*>(a.edge_y + 12 * ee);
+    const float4* eg4 = reinterpret_cast<const float4*>(a.gates + 12 * ee);
+    float dg[NP], dy[NK];
 #pragma unroll
-    for (int k = 0; k < NK; ++k) {
-      Y[k] = a.edge_y[12 * ee + k];
-      dy[k] = 0.f;
-    }
+    for (int k = 0; k < NK; ++k) dy[k] = 0.f;
 #pragma unroll
-    for (int p = 0; p < NP; ++p) {
-      g[p] = a.gates[12 * ee + p];
-      dg[p] = 0.f;
-    }
-    q_group<0, C>(x4, dz4, cg2, Y, g, dg, dy);
-    q_group<1, C>(x4, dz4, cg2, Y, g, dg, dy);
-    q_group<2, C>(x4, dz4, cg2, Y, g, dg, dy);
+    for (int p = 0; p < NP; ++p) dg[p] = 0.f;
+    q_group<0, C>(buf, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
+    q_group<1, C>(buf, zlist + zcount(0), x, src_row, dzn, cg2, ey4, eg4, dg, dy);
+    q_group<2, C>(buf, zlist + zcount(0) + zcount(1), x, src_row, dzn, cg2, ey4, eg4, dg, dy);
     if (!active) continue;
     float4* dgo = reinterpret_cast<float4*>(dgates + 12 * (int64_t)e);
     dgo[0] = make_float4(dg[0], dg[1], dg[2], dg[3]);
@@ -594,7 +641,18 @@ int launch_conv2_r(const ConvArgs& a, const float* G, float* R, cudaStream_t st)
 }
 int launch_conv2_q(const ConvArgs& a, const float* x, const float* dZ, float* dgates, float* dY,
                    cudaStream_t st) {
-  FSC_CONV_LAUNCH(conv2_q_kernel, a, x, dZ, dgates, dY);
+  if (a.N == 0) return FSC_OK;
+  const unsigned blocks = (unsigned)ceil_div(a.N, CONV_WARPS);
+  if (a.C == 32) {
+    cudaFuncSetAttribute(conv2_q_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QSMEM);
+    conv2_q_kernel<1><<<blocks, CONV_WARPS * 32, QSMEM, st>>>(a, x, dZ, dgates, dY);
+  } else if (a.C == 64) {
+    cudaFuncSetAttribute(conv2_q_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QSMEM);
+    conv2_q_kernel<2><<<blocks, CONV_WARPS * 32, QSMEM, st>>>(a, x, dZ, dgates, dY);
+  } else {
+    return fail(FSC_ERR_UNSUPPORTED, "ictd conv kernels support channels 32 or 64");
+  }
+  return check_launch("conv2_q_kernel");
 }
 
 }  // namespace fsc

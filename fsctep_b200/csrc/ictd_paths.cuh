@@ -14,6 +14,9 @@
 //   Yt[q] = gate_p * sum_{m2} CG_p[m1, m2, kk] * Y_{l2}[m2]
 #pragma once
 
+// Tables are switch statements rather than local arrays: with a loop index that the compiler
+// unrolls they fold to constants, where a local array may be materialised in local memory.
+
 namespace ictd2 {
 
 constexpr int NP = 11;
@@ -26,33 +29,63 @@ __host__ __device__ constexpr int L1(int p) {
   return p < 3 ? 0 : (p < 7 ? 1 : 2);
 }
 __host__ __device__ constexpr int L2(int p) {
-  constexpr int t[NP] = {0, 1, 2, 0, 1, 1, 2, 0, 1, 2, 2};
-  return t[p];
+  switch (p) {
+    case 0: case 3: case 7: return 0;
+    case 1: case 4: case 5: case 8: return 1;
+    default: return 2;  // p = 2, 6, 9, 10
+  }
 }
 __host__ __device__ constexpr int L3(int p) {
-  constexpr int t[NP] = {0, 1, 2, 1, 0, 2, 1, 2, 1, 0, 2};
-  return t[p];
+  switch (p) {
+    case 0: case 4: case 9: return 0;
+    case 1: case 3: case 6: case 8: return 1;
+    default: return 2;  // p = 2, 5, 7, 10
+  }
 }
 __host__ __device__ constexpr int KB(int l) { return l * l; }
 __host__ __device__ constexpr int NP3(int l3) { return l3 == 0 ? 3 : 4; }
 __host__ __device__ constexpr int OFF3(int l3) { return l3 == 0 ? 0 : (l3 == 1 ? 3 : 15); }
 __host__ __device__ constexpr int RANK3(int p) {
-  constexpr int t[NP] = {0, 0, 0, 1, 1, 1, 2, 2, 3, 2, 3};
-  return t[p];
+  switch (p) {
+    case 0: case 1: case 2: return 0;
+    case 3: case 4: case 5: return 1;
+    case 6: case 7: case 9: return 2;
+    default: return 3;  // p = 8, 10
+  }
 }
 __host__ __device__ constexpr int NP1(int l1) { return l1 == 0 ? 3 : 4; }
 __host__ __device__ constexpr int OFF1(int l1) { return l1 == 0 ? 0 : (l1 == 1 ? 3 : 15); }
 __host__ __device__ constexpr int RANK1(int p) {
-  constexpr int t[NP] = {0, 1, 2, 0, 1, 2, 3, 0, 1, 2, 3};
-  return t[p];
+  switch (p) {
+    case 0: case 3: case 7: return 0;
+    case 1: case 4: case 8: return 1;
+    case 2: case 5: case 9: return 2;
+    default: return 3;  // p = 6, 10
+  }
 }
 __host__ __device__ constexpr int QOFF(int p) {
-  constexpr int t[NP] = {0, 1, 4, 9, 18, 21, 36, 45, 70, 85, 90};
-  return t[p];
+  switch (p) {
+    case 0: return 0;
+    case 1: return 1;
+    case 2: return 4;
+    case 3: return 9;
+    case 4: return 18;
+    case 5: return 21;
+    case 6: return 36;
+    case 7: return 45;
+    case 8: return 70;
+    case 9: return 85;
+    default: return 90;  // p = 10
+  }
 }
 __host__ __device__ constexpr int zrow(int p, int kk) { return OFF3(L3(p)) + kk * NP3(L3(p)) + RANK3(p); }
 __host__ __device__ constexpr int rrow(int p, int m1) { return OFF1(L1(p)) + m1 * NP1(L1(p)) + RANK1(p); }
 __host__ __device__ constexpr int qidx(int p, int m1, int kk) { return QOFF(p) + m1 * (2 * L3(p) + 1) + kk; }
+
+// Paths with l1 = G: p in [P_LO(G), P_HI(G)), their Q entries [QOFF(P_LO), Q_END(G)).
+__host__ __device__ constexpr int P_LO(int G) { return G == 0 ? 0 : (G == 1 ? 3 : 7); }
+__host__ __device__ constexpr int P_HI(int G) { return G == 0 ? 3 : (G == 1 ? 7 : 11); }
+__host__ __device__ constexpr int Q_END(int G) { return G == 2 ? NQ : QOFF(P_HI(G)); }
 
 // conv1 paths (l, 0, l): 0, 3, 7
 __host__ __device__ constexpr int P1PATH(int l) { return l == 0 ? 0 : (l == 1 ? 3 : 7); }
