@@ -7,18 +7,16 @@
 //   dE/d|r| += (W1^T da1) . demb/d|r|
 // and, after the last layer, the direction part dE/dY -> dE/dr (edge_grad).
 //
-// One CTA owns a tile of 128 edges (thread = edge = TMEM lane = MMA row) and walks its tiles
-// persistently.  Every matrix product of the MLP is a chain of tcgen05.mma (kind::tf32,
-// M = 128) with the activations as the A operand in TMEM and the layer's weights as B operand
-// images in shared memory.  fp32 accuracy comes from the 3xTF32 split (hi*hi + hi*lo + lo*hi).
-// The element-wise steps (bias, SiLU and its derivative, tf32 split) run on the CUDA cores
-// between the MMA chains, reading the accumulators with tcgen05.ld and writing the next A with
-// tcgen05.st.  Two CTAs share an SM (256 TMEM columns each) so one CTA's element-wise work
-// overlaps the other's MMAs.
+// One CTA owns a tile of 128 edges (edge = TMEM lane = MMA row) and walks its tiles persistently.
+// Every matrix product of the MLP is a chain of tcgen05.mma (kind::tf32, M = 128) with the
+// activations as the A operand in TMEM and the layer's weights as B operand images in shared
+// memory.  fp32 accuracy comes from the 3xTF32 split (hi*hi + hi*lo + lo*hi).  The element-wise
+// steps (bias, SiLU and its derivative, tf32 split) run on the CUDA cores between the MMA chains,
+// reading the accumulators with tcgen05.ld and writing the next A with tcgen05.st: two threads per
+// edge (warps w and w + 4 share TMEM lanes 32 (w % 4) ...), each owning 32 of the 64 hidden
+// columns, so 16 warps per SM share the latency of those steps.  Two CTAs share an SM (256 TMEM
+// columns each) so one CTA's element-wise work overlaps the other's MMAs.
 //
-// TMEM columns of a CTA: D0 = [0, 64), D1 = [64, 128), A hi = [128, 192), A lo = [192, 256).
-// Where D1 is free, a K = 64 product is split over two accumulators (D0, D1) and an N = 16
-// product over eight (16 columns each in [0, 128)), summed on the CUDA cores.
 #include "common.cuh"
 #include "edge_common.cuh"
 #include "kernels.cuh"
@@ -29,6 +27,7 @@ namespace fsc {
 namespace {
 
 constexpr int RT = 128;      // edges per tile
+constexpr int RTH = 2 * RT;  // threads per CTA: two per edge
 constexpr int RH = 64;       // hidden width (fixed by the reference)
 constexpr int RP = 11;       // gates per layer
 constexpr int RT_PER_SM = 2; // CTAs per SM
@@ -57,14 +56,17 @@ struct BwdImg {
   static constexpr int SIZE = W1T + 16 * RH;
 };
 
-// Shared memory: hi images, lo images, biases, ypoly, mbarrier, TMEM slot.
+// Shared memory: hi images, lo images, biases, ypoly, the exchange rows of the two column
+// halves (an N = 16 product's partial sums), mbarrier, TMEM slot.
+constexpr int XST = 17;  // exchange row stride (odd: no bank conflicts)
 template <int SIZE>
 struct RtSmem {
   static constexpr uint32_t HI = 0;
   static constexpr uint32_t LO = 4u * SIZE;
   static constexpr uint32_t BIAS = 8u * SIZE;                   // b1[64], b2[64], b3[16]
   static constexpr uint32_t YPOLY = BIAS + 4u * 144;            // [NMONO][NK]
-  static constexpr uint32_t BAR = (YPOLY + 4u * 96 + 15u) & ~15u;
+  static constexpr uint32_t XCH = YPOLY + 4u * 96;              // [RT][XST]
+  static constexpr uint32_t BAR = (XCH + 4u * RT * XST + 15u) & ~15u;
   static constexpr uint32_t TOTAL_RAW = BAR + 16;
   static constexpr uint32_t TOTAL = TOTAL_RAW > kMinSmem ? TOTAL_RAW : kMinSmem;
 };
@@ -111,17 +113,29 @@ __device__ __forceinline__ void mma_3xtf32(uint32_t d, uint32_t a_hi, uint32_t a
   }
 }
 
-// Sum of the eight 16-column accumulators of an N = 16 product at columns [t, t + 128).
-__device__ __forceinline__ void ld_sum16x8(uint32_t t, float* out) {
+// Sum of four of the eight 16-column accumulators of an N = 16 product: columns [t, t + 64).
+__device__ __forceinline__ void ld_sum16x4(uint32_t t, float* out) {
+  uint32_t u[32], w[32];
+  tc::tmem_ld32(t, u);
+  tc::tmem_ld32(t + 32u, w);
+  tc::tmem_wait_ld();
 #pragma unroll
-  for (int q = 0; q < 16; ++q) out[q] = 0.f;
+  for (int q = 0; q < 16; ++q)
+    out[q] = (__uint_as_float(u[q]) + __uint_as_float(u[16 + q])) + (__uint_as_float(w[q]) + __uint_as_float(w[16 + q]));
+}
+
+// Full sum of the eight accumulators in the threads of column half 0: half 1 hands its partial
+// sums over through shared memory.  Block-wide (contains a barrier).
+__device__ __forceinline__ void sum16x8_halves(uint32_t t_lane, int half, int row, float* xch, float* out) {
+  ld_sum16x4(t_lane + 64u * half, out);
+  if (half == 1) {
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t u[32];
-    tc::tmem_ld32(t + 32u * c, u);
-    tc::tmem_wait_ld();
+    for (int q = 0; q < 16; ++q) xch[row * XST + q] = out[q];
+  }
+  __syncthreads();
+  if (half == 0) {
 #pragma unroll
-    for (int q = 0; q < 16; ++q) out[q] += __uint_as_float(u[q]) + __uint_as_float(u[16 + q]);
+    for (int q = 0; q < 16; ++q) out[q] += xch[row * XST + q];
   }
 }
 
@@ -163,17 +177,19 @@ __device__ __forceinline__ void drain(uint64_t* bar, uint32_t phase) {
 // HOUT: stop after the second hidden layer and write h2 = silu(W2 h1 + b2) ([nint][E][64]) for
 // callers that fold the last linear layer into their own contraction (pure-cartesian-sparse).
 template <int NBP, bool HOUT>
-__global__ void __launch_bounds__(RT, RT_PER_SM) radial_fwd_tc_kernel(RadialTcArgs a) {
+__global__ void __launch_bounds__(RTH, RT_PER_SM) radial_fwd_tc_kernel(RadialTcArgs a) {
   using IM = FwdImg<NBP>;
   using SM = RtSmem<IM::SIZE>;
   extern __shared__ __align__(1024) uint8_t smem[];
   float* img_hi = reinterpret_cast<float*>(smem + SM::HI);
   float* img_lo = reinterpret_cast<float*>(smem + SM::LO);
   float* bias = reinterpret_cast<float*>(smem + SM::BIAS);
+  float* xch = reinterpret_cast<float*>(smem + SM::XCH);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + SM::BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::BAR + 8);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  // thread = (column half, edge row); warps w and w + 4 read and write TMEM lanes 32 (w % 4) ...
+  const int tid = threadIdx.x, warp = tid >> 5, half = tid / RT, row = tid % RT;
   if (warp == 0) {
     tc::tmem_alloc(tmem_slot, 256);
     tc::tmem_relinquish();
@@ -186,8 +202,9 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_fwd_tc_kernel(RadialTcAr
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
   const uint32_t tD0 = tbase, tD1 = tbase + 64u, tAhi = tbase + 128u, tAlo = tbase + 192u;
+  const uint32_t hcol = 32u * half;  // this thread's hidden columns [hcol, hcol + 32)
   const uint32_t s_hi = tc::smem_u32(img_hi), s_lo = tc::smem_u32(img_lo);
   constexpr uint32_t id64 = tc::idesc_tf32(RT, 64), id16 = tc::idesc_tf32(RT, 16);
   const int64_t ntiles = (a.E + RT - 1) / RT;
@@ -200,13 +217,13 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_fwd_tc_kernel(RadialTcAr
     const float* w1 = a.rad.w1 + (size_t)layer * RH * a.nb;
     const float* w2 = a.rad.w2 + (size_t)layer * RH * RH;
     const float* w3 = a.rad.w3 + (size_t)layer * RP * RH;
-    for (int i = tid; i < RH * NBP; i += RT) {
+    for (int i = tid; i < RH * NBP; i += RTH) {
       const int k = i / NBP, b = i - k * NBP;
       put_b(img_hi, img_lo, IM::W1, RH, k, b, b < a.nb ? w1[k * a.nb + b] : 0.f);
     }
-    for (int i = tid; i < RH * RH; i += RT) put_b(img_hi, img_lo, IM::W2, RH, i >> 6, i & 63, w2[i]);
+    for (int i = tid; i < RH * RH; i += RTH) put_b(img_hi, img_lo, IM::W2, RH, i >> 6, i & 63, w2[i]);
     if (!HOUT) {
-      for (int i = tid; i < 16 * RH; i += RT) {
+      for (int i = tid; i < 16 * RH; i += RTH) {
         const int q = i >> 6, j = i & 63;
         put_b(img_hi, img_lo, IM::W3, 16, q, j, q < RP ? w3[q * RH + j] : 0.f);
       }
@@ -216,10 +233,10 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_fwd_tc_kernel(RadialTcAr
     __syncthreads();
 
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-      const int64_t e = tile * RT + tid;
+      const int64_t e = tile * RT + row;
       const bool valid = e < a.E;
-      // ---- A = emb
-      {
+      // ---- A = emb (columns [0, 32), written by half 0)
+      if (half == 0) {
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = 0.f;
@@ -238,15 +255,14 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_fwd_tc_kernel(RadialTcAr
       }
       if (!(ok = d_ready(bar, phase, a.err, 41))) break;
       // ---- h1 = silu(D0 + b1) -> A ; D0 = h1 W2^T
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      {
         uint32_t u[32];
         float v[32];
-        tc::tmem_ld32(tD0 + lane_off + 32u * h, u);
+        tc::tmem_ld32(tD0 + lane_off + hcol, u);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = silu(__uint_as_float(u[i]) + bias[32 * h + i]);
-        store_a32(tAhi + lane_off, tAlo + lane_off, 32u * h, v);
+        for (int i = 0; i < 32; ++i) v[i] = silu(__uint_as_float(u[i]) + bias[hcol + i]);
+        store_a32(tAhi + lane_off, tAlo + lane_off, hcol, v);
       }
       a_ready();
       if (tid == 0) {
@@ -256,23 +272,22 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_fwd_tc_kernel(RadialTcAr
       }
       if (!(ok = d_ready(bar, phase, a.err, 42))) break;
       // ---- h2 = silu(D0 + D1 + b2) -> A ; D0..D1 = h2 W3^T (eight 16-column accumulators)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      {
         uint32_t u[32], w[32];
         float v[32];
-        tc::tmem_ld32(tD0 + lane_off + 32u * h, u);
-        tc::tmem_ld32(tD1 + lane_off + 32u * h, w);
+        tc::tmem_ld32(tD0 + lane_off + hcol, u);
+        tc::tmem_ld32(tD1 + lane_off + hcol, w);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = silu((__uint_as_float(u[i]) + __uint_as_float(w[i])) + bias[RH + 32 * h + i]);
+        for (int i = 0; i < 32; ++i) v[i] = silu((__uint_as_float(u[i]) + __uint_as_float(w[i])) + bias[RH + hcol + i]);
         if (HOUT) {
           if (valid) {
-            float4* o = reinterpret_cast<float4*>(a.hout + ((int64_t)layer * a.E + e) * RH + 32 * h);
+            float4* o = reinterpret_cast<float4*>(a.hout + ((int64_t)layer * a.E + e) * RH + hcol);
 #pragma unroll
             for (int i = 0; i < 8; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
           }
         } else {
-          store_a32(tAhi + lane_off, tAlo + lane_off, 32u * h, v);
+          store_a32(tAhi + lane_off, tAlo + lane_off, hcol, v);
         }
       }
       if (HOUT) {
@@ -289,8 +304,8 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_fwd_tc_kernel(RadialTcAr
       // ---- gates = sum of the accumulators + b3
       {
         float gs[16];
-        ld_sum16x8(tD0 + lane_off, gs);
-        if (valid) {
+        sum16x8_halves(tD0 + lane_off, half, row, xch, gs);
+        if (half == 0 && valid) {
           float g[12];
 #pragma unroll
           for (int q = 0; q < 12; ++q) g[q] = q < RP ? gs[q] + bias[2 * RH + q] : 0.f;
@@ -316,7 +331,7 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_fwd_tc_kernel(RadialTcAr
 // HOUT: dE/dh2 comes from hout_grad ([nint][E][64]) instead of the gates, and every layer only
 // accumulates dE/d|r| into edge_grad[e][0] (the caller adds the direction part).
 template <int NBP, bool HOUT>
-__global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcArgs a) {
+__global__ void __launch_bounds__(RTH, RT_PER_SM) radial_bwd_tc_kernel(RadialTcArgs a) {
   using IM = BwdImg<NBP>;
   using SM = RtSmem<IM::SIZE>;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -324,12 +339,14 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcAr
   float* img_lo = reinterpret_cast<float*>(smem + SM::LO);
   float* bias = reinterpret_cast<float*>(smem + SM::BIAS);
   float* ypoly = reinterpret_cast<float*>(smem + SM::YPOLY);
+  float* xch = reinterpret_cast<float*>(smem + SM::XCH);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + SM::BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::BAR + 8);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  // thread = (column half, edge row); warps w and w + 4 read and write TMEM lanes 32 (w % 4) ...
+  const int tid = threadIdx.x, warp = tid >> 5, half = tid / RT, row = tid % RT;
   if (!HOUT)
-    for (int i = tid; i < ictd2::NMONO * ictd2::NK; i += RT) ypoly[i] = a.tables[ictd2::TAB_YPOLY + i];
+    for (int i = tid; i < ictd2::NMONO * ictd2::NK; i += RTH) ypoly[i] = a.tables[ictd2::TAB_YPOLY + i];
   if (warp == 0) {
     tc::tmem_alloc(tmem_slot, 256);
     tc::tmem_relinquish();
@@ -342,8 +359,9 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcAr
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
   const uint32_t tD0 = tbase, tD1 = tbase + 64u, tAhi = tbase + 128u, tAlo = tbase + 192u;
+  const uint32_t hcol = 32u * half;  // this thread's hidden columns [hcol, hcol + 32)
   const uint32_t s_hi = tc::smem_u32(img_hi), s_lo = tc::smem_u32(img_lo);
   constexpr uint32_t id64 = tc::idesc_tf32(RT, 64), id16 = tc::idesc_tf32(RT, 16);
   const int64_t ntiles = (a.E + RT - 1) / RT;
@@ -355,22 +373,22 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcAr
     const float* w1 = a.rad.w1 + (size_t)layer * RH * a.nb;
     const float* w2 = a.rad.w2 + (size_t)layer * RH * RH;
     const float* w3 = a.rad.w3 + (size_t)layer * RP * RH;
-    for (int i = tid; i < RH * NBP; i += RT) {
+    for (int i = tid; i < RH * NBP; i += RTH) {
       const int k = i / NBP, b = i - k * NBP;
       const float v = b < a.nb ? w1[k * a.nb + b] : 0.f;
       put_b(img_hi, img_lo, IM::W1, RH, k, b, v);
     }
-    for (int i = tid; i < RH * 16; i += RT) {  // W1T rows b < 16
+    for (int i = tid; i < RH * 16; i += RTH) {  // W1T rows b < 16
       const int b = i >> 6, k = i & 63;
       put_b(img_hi, img_lo, IM::W1T, 16, b, k, b < a.nb ? w1[k * a.nb + b] : 0.f);
     }
-    for (int i = tid; i < RH * RH; i += RT) {
+    for (int i = tid; i < RH * RH; i += RTH) {
       const int j = i >> 6, k = i & 63;
       put_b(img_hi, img_lo, IM::W2, RH, j, k, w2[i]);
       put_b(img_hi, img_lo, IM::W2T, RH, k, j, w2[i]);
     }
     if (!HOUT) {
-      for (int i = tid; i < RH * 16; i += RT) {
+      for (int i = tid; i < RH * 16; i += RTH) {
         const int j = i >> 4, q = i & 15;
         put_b(img_hi, img_lo, IM::W3P, RH, j, q, q < RP ? w3[q * RH + j] : 0.f);
       }
@@ -380,12 +398,12 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcAr
     __syncthreads();
 
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-      const int64_t e = tile * RT + tid;
+      const int64_t e = tile * RT + row;
       const bool valid = e < a.E;
-      float demb[NBP];
+      float demb[NBP];  // half 0
       float ry[3] = {0.f, 0.f, 0.f};
-      // ---- A = [emb (NBP) | dgates (16)] ; D0 = emb W1^T (a1 - b1), D1 = dg W3 (dh2)
-      {
+      // ---- A = [emb (NBP) | dgates (16)] (half 0) ; D0 = emb W1^T (a1 - b1), D1 = dg W3 (dh2)
+      if (half == 0) {
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = 0.f;
@@ -416,20 +434,19 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcAr
       }
       if (!(ok = d_ready(bar, phase, a.err, 51))) break;
       // ---- h1 = silu(a1) -> A, keep silu'(a1) ; D0 = h1 W2^T (a2 - b2)
-      float sg1[RH];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      float sg1[32];
+      {
         uint32_t u[32];
         float v[32];
-        tc::tmem_ld32(tD0 + lane_off + 32u * h, u);
+        tc::tmem_ld32(tD0 + lane_off + hcol, u);
         tc::tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float x = __uint_as_float(u[i]) + bias[32 * h + i];
+          const float x = __uint_as_float(u[i]) + bias[hcol + i];
           v[i] = silu(x);
-          sg1[32 * h + i] = silu_grad(x);
+          sg1[i] = silu_grad(x);
         }
-        store_a32(tAhi + lane_off, tAlo + lane_off, 32u * h, v);
+        store_a32(tAhi + lane_off, tAlo + lane_off, hcol, v);
       }
       a_ready();
       if (tid == 0) {
@@ -439,15 +456,14 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcAr
       }
       if (!(ok = d_ready(bar, phase, a.err, 52))) break;
       // ---- da2 = dh2 * silu'(a2) -> A ; D0 = da2 W2 (dh1)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      {
         uint32_t u[32], w[32];
         float v[32];
-        tc::tmem_ld32(tD0 + lane_off + 32u * h, u);
-        if (!HOUT) tc::tmem_ld32(tD1 + lane_off + 32u * h, w);
+        tc::tmem_ld32(tD0 + lane_off + hcol, u);
+        if (!HOUT) tc::tmem_ld32(tD1 + lane_off + hcol, w);
         tc::tmem_wait_ld();
         if (HOUT) {
-          const float4* g4 = reinterpret_cast<const float4*>(a.hout_grad + ((int64_t)layer * a.E + e) * RH + 32 * h);
+          const float4* g4 = reinterpret_cast<const float4*>(a.hout_grad + ((int64_t)layer * a.E + e) * RH + hcol);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float4 t = valid ? g4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -456,8 +472,8 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcAr
           }
         }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(w[i]) * silu_grad(__uint_as_float(u[i]) + bias[RH + 32 * h + i]);
-        store_a32(tAhi + lane_off, tAlo + lane_off, 32u * h, v);
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(w[i]) * silu_grad(__uint_as_float(u[i]) + bias[RH + hcol + i]);
+        store_a32(tAhi + lane_off, tAlo + lane_off, hcol, v);
       }
       a_ready();
       if (tid == 0) {
@@ -467,16 +483,15 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcAr
       }
       if (!(ok = d_ready(bar, phase, a.err, 53))) break;
       // ---- da1 = (D0 + D1) * silu'(a1) -> A ; D0..D1 = da1 W1 (dE/demb, eight accumulators)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      {
         uint32_t u[32], w[32];
         float v[32];
-        tc::tmem_ld32(tD0 + lane_off + 32u * h, u);
-        tc::tmem_ld32(tD1 + lane_off + 32u * h, w);
+        tc::tmem_ld32(tD0 + lane_off + hcol, u);
+        tc::tmem_ld32(tD1 + lane_off + hcol, w);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = (__uint_as_float(u[i]) + __uint_as_float(w[i])) * sg1[32 * h + i];
-        store_a32(tAhi + lane_off, tAlo + lane_off, 32u * h, v);
+        for (int i = 0; i < 32; ++i) v[i] = (__uint_as_float(u[i]) + __uint_as_float(w[i])) * sg1[i];
+        store_a32(tAhi + lane_off, tAlo + lane_off, hcol, v);
       }
       a_ready();
       if (tid == 0) {
@@ -485,11 +500,11 @@ __global__ void __launch_bounds__(RT, RT_PER_SM) radial_bwd_tc_kernel(RadialTcAr
         tc::mma_commit(bar);
       }
       if (!(ok = d_ready(bar, phase, a.err, 54))) break;
-      // ---- dE/d|r| of this layer; the last layer also applies the direction part
+      // ---- dE/d|r| of this layer; the last layer also applies the direction part (half 0)
       {
         float de[16];
-        ld_sum16x8(tD0 + lane_off, de);
-        if (valid) {
+        sum16x8_halves(tD0 + lane_off, half, row, xch, de);
+        if (half == 0 && valid) {
           float dl = 0.f;
 #pragma unroll
           for (int b = 0; b < NBP; ++b) dl = fmaf(de[b], demb[b], dl);
@@ -539,7 +554,7 @@ int launch_rt(K kernel, uint32_t smem, const RadialTcArgs& a, cudaStream_t st, c
     return fail(FSC_ERR_CUDA, std::string(name) + ": cannot set shared memory size");
   const int64_t ntiles = ceil_div(a.E, RT);
   const int64_t grid = ntiles < (int64_t)RT_PER_SM * num_sms() ? ntiles : (int64_t)RT_PER_SM * num_sms();
-  kernel<<<(unsigned)grid, RT, smem, st>>>(a);
+  kernel<<<(unsigned)grid, RTH, smem, st>>>(a);
   return check_launch(name);
 }
 
