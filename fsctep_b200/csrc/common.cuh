@@ -54,10 +54,13 @@ struct Arena {
   bool ok() const { return measuring || off <= cap; }
 };
 
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+// sigmoid through the hardware reciprocal (__fdividef, within 2 ulp); as x -> -inf the
+// denominator overflows to +inf and the result is the exact limit 0.
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float silu(float x) { return x * sigmoid_fast(x); }
 // d silu / dx = s (1 + x (1 - s)), s = sigmoid(x)
 __device__ __forceinline__ float silu_grad(float x) {
-  float s = 1.0f / (1.0f + __expf(-x));
+  const float s = sigmoid_fast(x);
   return s * (1.0f + x * (1.0f - s));
 }
 

@@ -148,6 +148,22 @@ __device__ __forceinline__ void store_a32(uint32_t t_ahi, uint32_t t_alo, uint32
   tc::tmem_st32(t_alo + col, lo);
 }
 
+// Splits NC (8 or 16) values into tf32 hi / lo and stores them as NC A columns at `col`.
+template <int NC>
+__device__ __forceinline__ void store_a_n(uint32_t t_ahi, uint32_t t_alo, uint32_t col, const float* v) {
+  static_assert(NC == 8 || NC == 16, "8 or 16 columns");
+  uint32_t hi[NC], lo[NC];
+#pragma unroll
+  for (int i = 0; i < NC; ++i) tc::split_tf32(v[i], hi[i], lo[i]);
+  if constexpr (NC == 8) {
+    tc::tmem_st8(t_ahi + col, hi);
+    tc::tmem_st8(t_alo + col, lo);
+  } else {
+    tc::tmem_st16(t_ahi + col, hi);
+    tc::tmem_st16(t_alo + col, lo);
+  }
+}
+
 // Hand-off from the CUDA-core phase to the MMA issuer: every thread's tcgen05.st is complete and
 // ordered before the barrier.
 __device__ __forceinline__ void a_ready() {
@@ -235,17 +251,17 @@ __global__ void __launch_bounds__(RTH, RT_PER_SM) radial_fwd_tc_kernel(RadialTcA
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
       const int64_t e = tile * RT + row;
       const bool valid = e < a.E;
-      // ---- A = emb (columns [0, 32), written by half 0)
+      // ---- A = emb (columns [0, NBP), written by half 0; the MMA reads no further)
       if (half == 0) {
-        float v[32];
+        float v[NBP];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        for (int i = 0; i < NBP; ++i) v[i] = 0.f;
         if (valid) {
           const float4 ry = reinterpret_cast<const float4*>(a.edge_y + 12 * e)[2];
           const float len = sqrtf(ry.y * ry.y + ry.z * ry.z + ry.w * ry.w);
           radial_basis<NBP>(a.basis_kind, a.nb, a.rc, len, v, nullptr);
         }
-        store_a32(tAhi + lane_off, tAlo + lane_off, 0, v);
+        store_a_n<NBP>(tAhi + lane_off, tAlo + lane_off, 0, v);
       }
       a_ready();
       if (tid == 0) {
@@ -402,11 +418,11 @@ __global__ void __launch_bounds__(RTH, RT_PER_SM) radial_bwd_tc_kernel(RadialTcA
       const bool valid = e < a.E;
       float demb[NBP];  // half 0
       float ry[3] = {0.f, 0.f, 0.f};
-      // ---- A = [emb (NBP) | dgates (16)] (half 0) ; D0 = emb W1^T (a1 - b1), D1 = dg W3 (dh2)
+      // ---- A = [emb (NBP, half 0) | dgates (16, half 1)] ; D0 = emb W1^T (a1 - b1), D1 = dg W3 (dh2)
       if (half == 0) {
-        float v[32];
+        float v[NBP];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        for (int i = 0; i < NBP; ++i) v[i] = 0.f;
 #pragma unroll
         for (int b = 0; b < NBP; ++b) demb[b] = 0.f;
         if (valid) {
@@ -414,15 +430,20 @@ __global__ void __launch_bounds__(RTH, RT_PER_SM) radial_bwd_tc_kernel(RadialTcA
           ry[0] = r4.y; ry[1] = r4.z; ry[2] = r4.w;
           const float len = sqrtf(r4.y * r4.y + r4.z * r4.z + r4.w * r4.w);
           radial_basis<NBP>(a.basis_kind, a.nb, a.rc, len, v, demb);
-          if (!HOUT) {
-            const float4* dg4 = reinterpret_cast<const float4*>(a.dgates + ((int64_t)layer * a.E + e) * 12);
-            const float4 g0 = dg4[0], g1 = dg4[1], g2 = dg4[2];
-            v[NBP + 0] = g0.x; v[NBP + 1] = g0.y; v[NBP + 2] = g0.z; v[NBP + 3] = g0.w;
-            v[NBP + 4] = g1.x; v[NBP + 5] = g1.y; v[NBP + 6] = g1.z; v[NBP + 7] = g1.w;
-            v[NBP + 8] = g2.x; v[NBP + 9] = g2.y; v[NBP + 10] = g2.z;
-          }
         }
-        store_a32(tAhi + lane_off, tAlo + lane_off, 0, v);
+        store_a_n<NBP>(tAhi + lane_off, tAlo + lane_off, 0, v);
+      } else if (!HOUT) {
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = 0.f;
+        if (valid) {
+          const float4* dg4 = reinterpret_cast<const float4*>(a.dgates + ((int64_t)layer * a.E + e) * 12);
+          const float4 g0 = dg4[0], g1 = dg4[1], g2 = dg4[2];
+          v[0] = g0.x; v[1] = g0.y; v[2] = g0.z; v[3] = g0.w;
+          v[4] = g1.x; v[5] = g1.y; v[6] = g1.z; v[7] = g1.w;
+          v[8] = g2.x; v[9] = g2.y; v[10] = g2.z;
+        }
+        store_a_n<16>(tAhi + lane_off, tAlo + lane_off, NBP, v);
       }
       a_ready();
       if (tid == 0) {
