@@ -199,9 +199,16 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_z_kernel(ConvArgs a, co
 #pragma unroll
     for (int c = 0; c < CPL; ++c) z[r][c] = 0.f;
   const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
+  // Senders of the edges [blk, blk + 32) are held one per lane and handed out by shuffle, so a
+  // row gather does not wait for its index load.
+  int blk = e0, my_src = e0 + lane < e1 ? a.src[e0 + lane] : 0;
   // a sender outside the previous layer's evaluated atoms is skipped and flagged
   auto fetch = [&](int e, float (&xd)[NK][CPL], float& yg) -> bool {
-    const int64_t s = a.src[e];
+    if (e >= blk + 32) {  // warp-uniform
+      blk += 32;
+      my_src = blk + lane < e1 ? a.src[blk + lane] : 0;
+    }
+    const int64_t s = __shfl_sync(0xffffffffu, my_src, e - blk);
     yg = load_yg(a, e, lane);
     const bool ok = s < a.src_limit;
 #pragma unroll
@@ -256,10 +263,22 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_r_kernel(ConvArgs a, co
 #pragma unroll
     for (int c = 0; c < CPL; ++c) r[i][c] = 0.f;
   const int t0 = a.tr_ptr[s], t1 = a.tr_ptr[s + 1];
+  // Edge ids and receivers of [blk, blk + 32) are held one per lane and handed out by shuffle
+  // (receivers precomputed: no dependent index chain through dst[e]).
+  int blk = t0, my_eid = 0, my_dst = 0;
+  if (t0 + lane < t1) {
+    my_eid = a.tr_eid[t0 + lane];
+    my_dst = a.tr_dst[t0 + lane];
+  }
   // a receiver not evaluated in this layer carries no gradient
   auto fetch = [&](int t, float (&gd)[NK][CPL], float& yg) -> bool {
-    const int64_t e = a.tr_eid[t];
-    const int64_t d = a.tr_dst[t];  // precomputed: no dependent index chain through dst[e]
+    if (t >= blk + 32) {  // warp-uniform
+      blk += 32;
+      my_eid = blk + lane < t1 ? a.tr_eid[blk + lane] : 0;
+      my_dst = blk + lane < t1 ? a.tr_dst[blk + lane] : 0;
+    }
+    const int64_t e = __shfl_sync(0xffffffffu, my_eid, t - blk);
+    const int64_t d = __shfl_sync(0xffffffffu, my_dst, t - blk);
     yg = load_yg(a, e, lane);
     const bool on = d < a.dst_limit;
     const float inv = on ? a.invdeg[d] : 0.f;
