@@ -9,7 +9,8 @@
 //   f_next[n, l3, kk, o] = (1/deg) sum_{p in l3} sum_i W[p,o,i] Z[n,p,kk,i]  (GEMM, gemm.cu)
 // which is the same sum in another order.  One warp owns one node; lanes own channels
 // (c = lane + 32*j, j < C/32); the per-edge coupled harmonics Yt (115 values) are built
-// once per edge by the warp into shared memory and read as broadcasts.
+// once per edge (one lane per edge, 32 edges at a time) into shared memory and read as
+// broadcasts.
 //
 // conv1 (ICTDIrrepsE3Conv, pure_cartesian_ictd_layers_full.py:341-473): x2 holds only the l=0
 // scalar Ai[dst], so only paths (l,0,l) contribute and
@@ -24,92 +25,77 @@ namespace fsc {
 
 using namespace ictd2;
 
-struct QTab {
-  int8_t path[NQ];
-  int8_t yb[NQ];
-  uint8_t qpad[NQ];  // position of q in the padded per-edge layout (QPOFF blocks)
-};
-
 // Per-edge coupled harmonics are stored with every path's block padded to a multiple of 4
 // entries (offsets QPOFF), so a path's weights are read as 16-byte shared-memory vectors.
 __host__ __device__ constexpr int QPOFF(int p) {
-  constexpr int t[NP] = {0, 4, 8, 16, 28, 32, 48, 60, 88, 104, 112};
-  return t[p];
+  switch (p) {
+    case 0: return 0;
+    case 1: return 4;
+    case 2: return 8;
+    case 3: return 16;
+    case 4: return 28;
+    case 5: return 32;
+    case 6: return 48;
+    case 7: return 60;
+    case 8: return 88;
+    case 9: return 104;
+    default: return 112;  // p = 10
+  }
 }
-constexpr int NQP = 140;
-
-constexpr QTab make_qtab() {
-  QTab t{};
-  for (int p = 0; p < NP; ++p)
-    for (int m1 = 0; m1 < 2 * L1(p) + 1; ++m1)
-      for (int kk = 0; kk < 2 * L3(p) + 1; ++kk) {
-        const int q = qidx(p, m1, kk);
-        t.path[q] = (int8_t)p;
-        t.yb[q] = (int8_t)KB(L2(p));
-        t.qpad[q] = (uint8_t)(QPOFF(p) + m1 * (2 * L3(p) + 1) + kk);
-      }
-  return t;
-}
-
-__constant__ QTab c_qtab = make_qtab();
+constexpr int NQP = 140;                      // padded row; NQP / 4 odd: 16-byte stores by 8 lanes hit 8 bank groups
+__host__ __device__ constexpr int NPATHQ(int p) { return (2 * L1(p) + 1) * (2 * L3(p) + 1); }
 
 constexpr int CONV_WARPS = 4;
+constexpr int YT_EDGES = 32;                  // edges whose Yt rows a warp holds at once
+constexpr int CG2_FLOATS = (NQ * 5 + 3) / 4 * 4;
+constexpr uint32_t ZR_SMEM = 4u * (CG2_FLOATS + CONV_WARPS * YT_EDGES * NQP);
 
-struct __align__(16) EdgeBuf {
-  float yt[NQP];
-  float yg[24];  // Y (12) then gates (12) of the edge
-};
+__device__ __forceinline__ void load_cg2(float* cg2, const float* tables) {
+  for (int i = threadIdx.x; i < NQ * 5; i += blockDim.x) cg2[i] = tables[TAB_CG2 + i];
+}
 
-// The Yt entries a lane builds are q = lane + 32 j (j < 4).  Their Y offset and path (byte j of
-// `info` = yb | path << 4) and padded position (byte j of `pad`) live in two registers, read once
-// per warp: per-lane indices into __constant__ memory serialise, which made the indexed-constant
-// path the limiter of the edge loops.
-struct LaneQ {
-  uint32_t info, pad;
-};
-__device__ __forceinline__ LaneQ lane_q(int lane) {
-  LaneQ r{0u, 0u};
+// One edge's coupled harmonics (the calling lane's), Yt[q] = gate_p sum_m cg2[q][m] Y[KB(l2)+m],
+// written to its padded row with 16-byte stores.  Y and g: the edge's 9 harmonics and 11 gates.
+__device__ __forceinline__ void build_yt_row(float* __restrict__ row, const float* __restrict__ cg2, const float* Y,
+                                             const float* g) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int q = lane + 32 * j;
-    if (q < NQ) {
-      const int p = c_qtab.path[q];
-      r.info |= (uint32_t)(c_qtab.yb[q] | (p << 4)) << (8 * j);
-      r.pad |= (uint32_t)(c_qtab.qpad[q]) << (8 * j);
+  for (int p = 0; p < NP; ++p) {
+    float v[28];
+#pragma unroll
+    for (int i = 0; i < 28; ++i) {
+      if (i < NPATHQ(p)) {
+        const int q = QOFF(p) + i;
+        float acc = 0.f;
+#pragma unroll
+        for (int m = 0; m < 2 * L2(p) + 1; ++m) acc = fmaf(cg2[5 * q + m], Y[KB(L2(p)) + m], acc);
+        v[i] = acc * g[p];
+      } else {
+        v[i] = 0.f;
+      }
     }
-  }
-  return r;
-}
-
-// This lane's share of edge e's Y and gates (lanes 0-11: Y, 12-23: gates).
-__device__ __forceinline__ float load_yg(const ConvArgs& a, int64_t e, int lane) {
-  return lane < 12 ? a.edge_y[12 * e + lane] : (lane < 24 ? a.gates[12 * e + lane - 12] : 0.f);
-}
-
-// Warp-cooperative: Yt[q] = gate[p(q)] * sum_m cg2[q][m] Y[yb(q) + m] into b.yt (padded layout).
-__device__ __forceinline__ void build_yt(EdgeBuf& b, const float* __restrict__ cg2, float yg, int lane, LaneQ lq) {
-  if (lane < 24) b.yg[lane] = yg;
-  __syncwarp();
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int q = lane + 32 * j;
-    if (q < NQ) {
-      const uint32_t t = lq.info >> (8 * j);
-      const int yb = (int)(t & 15u);
-      float v = 0.f;
-#pragma unroll
-      for (int m = 0; m < 5; ++m) v = fmaf(cg2[5 * q + m], b.yg[yb + m], v);
-      b.yt[(lq.pad >> (8 * j)) & 255u] = v * b.yg[12 + ((t >> 4) & 15u)];
-    }
+    for (int i = 0; i < (NPATHQ(p) + 3) / 4; ++i)
+      reinterpret_cast<float4*>(row + QPOFF(p))[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
   }
-  __syncwarp();
 }
 
-// Path p's (2 l1 + 1) x (2 l3 + 1) weights (m1-major) from the padded Yt into registers.
+// The 12-float rows of edge e in edge_y and gates.
+__device__ __forceinline__ void load_edge_yg(const ConvArgs& a, int64_t e, float* Y, float* g) {
+  const float4* y4 = reinterpret_cast<const float4*>(a.edge_y + 12 * e);
+  const float4* g4 = reinterpret_cast<const float4*>(a.gates + 12 * e);
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const float4 u = y4[i], v = g4[i];
+    Y[4 * i] = u.x; Y[4 * i + 1] = u.y; Y[4 * i + 2] = u.z; Y[4 * i + 3] = u.w;
+    g[4 * i] = v.x; g[4 * i + 1] = v.y; g[4 * i + 2] = v.z; g[4 * i + 3] = v.w;
+  }
+}
+
+// Path p's (2 l1 + 1) x (2 l3 + 1) weights (m1-major) from a padded Yt row into registers.
 template <int P>
-__device__ __forceinline__ void path_weights(const EdgeBuf& b, float* w) {
-  constexpr int n = (2 * L1(P) + 1) * (2 * L3(P) + 1);
-  const float4* v4 = reinterpret_cast<const float4*>(b.yt + QPOFF(P));
+__device__ __forceinline__ void path_weights(const float* __restrict__ yt, float* w) {
+  constexpr int n = NPATHQ(P);
+  const float4* v4 = reinterpret_cast<const float4*>(yt + QPOFF(P));
 #pragma unroll
   for (int i = 0; i < (n + 3) / 4; ++i) {
     const float4 v = v4[i];
@@ -118,10 +104,6 @@ __device__ __forceinline__ void path_weights(const EdgeBuf& b, float* w) {
     w[4 * i + 2] = v.z;
     w[4 * i + 3] = v.w;
   }
-}
-
-__device__ __forceinline__ void load_cg2(float* cg2, const float* tables) {
-  for (int i = threadIdx.x; i < NQ * 5; i += blockDim.x) cg2[i] = tables[TAB_CG2 + i];
 }
 
 // acc[c] += x[c] * w over this lane's channels; two channels go through one packed fp32 FMA.
@@ -138,9 +120,9 @@ __device__ __forceinline__ void fma_ch(const float (&x)[CPL], float w, float (&a
 }
 
 template <int P, int CPL>
-__device__ __forceinline__ void z_path(const EdgeBuf& b, const float (&xv)[NK][CPL], float (&z)[NZ][CPL]) {
+__device__ __forceinline__ void z_path(const float* yt, const float (&xv)[NK][CPL], float (&z)[NZ][CPL]) {
   float w[28];
-  path_weights<P>(b, w);
+  path_weights<P>(yt, w);
   constexpr int n3 = 2 * L3(P) + 1;
 #pragma unroll
   for (int m1 = 0; m1 < 2 * L1(P) + 1; ++m1)
@@ -149,9 +131,9 @@ __device__ __forceinline__ void z_path(const EdgeBuf& b, const float (&xv)[NK][C
 }
 
 template <int P, int CPL>
-__device__ __forceinline__ void r_path(const EdgeBuf& b, const float (&gv)[NK][CPL], float (&r)[NZ][CPL]) {
+__device__ __forceinline__ void r_path(const float* yt, const float (&gv)[NK][CPL], float (&r)[NZ][CPL]) {
   float w[28];
-  path_weights<P>(b, w);
+  path_weights<P>(yt, w);
   constexpr int n3 = 2 * L3(P) + 1;
 #pragma unroll
   for (int m1 = 0; m1 < 2 * L1(P) + 1; ++m1)
@@ -167,75 +149,78 @@ __device__ __forceinline__ void all_paths(T&... t) {
 }
 template <int P, int CPL>
 struct ZPath {
-  __device__ __forceinline__ static void run(const EdgeBuf& b, const float (&xv)[NK][CPL], float (&z)[NZ][CPL]) {
-    z_path<P, CPL>(b, xv, z);
+  __device__ __forceinline__ static void run(const float* yt, const float (&xv)[NK][CPL], float (&z)[NZ][CPL]) {
+    z_path<P, CPL>(yt, xv, z);
   }
 };
 template <int P, int CPL>
 struct RPath {
-  __device__ __forceinline__ static void run(const EdgeBuf& b, const float (&gv)[NK][CPL], float (&r)[NZ][CPL]) {
-    r_path<P, CPL>(b, gv, r);
+  __device__ __forceinline__ static void run(const float* yt, const float (&gv)[NK][CPL], float (&r)[NZ][CPL]) {
+    r_path<P, CPL>(yt, gv, r);
   }
 };
 
 // ---------------------------------------------------------------- conv2 forward: Z
-// The next edge's sender row, Y and gates are loaded while the current edge is contracted.
+// Edges are taken 32 at a time: each lane builds the Yt row of one edge (lane = edge) into the
+// warp's shared-memory rows and holds its sender; then the warp walks the edges (lanes =
+// channels), the next edge's sender row loaded while the current edge is contracted.
 template <int CPL>
-__global__ void __launch_bounds__(CONV_WARPS * 32) conv2_z_kernel(ConvArgs a, const float* __restrict__ x,
-                                                                  float* __restrict__ Z) {
-  __shared__ float cg2[NQ * 5];
-  __shared__ EdgeBuf bufs[CONV_WARPS];
+__global__ void __launch_bounds__(CONV_WARPS * 32, 3) conv2_z_kernel(ConvArgs a, const float* __restrict__ x,
+                                                                     float* __restrict__ Z) {
+  extern __shared__ float4 zr_smem4[];
+  float* cg2 = reinterpret_cast<float*>(zr_smem4);
   load_cg2(cg2, a.tables);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n = (int64_t)blockIdx.x * CONV_WARPS + warp;
   if (n >= a.N) return;
   constexpr int C = 32 * CPL;
-  EdgeBuf& b = bufs[warp];
-  const LaneQ lq = lane_q(lane);
+  float* yt = cg2 + CG2_FLOATS + warp * YT_EDGES * NQP;
   float z[NZ][CPL];
 #pragma unroll
   for (int r = 0; r < NZ; ++r)
 #pragma unroll
     for (int c = 0; c < CPL; ++c) z[r][c] = 0.f;
   const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
-  // Senders of the edges [blk, blk + 32) are held one per lane and handed out by shuffle, so a
-  // row gather does not wait for its index load.
-  int blk = e0, my_src = e0 + lane < e1 ? a.src[e0 + lane] : 0;
-  // a sender outside the previous layer's evaluated atoms is skipped and flagged
-  auto fetch = [&](int e, float (&xd)[NK][CPL], float& yg) -> bool {
-    if (e >= blk + 32) {  // warp-uniform
-      blk += 32;
-      my_src = blk + lane < e1 ? a.src[blk + lane] : 0;
+  for (int blk = e0; blk < e1; blk += YT_EDGES) {
+    const int nb = min(YT_EDGES, e1 - blk);
+    int my_src = 0;
+    __syncwarp();  // the previous block's rows are read
+    if (lane < nb) {
+      float Y[12], g[12];
+      my_src = a.src[blk + lane];
+      load_edge_yg(a, blk + lane, Y, g);
+      build_yt_row(yt + lane * NQP, cg2, Y, g);
     }
-    const int64_t s = __shfl_sync(0xffffffffu, my_src, e - blk);
-    yg = load_yg(a, e, lane);
-    const bool ok = s < a.src_limit;
+    __syncwarp();
+    // a sender outside the previous layer's evaluated atoms is skipped and flagged
+    auto fetch = [&](int j, float (&xd)[NK][CPL]) -> bool {
+      const int64_t s = __shfl_sync(0xffffffffu, my_src, j);
+      const bool ok = s < a.src_limit;
 #pragma unroll
-    for (int k = 0; k < NK; ++k)
+      for (int k = 0; k < NK; ++k)
 #pragma unroll
-      for (int c = 0; c < CPL; ++c) xd[k][c] = ok ? x[(s * NK + k) * C + lane + 32 * c] : 0.f;
-    return ok;
-  };
-  float xv[NK][CPL], yg = 0.f;
-  bool ok = e0 < e1 ? fetch(e0, xv, yg) : true;
-  for (int e = e0; e < e1; ++e) {
-    float xn[NK][CPL], ygn = 0.f;
-    bool okn = true;
-    if (e + 1 < e1) okn = fetch(e + 1, xn, ygn);
-    if (ok) {
-      build_yt(b, cg2, yg, lane, lq);
-      all_paths<CPL, ZPath>(b, xv, z);
-      __syncwarp();
-    } else if (lane == 0) {
-      atomicCAS(a.err, 0, 70);
+        for (int c = 0; c < CPL; ++c) xd[k][c] = ok ? x[(s * NK + k) * C + lane + 32 * c] : 0.f;
+      return ok;
+    };
+    float xv[NK][CPL];
+    bool ok = fetch(0, xv);
+    for (int j = 0; j < nb; ++j) {
+      float xn[NK][CPL];
+      bool okn = true;
+      if (j + 1 < nb) okn = fetch(j + 1, xn);
+      if (ok) {
+        const float* row = yt + j * NQP;
+        all_paths<CPL, ZPath>(row, xv, z);
+      } else if (lane == 0) {
+        atomicCAS(a.err, 0, 70);
+      }
+#pragma unroll
+      for (int k = 0; k < NK; ++k)
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) xv[k][c] = xn[k][c];
+      ok = okn;
     }
-#pragma unroll
-    for (int k = 0; k < NK; ++k)
-#pragma unroll
-      for (int c = 0; c < CPL; ++c) xv[k][c] = xn[k][c];
-    yg = ygn;
-    ok = okn;
   }
 #pragma unroll
   for (int r = 0; r < NZ; ++r)
@@ -244,67 +229,66 @@ __global__ void __launch_bounds__(CONV_WARPS * 32) conv2_z_kernel(ConvArgs a, co
 }
 
 // ---------------------------------------------------------------- conv2 backward: R (src-centric)
+// Same blocking as conv2_z over the sender's out-edges (transposed order); the receivers are
+// precomputed, so no dependent index chain runs through dst[e].
 template <int CPL>
-__global__ void __launch_bounds__(CONV_WARPS * 32) conv2_r_kernel(ConvArgs a, const float* __restrict__ G,
-                                                                  float* __restrict__ R) {
-  __shared__ float cg2[NQ * 5];
-  __shared__ EdgeBuf bufs[CONV_WARPS];
+__global__ void __launch_bounds__(CONV_WARPS * 32, 3) conv2_r_kernel(ConvArgs a, const float* __restrict__ G,
+                                                                     float* __restrict__ R) {
+  extern __shared__ float4 zr_smem4[];
+  float* cg2 = reinterpret_cast<float*>(zr_smem4);
   load_cg2(cg2, a.tables);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t s = (int64_t)blockIdx.x * CONV_WARPS + warp;
   if (s >= a.N) return;
   constexpr int C = 32 * CPL;
-  EdgeBuf& b = bufs[warp];
-  const LaneQ lq = lane_q(lane);
+  float* yt = cg2 + CG2_FLOATS + warp * YT_EDGES * NQP;
   float r[NZ][CPL];
 #pragma unroll
   for (int i = 0; i < NZ; ++i)
 #pragma unroll
     for (int c = 0; c < CPL; ++c) r[i][c] = 0.f;
   const int t0 = a.tr_ptr[s], t1 = a.tr_ptr[s + 1];
-  // Edge ids and receivers of [blk, blk + 32) are held one per lane and handed out by shuffle
-  // (receivers precomputed: no dependent index chain through dst[e]).
-  int blk = t0, my_eid = 0, my_dst = 0;
-  if (t0 + lane < t1) {
-    my_eid = a.tr_eid[t0 + lane];
-    my_dst = a.tr_dst[t0 + lane];
-  }
-  // a receiver not evaluated in this layer carries no gradient
-  auto fetch = [&](int t, float (&gd)[NK][CPL], float& yg) -> bool {
-    if (t >= blk + 32) {  // warp-uniform
-      blk += 32;
-      my_eid = blk + lane < t1 ? a.tr_eid[blk + lane] : 0;
-      my_dst = blk + lane < t1 ? a.tr_dst[blk + lane] : 0;
+  for (int blk = t0; blk < t1; blk += YT_EDGES) {
+    const int nb = min(YT_EDGES, t1 - blk);
+    int my_dst = 0;
+    float my_inv = 0.f;  // 1/deg(dst), 0 for a receiver not evaluated in this layer
+    __syncwarp();  // the previous block's rows are read
+    if (lane < nb) {
+      const int64_t e = a.tr_eid[blk + lane];
+      my_dst = a.tr_dst[blk + lane];
+      my_inv = my_dst < a.dst_limit ? a.invdeg[my_dst] : 0.f;
+      float Y[12], g[12];
+      load_edge_yg(a, e, Y, g);
+      build_yt_row(yt + lane * NQP, cg2, Y, g);
     }
-    const int64_t e = __shfl_sync(0xffffffffu, my_eid, t - blk);
-    const int64_t d = __shfl_sync(0xffffffffu, my_dst, t - blk);
-    yg = load_yg(a, e, lane);
-    const bool on = d < a.dst_limit;
-    const float inv = on ? a.invdeg[d] : 0.f;
+    __syncwarp();
+    auto fetch = [&](int j, float (&gd)[NK][CPL]) -> bool {
+      const int64_t d = __shfl_sync(0xffffffffu, my_dst, j);
+      const float inv = __shfl_sync(0xffffffffu, my_inv, j);
+      const bool on = d < a.dst_limit;
 #pragma unroll
-    for (int k = 0; k < NK; ++k)
+      for (int k = 0; k < NK; ++k)
 #pragma unroll
-      for (int c = 0; c < CPL; ++c) gd[k][c] = on ? G[(d * NK + k) * C + lane + 32 * c] * inv : 0.f;
-    return on;
-  };
-  float gv[NK][CPL], yg = 0.f;
-  bool on = t0 < t1 ? fetch(t0, gv, yg) : false;
-  for (int t = t0; t < t1; ++t) {
-    float gn[NK][CPL], ygn = 0.f;
-    bool onn = false;
-    if (t + 1 < t1) onn = fetch(t + 1, gn, ygn);
-    if (on) {
-      build_yt(b, cg2, yg, lane, lq);
-      all_paths<CPL, RPath>(b, gv, r);
-      __syncwarp();
+        for (int c = 0; c < CPL; ++c) gd[k][c] = on ? G[(d * NK + k) * C + lane + 32 * c] * inv : 0.f;
+      return on;
+    };
+    float gv[NK][CPL];
+    bool on = fetch(0, gv);
+    for (int j = 0; j < nb; ++j) {
+      float gn[NK][CPL];
+      bool onn = false;
+      if (j + 1 < nb) onn = fetch(j + 1, gn);
+      if (on) {
+        const float* row = yt + j * NQP;
+        all_paths<CPL, RPath>(row, gv, r);
+      }
+#pragma unroll
+      for (int k = 0; k < NK; ++k)
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) gv[k][c] = gn[k][c];
+      on = onn;
     }
-#pragma unroll
-    for (int k = 0; k < NK; ++k)
-#pragma unroll
-      for (int c = 0; c < CPL; ++c) gv[k][c] = gn[k][c];
-    yg = ygn;
-    on = onn;
   }
 #pragma unroll
   for (int i = 0; i < NZ; ++i)
@@ -652,26 +636,32 @@ int launch_conv1_backward(const ConvArgs& a, const float* ai, const float* vsp, 
                           float* dY, cudaStream_t st) {
   FSC_CONV_LAUNCH(conv1_backward_kernel, a, ai, vsp, G1, dgates, dY);
 }
+// Kernels with dynamic shared memory above the 48 KB default.
+#define FSC_CONV_LAUNCH_SMEM(KERNEL, SMEM, ...)                                                 \
+  do {                                                                                        \
+    const unsigned blocks = (unsigned)ceil_div(a.N, CONV_WARPS);                              \
+    if (a.N == 0) return FSC_OK;                                                              \
+    if (a.C == 32) {                                                                          \
+      cudaFuncSetAttribute(KERNEL<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(SMEM)); \
+      KERNEL<1><<<blocks, CONV_WARPS * 32, SMEM, st>>>(__VA_ARGS__);                          \
+    } else if (a.C == 64) {                                                                   \
+      cudaFuncSetAttribute(KERNEL<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(SMEM)); \
+      KERNEL<2><<<blocks, CONV_WARPS * 32, SMEM, st>>>(__VA_ARGS__);                          \
+    } else {                                                                                  \
+      return fail(FSC_ERR_UNSUPPORTED, "ictd conv kernels support channels 32 or 64");        \
+    }                                                                                         \
+    return check_launch(#KERNEL);                                                             \
+  } while (0)
+
 int launch_conv2_z(const ConvArgs& a, const float* x, float* Z, cudaStream_t st) {
-  FSC_CONV_LAUNCH(conv2_z_kernel, a, x, Z);
+  FSC_CONV_LAUNCH_SMEM(conv2_z_kernel, ZR_SMEM, a, x, Z);
 }
 int launch_conv2_r(const ConvArgs& a, const float* G, float* R, cudaStream_t st) {
-  FSC_CONV_LAUNCH(conv2_r_kernel, a, G, R);
+  FSC_CONV_LAUNCH_SMEM(conv2_r_kernel, ZR_SMEM, a, G, R);
 }
 int launch_conv2_q(const ConvArgs& a, const float* x, const float* dZ, float* dgates, float* dY,
                    cudaStream_t st) {
-  if (a.N == 0) return FSC_OK;
-  const unsigned blocks = (unsigned)ceil_div(a.N, CONV_WARPS);
-  if (a.C == 32) {
-    cudaFuncSetAttribute(conv2_q_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QSMEM);
-    conv2_q_kernel<1><<<blocks, CONV_WARPS * 32, QSMEM, st>>>(a, x, dZ, dgates, dY);
-  } else if (a.C == 64) {
-    cudaFuncSetAttribute(conv2_q_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QSMEM);
-    conv2_q_kernel<2><<<blocks, CONV_WARPS * 32, QSMEM, st>>>(a, x, dZ, dgates, dY);
-  } else {
-    return fail(FSC_ERR_UNSUPPORTED, "ictd conv kernels support channels 32 or 64");
-  }
-  return check_launch("conv2_q_kernel");
+  FSC_CONV_LAUNCH_SMEM(conv2_q_kernel, QSMEM, a, x, dZ, dgates, dY);
 }
 
 }  // namespace fsc
