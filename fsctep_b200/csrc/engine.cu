@@ -85,6 +85,7 @@ struct Plan {
   float* dFg;
   float* gmax;
   int* err;
+  int* work;  // conv2 node counter
   // tensor-core GEMM operand images of the weights (null: CUDA-core GEMM)
   bool gtc;
   float* img_fwd[8][3];     // conv2 layer k, l3
@@ -194,6 +195,7 @@ void layout(Plan& p, Arena& ar, const fsc_ictd_config* cfg, int64_t N, int64_t E
   p.rtc = g_radial_path == 0 && radial_tc_supported(p.nb);
   p.n_pad = ceil_div(std::max<int64_t>(N, 1), 128) * 128;
   p.err = ar.take<int>(64);
+  p.work = ar.take<int>(16);
   if (p.tc) {
     p.chunkbuf = nullptr;
     p.Fg = ar.take<float>(p.nrows * p.n_pad);
@@ -320,6 +322,7 @@ ConvArgs conv_args(const Ctx& c, int layer) {
   a.err = c.p.err;
   a.tr_dst = c.p.tr_dst;
   a.invdeg = c.p.invdeg;
+  a.work = c.p.work;
   return a;
 }
 

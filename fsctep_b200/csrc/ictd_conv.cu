@@ -17,6 +17,8 @@
 //   f1[n, l, k, o] = (1/deg) sum_i Vsp[Z_n, l, i, o] * S[n, l, k, i],
 //   S[n, l, k, i]  = sum_{e->n} gate_e[p(l,0,l)] * Y1_e[l,k] * Ai[Z_src, i],
 // with Vsp[s,l,i,o] = sum_j W1[p(l,0,l), o, i, j] Ai[s, j] precomputed per species.
+#include <algorithm>
+
 #include "common.cuh"
 #include "ictd_paths.cuh"
 #include "kernels.cuh"
@@ -24,6 +26,23 @@
 namespace fsc {
 
 using namespace ictd2;
+
+constexpr int CONV_WARPS = 4;
+
+// Node walk of the conv2 kernels.  With a work counter, warps take nodes in increasing order as
+// they free up (a persistent grid that keeps the nodes in flight, and so their neighbours' rows,
+// close together); without one, every warp owns one node.
+__device__ __forceinline__ int64_t take_node(int* work, int lane) {
+  int v = 0;
+  if (lane == 0) v = atomicAdd(work, 1);
+  return __shfl_sync(0xffffffffu, v, 0);
+}
+__device__ __forceinline__ int64_t first_node(const ConvArgs& a, int warp, int lane) {
+  return a.work ? take_node(a.work, lane) : (int64_t)blockIdx.x * CONV_WARPS + warp;
+}
+__device__ __forceinline__ int64_t next_node(const ConvArgs& a, int lane) {
+  return a.work ? take_node(a.work, lane) : a.N;
+}
 
 // Per-edge coupled harmonics are stored with every path's block padded to a multiple of 4
 // entries (offsets QPOFF), so a path's weights are read as 16-byte shared-memory vectors.
@@ -45,7 +64,6 @@ __host__ __device__ constexpr int QPOFF(int p) {
 constexpr int NQP = 140;                      // padded row; NQP / 4 odd: 16-byte stores by 8 lanes hit 8 bank groups
 __host__ __device__ constexpr int NPATHQ(int p) { return (2 * L1(p) + 1) * (2 * L3(p) + 1); }
 
-constexpr int CONV_WARPS = 4;
 constexpr int YT_EDGES = 32;                  // edges whose Yt rows a warp holds at once
 constexpr int CG2_FLOATS = (NQ * 5 + 3) / 4 * 4;
 constexpr uint32_t ZR_SMEM = 4u * (CG2_FLOATS + CONV_WARPS * YT_EDGES * NQP);
@@ -172,60 +190,60 @@ __global__ void __launch_bounds__(CONV_WARPS * 32, 3) conv2_z_kernel(ConvArgs a,
   load_cg2(cg2, a.tables);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t n = (int64_t)blockIdx.x * CONV_WARPS + warp;
-  if (n >= a.N) return;
-  constexpr int C = 32 * CPL;
-  float* yt = cg2 + CG2_FLOATS + warp * YT_EDGES * NQP;
-  float z[NZ][CPL];
+  for (int64_t n = first_node(a, warp, lane); n < a.N; n = next_node(a, lane)) {
+    constexpr int C = 32 * CPL;
+    float* yt = cg2 + CG2_FLOATS + warp * YT_EDGES * NQP;
+    float z[NZ][CPL];
 #pragma unroll
-  for (int r = 0; r < NZ; ++r)
+    for (int r = 0; r < NZ; ++r)
 #pragma unroll
-    for (int c = 0; c < CPL; ++c) z[r][c] = 0.f;
-  const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
-  for (int blk = e0; blk < e1; blk += YT_EDGES) {
-    const int nb = min(YT_EDGES, e1 - blk);
-    int my_src = 0;
-    __syncwarp();  // the previous block's rows are read
-    if (lane < nb) {
-      float Y[12], g[12];
-      my_src = a.src[blk + lane];
-      load_edge_yg(a, blk + lane, Y, g);
-      build_yt_row(yt + lane * NQP, cg2, Y, g);
-    }
-    __syncwarp();
-    // a sender outside the previous layer's evaluated atoms is skipped and flagged
-    auto fetch = [&](int j, float (&xd)[NK][CPL]) -> bool {
-      const int64_t s = __shfl_sync(0xffffffffu, my_src, j);
-      const bool ok = s < a.src_limit;
-#pragma unroll
-      for (int k = 0; k < NK; ++k)
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) xd[k][c] = ok ? x[(s * NK + k) * C + lane + 32 * c] : 0.f;
-      return ok;
-    };
-    float xv[NK][CPL];
-    bool ok = fetch(0, xv);
-    for (int j = 0; j < nb; ++j) {
-      float xn[NK][CPL];
-      bool okn = true;
-      if (j + 1 < nb) okn = fetch(j + 1, xn);
-      if (ok) {
-        const float* row = yt + j * NQP;
-        all_paths<CPL, ZPath>(row, xv, z);
-      } else if (lane == 0) {
-        atomicCAS(a.err, 0, 70);
+      for (int c = 0; c < CPL; ++c) z[r][c] = 0.f;
+    const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
+    for (int blk = e0; blk < e1; blk += YT_EDGES) {
+      const int nb = min(YT_EDGES, e1 - blk);
+      int my_src = 0;
+      __syncwarp();  // the previous block's rows are read
+      if (lane < nb) {
+        float Y[12], g[12];
+        my_src = a.src[blk + lane];
+        load_edge_yg(a, blk + lane, Y, g);
+        build_yt_row(yt + lane * NQP, cg2, Y, g);
       }
+      __syncwarp();
+      // a sender outside the previous layer's evaluated atoms is skipped and flagged
+      auto fetch = [&](int j, float (&xd)[NK][CPL]) -> bool {
+        const int64_t s = __shfl_sync(0xffffffffu, my_src, j);
+        const bool ok = s < a.src_limit;
 #pragma unroll
-      for (int k = 0; k < NK; ++k)
+        for (int k = 0; k < NK; ++k)
 #pragma unroll
-        for (int c = 0; c < CPL; ++c) xv[k][c] = xn[k][c];
-      ok = okn;
+          for (int c = 0; c < CPL; ++c) xd[k][c] = ok ? x[(s * NK + k) * C + lane + 32 * c] : 0.f;
+        return ok;
+      };
+      float xv[NK][CPL];
+      bool ok = fetch(0, xv);
+      for (int j = 0; j < nb; ++j) {
+        float xn[NK][CPL];
+        bool okn = true;
+        if (j + 1 < nb) okn = fetch(j + 1, xn);
+        if (ok) {
+          const float* row = yt + j * NQP;
+          all_paths<CPL, ZPath>(row, xv, z);
+        } else if (lane == 0) {
+          atomicCAS(a.err, 0, 70);
+        }
+#pragma unroll
+        for (int k = 0; k < NK; ++k)
+#pragma unroll
+          for (int c = 0; c < CPL; ++c) xv[k][c] = xn[k][c];
+        ok = okn;
+      }
     }
+#pragma unroll
+    for (int r = 0; r < NZ; ++r)
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) Z[(n * NZ + r) * C + lane + 32 * c] = z[r][c];
   }
-#pragma unroll
-  for (int r = 0; r < NZ; ++r)
-#pragma unroll
-    for (int c = 0; c < CPL; ++c) Z[(n * NZ + r) * C + lane + 32 * c] = z[r][c];
 }
 
 // ---------------------------------------------------------------- conv2 backward: R (src-centric)
@@ -239,61 +257,61 @@ __global__ void __launch_bounds__(CONV_WARPS * 32, 3) conv2_r_kernel(ConvArgs a,
   load_cg2(cg2, a.tables);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t s = (int64_t)blockIdx.x * CONV_WARPS + warp;
-  if (s >= a.N) return;
-  constexpr int C = 32 * CPL;
-  float* yt = cg2 + CG2_FLOATS + warp * YT_EDGES * NQP;
-  float r[NZ][CPL];
+  for (int64_t s = first_node(a, warp, lane); s < a.N; s = next_node(a, lane)) {
+    constexpr int C = 32 * CPL;
+    float* yt = cg2 + CG2_FLOATS + warp * YT_EDGES * NQP;
+    float r[NZ][CPL];
 #pragma unroll
-  for (int i = 0; i < NZ; ++i)
+    for (int i = 0; i < NZ; ++i)
 #pragma unroll
-    for (int c = 0; c < CPL; ++c) r[i][c] = 0.f;
-  const int t0 = a.tr_ptr[s], t1 = a.tr_ptr[s + 1];
-  for (int blk = t0; blk < t1; blk += YT_EDGES) {
-    const int nb = min(YT_EDGES, t1 - blk);
-    int my_dst = 0;
-    float my_inv = 0.f;  // 1/deg(dst), 0 for a receiver not evaluated in this layer
-    __syncwarp();  // the previous block's rows are read
-    if (lane < nb) {
-      const int64_t e = a.tr_eid[blk + lane];
-      my_dst = a.tr_dst[blk + lane];
-      my_inv = my_dst < a.dst_limit ? a.invdeg[my_dst] : 0.f;
-      float Y[12], g[12];
-      load_edge_yg(a, e, Y, g);
-      build_yt_row(yt + lane * NQP, cg2, Y, g);
-    }
-    __syncwarp();
-    auto fetch = [&](int j, float (&gd)[NK][CPL]) -> bool {
-      const int64_t d = __shfl_sync(0xffffffffu, my_dst, j);
-      const float inv = __shfl_sync(0xffffffffu, my_inv, j);
-      const bool on = d < a.dst_limit;
-#pragma unroll
-      for (int k = 0; k < NK; ++k)
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) gd[k][c] = on ? G[(d * NK + k) * C + lane + 32 * c] * inv : 0.f;
-      return on;
-    };
-    float gv[NK][CPL];
-    bool on = fetch(0, gv);
-    for (int j = 0; j < nb; ++j) {
-      float gn[NK][CPL];
-      bool onn = false;
-      if (j + 1 < nb) onn = fetch(j + 1, gn);
-      if (on) {
-        const float* row = yt + j * NQP;
-        all_paths<CPL, RPath>(row, gv, r);
+      for (int c = 0; c < CPL; ++c) r[i][c] = 0.f;
+    const int t0 = a.tr_ptr[s], t1 = a.tr_ptr[s + 1];
+    for (int blk = t0; blk < t1; blk += YT_EDGES) {
+      const int nb = min(YT_EDGES, t1 - blk);
+      int my_dst = 0;
+      float my_inv = 0.f;  // 1/deg(dst), 0 for a receiver not evaluated in this layer
+      __syncwarp();  // the previous block's rows are read
+      if (lane < nb) {
+        const int64_t e = a.tr_eid[blk + lane];
+        my_dst = a.tr_dst[blk + lane];
+        my_inv = my_dst < a.dst_limit ? a.invdeg[my_dst] : 0.f;
+        float Y[12], g[12];
+        load_edge_yg(a, e, Y, g);
+        build_yt_row(yt + lane * NQP, cg2, Y, g);
       }
+      __syncwarp();
+      auto fetch = [&](int j, float (&gd)[NK][CPL]) -> bool {
+        const int64_t d = __shfl_sync(0xffffffffu, my_dst, j);
+        const float inv = __shfl_sync(0xffffffffu, my_inv, j);
+        const bool on = d < a.dst_limit;
 #pragma unroll
-      for (int k = 0; k < NK; ++k)
+        for (int k = 0; k < NK; ++k)
 #pragma unroll
-        for (int c = 0; c < CPL; ++c) gv[k][c] = gn[k][c];
-      on = onn;
+          for (int c = 0; c < CPL; ++c) gd[k][c] = on ? G[(d * NK + k) * C + lane + 32 * c] * inv : 0.f;
+        return on;
+      };
+      float gv[NK][CPL];
+      bool on = fetch(0, gv);
+      for (int j = 0; j < nb; ++j) {
+        float gn[NK][CPL];
+        bool onn = false;
+        if (j + 1 < nb) onn = fetch(j + 1, gn);
+        if (on) {
+          const float* row = yt + j * NQP;
+          all_paths<CPL, RPath>(row, gv, r);
+        }
+#pragma unroll
+        for (int k = 0; k < NK; ++k)
+#pragma unroll
+          for (int c = 0; c < CPL; ++c) gv[k][c] = gn[k][c];
+        on = onn;
+      }
     }
+#pragma unroll
+    for (int i = 0; i < NZ; ++i)
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) R[(s * NZ + i) * C + lane + 32 * c] = r[i][c];
   }
-#pragma unroll
-  for (int i = 0; i < NZ; ++i)
-#pragma unroll
-    for (int c = 0; c < CPL; ++c) R[(s * NZ + i) * C + lane + 32 * c] = r[i][c];
 }
 
 // ---------------------------------------------------------------- conv2 backward: gates and Y (dst-centric)
@@ -303,15 +321,18 @@ __global__ void __launch_bounds__(CONV_WARPS * 32, 3) conv2_r_kernel(ConvArgs a,
 //   dgate[p]         = sum_{q in p} Q[q] * Yt0[q],     Yt0[q] = sum_m2 CG_p[m1,m2,kk] Y[KB(l2)+m2]
 //   dY[KB(l2)+m2]   += sum_{q in p} Q[q] * gate[p] * CG_p[m1,m2,kk]
 // Every reduction runs inside one thread: no cross-lane traffic.  The sender rows of the warp's 32
-// edges are staged in shared memory one (l1 group, 16-channel chunk) at a time by coalesced
-// 16-byte asynchronous copies (four lanes per 64-byte row chunk), and each lane then reads its own
-// edge's rows from there; dZ rows are 16-byte vectors that all lanes share (same node).
+// edges are staged in shared memory one (l1 group, 16-channel chunk) step at a time by coalesced
+// 16-byte asynchronous copies (four lanes per 64-byte row chunk), double-buffered so that the
+// next step's copies run under this step's arithmetic; each lane then reads its own edge's rows
+// from there, and the dZ rows of the step (same node for all lanes) as broadcasts.  Q is
+// accumulated as even / odd channel partial sums with packed fp32 FMAs (two channels per
+// instruction).
 constexpr int QCH = 16;                       // channels per staged chunk
 constexpr int QES = 4 * 5 + 1;                // float4 slots per edge in a chunk (odd: no bank conflicts)
 constexpr int QZR = 14;                       // dZ rows of the largest l1 group
-constexpr int QBUF_F4 = 32 * QES + 4 * QZR;   // per warp: sender rows, then dZ rows
+constexpr int QBUF_F4 = 32 * QES + 4 * QZR;   // one step: sender rows, then dZ rows
 constexpr int QTAB_F4 = (NQ * 5 + 3) / 4 + 9; // cg2, then the dZ row list of every group (35 ints)
-constexpr uint32_t QSMEM = 16u * (QTAB_F4 + CONV_WARPS * QBUF_F4);
+constexpr uint32_t QSMEM = 16u * (QTAB_F4 + CONV_WARPS * 2 * QBUF_F4);
 
 // Local index of (p, kk) among the dZ rows of p's l1 group: rows are listed path by path.
 __host__ __device__ constexpr int zlocal(int p, int kk) {
@@ -320,45 +341,75 @@ __host__ __device__ constexpr int zlocal(int p, int kk) {
   return j + kk;
 }
 __host__ __device__ constexpr int zcount(int G) { return zlocal(P_HI(G) - 1, 2 * L3(P_HI(G) - 1)) + 1; }
+__host__ __device__ constexpr int zbase(int G) { return G == 0 ? 0 : (G == 1 ? zcount(0) : zcount(0) + zcount(1)); }
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
                "l"(gmem_src)
                : "memory");
 }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// Issues the copies of step (G, cc) into `buf` as one group: 32 edges x (2G+1) rows x 4 float4
+// (lane copies slots f = lane + 32 i, f = (edge, m1, c4)), then the group's dZ rows.
 template <int G, int C>
-__device__ __forceinline__ void q_group(float4* __restrict__ buf, const int* __restrict__ zlist,
+__device__ __forceinline__ void q_stage(float4* __restrict__ buf, const int* __restrict__ zlist,
+                                        const float* __restrict__ x, int64_t src_row,
+                                        const float* __restrict__ dzn, int cc, int lane) {
+  constexpr int M1 = 2 * G + 1, NZG = zcount(G);
+  static_assert(NZG <= QZR, "dZ row buffer");
+#pragma unroll 1
+  for (int i = 0; i < 4 * M1; ++i) {
+    const int f = lane + 32 * i, e = f / (4 * M1), r = f - e * (4 * M1);
+    const int64_t row = __shfl_sync(0xffffffffu, src_row, e);
+    cp_async16(buf + e * QES + r, x + (row + KB(G) + (r >> 2)) * C + cc * QCH + 4 * (r & 3));
+  }
+  float4* zb = buf + 32 * QES;
+  for (int f = lane; f < 4 * NZG; f += 32)
+    cp_async16(zb + f, dzn + zlist[zbase(G) + (f >> 2)] * C + cc * QCH + 4 * (f & 3));
+  cp_async_commit();
+}
+
+__device__ __forceinline__ float2 ffma2(float a0, float a1, float b0, float b1, float2 c) {
+  return __ffma2_rn(make_float2(a0, a1), make_float2(b0, b1), c);
+}
+
+// Group G: its Q partial sums over all chunks, then its share of dgate / dY.  On entry step
+// (G, 0) is staged (or in flight) in bufs[0]; the group stages every following step, the first
+// step of group G + 1 included, one step ahead.
+template <int G, int C>
+__device__ __forceinline__ void q_group(float4* __restrict__ bufs, const int* __restrict__ zlist,
                                         const float* __restrict__ x, int64_t src_row, const float* __restrict__ dzn,
                                         const float* __restrict__ cg2, const float4* __restrict__ ey4,
                                         const float4* __restrict__ eg4, float* dg, float* dy) {
-  constexpr int Q0 = QOFF(P_LO(G)), NQG = Q_END(G) - Q0, M1 = 2 * G + 1, NZG = zcount(G);
-  static_assert(NZG <= QZR, "dZ row buffer");
+  constexpr int Q0 = QOFF(P_LO(G)), NQG = Q_END(G) - Q0, M1 = 2 * G + 1, NCH = C / QCH;
+  static_assert(NCH % 2 == 0, "every group starts in buffer 0");
   const int lane = threadIdx.x & 31;
-  float4* zb = buf + 32 * QES;
-  float Q[NQG];
+  float2 Q[NQG];
 #pragma unroll
-  for (int i = 0; i < NQG; ++i) Q[i] = 0.f;
+  for (int i = 0; i < NQG; ++i) Q[i] = make_float2(0.f, 0.f);
 #pragma unroll 1
-  for (int cc = 0; cc < C / QCH; ++cc) {
-    __syncwarp();  // every lane is done reading the previous chunk
-    // 32 edges x M1 rows x 4 float4: lane copies slots f = lane + 32 i, f = (e, m1, c4)
-#pragma unroll 1
-    for (int i = 0; i < 4 * M1; ++i) {
-      const int f = lane + 32 * i, e = f / (4 * M1), r = f - e * (4 * M1);
-      const int64_t row = __shfl_sync(0xffffffffu, src_row, e);
-      cp_async16(buf + e * QES + r, x + (row + KB(G) + (r >> 2)) * C + cc * QCH + 4 * (r & 3));
+  for (int cc = 0; cc < NCH; ++cc) {
+    float4* cur = bufs + (cc & 1) * QBUF_F4;
+    float4* nxt = bufs + ((cc + 1) & 1) * QBUF_F4;
+    if (cc + 1 < NCH) {
+      q_stage<G, C>(nxt, zlist, x, src_row, dzn, cc + 1, lane);
+      cp_async_wait<1>();
+    } else if (G < 2) {
+      q_stage<(G < 2 ? G + 1 : 2), C>(nxt, zlist, x, src_row, dzn, 0, lane);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
-    for (int f = lane; f < 4 * NZG; f += 32)
-      cp_async16(zb + f, dzn + zlist[f >> 2] * C + cc * QCH + 4 * (f & 3));
-    cp_async_wait_all();
     __syncwarp();
+    const float4* zb = cur + 32 * QES;
 #pragma unroll 1
     for (int c4 = 0; c4 < QCH / 4; ++c4) {
       float4 xv[M1];
 #pragma unroll
-      for (int m1 = 0; m1 < M1; ++m1) xv[m1] = buf[lane * QES + 4 * m1 + c4];
+      for (int m1 = 0; m1 < M1; ++m1) xv[m1] = cur[lane * QES + 4 * m1 + c4];
 #pragma unroll
       for (int p = P_LO(G); p < P_HI(G); ++p)
 #pragma unroll
@@ -366,15 +417,14 @@ __device__ __forceinline__ void q_group(float4* __restrict__ buf, const int* __r
           const float4 d = zb[4 * zlocal(p, kk) + c4];
 #pragma unroll
           for (int m1 = 0; m1 < M1; ++m1) {
-            float acc = Q[qidx(p, m1, kk) - Q0];
-            acc = fmaf(xv[m1].x, d.x, acc);
-            acc = fmaf(xv[m1].y, d.y, acc);
-            acc = fmaf(xv[m1].z, d.z, acc);
-            acc = fmaf(xv[m1].w, d.w, acc);
+            float2 acc = Q[qidx(p, m1, kk) - Q0];
+            acc = ffma2(xv[m1].x, xv[m1].y, d.x, d.y, acc);
+            acc = ffma2(xv[m1].z, xv[m1].w, d.z, d.w, acc);
             Q[qidx(p, m1, kk) - Q0] = acc;
           }
         }
     }
+    __syncwarp();  // every lane is done with `cur` before it is staged again
   }
   float Y[12], g[12];
 #pragma unroll
@@ -390,11 +440,12 @@ __device__ __forceinline__ void q_group(float4* __restrict__ buf, const int* __r
 #pragma unroll
       for (int kk = 0; kk < 2 * L3(p) + 1; ++kk) {
         const int q = qidx(p, m1, kk);
+        const float Qv = Q[q - Q0].x + Q[q - Q0].y;
         float y0 = 0.f;
 #pragma unroll
         for (int m2 = 0; m2 < 2 * L2(p) + 1; ++m2) y0 = fmaf(cg2[5 * q + m2], Y[KB(L2(p)) + m2], y0);
-        dg[p] = fmaf(Q[q - Q0], y0, dg[p]);
-        const float qg = Q[q - Q0] * g[p];
+        dg[p] = fmaf(Qv, y0, dg[p]);
+        const float qg = Qv * g[p];
 #pragma unroll
         for (int m2 = 0; m2 < 2 * L2(p) + 1; ++m2)
           dy[KB(L2(p)) + m2] = fmaf(qg, cg2[5 * q + m2], dy[KB(L2(p)) + m2]);
@@ -402,56 +453,57 @@ __device__ __forceinline__ void q_group(float4* __restrict__ buf, const int* __r
 }
 
 template <int CPL>
-__global__ void __launch_bounds__(CONV_WARPS * 32, 3) conv2_q_kernel(ConvArgs a, const float* __restrict__ x,
+__global__ void __launch_bounds__(CONV_WARPS * 32, 2) conv2_q_kernel(ConvArgs a, const float* __restrict__ x,
                                                                      const float* __restrict__ dZ,
                                                                      float* __restrict__ dgates,
                                                                      float* __restrict__ dY) {
   extern __shared__ float4 qsmem[];
   float* cg2 = reinterpret_cast<float*>(qsmem);
-  int* zlist = reinterpret_cast<int*>(qsmem + (NQ * 5 + 3) / 4);  // group G's rows at zlocal order
+  int* zlist = reinterpret_cast<int*>(qsmem + (NQ * 5 + 3) / 4);  // group G's rows at zbase(G) + zlocal
   load_cg2(cg2, a.tables);
   if (threadIdx.x < NP) {
-    const int p = threadIdx.x, base = p < P_HI(0) ? 0 : (p < P_HI(1) ? zcount(0) : zcount(0) + zcount(1));
-    for (int kk = 0; kk < 2 * L3(p) + 1; ++kk) zlist[base + zlocal(p, kk)] = zrow(p, kk);
+    const int p = threadIdx.x;
+    for (int kk = 0; kk < 2 * L3(p) + 1; ++kk) zlist[zbase(L1(p)) + zlocal(p, kk)] = zrow(p, kk);
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t n = (int64_t)blockIdx.x * CONV_WARPS + warp;
-  if (n >= a.N) return;
-  constexpr int C = 32 * CPL;
-  float4* buf = qsmem + QTAB_F4 + warp * QBUF_F4;
-  const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
-  if (n >= a.n_active) {  // receiver not evaluated in this layer: its edges' gate gradients are 0
-    for (int e = e0 + lane; e < e1; e += 32) {
-      float4* dgo = reinterpret_cast<float4*>(dgates + 12 * (int64_t)e);
-      dgo[0] = dgo[1] = dgo[2] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t n = first_node(a, warp, lane); n < a.N; n = next_node(a, lane)) {
+    constexpr int C = 32 * CPL;
+    float4* bufs = qsmem + QTAB_F4 + warp * 2 * QBUF_F4;
+    const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
+    if (n >= a.n_active) {  // receiver not evaluated in this layer: its edges' gate gradients are 0
+      for (int e = e0 + lane; e < e1; e += 32) {
+        float4* dgo = reinterpret_cast<float4*>(dgates + 12 * (int64_t)e);
+        dgo[0] = dgo[1] = dgo[2] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      continue;
     }
-    return;
-  }
-  const float* dzn = dZ + n * NZ * C;
-  for (int base = e0; base < e1; base += 32) {
-    const int e = base + lane;
-    const bool active = e < e1;
-    const int64_t ee = active ? e : e0;
-    const int64_t src_row = (int64_t)a.src[ee] * NK;
-    const float4* ey4 = reinterpret_cast<const float4*>(a.edge_y + 12 * ee);
-    const float4* eg4 = reinterpret_cast<const float4*>(a.gates + 12 * ee);
-    float dg[NP], dy[NK];
+    const float* dzn = dZ + n * NZ * C;
+    for (int base = e0; base < e1; base += 32) {
+      const int e = base + lane;
+      const bool active = e < e1;
+      const int64_t ee = active ? e : e0;
+      const int64_t src_row = (int64_t)a.src[ee] * NK;
+      const float4* ey4 = reinterpret_cast<const float4*>(a.edge_y + 12 * ee);
+      const float4* eg4 = reinterpret_cast<const float4*>(a.gates + 12 * ee);
+      float dg[NP], dy[NK];
 #pragma unroll
-    for (int k = 0; k < NK; ++k) dy[k] = 0.f;
+      for (int k = 0; k < NK; ++k) dy[k] = 0.f;
 #pragma unroll
-    for (int p = 0; p < NP; ++p) dg[p] = 0.f;
-    q_group<0, C>(buf, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
-    q_group<1, C>(buf, zlist + zcount(0), x, src_row, dzn, cg2, ey4, eg4, dg, dy);
-    q_group<2, C>(buf, zlist + zcount(0) + zcount(1), x, src_row, dzn, cg2, ey4, eg4, dg, dy);
-    if (!active) continue;
-    float4* dgo = reinterpret_cast<float4*>(dgates + 12 * (int64_t)e);
-    dgo[0] = make_float4(dg[0], dg[1], dg[2], dg[3]);
-    dgo[1] = make_float4(dg[4], dg[5], dg[6], dg[7]);
-    dgo[2] = make_float4(dg[8], dg[9], dg[10], 0.f);
-    float* dyo = dY + 12 * (int64_t)e;
+      for (int p = 0; p < NP; ++p) dg[p] = 0.f;
+      q_stage<0, C>(bufs, zlist, x, src_row, dzn, 0, lane);
+      q_group<0, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
+      q_group<1, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
+      q_group<2, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
+      if (!active) continue;
+      float4* dgo = reinterpret_cast<float4*>(dgates + 12 * (int64_t)e);
+      dgo[0] = make_float4(dg[0], dg[1], dg[2], dg[3]);
+      dgo[1] = make_float4(dg[4], dg[5], dg[6], dg[7]);
+      dgo[2] = make_float4(dg[8], dg[9], dg[10], 0.f);
+      float* dyo = dY + 12 * (int64_t)e;
 #pragma unroll
-    for (int k = 0; k < NK; ++k) dyo[k] += dy[k];
+      for (int k = 0; k < NK; ++k) dyo[k] += dy[k];
+    }
   }
 }
 
@@ -636,21 +688,34 @@ int launch_conv1_backward(const ConvArgs& a, const float* ai, const float* vsp, 
                           float* dY, cudaStream_t st) {
   FSC_CONV_LAUNCH(conv1_backward_kernel, a, ai, vsp, G1, dgates, dY);
 }
-// Kernels with dynamic shared memory above the 48 KB default.
-#define FSC_CONV_LAUNCH_SMEM(KERNEL, SMEM, ...)                                                 \
-  do {                                                                                        \
-    const unsigned blocks = (unsigned)ceil_div(a.N, CONV_WARPS);                              \
-    if (a.N == 0) return FSC_OK;                                                              \
-    if (a.C == 32) {                                                                          \
-      cudaFuncSetAttribute(KERNEL<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(SMEM)); \
-      KERNEL<1><<<blocks, CONV_WARPS * 32, SMEM, st>>>(__VA_ARGS__);                          \
-    } else if (a.C == 64) {                                                                   \
-      cudaFuncSetAttribute(KERNEL<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(SMEM)); \
-      KERNEL<2><<<blocks, CONV_WARPS * 32, SMEM, st>>>(__VA_ARGS__);                          \
-    } else {                                                                                  \
-      return fail(FSC_ERR_UNSUPPORTED, "ictd conv kernels support channels 32 or 64");        \
-    }                                                                                         \
-    return check_launch(#KERNEL);                                                             \
+// Kernels with dynamic shared memory above the 48 KB default.  With a work counter (zeroed here)
+// the grid is as many CTAs as fit on the device at once; without, one warp per node.
+template <typename K>
+unsigned conv_blocks(K kernel, uint32_t smem, const ConvArgs& a) {
+  if (!a.work) return (unsigned)ceil_div(a.N, CONV_WARPS);
+  int dev = 0, sms = 148, occ = 1;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, CONV_WARPS * 32, smem) != cudaSuccess || occ < 1)
+    occ = 1;
+  return (unsigned)std::min<int64_t>(ceil_div(a.N, CONV_WARPS), (int64_t)occ * sms);
+}
+
+#define FSC_CONV_LAUNCH_SMEM(KERNEL, SMEM, ...)                                                    \
+  do {                                                                                           \
+    if (a.N == 0) return FSC_OK;                                                                 \
+    if (a.work && cudaMemsetAsync(a.work, 0, sizeof(int), st) != cudaSuccess)                     \
+      return fail(FSC_ERR_CUDA, #KERNEL ": memset work counter");                                \
+    if (a.C == 32) {                                                                             \
+      cudaFuncSetAttribute(KERNEL<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(SMEM));  \
+      KERNEL<1><<<conv_blocks(KERNEL<1>, SMEM, a), CONV_WARPS * 32, SMEM, st>>>(__VA_ARGS__);     \
+    } else if (a.C == 64) {                                                                      \
+      cudaFuncSetAttribute(KERNEL<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(SMEM));  \
+      KERNEL<2><<<conv_blocks(KERNEL<2>, SMEM, a), CONV_WARPS * 32, SMEM, st>>>(__VA_ARGS__);     \
+    } else {                                                                                     \
+      return fail(FSC_ERR_UNSUPPORTED, "ictd conv kernels support channels 32 or 64");           \
+    }                                                                                            \
+    return check_launch(#KERNEL);                                                                \
   } while (0)
 
 int launch_conv2_z(const ConvArgs& a, const float* x, float* Z, cudaStream_t st) {

@@ -91,6 +91,8 @@ struct ConvArgs {
   int* err;
   const int32_t* tr_dst; // [E] receiver of edge tr_eid[t] (conv2_r)
   const float* invdeg;   // [N] 1 / max(in-degree, 1) (conv2_r)
+  int* work;             // conv2 z / r / q: node counter for dynamic scheduling (zeroed by the
+                         // launcher; null: one node per warp, one launch-wide grid)
 };
 
 // conv1: f1[n][k][c]
