@@ -629,11 +629,15 @@ __global__ void __launch_bounds__(256) fg_gather_kernel(FgArgs a) {
   }
 }
 
-// grads[layer][n][kc] += dFg[r(kc)][n]
+// grads[layer][n][kc] += dFg[r(kc)][n].  Both phases keep all of a thread's 16-byte loads in
+// flight: dFg rows as float4 of 4 nodes (8 lanes cover the block's 32 nodes of one row), the
+// gradient rows as float4 of 4 columns.
 template <int C>
-__global__ void __launch_bounds__(256) fg_scatter_add_kernel(FgArgs a) {
-  constexpr int W = 9 * C, W4 = W / 4, TS = W + 1, ROUND = 6;
-  constexpr int PER = FG_NODES * W4 / 256;
+__global__ void __launch_bounds__(256, 2) fg_scatter_add_kernel(FgArgs a) {
+  constexpr int W = 9 * C, W4 = W / 4, TS = W + 1;
+  constexpr int PER = FG_NODES * W4 / 256;  // float4 per thread in either phase
+  constexpr int RND = (PER + 1) / 2;        // loads in flight per round (two rounds: 2 CTAs per SM)
+  static_assert(FG_NODES == 32 && W % 32 == 0 && PER * 256 == FG_NODES * W4, "tile shape");
   extern __shared__ float tile[];
   int* sinv = reinterpret_cast<int*>(tile + FG_NODES * TS);
   const int layer = blockIdx.y, tid = threadIdx.x;
@@ -641,24 +645,38 @@ __global__ void __launch_bounds__(256) fg_scatter_add_kernel(FgArgs a) {
   for (int i = tid; i < W; i += 256) sinv[i] = a.xinv[(int64_t)layer * W + i];
   __syncthreads();
   {
-    const int nl = tid & (FG_NODES - 1);
-    const int64_t n = n0 + nl;
-    const float* fg = a.dFg + (n / TILE) * a.nrows * TILE + (n % TILE);
-#pragma unroll 8
-    for (int kc = tid >> 5; kc < W; kc += 8) tile[nl * TS + kc] = fg[(int64_t)sinv[kc] * TILE];
+    // rows of the padded operand exist for every node of the 128-node tile
+    const int g = tid & 7, rr = tid >> 3;
+    const float* fg = a.dFg + (n0 / TILE) * a.nrows * TILE + (n0 % TILE) + 4 * g;
+#pragma unroll
+    for (int j0 = 0; j0 < PER; j0 += RND) {
+      float4 v[RND];
+#pragma unroll
+      for (int j = 0; j < RND; ++j)
+        if (j0 + j < PER) v[j] = *reinterpret_cast<const float4*>(fg + (int64_t)sinv[rr + 32 * (j0 + j)] * TILE);
+#pragma unroll
+      for (int j = 0; j < RND; ++j) {
+        if (j0 + j >= PER) break;
+        float* t = tile + (4 * g) * TS + rr + 32 * (j0 + j);
+        t[0] = v[j].x;
+        t[TS] = v[j].y;
+        t[2 * TS] = v[j].z;
+        t[3 * TS] = v[j].w;
+      }
+    }
   }
   __syncthreads();
   float4* dst4 = reinterpret_cast<float4*>(a.grads[layer]);
 #pragma unroll
-  for (int j0 = 0; j0 < PER; j0 += ROUND) {
-    float4 g[ROUND];
+  for (int j0 = 0; j0 < PER; j0 += RND) {
+    float4 g[RND];
 #pragma unroll
-    for (int j = 0; j < ROUND; ++j) {
+    for (int j = 0; j < RND; ++j) {
       const int i = tid + 256 * (j0 + j), nl = i / W4, k4 = i - nl * W4;
       if (j0 + j < PER && n0 + nl < a.N) g[j] = dst4[(n0 + nl) * W4 + k4];
     }
 #pragma unroll
-    for (int j = 0; j < ROUND; ++j) {
+    for (int j = 0; j < RND; ++j) {
       const int i = tid + 256 * (j0 + j), nl = i / W4, k4 = i - nl * W4;
       if (j0 + j >= PER || n0 + nl >= a.N) continue;
       const float* t = tile + nl * TS + 4 * k4;
