@@ -17,6 +17,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -301,6 +302,242 @@ __global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_consta
   }
 }
 
+// ------------------------------------------------------------------ persistent, B resident
+// For short K and N <= 256 (the dZ channel mix and the MainNet layers here) the whole B image
+// fits in shared memory: one CTA per SM loads it once and walks row tiles.  Roles: producer warp (B once,
+// then A chunks by TMA into an NST-stage ring), 4 split warps (tf32 hi in place + lo), MMA warp,
+// 4 epilogue warps (thread = row = TMEM lane).  Two TMEM slots of 256 columns let tile i's
+// epilogue run under tile i + 1's loads and MMAs.  Within a slot, chunk group a (GC <= 2 chunks,
+// <= 24 MMAs) accumulates at column a * NT; the epilogue sums the groups in fp32.
+constexpr int TP_THREADS = 10 * 32;         // split 0-3, epilogue 4-7, producer 8, MMA 9
+constexpr uint32_t TP_BMAX = 128u * 1024u;  // B image bytes held in shared memory
+
+template <int NT>
+struct TpCfg {
+  static constexpr int NACC_MAX = 256 / NT;               // chunk groups per TMEM slot
+  static constexpr uint32_t BBYTES = 2u * KC * NT * 4u;   // one chunk's hi + lo planes
+  static constexpr uint32_t RING = 2u * ABYTES;           // one stage: A hi + A lo
+};
+
+struct TpShape {
+  int nchunks, nst, gc;
+  uint32_t b_off, bar_off, total;
+};
+
+template <int NT>
+__host__ __device__ inline TpShape tp_shape(int K) {
+  TpShape sh{};
+  sh.nchunks = (K + KC - 1) / KC;
+  const int nacc = sh.nchunks < TpCfg<NT>::NACC_MAX ? sh.nchunks : TpCfg<NT>::NACC_MAX;
+  sh.gc = (sh.nchunks + nacc - 1) / nacc;
+  const uint32_t bbytes = (uint32_t)sh.nchunks * TpCfg<NT>::BBYTES;
+  sh.nst = bbytes + 4u * TpCfg<NT>::RING <= 200u * 1024u ? 4 : 2;
+  sh.b_off = (uint32_t)sh.nst * TpCfg<NT>::RING;
+  sh.bar_off = sh.b_off + bbytes;
+  const uint32_t raw = sh.bar_off + 256u + 1024u;  // barriers, TMEM slot, 1024-byte alignment slack
+  sh.total = raw < 120u * 1024u ? 120u * 1024u : raw;  // one CTA per SM (512 TMEM columns)
+  return sh;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(TP_THREADS, 1) gemm_tcp_kernel(const __grid_constant__ CUtensorMap tmA, GemmTcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const TpShape sh = tp_shape<NT>(a.K);
+  const int NST = sh.nst, nchunks = sh.nchunks, GC = sh.gc;
+  uint8_t* sB = smem + sh.b_off;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + sh.bar_off);
+  uint64_t* full = bars;                 // [NST] A chunk landed
+  uint64_t* lo_ready = bars + 4;         // [NST] split done
+  uint64_t* empty = bars + 8;            // [NST] MMAs done with the stage
+  uint64_t* acc_full = bars + 12;        // [2] a tile's MMAs done
+  uint64_t* acc_empty = bars + 14;       // [2] epilogue done with the slot
+  uint64_t* b_full = bars + 16;          // B image landed
+  uint64_t* done = bars + 17;            // every MMA issued by this CTA completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t ntiles = (a.G + a.Gb - 1) / a.Gb;
+
+  if (warp == 9) {
+    tc::tmem_alloc(tmem_slot, 512);
+    tc::tmem_relinquish();
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NST; ++i) {
+      tc::mbar_init(full + i, 1);
+      tc::mbar_init(lo_ready + i, 4);
+      tc::mbar_init(empty + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(acc_full + i, 1);
+      tc::mbar_init(acc_empty + i, 4);
+    }
+    tc::mbar_init(b_full, 1);
+    tc::mbar_init(done, 1);
+    tc::fence_mbar_init();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp < 4) {
+    // ---------------- split A chunks into tf32 hi (in place) and lo
+    int64_t q = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      bool ok = true;
+      for (int c = 0; c < nchunks; ++c, ++q) {
+        const int st = (int)(q % NST);
+        if (!(ok = tc::mbar_wait(full + st, (uint32_t)((q / NST) & 1), a.err, 91))) break;
+        float4* pa = reinterpret_cast<float4*>(smem + st * TpCfg<NT>::RING);
+        float4* pl = reinterpret_cast<float4*>(smem + st * TpCfg<NT>::RING + ABYTES);
+#pragma unroll
+        for (int i = 0; i < (int)(ABYTES / 16) / MT; ++i) {
+          const int idx = threadIdx.x + MT * i;
+          const float4 v = pa[idx];
+          uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
+          tc::split_tf32(v.x, h0, l0);
+          tc::split_tf32(v.y, h1, l1);
+          tc::split_tf32(v.z, h2, l2);
+          tc::split_tf32(v.w, h3, l3);
+          pa[idx] = make_float4(__uint_as_float(h0), __uint_as_float(h1), __uint_as_float(h2), __uint_as_float(h3));
+          pl[idx] = make_float4(__uint_as_float(l0), __uint_as_float(l1), __uint_as_float(l2), __uint_as_float(l3));
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(lo_ready + st);
+      }
+      if (!ok) break;
+    }
+  } else if (warp < 8) {
+    // ---------------- epilogue: thread = tile row = TMEM lane
+    const int t = (warp - 4) * 32 + lane;
+    const uint32_t lane_off = (uint32_t)((warp - 4) * 32) << 16;
+    const int ngroups = (nchunks + GC - 1) / GC;
+    int64_t i = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++i) {
+      const int slot = (int)(i & 1);
+      if (!tc::mbar_wait(acc_full + slot, (uint32_t)((i >> 1) & 1), a.err, 92)) break;
+      tc::tc_fence_after();
+      const int64_t g = tile * a.Gb + t / a.R;
+      const int r = t % a.R;
+      const bool valid = t < a.R * a.Gb && g < a.G;
+      float scale = a.alpha != 0.f ? a.alpha : 1.f;
+      if (valid && a.deg_rowptr) {
+        const int d = a.deg_rowptr[g + 1] - a.deg_rowptr[g];
+        scale *= 1.f / (float)(d > 1 ? d : 1);
+      }
+      float* crow = valid ? a.C + g * a.c_gs + r * a.c_rs : nullptr;
+      const uint32_t tslot = tbase + (uint32_t)(slot * 256) + lane_off;
+#pragma unroll 1
+      for (int cb = 0; cb < NT / 16; ++cb) {
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[k] = 0.f;
+        for (int ga = 0; ga < ngroups; ++ga) {
+          uint32_t u[16];
+          tc::tmem_ld16(tslot + (uint32_t)(ga * NT) + 16u * cb, u);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int k = 0; k < 16; ++k) v[k] += __uint_as_float(u[k]);
+        }
+        const int nc = 16 * cb;
+        if (!crow || nc >= a.N) continue;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          v[k] *= scale;
+          if (a.bias && nc + k < a.N) v[k] += a.bias[nc + k];
+        }
+        float* cp = crow + nc;
+        if (nc + 16 <= a.N && (reinterpret_cast<uintptr_t>(cp) & 15) == 0) {
+          float4* c4 = reinterpret_cast<float4*>(cp);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            float4 o = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+            if (a.accumulate) {
+              const float4 pv = c4[k];
+              o.x += pv.x;
+              o.y += pv.y;
+              o.z += pv.z;
+              o.w += pv.w;
+            }
+            c4[k] = o;
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 16; ++k)
+            if (nc + k < a.N) cp[k] = a.accumulate ? cp[k] + v[k] : v[k];
+        }
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(acc_empty + slot);
+    }
+  } else if (warp == 8) {
+    // ---------------- producer
+    if (lane == 0) {
+      tc::mbar_arrive_expect_tx(b_full, (uint32_t)nchunks * TpCfg<NT>::BBYTES);
+      for (int c = 0; c < nchunks; ++c)
+        tc::bulk_g2s(sB + c * TpCfg<NT>::BBYTES, reinterpret_cast<const uint8_t*>(a.bimg) + (size_t)c * TpCfg<NT>::BBYTES,
+                     TpCfg<NT>::BBYTES, b_full);
+      int64_t q = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        for (int c = 0; c < nchunks; ++c, ++q) {
+          const int st = (int)(q % NST);
+          if (q >= NST && !(ok = tc::mbar_wait(empty + st, (uint32_t)(((q / NST) - 1) & 1), a.err, 93))) break;
+          tc::mbar_arrive_expect_tx(full + st, a.abox);
+          tma_load_3d(smem + st * TpCfg<NT>::RING, &tmA, c * KC, 0, (int)(tile * a.Gb), full + st);
+        }
+      }
+    }
+  } else {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_tf32(MT, NT);
+      const uint32_t s0 = tc::smem_u32(smem), b0 = tc::smem_u32(sB);
+      bool ok = tc::mbar_wait(b_full, 0, a.err, 94);
+      int64_t q = 0, i = 0;
+      for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++i) {
+        const int slot = (int)(i & 1);
+        if (i >= 2 && !(ok = tc::mbar_wait(acc_empty + slot, (uint32_t)(((i >> 1) - 1) & 1), a.err, 95))) break;
+        tc::tc_fence_after();
+        for (int c = 0; c < nchunks; ++c, ++q) {
+          const int st = (int)(q % NST);
+          if (!(ok = tc::mbar_wait(lo_ready + st, (uint32_t)((q / NST) & 1), a.err, 96))) break;
+          tc::tc_fence_after();
+          const uint32_t d = tbase + (uint32_t)(slot * 256 + (c / GC) * NT);
+          const bool first = c % GC == 0;
+          const uint32_t ah0 = s0 + st * TpCfg<NT>::RING, al0 = ah0 + ABYTES;
+#pragma unroll
+          for (int j = 0; j < KC / 8; ++j) {
+            const uint64_t ah = desc_sw128(ah0 + 32 * j);
+            const uint64_t al = desc_sw128(al0 + 32 * j);
+            const uint32_t bh_addr = b0 + c * TpCfg<NT>::BBYTES + j * 2 * 16 * NT;
+            const uint64_t bh = tc::smem_desc_kmajor(bh_addr, 16 * NT, 128);
+            const uint64_t bl = tc::smem_desc_kmajor(bh_addr + TpCfg<NT>::BBYTES / 2, 16 * NT, 128);
+            mma_tf32_ss(d, ah, bl, idesc, (!first || j > 0) ? 1u : 0u);
+            mma_tf32_ss(d, al, bh, idesc, 1u);
+            mma_tf32_ss(d, ah, bh, idesc, 1u);
+          }
+          tc::mma_commit(empty + st);
+        }
+        if (!ok) break;
+        tc::mma_commit(acc_full + slot);
+      }
+      tc::mma_commit(done);  // also when a wait failed: whatever was issued completes first
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    if (lane == 0) tc::mbar_wait(done, 0, a.err, 97);
+    __syncwarp();
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tbase, 512);
+  }
+}
+
 // B image: element (k, n) of B[k][n] (b_trans: B[n*ldb + k]) at
 //   [n / NT][k / KC][hi|lo][(k % KC) / 4][n % NT][k % 4], zero for n >= N or k >= K (K padded to
 //   whole chunks).
@@ -343,6 +580,35 @@ int launch_nt(const GemmArgs& g, const CUtensorMap& map, GemmTcArgs t, cudaStrea
   dim3 grid((unsigned)ceil_div(g.G, (int64_t)t.Gb), (unsigned)ceil_div(g.N, NT));
   gemm_tc_kernel<NT><<<grid, GT_THREADS, sm, st>>>(map, t);
   return check_launch("gemm_tc_kernel");
+}
+
+// The persistent kernel holds B (whole K) in shared memory and keeps every chunk group at <= 2
+// chunks within 256 TMEM columns.  It is used for K <= 128: with a longer K the resident B leaves
+// room for too few A stages to stream A (measured: the K = 192 / 256 channel mixes ran slower
+// than the two-CTA-per-SM kernel, the K = 64 / 128 dZ mix and MainNet layers faster).
+bool gemm_tcp_fits(int NT, int K) {
+  const int nchunks = (K + KC - 1) / KC;
+  const int nacc_max = 256 / NT;
+  return nchunks <= 4 && (uint32_t)nchunks * 2u * KC * NT * 4u <= TP_BMAX && (nchunks + nacc_max - 1) / nacc_max <= 2;
+}
+
+template <int NT>
+int launch_tp(const GemmArgs& g, const CUtensorMap& map, GemmTcArgs t, cudaStream_t st) {
+  const TpShape sh = tp_shape<NT>(g.K);
+  if (cudaFuncSetAttribute(gemm_tcp_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sh.total) !=
+      cudaSuccess)
+    return fail(FSC_ERR_CUDA, "gemm_tcp: cannot set shared memory size");
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  const int64_t ntiles = ceil_div(g.G, (int64_t)t.Gb);
+  const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sms);
+  gemm_tcp_kernel<NT><<<grid, TP_THREADS, sh.total, st>>>(map, t);
+  return check_launch("gemm_tcp_kernel");
 }
 
 }  // namespace
@@ -424,6 +690,14 @@ int launch_gemm_tc(const GemmArgs& g, const float* bimg, int* err, cudaStream_t 
                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (rc != CUDA_SUCCESS) return fail(FSC_ERR_CUDA, "cuTensorMapEncodeTiled failed for a GEMM operand");
+  if (g.N <= NT && gemm_tcp_fits(NT, g.K)) {
+    switch (NT) {
+      case 64: return launch_tp<64>(g, map, t, st);
+      case 128: return launch_tp<128>(g, map, t, st);
+      case 192: return launch_tp<192>(g, map, t, st);
+      default: return launch_tp<256>(g, map, t, st);
+    }
+  }
   switch (NT) {
     case 64: return launch_nt<64>(g, map, t, st);
     case 128: return launch_nt<128>(g, map, t, st);
