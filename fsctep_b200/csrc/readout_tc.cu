@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
 #pragma unroll
         for (int ci = 0; ci < 4; ++ci)
 #pragma unroll
-          for (int m = 0; m < M; ++m) tcv[ci][m] = pc[(ci * M + m) * TILE];
+          for (int m = 0; m < M; ++m) tcv[ci][m] = pc[(ci * M + m) * TILE] * scale;  // power of two: exact
       }
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(empty_C + rr % NSTC);
@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
 #pragma unroll
             for (int m = 0; m < M; ++m)
               g = __ffma2_rn(make_float2(tcv[ci][m], tcv[ci][m]), make_float2(tdv[2 * dp][m], tdv[2 * dp + 1][m]), g);
-            tc::split_f16x2(g.x * scale, g.y * scale, hi[2 * ci + dp], lo[2 * ci + dp]);
+            tc::split_f16x2(g.x, g.y, hi[2 * ci + dp], lo[2 * ci + dp]);
           }
         tc::tmem_st8(tA(st, 0) + lane_off + 8u * qq, hi);
         tc::tmem_st8(tA(st, 1) + lane_off + 8u * qq, lo);

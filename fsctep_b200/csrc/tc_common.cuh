@@ -191,10 +191,18 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
 // lo = fp16_rn(x - hi); returned packed as (x0 | x1 << 16) words, the element of lower K index in
 // the low half.  hi*hi + hi*lo + lo*hi carries ~22 significant bits, like the 3xTF32 split.
 __device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
-  const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
-  const __half l0 = __float2half_rn(x0 - __half2float(h0)), l1 = __float2half_rn(x1 - __half2float(h1));
-  hi = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-  lo = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+  // packed conversions (cvt.rn.f16x2.f32 puts its first source in the upper half): one cvt for
+  // both hi halves, the exact remainders x - hi by one packed FMA, one cvt for both lo halves
+  uint32_t h, l;
+  float f0, f1;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(x1), "f"(x0));
+  asm("{\n\t.reg .f16 a, b;\n\tmov.b32 {a, b}, %2;\n\tcvt.f32.f16 %0, a;\n\tcvt.f32.f16 %1, b;\n\t}"
+      : "=f"(f0), "=f"(f1)
+      : "r"(h));
+  const float2 r = __ffma2_rn(make_float2(f0, f1), make_float2(-1.f, -1.f), make_float2(x0, x1));
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(l) : "f"(r.y), "f"(r.x));
+  hi = h;
+  lo = l;
 }
 
 // Power-of-two factor that maps values bounded by `bound` (> 0) to at most 2^14 (fp16 keeps
