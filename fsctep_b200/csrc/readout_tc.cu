@@ -376,6 +376,10 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
   uint64_t* d_empty = bars + 11;  // [NSD2]
   uint64_t* a_ready = bars + 14;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  __shared__ float xch[4 * TILE * 10];  // row-end exchange of the epilogue quarters (2 c-rows x M <= 5)
+  __shared__ uint64_t xbar[2];
+  uint64_t* xfull = xbar;               // every epilogue warp wrote its exchange rows
+  uint64_t* xempty = xbar + 1;          // every epilogue warp read them
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nb = a.nC / 8, np = nb / 2;  // d-block pairs per row
@@ -401,6 +405,8 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
       tc::mbar_init(d_empty + i, NGEN_WARPS);
     }
     tc::mbar_init(a_ready, NGEN_WARPS);
+    tc::mbar_init(xfull, NGEN_WARPS);
+    tc::mbar_init(xempty, NGEN_WARPS);
     tc::fence_mbar_init();
   }
   tc::tc_fence_before();
@@ -441,17 +447,21 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
     tc::tc_fence_before();
     __syncwarp();
     if (lane == 0) tc::mbar_arrive(a_ready);
-    // epilogue over block pairs
+    // epilogue over block pairs: quarter qq = 2 dblk + cq2 contracts c-rows 4 cq2 .. 4 cq2 + 3
+    // with the 8 d-rows of d-block dblk of each pair (columns [32qq, 32qq + 32) of the pair's H:
+    // 4d + c % 4, see the image order); at the end of a row the two d-block halves are summed
+    // through shared memory and the thread writes c-rows 4 cq2 + 2 dblk, + 1.
+    const int dblk = qq >> 1, cq2 = qq & 1;
     float* dFt = a.dFg + (int64_t)blockIdx.x * a.nrows * TILE + row;
-    int s = 0;
+    int s = 0, xrow = 0;
     bool ok = true;
     auto epi_row = [&](auto mconst, int off, int cb) {
       constexpr int M = decltype(mconst)::value;
-      float acc[2][M];
+      float acc[4][M];
 #pragma unroll
-      for (int cq = 0; cq < 2; ++cq)
+      for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int m = 0; m < M; ++m) acc[cq][m] = 0.f;
+        for (int m = 0; m < M; ++m) acc[c][m] = 0.f;
       for (int dp = 0; dp < np; ++dp, ++s) {
         if (!ring_full(full_T, s, NSTT2, a.err, 20)) {
           ok = false;
@@ -463,23 +473,25 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
           return;
         }
         tc::tc_fence_after();
-        // H[c = 2qq + cq][d] of the pair's first / second d-block at columns 16qq + 8cq + dq / + 64
-        uint32_t hv[2][16];
-        tc::tmem_ld16(tD(st) + lane_off + 16u * qq, hv[0]);
-        tc::tmem_ld16(tD(st) + lane_off + 64u + 16u * qq, hv[1]);
-        const float* pt = sT + (s % NSTT2) * (TBYTES2 / 4) + row;
+        uint32_t hv[32];
+        tc::tmem_ld32(tD(st) + lane_off + 32u * qq, hv);
+        const float* pt = sT + (s % NSTT2) * (TBYTES2 / 4) + 8 * dblk * M * TILE + row;
 #pragma unroll
-        for (int dq = 0; dq < 16; ++dq) {
+        for (int d = 0; d < 8; ++d) {
           float td[M];
 #pragma unroll
-          for (int m = 0; m < M; ++m) td[m] = pt[(dq * M + m) * TILE];
-          if (dq == 0) tc::tmem_wait_ld();
-          const float2 h2 = make_float2(__uint_as_float(hv[dq >> 3][dq & 7]), __uint_as_float(hv[dq >> 3][8 + (dq & 7)]));
+          for (int m = 0; m < M; ++m) td[m] = pt[(d * M + m) * TILE];
+          if (d == 0) tc::tmem_wait_ld();
 #pragma unroll
-          for (int m = 0; m < M; ++m) {
-            const float2 t2 = __ffma2_rn(h2, make_float2(td[m], td[m]), make_float2(acc[0][m], acc[1][m]));
-            acc[0][m] = t2.x;
-            acc[1][m] = t2.y;
+          for (int cp = 0; cp < 2; ++cp) {
+            const float2 h2 = make_float2(__uint_as_float(hv[4 * d + 2 * cp]), __uint_as_float(hv[4 * d + 2 * cp + 1]));
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+              const float2 t2 =
+                  __ffma2_rn(h2, make_float2(td[m], td[m]), make_float2(acc[2 * cp][m], acc[2 * cp + 1][m]));
+              acc[2 * cp][m] = t2.x;
+              acc[2 * cp + 1][m] = t2.y;
+            }
           }
         }
         tc::tc_fence_before();
@@ -489,11 +501,32 @@ __global__ void __launch_bounds__(THREADS, 1) readout_bwd_tc_kernel(ReadoutTcArg
           tc::mbar_arrive(empty_T + s % NSTT2);
         }
       }
-      float* pd = dFt + (int64_t)(off + (8 * cb + 2 * qq) * M) * TILE;
+      // hand the partner quarter (other d-block, same c-rows) the two c-rows it writes; the
+      // exchange rows are reused row after row (bounded mbarrier waits, no block barrier)
+      if (xrow > 0 && !tc::mbar_wait(xempty, (uint32_t)((xrow - 1) & 1), a.err, 27)) {
+        ok = false;
+        return;
+      }
+      float* xs = xch + (qq * TILE + row) * 10;
 #pragma unroll
-      for (int cq = 0; cq < 2; ++cq)
+      for (int j = 0; j < 2; ++j)
 #pragma unroll
-        for (int m = 0; m < M; ++m) pd[(cq * M + m) * TILE] = unscale * acc[cq][m];
+        for (int m = 0; m < M; ++m) xs[j * M + m] = dblk ? acc[j][m] : acc[2 + j][m];
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(xfull);
+      if (!tc::mbar_wait(xfull, (uint32_t)(xrow & 1), a.err, 28)) {
+        ok = false;
+        return;
+      }
+      const float* xr = xch + (((1 - dblk) * 2 + cq2) * TILE + row) * 10;
+      float* pd = dFt + (int64_t)(off + (8 * cb + 4 * cq2 + 2 * dblk) * M) * TILE;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int m = 0; m < M; ++m) pd[(j * M + m) * TILE] = unscale * ((dblk ? acc[2 + j][m] : acc[j][m]) + xr[j * M + m]);
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(xempty);
+      ++xrow;
     };
     const RowOrder order(a.ngram, nb);
     for (int i = 0; i < order.rows && ok; ++i) {

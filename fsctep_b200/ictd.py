@@ -153,8 +153,11 @@ def readout_images(W_read, C: int, nint: int, ls=(0, 1, 2)):
         f = f.reshape(-1, S, 2, 4, 2, 4).permute(0, 1, 4, 2, 3, 5).reshape(-1, S, 64)
         fwd.append(f.reshape(-1, S, 8, 8).permute(0, 2, 1, 3))
         # backward: all blocks in pairs of d-blocks (db even, db + 1) -> N = 128 pairs per MMA,
-        # B = [o/8][pair of the two blocks][o%8], K = outputs o
-        b = blk.reshape(nb, nb // 2, 2, S, 64).permute(0, 1, 3, 2, 4).reshape(nb * nb // 2, S, 128)
+        # B = [o/8][pair of the two blocks][o%8], K = outputs o; within a block the pairs are
+        # ordered (c/4, d, c%4): epilogue quarter (d-block of the pair, c/4) reads its 32 columns
+        # at once, c-rows c, c + 1 side by side
+        bo = blk.reshape(nb, nb, S, 2, 4, 8).permute(0, 1, 2, 3, 5, 4).reshape(nb, nb, S, 64)
+        b = bo.reshape(nb, nb // 2, 2, S, 64).permute(0, 1, 3, 2, 4).reshape(nb * nb // 2, S, 128)
         bwd.append(b.reshape(-1, S // 8, 8, 128).permute(0, 1, 3, 2))
     return f16_image(torch.cat(fwd)), f16_image(torch.cat(bwd))
 

@@ -223,9 +223,10 @@ typedef struct {
    * 1/s, s = the power of two bringing max |W| in the image to <= 2^14; then per block the fp16
    * hi plane and lo plane of s*W (hi = fp16(s w), lo = fp16(s w - hi)).  nb = nC/8,
    * pair = (c - 8cb, d - 8db), Ws = (W_read.l + W_read.l^T)/2/sqrt(2l+1):
-   *   wimg_fwd: for l, cb <= db:  [k/8][o][k%8], K = 64 pairs ordered (d/2, c, d%2), Ws x2 off
-   *             the diagonal block
-   *   wimg_bwd: for l, cb, db pairs (db even, db+1):  [o/8][n][o%8], n = 64 (db odd) + 8c + d  */
+   *   wimg_fwd: for l, cb <= db:  [k/8][o][k%8], K = 64 pairs ordered (d/4, c/4, c%4, d%4), Ws x2
+   *             off the diagonal block
+   *   wimg_bwd: for l, cb, db pairs (db even, db+1):  [o/8][n][o%8],
+   *             n = 64 (db odd) + 32 (c/4) + 4d + c%4                                           */
   const float* wimg_fwd; /* header + [3*nb*(nb+1)/2][2][8][S][8] fp16                         */
   const float* wimg_bwd; /* header + [3*nb*nb/2][2][S/8][128][8] fp16                         */
   const float* mn_in_g;  /* [D0]  proj_total.input_norm.weight, D0 = 3*nC + S             */
