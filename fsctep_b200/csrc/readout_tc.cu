@@ -182,9 +182,9 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
     const int row = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const bool has_cols = 16 * qq < S;  // this warp owns output columns [16qq, 16qq+16)
-    float acc[16];
+    float2 acc[8];                      // columns 2i, 2i + 1
 #pragma unroll
-    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+    for (int i = 0; i < 8; ++i) acc[i] = make_float2(0.f, 0.f);
     bool ok = true;
     int s = 0, rr = 0;
     const int64_t n = n0 + row;
@@ -204,7 +204,9 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
         tc::tmem_ld16(tD(dst) + lane_off + 16u * qq, v);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] = fmaf(__uint_as_float(v[i]), inv, acc[i]);
+        for (int i = 0; i < 8; ++i)
+          acc[i] = __ffma2_rn(make_float2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])), make_float2(inv, inv),
+                              acc[i]);
       }
       tc::tc_fence_before();
       __syncwarp();
@@ -225,13 +227,16 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
         ok = false;
         return;
       }
-      float tcv[4][M];
+      float2 tcv[4][M];  // (t, t): the packed Gram FMA's broadcast operand, ready for the whole row
       {
         const float* pc = sC + (rr % NSTC) * (TBYTES / 4) + 4 * (qq & 1) * M * TILE + row;
 #pragma unroll
         for (int ci = 0; ci < 4; ++ci)
 #pragma unroll
-          for (int m = 0; m < M; ++m) tcv[ci][m] = pc[(ci * M + m) * TILE] * scale;  // power of two: exact
+          for (int m = 0; m < M; ++m) {
+            const float t = pc[(ci * M + m) * TILE] * scale;  // power of two: exact
+            tcv[ci][m] = make_float2(t, t);
+          }
       }
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(empty_C + rr % NSTC);
@@ -264,7 +269,7 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
             float2 g = make_float2(0.f, 0.f);
 #pragma unroll
             for (int m = 0; m < M; ++m)
-              g = __ffma2_rn(make_float2(tcv[ci][m], tcv[ci][m]), make_float2(tdv[2 * dp][m], tdv[2 * dp + 1][m]), g);
+              g = __ffma2_rn(tcv[ci][m], make_float2(tdv[2 * dp][m], tdv[2 * dp + 1][m]), g);
             tc::split_f16x2(g.x, g.y, hi[2 * ci + dp], lo[2 * ci + dp]);
           }
         tc::tmem_st8(tA(st, 0) + lane_off + 8u * qq, hi);
@@ -293,7 +298,7 @@ __global__ void __launch_bounds__(THREADS, 1) readout_fwd_tc_kernel(ReadoutTcArg
     if (ok && has_cols && n < a.N) {
       float4* out = reinterpret_cast<float4*>(a.scalars + n * S + 16 * qq);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) out[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+      for (int i = 0; i < 4; ++i) out[i] = make_float4(acc[2 * i].x, acc[2 * i].y, acc[2 * i + 1].x, acc[2 * i + 1].y);
     }
   } else if (warp == NGEN_WARPS) {
     // ---------------- MMA issuer
