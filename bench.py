@@ -137,10 +137,19 @@ def algorithmic_work(stage, N, E, cfg):
     return table.get(stage)
 
 
-# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per node of one launch, from the ncu
-# capture of the si64k workload summarised in profiles/readout_tc_si64k.md (0.524 GB + 50 MB and
-# 1.905 GB + 466 MB for 64,000 nodes); the traffic grows with the node count (per-tile operands).
-TRAFFIC_PER_NODE = {"readout_gram_forward": 0.574e9 / 64000, "readout_gram_backward": 2.371e9 / 64000}
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per node of one launch of the
+# stage's kernel, from the ncu captures of the si64k workload (64,000 nodes, 1,792,016 edges)
+# kept as text summaries under profiles/; every term grows with the node (and edge) count, so a
+# launch on another workload is scaled by its nodes.
+TRAFFIC_PER_NODE = {
+    "readout_gram_forward": (0.528e9 + 0.051e9) / 64000,
+    "readout_gram_backward": (1.697e9 + 0.466e9) / 64000,
+    "conv2_edge_forward": (0.339e9 + 0.528e9) / 64000,
+    "conv2_edge_backward_gates": (1.011e9 + 0.164e9) / 64000,
+    "conv2_edge_backward_x": (0.357e9 + 0.531e9) / 64000,
+    "edge_forward": (0.255e9 + 0.210e9) / 64000,
+    "edge_backward": (0.662e9 + 0.062e9) / 64000,
+}
 
 
 def run_native(args, rank, world, device):
@@ -355,7 +364,7 @@ def main():
                       "algorithmic_tflops": ach}
             if dom.startswith("conv2_edge"):
                 # CUDA-core tensor-product kernels: reported against HBM (their inputs are L2-resident
-                # re-reads; the FP32 pipe is the real limit, see profiles/conv2_si64k.md)
+                # re-reads; the FP32 pipe and L1/shared-memory throughput are the real limits)
                 roofline = dict(common, bound="hbm", achieved=hbm, peak=pk["hbm_gbs"], unit="GB/s",
                                 frac=hbm / pk["hbm_gbs"], peak_source=pk["source"] + " HBM copy")
             else:
