@@ -7,7 +7,7 @@
 //  * producer warp: per K-chunk of 32, one 3-D TMA load of the A tile (dims K, R, G: the two-level
 //    row addressing needs no copy; 128-byte swizzle, so each row is one swizzle row) and one bulk
 //    copy of the B chunk from a pre-formatted image, into a shared-memory ring;
-//  * 4 math warps: split the staged A in place into tf32 hi (top 19 bits) and write lo =
+//  * 4 math warps: split the staged A in place into tf32 hi = round_tf32(a) and write lo =
 //    round_tf32(a - hi) to a second buffer of the same layout (elementwise, so the swizzle needs
 //    no decoding); after the last chunk they read the accumulators and write C;
 //  * MMA warp: per chunk 4 K-steps x (hi*hi, hi*lo, lo*hi) kind::tf32 MMAs (A and B from shared

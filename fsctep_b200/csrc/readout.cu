@@ -5,6 +5,8 @@
 // with the features of all layers concatenated along channels (c' = layer*C + c).
 // The Gram contraction runs as  packed Gram (this file) x symmetrised W_read (GEMM); its
 // backward as  H = dscalars x W_sym (GEMM) then dt = 2 H t (this file).
+#include <algorithm>
+
 #include "common.cuh"
 #include "ictd_paths.cuh"
 #include "kernels.cuh"
@@ -126,64 +128,65 @@ __global__ void heads_finalize_kernel(const double* __restrict__ acc, int nheads
 
 // MainNet input [0e | scalars | (o3: zero 1e) | 1 | 2] (product_5 of the concatenated per-layer
 // features, pure_cartesian_ictd_layers_o3.py:1046-1057 for o3).
-__global__ void p5_forward_kernel(ReadoutArgs a, const float* __restrict__ scalars, float* __restrict__ p5) {
+__global__ void __launch_bounds__(128) p5_forward_kernel(ReadoutArgs a, const float* __restrict__ scalars,
+                                                         float* __restrict__ p5) {
   const int nC = a.C * a.nint;
   const int z = a.o3 ? nC : 0;
   const int D0 = 3 * nC + a.S + z;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= a.N * D0) return;
-  const int64_t n = idx / D0;
-  const int j = (int)(idx - n * D0);
   const float* f = a.tables + ictd2::TAB_P5;
-  float v;
-  if (j < nC) {
-    int c;
-    const float* r = feat_row(a, n, 0, j, c);
-    v = f[0] * r[c] * r[c];
-  } else if (j < nC + a.S) {
-    const float s = scalars[n * a.S + (j - nC)];
-    v = f[0] * s * s;
-  } else if (j < nC + a.S + z) {
-    v = 0.f;
-  } else {
-    const int l = j < 2 * nC + a.S + z ? 1 : 2;
-    const int cp = j - (nC + a.S + z) - (l - 1) * nC;
-    const int k = cp / a.C, c = cp - k * a.C;
-    const float* r = a.feats[k] + (n * NK + KB(l)) * a.C + c;
-    float acc = 0.f;
-    for (int m = 0; m < 2 * l + 1; ++m) acc = fmaf(r[m * a.C], r[m * a.C], acc);
-    v = f[l] * acc;
+  for (int64_t n = blockIdx.x; n < a.N; n += gridDim.x) {  // one node per CTA pass: no index division
+    for (int j = threadIdx.x; j < D0; j += blockDim.x) {
+      float v;
+      if (j < nC) {
+        int c;
+        const float* r = feat_row(a, n, 0, j, c);
+        v = f[0] * r[c] * r[c];
+      } else if (j < nC + a.S) {
+        const float s = scalars[n * a.S + (j - nC)];
+        v = f[0] * s * s;
+      } else if (j < nC + a.S + z) {
+        v = 0.f;
+      } else {
+        const int l = j < 2 * nC + a.S + z ? 1 : 2;
+        const int cp = j - (nC + a.S + z) - (l - 1) * nC;
+        const int k = cp / a.C, c = cp - k * a.C;
+        const float* r = a.feats[k] + (n * NK + KB(l)) * a.C + c;
+        float acc = 0.f;
+        for (int m = 0; m < 2 * l + 1; ++m) acc = fmaf(r[m * a.C], r[m * a.C], acc);
+        v = f[l] * acc;
+      }
+      p5[n * D0 + j] = v;
+    }
   }
-  p5[idx] = v;
 }
 
-__global__ void p5_backward_kernel(ReadoutArgs a, GradPtrs g, const float* __restrict__ scalars,
-                                   const float* __restrict__ dp5, float* __restrict__ dscalars) {
+__global__ void __launch_bounds__(128) p5_backward_kernel(ReadoutArgs a, GradPtrs g, const float* __restrict__ scalars,
+                                                          const float* __restrict__ dp5, float* __restrict__ dscalars) {
   const int nC = a.C * a.nint;
   const int z = a.o3 ? nC : 0;
   const int D0 = 3 * nC + a.S + z;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= a.N * D0) return;
-  const int64_t n = idx / D0;
-  const int j = (int)(idx - n * D0);
   const float* f = a.tables + ictd2::TAB_P5;
-  const float d = dp5[idx];
-  if (j < nC) {
-    const int k = j / a.C, c = j - k * a.C;
-    const int64_t off = (n * NK) * a.C + c;
-    g.p[k][off] = 2.f * f[0] * a.feats[k][off] * d;
-  } else if (j < nC + a.S) {
-    const int o = j - nC;
-    dscalars[n * a.S + o] = 2.f * f[0] * scalars[n * a.S + o] * d;
-  } else if (j < nC + a.S + z) {
-    // zero 1e slot: no input depends on it
-  } else {
-    const int l = j < 2 * nC + a.S + z ? 1 : 2;
-    const int cp = j - (nC + a.S + z) - (l - 1) * nC;
-    const int k = cp / a.C, c = cp - k * a.C;
-    for (int m = 0; m < 2 * l + 1; ++m) {
-      const int64_t off = (n * NK + KB(l) + m) * a.C + c;
-      g.p[k][off] = 2.f * f[l] * a.feats[k][off] * d;
+  for (int64_t n = blockIdx.x; n < a.N; n += gridDim.x) {  // one node per CTA pass: no index division
+    for (int j = threadIdx.x; j < D0; j += blockDim.x) {
+      const float d = dp5[n * D0 + j];
+      if (j < nC) {
+        const int k = j / a.C, c = j - k * a.C;
+        const int64_t off = (n * NK) * a.C + c;
+        g.p[k][off] = 2.f * f[0] * a.feats[k][off] * d;
+      } else if (j < nC + a.S) {
+        const int o = j - nC;
+        dscalars[n * a.S + o] = 2.f * f[0] * scalars[n * a.S + o] * d;
+      } else if (j < nC + a.S + z) {
+        // zero 1e slot: no input depends on it
+      } else {
+        const int l = j < 2 * nC + a.S + z ? 1 : 2;
+        const int cp = j - (nC + a.S + z) - (l - 1) * nC;
+        const int k = cp / a.C, c = cp - k * a.C;
+        for (int m = 0; m < 2 * l + 1; ++m) {
+          const int64_t off = (n * NK + KB(l) + m) * a.C + c;
+          g.p[k][off] = 2.f * f[l] * a.feats[k][off] * d;
+        }
+      }
     }
   }
 }
@@ -313,7 +316,7 @@ int launch_gram_apply(const ReadoutArgs& a, int l, int64_t n0, int64_t nn, const
 int launch_p5_forward(const ReadoutArgs& a, const float* scalars, float* p5, cudaStream_t st) {
   const int64_t total = a.N * ((a.o3 ? 4 : 3) * a.C * a.nint + a.S);
   if (total == 0) return FSC_OK;
-  p5_forward_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(a, scalars, p5);
+  p5_forward_kernel<<<(unsigned)std::min<int64_t>(a.N, 1 << 20), 128, 0, st>>>(a, scalars, p5);
   return check_launch("p5_forward_kernel");
 }
 
@@ -321,7 +324,7 @@ int launch_p5_backward(const ReadoutArgs& a, const float* scalars, const float* 
                        float* dscalars, cudaStream_t st) {
   const int64_t total = a.N * ((a.o3 ? 4 : 3) * a.C * a.nint + a.S);
   if (total == 0) return FSC_OK;
-  p5_backward_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(a, to_ptrs(grads, a.nint), scalars, dp5,
+  p5_backward_kernel<<<(unsigned)std::min<int64_t>(a.N, 1 << 20), 128, 0, st>>>(a, to_ptrs(grads, a.nint), scalars, dp5,
                                                                        dscalars);
   return check_launch("p5_backward_kernel");
 }
