@@ -34,8 +34,15 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 WORKLOADS = {
-    "si1m": dict(cells=(50, 50, 50), channels=64, num_interaction=3, Z=14, max_atomvalue=16),
-    "si64k": dict(cells=(20, 20, 20), channels=64, num_interaction=3, Z=14, max_atomvalue=16),
+    "si1m": dict(model="ictd", cells=(50, 50, 50), channels=64, num_interaction=3, Z=14, max_atomvalue=16),
+    "si64k": dict(model="ictd", cells=(20, 20, 20), channels=64, num_interaction=3, Z=14, max_atomvalue=16),
+    # pure-cartesian-sparse (one GPU): config 2 in full, and config 5's model on FCC crystals
+    "water3k": dict(model="sparse", system="water", n_side=10, box=31.0, channels=64, lmax=2, num_interaction=3,
+                    max_atomvalue=10, cpu_n_side=4),
+    "fcc32k": dict(model="sparse", system="fcc", cells=(20, 20, 20), channels=128, lmax=3, num_interaction=3,
+                   max_atomvalue=30, cpu_cells=(2, 2, 2)),
+    "fcc250k": dict(model="sparse", system="fcc", cells=(50, 50, 25), channels=128, lmax=3, num_interaction=3,
+                    max_atomvalue=30, cpu_cells=(2, 2, 2)),
 }
 CPU_SAMPLE_CELLS = (6, 6, 6)  # 1,728-atom replica of the same crystal for the CPU baseline
 
@@ -117,8 +124,45 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def sparse_cfg(w):
+    from fsctep_b200.sparse import SparseConfig
+
+    return SparseConfig(channels=w["channels"], lmax=w["lmax"], num_interaction=w["num_interaction"],
+                        number_of_basis=8, max_radius=5.0, function_type="gaussian", max_atomvalue=w["max_atomvalue"])
+
+
+def sparse_weights(cfg, seed=2024):
+    """Seeded weights in the reference state_dict layout of PureCartesianSparseTransformerLayer."""
+    from fsctep_b200.models import PureCartesianSparseTransformerLayer
+    from fsctep_b200.weights import seeded_state_dict
+
+    with torch.device("meta"):
+        m = PureCartesianSparseTransformerLayer(
+            max_embed_radius=cfg.max_radius, main_max_radius=cfg.max_radius, main_number_of_basis=cfg.number_of_basis,
+            hidden_dim_conv=cfg.channels, lmax=cfg.lmax, num_interaction=cfg.num_interaction,
+            function_type_main=cfg.function_type, max_atomvalue=cfg.max_atomvalue)
+    return seeded_state_dict({k: tuple(v.shape) for k, v in m.state_dict().items()}, seed)
+
+
+def sparse_system(w, seed=1000, cpu=False):
+    from fsctep_b200 import systems
+
+    if w["system"] == "water":
+        n_side = w["cpu_n_side"] if cpu else w["n_side"]
+        return systems.water_box(n_side=n_side, box=w["box"] * n_side / w["n_side"], seed=seed)
+    return systems.fcc_crystal(n_cells=w["cpu_cells"] if cpu else w["cells"], seed=seed)
+
+
+def sparse_comps(lmax):
+    from fsctep_b200.sparse import sparse_paths
+
+    return sum(3 ** Lo for (_, _, Lo) in sparse_paths(lmax))
+
+
 def algorithmic_work(stage, N, E, cfg):
     """(flops, bytes) per launch of a stage, from the per-unit figures of the hot path."""
+    if stage.startswith("sparse_"):
+        return sparse_work(stage, N, E, cfg)
     C, nint = cfg.channels, cfg.num_interaction
     nC = C * nint
     S = (nint - 1) * cfg.invariant_channels
@@ -133,6 +177,20 @@ def algorithmic_work(stage, N, E, cfg):
         "conv2_edge_backward_x": (2.0 * E * C * 115, N * 9 * C * 4.0 + N * 35 * C * 4.0 + E * 100.0),
         "edge_forward": (E * nint * 2.0 * (8 * 64 + 64 * 64 + 64 * 11), E * (12 + 48 + nint * 48.0)),
         "edge_backward": (E * nint * 4.0 * (8 * 64 + 64 * 64 + 64 * 11), E * (48 + 48 + nint * 48.0 + 12)),
+    }
+    return table.get(stage)
+
+
+def sparse_work(stage, N, E, cfg):
+    """(flops, bytes) per layer of a pure-cartesian-sparse stage.  Per edge and output component
+    the aggregation costs 65 x C multiply-adds (radial hidden row + bias times the sender channels);
+    fc.4 is one GEMM per node after the aggregation (65 x C x C per output component)."""
+    C, J, K3 = cfg.channels, 65, sparse_comps(cfg.lmax)
+    R = sum(3 ** L for L in range(cfg.lmax + 1))
+    feat = N * R * C * 4.0
+    table = {
+        "sparse_conv2_forward": (2.0 * E * J * C * K3 + 2.0 * N * K3 * J * C * C, 2 * feat + E * (64 * 4.0 + 16)),
+        "sparse_conv2_backward": (4.0 * E * J * C * K3 + 2.0 * N * K3 * J * C * C, 3 * feat + E * (2 * 64 * 4.0 + 16)),
     }
     return table.get(stage)
 
@@ -257,6 +315,108 @@ def run_native(args, rank, world, device):
                 ghosts=info["ghosts"], dims=dims)
 
 
+def run_sparse(args, device):
+    """One GPU: pure-cartesian-sparse energy + forces (+ virial) of a seeded crystal or water box."""
+    from fsctep_b200 import _native as NAT
+    from fsctep_b200.neighbors import build_graph
+    from fsctep_b200.sparse import SparseEngine
+
+    w = WORKLOADS[args.workload]
+    cfg = sparse_cfg(w)
+    eng = SparseEngine(sparse_weights(cfg), cfg, device)
+    sysd = sparse_system(w)
+    n = sysd["pos"].shape[0]
+    pos_d = torch.tensor(sysd["pos"], device=device)
+    cell_d = torch.tensor(sysd["cell"], device=device)
+    Z = torch.tensor(sysd["Z"], device=device, dtype=torch.int32)
+    batch = torch.zeros(n, device=device, dtype=torch.int32)
+    pos_h = torch.tensor(sysd["pos"]).pin_memory()
+    forces_h = torch.empty(n, 3, dtype=torch.float32).pin_memory()
+    energy_h = torch.empty(1, dtype=torch.float32).pin_memory()
+    info = {}
+
+    def step(pos, cell):
+        g = build_graph(pos, cell, cfg.max_radius)
+        energy, _ = eng.forward(pos, Z, batch, cell, g)
+        out = eng.backward(want_virial=True)
+        info["edges"] = g.num_edges
+        return energy, out["forces"]
+
+    def e2e_step():
+        energy, forces = step(pos_h.to(device, non_blocking=True), cell_d)
+        forces_h.copy_(forces, non_blocking=True)
+        energy_h.copy_(energy, non_blocking=True)
+
+    for _ in range(args.warmup):
+        step(pos_d, cell_d)
+    torch.cuda.synchronize()
+    if eng.status() != 0:
+        raise RuntimeError(f"sparse engine status {eng.status()}")
+    ours = None
+    if not args.no_launch_count:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step(pos_d, cell_d)
+            torch.cuda.synchronize()
+        ours = sum(e.count for e in prof.key_averages() if "fsc::" in e.key or "cub::" in e.key)
+    torch.cuda.synchronize()
+    NAT.profile_enable(True)
+    stage_ms = {}
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        t0.record()
+        for _ in range(args.steps):
+            step(pos_d, cell_d)
+            for name, ms in NAT.profile_read():
+                stage_ms.setdefault(name, []).append(ms)
+        t1.record()
+        torch.cuda.synchronize()
+    NAT.profile_enable(False)
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    return dict(n=n, E=info["edges"], ms_step=t0.elapsed_time(t1) / args.steps, ms_e2e=e0.elapsed_time(e1) / args.steps,
+                stage_ms=stage_ms, clocks=clk.summary(), launches=None if ours is None else ours * args.steps,
+                cfg=cfg, ghosts=0, dims=(1, 1, 1))
+
+
+def cpu_reference_sparse(w, steps, warmup):
+    """Time the oracle port of the reference sparse CPU path on a small replica of the workload."""
+    from oracle import neighbors as ON
+    from oracle import sparse_model as OS
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = sparse_cfg(w)
+    sd = {k: v.float() for k, v in sparse_weights(cfg).items()}
+    sysd = sparse_system(w, cpu=True)
+    src, dst, S = ON.neighbor_list(sysd["pos"], sysd["cell"][0], 5.0)
+    args = (torch.tensor(sysd["pos"], dtype=torch.float32), torch.tensor(sysd["Z"]), torch.tensor(sysd["batch"]),
+            torch.tensor(src), torch.tensor(dst), torch.tensor(S, dtype=torch.float32),
+            torch.tensor(sysd["cell"], dtype=torch.float32))
+    for _ in range(warmup):
+        OS.sparse_energy_forces_stress(sd, cfg, *args, want_stress=True)
+    times = []
+    for _ in range(steps):
+        t = time.perf_counter()
+        OS.sparse_energy_forces_stress(sd, cfg, *args, want_stress=True)
+        times.append(time.perf_counter() - t)
+    n = sysd["pos"].shape[0]
+    med = float(np.median(times))
+    return {"value": n / med, "unit": "atom-steps/s", "cores": threads, "kind": "port",
+            "sample": f"{n}-atom replica ({len(src)} edges) of the same model and system kind, fp32 PyTorch eager "
+                      f"(oracle port of the reference CPU path: per-edge fc.4 weights materialised), energy + forces "
+                      f"+ stress, median of {steps} steps after {warmup} warm-up, neighbour list excluded",
+            "seconds_per_step": med}
+
+
 def cpu_reference(steps, warmup, budget_s=None):
     """Time the oracle port of the reference CPU path on a bounded replica of the workload."""
     from fsctep_b200 import systems
@@ -309,7 +469,10 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     metric = "atom-steps/s (E+F)"
     w = WORKLOADS[args.workload]
-    n_atoms = int(np.prod(w["cells"])) * 8
+    sparse = w["model"] == "sparse"
+    if sparse and (world > 1 or args.gpus > 1):
+        raise SystemExit(f"--workload {args.workload}: the pure-cartesian-sparse workloads run on one GPU")
+    n_atoms = int(np.prod(w["cells"])) * 8 if not sparse else None
     config = {"workload": f"{args.workload}: pure-cartesian-ictd diamond Si {n_atoms} atoms (config 4)",
               "model": "pure-cartesian-ictd", "channels": w["channels"], "num_interaction": w["num_interaction"],
               "lmax": 2, "cutoff": 5.0, "radial_basis": "gaussian x8", "atoms_per_gpu": n_atoms,
@@ -319,11 +482,31 @@ def main():
                                 "exchange per step (NCCL all_to_all), energy all_reduce") if args.gpus > 1 else None,
               "step": "neighbour list + forward + backward (energy, forces)",
               "l2": "inputs larger than L2 (features 2.3 GB per layer at 1M atoms)"}
+    if sparse:
+        if w["system"] == "water":
+            n_atoms = 3 * w["n_side"] ** 3
+            what = (f"liquid-water-like box of {n_atoms // 3} H2O ({n_atoms} atoms) in a {w['box']} A cube, "
+                    "O on a jittered grid (sigma 0.3 A), O-H 0.96 A, HOH 104.5 deg, random orientations (config 2)")
+        else:
+            n_atoms = 4 * int(np.prod(w["cells"]))
+            what = (f"FCC metal-like crystal, a = 3.61 A, sigma = 0.1 A, single species, {n_atoms} atoms "
+                    + ("(config 5's 250,000 atoms per GPU)" if n_atoms == 250000 else
+                       "(config 5's model and lattice; the 250,000-atom per-GPU crystal is --workload fcc250k)"))
+        config = {"workload": f"{args.workload}: pure-cartesian-sparse {what}", "model": "pure-cartesian-sparse",
+                  "channels": w["channels"], "num_interaction": w["num_interaction"], "lmax": w["lmax"],
+                  "max_rank_other": 1, "k_policy": "k0", "cutoff": 5.0, "radial_basis": "gaussian x8",
+                  "atoms_per_gpu": n_atoms, "parallelism": "single", "decomposition": None,
+                  "step": "neighbour list + forward + backward (energy, forces, virial)",
+                  "l2": "inputs smaller than L2 for water3k (re-read from L2 between steps); "
+                        "per-layer aggregation buffers larger than L2 for the FCC workloads"}
 
     if args.impl == "reference":
         if rank != 0:
             return
-        r = cpu_reference(max(1, args.steps), max(0, min(args.warmup, 1)))
+        if sparse:
+            r = cpu_reference_sparse(w, max(1, min(args.steps, 3)), max(0, min(args.warmup, 1)))
+        else:
+            r = cpu_reference(max(1, args.steps), max(0, min(args.warmup, 1)))
         line = {"metric": metric, "value": r["value"], "unit": "atom-steps/s", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["seconds_per_step"] * 1e3,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -338,7 +521,7 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300))
     device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(device)
-    res = run_native(args, rank, world, device)
+    res = run_sparse(args, device) if sparse else run_native(args, rank, world, device)
     n, E = res["n"], res["E"]
     value = n * world / (res["ms_step"] / 1e3)
     e2e_value = n * world / (res["ms_e2e"] / 1e3)
@@ -362,7 +545,7 @@ def main():
                       "traffic_source": "ncu si64k capture scaled by nodes" if tpn is not None else None,
                       "avg_launch_ms": avg_launch_ms, "algorithmic_bytes_per_launch": nbytes,
                       "algorithmic_tflops": ach}
-            if dom.startswith("conv2_edge"):
+            if dom.startswith("conv2_edge") or dom.startswith("sparse_conv2"):
                 # CUDA-core tensor-product kernels: reported against HBM (their inputs are L2-resident
                 # re-reads; the FP32 pipe and L1/shared-memory throughput are the real limits)
                 roofline = dict(common, bound="hbm", achieved=hbm, peak=pk["hbm_gbs"], unit="GB/s",
@@ -382,7 +565,7 @@ def main():
                     "d2h_bytes_per_step": n * 3 * 4 + 4},
             "stages_ms": {k: round(v[0], 3) for k, v in sorted(stage_avg.items(), key=lambda kv: -kv[1][0])}}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        r = cpu_reference(2, 1)
+        r = cpu_reference_sparse(w, 2, 1) if sparse else cpu_reference(2, 1)
         line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
     if rank == 0:
         print(json.dumps(line))

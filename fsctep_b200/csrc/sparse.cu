@@ -856,6 +856,7 @@ int forward(Ctx& c) {
   const fsc_graph* g = c.g;
   const fsc_sparse_weights* w = c.w;
   cudaStream_t st = c.st;
+  prof::mark("begin", st);
   FSC_TRY(build_gemm_images(p, w, st));
   FSC_TRY(launch_edge_dst(g->row_ptr, p.dst, p.N, st));
   if (p.E > 0) {
