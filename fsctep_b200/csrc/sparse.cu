@@ -22,6 +22,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "tc_common.cuh"
 
 namespace fsc {
 namespace sp {
@@ -31,7 +32,9 @@ constexpr int RH = 64;
 constexpr int MAXR = 40;       // components up to rank 3
 constexpr int MAXROWS = 144;   // sum over paths of 3^Lout (142 at lmax 3)
 constexpr int64_t kMaxGraphs = 4096;
-constexpr int64_t kZBudgetFloats = (int64_t)1 << 30;  // aggregation buffer, 4 GB
+// Aggregation buffer budget, 16 GB: the per-rank fc.4 GEMMs over one node chunk have
+// chunk x 3^Lout rows, and the low ranks need large chunks to fill the GPU.
+constexpr int64_t kZBudgetFloats = (int64_t)1 << 32;
 constexpr int64_t kGramChunk = 16384;
 
 __host__ __device__ constexpr int pow3(int L) { return L == 0 ? 1 : 3 * pow3(L - 1); }
@@ -348,6 +351,195 @@ __global__ void __launch_bounds__(256) z_kernel(Args a, Rows rows, const float* 
       zr[(int64_t)RH * C] = accb;
     }
   }
+}
+
+// ---------------------------------------------------------------- conv2 forward aggregation, tensor cores
+// The same Z as z_kernel, as one small GEMM per receiving node n with K = its edges:
+//   D[(r, a)][j] = sum_e A[(r, a)][e] B[j][e],   A[(r, a)][e] = x1[src_e][c1(r)][a] n_e^{(x)L2}[c2(r)],
+//   B[j][e] = h2'_e[j] (j < 65; rows 65..79 zero),  Z[n][r][j][a] = D[(r, a)][j].
+// M = 128 consecutive (r, a) pairs per tile (TMEM lane = pair), N = 80, K = the node's edges in
+// chunks of 64.  A is built by the CUDA cores straight into TMEM (tf32 hi / lo split; warps w and
+// w + 4 share lanes and build K columns [0, 32) and [32, 64)), B is the node's h2' rows as a
+// K-major shared-memory image (hi / lo), so every tile of the node reuses it; the product is
+// 3xTF32 (hi*lo and lo*hi issued before hi*hi).  A node with more than ZTC_KMAX edges is done in
+// edge groups, the later groups adding into Z.  Persistent grid of two CTAs per SM.
+constexpr int ZTC_M = 128, ZTC_N = 80, ZTC_KC = 64, ZTC_KMAX = 128, ZTC_THREADS = 256;
+constexpr uint32_t ZTC_IMG = 4u * ZTC_N * ZTC_KMAX;  // bytes of one B image (hi or lo)
+struct ZtcSmem {
+  static constexpr uint32_t BHI = 0;
+  static constexpr uint32_t BLO = ZTC_IMG;
+  static constexpr uint32_t NP = 2 * ZTC_IMG;                    // [ZTC_KMAX][MAXR] n^{(x)L}
+  static constexpr uint32_t XOFF = NP + 4u * ZTC_KMAX * MAXR;    // [ZTC_KMAX] source row offsets in x
+  static constexpr uint32_t BAR = XOFF + 8u * ZTC_KMAX;
+  static constexpr uint32_t TOTAL = BAR + 16;
+};
+static_assert(3 * ZtcSmem::TOTAL > 228u * 1024u, "at most two CTAs per SM (256 TMEM columns each)");
+
+// element (n, k) of a K-major no-swizzle B image with N rows
+__device__ __forceinline__ int zimg(int n, int k) { return (k >> 2) * 4 * ZTC_N + 4 * n + (k & 3); }
+
+__global__ void __launch_bounds__(ZTC_THREADS, 2) z_tc_kernel(Args a, Rows rows, const float* __restrict__ x,
+                                                              const float* __restrict__ h2, int64_t n0, int64_t nc,
+                                                              float* __restrict__ Z, int* err) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  float* bhi = reinterpret_cast<float*>(smem + ZtcSmem::BHI);
+  float* blo = reinterpret_cast<float*>(smem + ZtcSmem::BLO);
+  float* np = reinterpret_cast<float*>(smem + ZtcSmem::NP);
+  int64_t* xoff = reinterpret_cast<int64_t*>(smem + ZtcSmem::XOFF);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + ZtcSmem::BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + ZtcSmem::BAR + 8);
+
+  const int tid = threadIdx.x, warp = tid >> 5, half = tid / ZTC_M, row = tid % ZTC_M;
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_slot, 256);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    tc::mbar_init(bar, 1);
+    tc::fence_mbar_init();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+  const uint32_t tD = tbase, tAhi = tbase + 128u, tAlo = tbase + 192u;  // D: 80 columns, A: 64 + 64
+  const uint32_t s_hi = tc::smem_u32(bhi), s_lo = tc::smem_u32(blo);
+  constexpr uint32_t idesc = tc::idesc_tf32(ZTC_M, ZTC_N);
+  // tile = ZTC_M / C rows (slots) taken in the order of rows.rlist, where rows with the same x1
+  // component are adjacent: a thread keeps its gathered x1 values while the component repeats
+  const int C = a.C, R = a.R, S = ZTC_M / C, slot = row / C, ch = row - slot * C;
+  const int ntiles = (rows.nrows + S - 1) / S;
+  uint32_t phase = 0;
+  bool ok = true;
+
+  for (int64_t nl = blockIdx.x; nl < nc && ok; nl += gridDim.x) {
+    const int64_t n = n0 + nl;
+    const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
+    float* zn = Z + nl * (int64_t)rows.nrows * J * C;
+    for (int g0 = e0, grp = 0; (g0 < e1 || grp == 0) && ok; g0 += ZTC_KMAX, ++grp) {
+      const int kg = min(ZTC_KMAX, e1 - g0);  // edges of this group (0 for an isolated node)
+      const int nchunks = max(1, (kg + ZTC_KC - 1) / ZTC_KC);
+      // ---- the group's edge data and B image (previous MMAs finished: d_ready below)
+      __syncthreads();
+      if (tid < ZTC_KMAX) {
+        if (tid < kg) {
+          const int e = g0 + tid;
+          xoff[tid] = (int64_t)a.src[e] * R * C;
+          const float* y = a.edge_y + 12 * (int64_t)e;
+          npow_all(a.lmax, y[0], y[1], y[2], np + tid * MAXR);
+        } else {
+          xoff[tid] = 0;
+        }
+      }
+      for (int i = tid; i < ZTC_N * nchunks * ZTC_KC; i += ZTC_THREADS) {
+        const int k = i / ZTC_N, j = i - k * ZTC_N;
+        float v = 0.f;
+        if (k < kg && j < J) v = j < RH ? h2[(int64_t)(g0 + k) * RH + j] : 1.f;
+        uint32_t hi, lo;
+        tc::split_tf32(v, hi, lo);
+        bhi[zimg(j, k)] = __uint_as_float(hi);
+        blo[zimg(j, k)] = __uint_as_float(lo);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncthreads();
+      int cached_c1 = -1;
+      float xv[32];
+      for (int tile = 0; tile < ntiles && ok; ++tile) {
+        const int q = tile * S + slot;
+        const bool valid = q < rows.nrows;
+        const int r = valid ? rows.rlist[q] : 0;
+        const int c1 = rows.c1[r], c2 = rows.c2[r];
+        for (int cc = 0; cc < nchunks; ++cc) {
+          // ---- A columns [32 half, 32 half + 32) of chunk cc
+          const int kb = cc * ZTC_KC + 32 * half;
+          if (nchunks > 1 || c1 != cached_c1) {  // warp-uniform: a warp's lanes share the row
+            const float* xc = x + (int64_t)c1 * C + ch;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) xv[i] = (valid && kb + i < kg) ? xc[xoff[kb + i]] : 0.f;
+            cached_c1 = nchunks == 1 ? c1 : -1;
+          }
+          uint32_t hi[32], lo[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float v = kb + i < kg ? xv[i] * np[(kb + i) * MAXR + c2] : 0.f;
+            tc::split_tf32(v, hi[i], lo[i]);
+          }
+          tc::tmem_st32(tAhi + lane_off + 32u * half, hi);
+          tc::tmem_st32(tAlo + lane_off + 32u * half, lo);
+          tc::tmem_wait_st();
+          tc::tc_fence_before();
+          __syncthreads();
+          if (tid == 0) {
+            tc::tc_fence_after();
+            const int ksteps = kg > 0 ? min(ZTC_KC, kg - cc * ZTC_KC + 7) / 8 : 1;
+            for (int j = 0; j < ksteps; ++j) {
+              const uint32_t off = 32u * ZTC_N * (uint32_t)(cc * (ZTC_KC / 8) + j);
+              const uint64_t dh = tc::smem_desc_kmajor(s_hi + off, 16u * ZTC_N, 128);
+              const uint64_t dl = tc::smem_desc_kmajor(s_lo + off, 16u * ZTC_N, 128);
+              tc::mma_tf32_ts(tD, tAhi + 8u * j, dl, idesc, (cc > 0 || j > 0) ? 1u : 0u);
+              tc::mma_tf32_ts(tD, tAlo + 8u * j, dh, idesc, 1u);
+            }
+            for (int j = 0; j < ksteps; ++j) {
+              const uint32_t off = 32u * ZTC_N * (uint32_t)(cc * (ZTC_KC / 8) + j);
+              const uint64_t dh = tc::smem_desc_kmajor(s_hi + off, 16u * ZTC_N, 128);
+              tc::mma_tf32_ts(tD, tAhi + 8u * j, dh, idesc, 1u);
+            }
+            tc::mma_commit(bar);
+          }
+          // one thread polls the barrier; the others wait at the CTA barrier without issuing
+          const bool w = tid != 0 || tc::mbar_wait(bar, phase, err, 81);
+          phase ^= 1u;
+          const bool failed = __syncthreads_or(!w);
+          tc::tc_fence_after();
+          if (failed) {
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) break;
+        // ---- epilogue -> Z[n][r][j][a]: half 0 columns [0, 32) and the bias column 64, half 1 [32, 64)
+        uint32_t u[48];
+        tc::tmem_ld32(tD + lane_off + 32u * half, u);
+        if (half == 0) tc::tmem_ld16(tD + lane_off + 64u, u + 32);
+        tc::tmem_wait_ld();
+        if (valid) {
+          float* zr = zn + (int64_t)r * J * C + ch + (int64_t)32 * half * C;
+          if (grp == 0) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) zr[(int64_t)i * C] = __uint_as_float(u[i]);
+            if (half == 0) zr[(int64_t)RH * C] = __uint_as_float(u[32]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) zr[(int64_t)i * C] += __uint_as_float(u[i]);
+            if (half == 0) zr[(int64_t)RH * C] += __uint_as_float(u[32]);
+          }
+        }
+        tc::tc_fence_before();
+      }
+    }
+  }
+  if (!ok && tid == 0) {  // a wait gave up: let the last committed chain finish before freeing TMEM
+    const long long t0 = clock64();
+    while (!tc::mbar_try_wait(bar, phase ^ 1u))
+      if (clock64() - t0 > tc::kWaitCycles) break;
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tbase, 256);
+}
+
+int launch_z_tc(const Args& a, const Rows& rows, const float* x, const float* h2, int64_t n0, int64_t nc, float* Z,
+                int* err, cudaStream_t st) {
+  if (nc <= 0) return FSC_OK;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaFuncSetAttribute(z_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ZtcSmem::TOTAL) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "z_tc_kernel: shared memory attribute");
+  const unsigned blocks = (unsigned)std::min<int64_t>(nc, 2 * (int64_t)sms);
+  z_tc_kernel<<<blocks, ZTC_THREADS, ZtcSmem::TOTAL, st>>>(a, rows, x, h2, n0, nc, Z, err);
+  return check_launch("sparse z_tc_kernel");
 }
 
 // ---------------------------------------------------------------- conv2 backward
@@ -881,8 +1073,12 @@ int forward(Ctx& c) {
   for (int k = 1; k < p.nint; ++k) {
     for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
       const int64_t nc = std::min(p.chunk, p.N - n0);
-      z_kernel<<<(unsigned)nc, 256, 0, st>>>(a, p.rows, p.feats[k - 1], p.h2 + (int64_t)k * p.E * RH, n0, p.zbuf);
-      FSC_TRY(check_launch("sparse z_kernel"));
+      if (p.gtc) {
+        FSC_TRY(launch_z_tc(a, p.rows, p.feats[k - 1], p.h2 + (int64_t)k * p.E * RH, n0, nc, p.zbuf, p.err, st));
+      } else {
+        z_kernel<<<(unsigned)nc, 256, 0, st>>>(a, p.rows, p.feats[k - 1], p.h2 + (int64_t)k * p.E * RH, n0, p.zbuf);
+        FSC_TRY(check_launch("sparse z_kernel"));
+      }
       for (int Lo = 0; Lo <= p.lmax; ++Lo) {
         const int K = p.rows.npl[Lo] * J * p.C;
         GemmArgs ga = gemm(p.zbuf + (int64_t)p.rows.zoff[Lo] * J * p.C, p.zstride, K, w->mix + mix_offset(p, k, Lo),
