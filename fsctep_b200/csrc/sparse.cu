@@ -618,6 +618,214 @@ __global__ void __launch_bounds__(256) bwd_dm_kernel(Args a, Rows rows, const fl
   }
 }
 
+// dm on tensor cores, per receiving node n and 128 consecutive (r, a) pairs (rows.rlist order):
+//   D[(r, a)][e] = sum_{j < 64} dZ[n][r][j][a] h2_e[j]      (M = 128, N = 64 edges, K = 64, 3xTF32)
+//   dm = D + dZ[n][r][64][a]                                (the bias row of h2' = [h2, 1])
+// A (the dZ rows) is written to TMEM by the CUDA cores, B is the node's h2 rows as a K-major image
+// in shared memory (up to two 64-edge chunks).  The epilogue is bwd_dm_kernel's: the source
+// feature gradients by atomics, dE/dn^{(x)L2} reduced over the warp's 32 channels by a transpose
+// reduction (lane i ends with edge i's sum) into per-edge shared-memory rows.
+constexpr int DTC_NE = 64;
+struct DtcSmem {
+  static constexpr uint32_t IMG = 4u * DTC_NE * 64u * 2u;        // one hi or lo image, two edge chunks
+  static constexpr uint32_t BHI = 0;
+  static constexpr uint32_t BLO = IMG;
+  static constexpr uint32_t NP = 2 * IMG;                          // [ZTC_KMAX][MAXR]
+  static constexpr uint32_t SDN = NP + 4u * ZTC_KMAX * MAXR;       // [ZTC_KMAX][MAXR] dE/dn^{(x)L} partials
+  static constexpr uint32_t XOFF = SDN + 4u * ZTC_KMAX * MAXR;     // [ZTC_KMAX]
+  static constexpr uint32_t BAR = XOFF + 8u * ZTC_KMAX;
+  static constexpr uint32_t TOTAL = BAR + 16;
+};
+static_assert(3 * DtcSmem::TOTAL > 228u * 1024u, "at most two CTAs per SM (256 TMEM columns each)");
+
+__device__ __forceinline__ int dimg(int n, int k) { return (k >> 2) * 4 * DTC_NE + 4 * n + (k & 3); }
+
+// Sum over the 32 lanes of t[i] for every i; lane i returns the sum of t[i].
+__device__ __forceinline__ float transpose_reduce32(float (&t)[32], int lane) {
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1) {
+    const bool up = (lane & w) != 0;
+#pragma unroll
+    for (int i = 0; i < w; ++i) {
+      const float send = up ? t[i] : t[i + w];
+      const float keep = up ? t[i + w] : t[i];
+      t[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+    }
+  }
+  return t[0];
+}
+
+__global__ void __launch_bounds__(ZTC_THREADS, 2) dm_tc_kernel(Args a, Rows rows, const float* __restrict__ x,
+                                                               const float* __restrict__ h2, const float* __restrict__ dZ,
+                                                               int64_t n0, int64_t nc, float* __restrict__ gx,
+                                                               float* __restrict__ dnp, int* err) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  float* bhi = reinterpret_cast<float*>(smem + DtcSmem::BHI);
+  float* blo = reinterpret_cast<float*>(smem + DtcSmem::BLO);
+  float* np = reinterpret_cast<float*>(smem + DtcSmem::NP);
+  float* sdn = reinterpret_cast<float*>(smem + DtcSmem::SDN);
+  int64_t* xoff = reinterpret_cast<int64_t*>(smem + DtcSmem::XOFF);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + DtcSmem::BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + DtcSmem::BAR + 8);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, half = tid / ZTC_M, row = tid % ZTC_M;
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_slot, 256);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    tc::mbar_init(bar, 1);
+    tc::fence_mbar_init();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+  const uint32_t tD = tbase, tAhi = tbase + 128u, tAlo = tbase + 192u;  // D: 64 columns, A: 64 + 64
+  const uint32_t s_hi = tc::smem_u32(bhi), s_lo = tc::smem_u32(blo);
+  constexpr uint32_t idesc = tc::idesc_tf32(ZTC_M, DTC_NE);
+  const int C = a.C, R = a.R, S = ZTC_M / C, slot = row / C, ch = row - slot * C;
+  const int ntiles = (rows.nrows + S - 1) / S;
+  uint32_t phase = 0;
+  bool ok = true;
+
+  for (int64_t nl = blockIdx.x; nl < nc && ok; nl += gridDim.x) {
+    const int64_t n = n0 + nl;
+    const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
+    const float* dzn = dZ + nl * (int64_t)rows.nrows * J * C;
+    for (int g0 = e0; g0 < e1 && ok; g0 += ZTC_KMAX) {
+      const int kg = min(ZTC_KMAX, e1 - g0);
+      const int nch = (kg + DTC_NE - 1) / DTC_NE;
+      __syncthreads();
+      if (tid < ZTC_KMAX) {
+        if (tid < kg) {
+          const int e = g0 + tid;
+          xoff[tid] = (int64_t)a.src[e] * R * C;
+          const float* y = a.edge_y + 12 * (int64_t)e;
+          npow_all(a.lmax, y[0], y[1], y[2], np + tid * MAXR);
+        } else {
+          xoff[tid] = 0;
+        }
+#pragma unroll 8
+        for (int c = 0; c < MAXR; ++c) sdn[tid * MAXR + c] = 0.f;
+      }
+      for (int i = tid; i < nch * DTC_NE * 64; i += ZTC_THREADS) {
+        const int k = i >> 6, j = i & 63;  // edge of the group, hidden unit
+        const float v = k < kg ? h2[(int64_t)(g0 + k) * RH + j] : 0.f;
+        uint32_t hi, lo;
+        tc::split_tf32(v, hi, lo);
+        const int o = (k / DTC_NE) * DTC_NE * 64 + dimg(k % DTC_NE, j);
+        bhi[o] = __uint_as_float(hi);
+        blo[o] = __uint_as_float(lo);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncthreads();
+      int cached_c1 = -1;
+      float xv[32];
+      for (int tile = 0; tile < ntiles && ok; ++tile) {
+        const int q = tile * S + slot;
+        const bool valid = q < rows.nrows;
+        const int r = valid ? rows.rlist[q] : 0;
+        const int c1 = rows.c1[r], c2 = rows.c2[r];
+        const float* dzc = dzn + (int64_t)r * J * C + ch;
+        // ---- A = dZ[n][r][j][a], columns j in [32 half, 32 half + 32)
+        {
+          uint32_t hi[32], lo[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float v = valid ? dzc[(int64_t)(32 * half + i) * C] : 0.f;
+            tc::split_tf32(v, hi[i], lo[i]);
+          }
+          tc::tmem_st32(tAhi + lane_off + 32u * half, hi);
+          tc::tmem_st32(tAlo + lane_off + 32u * half, lo);
+        }
+        const float bias = valid ? dzc[(int64_t)RH * C] : 0.f;
+        tc::tmem_wait_st();
+        for (int cc = 0; cc < nch; ++cc) {
+          tc::tc_fence_before();
+          __syncthreads();  // A written (first chunk) / previous chunk's D read (later chunks)
+          if (tid == 0) {
+            tc::tc_fence_after();
+            const uint32_t base = 4u * DTC_NE * 64u * (uint32_t)cc;
+            for (int j = 0; j < 8; ++j) {
+              const uint32_t off = base + 32u * DTC_NE * (uint32_t)j;
+              const uint64_t dh = tc::smem_desc_kmajor(s_hi + off, 16u * DTC_NE, 128);
+              const uint64_t dl = tc::smem_desc_kmajor(s_lo + off, 16u * DTC_NE, 128);
+              tc::mma_tf32_ts(tD, tAhi + 8u * j, dl, idesc, j > 0 ? 1u : 0u);
+              tc::mma_tf32_ts(tD, tAlo + 8u * j, dh, idesc, 1u);
+            }
+            for (int j = 0; j < 8; ++j) {
+              const uint32_t off = base + 32u * DTC_NE * (uint32_t)j;
+              const uint64_t dh = tc::smem_desc_kmajor(s_hi + off, 16u * DTC_NE, 128);
+              tc::mma_tf32_ts(tD, tAhi + 8u * j, dh, idesc, 1u);
+            }
+            tc::mma_commit(bar);
+          }
+          const bool w = tid != 0 || tc::mbar_wait(bar, phase, err, 83);
+          phase ^= 1u;
+          const bool failed = __syncthreads_or(!w);
+          tc::tc_fence_after();
+          if (failed) {
+            ok = false;
+            break;
+          }
+          // ---- epilogue: this thread's 32 edges kb .. kb + 31 of the group
+          const int kb = cc * DTC_NE + 32 * half;
+          uint32_t u[32];
+          tc::tmem_ld32(tD + lane_off + 32u * half, u);
+          tc::tmem_wait_ld();
+          if (nch > 1 || c1 != cached_c1) {  // warp-uniform
+            const float* xc = x + (int64_t)c1 * C + ch;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) xv[i] = (valid && kb + i < kg) ? xc[xoff[kb + i]] : 0.f;
+            cached_c1 = nch == 1 ? c1 : -1;
+          }
+          float t[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int k = kb + i;
+            const float dm = __uint_as_float(u[i]) + bias;
+            t[i] = 0.f;
+            if (valid && k < kg) {
+              atomicAdd(gx + xoff[k] + (int64_t)c1 * C + ch, dm * np[k * MAXR + c2]);
+              t[i] = dm * xv[i];
+            }
+          }
+          const float tsum = transpose_reduce32(t, lane);  // lane i: edge kb + i, summed over the warp's channels
+          if (valid && kb + lane < kg) atomicAdd(&sdn[(kb + lane) * MAXR + c2], tsum);
+        }
+      }
+      __syncthreads();
+      for (int i = tid; i < kg * R; i += ZTC_THREADS) {
+        const int k = i / R, c = i - k * R;
+        dnp[(int64_t)(g0 + k) * MAXR + c] += sdn[k * MAXR + c];
+      }
+    }
+  }
+  if (!ok && tid == 0) {
+    const long long t0 = clock64();
+    while (!tc::mbar_try_wait(bar, phase ^ 1u))
+      if (clock64() - t0 > tc::kWaitCycles) break;
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tbase, 256);
+}
+
+int launch_dm_tc(const Args& a, const Rows& rows, const float* x, const float* h2, const float* dZ, int64_t n0,
+                 int64_t nc, float* gx, float* dnp, int* err, cudaStream_t st) {
+  if (nc <= 0) return FSC_OK;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaFuncSetAttribute(dm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DtcSmem::TOTAL) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "dm_tc_kernel: shared memory attribute");
+  const unsigned blocks = (unsigned)std::min<int64_t>(nc, 2 * (int64_t)sms);
+  dm_tc_kernel<<<blocks, ZTC_THREADS, DtcSmem::TOTAL, st>>>(a, rows, x, h2, dZ, n0, nc, gx, dnp, err);
+  return check_launch("sparse dm_tc_kernel");
+}
+
 // dh_kernel: dE/dh2_e[j] = sum_{(r, a)} dZ[n][r][j][a] * x1[src_e][c1(r)][a] * n_e^{(x)L2}[c2(r)],
 // a (edges x columns) . (columns x 64) product tiled through shared memory (64 edges x 64 j per
 // pass, 32 columns per step, 4 x 4 outputs per thread).
@@ -1175,9 +1383,14 @@ int backward(Ctx& c) {
         ga.alpha = 1.f / avg;
         FSC_TRY(run_gemm(ga, p.img_mixT[k][Lo], p.err, st));
       }
-      bwd_dm_kernel<<<(unsigned)nc, 256, 0, st>>>(a, p.rows, p.feats[k - 1], p.h2 + (int64_t)k * p.E * RH, p.zbuf,
-                                                   n0, p.grads[k - 1], p.dnp);
-      FSC_TRY(check_launch("sparse bwd_dm_kernel"));
+      if (p.gtc) {
+        FSC_TRY(launch_dm_tc(a, p.rows, p.feats[k - 1], p.h2 + (int64_t)k * p.E * RH, p.zbuf, n0, nc, p.grads[k - 1],
+                             p.dnp, p.err, st));
+      } else {
+        bwd_dm_kernel<<<(unsigned)nc, 256, 0, st>>>(a, p.rows, p.feats[k - 1], p.h2 + (int64_t)k * p.E * RH, p.zbuf,
+                                                     n0, p.grads[k - 1], p.dnp);
+        FSC_TRY(check_launch("sparse bwd_dm_kernel"));
+      }
       bwd_dh_kernel<<<(unsigned)nc, 256, 0, st>>>(a, p.rows, p.feats[k - 1], p.zbuf, n0,
                                                    p.dh2 + (int64_t)k * p.E * RH);
       FSC_TRY(check_launch("sparse bwd_dh_kernel"));
