@@ -901,6 +901,190 @@ __global__ void __launch_bounds__(256) bwd_dh_kernel(Args a, Rows rows, const fl
   }
 }
 
+// dh on tensor cores, per receiving node n and up to 128 of its edges (TMEM lane = edge):
+//   D[e][j] = sum_{(r, a)} A[e][(r, a)] B[j][(r, a)],  A[e][(r, a)] = x1[src_e][c1(r)][a] n_e^{(x)L2}[c2(r)],
+//   B[j][(r, a)] = dZ[n][r][j][a]   (M = 128, N = 64, K = rows x C in chunks of 32 channels, 3xTF32).
+// Each chunk is a fresh 12-MMA chain; every second chunk the accumulator is added into fp32
+// registers (short tensor-core chains, sums rounded to nearest), and dh2_e = the register sums.
+// Warps w and w + 4 share lanes: each builds 16 of a chunk's 32 A columns and drains 32 of D's 64.
+constexpr int HTC_KC = 32;
+struct HtcSmem {
+  static constexpr uint32_t IMG = 4u * 64u * HTC_KC;           // one hi or lo image: N = 64, K = 32
+  static constexpr uint32_t BHI = 0;
+  static constexpr uint32_t BLO = IMG;
+  static constexpr uint32_t NP = 2 * IMG;                       // [ZTC_KMAX][MAXR]
+  static constexpr uint32_t XOFF = NP + 4u * ZTC_KMAX * MAXR;   // [ZTC_KMAX]
+  static constexpr uint32_t BAR = XOFF + 8u * ZTC_KMAX;
+  static constexpr uint32_t USED = BAR + 16;
+  static constexpr uint32_t TOTAL = USED > 80u * 1024u ? USED : 80u * 1024u;  // at most two CTAs per SM
+};
+
+__device__ __forceinline__ int himg(int n, int k) { return (k >> 2) * 4 * 64 + 4 * n + (k & 3); }
+
+__global__ void __launch_bounds__(ZTC_THREADS, 2) dh_tc_kernel(Args a, Rows rows, const float* __restrict__ x,
+                                                               const float* __restrict__ dZ, int64_t n0, int64_t nc,
+                                                               float* __restrict__ dh2, int* err) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  float* bhi = reinterpret_cast<float*>(smem + HtcSmem::BHI);
+  float* blo = reinterpret_cast<float*>(smem + HtcSmem::BLO);
+  float* np = reinterpret_cast<float*>(smem + HtcSmem::NP);
+  int64_t* xoff = reinterpret_cast<int64_t*>(smem + HtcSmem::XOFF);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + HtcSmem::BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + HtcSmem::BAR + 8);
+
+  const int tid = threadIdx.x, warp = tid >> 5, half = tid / ZTC_M, row = tid % ZTC_M;
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_slot, 256);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    tc::mbar_init(bar, 1);
+    tc::fence_mbar_init();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+  const uint32_t tD = tbase, tAhi = tbase + 128u, tAlo = tbase + 192u;  // D: 64 columns, A: 32 + 32
+  const uint32_t s_hi = tc::smem_u32(bhi), s_lo = tc::smem_u32(blo);
+  constexpr uint32_t idesc = tc::idesc_tf32(ZTC_M, 64);
+  const int C = a.C, R = a.R, cpr = C / HTC_KC;  // chunks per row
+  const int nchunks = rows.nrows * cpr;
+  uint32_t phase = 0;
+  bool ok = true;
+
+  for (int64_t nl = blockIdx.x; nl < nc && ok; nl += gridDim.x) {
+    const int64_t n = n0 + nl;
+    const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
+    const float* dzn = dZ + nl * (int64_t)rows.nrows * J * C;
+    for (int g0 = e0; g0 < e1 && ok; g0 += ZTC_KMAX) {
+      const int kg = min(ZTC_KMAX, e1 - g0);
+      __syncthreads();
+      if (tid < ZTC_KMAX) {
+        if (tid < kg) {
+          const int e = g0 + tid;
+          xoff[tid] = (int64_t)a.src[e] * R * C;
+          const float* y = a.edge_y + 12 * (int64_t)e;
+          npow_all(a.lmax, y[0], y[1], y[2], np + tid * MAXR);
+        } else {
+          xoff[tid] = 0;
+        }
+      }
+      __syncthreads();
+      const bool erow = row < kg;
+      float acc[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+      for (int kc = 0; kc < nchunks && ok; ++kc) {
+        const int r = kc / cpr, a0 = (kc - r * cpr) * HTC_KC;
+        const int c1 = rows.c1[r], c2 = rows.c2[r];
+        // ---- A columns [16 half, 16 half + 16) of the chunk: this lane's edge
+        {
+          float v[16];
+          if (erow) {
+            const float4* xs = reinterpret_cast<const float4*>(x + xoff[row] + (int64_t)c1 * C + a0 + 16 * half);
+            const float w = np[row * MAXR + c2];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float4 t = xs[i];
+              v[4 * i] = t.x * w; v[4 * i + 1] = t.y * w; v[4 * i + 2] = t.z * w; v[4 * i + 3] = t.w * w;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = 0.f;
+          }
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) tc::split_tf32(v[i], hi[i], lo[i]);
+          tc::tmem_st16(tAhi + lane_off + 16u * half, hi);
+          tc::tmem_st16(tAlo + lane_off + 16u * half, lo);
+        }
+        // ---- B = dZ[n][r][j][a0 .. a0 + 32) for j < 64 (thread: one j, four channels, two passes)
+        {
+          const float* dzr = dzn + (int64_t)r * J * C + a0;
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int i = tid + ZTC_THREADS * t, j = i & 63, k4 = i >> 6;
+            const float4 v = *reinterpret_cast<const float4*>(dzr + (int64_t)j * C + 4 * k4);
+            uint32_t h0, l0, h1, l1, h2_, l2, h3, l3;
+            tc::split_tf32(v.x, h0, l0);
+            tc::split_tf32(v.y, h1, l1);
+            tc::split_tf32(v.z, h2_, l2);
+            tc::split_tf32(v.w, h3, l3);
+            const int o = himg(j, 4 * k4);
+            *reinterpret_cast<uint4*>(bhi + o) = make_uint4(h0, h1, h2_, h3);
+            *reinterpret_cast<uint4*>(blo + o) = make_uint4(l0, l1, l2, l3);
+          }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+          tc::tc_fence_after();
+          const uint32_t acc0 = (kc & 1) ? 1u : 0u;  // chunks are summed in pairs on the tensor core
+          for (int j = 0; j < HTC_KC / 8; ++j) {
+            const uint32_t off = 32u * 64u * (uint32_t)j;
+            const uint64_t dh = tc::smem_desc_kmajor(s_hi + off, 16u * 64u, 128);
+            const uint64_t dl = tc::smem_desc_kmajor(s_lo + off, 16u * 64u, 128);
+            tc::mma_tf32_ts(tD, tAhi + 8u * j, dl, idesc, (j > 0 || acc0) ? 1u : 0u);
+            tc::mma_tf32_ts(tD, tAlo + 8u * j, dh, idesc, 1u);
+          }
+          for (int j = 0; j < HTC_KC / 8; ++j) {
+            const uint32_t off = 32u * 64u * (uint32_t)j;
+            const uint64_t dh = tc::smem_desc_kmajor(s_hi + off, 16u * 64u, 128);
+            tc::mma_tf32_ts(tD, tAhi + 8u * j, dh, idesc, 1u);
+          }
+          tc::mma_commit(bar);
+        }
+        const bool w = tid != 0 || tc::mbar_wait(bar, phase, err, 84);
+        phase ^= 1u;
+        const bool failed = __syncthreads_or(!w);
+        tc::tc_fence_after();
+        if (failed) {
+          ok = false;
+          break;
+        }
+        if ((kc & 1) || kc == nchunks - 1) {  // drain the pair's sum into the registers
+          uint32_t u[32];
+          tc::tmem_ld32(tD + lane_off + 32u * half, u);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[i] += __uint_as_float(u[i]);
+        }
+        tc::tc_fence_before();
+      }
+      if (ok && erow) {
+        float4* o = reinterpret_cast<float4*>(dh2 + (int64_t)(g0 + row) * RH + 32 * half);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+      }
+    }
+  }
+  if (!ok && tid == 0) {
+    const long long t0 = clock64();
+    while (!tc::mbar_try_wait(bar, phase ^ 1u))
+      if (clock64() - t0 > tc::kWaitCycles) break;
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tbase, 256);
+}
+
+int launch_dh_tc(const Args& a, const Rows& rows, const float* x, const float* dZ, int64_t n0, int64_t nc, float* dh2,
+                 int* err, cudaStream_t st) {
+  if (nc <= 0) return FSC_OK;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaFuncSetAttribute(dh_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)HtcSmem::TOTAL) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "dh_tc_kernel: shared memory attribute");
+  const unsigned blocks = (unsigned)std::min<int64_t>(nc, 2 * (int64_t)sms);
+  dh_tc_kernel<<<blocks, ZTC_THREADS, HtcSmem::TOTAL, st>>>(a, rows, x, dZ, n0, nc, dh2, err);
+  return check_launch("sparse dh_tc_kernel");
+}
+
 // ---------------------------------------------------------------- edge gradient
 // g_e = dE/d|r| n + (I - n n^T) / |r| dE/dn,  dE/dn from dE/dn^{(x)L}; dE/d|r| in g_e[0] on entry.
 __global__ void edge_grad_kernel(int64_t E, int lmax, const float* __restrict__ ey, const float* __restrict__ dnp,
@@ -1391,9 +1575,13 @@ int backward(Ctx& c) {
                                                      n0, p.grads[k - 1], p.dnp);
         FSC_TRY(check_launch("sparse bwd_dm_kernel"));
       }
-      bwd_dh_kernel<<<(unsigned)nc, 256, 0, st>>>(a, p.rows, p.feats[k - 1], p.zbuf, n0,
-                                                   p.dh2 + (int64_t)k * p.E * RH);
-      FSC_TRY(check_launch("sparse bwd_dh_kernel"));
+      if (p.gtc) {
+        FSC_TRY(launch_dh_tc(a, p.rows, p.feats[k - 1], p.zbuf, n0, nc, p.dh2 + (int64_t)k * p.E * RH, p.err, st));
+      } else {
+        bwd_dh_kernel<<<(unsigned)nc, 256, 0, st>>>(a, p.rows, p.feats[k - 1], p.zbuf, n0,
+                                                     p.dh2 + (int64_t)k * p.E * RH);
+        FSC_TRY(check_launch("sparse bwd_dh_kernel"));
+      }
     }
     prof::mark("sparse_conv2_backward", st);
   }
