@@ -136,6 +136,21 @@ __device__ __forceinline__ void npow_grad(int lmax, const float* n, const float*
         }
 }
 
+// Sum over the 32 lanes of t[i] for every i; lane i returns the sum of t[i].
+__device__ __forceinline__ float transpose_reduce32(float (&t)[32], int lane) {
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1) {
+    const bool up = (lane & w) != 0;
+#pragma unroll
+    for (int i = 0; i < w; ++i) {
+      const float send = up ? t[i] : t[i + w];
+      const float keep = up ? t[i + w] : t[i];
+      t[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+    }
+  }
+  return t[0];
+}
+
 struct GradList {
   float* p[8];
 };
@@ -226,13 +241,18 @@ __global__ void __launch_bounds__(256) conv1_fwd_kernel(Args a, const float* __r
 }
 
 // conv1 backward: per edge dE/dh2 (layer 0) and dE/dn^{(x)L} (accumulated), from G1 = dE/df1.
+// Warp per receiving node, lanes over channels.  Per edge and rank L, with d_L[c] = sum_{q in L}
+// G1[n][q][c] n^{(x)L}[q] / deg:
+//   g_L[c] = sum_j h2'_e[j] K[L][j][c],   dE/dh2_e[j] = sum_{L, c} d_L[c] K[L][j][c],
+//   dE/dn^{(x)L}[q] += sum_c G1[n][q][c] g_L[c] / deg,
+// one coalesced pass over K gives both g and the lane's partial dE/dh2; the per-lane partials
+// are summed over the warp by transpose reductions (lane l ends with j = l and j = 32 + l).
 template <int CPL>
 __global__ void __launch_bounds__(256) conv1_bwd_kernel(Args a, const float* __restrict__ K, const float* __restrict__ h2,
                                                         const float* __restrict__ G1, float* __restrict__ dh2,
                                                         float* __restrict__ dnp) {
   __shared__ float hs[8][J + 3];
   __shared__ float np[8][MAXR];
-  __shared__ float dg[8][4][128];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n = (int64_t)blockIdx.x * 8 + warp;
   if (n >= a.N) return;
@@ -241,9 +261,10 @@ __global__ void __launch_bounds__(256) conv1_bwd_kernel(Args a, const float* __r
   const int deg = e1 - e0;
   const float inv = 1.f / (float)(deg > 1 ? deg : 1);
   const int sn = a.species[n];
+  const float* g1n = G1 + n * R * C + lane;
   for (int e = e0; e < e1; ++e) {
     const int s = a.src[e];
-    const float* kt = K + ((int64_t)a.species[s] * a.S_species + sn) * (a.lmax + 1) * J * C;
+    const float* kt = K + ((int64_t)a.species[s] * a.S_species + sn) * (a.lmax + 1) * J * C + lane;
     hs[warp][lane] = h2[(int64_t)e * RH + lane];
     hs[warp][lane + 32] = h2[(int64_t)e * RH + lane + 32];
     if (lane == 0) {
@@ -252,43 +273,68 @@ __global__ void __launch_bounds__(256) conv1_bwd_kernel(Args a, const float* __r
       npow_all(a.lmax, y[0], y[1], y[2], np[warp]);
     }
     __syncwarp();
-    float dnl[MAXR];
-    for (int L = 0; L <= a.lmax; ++L) {
-      float g[CPL], d[CPL];
+    float ph[64];
 #pragma unroll
-      for (int i = 0; i < CPL; ++i) g[i] = d[i] = 0.f;
-      const float* kl = kt + (int64_t)L * J * C;
-      for (int j = 0; j < J; ++j) {
-        const float h = hs[warp][j];
+    for (int j = 0; j < 64; ++j) ph[j] = 0.f;
+    float dn[64];  // this lane's partial dE/dn^{(x)L}[q], q < R (entries q >= R stay 0)
 #pragma unroll
-        for (int i = 0; i < CPL; ++i) g[i] = fmaf(h, kl[j * C + lane + 32 * i], g[i]);
-      }
+    for (int q = 0; q < 64; ++q) dn[q] = 0.f;
+#pragma unroll
+    for (int L = 0; L < 4; ++L) {
+      if (L > a.lmax) break;
+      float d[CPL], g[CPL];
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) d[i] = g[i] = 0.f;
       for (int q = roff(L); q < roff(L + 1); ++q) {
-        const float v = np[warp][q];
+        const float v = np[warp][q] * inv;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) d[i] = fmaf(g1n[q * C + 32 * i], v, d[i]);
+      }
+      const float* kl = kt + (int64_t)L * J * C;
+#pragma unroll
+      for (int j = 0; j < RH; ++j) {
+        const float h = hs[warp][j];
         float t = 0.f;
 #pragma unroll
         for (int i = 0; i < CPL; ++i) {
-          const float gv = G1[(n * R + q) * C + lane + 32 * i] * inv;
-          d[i] = fmaf(gv, v, d[i]);
-          t = fmaf(gv, g[i], t);
+          const float k = kl[j * C + 32 * i];
+          g[i] = fmaf(h, k, g[i]);
+          t = fmaf(d[i], k, t);
         }
-        dnl[q] = warp_sum(t);
+        ph[j] += t;
       }
 #pragma unroll
-      for (int i = 0; i < CPL; ++i) dg[warp][L][lane + 32 * i] = d[i];
-    }
-    __syncwarp();
-    // dh2'[j] = sum_L sum_c dg_L[c] K[L][j][c], lanes over j
-    for (int j = lane; j < RH; j += 32) {
-      float t = 0.f;
-      for (int L = 0; L <= a.lmax; ++L) {
-        const float* kr = kt + ((int64_t)L * J + j) * C;
-        for (int c = 0; c < C; ++c) t = fmaf(dg[warp][L][c], kr[c], t);
+      for (int i = 0; i < CPL; ++i) g[i] += kl[RH * C + 32 * i];  // the bias row, h2'[64] = 1
+#pragma unroll
+      for (int q = 0; q < 40; ++q) {
+        if (q >= roff(L) && q < roff(L + 1)) {
+          float t = 0.f;
+#pragma unroll
+          for (int i = 0; i < CPL; ++i) t = fmaf(g1n[q * C + 32 * i], g[i], t);
+          dn[q] = t * inv;
+        }
       }
-      dh2[(int64_t)e * RH + j] = t;
     }
-    if (lane == 0)
-      for (int q = 0; q < R; ++q) dnp[(int64_t)e * MAXR + q] += dnl[q];
+    float lo[32], hi[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      lo[j] = ph[j];
+      hi[j] = ph[32 + j];
+    }
+    const float dlo = transpose_reduce32(lo, lane);
+    const float dhi = transpose_reduce32(hi, lane);
+    dh2[(int64_t)e * RH + lane] = dlo;
+    dh2[(int64_t)e * RH + 32 + lane] = dhi;
+    float q0[32], q1[32];
+#pragma unroll
+    for (int q = 0; q < 32; ++q) {
+      q0[q] = dn[q];
+      q1[q] = dn[32 + q];
+    }
+    const float s0 = transpose_reduce32(q0, lane);
+    const float s1 = transpose_reduce32(q1, lane);
+    if (lane < R) dnp[(int64_t)e * MAXR + lane] += s0;
+    if (32 + lane < R) dnp[(int64_t)e * MAXR + 32 + lane] += s1;
     __syncwarp();
   }
 }
@@ -639,21 +685,6 @@ struct DtcSmem {
 static_assert(3 * DtcSmem::TOTAL > 228u * 1024u, "at most two CTAs per SM (256 TMEM columns each)");
 
 __device__ __forceinline__ int dimg(int n, int k) { return (k >> 2) * 4 * DTC_NE + 4 * n + (k & 3); }
-
-// Sum over the 32 lanes of t[i] for every i; lane i returns the sum of t[i].
-__device__ __forceinline__ float transpose_reduce32(float (&t)[32], int lane) {
-#pragma unroll
-  for (int w = 16; w >= 1; w >>= 1) {
-    const bool up = (lane & w) != 0;
-#pragma unroll
-    for (int i = 0; i < w; ++i) {
-      const float send = up ? t[i] : t[i + w];
-      const float keep = up ? t[i + w] : t[i];
-      t[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
-    }
-  }
-  return t[0];
-}
 
 __global__ void __launch_bounds__(ZTC_THREADS, 2) dm_tc_kernel(Args a, Rows rows, const float* __restrict__ x,
                                                                const float* __restrict__ h2, const float* __restrict__ dZ,
