@@ -668,6 +668,18 @@ int run_backward(Ctx& c, fsc_ictd_outputs* out) {
 
 int gemm_path() { return g_gemm_path; }
 
+int launch_graph_reduce(int width, const float* e, const float* edge_y, const float* grad, const int32_t* item_atom,
+                        const int32_t* batch, int64_t count, int64_t limit, double* out, const float* shift,
+                        cudaStream_t st) {
+  if (count <= 0) return FSC_OK;
+  const unsigned blocks = (unsigned)ceil_div(count, 256);
+  if (width == 1)
+    graph_reduce_kernel<1><<<blocks, 256, 0, st>>>(e, edge_y, grad, item_atom, batch, count, limit, out, shift);
+  else
+    graph_reduce_kernel<9><<<blocks, 256, 0, st>>>(e, edge_y, grad, item_atom, batch, count, limit, out, shift);
+  return check_launch("graph_reduce_kernel");
+}
+
 }  // namespace fsc
 
 extern "C" {

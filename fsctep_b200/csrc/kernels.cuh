@@ -158,6 +158,13 @@ struct GemmImageBatch {
 int run_gemm(const GemmArgs& a, const float* img, int* err, cudaStream_t st);
 // Process-wide GEMM path (fsc_ictd_set_gemm_path): 0 = tensor cores where supported.
 int gemm_path();
+// Per-graph float64 sums, block-reduced where a block's items share one graph:
+// width 1: out[b] += e[i] over atoms i < min(count, limit) of graph b;
+// width 9: out[b][3p+q] += r_i[p] g_i[q] over edges i (r = edge_y[i][9..11], or shift[i] if given),
+// graph of edge i = batch[item_atom[i]].
+int launch_graph_reduce(int width, const float* e, const float* edge_y, const float* grad, const int32_t* item_atom,
+                        const int32_t* batch, int64_t count, int64_t limit, double* out, const float* shift,
+                        cudaStream_t st);
 
 // Readout (pure_cartesian_ictd_layers_full.py:956-1054)
 struct ReadoutArgs {

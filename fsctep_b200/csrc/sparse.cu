@@ -1144,11 +1144,12 @@ struct RdArgs {
   const float* feats[8];
 };
 
+// Gp[nl][j] = sum_m t_L[c][m] t_L[d][m], (c, d) = pairs[j]; grid (pair blocks, nodes)
 __global__ void gram_pack_kernel(RdArgs a, int L, int64_t n0, int64_t nn, const int32_t* __restrict__ pairs,
                                  int64_t npairs, float* __restrict__ Gp) {
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= nn * npairs) return;
-  const int64_t nl = idx / npairs, j = idx - nl * npairs;
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t nl = blockIdx.y;
+  if (j >= npairs || nl >= nn) return;
   const int64_t n = n0 + nl;
   const int32_t pr = pairs[j];
   const int cp = pr & 0xffff, dp = pr >> 16;
@@ -1157,23 +1158,23 @@ __global__ void gram_pack_kernel(RdArgs a, int L, int64_t n0, int64_t nn, const 
   const float* fd = a.feats[kd] + (n * a.R + roff(L)) * a.C + d;
   float acc = 0.f;
   for (int m = 0; m < pow3(L); ++m) acc = fmaf(fc[m * a.C], fd[m * a.C], acc);
-  Gp[idx] = acc;
+  Gp[nl * npairs + j] = acc;
 }
 
-// grads at t_L[c'][m] += 2 sum_d H[n][c'][d] t_L[d][m]
+// grads at t_L[c'][m] += 2 sum_d H[n][c'][d] t_L[d][m]; grid (channel blocks, nodes).  H is
+// symmetric (ds times the symmetrised W_read), so H[n][d][c'] is read: coalesced over c'.
 __global__ void gram_apply_kernel(RdArgs a, GradList g, int L, int64_t n0, int64_t nn, const float* __restrict__ H) {
   const int nC = a.C * a.nint;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= nn * nC) return;
-  const int64_t nl = idx / nC;
-  const int cp = (int)(idx - nl * nC);
+  const int cp = blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t nl = blockIdx.y;
+  if (cp >= nC || nl >= nn) return;
   const int64_t n = n0 + nl;
   const int M = pow3(L);
-  const float* h = H + (nl * nC + cp) * (int64_t)nC;
+  const float* h = H + nl * (int64_t)nC * nC + cp;
   float acc[27];
   for (int m = 0; m < M; ++m) acc[m] = 0.f;
   for (int d = 0; d < nC; ++d) {
-    const float hv = h[d];
+    const float hv = h[(int64_t)d * nC];
     const int kd = d / a.C, dd = d - kd * a.C;
     const float* fd = a.feats[kd] + (n * a.R + roff(L)) * a.C + dd;
     for (int m = 0; m < M; ++m) acc[m] = fmaf(hv, fd[m * a.C], acc[m]);
@@ -1226,24 +1227,6 @@ __global__ void p5_bwd_kernel(RdArgs a, GradList g, int lmax, const float* __res
 }
 
 // per-graph sums of r (x) g (virial) or S (x) g (cell gradient), double atomics
-__global__ void edge_reduce_kernel(int64_t E, const float* __restrict__ ey, const float* __restrict__ shift,
-                                   const float* __restrict__ g, const int32_t* __restrict__ src,
-                                   const int32_t* __restrict__ batch, int use_shift, double* __restrict__ out) {
-  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= E) return;
-  const float* r = use_shift ? shift + 3 * e : ey + 12 * e + 9;
-  double* o = out + 9 * (int64_t)batch[src[e]];
-  for (int p = 0; p < 3; ++p)
-    for (int q = 0; q < 3; ++q) atomicAdd(o + 3 * p + q, (double)r[p] * (double)g[3 * e + q]);
-}
-
-__global__ void energy_reduce_kernel(int64_t N, int64_t nlocal, const float* __restrict__ ae,
-                                     const int32_t* __restrict__ batch, double* __restrict__ out) {
-  const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= nlocal || n >= N) return;
-  atomicAdd(out + batch[n], (double)ae[n]);
-}
-
 __global__ void to_float_kernel(const double* __restrict__ in, int64_t n, float* __restrict__ out) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) out[i] = (float)in[i];
@@ -1520,8 +1503,8 @@ int forward(Ctx& c) {
     const float* Wp = w->wread_p + (int64_t)L * p.S * p.npairs;
     for (int64_t n0 = 0; n0 < p.N; n0 += p.gchunk) {
       const int64_t nn = std::min(p.gchunk, p.N - n0);
-      gram_pack_kernel<<<(unsigned)ceil_div(nn * p.npairs, 256), 256, 0, st>>>(rd, L, n0, nn, w->pairs, p.npairs,
-                                                                               p.gbuf);
+      const dim3 grid((unsigned)ceil_div(p.npairs, 256), (unsigned)nn);
+      gram_pack_kernel<<<grid, 256, 0, st>>>(rd, L, n0, nn, w->pairs, p.npairs, p.gbuf);
       FSC_TRY(check_launch("sparse gram_pack_kernel"));
       GemmArgs ga = gemm(p.gbuf, p.npairs, 0, Wp, p.npairs, 1, p.scalars + n0 * p.S, p.S, 0, nn, 1, (int)p.npairs, p.S);
       ga.accumulate = 1;
@@ -1579,7 +1562,7 @@ int backward(Ctx& c) {
       GemmArgs ga = gemm(p.dscalars + n0 * p.S, p.S, 0, Ws, (int64_t)p.nC * p.nC, 0, p.gbuf, (int64_t)p.nC * p.nC, 0,
                          nn, 1, p.S, p.nC * p.nC);
       FSC_TRY(run_gemm(ga, p.img_gb[L], p.err, st));
-      gram_apply_kernel<<<(unsigned)ceil_div(nn * p.nC, 128), 128, 0, st>>>(rd, gl, L, n0, nn, p.gbuf);
+      gram_apply_kernel<<<dim3((unsigned)ceil_div(p.nC, 128), (unsigned)nn), 128, 0, st>>>(rd, gl, L, n0, nn, p.gbuf);
       FSC_TRY(check_launch("sparse gram_apply_kernel"));
     }
   }
@@ -1654,10 +1637,8 @@ int run_forward(Ctx& c, float* energy, float* atom_energy) {
   float* ebuf = atom_energy ? atom_energy : p.dxb;
   FSC_TRY(launch_energy(p.act_post[p.n_hidden - 1], p.N, H, c.w->out_v, c.w->out_c0, c.g->batch, c.g->num_local, ebuf,
                         nullptr, c.st));
-  if (p.N > 0) {
-    energy_reduce_kernel<<<(unsigned)ceil_div(p.N, 256), 256, 0, c.st>>>(p.N, c.g->num_local, ebuf, c.g->batch, p.acc_d);
-    FSC_TRY(check_launch("sparse energy_reduce_kernel"));
-  }
+  FSC_TRY(launch_graph_reduce(1, ebuf, nullptr, nullptr, nullptr, c.g->batch, p.N, c.g->num_local, p.acc_d, nullptr,
+                              c.st));
   if (energy) {
     to_float_kernel<<<(unsigned)ceil_div(p.B, 256), 256, 0, c.st>>>(p.acc_d, p.B, energy);
     FSC_TRY(check_launch("sparse to_float_kernel"));
@@ -1684,17 +1665,13 @@ int run_backward(Ctx& c, fsc_ictd_outputs* out) {
   double* cg = p.acc_d + 10 * kMaxGraphs;
   if (out->virial) {
     if (cudaMemsetAsync(vir, 0, sizeof(double) * 9 * kMaxGraphs, c.st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset");
-    if (p.E > 0)
-      edge_reduce_kernel<<<(unsigned)ceil_div(p.E, 256), 256, 0, c.st>>>(p.E, p.edge_y, g->shift, eg, g->src, g->batch,
-                                                                        0, vir);
+    FSC_TRY(launch_graph_reduce(9, nullptr, p.edge_y, eg, g->src, g->batch, p.E, p.E, vir, nullptr, c.st));
     to_float_kernel<<<(unsigned)ceil_div(9 * p.B, 256), 256, 0, c.st>>>(vir, 9 * p.B, out->virial);
     FSC_TRY(check_launch("sparse virial"));
   }
   if (out->cell_grad) {
     if (cudaMemsetAsync(cg, 0, sizeof(double) * 9 * kMaxGraphs, c.st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset");
-    if (p.E > 0)
-      edge_reduce_kernel<<<(unsigned)ceil_div(p.E, 256), 256, 0, c.st>>>(p.E, p.edge_y, g->shift, eg, g->src, g->batch,
-                                                                        1, cg);
+    FSC_TRY(launch_graph_reduce(9, nullptr, p.edge_y, eg, g->src, g->batch, p.E, p.E, cg, g->shift, c.st));
     to_float_kernel<<<(unsigned)ceil_div(9 * p.B, 256), 256, 0, c.st>>>(cg, 9 * p.B, out->cell_grad);
     FSC_TRY(check_launch("sparse cell grad"));
   }
