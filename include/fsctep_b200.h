@@ -308,8 +308,9 @@ void fsc_ictd_set_readout_path(int path);
 /* Radial MLP path (per-edge fc / fc2_layers and their backward): 0 = tensor cores where
  * supported (default; number_of_basis <= 16), 1 = CUDA-core kernels.  Process-wide. */
 void fsc_ictd_set_radial_path(int path);
-/* Channel-mixing and MainNet GEMMs: 0 = tensor cores (tcgen05, TMA-staged operands, 3xTF32)
- * where the shape qualifies (default), 1 = CUDA-core kernel.  Process-wide. */
+/* Channel-mixing and MainNet GEMMs, and the pure-cartesian-sparse per-node aggregation kernels
+ * (forward Z and its two reverse contractions): 0 = tensor cores (tcgen05, 3xTF32) where the
+ * shape qualifies (default), 1 = CUDA-core kernels.  Process-wide. */
 void fsc_ictd_set_gemm_path(int path);
 /* Physical-tensor heads of the o3 model (pure_cartesian_ictd_layers_o3.py:1010-1044), from the
  * features left in the workspace by the last fsc_ictd_forward on it: for head h,
