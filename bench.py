@@ -315,16 +315,23 @@ def run_native(args, rank, world, device):
                 ghosts=info["ghosts"], dims=dims)
 
 
-def run_sparse(args, device):
-    """One GPU: pure-cartesian-sparse energy + forces (+ virial) of a seeded crystal or water box."""
+def run_sparse(args, rank, world, device):
+    """pure-cartesian-sparse energy + forces (+ virial) of a seeded crystal or water box; under
+    torchrun the FCC crystal grows with the ranks and is decomposed as the ictd workloads are."""
     from fsctep_b200 import _native as NAT
+    from fsctep_b200 import domain as D
+    from fsctep_b200 import systems
     from fsctep_b200.neighbors import build_graph
     from fsctep_b200.sparse import SparseEngine
 
     w = WORKLOADS[args.workload]
     cfg = sparse_cfg(w)
     eng = SparseEngine(sparse_weights(cfg), cfg, device)
-    sysd = sparse_system(w)
+    dims = D.grid_for(world)
+    if world == 1:
+        sysd = sparse_system(w)
+    else:  # this rank's block of a (dims * cells) FCC crystal
+        sysd = systems.fcc_block(D.block_of(rank, dims), dims, n_cells=w["cells"], seed=1000 + rank)
     n = sysd["pos"].shape[0]
     pos_d = torch.tensor(sysd["pos"], device=device)
     cell_d = torch.tensor(sysd["cell"], device=device)
@@ -333,14 +340,27 @@ def run_sparse(args, device):
     pos_h = torch.tensor(sysd["pos"]).pin_memory()
     forces_h = torch.empty(n, 3, dtype=torch.float32).pin_memory()
     energy_h = torch.empty(1, dtype=torch.float32).pin_memory()
-    info = {}
+    info = {"ghosts": 0}
+    if world == 1:
+        def step(pos, cell):
+            g = build_graph(pos, cell, cfg.max_radius)
+            energy, _ = eng.forward(pos, Z, batch, cell, g)
+            out = eng.backward(want_virial=True)
+            info["edges"] = g.num_edges
+            return energy, out["forces"]
+    else:
+        dec = D.Decomposition(sysd["cell"][0], dims, cfg.num_interaction * cfg.max_radius)
+        evaluate = D.sparse_evaluator(eng, sysd["cell"][0], cfg.max_radius, want_virial=True)
 
-    def step(pos, cell):
-        g = build_graph(pos, cell, cfg.max_radius)
-        energy, _ = eng.forward(pos, Z, batch, cell, g)
-        out = eng.backward(want_virial=True)
-        info["edges"] = g.num_edges
-        return energy, out["forces"]
+        def counting_eval(p, s_, nl, pbc):
+            out = evaluate(p, s_, nl, pbc)
+            info["edges"] = eng._last[4].num_edges
+            return out
+
+        def step(pos, cell):
+            r = D.run_dist(D.decomposed_step(dec, rank, pos, Z, counting_eval, want_virial=True))
+            info["ghosts"] = r["num_ghosts"]
+            return r["energy"].reshape(1), r["forces"]
 
     def e2e_step():
         energy, forces = step(pos_h.to(device, non_blocking=True), cell_d)
@@ -352,6 +372,8 @@ def run_sparse(args, device):
     torch.cuda.synchronize()
     if eng.status() != 0:
         raise RuntimeError(f"sparse engine status {eng.status()}")
+    if world > 1:
+        torch.distributed.barrier()
     ours = None
     if not args.no_launch_count:
         from torch.profiler import ProfilerActivity, profile
@@ -364,7 +386,7 @@ def run_sparse(args, device):
     NAT.profile_enable(True)
     stage_ms = {}
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(torch.cuda.current_device()) as clk:
+    with ClockSampler(torch.cuda.current_device() if world == 1 else int(os.environ.get("LOCAL_RANK", 0))) as clk:
         t0.record()
         for _ in range(args.steps):
             step(pos_d, cell_d)
@@ -373,6 +395,9 @@ def run_sparse(args, device):
         t1.record()
         torch.cuda.synchronize()
     NAT.profile_enable(False)
+    ms_total = t0.elapsed_time(t1)
+    if world > 1:
+        torch.distributed.barrier()
     for _ in range(max(1, args.warmup // 2)):
         e2e_step()
     torch.cuda.synchronize()
@@ -382,9 +407,12 @@ def run_sparse(args, device):
         e2e_step()
     e1.record()
     torch.cuda.synchronize()
-    return dict(n=n, E=info["edges"], ms_step=t0.elapsed_time(t1) / args.steps, ms_e2e=e0.elapsed_time(e1) / args.steps,
+    ms = torch.tensor([ms_total, e0.elapsed_time(e1)], device=device, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    return dict(n=n, E=info["edges"], ms_step=float(ms[0]) / args.steps, ms_e2e=float(ms[1]) / args.steps,
                 stage_ms=stage_ms, clocks=clk.summary(), launches=None if ours is None else ours * args.steps,
-                cfg=cfg, ghosts=0, dims=(1, 1, 1))
+                cfg=cfg, ghosts=info["ghosts"], dims=dims)
 
 
 def cpu_reference_sparse(w, steps, warmup):
@@ -470,8 +498,8 @@ def main():
     metric = "atom-steps/s (E+F)"
     w = WORKLOADS[args.workload]
     sparse = w["model"] == "sparse"
-    if sparse and (world > 1 or args.gpus > 1):
-        raise SystemExit(f"--workload {args.workload}: the pure-cartesian-sparse workloads run on one GPU")
+    if sparse and w["system"] != "fcc" and (world > 1 or args.gpus > 1):
+        raise SystemExit(f"--workload {args.workload}: runs on one GPU (the FCC workloads decompose over GPUs)")
     n_atoms = int(np.prod(w["cells"])) * 8 if not sparse else None
     config = {"workload": f"{args.workload}: pure-cartesian-ictd diamond Si {n_atoms} atoms (config 4)",
               "model": "pure-cartesian-ictd", "channels": w["channels"], "num_interaction": w["num_interaction"],
@@ -495,7 +523,12 @@ def main():
         config = {"workload": f"{args.workload}: pure-cartesian-sparse {what}", "model": "pure-cartesian-sparse",
                   "channels": w["channels"], "num_interaction": w["num_interaction"], "lmax": w["lmax"],
                   "max_rank_other": 1, "k_policy": "k0", "cutoff": 5.0, "radial_basis": "gaussian x8",
-                  "atoms_per_gpu": n_atoms, "parallelism": "single", "decomposition": None,
+                  "atoms_per_gpu": n_atoms,
+                  "parallelism": ("spatial%dx%dx%d" % grid_for(args.gpus)) if args.gpus > 1 else "single",
+                  "decomposition": ("blocks of a dims x cells FCC crystal, halo = num_interaction x cutoff = 15 A of "
+                                    "recomputed ghosts (every layer on all local atoms), one position halo exchange "
+                                    "and one reverse ghost-force exchange per step (NCCL all_to_all), energy and "
+                                    "virial all_reduce") if args.gpus > 1 else None,
                   "step": "neighbour list + forward + backward (energy, forces, virial)",
                   "l2": "inputs smaller than L2 for water3k (re-read from L2 between steps); "
                         "per-layer aggregation buffers larger than L2 for the FCC workloads"}
@@ -521,7 +554,7 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300))
     device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(device)
-    res = run_sparse(args, device) if sparse else run_native(args, rank, world, device)
+    res = run_sparse(args, rank, world, device) if sparse else run_native(args, rank, world, device)
     n, E = res["n"], res["E"]
     value = n * world / (res["ms_step"] / 1e3)
     e2e_value = n * world / (res["ms_e2e"] / 1e3)

@@ -40,7 +40,7 @@ class IctdWeights(C.Structure):
 class SparseConfig(C.Structure):
     _fields_ = [("channels", I32), ("lmax", I32), ("num_interaction", I32), ("number_of_basis", I32),
                 ("basis_kind", I32), ("max_radius", C.c_float), ("num_species", I32), ("invariant_channels", I32),
-                ("n_hidden", I32), ("hidden", I32 * 4), ("n_out", I32)]
+                ("n_hidden", I32), ("hidden", I32 * 4), ("n_out", I32), ("avg_num_neighbors", C.c_float)]
 
 
 class SparseWeights(C.Structure):

@@ -1280,6 +1280,8 @@ int validate(const fsc_sparse_config* cfg) {
   if (cfg->num_species < 1 || cfg->num_species > 128) return fail(FSC_ERR_UNSUPPORTED, "num_species in [1, 128]");
   if (cfg->invariant_channels < 1) return fail(FSC_ERR_ARGUMENT, "invariant_channels must be >= 1");
   if (cfg->channels * cfg->num_interaction > 65535) return fail(FSC_ERR_UNSUPPORTED, "too many channels");
+  if (!(cfg->avg_num_neighbors >= 0.f) || !std::isfinite(cfg->avg_num_neighbors))
+    return fail(FSC_ERR_ARGUMENT, "avg_num_neighbors must be finite and >= 0");
   return FSC_OK;
 }
 
@@ -1449,6 +1451,12 @@ int by_cpl(int C, F f) {
   return f(std::integral_constant<int, 4>{});
 }
 
+// avg_num_neighbors of the conv2 layers: the caller's value, else E / N of this graph
+float conv2_norm(const Ctx& c) {
+  if (c.cfg->avg_num_neighbors > 0.f) return c.cfg->avg_num_neighbors;
+  return (float)std::max(1e-8, (double)c.p.E / (double)std::max<int64_t>(c.p.N, 1));
+}
+
 int forward(Ctx& c) {
   Plan& p = c.p;
   const fsc_graph* g = c.g;
@@ -1475,7 +1483,7 @@ int forward(Ctx& c) {
     }));
   }
   prof::mark("sparse_conv1_forward", st);
-  const float avg = (float)std::max(1e-8, (double)p.E / (double)std::max<int64_t>(p.N, 1));
+  const float avg = conv2_norm(c);
   for (int k = 1; k < p.nint; ++k) {
     for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
       const int64_t nc = std::min(p.chunk, p.N - n0);
@@ -1569,7 +1577,7 @@ int backward(Ctx& c) {
   prof::mark("sparse_readout_gram_backward", st);
   if (cudaMemsetAsync(p.dnp, 0, sizeof(float) * p.E * MAXR, st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset");
   Args a = args(c);
-  const float avg = (float)std::max(1e-8, (double)p.E / (double)std::max<int64_t>(p.N, 1));
+  const float avg = conv2_norm(c);
   for (int k = p.nint - 1; k >= 1; --k) {
     for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
       const int64_t nc = std::min(p.chunk, p.N - n0);

@@ -293,7 +293,12 @@ def decomposed_step(dec: Decomposition, rank: int, pos: torch.Tensor, species: t
     plan = yield from halo_exchange(dec, rank, pos, species)
     pos_l = torch.cat([pos, plan.ghost_pos.to(pos.dtype)])
     spec_l = torch.cat([species, plan.ghost_species.to(species.dtype)])
-    out = evaluate(pos_l, spec_l, n, dec.local_pbc)
+    counts = getattr(evaluate, "local_counts", None)
+    if counts is not None:  # an evaluator that needs whole-system sums of per-rank counts
+        totals = yield from all_reduce_sum(counts(pos_l, n, dec.local_pbc))
+        out = evaluate(pos_l, spec_l, n, dec.local_pbc, totals=totals)
+    else:
+        out = evaluate(pos_l, spec_l, n, dec.local_pbc)
     f = out["forces"]
     forces = yield from return_ghost_forces(plan, f[:n], f[n:])
     red = [out["energy"].reshape(1).to(torch.float64)]
@@ -391,4 +396,53 @@ def ictd_evaluator(engine, cell, cutoff: float, want_virial: bool = False, restr
             res["virial"] = out["virial"][0]
         return res
 
+    return evaluate
+
+
+def sparse_evaluator(engine, cell, cutoff: float, want_virial: bool = False) -> Evaluator:
+    """Evaluator of :func:`decomposed_step` backed by the native pure-cartesian-sparse engine:
+    GPU cell-list neighbour list of the local system, forward with ``num_local`` (owned atoms'
+    energies), reverse pass for the forces (and the virial).  Every layer runs on all local atoms
+    (the sparse engine has no receptive-field restriction); the owned energies are exact because
+    the halo covers the receptive field.
+
+    The reference's conv2 divides by E / N of the graph it is given
+    (``pure_cartesian_sparse_layers.py:418``); a rank's local graph has truncated neighbour lists
+    at the halo's edge, so the evaluator asks :func:`decomposed_step` for the whole system's
+    E / N: ``local_counts`` gives (edges into owned atoms, owned atoms), summed over ranks."""
+    from .neighbors import build_graph
+
+    dev = engine.device
+    cell_t = torch.as_tensor(np.asarray(cell), dtype=torch.float64, device=dev).reshape(1, 3, 3)
+    batch_cache = {}
+    graph = {}
+
+    def local_counts(pos, num_local, pbc):
+        g = build_graph(pos, cell_t, cutoff, pbc=pbc)
+        graph["g"], graph["key"] = g, (pos.data_ptr(), int(pos.shape[0]))
+        e_owned = g.row_ptr[num_local].to(torch.float64)  # edges are sorted by receiver, owned first
+        return torch.stack([e_owned, torch.tensor(float(num_local), dtype=torch.float64, device=e_owned.device)])
+
+    def evaluate(pos, species, num_local, pbc, totals=None):
+        if graph.get("key") == (pos.data_ptr(), int(pos.shape[0])):
+            g = graph.pop("g")
+            graph.pop("key")
+        else:
+            g = build_graph(pos, cell_t, cutoff, pbc=pbc)
+        n = int(pos.shape[0])
+        if n not in batch_cache:
+            batch_cache.clear()
+            batch_cache[n] = torch.zeros(n, dtype=torch.int32, device=dev)
+        avg = None
+        if totals is not None:
+            avg = max(float(totals[0]) / max(float(totals[1]), 1.0), 1e-8)
+        energy, atom_e = engine.forward(pos, species, batch_cache[n], cell_t, g, num_local=num_local,
+                                        avg_num_neighbors=avg)
+        out = engine.backward(want_virial=want_virial)
+        res = {"energy": energy[0], "forces": out["forces"], "atom_energy": atom_e}
+        if want_virial:
+            res["virial"] = out["virial"][0]
+        return res
+
+    evaluate.local_counts = local_counts
     return evaluate

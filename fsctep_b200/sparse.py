@@ -182,7 +182,10 @@ class SparseEngine:
         s.field = 0
         return s
 
-    def forward(self, pos, species, batch, cell, g: GraphCSR, num_local=None):
+    def forward(self, pos, species, batch, cell, g: GraphCSR, num_local=None, avg_num_neighbors=None):
+        """``avg_num_neighbors``: the conv2 normaliser; None = E / N of this graph (the reference's
+        per-call value).  The backward of this forward uses the same value."""
+        self.ncfg.avg_num_neighbors = 0.0 if avg_num_neighbors is None else float(avg_num_neighbors)
         pos = pos.detach().to(torch.float32).contiguous()
         species = species.to(torch.int32).contiguous()
         batch = batch.to(torch.int32).contiguous()

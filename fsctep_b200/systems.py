@@ -127,12 +127,21 @@ def diamond_block(block, dims, n_cells=(50, 50, 50), a=5.43, sigma=0.08, seed=0,
     decomposition, weak scaling: n_cells per rank).  Positions are wrapped into the global cell
     only along unsplit axes (dims == 1); along split axes a displaced atom stays next to its
     own block.  Returns the block's atoms and the global cell."""
+    return _lattice_block(DIAMOND_BASIS, block, dims, n_cells, a, sigma, seed, Z)
+
+
+def fcc_block(block, dims, n_cells=(50, 50, 25), a=3.61, sigma=0.1, seed=0, Z=29):
+    """One rank's block of an FCC crystal of dims * n_cells cells (as :func:`diamond_block`)."""
+    return _lattice_block(FCC_BASIS, block, dims, n_cells, a, sigma, seed, Z)
+
+
+def _lattice_block(basis, block, dims, n_cells, a, sigma, seed, Z):
     rng = np.random.default_rng(seed)
     nx, ny, nz = n_cells
     ii, jj, kk = np.meshgrid(np.arange(nx), np.arange(ny), np.arange(nz), indexing="ij")
     origins = np.stack([ii, jj, kk], axis=-1).reshape(-1, 1, 3).astype(np.float64)
     origins = origins + (np.asarray(block, dtype=np.float64) * np.asarray(n_cells))[None, None, :]
-    pos = ((origins + np.asarray(DIAMOND_BASIS)[None]) * a).reshape(-1, 3)
+    pos = ((origins + np.asarray(basis)[None]) * a).reshape(-1, 3)
     pos = pos + rng.normal(scale=sigma, size=pos.shape)
     L = np.asarray(n_cells, dtype=np.float64) * np.asarray(dims) * a
     for k in range(3):

@@ -347,6 +347,10 @@ typedef struct {
   int32_t n_hidden;
   int32_t hidden[4];
   int32_t n_out;             /* 17                                                */
+  float avg_num_neighbors;   /* conv2 normaliser: 0 = E / N of the call's graph, as the reference
+                                (pure_cartesian_sparse_layers.py:418); > 0 = this value (the
+                                whole system's E / N when a spatial-decomposition rank passes its
+                                local graph of owned atoms and ghosts)                        */
 } fsc_sparse_config;
 
 /* Packed fp32 device weights (host derives them from the reference state_dict):

@@ -88,3 +88,43 @@ def test_layer_atoms_contract_violation_is_reported():
     assert eng.status() == 70
     with pytest.raises(NAT.NativeError):
         eng.forward(pos, Z, torch.zeros_like(Z), cell, g, num_local=8, layer_atoms=[16, 32, 8])  # increasing
+
+
+@pytest.mark.parametrize("dims", [(2, 1, 1), (2, 2, 1)])
+def test_decomposed_sparse_engine_matches_single_domain(dims):
+    """The pure-cartesian-sparse engine behind the same decomposition (halo = 3 x cutoff)."""
+    from fsctep_b200.sparse import SparseConfig, SparseEngine
+    import golden_io
+
+    cfg, sd, _ = golden_io.sparse_case("b")  # lmax 3, FCC fixture weights
+    scfg = SparseConfig(channels=int(cfg["channels"]), lmax=int(cfg["lmax"]),
+                        num_interaction=int(cfg["num_interaction"]), number_of_basis=int(cfg["number_of_basis"]),
+                        max_radius=float(cfg["max_radius"]), function_type=str(cfg["function_type"]),
+                        max_atomvalue=int(cfg["max_atomvalue"]))
+    eng = SparseEngine(sd, scfg, "cuda")
+    s = systems.fcc_crystal(n_cells=(9, 9, 9), seed=43)
+    dev = torch.device("cuda")
+    pos, cell = torch.tensor(s["pos"], device=dev), torch.tensor(s["cell"], device=dev)
+    Z = torch.tensor(s["Z"], device=dev, dtype=torch.int32)
+    g = build_graph(pos, cell, 5.0)
+    ref = eng.energy_forces(pos, Z, torch.zeros_like(Z), cell, g)
+    ref_e = ref["energy"].double().item()
+    ref_f = ref["forces"].double().cpu().numpy()
+    ref_v = ref["virial"][0].double().cpu().numpy()
+
+    c0 = s["cell"][0]
+    dec = D.Decomposition(c0, dims, scfg.num_interaction * scfg.max_radius)
+    ev = D.sparse_evaluator(eng, c0, scfg.max_radius, want_virial=True)
+    owned = [_owned(dec, r, s["pos"], c0) for r in range(dec.world)]
+    gens = [D.decomposed_step(dec, r, pos[torch.tensor(o, device=dev)], Z[torch.tensor(o, device=dev)], ev,
+                              want_virial=True) for r, o in enumerate(owned)]
+    res = D.run_local(gens)
+    torch.cuda.synchronize()
+    assert eng.status() == 0
+    F = np.zeros_like(ref_f)
+    for o, r in zip(owned, res):
+        F[o] = r["forces"].double().cpu().numpy()
+        assert abs(r["energy"].item() - ref_e) <= 1e-5 * abs(ref_e), (r["energy"].item(), ref_e)
+        assert U.rel_max(r["virial"].cpu().numpy(), ref_v) <= 1e-4
+    assert U.rel_max(F, ref_f) <= 1e-4, U.rel_max(F, ref_f)
+    assert all(r["num_ghosts"] > 0 for r in res)
