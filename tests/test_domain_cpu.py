@@ -180,3 +180,61 @@ def test_gloo_two_ranks():
     import torch.multiprocessing as mp
 
     mp.spawn(_gloo_rank, args=(2, _free_port(), (2, 1, 1)), nprocs=2, join=True)
+
+
+def toy_avg_evaluate(cell, use_counts=True):
+    """A 2-hop potential whose messages are divided by the whole system's average in-degree
+    E / N, as the sparse model's conv2 (pure_cartesian_sparse_layers.py:418).  With
+    ``use_counts`` the evaluator asks decomposed_step for the per-rank (edges into owned atoms,
+    owned atoms) sums (``local_counts``); without it, it uses its local graph's E / N."""
+    cell_t = torch.tensor(cell, dtype=torch.float64)
+
+    def local_counts(pos, num_local, pbc):
+        _, dst, _ = ON.neighbor_list(pos.detach().numpy(), cell, RC, pbc=pbc)
+        return torch.tensor([float((dst < num_local).sum()), float(num_local)], dtype=torch.float64)
+
+    def evaluate(pos, species, num_local, pbc, totals=None):
+        src, dst, S = ON.neighbor_list(pos.detach().numpy(), cell, RC, pbc=pbc)
+        n = pos.shape[0]
+        avg = float(totals[0] / totals[1]) if totals is not None else len(src) / n
+        p = pos.detach().clone().requires_grad_(True)
+        src_t, dst_t = torch.tensor(src), torch.tensor(dst)
+        r = p[dst_t] - p[src_t] + torch.tensor(S, dtype=torch.float64) @ cell_t
+        r.retain_grad()
+        phi = (1.0 - r.norm(dim=1) / RC) ** 2
+        w = 1.0 + 0.1 * species.to(torch.float64)
+        m1 = torch.zeros(n, dtype=torch.float64).index_add(0, dst_t, phi * w[src_t]) / avg
+        m2 = torch.zeros(n, dtype=torch.float64).index_add(0, dst_t, phi * torch.tanh(0.3 * m1[src_t])) / avg
+        e = 0.01 * m2 ** 2 + 0.5 * m1 + 0.05 * m1 * m2
+        E = e[:num_local].sum()
+        E.backward()
+        return {"energy": E.detach(), "forces": -p.grad, "atom_energy": e.detach(), "virial": r.detach().T @ r.grad}
+
+    if use_counts:
+        evaluate.local_counts = local_counts
+    return evaluate
+
+
+@pytest.mark.parametrize("use_counts", [True, False])
+def test_whole_system_average_degree_reaches_every_rank(use_counts):
+    """decomposed_step sums the evaluator's local_counts over ranks before evaluating, so a
+    potential normalised by the whole system's E / N decomposes exactly; a rank's own E / N
+    (truncated neighbour lists at the halo's edge) does not."""
+    s = _system()
+    pos = torch.tensor(s["pos"], dtype=torch.float64)
+    ref = toy_avg_evaluate(s["cell"][0], use_counts=False)(pos, torch.tensor(s["Z"]), pos.shape[0], (True, True, True))
+    dec = D.Decomposition(s["cell"][0], (2, 1, 1), NHOP * RC)
+    ev = toy_avg_evaluate(s["cell"][0], use_counts)
+    owned = [_owned(dec, r, s) for r in range(dec.world)]
+    gens = [D.decomposed_step(dec, r, torch.tensor(s["pos"][o], dtype=torch.float64), torch.tensor(s["Z"][o]), ev)
+            for r, o in enumerate(owned)]
+    res = D.run_local(gens)
+    F = np.zeros_like(s["pos"])
+    for o, r in zip(owned, res):
+        F[o] = r["forces"].numpy()
+    rel = abs(res[0]["energy"].item() - ref["energy"].item()) / abs(ref["energy"].item())
+    if use_counts:
+        assert rel <= 1e-10
+        np.testing.assert_allclose(F, ref["forces"].numpy(), rtol=1e-9, atol=1e-10)
+    else:
+        assert rel > 1e-6
