@@ -46,3 +46,33 @@ def test_argument_errors_are_reported_not_raised_in_c():
     st = N.lib().fsc_project_bucket_forward(7, None, None, None, None, 1, 1, 1, 1, 1, 1, 1, None)
     assert st == 1
     assert b"dtype" in N.lib().fsc_last_error()
+
+
+def test_struct_layouts_agree_with_the_c_header(tmp_path):
+    """sizeof and field offsets of every ABI struct, as compiled from include/fsctep_b200.h by the C
+    compiler, equal the ctypes mirrors the host side passes by pointer."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    structs = {"fsc_ictd_config": N.IctdConfig, "fsc_ictd_weights": N.IctdWeights,
+               "fsc_sparse_config": N.SparseConfig, "fsc_sparse_weights": N.SparseWeights,
+               "fsc_graph": N.Graph, "fsc_ictd_outputs": N.IctdOutputs}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "fsctep_b200.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'  printf("{cname} sizeof %zu\\n", sizeof({cname}));')
+        for field, _ in py._fields_:
+            lines.append(f'  printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-std=c99", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    got = {(a, b): int(c) for a, b, c in (ln.split() for ln in out if ln)}
+    for cname, py in structs.items():
+        assert got[(cname, "sizeof")] == __import__("ctypes").sizeof(py), cname
+        for field, _ in py._fields_:
+            assert got[(cname, field)] == getattr(py, field).offset, (cname, field)
