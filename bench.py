@@ -210,6 +210,19 @@ TRAFFIC_PER_NODE = {
 }
 
 
+def fp32_context(roofline, clocks, sms=148):
+    """The dominant kernel's FP32 rate against the nominal CUDA-core FP32 peak (sms x 128 lanes x 2
+    FLOP x the median SM clock sampled during the timed region; no measured FP32 peak exists for
+    this pool).  Only for the CUDA-core kernels, which the HBM roofline undersells."""
+    if not roofline or roofline.get("bound") != "hbm" or roofline.get("algorithmic_tflops") is None:
+        return None
+    mhz = (clocks or {}).get("sm_mhz") or (clocks or {}).get("sm_max_mhz") or 1965.0
+    peak = sms * 128 * 2 * float(mhz) * 1e6 / 1e12
+    ach = float(roofline["algorithmic_tflops"])
+    return {"achieved_tflops": ach, "peak_tflops": peak, "frac": ach / peak, "sm_mhz": float(mhz),
+            "peak_source": f"nominal: {sms} SMs x 128 FP32 lanes x 2 FLOP x SM clock"}
+
+
 def run_native(args, rank, world, device):
     from fsctep_b200 import _native as NAT
     from fsctep_b200 import domain as D
@@ -588,6 +601,13 @@ def main():
                                 frac=ach / pk["bf16_tflops"], hbm_achieved_gbs=hbm,
                                 peak_source=pk["source"] + " bf16 dense (kind::f16 runs at the bf16 rate; useful "
                                 "FLOPs, the split issues 3 products per useful one)")
+    if roofline is not None:
+        try:
+            ctx = fp32_context(roofline, res["clocks"], torch.cuda.get_device_properties(device).multi_processor_count)
+        except Exception:  # reporting context only: never block the line
+            ctx = None
+        if ctx is not None:
+            roofline["fp32_simt"] = ctx
     line = {"metric": metric, "value": value, "unit": "atom-steps/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": res["ms_step"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded positions and weights)",

@@ -43,3 +43,13 @@ def test_sparse_stage_work(lmax, C):
     assert bwd_flops == pytest.approx(2 * edge + node)
     assert fwd_bytes > 0 and bwd_bytes > fwd_bytes
     assert bench.algorithmic_work("sparse_readout_gram_forward", N, E, cfg) is None
+
+
+def test_fp32_context():
+    roof = {"bound": "hbm", "algorithmic_tflops": 17.08}
+    ctx = bench.fp32_context(roof, {"sm_mhz": 1965.0})
+    assert ctx["peak_tflops"] == pytest.approx(148 * 128 * 2 * 1965e6 / 1e12)
+    assert ctx["frac"] == pytest.approx(17.08 / ctx["peak_tflops"])
+    assert bench.fp32_context(roof, {"sm_mhz": None, "reasons": ["no samples"]})["sm_mhz"] == 1965.0
+    assert bench.fp32_context({"bound": "tensor", "algorithmic_tflops": 300.0}, {"sm_mhz": 1965.0}) is None
+    assert bench.fp32_context(None, None) is None
