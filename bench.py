@@ -591,16 +591,18 @@ def main():
                       "traffic_source": "ncu si64k capture scaled by nodes" if tpn is not None else None,
                       "avg_launch_ms": avg_launch_ms, "algorithmic_bytes_per_launch": nbytes,
                       "algorithmic_tflops": ach}
-            if dom.startswith("conv2_edge") or dom.startswith("sparse_conv2"):
+            if dom.startswith("conv2_edge"):
                 # CUDA-core tensor-product kernels: reported against HBM (their inputs are L2-resident
                 # re-reads; the FP32 pipe and L1/shared-memory throughput are the real limits)
                 roofline = dict(common, bound="hbm", achieved=hbm, peak=pk["hbm_gbs"], unit="GB/s",
                                 frac=hbm / pk["hbm_gbs"], peak_source=pk["source"] + " HBM copy")
             else:
+                how = ("kind::tf32 3xTF32 contractions and fc.4 GEMMs (plus CUDA-core epilogues); useful FLOPs, "
+                       "the split issues 3 tf32 products per useful one" if dom.startswith("sparse_") else
+                       "kind::f16 runs at the bf16 rate; useful FLOPs, the split issues 3 products per useful one")
                 roofline = dict(common, bound="tensor", achieved=ach, peak=pk["bf16_tflops"], unit="TFLOP/s",
                                 frac=ach / pk["bf16_tflops"], hbm_achieved_gbs=hbm,
-                                peak_source=pk["source"] + " bf16 dense (kind::f16 runs at the bf16 rate; useful "
-                                "FLOPs, the split issues 3 products per useful one)")
+                                peak_source=pk["source"] + " bf16 dense (" + how + ")")
     if roofline is not None:
         try:
             ctx = fp32_context(roofline, res["clocks"], torch.cuda.get_device_properties(device).multi_processor_count)
