@@ -238,3 +238,22 @@ def test_whole_system_average_degree_reaches_every_rank(use_counts):
         np.testing.assert_allclose(F, ref["forces"].numpy(), rtol=1e-9, atol=1e-10)
     else:
         assert rel > 1e-6
+
+
+@pytest.mark.parametrize("make,per_cell", [(systems.diamond_block, 8), (systems.fcc_block, 4)])
+def test_lattice_blocks_tile_the_global_crystal(make, per_cell):
+    """Weak-scaling blocks: each rank's block holds its cells' atoms next to its own region of the
+    dims * n_cells crystal; unsplit axes are wrapped into the global cell."""
+    dims, cells = (2, 2, 1), (3, 3, 3)
+    blocks = [make(D.block_of(r, dims), dims, n_cells=cells, seed=r) for r in range(4)]
+    L = blocks[0]["cell"][0].diagonal()
+    for r, b in enumerate(blocks):
+        assert b["pos"].shape[0] == per_cell * 27
+        np.testing.assert_allclose(b["cell"][0].diagonal(), L)
+        lo = np.asarray(D.block_of(r, dims)) * L / np.asarray(dims)
+        hi = lo + L / np.asarray(dims)
+        for k in range(3):
+            if dims[k] > 1:  # thermal displacements stay within a fraction of a lattice constant
+                assert b["pos"][:, k].min() > lo[k] - 1.0 and b["pos"][:, k].max() < hi[k] + 1.0
+            else:
+                assert b["pos"][:, k].min() >= 0.0 and b["pos"][:, k].max() < L[k]
