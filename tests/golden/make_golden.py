@@ -22,7 +22,8 @@ Fixtures:
   of non-periodic molecules: energies, forces, per-atom energies and the heads' outputs.
 * ``sparse_{a,b}.npz`` -- the same for ``PureCartesianSparseTransformerLayer``
   (``pure_cartesian_sparse_layers.py``; max_rank_other 1, k_policy k0): a config-2-like water box
-  (Lmax 2) and a config-5-like FCC crystal (Lmax 3, with stress).
+  (Lmax 2) and a config-5-like FCC crystal (Lmax 3, with stress); ``sparse_{c,d}.npz`` the same
+  at configs 2 and 5's channel widths (C 64 / Lmax 2, C 128 / Lmax 3).
 * ``tp_ops.npz`` -- the ``_C_ictd_tp`` operator family evaluated by the reference's
   einsum references (``models/ictd_irreps_cuda.py:169-311``) on the shapes of
   ``test/test_ictd_tp_backend.py``.
@@ -232,6 +233,17 @@ def sparse():
     sparse_case("b", systems.fcc_crystal(n_cells=(3, 3, 3), seed=19), cfg5, seed=7)
 
 
+def sparse_widths():
+    """Configs 2 and 5's channel widths (the fixtures above are C 32): C 64 / Lmax 2 on a small
+    water box and C 128 / Lmax 3 on a 32-atom FCC crystal."""
+    cfg2 = dict(channels=64, lmax=2, num_interaction=3, number_of_basis=8, max_radius=5.0,
+                function_type="gaussian", max_atomvalue=10)
+    sparse_case("c", systems.water_box(n_side=3, box=9.3, seed=20), cfg2, seed=8)
+    cfg5 = dict(channels=128, lmax=3, num_interaction=3, number_of_basis=8, max_radius=5.0,
+                function_type="gaussian", max_atomvalue=30)
+    sparse_case("d", systems.fcc_crystal(n_cells=(2, 2, 2), seed=21), cfg5, seed=9)
+
+
 def tp_ops():
     from molecular_force_field.models import ictd_irreps_cuda as RC
 
@@ -269,6 +281,7 @@ def main():
     model_case("c", systems.diamond_crystal(n_cells=(2, 2, 2), seed=13, sigma=0.15), cfg_c, seed=3)
     o3()
     sparse()
+    sparse_widths()
 
 
 def o3():
@@ -284,5 +297,7 @@ if __name__ == "__main__":
         o3()
     elif len(sys.argv) > 1 and sys.argv[1] == "sparse":
         sparse()
+    elif len(sys.argv) > 1 and sys.argv[1] == "sparse_widths":
+        sparse_widths()
     else:
         main()
