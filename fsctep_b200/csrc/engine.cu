@@ -173,7 +173,7 @@ void layout(Plan& p, Arena& ar, const fsc_ictd_config* cfg, int64_t N, int64_t E
   p.edge_grad = ar.take<float>(E * 3);
   p.heads_d = ar.take<double>(4 * kMaxGraphs * 5);
   p.tc = g_readout_path == 0 && readout_tc_supported(p.nC, p.S);
-  p.gtc = g_gemm_path == 0;
+  p.gtc = g_gemm_path == 0 || g_gemm_path == 3;  // 3: tensor-core GEMMs with CUDA-core sparse aggregation
   for (int k = 0; k < 8; ++k)
     for (int l = 0; l < 3; ++l) p.img_fwd[k][l] = p.img_dz[k][l] = p.img_dx[k][l] = nullptr;
   for (int k = 0; k < 4; ++k) p.img_mnf[k] = p.img_mnb[k] = nullptr;
@@ -410,6 +410,7 @@ int forward(Ctx& c) {
       GemmArgs ga = gemm(p.chunkbuf, p.npairs, 0, Wp, p.npairs, 1, p.scalars + n0 * p.S, p.S, 0, nn, 1,
                          (int)p.npairs, p.S);
       ga.accumulate = 1;
+      ga.precise = 1;
       FSC_TRY(launch_gemm(ga, st));
     }
   }

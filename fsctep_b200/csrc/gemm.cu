@@ -31,7 +31,9 @@ __global__ void __launch_bounds__(256) gemm_kernel(GemmArgs a) {
   // B loads: k = tid / 16 (0..15), cols (tid % 16) * 4 .. +3
   const int bk = tid >> 4, bc = (tid & 15) * 4;
 
-  float acc[4][4] = {};
+  // Each K step of 16 is summed into a fresh partial; with a.precise the partials are added
+  // with Kahan compensation (long K with heavy cancellation, e.g. the readout Gram contraction).
+  float acc[4][4] = {}, comp[4][4] = {};
   for (int k0 = 0; k0 < a.K; k0 += GT_K) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -46,6 +48,7 @@ __global__ void __launch_bounds__(256) gemm_kernel(GemmArgs a) {
       Bs[bk][bc + j] = v;
     }
     __syncthreads();
+    float part[4][4] = {};
 #pragma unroll
     for (int k = 0; k < GT_K; ++k) {
       float av[4], bv[4];
@@ -56,8 +59,21 @@ __global__ void __launch_bounds__(256) gemm_kernel(GemmArgs a) {
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        for (int j = 0; j < 4; ++j) part[i][j] = fmaf(av[i], bv[j], part[i][j]);
     }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (a.precise) {
+          const float y = part[i][j] - comp[i][j];
+          const float t = acc[i][j] + y;
+          comp[i][j] = (t - acc[i][j]) - y;
+          acc[i][j] = t;
+        } else {
+          acc[i][j] += part[i][j];
+        }
+      }
     __syncthreads();
   }
 #pragma unroll

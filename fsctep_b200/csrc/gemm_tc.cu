@@ -10,9 +10,10 @@
 //  * 4 math warps: split the staged A in place into tf32 hi = round_tf32(a) and write lo =
 //    round_tf32(a - hi) to a second buffer of the same layout (elementwise, so the swizzle needs
 //    no decoding); after the last chunk they read the accumulators and write C;
-//  * MMA warp: per chunk 4 K-steps x (hi*hi, hi*lo, lo*hi) kind::tf32 MMAs (A and B from shared
-//    memory) into accumulator chunk % NACC, so no accumulator carries a long chain; the epilogue
-//    sums the NACC accumulators in fp32.
+//  * MMA warp: per chunk the 8 small products (hi*lo, lo*hi of 4 K-steps) and then the 4 hi*hi
+//    kind::tf32 MMAs (A and B from shared memory): the small terms accumulate before the large
+//    ones, so they are not truncated against the full magnitude (tensor-core accumulation rounds
+//    toward zero); no accumulator carries a long chain (see GCfg).
 // B images (hi / lo planes, K-major, no swizzle) are built from the weights by gemm_image_kernel.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -33,14 +34,17 @@ constexpr int MT = 128;                     // rows per tile
 constexpr uint32_t ABYTES = MT * KC * 4u;   // 16 KB
 constexpr int GT_THREADS = 6 * 32;          // 4 math warps, producer warp, MMA warp
 
-// NT <= 128 (FLUSH): every group of GC K-chunks (24 MMAs) accumulates into a fresh one of two TMEM
-// slots, which the math warps add to fp32 registers (tensor-core accumulation truncates, so long
-// chains over large K would bias the result).  Wider tiles (only used with K <= 128 here) rotate
-// the chunks over NACC accumulators summed in the epilogue.
-template <int NT>
+// NT <= 128 (FLUSH): every group of GC K-chunks (12 GC MMAs) accumulates into a fresh one of two
+// TMEM slots, which the math warps add to fp32 registers (tensor-core accumulation truncates, so
+// long chains over large K would bias the result).  PRECISE (long K with heavy cancellation, e.g.
+// the readout's Gram contraction): a fresh slot every chunk, and for NT <= 64 the register sums
+// are compensated (Kahan).  Wider tiles (gemm_tc_nt gives them only for K <= 128) rotate the
+// chunks over NACC accumulators summed in the epilogue.
+template <int NT, bool PRECISE = false>
 struct GCfg {
   static constexpr bool FLUSH = NT <= 128;
-  static constexpr int GC = 2;
+  static constexpr bool KAHAN = PRECISE && NT <= 64;
+  static constexpr int GC = PRECISE ? 1 : 2;
   static constexpr int NACC = FLUSH ? 2 : 2;
   static constexpr int NST = 2;
   static constexpr uint32_t BBYTES = 2u * KC * NT * 4u;  // hi + lo planes of one chunk
@@ -95,9 +99,9 @@ struct GemmTcArgs {
   int* err;
 };
 
-template <int NT>
+template <int NT, bool PRECISE>
 __global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, GemmTcArgs a) {
-  using CF = GCfg<NT>;
+  using CF = GCfg<NT, PRECISE>;
   constexpr int NST = CF::NST, NACC = CF::NACC;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -145,8 +149,11 @@ __global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_consta
     bool ok = true;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     float sum[CF::FLUSH ? NT : 1];
+    float comp[CF::KAHAN ? NT : 1];  // Kahan compensation of sum
 #pragma unroll
     for (int i = 0; i < (CF::FLUSH ? NT : 1); ++i) sum[i] = 0.f;
+#pragma unroll
+    for (int i = 0; i < (CF::KAHAN ? NT : 1); ++i) comp[i] = 0.f;
     auto flush = [&](int g) {  // FLUSH: add group g's slot to the fp32 sums and free it
       const int slot = g & 1;
       if (!(ok = tc::mbar_wait(grp_full + slot, (g >> 1) & 1, a.err, 86))) return;
@@ -156,8 +163,19 @@ __global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_consta
         uint32_t u[16];
         tc::tmem_ld16(tbase + (uint32_t)(slot * NT) + lane_off + 16u * cb, u);
         tc::tmem_wait_ld();
+        if (CF::KAHAN) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) sum[16 * cb + i] += __uint_as_float(u[i]);
+          for (int i = 0; i < 16; ++i) {
+            const int q = CF::KAHAN ? 16 * cb + i : 0;
+            const float y = __uint_as_float(u[i]) - comp[q];
+            const float t = sum[16 * cb + i] + y;
+            comp[q] = (t - sum[16 * cb + i]) - y;
+            sum[16 * cb + i] = t;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) sum[16 * cb + i] += __uint_as_float(u[i]);
+        }
       }
       tc::tc_fence_before();
       __syncwarp();
@@ -275,15 +293,20 @@ __global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_consta
         tc::tc_fence_after();
         const uint32_t d = tbase + (uint32_t)((CF::FLUSH ? (g & 1) : (c % NACC)) * NT);
 #pragma unroll
-        for (int j = 0; j < KC / 8; ++j) {
+        for (int j = 0; j < KC / 8; ++j) {  // small products first
           const uint64_t ah = desc_sw128(a0 + st * ABYTES + 32 * j);
           const uint64_t al = desc_sw128(l0 + st * ABYTES + 32 * j);
           const uint32_t bh_addr = b0 + st * CF::BBYTES + j * 2 * 16 * NT;
           const uint64_t bh = tc::smem_desc_kmajor(bh_addr, 16 * NT, 128);
           const uint64_t bl = tc::smem_desc_kmajor(bh_addr + CF::BBYTES / 2, 16 * NT, 128);
-          mma_tf32_ss(d, ah, bh, idesc, (!first || j > 0) ? 1u : 0u);
-          mma_tf32_ss(d, ah, bl, idesc, 1u);
+          mma_tf32_ss(d, ah, bl, idesc, (!first || j > 0) ? 1u : 0u);
           mma_tf32_ss(d, al, bh, idesc, 1u);
+        }
+#pragma unroll
+        for (int j = 0; j < KC / 8; ++j) {
+          const uint64_t ah = desc_sw128(a0 + st * ABYTES + 32 * j);
+          const uint64_t bh = tc::smem_desc_kmajor(b0 + st * CF::BBYTES + j * 2 * 16 * NT, 16 * NT, 128);
+          mma_tf32_ss(d, ah, bh, idesc, 1u);
         }
         tc::mma_commit(empty + st);
         if (CF::FLUSH && (c % CF::GC == CF::GC - 1 || c == nchunks - 1)) tc::mma_commit(grp_full + (g & 1));
@@ -573,12 +596,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-template <int NT>
+template <int NT, bool PRECISE>
 int launch_nt(const GemmArgs& g, const CUtensorMap& map, GemmTcArgs t, cudaStream_t st) {
-  const int sm = (int)GCfg<NT>::TOTAL;
-  cudaFuncSetAttribute(gemm_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  const int sm = (int)GCfg<NT, PRECISE>::TOTAL;
+  cudaFuncSetAttribute(gemm_tc_kernel<NT, PRECISE>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
   dim3 grid((unsigned)ceil_div(g.G, (int64_t)t.Gb), (unsigned)ceil_div(g.N, NT));
-  gemm_tc_kernel<NT><<<grid, GT_THREADS, sm, st>>>(map, t);
+  gemm_tc_kernel<NT, PRECISE><<<grid, GT_THREADS, sm, st>>>(map, t);
   return check_launch("gemm_tc_kernel");
 }
 
@@ -613,7 +636,12 @@ int launch_tp(const GemmArgs& g, const CUtensorMap& map, GemmTcArgs t, cudaStrea
 
 }  // namespace
 
-int gemm_tc_nt(int N) { return N <= 64 ? 64 : (N <= 128 ? 128 : (N <= 192 ? 192 : (N <= 256 ? 256 : 128))); }
+// Output tile width.  Tiles wider than 128 hold no fp32 register sums (their K chunks rotate over
+// two TMEM accumulators), so they are used only while those chains stay short (K <= 4 chunks).
+int gemm_tc_nt(int N, int K) {
+  if (N > 128 && K > 4 * KC) return 128;
+  return N <= 64 ? 64 : (N <= 128 ? 128 : (N <= 192 ? 192 : (N <= 256 ? 256 : 128)));
+}
 
 bool gemm_tc_supported(const GemmArgs& g) {
   if (g.K % 4 || g.K <= 0 || g.R < 1 || g.R > MT || g.N <= 0) return false;
@@ -624,7 +652,7 @@ bool gemm_tc_supported(const GemmArgs& g) {
 }
 
 int64_t gemm_image_floats(int K, int N) {
-  const int NT = gemm_tc_nt(N);
+  const int NT = gemm_tc_nt(N, K);
   return (int64_t)ceil_div(N, NT) * NT * ((K + KC - 1) / KC * KC) * 2;
 }
 
@@ -642,7 +670,7 @@ int GemmImageBatch::add(const float* B, int64_t ldb, int b_trans, int K, int N, 
   j.b_trans = b_trans;
   j.K = K;
   j.N = N;
-  j.NT = gemm_tc_nt(N);
+  j.NT = gemm_tc_nt(N, K);
   j.ntiles = (int)ceil_div(N, j.NT);
   j.out = out;
   return n == kMaxImageJobs ? flush(st) : FSC_OK;
@@ -663,7 +691,7 @@ int launch_gemm_tc(const GemmArgs& g, const float* bimg, int* err, cudaStream_t 
   const int64_t M = g.G * (int64_t)g.R;
   if (M == 0 || g.N == 0) return FSC_OK;
   if (!gemm_tc_supported(g)) return fail(FSC_ERR_UNSUPPORTED, "gemm_tc: unsupported shape or alignment");
-  const int NT = gemm_tc_nt(g.N);
+  const int NT = gemm_tc_nt(g.N, g.K);
   GemmTcArgs t{};
   t.bimg = bimg;
   t.K = g.K;
@@ -698,12 +726,34 @@ int launch_gemm_tc(const GemmArgs& g, const float* bimg, int* err, cudaStream_t 
       default: return launch_tp<256>(g, map, t, st);
     }
   }
+  if (g.precise) {
+    if (NT == 64) return launch_nt<64, true>(g, map, t, st);
+    if (NT == 128) return launch_nt<128, true>(g, map, t, st);
+  }
   switch (NT) {
-    case 64: return launch_nt<64>(g, map, t, st);
-    case 128: return launch_nt<128>(g, map, t, st);
-    case 192: return launch_nt<192>(g, map, t, st);
-    default: return launch_nt<256>(g, map, t, st);
+    case 64: return launch_nt<64, false>(g, map, t, st);
+    case 128: return launch_nt<128, false>(g, map, t, st);
+    case 192: return launch_nt<192, false>(g, map, t, st);
+    default: return launch_nt<256, false>(g, map, t, st);
   }
 }
 
 }  // namespace fsc
+
+extern "C" int fsc_gemm_tc_plan(int K, int N, int precise, int* tile_n, int* max_chain) {
+  using namespace fsc;
+  if (K <= 0 || N <= 0 || !tile_n || !max_chain) return fail(FSC_ERR_ARGUMENT, "fsc_gemm_tc_plan: bad arguments");
+  const int NT = gemm_tc_nt(N, K);
+  const int nchunks = (K + KC - 1) / KC;
+  constexpr int kPerChunk = 3 * (KC / 8);  // 3xTF32 MMAs per 32-wide K chunk
+  *tile_n = NT;
+  if (N <= NT && gemm_tcp_fits(NT, K)) {  // persistent kernel: chunk groups of gc chunks
+    const int nacc = std::min(nchunks, 256 / NT);
+    *max_chain = kPerChunk * ((nchunks + nacc - 1) / nacc);
+  } else if (NT <= 128) {  // flushed to fp32 registers every GC chunks
+    *max_chain = kPerChunk * std::min(nchunks, precise ? 1 : 2);
+  } else {  // chunks rotate over two accumulators
+    *max_chain = kPerChunk * ((nchunks + 1) / 2);
+  }
+  return FSC_OK;
+}

@@ -126,6 +126,7 @@ struct GemmArgs {
   const float* bias;
   int accumulate;
   float alpha;  // extra scale of the product (0 means 1)
+  int precise;  // long K with heavy cancellation: shortest tensor-core chains, compensated sums
 };
 int launch_gemm(const GemmArgs& a, cudaStream_t st);
 
@@ -133,7 +134,7 @@ int launch_gemm(const GemmArgs& a, cudaStream_t st);
 // B from a pre-formatted hi/lo image (gemm_image_kernel), 3xTF32.  Needs K % 4 == 0, A and its
 // row strides 16-byte aligned, rows of one group contiguous (a_rs >= K) when R > 1.
 bool gemm_tc_supported(const GemmArgs& a);
-int gemm_tc_nt(int N);
+int gemm_tc_nt(int N, int K);
 int64_t gemm_image_floats(int K, int N);
 int launch_gemm_tc(const GemmArgs& a, const float* bimg, int* err, cudaStream_t st);
 constexpr int kMaxImageJobs = 32;

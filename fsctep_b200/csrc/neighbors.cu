@@ -607,8 +607,14 @@ int fsc_csr_transpose_static(const int32_t* row_ptr, const int32_t* src, int64_t
                                       " atoms and " + std::to_string(kStaticMaxEdges) + " edges (got " +
                                       std::to_string(num_atoms) + ", " + std::to_string(num_edges) +
                                       "); use fsc_csr_transpose with a caller workspace");
-  if (scan_temp_bytes(num_atoms + 1) + 16 > kStaticScanBytes)
-    return fail(FSC_ERR_CAPACITY, "scan temporaries exceed the static scratch");
+  // the same arithmetic (per-block rounding included) that fsc_csr_transpose's arena applies
+  const size_t need = fsc_csr_transpose_workspace_bytes(num_atoms, num_edges);
+  if (need > kStaticScratchBytes)
+    return fail(FSC_ERR_CAPACITY, "fsc_csr_transpose_static: " + std::to_string(num_atoms) + " atoms and " +
+                                      std::to_string(num_edges) + " edges need " + std::to_string(need) +
+                                      " scratch bytes, more than the static " + std::to_string(kStaticScratchBytes) +
+                                      " (at most " + std::to_string(kStaticMaxAtoms) + " atoms and " +
+                                      std::to_string(kStaticMaxEdges) + " edges); use fsc_csr_transpose");
   void* scratch = nullptr;
   FSC_TRY(static_scratch(&scratch));
   // Same kernels and layout as fsc_csr_transpose; the counters are cleared on every call.

@@ -519,11 +519,11 @@ __global__ void __launch_bounds__(ZTC_THREADS, 2) z_tc_kernel(Args a, Rows rows,
           if (tid == 0) {
             tc::tc_fence_after();
             const int ksteps = kg > 0 ? min(ZTC_KC, kg - cc * ZTC_KC + 7) / 8 : 1;
-            for (int j = 0; j < ksteps; ++j) {
+            for (int j = 0; j < ksteps; ++j) {  // a fresh chain per chunk: at most 24 MMAs
               const uint32_t off = 32u * ZTC_N * (uint32_t)(cc * (ZTC_KC / 8) + j);
               const uint64_t dh = tc::smem_desc_kmajor(s_hi + off, 16u * ZTC_N, 128);
               const uint64_t dl = tc::smem_desc_kmajor(s_lo + off, 16u * ZTC_N, 128);
-              tc::mma_tf32_ts(tD, tAhi + 8u * j, dl, idesc, (cc > 0 || j > 0) ? 1u : 0u);
+              tc::mma_tf32_ts(tD, tAhi + 8u * j, dl, idesc, j > 0 ? 1u : 0u);
               tc::mma_tf32_ts(tD, tAlo + 8u * j, dh, idesc, 1u);
             }
             for (int j = 0; j < ksteps; ++j) {
@@ -542,26 +542,27 @@ __global__ void __launch_bounds__(ZTC_THREADS, 2) z_tc_kernel(Args a, Rows rows,
             ok = false;
             break;
           }
+          // ---- epilogue of the chunk -> Z[n][r][j][a]: half 0 columns [0, 32) and the bias column
+          // 64, half 1 [32, 64); later chunks and edge groups add in fp32
+          uint32_t u[48];
+          tc::tmem_ld32(tD + lane_off + 32u * half, u);
+          if (half == 0) tc::tmem_ld16(tD + lane_off + 64u, u + 32);
+          tc::tmem_wait_ld();
+          if (valid) {
+            float* zr = zn + (int64_t)r * J * C + ch + (int64_t)32 * half * C;
+            if (grp == 0 && cc == 0) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) zr[(int64_t)i * C] = __uint_as_float(u[i]);
+              if (half == 0) zr[(int64_t)RH * C] = __uint_as_float(u[32]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) zr[(int64_t)i * C] += __uint_as_float(u[i]);
+              if (half == 0) zr[(int64_t)RH * C] += __uint_as_float(u[32]);
+            }
+          }
+          tc::tc_fence_before();
         }
         if (!ok) break;
-        // ---- epilogue -> Z[n][r][j][a]: half 0 columns [0, 32) and the bias column 64, half 1 [32, 64)
-        uint32_t u[48];
-        tc::tmem_ld32(tD + lane_off + 32u * half, u);
-        if (half == 0) tc::tmem_ld16(tD + lane_off + 64u, u + 32);
-        tc::tmem_wait_ld();
-        if (valid) {
-          float* zr = zn + (int64_t)r * J * C + ch + (int64_t)32 * half * C;
-          if (grp == 0) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) zr[(int64_t)i * C] = __uint_as_float(u[i]);
-            if (half == 0) zr[(int64_t)RH * C] = __uint_as_float(u[32]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) zr[(int64_t)i * C] += __uint_as_float(u[i]);
-            if (half == 0) zr[(int64_t)RH * C] += __uint_as_float(u[32]);
-          }
-        }
-        tc::tc_fence_before();
       }
     }
   }
@@ -1260,6 +1261,7 @@ struct Plan {
   int* err;
   // tensor-core GEMM operand images of the weights (null: CUDA-core GEMM)
   bool gtc;
+  bool atc;  // per-node aggregation kernels (z / dm / dh) on tensor cores
   float* img_mix[8][4];    // conv2 layer k, Lout: fc.4 regrouped, forward
   float* img_mixT[8][4];   // its transpose (backward dZ)
   float* img_gf[4];        // packed Gram x W_read (forward), per L
@@ -1329,7 +1331,10 @@ void layout(Plan& p, Arena& ar, const fsc_sparse_config* cfg, int64_t N, int64_t
   p.edge_grad = ar.take<float>(E * 3);
   p.gbuf = ar.take<float>(p.gchunk * std::max<int64_t>(p.npairs, (int64_t)p.nC * p.nC));
   p.err = ar.take<int>(64);
-  p.gtc = gemm_path() == 0;
+  // gemm_path 0: both on tensor cores; 1: both on CUDA cores; 2: tensor-core aggregation with
+  // CUDA-core GEMMs; 3: CUDA-core aggregation with tensor-core GEMMs
+  p.gtc = gemm_path() == 0 || gemm_path() == 3;
+  p.atc = gemm_path() == 0 || gemm_path() == 2;
   for (int k = 0; k < 8; ++k)
     for (int L = 0; L < 4; ++L) p.img_mix[k][L] = p.img_mixT[k][L] = nullptr;
   for (int k = 0; k < 4; ++k) p.img_gf[k] = p.img_gb[k] = p.img_mnf[k] = p.img_mnb[k] = nullptr;
@@ -1487,7 +1492,7 @@ int forward(Ctx& c) {
   for (int k = 1; k < p.nint; ++k) {
     for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
       const int64_t nc = std::min(p.chunk, p.N - n0);
-      if (p.gtc) {
+      if (p.atc) {
         FSC_TRY(launch_z_tc(a, p.rows, p.feats[k - 1], p.h2 + (int64_t)k * p.E * RH, n0, nc, p.zbuf, p.err, st));
       } else {
         z_kernel<<<(unsigned)nc, 256, 0, st>>>(a, p.rows, p.feats[k - 1], p.h2 + (int64_t)k * p.E * RH, n0, p.zbuf);
@@ -1499,6 +1504,7 @@ int forward(Ctx& c) {
                            p.C, 0, p.feats[k] + (n0 * p.R + roff(Lo)) * p.C, (int64_t)p.R * p.C, p.C, nc, pow3(Lo),
                            K, p.C);
         ga.alpha = 1.f / avg;
+        ga.precise = 1;
         FSC_TRY(run_gemm(ga, p.img_mix[k][Lo], p.err, st));
       }
     }
@@ -1516,6 +1522,7 @@ int forward(Ctx& c) {
       FSC_TRY(check_launch("sparse gram_pack_kernel"));
       GemmArgs ga = gemm(p.gbuf, p.npairs, 0, Wp, p.npairs, 1, p.scalars + n0 * p.S, p.S, 0, nn, 1, (int)p.npairs, p.S);
       ga.accumulate = 1;
+      ga.precise = 1;  // K = nC (nC + 1) / 2 Gram pairs whose terms cancel heavily
       FSC_TRY(run_gemm(ga, p.img_gf[L], p.err, st));
     }
   }
@@ -1589,7 +1596,7 @@ int backward(Ctx& c) {
         ga.alpha = 1.f / avg;
         FSC_TRY(run_gemm(ga, p.img_mixT[k][Lo], p.err, st));
       }
-      if (p.gtc) {
+      if (p.atc) {
         FSC_TRY(launch_dm_tc(a, p.rows, p.feats[k - 1], p.h2 + (int64_t)k * p.E * RH, p.zbuf, n0, nc, p.grads[k - 1],
                              p.dnp, p.err, st));
       } else {
@@ -1597,7 +1604,7 @@ int backward(Ctx& c) {
                                                      n0, p.grads[k - 1], p.dnp);
         FSC_TRY(check_launch("sparse bwd_dm_kernel"));
       }
-      if (p.gtc) {
+      if (p.atc) {
         FSC_TRY(launch_dh_tc(a, p.rows, p.feats[k - 1], p.zbuf, n0, nc, p.dh2 + (int64_t)k * p.E * RH, p.err, st));
       } else {
         bwd_dh_kernel<<<(unsigned)nc, 256, 0, st>>>(a, p.rows, p.feats[k - 1], p.zbuf, n0,

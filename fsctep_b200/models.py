@@ -9,9 +9,10 @@ cell gradient that the trainer's strain-based stress needs), so
 ``torch.autograd.grad(E, pos)`` works as in ``evaluation/calculator.py:158-159``.
 
 Covered: lmax 2, path policy "full", channels 32/64, gaussian or bessel radial basis,
-no external tensor, no physical-tensor heads, no long-range / spectral modules, no
-``sync_after_scatter`` hook and no ``precomputed_edge_vec``.  Anything else raises
-``NotImplementedError`` (there is no CPU path to fall back to).
+no external tensor, no physical-tensor heads, no long-range / spectral modules.  With
+``precomputed_edge_vec`` (the LAMMPS ML-IAP call, ``interfaces/lammps_mliap.py:395-420, 745-760``)
+the energy depends on the given edge vectors only and is differentiable in them.  Anything else
+raises ``NotImplementedError`` (there is no CPU path to fall back to).
 """
 
 from __future__ import annotations
@@ -91,6 +92,52 @@ class _NativeEnergy(torch.autograd.Function):
         return gpos, gcell, None, None, None, None, None
 
 
+class _NativeEnergyEdgeVec(torch.autograd.Function):
+    """Per-atom energy from caller-given edge vectors (the reference's ``precomputed_edge_vec``,
+    ``pure_cartesian_ictd_layers_full.py:901-902``): the engine sees zero positions, identity
+    cells and shift = edge_vec, so r_e = edge_vec exactly; the backward returns dE/d(edge_vec) =
+    the engine's per-edge dE/dr_e, in the caller's edge order."""
+
+    @staticmethod
+    def forward(ctx, edge_vec, owner, graph, species, batch, num_graphs, field=None):
+        eng = owner._engine
+        pos0, eye = _edge_vec_frame(species.shape[0], num_graphs, edge_vec.device)
+        _, atom_e = eng.forward(pos0, species, batch, eye, graph, field=field)
+        ctx.owner, ctx.graph, ctx.species, ctx.batch, ctx.field = owner, graph, species, batch, field
+        ctx.num_graphs = num_graphs
+        ctx.generation = owner._bump()
+        ctx.vec_dtype = edge_vec.dtype
+        return atom_e.view(-1, 1).to(edge_vec.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_e):
+        owner, g = ctx.owner, ctx.graph
+        eng = owner._engine
+        if owner._generation != ctx.generation:
+            pos0, eye = _edge_vec_frame(ctx.species.shape[0], ctx.num_graphs, grad_e.device)
+            eng.forward(pos0, ctx.species, ctx.batch, eye, g, field=ctx.field)
+            owner._generation = ctx.generation
+        out = eng.backward(energy_weight=grad_e.reshape(-1), want_virial=False, want_edge_grad=True)
+        gvec = torch.empty_like(out["edge_grad"])
+        gvec[g.order] = out["edge_grad"]
+        return gvec.to(ctx.vec_dtype), None, None, None, None, None, None
+
+
+def _edge_vec_frame(n, num_graphs, device):
+    """Zero positions and identity cells: with shift = edge_vec the engine's r_e is edge_vec."""
+    pos0 = torch.zeros(n, 3, dtype=torch.float32, device=device)
+    eye = torch.eye(3, dtype=torch.float32, device=device).expand(num_graphs, 3, 3).contiguous()
+    return pos0, eye
+
+
+def _edge_vec_graph(edge_src, edge_dst, edge_vec, n):
+    if edge_vec.shape != (edge_src.shape[0], 3):
+        raise ValueError(f"precomputed_edge_vec must be (E, 3) = ({edge_src.shape[0]}, 3), got {tuple(edge_vec.shape)}")
+    if not edge_vec.is_cuda:
+        raise RuntimeError("fsctep_b200 runs on CUDA devices only (no CPU path)")
+    return GraphCSR.from_edges(edge_src.long(), edge_dst.long(), edge_vec.detach(), n)
+
+
 class PureCartesianICTDTransformerLayer(nn.Module):
     def __init__(self, max_embed_radius: float, main_max_radius: float, main_number_of_basis: int,
                  hidden_dim_conv: int, hidden_dim_sh=None, hidden_dim=None, channel_in2: int = 32,
@@ -168,10 +215,10 @@ class PureCartesianICTDTransformerLayer(nn.Module):
     def forward(self, pos, A, batch, edge_src, edge_dst, edge_shifts, cell, *, precomputed_edge_vec=None,
                 sync_after_scatter=None, external_tensor=None, external_tensor_blocks=None, fidelity_ids=None,
                 return_physical_tensors: bool = False, return_reciprocal_source: bool = False):
-        if precomputed_edge_vec is not None or sync_after_scatter is not None or external_tensor is not None \
+        if sync_after_scatter is not None or external_tensor is not None \
                 or external_tensor_blocks is not None or return_physical_tensors or return_reciprocal_source:
             raise NotImplementedError("fsctep_b200 pure-cartesian-ictd forward covers (pos, A, batch, edges, cell) "
-                                      "with no optional inputs")
+                                      "and precomputed_edge_vec")
         if not pos.is_cuda:
             raise RuntimeError("fsctep_b200 runs on CUDA devices only (no CPU path)")
         n = pos.shape[0]
@@ -182,6 +229,9 @@ class PureCartesianICTDTransformerLayer(nn.Module):
         if n and int(batch.max().item()) >= cell.shape[0]:
             raise IndexError("batch index out of range of cell")
         self._ensure_engine(pos.device)
+        if precomputed_edge_vec is not None:
+            graph = _edge_vec_graph(edge_src, edge_dst, precomputed_edge_vec, n)
+            return _NativeEnergyEdgeVec.apply(precomputed_edge_vec, self, graph, species, batch, cell.shape[0])
         graph = GraphCSR.from_edges(edge_src.long(), edge_dst.long(), edge_shifts, n)
         return _NativeEnergy.apply(pos, cell, self, graph, species, batch)
 
@@ -296,10 +346,10 @@ class PureCartesianICTDO3TransformerLayer(nn.Module):
     def forward(self, pos, A, batch, edge_src, edge_dst, edge_shifts, cell, *, precomputed_edge_vec=None,
                 sync_after_scatter=None, external_tensor=None, fidelity_ids=None,
                 return_physical_tensors: bool = False, return_reciprocal_source: bool = False):
-        if precomputed_edge_vec is not None or sync_after_scatter is not None or return_reciprocal_source \
-                or fidelity_ids is not None:
+        if sync_after_scatter is not None or return_reciprocal_source or fidelity_ids is not None:
             raise NotImplementedError("fsctep_b200 pure-cartesian-ictd-o3 forward: optional inputs other than "
-                                      "external_tensor / return_physical_tensors are not covered")
+                                      "precomputed_edge_vec / external_tensor / return_physical_tensors are not "
+                                      "covered")
         if not pos.is_cuda:
             raise RuntimeError("fsctep_b200 runs on CUDA devices only (no CPU path)")
         n = pos.shape[0]
@@ -313,8 +363,12 @@ class PureCartesianICTDO3TransformerLayer(nn.Module):
                 raise ValueError("external_tensor given but the model has no external tensor input")
             field = external_tensor.detach().reshape(-1, 3)
         eng = self._ensure_engine(pos.device)
-        graph = GraphCSR.from_edges(edge_src.long(), edge_dst.long(), edge_shifts, n)
-        e = _NativeEnergy.apply(pos, cell, self, graph, species, batch, field)
+        if precomputed_edge_vec is not None:
+            graph = _edge_vec_graph(edge_src, edge_dst, precomputed_edge_vec, n)
+            e = _NativeEnergyEdgeVec.apply(precomputed_edge_vec, self, graph, species, batch, cell.shape[0], field)
+        else:
+            graph = GraphCSR.from_edges(edge_src.long(), edge_dst.long(), edge_shifts, n)
+            e = _NativeEnergy.apply(pos, cell, self, graph, species, batch, field)
         if not return_physical_tensors:
             return e
         if self.physical_tensor_heads is None:
@@ -439,8 +493,11 @@ class PureCartesianSparseTransformerLayer(nn.Module):
     def forward(self, pos, A, batch, edge_src, edge_dst, edge_shifts, cell, *, precomputed_edge_vec=None,
                 external_tensor=None, fidelity_ids=None, return_physical_tensors: bool = False,
                 return_reciprocal_source: bool = False, **_unused):
-        if precomputed_edge_vec is not None or external_tensor is not None or fidelity_ids is not None \
-                or return_physical_tensors or return_reciprocal_source:
+        # The reference accepts precomputed_edge_vec here but never reads it (its forward always
+        # rebuilds the edge vectors from pos, shifts and cell, pure_cartesian_sparse_layers.py:745-756),
+        # and it swallows sync_after_scatter through **_unused: both are accepted and ignored alike.
+        if external_tensor is not None or fidelity_ids is not None or return_physical_tensors \
+                or return_reciprocal_source:
             raise NotImplementedError("fsctep_b200 pure-cartesian-sparse forward covers (pos, A, batch, edges, cell)")
         if not pos.is_cuda:
             raise RuntimeError("fsctep_b200 runs on CUDA devices only (no CPU path)")

@@ -310,8 +310,16 @@ void fsc_ictd_set_readout_path(int path);
 void fsc_ictd_set_radial_path(int path);
 /* Channel-mixing and MainNet GEMMs, and the pure-cartesian-sparse per-node aggregation kernels
  * (forward Z and its two reverse contractions): 0 = tensor cores (tcgen05, 3xTF32) where the
- * shape qualifies (default), 1 = CUDA-core kernels.  Process-wide. */
+ * shape qualifies (default), 1 = CUDA-core kernels, 2 = tensor-core aggregation with CUDA-core
+ * GEMMs, 3 = CUDA-core aggregation with tensor-core GEMMs.  Process-wide. */
 void fsc_ictd_set_gemm_path(int path);
+/* Plan of the tensor-core GEMM for a K x N product (host arithmetic, no device work): the output
+ * tile width and the longest chain of tcgen05.mma instructions that accumulate into one TMEM
+ * accumulator before the partial sum moves to fp32 registers (tensor-core accumulation rounds
+ * toward zero, so the engines keep these chains at <= 24).  `precise` selects the variant used
+ * for long K with heavy cancellation (the readout's Gram contraction).  No reference
+ * counterpart: a diagnostic of this library's accumulation order. */
+int fsc_gemm_tc_plan(int K, int N, int precise, int* tile_n, int* max_chain);
 /* Physical-tensor heads of the o3 model (pure_cartesian_ictd_layers_o3.py:1010-1044), from the
  * features left in the workspace by the last fsc_ictd_forward on it: for head h,
  *   out[h][b][m] = sum_{n in graph b} sum_c weights[h][c] * t_{block[h]}[n][c][m],  m < 2l+1,

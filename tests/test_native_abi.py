@@ -76,3 +76,16 @@ def test_struct_layouts_agree_with_the_c_header(tmp_path):
         assert got[(cname, "sizeof")] == __import__("ctypes").sizeof(py), cname
         for field, _ in py._fields_:
             assert got[(cname, field)] == getattr(py, field).offset, (cname, field)
+
+
+def test_static_transpose_capacity_checked_before_device_work():
+    """The allocation-free transpose rejects sizes beyond its static scratch with a capacity error
+    before any device call; at its stated limits the capacity check passes (on a machine without
+    a GPU the call then fails on the device query instead)."""
+    L = N.lib()
+    st = L.fsc_csr_transpose_static(None, None, 262144 + 1, 10, None, None, None)
+    assert st == 4 and b"at most" in L.fsc_last_error()
+    st = L.fsc_csr_transpose_static(None, None, 10, 4194304 + 1, None, None, None)
+    assert st == 4
+    st = L.fsc_csr_transpose_static(None, None, 262144, 4194304, None, None, None)
+    assert st != 4, L.fsc_last_error()
