@@ -9,9 +9,8 @@ reference semantics) + forward + hand-written backward (energy, forces).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
 
-``--impl reference`` times the reference algorithm's CPU path (the oracle port of the
-reference PyTorch implementation, fp32, all host threads) on a bounded replica of the same
-workload.  Under torchrun (N > 1) the crystal grows with N (weak scaling, 1,000,000 owned atoms
+``--impl reference`` times the reference's own CPU path (its PyTorch modules, installed unmodified
+under baseline/_ref, fp32, all host threads) on a bounded replica of the same workload.  Under torchrun (N > 1) the crystal grows with N (weak scaling, 1,000,000 owned atoms
 per GPU) and is cut into a (2, 1, 1) / (2, 2, 1) / (2, 2, 2) grid of blocks, one per rank: each
 step exchanges a 15 A halo of ghost positions, evaluates the owned atoms' energies and forces
 on the local system, returns the ghost forces to their owners and sums the energy
@@ -25,6 +24,7 @@ import json
 import os
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -44,7 +44,7 @@ WORKLOADS = {
     "fcc250k": dict(model="sparse", system="fcc", cells=(50, 50, 25), channels=128, lmax=3, num_interaction=3,
                     max_atomvalue=30, cpu_cells=(2, 2, 2)),
 }
-CPU_SAMPLE_CELLS = (6, 6, 6)  # 1,728-atom replica of the same crystal for the CPU baseline
+CPU_KEYS = ("value", "unit", "cores", "kind", "sample", "steps", "warmup", "statistic", "cpu_model")
 
 
 def peaks():
@@ -76,10 +76,10 @@ class ClockSampler:
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index):
+    def __init__(self, index, path=None):
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{index}.csv")
+        self.path = path or os.path.join(tempfile.mkdtemp(prefix="fsctep_clocks_"), f"clocks_rank{index}.csv")
 
     def __enter__(self):
         try:
@@ -223,8 +223,38 @@ def fp32_context(roofline, clocks, sms=148):
             "peak_source": f"nominal: {sms} SMs x 128 FP32 lanes x 2 FLOP x SM clock"}
 
 
-def run_native(args, rank, world, device):
+def timed_steps(args, world, step):
+    """args.steps steps between CUDA events on the launching stream, clocks sampled meanwhile;
+    no stage profiling inside."""
+    dev = torch.cuda.current_device() if world == 1 else int(os.environ.get("LOCAL_RANK", 0))
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev, args.clocks_csv) as clk:
+        t0.record()
+        for _ in range(args.steps):
+            step()
+        t1.record()
+        torch.cuda.synchronize()
+    return t0.elapsed_time(t1), clk.summary()
+
+
+def stage_pass(args, world, step):
+    """Per-stage CUDA-event times from a separate, untimed pass of the same steps."""
     from fsctep_b200 import _native as NAT
+
+    if world > 1:
+        torch.distributed.barrier()
+    stage_ms = {}
+    NAT.profile_enable(True)
+    for _ in range(args.steps):
+        step()
+        for name, ms in NAT.profile_read():
+            stage_ms.setdefault(name, []).append(ms)
+    NAT.profile_enable(False)
+    torch.cuda.synchronize()
+    return stage_ms
+
+
+def run_native(args, rank, world, device):
     from fsctep_b200 import domain as D
     from fsctep_b200 import systems
     from fsctep_b200.ictd import ICTDEngine
@@ -293,19 +323,8 @@ def run_native(args, rank, world, device):
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    NAT.profile_enable(True)
-    stage_ms = {}
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(torch.cuda.current_device() if world == 1 else int(os.environ.get("LOCAL_RANK", 0))) as clk:
-        t0.record()
-        for _ in range(args.steps):
-            step(pos_d, cell_d)
-            for name, ms in NAT.profile_read():
-                stage_ms.setdefault(name, []).append(ms)
-        t1.record()
-        torch.cuda.synchronize()
-    NAT.profile_enable(False)
-    ms_total = t0.elapsed_time(t1)
+    ms_total, clk = timed_steps(args, world, lambda: step(pos_d, cell_d))
+    stage_ms = stage_pass(args, world, lambda: step(pos_d, cell_d))
     if world > 1:
         torch.distributed.barrier()
     # end-to-end through the public API with host buffers
@@ -324,14 +343,13 @@ def run_native(args, rank, world, device):
         torch.distributed.all_reduce(ms_total_t, op=torch.distributed.ReduceOp.MAX)
     ms_total, ms_e2e = float(ms_total_t[0]), float(ms_total_t[1])
     return dict(n=n, E=E_edges, ms_step=ms_total / args.steps, ms_e2e=ms_e2e / args.steps, stage_ms=stage_ms,
-                clocks=clk.summary(), launches=None if ours is None else ours * args.steps, cfg=cfg,
+                clocks=clk, launches=None if ours is None else ours * args.steps, cfg=cfg,
                 ghosts=info["ghosts"], dims=dims)
 
 
 def run_sparse(args, rank, world, device):
     """pure-cartesian-sparse energy + forces (+ virial) of a seeded crystal or water box; under
     torchrun the FCC crystal grows with the ranks and is decomposed as the ictd workloads are."""
-    from fsctep_b200 import _native as NAT
     from fsctep_b200 import domain as D
     from fsctep_b200 import systems
     from fsctep_b200.neighbors import build_graph
@@ -395,20 +413,11 @@ def run_sparse(args, rank, world, device):
             step(pos_d, cell_d)
             torch.cuda.synchronize()
         ours = sum(e.count for e in prof.key_averages() if "fsc::" in e.key or "cub::" in e.key)
+    if world > 1:
+        torch.distributed.barrier()
     torch.cuda.synchronize()
-    NAT.profile_enable(True)
-    stage_ms = {}
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(torch.cuda.current_device() if world == 1 else int(os.environ.get("LOCAL_RANK", 0))) as clk:
-        t0.record()
-        for _ in range(args.steps):
-            step(pos_d, cell_d)
-            for name, ms in NAT.profile_read():
-                stage_ms.setdefault(name, []).append(ms)
-        t1.record()
-        torch.cuda.synchronize()
-    NAT.profile_enable(False)
-    ms_total = t0.elapsed_time(t1)
+    ms_total, clk = timed_steps(args, world, lambda: step(pos_d, cell_d))
+    stage_ms = stage_pass(args, world, lambda: step(pos_d, cell_d))
     if world > 1:
         torch.distributed.barrier()
     for _ in range(max(1, args.warmup // 2)):
@@ -424,72 +433,127 @@ def run_sparse(args, rank, world, device):
     if world > 1:
         torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
     return dict(n=n, E=info["edges"], ms_step=float(ms[0]) / args.steps, ms_e2e=float(ms[1]) / args.steps,
-                stage_ms=stage_ms, clocks=clk.summary(), launches=None if ours is None else ours * args.steps,
+                stage_ms=stage_ms, clocks=clk, launches=None if ours is None else ours * args.steps,
                 cfg=cfg, ghosts=info["ghosts"], dims=dims)
 
 
-def cpu_reference_sparse(w, steps, warmup):
-    """Time the oracle port of the reference sparse CPU path on a small replica of the workload."""
-    from oracle import neighbors as ON
-    from oracle import sparse_model as OS
-
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    cfg = sparse_cfg(w)
-    sd = {k: v.float() for k, v in sparse_weights(cfg).items()}
-    sysd = sparse_system(w, cpu=True)
-    src, dst, S = ON.neighbor_list(sysd["pos"], sysd["cell"][0], 5.0)
-    args = (torch.tensor(sysd["pos"], dtype=torch.float32), torch.tensor(sysd["Z"]), torch.tensor(sysd["batch"]),
-            torch.tensor(src), torch.tensor(dst), torch.tensor(S, dtype=torch.float32),
-            torch.tensor(sysd["cell"], dtype=torch.float32))
-    for _ in range(warmup):
-        OS.sparse_energy_forces_stress(sd, cfg, *args, want_stress=True)
-    times = []
-    for _ in range(steps):
-        t = time.perf_counter()
-        OS.sparse_energy_forces_stress(sd, cfg, *args, want_stress=True)
-        times.append(time.perf_counter() - t)
-    n = sysd["pos"].shape[0]
-    med = float(np.median(times))
-    return {"value": n / med, "unit": "atom-steps/s", "cores": threads, "kind": "port",
-            "sample": f"{n}-atom replica ({len(src)} edges) of the same model and system kind, fp32 PyTorch eager "
-                      f"(oracle port of the reference CPU path: per-edge fc.4 weights materialised), energy + forces "
-                      f"+ stress, median of {steps} steps after {warmup} warm-up, neighbour list excluded",
-            "seconds_per_step": med}
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+# CPU replicas (1/64 of the GPU workload's atoms where the reference can hold it in host memory;
+# the sparse reference materialises per-edge fc.4 weights, P x C x C floats per edge and layer)
+CPU_SAMPLES = {"si1m": (12, 12, 13), "si64k": (6, 6, 6), "water3k": 4, "fcc32k": (2, 2, 2), "fcc250k": (2, 2, 2)}
 
 
-def cpu_reference(steps, warmup, budget_s=None):
-    """Time the oracle port of the reference CPU path on a bounded replica of the workload."""
+def cpu_sample(workload):
+    """Seeded system of the CPU replica and a one-line description (shared by both CPU legs)."""
     from fsctep_b200 import systems
-    from oracle import ictd_model as OM
+
+    w = WORKLOADS[workload]
+    rep = CPU_SAMPLES[workload]
+    if w["model"] == "ictd":
+        sysd = systems.diamond_crystal(n_cells=rep, seed=1000, Z=w["Z"])
+        n = sysd["pos"].shape[0]
+        what = (f"{n}-atom diamond Si replica ({rep[0]}x{rep[1]}x{rep[2]} conventional cells, "
+                f"{n / (8 * np.prod(w['cells'])):.4f} of the GPU workload's atoms) of the same model")
+    elif w["system"] == "water":
+        sysd = systems.water_box(n_side=rep, box=w["box"] * rep / w["n_side"], seed=1000)
+        what = f"{rep ** 3}-molecule water box of the same density ({3 * rep ** 3} atoms) and model"
+    else:
+        sysd = systems.fcc_crystal(n_cells=rep, seed=1000)
+        what = f"{4 * int(np.prod(rep))}-atom FCC replica ({rep[0]}x{rep[1]}x{rep[2]} cells) of the same model"
+    return sysd, what
+
+
+def _reference_model(w, sd):
+    """The reference's own module (installed unmodified under baseline/_ref), fp32, seeded weights."""
+    from oracle import ref_import
+
+    ref_import.install(REF_DIR)
+    kw = dict(max_embed_radius=5.0, main_max_radius=5.0, main_number_of_basis=8, hidden_dim_conv=w["channels"],
+              hidden_dim_sh=32, hidden_dim=64, num_interaction=w["num_interaction"], function_type_main="gaussian",
+              max_atomvalue=w["max_atomvalue"], device=torch.device("cpu"))
+    if w["model"] == "ictd":
+        from molecular_force_field.models.pure_cartesian_ictd_layers_full import PureCartesianICTDTransformerLayer
+
+        m = PureCartesianICTDTransformerLayer(lmax=2, internal_compute_dtype=torch.float32, **kw)
+    else:
+        from molecular_force_field.models.pure_cartesian_sparse_layers import PureCartesianSparseTransformerLayer
+
+        m = PureCartesianSparseTransformerLayer(lmax=w["lmax"], **kw)
+    m = m.float()
+    m.load_state_dict({k: v.float() for k, v in sd.items()})
+    return m.eval()
+
+
+def cpu_reference(workload, steps, warmup):
+    """Time the reference's CPU path on the workload's CPU replica: its own PyTorch modules from
+    baseline/_ref (fp32 eager, all host threads); one step = forward + autograd forces (and the
+    strain derivative for the virial where the GPU step computes one), neighbour list excluded.
+    Without the installed reference, the oracle port of the same path is timed (kind "port")."""
     from oracle import neighbors as ON
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    w = WORKLOADS["si1m"]
-    cfg = model_cfg(w)
-    sd = {k: v.float() for k, v in seeded_weights(cfg).items()}
-    sysd = systems.diamond_crystal(n_cells=CPU_SAMPLE_CELLS, seed=1000, Z=w["Z"])
+    w = WORKLOADS[workload]
+    sparse = w["model"] == "sparse"
+    cfg = sparse_cfg(w) if sparse else model_cfg(w)
+    sd = sparse_weights(cfg) if sparse else seeded_weights(cfg)
+    sysd, what = cpu_sample(workload)
     src, dst, S = ON.neighbor_list(sysd["pos"], sysd["cell"][0], 5.0)
-    args = (torch.tensor(sysd["pos"], dtype=torch.float32), torch.tensor(sysd["Z"]), torch.tensor(sysd["batch"]),
-            torch.tensor(src), torch.tensor(dst), torch.tensor(S, dtype=torch.float32),
-            torch.tensor(sysd["cell"], dtype=torch.float32))
-    ocfg = OM.ICTDConfig(channels=cfg.channels, num_interaction=cfg.num_interaction, function_type="gaussian",
-                         max_atomvalue=cfg.max_atomvalue)
-    tabs = OM._TPTables(2, torch.float32)
+    pos0 = torch.tensor(sysd["pos"], dtype=torch.float32)
+    Z, b = torch.tensor(sysd["Z"]).long(), torch.tensor(sysd["batch"]).long()
+    src_t, dst_t, S_t = torch.tensor(src).long(), torch.tensor(dst).long(), torch.tensor(S, dtype=torch.float32)
+    cell = torch.tensor(sysd["cell"], dtype=torch.float32)
+    kind = "reference" if os.path.isdir(os.path.join(REF_DIR, "molecular_force_field")) else "port"
+    if kind == "reference":
+        model = _reference_model(w, sd)
+
+        def step():
+            pos = pos0.clone().requires_grad_(True)
+            if sparse:  # virial through the strain derivative (trainer convention)
+                strain = torch.zeros(1, 3, 3, requires_grad=True)
+                D = torch.eye(3) + 0.5 * (strain + strain.transpose(-1, -2))
+                e = model(pos @ D[0], Z, b, src_t, dst_t, S_t, torch.bmm(cell, D))
+                torch.autograd.grad(e.sum(), [pos, strain])
+            else:
+                e = model(pos, Z, b, src_t, dst_t, S_t, cell)
+                torch.autograd.grad(e.sum(), [pos])
+        how = "the reference's own PyTorch modules (baseline/_ref, unmodified; import shims: bare models package, " \
+              "torch_scatter -> its utils/scatter fallback, e3nn soft_one_hot_linspace restated)"
+    else:
+        from oracle import ictd_model as OM
+        from oracle import sparse_model as OS
+
+        sd32 = {k: v.float() for k, v in sd.items()}
+        args = (pos0, Z, b, src_t, dst_t, S_t, cell)
+        if sparse:
+            def step():
+                OS.sparse_energy_forces_stress(sd32, cfg, *args, want_stress=True)
+        else:
+            ocfg = OM.ICTDConfig(channels=cfg.channels, num_interaction=cfg.num_interaction, function_type="gaussian",
+                                 max_atomvalue=cfg.max_atomvalue)
+            tabs = OM._TPTables(2, torch.float32)
+
+            def step():
+                OM.energy_forces_stress(sd32, ocfg, *args, want_stress=False, tabs=tabs)
+        how = "the oracle port of the reference CPU path (the reference is not installed under baseline/_ref)"
     for _ in range(warmup):
-        OM.energy_forces_stress(sd, ocfg, *args, want_stress=False, tabs=tabs)
+        step()
     times = []
     for _ in range(steps):
         t = time.perf_counter()
-        OM.energy_forces_stress(sd, ocfg, *args, want_stress=False, tabs=tabs)
+        step()
         times.append(time.perf_counter() - t)
     n = sysd["pos"].shape[0]
     med = float(np.median(times))
-    return {"value": n / med, "unit": "atom-steps/s", "cores": threads, "kind": "port",
-            "sample": f"{n}-atom diamond replica ({CPU_SAMPLE_CELLS[0]}^3 cells, {len(src)} edges) of the same "
-                      f"model, fp32 PyTorch eager (oracle port of the reference CPU path), energy+forces, "
-                      f"median of {steps} steps after {warmup} warm-up, neighbour list excluded",
+    try:
+        cpu_model = next((ln.split(":", 1)[1].strip() for ln in open("/proc/cpuinfo") if ln.startswith("model name")),
+                         "unknown")
+    except OSError:
+        cpu_model = "unknown"
+    return {"value": n / med, "unit": "atom-steps/s", "cores": threads, "kind": kind,
+            "sample": f"{what}, {len(src)} edges; fp32 PyTorch eager, energy + forces"
+                      + (" + virial" if sparse else "") + f", neighbour list excluded; {how}",
+            "steps": steps, "warmup": warmup, "statistic": "median", "cpu_model": cpu_model,
             "seconds_per_step": med}
 
 
@@ -504,6 +568,8 @@ def main():
     ap.add_argument("--workload", default="si1m", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-launch-count", action="store_true", help="skip the torch.profiler launch count (for ncu)")
+    ap.add_argument("--clocks-csv", default=None, help="where to write the nvidia-smi clock samples (default: a "
+                                                        "temporary directory)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -549,15 +615,12 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        if sparse:
-            r = cpu_reference_sparse(w, max(1, min(args.steps, 3)), max(0, min(args.warmup, 1)))
-        else:
-            r = cpu_reference(max(1, args.steps), max(0, min(args.warmup, 1)))
+        r = cpu_reference(args.workload, max(1, min(args.steps, 5)), min(max(args.warmup, 0), 2))
         line = {"metric": metric, "value": r["value"], "unit": "atom-steps/s", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["seconds_per_step"] * 1e3,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic", "config": config, "impl": "reference",
-                "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "cpu_baseline": {k: r[k] for k in CPU_KEYS},
                 "e2e": {"value": r["value"], "unit": "atom-steps/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
@@ -620,8 +683,8 @@ def main():
                     "d2h_bytes_per_step": n * 3 * 4 + 4},
             "stages_ms": {k: round(v[0], 3) for k, v in sorted(stage_avg.items(), key=lambda kv: -kv[1][0])}}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        r = cpu_reference_sparse(w, 2, 1) if sparse else cpu_reference(2, 1)
-        line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        r = cpu_reference(args.workload, 3, 1)
+        line["cpu_baseline"] = {k: r[k] for k in CPU_KEYS}
     if rank == 0:
         print(json.dumps(line))
     if world > 1:

@@ -1,10 +1,10 @@
 """Generate the golden fixtures in this directory from the unmodified reference.
 
-Run where the reference tree is mounted (``FSCTEP_REFERENCE_ROOT``, default the
-container's read-only mount); the outputs are committed and the tests read only
-them, so nothing at test time needs the reference.
+Run where the reference source tree is available, with ``FSCTEP_REFERENCE_ROOT`` naming it;
+the outputs are committed and the tests read only them, so nothing at test time needs the
+reference.
 
-    python tests/golden/make_golden.py
+    FSCTEP_REFERENCE_ROOT=<reference tree> python tests/golden/make_golden.py
 
 Fixtures:
 
@@ -38,11 +38,12 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, HERE)
-import ref_shims  # noqa: E402
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+from oracle import ref_import  # noqa: E402
 
-ref_shims.install()
-sys.path.insert(0, ref_shims.REPO_ROOT)
+if "FSCTEP_REFERENCE_ROOT" not in os.environ:
+    raise SystemExit("set FSCTEP_REFERENCE_ROOT to the reference source tree")
+ref_import.install(os.environ["FSCTEP_REFERENCE_ROOT"])
 
 from fsctep_b200 import systems  # noqa: E402
 from fsctep_b200.weights import seeded_state_dict  # noqa: E402
