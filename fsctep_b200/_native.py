@@ -97,6 +97,12 @@ _PROTOS = {
     "fsc_ictd_backward": (C.c_int, [C.POINTER(IctdConfig), C.POINTER(IctdWeights), C.POINTER(Graph),
                                     C.POINTER(IctdOutputs), P, C.c_size_t, P]),
     "fsc_ictd_status": (C.c_int, [C.POINTER(IctdConfig), I64, I64, P, P, C.POINTER(C.c_int)]),
+    "fsc_ictd_forward_step": (C.c_int, [C.POINTER(IctdConfig), C.POINTER(IctdWeights), C.POINTER(Graph), C.c_int,
+                                        P, P, P, C.c_size_t, P]),
+    "fsc_ictd_backward_step": (C.c_int, [C.POINTER(IctdConfig), C.POINTER(IctdWeights), C.POINTER(Graph), C.c_int,
+                                         C.POINTER(IctdOutputs), P, C.c_size_t, P]),
+    "fsc_ictd_feature_buffer": (C.c_int, [C.POINTER(IctdConfig), I64, I64, P, C.c_int, C.c_int,
+                                          C.POINTER(C.c_void_p)]),
     "fsc_ictd_set_readout_path": (None, [C.c_int]),
     "fsc_sparse_workspace_bytes": (C.c_size_t, [C.POINTER(SparseConfig), I64, I64]),
     "fsc_sparse_forward": (C.c_int, [C.POINTER(SparseConfig), C.POINTER(SparseWeights), C.POINTER(Graph), P, P, P,

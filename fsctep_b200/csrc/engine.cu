@@ -348,12 +348,13 @@ RadialW radial(const fsc_ictd_weights* w) {
   return RadialW{w->rad_w1, w->rad_b1, w->rad_w2, w->rad_b2, w->rad_w3, w->rad_b3};
 }
 
-int forward(Ctx& c) {
+// Forward in steps (fsc_ictd_forward_step): 0 = edge geometry, radial MLPs and conv1; k in
+// [1, nint) = conv2 layer k; nint = readout.
+int forward_step0(Ctx& c) {
   Plan& p = c.p;
   const fsc_graph* g = c.g;
   const fsc_ictd_weights* w = c.w;
   cudaStream_t st = c.st;
-  const int C = p.C;
   prof::mark("begin", st);
   FSC_TRY(build_gemm_images(p, w, st));
   FSC_TRY(launch_edge_dst(g->row_ptr, p.dst, p.N, st));
@@ -374,20 +375,34 @@ int forward(Ctx& c) {
   prof::mark("edge_forward", st);
   FSC_TRY(launch_conv1_forward(conv_args(c, 0), w->ai, w->vsp, p.feats[0], st));
   prof::mark("conv1_forward", st);
-  for (int k = 1; k < p.nint; ++k) {
-    FSC_TRY(launch_conv2_z(conv_args(c, k), p.feats[k - 1], p.zbuf, st));
-    prof::mark("conv2_edge_forward", st);
-    const float* W = w->mix_fwd + (int64_t)(k - 1) * NP * C * C;
-    int64_t boff = 0;
-    for (int l3 = 0; l3 < 3; ++l3) {
-      GemmArgs ga = gemm(p.zbuf + OFF3(l3) * C, NZ * C, NP3(l3) * C, W + boff, C, 0, p.feats[k] + KB(l3) * C,
-                         NK * C, C, p.nk[k], 2 * l3 + 1, NP3(l3) * C, C);
-      ga.deg_rowptr = g->row_ptr;
-      FSC_TRY(run_gemm(ga, p.img_fwd[k][l3], p.err, st));
-      boff += (int64_t)NP3(l3) * C * C;
-    }
-    prof::mark("conv2_mix_forward", st);
+  return FSC_OK;
+}
+
+int forward_conv2(Ctx& c, int k) {
+  Plan& p = c.p;
+  const fsc_graph* g = c.g;
+  const fsc_ictd_weights* w = c.w;
+  cudaStream_t st = c.st;
+  const int C = p.C;
+  FSC_TRY(launch_conv2_z(conv_args(c, k), p.feats[k - 1], p.zbuf, st));
+  prof::mark("conv2_edge_forward", st);
+  const float* W = w->mix_fwd + (int64_t)(k - 1) * NP * C * C;
+  int64_t boff = 0;
+  for (int l3 = 0; l3 < 3; ++l3) {
+    GemmArgs ga = gemm(p.zbuf + OFF3(l3) * C, NZ * C, NP3(l3) * C, W + boff, C, 0, p.feats[k] + KB(l3) * C,
+                       NK * C, C, p.nk[k], 2 * l3 + 1, NP3(l3) * C, C);
+    ga.deg_rowptr = g->row_ptr;
+    FSC_TRY(run_gemm(ga, p.img_fwd[k][l3], p.err, st));
+    boff += (int64_t)NP3(l3) * C * C;
   }
+  prof::mark("conv2_mix_forward", st);
+  return FSC_OK;
+}
+
+int forward_readout(Ctx& c) {
+  Plan& p = c.p;
+  const fsc_ictd_weights* w = c.w;
+  cudaStream_t st = c.st;
   // readout scalars: packed Gram x symmetrised W_read
   ReadoutArgs ra = readout_args(c);
   if (p.tc) {
@@ -431,7 +446,10 @@ int forward(Ctx& c) {
   return FSC_OK;
 }
 
-int backward(Ctx& c) {
+// Backward in steps (fsc_ictd_backward_step): nint = readout backward (every layer's feature
+// gradient from the readout); k in [1, nint) = conv2 layer k backward (adds into layer k - 1's
+// gradient); 0 = conv1 backward (then the edge part, run_backward_edges).
+int backward_readout(Ctx& c) {
   Plan& p = c.p;
   const fsc_graph* g = c.g;
   const fsc_ictd_weights* w = c.w;
@@ -474,7 +492,16 @@ int backward(Ctx& c) {
         cudaMemsetAsync(p.grads[k] + p.nro * NK * C, 0, sizeof(float) * (p.nk[k] - p.nro) * NK * C, st) != cudaSuccess)
       return fail(FSC_ERR_CUDA, "memset grads");
   if (cudaMemsetAsync(p.dY, 0, sizeof(float) * p.E * 12, st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset dY");
-  for (int k = p.nint - 1; k >= 1; --k) {
+  return FSC_OK;
+}
+
+int backward_conv2(Ctx& c, int k) {
+  Plan& p = c.p;
+  const fsc_graph* g = c.g;
+  const fsc_ictd_weights* w = c.w;
+  cudaStream_t st = c.st;
+  const int C = p.C;
+  {
     ConvArgs ca = conv_args(c, k);
     // dZ = (1/deg) G_k x W   (l3 blocks)
     const float* Wb = w->mix_bwd + (int64_t)(k - 1) * NP * C * C;
@@ -506,6 +533,13 @@ int backward(Ctx& c) {
     }
     prof::mark("conv2_mix_backward_dx", st);
   }
+  return FSC_OK;
+}
+
+int backward_conv1(Ctx& c) {
+  Plan& p = c.p;
+  const fsc_ictd_weights* w = c.w;
+  cudaStream_t st = c.st;
   ConvArgs c1 = conv_args(c, 0);
   c1.N = p.N;
   FSC_TRY(launch_conv1_backward(c1, w->ai, w->vsp, p.grads[0], p.dgates, p.dY, st));
@@ -592,11 +626,15 @@ int prepare(Ctx& c, void* workspace, size_t bytes) {
   return FSC_OK;
 }
 
-int run_forward(Ctx& c, float* energy, float* atom_energy) {
-  if (cudaMemsetAsync(c.p.energy_d, 0, sizeof(double) * kMaxGraphs * 19, c.st) != cudaSuccess ||
-      cudaMemsetAsync(c.p.err, 0, sizeof(int) * 64, c.st) != cudaSuccess)
-    return fail(FSC_ERR_CUDA, "memset accumulators");
-  FSC_TRY(forward(c));
+int run_forward_step(Ctx& c, int step, float* energy, float* atom_energy) {
+  if (step == 0) {
+    if (cudaMemsetAsync(c.p.energy_d, 0, sizeof(double) * kMaxGraphs * 19, c.st) != cudaSuccess ||
+        cudaMemsetAsync(c.p.err, 0, sizeof(int) * 64, c.st) != cudaSuccess)
+      return fail(FSC_ERR_CUDA, "memset accumulators");
+    return forward_step0(c);
+  }
+  if (step < c.p.nint) return forward_conv2(c, step);
+  FSC_TRY(forward_readout(c));
   const int H = c.p.hidden[c.p.n_hidden - 1];
   float* ebuf = atom_energy ? atom_energy : c.p.dxb;  // dxb is free until the backward starts
   FSC_TRY(launch_energy(c.p.act_post[c.p.n_hidden - 1], c.p.nro, H, c.w->out_v, c.w->out_c0, c.g->batch,
@@ -616,9 +654,28 @@ int run_forward(Ctx& c, float* energy, float* atom_energy) {
   return FSC_OK;
 }
 
+int run_forward(Ctx& c, float* energy, float* atom_energy) {
+  for (int step = 0; step <= c.p.nint; ++step) FSC_TRY(run_forward_step(c, step, energy, atom_energy));
+  return FSC_OK;
+}
+
+int run_backward_edges(Ctx& c, fsc_ictd_outputs* out);
+
+int run_backward_step(Ctx& c, int step, fsc_ictd_outputs* out) {
+  if (step == c.p.nint) return backward_readout(c);
+  if (step > 0) return backward_conv2(c, step);
+  FSC_TRY(backward_conv1(c));
+  return run_backward_edges(c, out);
+}
+
 int run_backward(Ctx& c, fsc_ictd_outputs* out) {
+  for (int step = c.p.nint; step >= 0; --step) FSC_TRY(run_backward_step(c, step, out));
+  return FSC_OK;
+}
+
+// radial / direction backward, forces, virial and cell gradient from dgates and dY
+int run_backward_edges(Ctx& c, fsc_ictd_outputs* out) {
   const fsc_graph* g = c.g;
-  FSC_TRY(backward(c));
   EdgeBwdArgs eb{};
   eb.E = c.p.E; eb.src = g->src; eb.batch = g->batch; eb.tables = c.w->tables; eb.rad = radial(c.w);
   eb.nint = c.p.nint; eb.nb = c.p.nb; eb.basis_kind = c.cfg->basis_kind; eb.rc = c.cfg->max_radius;
@@ -715,6 +772,36 @@ int fsc_ictd_energy_forces(const fsc_ictd_config* cfg, const fsc_ictd_weights* w
   FSC_TRY(fsc::prepare(c, workspace, workspace_bytes));
   FSC_TRY(fsc::run_forward(c, out->energy, out->atom_energy));
   return fsc::run_backward(c, out);
+}
+
+int fsc_ictd_forward_step(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g, int step,
+                          float* energy, float* atom_energy, void* workspace, size_t workspace_bytes, void* stream) {
+  fsc::Ctx c{cfg, w, g, fsc::Plan{}, fsc::as_stream(stream)};
+  FSC_TRY(fsc::prepare(c, workspace, workspace_bytes));
+  FSC_REQUIRE(step >= 0 && step <= c.p.nint, "forward step out of range [0, num_interaction]");
+  return fsc::run_forward_step(c, step, energy, atom_energy);
+}
+
+int fsc_ictd_backward_step(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g, int step,
+                           fsc_ictd_outputs* out, void* workspace, size_t workspace_bytes, void* stream) {
+  fsc::Ctx c{cfg, w, g, fsc::Plan{}, fsc::as_stream(stream)};
+  FSC_TRY(fsc::prepare(c, workspace, workspace_bytes));
+  FSC_REQUIRE(step >= 0 && step <= c.p.nint, "backward step out of range [0, num_interaction]");
+  FSC_REQUIRE(step > 0 || out != nullptr, "outputs required for backward step 0");
+  return fsc::run_backward_step(c, step, out);
+}
+
+int fsc_ictd_feature_buffer(const fsc_ictd_config* cfg, int64_t num_atoms, int64_t num_edges, void* workspace,
+                            int which, int layer, float** out) {
+  FSC_REQUIRE(out && workspace, "workspace and output pointer required");
+  FSC_TRY(fsc::validate(cfg));
+  FSC_REQUIRE(which == 0 || which == 1, "which must be 0 (features) or 1 (gradients)");
+  FSC_REQUIRE(layer >= 0 && layer < cfg->num_interaction, "layer out of range");
+  fsc::Plan p{};
+  fsc::Arena ar(workspace, (size_t)-1);
+  fsc::layout(p, ar, cfg, num_atoms, num_edges);
+  *out = which == 0 ? p.feats[layer] : p.grads[layer];
+  return FSC_OK;
 }
 
 int fsc_ictd_energy(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g, float* energy,

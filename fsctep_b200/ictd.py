@@ -437,6 +437,82 @@ class ICTDEngine:
         self._field_dev = fdev
         return energy, atom_e
 
+    def feature_buffer(self, which: int, layer: int):
+        """View (num_atoms, 9, C) of layer ``layer``'s node features (which = 0) or of their
+        gradient (which = 1) in the workspace of the last call (rows l^2 + m, channel innermost)."""
+        g = self._last[4]
+        ws = self.workspace(g.num_atoms, g.num_edges)
+        addr = C.c_void_p(0)
+        N.check(N.lib().fsc_ictd_feature_buffer(C.byref(self.ncfg), g.num_atoms, g.num_edges, N.ptr(ws), which,
+                                                layer, C.byref(addr)), "fsc_ictd_feature_buffer")
+        off = int(addr.value) - ws.data_ptr()
+        nbytes = g.num_atoms * 9 * self.cfg.channels * 4
+        return ws[off:off + nbytes].view(torch.float32).view(g.num_atoms, 9, self.cfg.channels)
+
+    def forward_layers(self, pos, species, batch, cell, g: GraphCSR, on_layer, num_local=None, field=None):
+        """:meth:`forward` in steps: after interaction layer k's features are written,
+        ``on_layer(k, feats)`` may rewrite ``feats`` (a (num_atoms, 9, C) view, see
+        :meth:`feature_buffer`) in place on the current stream before layer k + 1 reads them (the
+        reference's sync_after_scatter points, ``pure_cartesian_ictd_layers_full.py:923-953``)."""
+        pos, species, batch, cell = self._inputs(pos, species, batch, cell)
+        B = cell.shape[0]
+        ws = self.workspace(g.num_atoms, g.num_edges)
+        energy = torch.empty(B, dtype=torch.float32, device=self.device)
+        atom_e = torch.empty(g.num_atoms, dtype=torch.float32, device=self.device)
+        fdev = self._field(field, B)
+        gs = self._graph(pos, species, batch, cell, g, B, num_local, None, fdev, None)
+        self._last = (pos, species, batch, cell, g, num_local)
+        self._last_layers = None
+        self._field_dev = fdev
+        nint = self.cfg.num_interaction
+        for step in range(nint + 1):
+            last = step == nint
+            N.check(N.lib().fsc_ictd_forward_step(C.byref(self.ncfg), C.byref(self.weights.struct), C.byref(gs), step,
+                                                  N.ptr(energy) if last else None, N.ptr(atom_e) if last else None,
+                                                  N.ptr(ws), ws.numel(), N.stream_ptr(self.device)),
+                    f"fsc_ictd_forward_step({step})")
+            if not last:
+                on_layer(step, self.feature_buffer(0, step))
+        return energy, atom_e
+
+    def backward_layers(self, on_grad, energy_weight=None, want_virial=True, want_cell_grad=False,
+                        want_edge_grad=False):
+        """:meth:`backward` in steps: before the reverse pass of interaction layer k reads the
+        complete gradient of layer k's features, ``on_grad(k, grads)`` may rewrite it in place
+        (the adjoint of the forward's ``on_layer``)."""
+        pos, species, batch, cell, g, num_local = self._last
+        B = cell.shape[0]
+        ws = self.workspace(g.num_atoms, g.num_edges)
+        out, o = self._outputs(g, B, want_virial, want_cell_grad, want_edge_grad)
+        if energy_weight is not None:
+            energy_weight = energy_weight.detach().to(torch.float32).reshape(-1).contiguous()
+        gs = self._graph(pos, species, batch, cell, g, B, num_local, energy_weight, getattr(self, "_field_dev", None),
+                         None)
+        nint = self.cfg.num_interaction
+        for step in range(nint, -1, -1):
+            if step < nint:
+                on_grad(step, self.feature_buffer(1, step))
+            N.check(N.lib().fsc_ictd_backward_step(C.byref(self.ncfg), C.byref(self.weights.struct), C.byref(gs),
+                                                   step, C.byref(o), N.ptr(ws), ws.numel(),
+                                                   N.stream_ptr(self.device)), f"fsc_ictd_backward_step({step})")
+        return out
+
+    def _outputs(self, g, B, want_virial, want_cell_grad, want_edge_grad):
+        dev = self.device
+        out = {"forces": torch.empty(g.num_atoms, 3, dtype=torch.float32, device=dev)}
+        if want_virial:
+            out["virial"] = torch.empty(B, 3, 3, dtype=torch.float32, device=dev)
+        if want_cell_grad:
+            out["cell_grad"] = torch.empty(B, 3, 3, dtype=torch.float32, device=dev)
+        if want_edge_grad:
+            out["edge_grad"] = torch.empty(g.num_edges, 3, dtype=torch.float32, device=dev)
+        o = N.IctdOutputs()
+        o.forces = out["forces"].data_ptr()
+        o.virial = out["virial"].data_ptr() if want_virial else 0
+        o.cell_grad = out["cell_grad"].data_ptr() if want_cell_grad else 0
+        o.edge_grad = out["edge_grad"].data_ptr() if want_edge_grad else 0
+        return out, o
+
     def heads(self):
         """Physical-tensor heads of the last forward (o3 model): {name: {l: (B, 1, 2l+1)}}."""
         w = self.weights
@@ -463,22 +539,11 @@ class ICTDEngine:
         B = cell.shape[0]
         ws = self.workspace(g.num_atoms, g.num_edges)
         dev = self.device
-        out = {"forces": torch.empty(g.num_atoms, 3, dtype=torch.float32, device=dev)}
-        if want_virial:
-            out["virial"] = torch.empty(B, 3, 3, dtype=torch.float32, device=dev)
-        if want_cell_grad:
-            out["cell_grad"] = torch.empty(B, 3, 3, dtype=torch.float32, device=dev)
-        if want_edge_grad:
-            out["edge_grad"] = torch.empty(g.num_edges, 3, dtype=torch.float32, device=dev)
+        out, o = self._outputs(g, B, want_virial, want_cell_grad, want_edge_grad)
         if energy_weight is not None:
             energy_weight = energy_weight.detach().to(torch.float32).reshape(-1).contiguous()
         gs = self._graph(pos, species, batch, cell, g, B, num_local, energy_weight, getattr(self, "_field_dev", None),
                          getattr(self, "_last_layers", None))
-        o = N.IctdOutputs()
-        o.forces = out["forces"].data_ptr()
-        o.virial = out["virial"].data_ptr() if want_virial else 0
-        o.cell_grad = out["cell_grad"].data_ptr() if want_cell_grad else 0
-        o.edge_grad = out["edge_grad"].data_ptr() if want_edge_grad else 0
         N.check(N.lib().fsc_ictd_backward(C.byref(self.ncfg), C.byref(self.weights.struct), C.byref(gs), C.byref(o),
                                           N.ptr(ws), ws.numel(), N.stream_ptr(dev)), "fsc_ictd_backward")
         return out

@@ -11,8 +11,11 @@ cell gradient that the trainer's strain-based stress needs), so
 Covered: lmax 2, path policy "full", channels 32/64, gaussian or bessel radial basis,
 no external tensor, no physical-tensor heads, no long-range / spectral modules.  With
 ``precomputed_edge_vec`` (the LAMMPS ML-IAP call, ``interfaces/lammps_mliap.py:395-420, 745-760``)
-the energy depends on the given edge vectors only and is differentiable in them.  Anything else
-raises ``NotImplementedError`` (there is no CPU path to fall back to).
+the energy depends on the given edge vectors only and is differentiable in them.
+``sync_after_scatter`` (``cli/inference_ddp.py:143-340``) is called after conv1 and after every
+conv2 scatter on the node features in the reference layout, through the engine's stepwise
+evaluation, and its vector-Jacobian product enters the native reverse pass.  Anything else raises
+``NotImplementedError`` (there is no CPU path to fall back to).
 """
 
 from __future__ import annotations
@@ -67,60 +70,112 @@ class _WeightedSum(nn.Module):
 
 
 class _NativeEnergy(torch.autograd.Function):
+    """Per-atom energy of the native engine, differentiable in ``pos`` and ``cell`` -- or, with
+    ``edge_vec`` (the reference's ``precomputed_edge_vec``, ``pure_cartesian_ictd_layers_full.py:
+    901-902``), in the given edge vectors only: the engine then sees zero positions, identity cells
+    and shift = edge_vec, so r_e = edge_vec exactly, and dE/d(edge_vec) is its per-edge dE/dr_e in
+    the caller's edge order.  ``hook`` is the reference's ``sync_after_scatter``: it is called on
+    every layer's node features in the reference layout and its vector-Jacobian product is
+    applied to their gradient in the reverse pass."""
+
     @staticmethod
-    def forward(ctx, pos, cell, owner, graph, species, batch, field=None):
+    def forward(ctx, pos, cell, edge_vec, owner, graph, species, batch, field, hook):
         eng = owner._engine
-        _, atom_e = eng.forward(pos, species, batch, cell, graph, field=field)
-        ctx.owner, ctx.graph, ctx.species, ctx.batch, ctx.field = owner, graph, species, batch, field
+        ctx.owner, ctx.graph, ctx.species, ctx.batch, ctx.field, ctx.hook = owner, graph, species, batch, field, hook
+        ctx.num_graphs = cell.shape[0]
+        ctx.edge_mode = edge_vec is not None
+        ctx.hook_io = []
+        _, atom_e = _run_forward(ctx, pos, cell, replay=False)
         ctx.generation = owner._bump()
         ctx.save_for_backward(pos, cell)
+        ctx.out_dtype = (edge_vec if ctx.edge_mode else pos).dtype
         ctx.pos_dtype, ctx.cell_dtype = pos.dtype, cell.dtype
-        return atom_e.view(-1, 1).to(pos.dtype)
+        return atom_e.view(-1, 1).to(ctx.out_dtype)
 
     @staticmethod
     def backward(ctx, grad_e):
         pos, cell = ctx.saved_tensors
-        owner = ctx.owner
-        eng = owner._engine
-        if owner._generation != ctx.generation:  # another forward reused the workspace: recompute
-            eng.forward(pos, ctx.species, ctx.batch, cell, ctx.graph, field=ctx.field)
-            owner._generation = ctx.generation
-        out = eng.backward(energy_weight=grad_e.reshape(-1), want_virial=False,
-                           want_cell_grad=ctx.needs_input_grad[1])
-        gpos = (-out["forces"]).to(ctx.pos_dtype) if ctx.needs_input_grad[0] else None
-        gcell = out["cell_grad"].to(ctx.cell_dtype).reshape(cell.shape) if ctx.needs_input_grad[1] else None
-        return gpos, gcell, None, None, None, None, None
-
-
-class _NativeEnergyEdgeVec(torch.autograd.Function):
-    """Per-atom energy from caller-given edge vectors (the reference's ``precomputed_edge_vec``,
-    ``pure_cartesian_ictd_layers_full.py:901-902``): the engine sees zero positions, identity
-    cells and shift = edge_vec, so r_e = edge_vec exactly; the backward returns dE/d(edge_vec) =
-    the engine's per-edge dE/dr_e, in the caller's edge order."""
-
-    @staticmethod
-    def forward(ctx, edge_vec, owner, graph, species, batch, num_graphs, field=None):
-        eng = owner._engine
-        pos0, eye = _edge_vec_frame(species.shape[0], num_graphs, edge_vec.device)
-        _, atom_e = eng.forward(pos0, species, batch, eye, graph, field=field)
-        ctx.owner, ctx.graph, ctx.species, ctx.batch, ctx.field = owner, graph, species, batch, field
-        ctx.num_graphs = num_graphs
-        ctx.generation = owner._bump()
-        ctx.vec_dtype = edge_vec.dtype
-        return atom_e.view(-1, 1).to(edge_vec.dtype)
-
-    @staticmethod
-    def backward(ctx, grad_e):
         owner, g = ctx.owner, ctx.graph
         eng = owner._engine
-        if owner._generation != ctx.generation:
-            pos0, eye = _edge_vec_frame(ctx.species.shape[0], ctx.num_graphs, grad_e.device)
-            eng.forward(pos0, ctx.species, ctx.batch, eye, g, field=ctx.field)
+        if owner._generation != ctx.generation:  # another forward reused the workspace: recompute
+            _run_forward(ctx, pos, cell, replay=True)
             owner._generation = ctx.generation
-        out = eng.backward(energy_weight=grad_e.reshape(-1), want_virial=False, want_edge_grad=True)
-        gvec = torch.empty_like(out["edge_grad"])
-        gvec[g.order] = out["edge_grad"]
-        return gvec.to(ctx.vec_dtype), None, None, None, None, None, None
+        want_cell = (not ctx.edge_mode) and ctx.needs_input_grad[1]
+        kw = dict(energy_weight=grad_e.reshape(-1), want_virial=False, want_cell_grad=want_cell,
+                  want_edge_grad=ctx.edge_mode)
+        if ctx.hook is None:
+            out = eng.backward(**kw)
+        else:
+            blocks = owner._ref_blocks()
+
+            def on_grad(k, grads):
+                x, y = ctx.hook_io[k]
+                if not y.requires_grad:  # the hook cut the graph: nothing flows back through it
+                    grads.zero_()
+                    return
+                (gx,) = torch.autograd.grad(y, x, _native_to_ref(grads, blocks).to(y.dtype))
+                _ref_to_native(gx, blocks, grads)
+
+            out = eng.backward_layers(on_grad, **kw)
+        gpos = gcell = gvec = None
+        if ctx.edge_mode:
+            gvec = torch.empty_like(out["edge_grad"])
+            gvec[g.order] = out["edge_grad"]
+            gvec = gvec.to(ctx.out_dtype)
+        else:
+            gpos = (-out["forces"]).to(ctx.pos_dtype) if ctx.needs_input_grad[0] else None
+            gcell = out["cell_grad"].to(ctx.cell_dtype).reshape(cell.shape) if want_cell else None
+        return gpos, gcell, gvec, None, None, None, None, None, None
+
+
+def _run_forward(ctx, pos, cell, replay):
+    """The engine's forward for the autograd function; with a hook, the hook's inputs and outputs
+    are kept for the reverse pass (a replay after the workspace was reused writes the kept outputs
+    again instead of calling the hook, which may hold collectives, a second time)."""
+    eng = ctx.owner._engine
+    if ctx.edge_mode:
+        pos, cell = _edge_vec_frame(ctx.species.shape[0], ctx.num_graphs, ctx.species.device)
+    if ctx.hook is None:
+        return eng.forward(pos, ctx.species, ctx.batch, cell, ctx.graph, field=ctx.field)
+    blocks = ctx.owner._ref_blocks()
+
+    def on_layer(k, feats):
+        if replay:
+            _ref_to_native(ctx.hook_io[k][1].detach(), blocks, feats)
+            return
+        x = _native_to_ref(feats, blocks).requires_grad_(True)
+        with torch.enable_grad():
+            y = ctx.hook(x)
+        if not isinstance(y, torch.Tensor) or y.shape != x.shape:
+            raise ValueError(f"sync_after_scatter must return a tensor of shape {tuple(x.shape)}")
+        ctx.hook_io.append((x, y))
+        _ref_to_native(y.detach(), blocks, feats)
+
+    return eng.forward_layers(pos, ctx.species, ctx.batch, cell, ctx.graph, on_layer, field=ctx.field)
+
+
+def _native_to_ref(feats, blocks):
+    """(N, 9, C) native rows (l^2 + m, channel innermost) -> the reference's flat per-node layout:
+    per irrep block, channel-major (C, 2l + 1) (``_merge_irreps``); blocks without native storage
+    (the o3 model's 1e, identically zero) are zeros."""
+    n, _, c = feats.shape
+    parts = []
+    for r0, m in blocks:
+        if r0 is None:
+            parts.append(feats.new_zeros(n, c * m))
+        else:
+            parts.append(feats[:, r0:r0 + m, :].transpose(1, 2).reshape(n, c * m))
+    return torch.cat(parts, dim=-1)
+
+
+def _ref_to_native(x, blocks, feats):
+    """Inverse of :func:`_native_to_ref`, written into ``feats`` in place (zero blocks skipped)."""
+    n, _, c = feats.shape
+    off = 0
+    for r0, m in blocks:
+        if r0 is not None:
+            feats[:, r0:r0 + m, :] = x[:, off:off + c * m].reshape(n, c, m).transpose(1, 2).to(feats.dtype)
+        off += c * m
 
 
 def _edge_vec_frame(n, num_graphs, device):
@@ -205,6 +260,10 @@ class PureCartesianICTDTransformerLayer(nn.Module):
         self._generation += 1
         return self._generation
 
+    def _ref_blocks(self):
+        """(native first row or None, 2l + 1) per irrep block of the reference feature layout."""
+        return [(0, 1), (1, 3), (4, 5)]
+
     def _ensure_engine(self, device):
         key = (str(device),) + tuple((p.data_ptr(), p._version) for p in self.parameters())
         if self._engine is None or self._engine_key != key:
@@ -215,10 +274,10 @@ class PureCartesianICTDTransformerLayer(nn.Module):
     def forward(self, pos, A, batch, edge_src, edge_dst, edge_shifts, cell, *, precomputed_edge_vec=None,
                 sync_after_scatter=None, external_tensor=None, external_tensor_blocks=None, fidelity_ids=None,
                 return_physical_tensors: bool = False, return_reciprocal_source: bool = False):
-        if sync_after_scatter is not None or external_tensor is not None \
-                or external_tensor_blocks is not None or return_physical_tensors or return_reciprocal_source:
-            raise NotImplementedError("fsctep_b200 pure-cartesian-ictd forward covers (pos, A, batch, edges, cell) "
-                                      "and precomputed_edge_vec")
+        if external_tensor is not None or external_tensor_blocks is not None or return_physical_tensors \
+                or return_reciprocal_source:
+            raise NotImplementedError("fsctep_b200 pure-cartesian-ictd forward covers (pos, A, batch, edges, cell), "
+                                      "precomputed_edge_vec and sync_after_scatter")
         if not pos.is_cuda:
             raise RuntimeError("fsctep_b200 runs on CUDA devices only (no CPU path)")
         n = pos.shape[0]
@@ -231,9 +290,10 @@ class PureCartesianICTDTransformerLayer(nn.Module):
         self._ensure_engine(pos.device)
         if precomputed_edge_vec is not None:
             graph = _edge_vec_graph(edge_src, edge_dst, precomputed_edge_vec, n)
-            return _NativeEnergyEdgeVec.apply(precomputed_edge_vec, self, graph, species, batch, cell.shape[0])
-        graph = GraphCSR.from_edges(edge_src.long(), edge_dst.long(), edge_shifts, n)
-        return _NativeEnergy.apply(pos, cell, self, graph, species, batch)
+        else:
+            graph = GraphCSR.from_edges(edge_src.long(), edge_dst.long(), edge_shifts, n)
+        return _NativeEnergy.apply(pos, cell, precomputed_edge_vec, self, graph, species, batch, None,
+                                   sync_after_scatter)
 
 
 _O3_IRREPS = {("0e", "1o", "2e"), ("0e", "1e", "1o", "2e")}
@@ -343,13 +403,19 @@ class PureCartesianICTDO3TransformerLayer(nn.Module):
     _bump = PureCartesianICTDTransformerLayer._bump
     _ensure_engine = PureCartesianICTDTransformerLayer._ensure_engine
 
+    def _ref_blocks(self):
+        # reference irrep order (l, even before odd): 0e, [1e,] 1o, 2e; the native rows hold
+        # 0e, 1o, 2e (1e couples only to itself and stays zero without a 1e input)
+        rows = {"0e": (0, 1), "1e": (None, 3), "1o": (1, 3), "2e": (4, 5)}
+        return [rows[k] for k in self.irreps]
+
     def forward(self, pos, A, batch, edge_src, edge_dst, edge_shifts, cell, *, precomputed_edge_vec=None,
                 sync_after_scatter=None, external_tensor=None, fidelity_ids=None,
                 return_physical_tensors: bool = False, return_reciprocal_source: bool = False):
-        if sync_after_scatter is not None or return_reciprocal_source or fidelity_ids is not None:
+        if return_reciprocal_source or fidelity_ids is not None:
             raise NotImplementedError("fsctep_b200 pure-cartesian-ictd-o3 forward: optional inputs other than "
-                                      "precomputed_edge_vec / external_tensor / return_physical_tensors are not "
-                                      "covered")
+                                      "precomputed_edge_vec / sync_after_scatter / external_tensor / "
+                                      "return_physical_tensors are not covered")
         if not pos.is_cuda:
             raise RuntimeError("fsctep_b200 runs on CUDA devices only (no CPU path)")
         n = pos.shape[0]
@@ -365,10 +431,10 @@ class PureCartesianICTDO3TransformerLayer(nn.Module):
         eng = self._ensure_engine(pos.device)
         if precomputed_edge_vec is not None:
             graph = _edge_vec_graph(edge_src, edge_dst, precomputed_edge_vec, n)
-            e = _NativeEnergyEdgeVec.apply(precomputed_edge_vec, self, graph, species, batch, cell.shape[0], field)
         else:
             graph = GraphCSR.from_edges(edge_src.long(), edge_dst.long(), edge_shifts, n)
-            e = _NativeEnergy.apply(pos, cell, self, graph, species, batch, field)
+        e = _NativeEnergy.apply(pos, cell, precomputed_edge_vec, self, graph, species, batch, field,
+                                sync_after_scatter)
         if not return_physical_tensors:
             return e
         if self.physical_tensor_heads is None:

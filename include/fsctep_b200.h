@@ -299,6 +299,27 @@ int fsc_ictd_forward(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, cons
                      void* stream);
 int fsc_ictd_backward(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g,
                       fsc_ictd_outputs* out, void* workspace, size_t workspace_bytes, void* stream);
+/* Stepwise evaluation, for callers that act on the node features between interaction layers:
+ * the reference's sync_after_scatter hook (pure_cartesian_ictd_layers_full.py:923-924, 952-953;
+ * pure_cartesian_ictd_layers_o3.py:947-948, 971-972) or a per-layer ghost-feature exchange of a
+ * spatial decomposition (cli/inference_ddp.py:143-340).  Forward steps: 0 = edge geometry, radial
+ * MLPs and conv1 (layer 0's features); k in [1, num_interaction) = conv2 layer k; num_interaction
+ * = readout (energy, atom_energy; both may be NULL before it).  Steps 0..num_interaction in order
+ * equal fsc_ictd_forward.  Backward steps, after a forward on the same workspace: num_interaction
+ * = readout backward (every layer's feature gradient from the readout); k in [1, num_interaction)
+ * = conv2 layer k backward (needs layer k's gradient complete, adds into layer k - 1's); 0 =
+ * conv1 backward and the edge part (forces / virial / edge_grad / cell_grad into `out`).  Steps
+ * num_interaction..0 in order equal fsc_ictd_backward.  Between steps the caller may rewrite the
+ * buffers fsc_ictd_feature_buffer names, on the same stream. */
+int fsc_ictd_forward_step(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g, int step,
+                          float* energy, float* atom_energy, void* workspace, size_t workspace_bytes, void* stream);
+int fsc_ictd_backward_step(const fsc_ictd_config* cfg, const fsc_ictd_weights* w, const fsc_graph* g, int step,
+                           fsc_ictd_outputs* out, void* workspace, size_t workspace_bytes, void* stream);
+/* Device address, inside a workspace laid out for (cfg, num_atoms, num_edges), of layer `layer`'s
+ * node features (which = 0) or of their gradient (which = 1): float [num_atoms][9][C], row
+ * l^2 + m (l = 0..2; with the o3 model the rows are 0e, 1o, 2e), channel innermost. */
+int fsc_ictd_feature_buffer(const fsc_ictd_config* cfg, int64_t num_atoms, int64_t num_edges, void* workspace,
+                            int which, int layer, float** out);
 /* Device status word of the last call on `workspace` (0 = ok; else the id of a bounded
  * wait in a tensor-core kernel that timed out).  Synchronises `stream`.  */
 int fsc_ictd_status(const fsc_ictd_config* cfg, int64_t num_atoms, int64_t num_edges, void* workspace,

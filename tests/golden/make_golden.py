@@ -24,6 +24,9 @@ Fixtures:
   (``pure_cartesian_sparse_layers.py``; max_rank_other 1, k_policy k0): a config-2-like water box
   (Lmax 2) and a config-5-like FCC crystal (Lmax 3, with stress); ``sparse_{c,d}.npz`` the same
   at configs 2 and 5's channel widths (C 64 / Lmax 2, C 128 / Lmax 3).
+* ``ictd_hook.npz`` / ``ictd_o3_hook.npz`` -- an ictd and an o3 model evaluated with a seeded,
+  differentiable ``sync_after_scatter`` (per-node scale, then ghost rows overwritten by owner
+  rows): energies and forces.
 * ``tp_ops.npz`` -- the ``_C_ictd_tp`` operator family evaluated by the reference's
   einsum references (``models/ictd_irreps_cuda.py:169-311``) on the shapes of
   ``test/test_ictd_tp_backend.py``.
@@ -268,6 +271,79 @@ def tp_ops():
     np.savez_compressed(os.path.join(HERE, "tp_ops.npz"), **out)
 
 
+def layer_hook(n, seed):
+    """A deterministic, differentiable sync_after_scatter stand-in: every node's features scaled by
+    a seeded factor, then the rows of n // 8 "ghost" nodes replaced by copies of other ("owner")
+    nodes' rows, the shape of a halo exchange (cli/inference_ddp.py:143-340)."""
+    rng = np.random.default_rng(seed)
+    scale = rng.uniform(0.8, 1.2, n)
+    perm = rng.permutation(n)
+    ghosts, owners = perm[: n // 8], perm[n // 8: 2 * (n // 8)]
+
+    def hook(x):
+        y = x * torch.tensor(scale, dtype=x.dtype).unsqueeze(1)
+        return y.index_copy(0, torch.tensor(ghosts), y[torch.tensor(owners)])
+
+    return hook, {"hook_scale": scale, "hook_ghosts": ghosts.astype(np.int64), "hook_owners": owners.astype(np.int64)}
+
+
+def hook_cases():
+    """ictd (C 32, 3 layers) and o3 (0e, 1e, 1o, 2e, field) with the layer_hook stand-in as
+    sync_after_scatter: per-graph energies and forces of the reference, float64."""
+    from molecular_force_field.models.pure_cartesian_ictd_layers_full import PureCartesianICTDTransformerLayer
+    from molecular_force_field.models.pure_cartesian_ictd_layers_o3 import PureCartesianICTDO3TransformerLayer
+
+    torch.set_default_dtype(torch.float64)
+    cases = [("ictd_hook", systems.diamond_crystal(n_cells=(2, 2, 2), seed=22),
+              dict(channels=32, lmax=2, num_interaction=3, number_of_basis=8, max_radius=5.0,
+                   function_type="gaussian", max_atomvalue=16), 31, None),
+             ("ictd_o3_hook", systems.organic_molecules(n_mol=4, seed=23),
+              dict(channels=32, lmax=2, num_interaction=3, number_of_basis=8, max_radius=5.0,
+                   function_type="gaussian", max_atomvalue=10), 32, 33)]
+    for name, system, cfg, seed, field_seed in cases:
+        kw = dict(max_embed_radius=cfg["max_radius"], main_max_radius=cfg["max_radius"],
+                  main_number_of_basis=cfg["number_of_basis"], hidden_dim_conv=cfg["channels"], hidden_dim_sh=32,
+                  hidden_dim=64, lmax=cfg["lmax"], num_interaction=cfg["num_interaction"],
+                  function_type_main=cfg["function_type"], max_atomvalue=cfg["max_atomvalue"],
+                  internal_compute_dtype=torch.float64, device=torch.device("cpu"))
+        if field_seed is None:
+            model = PureCartesianICTDTransformerLayer(**kw)
+        else:
+            model = PureCartesianICTDO3TransformerLayer(external_tensor_rank=1, external_tensor_irrep="1o",
+                                                        o3_active_irreps=["0e", "1e", "1o", "2e"], **kw)
+        shapes = _perturb(model, seed)
+        n = system["pos"].shape[0]
+        B = system["cell"].shape[0]
+        hook, hook_data = layer_hook(n, seed + 100)
+        src, dst, S = neighbors.batched_neighbor_list(system["pos"], system["batch"], system["cell"],
+                                                      cfg["max_radius"], system["pbc"])
+        pos = torch.tensor(system["pos"], requires_grad=True)
+        b = torch.tensor(system["batch"])
+        extra = {}
+        if field_seed is not None:
+            field = np.random.default_rng(field_seed).normal(scale=0.05, size=(B, 3))
+            extra = {"external_tensor": torch.tensor(field)}
+        e = model(pos, torch.tensor(system["Z"]), b, torch.tensor(src), torch.tensor(dst),
+                  torch.tensor(S.astype(np.float64)), torch.tensor(system["cell"]), sync_after_scatter=hook, **extra)
+        Eg = torch.zeros(B, dtype=torch.float64).index_add(0, b, e.squeeze(-1))
+        (gp,) = torch.autograd.grad(Eg.sum(), [pos])
+        out = {"pos": system["pos"], "Z": system["Z"], "batch": system["batch"], "cell": system["cell"],
+               "pbc": np.array(system["pbc"]), "edge_src": src.astype(np.int32), "edge_dst": dst.astype(np.int32),
+               "edge_shifts": S.astype(np.int8), **hook_data}
+        if field_seed is not None:
+            out["field"] = field
+        for k, v in cfg.items():
+            out[f"cfg_{k}"] = np.array(v)
+        out["sd_seed"] = np.array(seed)
+        for k, v in model.state_dict().items():
+            out[f"sdshape/{k}"] = np.array(shapes[k], dtype=np.int64)
+            out[f"sdsum/{k}"] = np.array(float(v.double().sum()))
+        out["ref64_energy"] = Eg.detach().numpy()
+        out["ref64_forces"] = (-gp).numpy()
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
+        print(name, "atoms", n, "edges", src.shape[0], "E", out["ref64_energy"][:3])
+
+
 def main():
     tables()
     tp_ops()
@@ -283,6 +359,7 @@ def main():
     o3()
     sparse()
     sparse_widths()
+    hook_cases()
 
 
 def o3():
@@ -300,5 +377,7 @@ if __name__ == "__main__":
         sparse()
     elif len(sys.argv) > 1 and sys.argv[1] == "sparse_widths":
         sparse_widths()
+    elif len(sys.argv) > 1 and sys.argv[1] == "hooks":
+        hook_cases()
     else:
         main()

@@ -35,10 +35,11 @@ def test_unsupported_options_raise():
           torch.ones(1).long(), torch.zeros(1, 3), torch.eye(3)[None])
 
 
-def _o3_module(cfg, device="meta"):
+def _o3_module(cfg, device="meta", heads=True):
     from fsctep_b200.models import PureCartesianICTDO3TransformerLayer
 
-    heads = {"dipole": {"irreps": ["1o"], "reduce": "sum"}, "polarizability": {"ls": [0, 2], "reduce": "sum"}}
+    heads = {"dipole": {"irreps": ["1o"], "reduce": "sum"}, "polarizability": {"ls": [0, 2], "reduce": "sum"}} \
+        if heads else None
     with torch.device(device):
         return PureCartesianICTDO3TransformerLayer(
             max_embed_radius=float(cfg["max_radius"]), main_max_radius=float(cfg["max_radius"]),
@@ -86,3 +87,24 @@ def test_sparse_module_state_dict_matches_reference(tag):
     cfg = {k[4:]: z[k].item() for k in z.files if k.startswith("cfg_")}
     mine = {k: tuple(v.shape) for k, v in _sparse_module(cfg).state_dict().items()}
     assert mine == ref
+
+
+def test_feature_layout_maps_to_the_reference_merge():
+    """Native rows (l^2 + m, channel innermost) <-> the reference's flat node layout (per irrep
+    block channel-major (C, 2l + 1), pure_cartesian_ictd_layers_full.py _merge_irreps); the o3
+    model's 1e block has no native storage and maps to zeros."""
+    from fsctep_b200.models import _native_to_ref, _ref_to_native
+
+    n, C = 5, 4
+    feats = torch.randn(n, 9, C, dtype=torch.float64)
+    blocks = [(0, 1), (1, 3), (4, 5)]
+    flat = _native_to_ref(feats, blocks)
+    ref = torch.cat([feats[:, l * l:(l + 1) ** 2, :].transpose(1, 2).reshape(n, -1) for l in range(3)], dim=-1)
+    assert torch.equal(flat, ref)
+    back = torch.zeros_like(feats)
+    _ref_to_native(flat, blocks, back)
+    assert torch.equal(back, feats)
+    o3 = [(0, 1), (None, 3), (1, 3), (4, 5)]
+    flat3 = _native_to_ref(feats, o3)
+    assert flat3.shape == (n, 12 * C) and torch.count_nonzero(flat3[:, C:4 * C]) == 0
+    assert torch.equal(flat3[:, 4 * C:7 * C], ref[:, C:4 * C])
