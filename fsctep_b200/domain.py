@@ -1,9 +1,11 @@
 """Spatial domain decomposition of one periodic system over ranks (one GPU per rank).
 
 The reference's multi-GPU inference (``cli/inference_ddp.py:143-340``) partitions atoms by
-region and exchanges ghost-atom features after every layer.  This build takes the other
-exchange pattern named for the same path: ghosts are recomputed redundantly, so there is no
-per-layer communication.
+region and exchanges ghost-atom features after every layer.  Both exchange patterns are here:
+:func:`layer_exchange_step` does that (a one-cutoff halo, the ictd engine run in steps, ghost
+feature rows exchanged after every layer and their gradients returned in the reverse pass);
+:func:`decomposed_step` recomputes the ghosts redundantly over a receptive-field halo, with no
+per-layer communication.  The notes below describe the latter; both share the halo exchange.
 
 * The cell is cut into a ``(px, py, pz)`` grid of blocks; rank ``r`` owns the atoms of one block
   (in practice: whatever atoms the caller hands it; only their bounding box matters).
@@ -307,6 +309,92 @@ def decomposed_step(dec: Decomposition, rank: int, pos: torch.Tensor, species: t
     tot = yield from all_reduce_sum(torch.cat(red))
     res = {"energy": tot[0], "forces": forces, "atom_energy": out["atom_energy"][:n],
            "num_ghosts": int(pos_l.shape[0] - n)}
+    if want_virial:
+        res["virial"] = tot[1:10].reshape(3, 3)
+    return res
+
+
+# ---------------------------------------------------------------------------- per-layer exchange
+def exchange_ghost_rows(plan: HaloPlan, rows: torch.Tensor, num_local: int):
+    """Forward ghost-feature exchange (the reference's sync_after_scatter, cli/inference_ddp.py:
+    191-246): every rank sends the rows of its owned atoms that are ghosts elsewhere and
+    overwrites its own ghost rows ``rows[num_local:]`` with their owners' rows, in place."""
+    flat = rows.reshape(rows.shape[0], -1)
+    recv, _ = yield from all_to_all(flat[plan.send_idx], plan.send_counts, plan.recv_counts)
+    if recv.shape[0]:
+        flat[num_local:num_local + recv.shape[0]] = recv
+    return rows
+
+
+def return_ghost_rows(plan: HaloPlan, rows: torch.Tensor, num_local: int):
+    """Adjoint of :func:`exchange_ghost_rows` on gradients: the ghost rows' gradients go back to
+    their owners and are added to the owned rows; the ghost rows are then zero (a ghost's own
+    value was overwritten, so nothing flows through it)."""
+    flat = rows.reshape(rows.shape[0], -1)
+    back, _ = yield from all_to_all(flat[num_local:].contiguous(), plan.recv_counts, plan.send_counts)
+    if back.shape[0]:
+        flat.index_add_(0, plan.send_idx, back)
+    flat[num_local:] = 0
+    return rows
+
+
+def owned_receiver_graph(g, num_local: int):
+    """The dst-sorted CSR graph restricted to edges whose receiver is owned (rows of ghosts empty):
+    with ghost features exchanged every layer, only owned receivers are evaluated."""
+    from .ictd import GraphCSR
+
+    e_own = int(g.row_ptr[num_local].item())
+    row_ptr = g.row_ptr.clone()
+    row_ptr[num_local + 1:] = e_own
+    src = g.src[:e_own].contiguous()
+    shift = g.shift[:e_own].contiguous()
+    tr_ptr, tr_eid = GraphCSR.transpose(row_ptr, src, g.num_atoms)
+    order = g.order[:e_own] if g.order is not None else None
+    return GraphCSR(g.num_atoms, row_ptr, src, shift, tr_ptr, tr_eid, order)
+
+
+def layer_exchange_step(dec: Decomposition, rank: int, pos: torch.Tensor, species: torch.Tensor, engine,
+                        cutoff: float, want_virial: bool = False):
+    """One energy + forces step of the ictd engine with a per-layer ghost-feature exchange (a
+    generator of collectives, like :func:`decomposed_step`): the halo ``dec.halo`` needs to cover
+    one cutoff only.  The local graph holds the edges into owned atoms; after each interaction
+    layer whose features a later layer reads, the ghost rows are overwritten by their owners'
+    rows; in the reverse pass the ghost rows' gradients go back to their owners before the layer
+    that produced them runs backward; the ghost forces (edge endpoints) go back as in
+    :func:`decomposed_step`.  Energies and virials are summed over ranks."""
+    from .neighbors import build_graph
+
+    n = pos.shape[0]
+    dev = pos.device
+    nint = engine.cfg.num_interaction
+    plan = yield from halo_exchange(dec, rank, pos, species)
+    pos_l = torch.cat([pos, plan.ghost_pos.to(pos.dtype)])
+    spec_l = torch.cat([species, plan.ghost_species.to(species.dtype)])
+    n_all = int(pos_l.shape[0])
+    cell_t = torch.as_tensor(dec.cell, dtype=torch.float64, device=dev).reshape(1, 3, 3)
+    g = owned_receiver_graph(build_graph(pos_l, cell_t, cutoff, pbc=dec.local_pbc), n)
+    batch = torch.zeros(n_all, dtype=torch.int32, device=dev)
+    # every layer on all rows (ghost rows have no edges and are overwritten), the readout on the owned
+    engine.begin_steps(pos_l, spec_l, batch, cell_t, g, num_local=n, layer_atoms=[n_all] * (nint - 1) + [n])
+    for k in range(nint - 1):
+        feats = engine.forward_step(k)
+        yield from exchange_ghost_rows(plan, feats, n)
+    engine.forward_step(nint - 1)  # read by the readout only
+    energy, atom_e = engine.forward_step(nint)
+    out = engine.begin_backward(want_virial=want_virial)
+    engine.backward_step(nint)
+    for k in range(nint - 1, -1, -1):
+        if k < nint - 1:
+            yield from return_ghost_rows(plan, engine.feature_buffer(1, k), n)
+        engine.backward_step(k)
+    f = out["forces"]
+    forces = yield from return_ghost_forces(plan, f[:n], f[n:])
+    red = [energy.reshape(1).to(torch.float64)]
+    if want_virial:
+        red.append(out["virial"].reshape(9).to(torch.float64))
+    tot = yield from all_reduce_sum(torch.cat(red))
+    res = {"energy": tot[0], "forces": forces, "atom_energy": atom_e[:n], "num_ghosts": n_all - n,
+           "num_edges": g.num_edges}
     if want_virial:
         res["virial"] = tot[1:10].reshape(3, 3)
     return res

@@ -449,52 +449,78 @@ class ICTDEngine:
         nbytes = g.num_atoms * 9 * self.cfg.channels * 4
         return ws[off:off + nbytes].view(torch.float32).view(g.num_atoms, 9, self.cfg.channels)
 
-    def forward_layers(self, pos, species, batch, cell, g: GraphCSR, on_layer, num_local=None, field=None):
+    def begin_steps(self, pos, species, batch, cell, g: GraphCSR, num_local=None, field=None, layer_atoms=None):
+        """Set up a stepwise evaluation (:meth:`forward_step` / :meth:`backward_step`)."""
+        pos, species, batch, cell = self._inputs(pos, species, batch, cell)
+        B = cell.shape[0]
+        self.workspace(g.num_atoms, g.num_edges)
+        fdev = self._field(field, B)
+        self._last = (pos, species, batch, cell, g, num_local)
+        self._last_layers = layer_atoms
+        self._field_dev = fdev
+        self._step_out = (torch.empty(B, dtype=torch.float32, device=self.device),
+                          torch.empty(g.num_atoms, dtype=torch.float32, device=self.device))
+
+    def forward_step(self, step: int):
+        """Forward step ``step`` (0 = edges + conv1, k = conv2 layer k, num_interaction = readout);
+        returns (energy, atom_energy) after the last step, else layer ``step``'s feature view."""
+        pos, species, batch, cell, g, num_local = self._last
+        ws = self.workspace(g.num_atoms, g.num_edges)
+        energy, atom_e = self._step_out
+        gs = self._graph(pos, species, batch, cell, g, cell.shape[0], num_local, None, self._field_dev,
+                         self._last_layers)
+        last = step == self.cfg.num_interaction
+        N.check(N.lib().fsc_ictd_forward_step(C.byref(self.ncfg), C.byref(self.weights.struct), C.byref(gs), step,
+                                              N.ptr(energy) if last else None, N.ptr(atom_e) if last else None,
+                                              N.ptr(ws), ws.numel(), N.stream_ptr(self.device)),
+                f"fsc_ictd_forward_step({step})")
+        return (energy, atom_e) if last else self.feature_buffer(0, step)
+
+    def begin_backward(self, energy_weight=None, want_virial=True, want_cell_grad=False, want_edge_grad=False):
+        g, B = self._last[4], self._last[3].shape[0]
+        out, o = self._outputs(g, B, want_virial, want_cell_grad, want_edge_grad)
+        if energy_weight is not None:
+            energy_weight = energy_weight.detach().to(torch.float32).reshape(-1).contiguous()
+        self._bwd = (out, o, energy_weight)
+        return out
+
+    def backward_step(self, step: int):
+        """Backward step ``step`` (num_interaction = readout, k = conv2 layer k, 0 = conv1 + edges);
+        returns the gradient view of layer ``step - 1`` (complete once this step ran) for
+        ``step >= 1``, else the outputs."""
+        pos, species, batch, cell, g, num_local = self._last
+        ws = self.workspace(g.num_atoms, g.num_edges)
+        out, o, ew = self._bwd
+        gs = self._graph(pos, species, batch, cell, g, cell.shape[0], num_local, ew, self._field_dev,
+                         self._last_layers)
+        N.check(N.lib().fsc_ictd_backward_step(C.byref(self.ncfg), C.byref(self.weights.struct), C.byref(gs), step,
+                                               C.byref(o), N.ptr(ws), ws.numel(), N.stream_ptr(self.device)),
+                f"fsc_ictd_backward_step({step})")
+        return self.feature_buffer(1, step - 1) if step >= 1 else out
+
+    def forward_layers(self, pos, species, batch, cell, g: GraphCSR, on_layer, num_local=None, field=None,
+                       layer_atoms=None):
         """:meth:`forward` in steps: after interaction layer k's features are written,
         ``on_layer(k, feats)`` may rewrite ``feats`` (a (num_atoms, 9, C) view, see
         :meth:`feature_buffer`) in place on the current stream before layer k + 1 reads them (the
         reference's sync_after_scatter points, ``pure_cartesian_ictd_layers_full.py:923-953``)."""
-        pos, species, batch, cell = self._inputs(pos, species, batch, cell)
-        B = cell.shape[0]
-        ws = self.workspace(g.num_atoms, g.num_edges)
-        energy = torch.empty(B, dtype=torch.float32, device=self.device)
-        atom_e = torch.empty(g.num_atoms, dtype=torch.float32, device=self.device)
-        fdev = self._field(field, B)
-        gs = self._graph(pos, species, batch, cell, g, B, num_local, None, fdev, None)
-        self._last = (pos, species, batch, cell, g, num_local)
-        self._last_layers = None
-        self._field_dev = fdev
+        self.begin_steps(pos, species, batch, cell, g, num_local, field, layer_atoms)
         nint = self.cfg.num_interaction
-        for step in range(nint + 1):
-            last = step == nint
-            N.check(N.lib().fsc_ictd_forward_step(C.byref(self.ncfg), C.byref(self.weights.struct), C.byref(gs), step,
-                                                  N.ptr(energy) if last else None, N.ptr(atom_e) if last else None,
-                                                  N.ptr(ws), ws.numel(), N.stream_ptr(self.device)),
-                    f"fsc_ictd_forward_step({step})")
-            if not last:
-                on_layer(step, self.feature_buffer(0, step))
-        return energy, atom_e
+        for step in range(nint):
+            on_layer(step, self.forward_step(step))
+        return self.forward_step(nint)
 
     def backward_layers(self, on_grad, energy_weight=None, want_virial=True, want_cell_grad=False,
                         want_edge_grad=False):
         """:meth:`backward` in steps: before the reverse pass of interaction layer k reads the
         complete gradient of layer k's features, ``on_grad(k, grads)`` may rewrite it in place
         (the adjoint of the forward's ``on_layer``)."""
-        pos, species, batch, cell, g, num_local = self._last
-        B = cell.shape[0]
-        ws = self.workspace(g.num_atoms, g.num_edges)
-        out, o = self._outputs(g, B, want_virial, want_cell_grad, want_edge_grad)
-        if energy_weight is not None:
-            energy_weight = energy_weight.detach().to(torch.float32).reshape(-1).contiguous()
-        gs = self._graph(pos, species, batch, cell, g, B, num_local, energy_weight, getattr(self, "_field_dev", None),
-                         None)
+        self.begin_backward(energy_weight, want_virial, want_cell_grad, want_edge_grad)
         nint = self.cfg.num_interaction
         for step in range(nint, -1, -1):
             if step < nint:
                 on_grad(step, self.feature_buffer(1, step))
-            N.check(N.lib().fsc_ictd_backward_step(C.byref(self.ncfg), C.byref(self.weights.struct), C.byref(gs),
-                                                   step, C.byref(o), N.ptr(ws), ws.numel(),
-                                                   N.stream_ptr(self.device)), f"fsc_ictd_backward_step({step})")
+            out = self.backward_step(step)
         return out
 
     def _outputs(self, g, B, want_virial, want_cell_grad, want_edge_grad):

@@ -257,3 +257,80 @@ def test_lattice_blocks_tile_the_global_crystal(make, per_cell):
                 assert b["pos"][:, k].min() > lo[k] - 1.0 and b["pos"][:, k].max() < hi[k] + 1.0
             else:
                 assert b["pos"][:, k].min() >= 0.0 and b["pos"][:, k].max() < L[k]
+
+
+def _exchange_adjoint_gen(dec, rank, pos, Z, seed):
+    """Per rank: halo plan, then <x_after_exchange, y> versus <x, y_after_return>."""
+    plan = yield from D.halo_exchange(dec, rank, pos, Z)
+    n, G = pos.shape[0], plan.ghost_pos.shape[0]
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(n + G, 2, 3, generator=g, dtype=torch.float64)
+    y = torch.randn(n + G, 2, 3, generator=g, dtype=torch.float64)
+    x_owned = x[:n].clone()
+    xe = x.clone()
+    yield from D.exchange_ghost_rows(plan, xe, n)
+    yr = y.clone()
+    yield from D.return_ghost_rows(plan, yr, n)
+    # owned rows are untouched by the forward exchange; ghosts were overwritten and are zero in yr
+    assert torch.equal(xe[:n], x_owned) and torch.count_nonzero(yr[n:]) == 0
+    lhs = yield from D.all_reduce_sum((xe * y).sum().reshape(1))
+    rhs = yield from D.all_reduce_sum((x * yr).sum().reshape(1))
+    # every received ghost row equals its owner's row, wherever the owner lives
+    return float(lhs), float(rhs), G
+
+
+@pytest.mark.parametrize("dims", [(2, 1, 1), (2, 2, 1), (2, 2, 2)])
+def test_ghost_row_exchange_and_return_are_adjoint(dims):
+    """The per-layer ghost-feature exchange and its gradient return satisfy <E x, y> = <x, E^T y>
+    (emulated ranks in one process)."""
+    s = _system()
+    dec = D.Decomposition(s["cell"][0], dims, RC)
+    owned = [_owned(dec, r, s) for r in range(dec.world)]
+    gens = [_exchange_adjoint_gen(dec, r, torch.tensor(s["pos"][o], dtype=torch.float64), torch.tensor(s["Z"][o]),
+                                  100 + r) for r, o in enumerate(owned)]
+    res = D.run_local(gens)
+    for lhs, rhs, G in res:
+        assert G > 0
+        assert abs(lhs - rhs) <= 1e-10 * max(1.0, abs(lhs))
+
+
+def test_ghost_rows_carry_owner_values():
+    """After the exchange every ghost row is the row of the owned atom it images."""
+    s = _system()
+    dec = D.Decomposition(s["cell"][0], (2, 2, 1), RC)
+    owned = [_owned(dec, r, s) for r in range(dec.world)]
+
+    def gen(rank, o):
+        pos = torch.tensor(s["pos"][o], dtype=torch.float64)
+        plan = yield from D.halo_exchange(dec, rank, pos, torch.tensor(s["Z"][o]))
+        rows = torch.cat([torch.tensor(o, dtype=torch.float64).unsqueeze(1),
+                          torch.full((plan.ghost_pos.shape[0], 1), -1.0, dtype=torch.float64)])
+        yield from D.exchange_ghost_rows(plan, rows, len(o))
+        return rows[len(o):, 0].long().numpy(), plan.ghost_pos.numpy()
+
+    for gids, gpos in D.run_local([gen(r, o) for r, o in enumerate(owned)]):
+        assert (gids >= 0).all()
+        # a ghost image differs from its owner's position by a lattice vector
+        d = (gpos - s["pos"][gids]) @ np.linalg.inv(s["cell"][0])
+        assert np.abs(d - np.round(d)).max() < 1e-9
+
+
+def _gloo_exchange_rank(rank, world, port, dims):
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        s = _system()
+        dec = D.Decomposition(s["cell"][0], dims, RC)
+        o = _owned(dec, rank, s)
+        lhs, rhs, G = D.run_dist(_exchange_adjoint_gen(dec, rank, torch.tensor(s["pos"][o], dtype=torch.float64),
+                                                       torch.tensor(s["Z"][o]), 100 + rank))
+        assert G > 0 and abs(lhs - rhs) <= 1e-10 * max(1.0, abs(lhs))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_ghost_row_exchange():
+    import torch.multiprocessing as mp
+
+    mp.spawn(_gloo_exchange_rank, args=(2, _free_port(), (2, 1, 1)), nprocs=2, join=True)

@@ -45,7 +45,7 @@ def _model(kind):
         cfg, sd, c = golden_io.model_case("hook", prefix="ictd_o3")
         m = _o3_module(cfg, device="cpu", heads=False)
     m.load_state_dict({k: v.float() for k, v in sd.items()})
-    return m.cuda(), c
+    return m.cuda(), c, cfg
 
 
 def _args(c, dev):
@@ -56,7 +56,7 @@ def _args(c, dev):
 
 @pytest.mark.parametrize("kind", ["ictd", "o3"])
 def test_hook_matches_reference(kind):
-    m, c = _model(kind)
+    m, c, cfg = _model(kind)
     dev = torch.device("cuda")
     hook, calls = _hook(c, dev)
     pos = torch.tensor(c["pos"], device=dev, dtype=torch.float32).requires_grad_(True)
@@ -67,8 +67,8 @@ def test_hook_matches_reference(kind):
     b = torch.tensor(c["batch"], device=dev)
     Eg = torch.zeros(c["cell"].shape[0], device=dev).index_add(0, b, e.view(-1))
     (gp,) = torch.autograd.grad(Eg.sum(), [pos])
-    nint = int(c["cfg_num_interaction"])
-    width = int(c["cfg_channels"]) * (12 if kind == "o3" else 9)
+    nint = int(cfg["num_interaction"])
+    width = int(cfg["channels"]) * (12 if kind == "o3" else 9)
     assert calls == [(c["pos"].shape[0], width)] * nint
     E, ref = Eg.detach().double().cpu().numpy(), c["ref64_energy"]
     assert np.all(np.abs(E - ref) <= U.E_RTOL * np.abs(ref).max()), (E, ref)
@@ -78,7 +78,7 @@ def test_hook_matches_reference(kind):
 def test_identity_hook_is_the_plain_path():
     """The stepwise evaluation with an identity hook gives the same energies and forces, bit for
     bit, as the one-call path, also through precomputed edge vectors."""
-    m, c = _model("ictd")
+    m, c, _ = _model("ictd")
     dev = torch.device("cuda")
     outs = []
     for hook in (None, lambda x: x):
