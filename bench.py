@@ -266,6 +266,11 @@ def run_native(args, rank, world, device):
     dims = D.grid_for(world)
     if world == 1:
         sysd = systems.diamond_crystal(n_cells=w["cells"], seed=1000 + rank, Z=w["Z"])
+    elif args.scaling == "strong":  # this rank's block of the one fixed crystal
+        per = tuple(c // d for c, d in zip(w["cells"], dims))
+        if any(p * d != c for p, d, c in zip(per, dims, w["cells"])):
+            raise SystemExit(f"--scaling strong: cells {w['cells']} do not split into {dims} blocks")
+        sysd = systems.diamond_block(D.block_of(rank, dims), dims, n_cells=per, seed=1000 + rank, Z=w["Z"])
     else:  # this rank's block of a (dims * cells) crystal
         sysd = systems.diamond_block(D.block_of(rank, dims), dims, n_cells=w["cells"], seed=1000 + rank, Z=w["Z"])
     n = sysd["pos"].shape[0]
@@ -283,6 +288,14 @@ def run_native(args, rank, world, device):
             energy, _ = eng.forward(pos, Z, batch, cell, g)
             out = eng.backward(want_virial=False)
             return energy, out["forces"], {"edges": g.num_edges, "ghosts": 0}
+    elif args.halo == "layer":
+        dec = D.Decomposition(sysd["cell"][0], dims, cfg.max_radius)
+        info = {}
+
+        def step(pos, cell):
+            r = D.run_dist(D.layer_exchange_step(dec, rank, pos, Z, eng, cfg.max_radius))
+            info["ghosts"], info["edges"] = r["num_ghosts"], r["num_edges"]
+            return r["energy"].reshape(1), r["forces"], dict(info)
     else:
         dec = D.Decomposition(sysd["cell"][0], dims, cfg.num_interaction * cfg.max_radius)
         evaluate = D.ictd_evaluator(eng, sysd["cell"][0], cfg.max_radius)
@@ -568,6 +581,12 @@ def main():
     ap.add_argument("--workload", default="si1m", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-launch-count", action="store_true", help="skip the torch.profiler launch count (for ncu)")
+    ap.add_argument("--halo", default="layer", choices=["layer", "recompute"],
+                    help="N > 1, pure-cartesian-ictd: per-layer ghost-feature exchange over a one-cutoff halo "
+                         "(default) or ghosts recomputed over a num_interaction x cutoff halo")
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="N > 1, pure-cartesian-ictd: a fixed crystal per GPU (weak, default) or one fixed "
+                         "crystal cut over the GPUs (strong)")
     ap.add_argument("--clocks-csv", default=None, help="where to write the nvidia-smi clock samples (default: a "
                                                         "temporary directory)")
     args = ap.parse_args()
@@ -582,11 +601,16 @@ def main():
     n_atoms = int(np.prod(w["cells"])) * 8 if not sparse else None
     config = {"workload": f"{args.workload}: pure-cartesian-ictd diamond Si {n_atoms} atoms (config 4)",
               "model": "pure-cartesian-ictd", "channels": w["channels"], "num_interaction": w["num_interaction"],
-              "lmax": 2, "cutoff": 5.0, "radial_basis": "gaussian x8", "atoms_per_gpu": n_atoms,
+              "lmax": 2, "cutoff": 5.0, "radial_basis": "gaussian x8", "atoms_per_gpu": n_atoms if args.scaling == "weak" else n_atoms // max(args.gpus, 1),
               "parallelism": ("spatial%dx%dx%d" % grid_for(args.gpus)) if args.gpus > 1 else "single",
-              "decomposition": ("blocks of a (50 px, 50 py, 50 pz)-cell crystal, halo = num_interaction x cutoff "
-                                "= 15 A of recomputed ghosts, one position halo exchange and one reverse ghost-force "
-                                "exchange per step (NCCL all_to_all), energy all_reduce") if args.gpus > 1 else None,
+              "decomposition": None if args.gpus == 1 else (
+                  ("blocks of " + ("a (50 px, 50 py, 50 pz)-cell crystal" if args.scaling == "weak" else
+                                   "one 50^3-cell crystal (1,000,000 atoms in total)") + ", ") +
+                  ("halo = cutoff = 5 A: one position halo exchange, a ghost-feature exchange after each "
+                   "interaction layer that a later layer reads and its adjoint in the reverse pass, one reverse "
+                   "ghost-force exchange (NCCL all_to_all), energy all_reduce" if args.halo == "layer" else
+                   "halo = num_interaction x cutoff = 15 A of recomputed ghosts, one position halo exchange and "
+                   "one reverse ghost-force exchange per step (NCCL all_to_all), energy all_reduce")),
               "step": "neighbour list + forward + backward (energy, forces)",
               "l2": "inputs larger than L2 (features 2.3 GB per layer at 1M atoms)"}
     if sparse:
@@ -632,8 +656,13 @@ def main():
     torch.cuda.set_device(device)
     res = run_sparse(args, rank, world, device) if sparse else run_native(args, rank, world, device)
     n, E = res["n"], res["E"]
-    value = n * world / (res["ms_step"] / 1e3)
-    e2e_value = n * world / (res["ms_e2e"] / 1e3)
+    n_total = n
+    if world > 1:  # atoms of all ranks (blocks of a strong-scaling crystal differ slightly)
+        t = torch.tensor([float(n)], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(t)
+        n_total = int(t.item())
+    value = n_total / (res["ms_step"] / 1e3)
+    e2e_value = n_total / (res["ms_e2e"] / 1e3)
     # dominant stage and its roofline
     stage_avg = {}
     for name, lst in res["stage_ms"].items():
@@ -674,7 +703,8 @@ def main():
         if ctx is not None:
             roofline["fp32_simt"] = ctx
     line = {"metric": metric, "value": value, "unit": "atom-steps/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": res["ms_step"], "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": res["ms_step"], "higher_is_better": True,
+            "scaling": args.scaling if (world > 1 and not sparse) else "weak", "atoms_total": n_total,
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded positions and weights)",
             "config": config, "edges_per_gpu": E, "ghost_atoms_per_gpu": res["ghosts"], "roofline": roofline,
             "clocks": res["clocks"],
