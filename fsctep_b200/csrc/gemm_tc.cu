@@ -37,13 +37,12 @@ constexpr int GT_THREADS = 6 * 32;          // 4 math warps, producer warp, MMA 
 // NT <= 128 (FLUSH): every group of GC K-chunks (12 GC MMAs) accumulates into a fresh one of two
 // TMEM slots, which the math warps add to fp32 registers (tensor-core accumulation truncates, so
 // long chains over large K would bias the result).  PRECISE (long K with heavy cancellation, e.g.
-// the readout's Gram contraction): a fresh slot every chunk, and for NT <= 64 the register sums
-// are compensated (Kahan).  Wider tiles (gemm_tc_nt gives them only for K <= 128) rotate the
-// chunks over NACC accumulators summed in the epilogue.
+// the readout's Gram contraction): a fresh slot every chunk (12 MMAs, 4 of them hi*hi).  Wider
+// tiles (gemm_tc_nt gives them only for K <= 128) rotate the chunks over NACC accumulators summed
+// in the epilogue.
 template <int NT, bool PRECISE = false>
 struct GCfg {
   static constexpr bool FLUSH = NT <= 128;
-  static constexpr bool KAHAN = PRECISE && NT <= 64;
   static constexpr int GC = PRECISE ? 1 : 2;
   static constexpr int NACC = FLUSH ? 2 : 2;
   static constexpr int NST = 2;
@@ -149,11 +148,8 @@ __global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_consta
     bool ok = true;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     float sum[CF::FLUSH ? NT : 1];
-    float comp[CF::KAHAN ? NT : 1];  // Kahan compensation of sum
 #pragma unroll
     for (int i = 0; i < (CF::FLUSH ? NT : 1); ++i) sum[i] = 0.f;
-#pragma unroll
-    for (int i = 0; i < (CF::KAHAN ? NT : 1); ++i) comp[i] = 0.f;
     auto flush = [&](int g) {  // FLUSH: add group g's slot to the fp32 sums and free it
       const int slot = g & 1;
       if (!(ok = tc::mbar_wait(grp_full + slot, (g >> 1) & 1, a.err, 86))) return;
@@ -163,19 +159,8 @@ __global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_consta
         uint32_t u[16];
         tc::tmem_ld16(tbase + (uint32_t)(slot * NT) + lane_off + 16u * cb, u);
         tc::tmem_wait_ld();
-        if (CF::KAHAN) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int q = CF::KAHAN ? 16 * cb + i : 0;
-            const float y = __uint_as_float(u[i]) - comp[q];
-            const float t = sum[16 * cb + i] + y;
-            comp[q] = (t - sum[16 * cb + i]) - y;
-            sum[16 * cb + i] = t;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) sum[16 * cb + i] += __uint_as_float(u[i]);
-        }
+        for (int i = 0; i < 16; ++i) sum[16 * cb + i] += __uint_as_float(u[i]);
       }
       tc::tc_fence_before();
       __syncwarp();

@@ -1504,7 +1504,6 @@ int forward(Ctx& c) {
                            p.C, 0, p.feats[k] + (n0 * p.R + roff(Lo)) * p.C, (int64_t)p.R * p.C, p.C, nc, pow3(Lo),
                            K, p.C);
         ga.alpha = 1.f / avg;
-        ga.precise = 1;
         FSC_TRY(run_gemm(ga, p.img_mix[k][Lo], p.err, st));
       }
     }

@@ -1,7 +1,7 @@
 """CPU check of the tensor-core GEMM plans: every GEMM shape the engines issue at the benchmark
 widths keeps its tcgen05 accumulation chains at <= 24 MMAs (tensor-core accumulation rounds
 toward zero, so longer chains bias long-K products), and the precise variant used for the
-readout's Gram contraction and the sparse fc.4 products at <= 12."""
+readout's Gram contraction at <= 12."""
 
 import ctypes as C
 
@@ -37,7 +37,7 @@ def sparse_shapes(C_, lmax, nint, inv=32, hidden=(128, 128, 128)):
     shapes, precise = [], []
     for L in range(lmax + 1):
         K = npl[L] * 65 * C_
-        precise.append((K, C_))          # fc.4 after the aggregation
+        shapes.append((K, C_))           # fc.4 after the aggregation
         shapes.append((C_, K))           # its transpose (dZ)
         precise.append((nC * (nC + 1) // 2, S))  # readout Gram contraction
         shapes.append((S, nC * nC))      # its gradient
