@@ -392,6 +392,13 @@ def run_sparse(args, rank, world, device):
             out = eng.backward(want_virial=True)
             info["edges"] = g.num_edges
             return energy, out["forces"]
+    elif args.halo == "layer":
+        dec = D.Decomposition(sysd["cell"][0], dims, cfg.max_radius)
+
+        def step(pos, cell):
+            r = D.run_dist(D.layer_exchange_step(dec, rank, pos, Z, eng, cfg.max_radius, want_virial=True))
+            info["ghosts"], info["edges"] = r["num_ghosts"], r["num_edges"]
+            return r["energy"].reshape(1), r["forces"]
     else:
         dec = D.Decomposition(sysd["cell"][0], dims, cfg.num_interaction * cfg.max_radius)
         evaluate = D.sparse_evaluator(eng, sysd["cell"][0], cfg.max_radius, want_virial=True)
@@ -628,10 +635,15 @@ def main():
                   "max_rank_other": 1, "k_policy": "k0", "cutoff": 5.0, "radial_basis": "gaussian x8",
                   "atoms_per_gpu": n_atoms,
                   "parallelism": ("spatial%dx%dx%d" % grid_for(args.gpus)) if args.gpus > 1 else "single",
-                  "decomposition": ("blocks of a dims x cells FCC crystal, halo = num_interaction x cutoff = 15 A of "
-                                    "recomputed ghosts (every layer on all local atoms), one position halo exchange "
-                                    "and one reverse ghost-force exchange per step (NCCL all_to_all), energy and "
-                                    "virial all_reduce") if args.gpus > 1 else None,
+                  "decomposition": None if args.gpus == 1 else (
+                      "blocks of a dims x cells FCC crystal, " +
+                      ("halo = cutoff = 5 A: one position halo exchange, a ghost-feature exchange after each "
+                       "interaction layer that a later layer reads and its adjoint in the reverse pass, one reverse "
+                       "ghost-force exchange (NCCL all_to_all), whole-system E/N, energy and virial all_reduce"
+                       if args.halo == "layer" else
+                       "halo = num_interaction x cutoff = 15 A of recomputed ghosts (every layer on all local "
+                       "atoms), one position halo exchange and one reverse ghost-force exchange per step (NCCL "
+                       "all_to_all), energy and virial all_reduce")),
                   "step": "neighbour list + forward + backward (energy, forces, virial)",
                   "l2": "inputs smaller than L2 for water3k (re-read from L2 between steps); "
                         "per-layer aggregation buffers larger than L2 for the FCC workloads"}

@@ -110,6 +110,12 @@ _PROTOS = {
     "fsc_sparse_backward": (C.c_int, [C.POINTER(SparseConfig), C.POINTER(SparseWeights), C.POINTER(Graph),
                                       C.POINTER(IctdOutputs), P, C.c_size_t, P]),
     "fsc_sparse_status": (C.c_int, [C.POINTER(SparseConfig), I64, I64, P, P, C.POINTER(C.c_int)]),
+    "fsc_sparse_forward_step": (C.c_int, [C.POINTER(SparseConfig), C.POINTER(SparseWeights), C.POINTER(Graph),
+                                          C.c_int, P, P, P, C.c_size_t, P]),
+    "fsc_sparse_backward_step": (C.c_int, [C.POINTER(SparseConfig), C.POINTER(SparseWeights), C.POINTER(Graph),
+                                           C.c_int, C.POINTER(IctdOutputs), P, C.c_size_t, P]),
+    "fsc_sparse_feature_buffer": (C.c_int, [C.POINTER(SparseConfig), I64, I64, P, C.c_int, C.c_int,
+                                            C.POINTER(C.c_void_p)]),
     "fsc_ictd_heads": (C.c_int, [P, P, P, C.c_int, P, P, P, P, C.c_size_t, P]),
     "fsc_ictd_set_radial_path": (None, [C.c_int]),
     "fsc_ictd_set_gemm_path": (None, [C.c_int]),

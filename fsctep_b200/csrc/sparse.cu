@@ -1462,7 +1462,9 @@ float conv2_norm(const Ctx& c) {
   return (float)std::max(1e-8, (double)c.p.E / (double)std::max<int64_t>(c.p.N, 1));
 }
 
-int forward(Ctx& c) {
+// Forward in steps (fsc_sparse_forward_step): 0 = edge geometry, radial MLPs and conv1; k in
+// [1, nint) = conv2 layer k; nint = readout.
+int forward_step0(Ctx& c) {
   Plan& p = c.p;
   const fsc_graph* g = c.g;
   const fsc_sparse_weights* w = c.w;
@@ -1488,8 +1490,16 @@ int forward(Ctx& c) {
     }));
   }
   prof::mark("sparse_conv1_forward", st);
+  return FSC_OK;
+}
+
+int forward_conv2(Ctx& c, int k) {
+  Plan& p = c.p;
+  const fsc_sparse_weights* w = c.w;
+  cudaStream_t st = c.st;
+  Args a = args(c);
   const float avg = conv2_norm(c);
-  for (int k = 1; k < p.nint; ++k) {
+  {
     for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
       const int64_t nc = std::min(p.chunk, p.N - n0);
       if (p.atc) {
@@ -1509,6 +1519,13 @@ int forward(Ctx& c) {
     }
     prof::mark("sparse_conv2_forward", st);
   }
+  return FSC_OK;
+}
+
+int forward_readout(Ctx& c) {
+  Plan& p = c.p;
+  const fsc_sparse_weights* w = c.w;
+  cudaStream_t st = c.st;
   // readout: bilinear invariants of the channel concatenation, 0e products, MainNet
   RdArgs rd = rd_args(p);
   if (cudaMemsetAsync(p.scalars, 0, sizeof(float) * p.N * p.S, st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset");
@@ -1545,7 +1562,9 @@ int forward(Ctx& c) {
   return FSC_OK;
 }
 
-int backward(Ctx& c) {
+// Backward in steps (fsc_sparse_backward_step): nint = readout backward; k in [1, nint) = conv2
+// layer k backward (adds into layer k - 1's feature gradient); 0 = conv1 backward and the edge part.
+int backward_readout(Ctx& c) {
   Plan& p = c.p;
   const fsc_graph* g = c.g;
   const fsc_sparse_weights* w = c.w;
@@ -1582,9 +1601,16 @@ int backward(Ctx& c) {
   }
   prof::mark("sparse_readout_gram_backward", st);
   if (cudaMemsetAsync(p.dnp, 0, sizeof(float) * p.E * MAXR, st) != cudaSuccess) return fail(FSC_ERR_CUDA, "memset");
+  return FSC_OK;
+}
+
+int backward_conv2(Ctx& c, int k) {
+  Plan& p = c.p;
+  const fsc_sparse_weights* w = c.w;
+  cudaStream_t st = c.st;
   Args a = args(c);
   const float avg = conv2_norm(c);
-  for (int k = p.nint - 1; k >= 1; --k) {
+  {
     for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
       const int64_t nc = std::min(p.chunk, p.N - n0);
       for (int Lo = 0; Lo <= p.lmax; ++Lo) {
@@ -1613,6 +1639,14 @@ int backward(Ctx& c) {
     }
     prof::mark("sparse_conv2_backward", st);
   }
+  return FSC_OK;
+}
+
+int backward_conv1(Ctx& c) {
+  Plan& p = c.p;
+  const fsc_sparse_weights* w = c.w;
+  cudaStream_t st = c.st;
+  Args a = args(c);
   if (p.N > 0) {
     FSC_TRY(by_cpl(p.C, [&](auto cpl) {
       conv1_bwd_kernel<decltype(cpl)::value><<<(unsigned)ceil_div(p.N, 8), 256, 0, st>>>(a, w->pair_k, p.h2, p.grads[0],
@@ -1641,12 +1675,16 @@ int prepare(Ctx& c, void* workspace, size_t bytes) {
   return FSC_OK;
 }
 
-int run_forward(Ctx& c, float* energy, float* atom_energy) {
+int run_forward_step(Ctx& c, int step, float* energy, float* atom_energy) {
   Plan& p = c.p;
-  if (cudaMemsetAsync(p.acc_d, 0, sizeof(double) * kMaxGraphs * 19, c.st) != cudaSuccess ||
-      cudaMemsetAsync(p.err, 0, sizeof(int) * 64, c.st) != cudaSuccess)
-    return fail(FSC_ERR_CUDA, "memset accumulators");
-  FSC_TRY(forward(c));
+  if (step == 0) {
+    if (cudaMemsetAsync(p.acc_d, 0, sizeof(double) * kMaxGraphs * 19, c.st) != cudaSuccess ||
+        cudaMemsetAsync(p.err, 0, sizeof(int) * 64, c.st) != cudaSuccess)
+      return fail(FSC_ERR_CUDA, "memset accumulators");
+    return forward_step0(c);
+  }
+  if (step < p.nint) return forward_conv2(c, step);
+  FSC_TRY(forward_readout(c));
   const int H = p.hidden[p.n_hidden - 1];
   float* ebuf = atom_energy ? atom_energy : p.dxb;
   FSC_TRY(launch_energy(p.act_post[p.n_hidden - 1], p.N, H, c.w->out_v, c.w->out_c0, c.g->batch, c.g->num_local, ebuf,
@@ -1660,10 +1698,28 @@ int run_forward(Ctx& c, float* energy, float* atom_energy) {
   return FSC_OK;
 }
 
+int run_forward(Ctx& c, float* energy, float* atom_energy) {
+  for (int step = 0; step <= c.p.nint; ++step) FSC_TRY(run_forward_step(c, step, energy, atom_energy));
+  return FSC_OK;
+}
+
+int run_backward_edges(Ctx& c, fsc_ictd_outputs* out);
+
+int run_backward_step(Ctx& c, int step, fsc_ictd_outputs* out) {
+  if (step == c.p.nint) return backward_readout(c);
+  if (step > 0) return backward_conv2(c, step);
+  FSC_TRY(backward_conv1(c));
+  return run_backward_edges(c, out);
+}
+
 int run_backward(Ctx& c, fsc_ictd_outputs* out) {
+  for (int step = c.p.nint; step >= 0; --step) FSC_TRY(run_backward_step(c, step, out));
+  return FSC_OK;
+}
+
+int run_backward_edges(Ctx& c, fsc_ictd_outputs* out) {
   Plan& p = c.p;
   const fsc_graph* g = c.g;
-  FSC_TRY(backward(c));
   float* eg = out->edge_grad ? out->edge_grad : p.edge_grad;
   RadialTcArgs ra{};
   ra.E = p.E; ra.rad = radial(c.w); ra.nint = p.nint; ra.nb = p.nb; ra.basis_kind = c.cfg->basis_kind;
@@ -1721,6 +1777,36 @@ int fsc_sparse_backward(const fsc_sparse_config* cfg, const fsc_sparse_weights* 
   sp::Ctx c{cfg, w, g, sp::Plan{}, as_stream(stream)};
   FSC_TRY(sp::prepare(c, workspace, workspace_bytes));
   return sp::run_backward(c, out);
+}
+
+int fsc_sparse_forward_step(const fsc_sparse_config* cfg, const fsc_sparse_weights* w, const fsc_graph* g, int step,
+                            float* energy, float* atom_energy, void* workspace, size_t workspace_bytes, void* stream) {
+  sp::Ctx c{cfg, w, g, sp::Plan{}, as_stream(stream)};
+  FSC_TRY(sp::prepare(c, workspace, workspace_bytes));
+  FSC_REQUIRE(step >= 0 && step <= c.p.nint, "forward step out of range [0, num_interaction]");
+  return sp::run_forward_step(c, step, energy, atom_energy);
+}
+
+int fsc_sparse_backward_step(const fsc_sparse_config* cfg, const fsc_sparse_weights* w, const fsc_graph* g, int step,
+                             fsc_ictd_outputs* out, void* workspace, size_t workspace_bytes, void* stream) {
+  sp::Ctx c{cfg, w, g, sp::Plan{}, as_stream(stream)};
+  FSC_TRY(sp::prepare(c, workspace, workspace_bytes));
+  FSC_REQUIRE(step >= 0 && step <= c.p.nint, "backward step out of range [0, num_interaction]");
+  FSC_REQUIRE(step > 0 || out != nullptr, "outputs required for backward step 0");
+  return sp::run_backward_step(c, step, out);
+}
+
+int fsc_sparse_feature_buffer(const fsc_sparse_config* cfg, int64_t num_atoms, int64_t num_edges, void* workspace,
+                              int which, int layer, float** out) {
+  FSC_REQUIRE(out && workspace, "workspace and output pointer required");
+  FSC_TRY(sp::validate(cfg));
+  FSC_REQUIRE(which == 0 || which == 1, "which must be 0 (features) or 1 (gradients)");
+  FSC_REQUIRE(layer >= 0 && layer < cfg->num_interaction, "layer out of range");
+  sp::Plan p{};
+  Arena ar(workspace, (size_t)-1);
+  sp::layout(p, ar, cfg, num_atoms, num_edges);
+  *out = which == 0 ? p.feats[layer] : p.grads[layer];
+  return FSC_OK;
 }
 
 int fsc_sparse_status(const fsc_sparse_config* cfg, int64_t num_atoms, int64_t num_edges, void* workspace, void* stream,

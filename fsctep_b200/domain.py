@@ -355,14 +355,17 @@ def owned_receiver_graph(g, num_local: int):
 
 def layer_exchange_step(dec: Decomposition, rank: int, pos: torch.Tensor, species: torch.Tensor, engine,
                         cutoff: float, want_virial: bool = False):
-    """One energy + forces step of the ictd engine with a per-layer ghost-feature exchange (a
-    generator of collectives, like :func:`decomposed_step`): the halo ``dec.halo`` needs to cover
-    one cutoff only.  The local graph holds the edges into owned atoms; after each interaction
-    layer whose features a later layer reads, the ghost rows are overwritten by their owners'
-    rows; in the reverse pass the ghost rows' gradients go back to their owners before the layer
-    that produced them runs backward; the ghost forces (edge endpoints) go back as in
-    :func:`decomposed_step`.  Energies and virials are summed over ranks."""
+    """One energy + forces step with a per-layer ghost-feature exchange (a generator of
+    collectives, like :func:`decomposed_step`), for the ictd and the sparse engine: the halo
+    ``dec.halo`` needs to cover one cutoff only.  The local graph holds the edges into owned
+    atoms; after each interaction layer whose features a later layer reads, the ghost rows are
+    overwritten by their owners' rows; in the reverse pass the ghost rows' gradients go back to
+    their owners before the layer that produced them runs backward; the ghost forces (edge
+    endpoints) go back as in :func:`decomposed_step`.  Energies and virials are summed over ranks.
+    The sparse model's conv2 normaliser is the whole system's E / N (edges into owned atoms and
+    owned atoms, summed over ranks), as the reference computes it on the whole graph."""
     from .neighbors import build_graph
+    from .sparse import SparseEngine
 
     n = pos.shape[0]
     dev = pos.device
@@ -374,8 +377,15 @@ def layer_exchange_step(dec: Decomposition, rank: int, pos: torch.Tensor, specie
     cell_t = torch.as_tensor(dec.cell, dtype=torch.float64, device=dev).reshape(1, 3, 3)
     g = owned_receiver_graph(build_graph(pos_l, cell_t, cutoff, pbc=dec.local_pbc), n)
     batch = torch.zeros(n_all, dtype=torch.int32, device=dev)
-    # every layer on all rows (ghost rows have no edges and are overwritten), the readout on the owned
-    engine.begin_steps(pos_l, spec_l, batch, cell_t, g, num_local=n, layer_atoms=[n_all] * (nint - 1) + [n])
+    if isinstance(engine, SparseEngine):
+        counts = torch.stack([g.row_ptr[n].to(torch.float64),
+                              torch.tensor(float(n), dtype=torch.float64, device=dev)])
+        totals = yield from all_reduce_sum(counts)
+        avg = max(float(totals[0]) / max(float(totals[1]), 1.0), 1e-8)
+        engine.begin_steps(pos_l, spec_l, batch, cell_t, g, num_local=n, avg_num_neighbors=avg)
+    else:
+        # every layer on all rows (ghost rows have no edges and are overwritten), the readout on the owned
+        engine.begin_steps(pos_l, spec_l, batch, cell_t, g, num_local=n, layer_atoms=[n_all] * (nint - 1) + [n])
     for k in range(nint - 1):
         feats = engine.forward_step(k)
         yield from exchange_ghost_rows(plan, feats, n)

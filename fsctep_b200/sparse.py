@@ -225,6 +225,78 @@ class SparseEngine:
                                             C.byref(o), N.ptr(ws), ws.numel(), N.stream_ptr(dev)), "fsc_sparse_backward")
         return out
 
+    # ---- stepwise evaluation (per-layer ghost-feature exchange of a decomposition)
+    def _rows(self):
+        return sum(3 ** L for L in range(self.cfg.lmax + 1))
+
+    def feature_buffer(self, which: int, layer: int):
+        """View (num_atoms, R, C) of layer ``layer``'s features (which = 0) or their gradient
+        (which = 1) in the workspace of the last call."""
+        g = self._last[4]
+        ws = self.workspace(g.num_atoms, g.num_edges)
+        addr = C.c_void_p(0)
+        N.check(N.lib().fsc_sparse_feature_buffer(C.byref(self.ncfg), g.num_atoms, g.num_edges, N.ptr(ws), which,
+                                                  layer, C.byref(addr)), "fsc_sparse_feature_buffer")
+        off = int(addr.value) - ws.data_ptr()
+        R, Cc = self._rows(), self.cfg.channels
+        return ws[off:off + g.num_atoms * R * Cc * 4].view(torch.float32).view(g.num_atoms, R, Cc)
+
+    def begin_steps(self, pos, species, batch, cell, g: GraphCSR, num_local=None, avg_num_neighbors=None,
+                    layer_atoms=None):
+        if layer_atoms is not None:
+            raise ValueError("the sparse engine evaluates every layer on all atoms (no layer_atoms)")
+        self.ncfg.avg_num_neighbors = 0.0 if avg_num_neighbors is None else float(avg_num_neighbors)
+        pos = pos.detach().to(torch.float32).contiguous()
+        species = species.to(torch.int32).contiguous()
+        batch = batch.to(torch.int32).contiguous()
+        cell = cell.detach().to(torch.float32).reshape(-1, 3, 3).contiguous()
+        self.workspace(g.num_atoms, g.num_edges)
+        self._last = (pos, species, batch, cell, g, num_local)
+        self._step_out = (torch.empty(cell.shape[0], dtype=torch.float32, device=self.device),
+                          torch.empty(g.num_atoms, dtype=torch.float32, device=self.device))
+
+    def forward_step(self, step: int):
+        pos, species, batch, cell, g, num_local = self._last
+        ws = self.workspace(g.num_atoms, g.num_edges)
+        energy, atom_e = self._step_out
+        gs = self._graph(pos, species, batch, cell, g, cell.shape[0], num_local, None)
+        last = step == self.cfg.num_interaction
+        N.check(N.lib().fsc_sparse_forward_step(C.byref(self.ncfg), C.byref(self.weights.struct), C.byref(gs), step,
+                                                N.ptr(energy) if last else None, N.ptr(atom_e) if last else None,
+                                                N.ptr(ws), ws.numel(), N.stream_ptr(self.device)),
+                f"fsc_sparse_forward_step({step})")
+        return (energy, atom_e) if last else self.feature_buffer(0, step)
+
+    def begin_backward(self, energy_weight=None, want_virial=True, want_cell_grad=False, want_edge_grad=False):
+        g, B = self._last[4], self._last[3].shape[0]
+        dev = self.device
+        out = {"forces": torch.empty(g.num_atoms, 3, dtype=torch.float32, device=dev)}
+        if want_virial:
+            out["virial"] = torch.empty(B, 3, 3, dtype=torch.float32, device=dev)
+        if want_cell_grad:
+            out["cell_grad"] = torch.empty(B, 3, 3, dtype=torch.float32, device=dev)
+        if want_edge_grad:
+            out["edge_grad"] = torch.empty(g.num_edges, 3, dtype=torch.float32, device=dev)
+        o = N.IctdOutputs()
+        o.forces = out["forces"].data_ptr()
+        o.virial = out["virial"].data_ptr() if want_virial else 0
+        o.cell_grad = out["cell_grad"].data_ptr() if want_cell_grad else 0
+        o.edge_grad = out["edge_grad"].data_ptr() if want_edge_grad else 0
+        if energy_weight is not None:
+            energy_weight = energy_weight.detach().to(torch.float32).reshape(-1).contiguous()
+        self._bwd = (out, o, energy_weight)
+        return out
+
+    def backward_step(self, step: int):
+        pos, species, batch, cell, g, num_local = self._last
+        ws = self.workspace(g.num_atoms, g.num_edges)
+        out, o, ew = self._bwd
+        gs = self._graph(pos, species, batch, cell, g, cell.shape[0], num_local, ew)
+        N.check(N.lib().fsc_sparse_backward_step(C.byref(self.ncfg), C.byref(self.weights.struct), C.byref(gs),
+                                                 step, C.byref(o), N.ptr(ws), ws.numel(), N.stream_ptr(self.device)),
+                f"fsc_sparse_backward_step({step})")
+        return self.feature_buffer(1, step - 1) if step >= 1 else out
+
     def status(self) -> int:
         pos, species, batch, cell, g, num_local = self._last
         ws = self.workspace(g.num_atoms, g.num_edges)

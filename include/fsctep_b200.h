@@ -417,6 +417,17 @@ int fsc_sparse_backward(const fsc_sparse_config* cfg, const fsc_sparse_weights* 
                         fsc_ictd_outputs* out, void* workspace, size_t workspace_bytes, void* stream);
 int fsc_sparse_status(const fsc_sparse_config* cfg, int64_t num_atoms, int64_t num_edges, void* workspace,
                       void* stream, int* status_host);
+/* Stepwise pure-cartesian-sparse evaluation, as fsc_ictd_forward_step / fsc_ictd_backward_step
+ * (same step numbering; the reference sparse model has no sync_after_scatter hook, but a
+ * per-layer ghost-feature exchange of a spatial decomposition uses the steps).  Feature buffers:
+ * float [num_atoms][R][C], R = sum_{L <= lmax} 3^L rows (rank-L Cartesian components, row-major),
+ * channel innermost. */
+int fsc_sparse_forward_step(const fsc_sparse_config* cfg, const fsc_sparse_weights* w, const fsc_graph* g, int step,
+                            float* energy, float* atom_energy, void* workspace, size_t workspace_bytes, void* stream);
+int fsc_sparse_backward_step(const fsc_sparse_config* cfg, const fsc_sparse_weights* w, const fsc_graph* g, int step,
+                             fsc_ictd_outputs* out, void* workspace, size_t workspace_bytes, void* stream);
+int fsc_sparse_feature_buffer(const fsc_sparse_config* cfg, int64_t num_atoms, int64_t num_edges, void* workspace,
+                              int which, int layer, float** out);
 
 /* ---- stage timing ------------------------------------------------------
  * When enabled, the engine records a CUDA event after each stage on its stream;

@@ -166,3 +166,41 @@ def test_decomposed_sparse_engine_matches_single_domain(dims):
         assert U.rel_max(r["virial"].cpu().numpy(), ref_v) <= 1e-4
     assert U.rel_max(F, ref_f) <= 1e-4, U.rel_max(F, ref_f)
     assert all(r["num_ghosts"] > 0 for r in res)
+
+
+@pytest.mark.parametrize("dims", [(2, 1, 1), (2, 2, 1)])
+def test_sparse_layer_exchange_matches_single_domain(dims):
+    """The pure-cartesian-sparse engine with the per-layer ghost-feature exchange (one-cutoff halo,
+    whole-system E / N through the owned edge and atom counts)."""
+    from fsctep_b200.sparse import SparseConfig, SparseEngine
+    import golden_io
+
+    cfg, sd, _ = golden_io.sparse_case("b")
+    scfg = SparseConfig(channels=int(cfg["channels"]), lmax=int(cfg["lmax"]),
+                        num_interaction=int(cfg["num_interaction"]), number_of_basis=int(cfg["number_of_basis"]),
+                        max_radius=float(cfg["max_radius"]), function_type=str(cfg["function_type"]),
+                        max_atomvalue=int(cfg["max_atomvalue"]))
+    eng = SparseEngine(sd, scfg, "cuda")
+    s = systems.fcc_crystal(n_cells=(9, 9, 9), seed=43)
+    dev = torch.device("cuda")
+    pos, cell = torch.tensor(s["pos"], device=dev), torch.tensor(s["cell"], device=dev)
+    Z = torch.tensor(s["Z"], device=dev, dtype=torch.int32)
+    ref = eng.energy_forces(pos, Z, torch.zeros_like(Z), cell, build_graph(pos, cell, 5.0))
+    ref_e = ref["energy"].double().item()
+    ref_f = ref["forces"].double().cpu().numpy()
+    ref_v = ref["virial"][0].double().cpu().numpy()
+    c0 = s["cell"][0]
+    dec = D.Decomposition(c0, dims, scfg.max_radius)
+    owned = [_owned(dec, r, s["pos"], c0) for r in range(dec.world)]
+    engines = [SparseEngine(sd, scfg, "cuda") for _ in owned]  # one workspace per emulated rank
+    gens = [D.layer_exchange_step(dec, r, pos[torch.tensor(o, device=dev)], Z[torch.tensor(o, device=dev)],
+                                  engines[r], scfg.max_radius, want_virial=True) for r, o in enumerate(owned)]
+    res = D.run_local(gens)
+    torch.cuda.synchronize()
+    F = np.zeros_like(ref_f)
+    for o, r, er in zip(owned, res, engines):
+        assert er.status() == 0
+        F[o] = r["forces"].double().cpu().numpy()
+        assert abs(r["energy"].item() - ref_e) <= 1e-5 * abs(ref_e), (r["energy"].item(), ref_e)
+        assert U.rel_max(r["virial"].cpu().numpy(), ref_v) <= 1e-4
+    assert U.rel_max(F, ref_f) <= 1e-4, U.rel_max(F, ref_f)
