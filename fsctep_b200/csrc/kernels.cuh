@@ -126,7 +126,7 @@ struct GemmArgs {
   const float* bias;
   int accumulate;
   float alpha;  // extra scale of the product (0 means 1)
-  int precise;  // long K with heavy cancellation: shortest tensor-core chains (CUDA cores: Kahan sums)
+  int precise;  // long K with heavy cancellation: shortest tensor-core chains
 };
 int launch_gemm(const GemmArgs& a, cudaStream_t st);
 
