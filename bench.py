@@ -43,7 +43,14 @@ WORKLOADS = {
                    max_atomvalue=30, cpu_cells=(2, 2, 2)),
     "fcc250k": dict(model="sparse", system="fcc", cells=(50, 50, 25), channels=128, lmax=3, num_interaction=3,
                     max_atomvalue=30, cpu_cells=(2, 2, 2)),
+    # batched small systems (one GPU): config 1 (E + F + stress) and config 3 (o3, field, heads)
+    "frames8": dict(model="ictd", system="frames", n_frames=8, n_atoms=96, box=10.0, channels=32, num_interaction=2,
+                    basis="bessel", max_atomvalue=10),
+    "mol256": dict(model="o3", system="molecules", n_mol=256, channels=64, num_interaction=3, basis="gaussian",
+                   max_atomvalue=10),
 }
+BATCHED = ("frames", "molecules")
+O3_HEADS = {"dipole": {"irreps": ["1o"], "reduce": "sum"}, "polarizability": {"ls": [0, 2], "reduce": "sum"}}
 CPU_KEYS = ("value", "unit", "cores", "kind", "sample", "steps", "warmup", "statistic", "cpu_model")
 
 
@@ -59,14 +66,36 @@ def model_cfg(w):
     from fsctep_b200.ictd import ICTDConfig
 
     return ICTDConfig(channels=w["channels"], num_interaction=w["num_interaction"], number_of_basis=8,
-                      max_radius=5.0, function_type="gaussian", max_atomvalue=w["max_atomvalue"])
+                      max_radius=5.0, function_type=w.get("basis", "gaussian"), max_atomvalue=w["max_atomvalue"],
+                      o3=w["model"] == "o3")
 
 
 def seeded_weights(cfg, seed=2024):
-    from fsctep_b200.models import reference_state_dict_shapes
+    from fsctep_b200.models import PureCartesianICTDO3TransformerLayer, reference_state_dict_shapes
     from fsctep_b200.weights import seeded_state_dict
 
-    return seeded_state_dict(reference_state_dict_shapes(cfg), seed)
+    if not cfg.o3:
+        return seeded_state_dict(reference_state_dict_shapes(cfg), seed)
+    with torch.device("meta"):
+        m = PureCartesianICTDO3TransformerLayer(
+            max_embed_radius=cfg.max_radius, main_max_radius=cfg.max_radius, main_number_of_basis=cfg.number_of_basis,
+            hidden_dim_conv=cfg.channels, num_interaction=cfg.num_interaction, function_type_main=cfg.function_type,
+            max_atomvalue=cfg.max_atomvalue, external_tensor_rank=1, external_tensor_irrep="1o",
+            physical_tensor_outputs=O3_HEADS, o3_active_irreps=list(cfg.o3_irreps))
+    return seeded_state_dict({k: tuple(v.shape) for k, v in m.state_dict().items()}, seed)
+
+
+def batched_system(w, seed=1000):
+    """Config 1's periodic frames or config 3's molecules (with one field vector per molecule)."""
+    from fsctep_b200 import systems
+
+    if w["system"] == "frames":
+        s = systems.random_frames(n_frames=w["n_frames"], n_atoms=w["n_atoms"], box=w["box"], seed=seed)
+    else:
+        s = systems.organic_molecules(n_mol=w["n_mol"], seed=seed)
+        s["field"] = np.random.default_rng(seed + 1).normal(scale=0.05, size=(w["n_mol"], 3))
+    s["frame_ptr"] = np.concatenate([[0], np.cumsum(np.bincount(s["batch"], minlength=s["cell"].shape[0]))])
+    return s
 
 
 class ClockSampler:
@@ -360,6 +389,75 @@ def run_native(args, rank, world, device):
                 ghosts=info["ghosts"], dims=dims)
 
 
+def run_batched(args, rank, world, device):
+    """Config 1 (8 periodic frames, E + F + stress) or config 3 (256 molecules, o3 model with an
+    external field per molecule, dipole and polarizability heads, E + F) on one GPU: one step =
+    batched neighbour list + forward (+ heads) + backward."""
+    from fsctep_b200.ictd import ICTDEngine
+    from fsctep_b200.neighbors import build_graph
+
+    w = WORKLOADS[args.workload]
+    cfg = model_cfg(w)
+    eng = ICTDEngine(seeded_weights(cfg), cfg, device)
+    sysd = batched_system(w)
+    n = sysd["pos"].shape[0]
+    pos_d = torch.tensor(sysd["pos"], device=device)
+    cell_d = torch.tensor(sysd["cell"], device=device)
+    Z = torch.tensor(sysd["Z"], device=device, dtype=torch.int32)
+    batch = torch.tensor(sysd["batch"], device=device, dtype=torch.int32)
+    fp, pbc = sysd["frame_ptr"], sysd["pbc"]
+    field = torch.tensor(sysd["field"], device=device) if "field" in sysd else None
+    stress = w["system"] == "frames"
+    B = cell_d.shape[0]
+    pos_h = torch.tensor(sysd["pos"]).pin_memory()
+    forces_h = torch.empty(n, 3, dtype=torch.float32).pin_memory()
+    energy_h = torch.empty(B, dtype=torch.float32).pin_memory()
+    info = {}
+
+    def step(pos, cell):
+        g = build_graph(pos, cell, cfg.max_radius, frame_ptr=fp, pbc=pbc)
+        energy, _ = eng.forward(pos, Z, batch, cell, g, field=field)
+        if cfg.o3:
+            info["heads"] = eng.heads()
+        out = eng.backward(want_virial=stress)
+        info["edges"] = g.num_edges
+        return energy, out["forces"]
+
+    def e2e_step():
+        energy, forces = step(pos_h.to(device, non_blocking=True), cell_d)
+        forces_h.copy_(forces, non_blocking=True)
+        energy_h.copy_(energy, non_blocking=True)
+
+    for _ in range(args.warmup):
+        step(pos_d, cell_d)
+    torch.cuda.synchronize()
+    if eng.status() != 0:
+        raise RuntimeError(f"engine status {eng.status()}")
+    ours = None
+    if not args.no_launch_count:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step(pos_d, cell_d)
+            torch.cuda.synchronize()
+        ours = sum(e.count for e in prof.key_averages() if "fsc::" in e.key or "cub::" in e.key)
+    torch.cuda.synchronize()
+    ms_total, clk = timed_steps(args, world, lambda: step(pos_d, cell_d))
+    stage_ms = stage_pass(args, world, lambda: step(pos_d, cell_d))
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    return dict(n=n, E=info["edges"], ms_step=ms_total / args.steps, ms_e2e=e0.elapsed_time(e1) / args.steps,
+                stage_ms=stage_ms, clocks=clk, launches=None if ours is None else ours * args.steps, cfg=cfg,
+                ghosts=0, dims=(1, 1, 1), graphs=B)
+
+
 def run_sparse(args, rank, world, device):
     """pure-cartesian-sparse energy + forces (+ virial) of a seeded crystal or water box; under
     torchrun the FCC crystal grows with the ranks and is decomposed as the ictd workloads are."""
@@ -468,6 +566,9 @@ def cpu_sample(workload):
     from fsctep_b200 import systems
 
     w = WORKLOADS[workload]
+    if w.get("system") in BATCHED:  # configs 1 and 3 run in full on the CPU
+        sysd = batched_system(w)
+        return sysd, f"the full workload ({sysd['pos'].shape[0]} atoms in {sysd['cell'].shape[0]} graphs)"
     rep = CPU_SAMPLES[workload]
     if w["model"] == "ictd":
         sysd = systems.diamond_crystal(n_cells=rep, seed=1000, Z=w["Z"])
@@ -491,10 +592,17 @@ def _reference_model(w, sd):
     kw = dict(max_embed_radius=5.0, main_max_radius=5.0, main_number_of_basis=8, hidden_dim_conv=w["channels"],
               hidden_dim_sh=32, hidden_dim=64, num_interaction=w["num_interaction"], function_type_main="gaussian",
               max_atomvalue=w["max_atomvalue"], device=torch.device("cpu"))
+    kw["function_type_main"] = w.get("basis", "gaussian")
     if w["model"] == "ictd":
         from molecular_force_field.models.pure_cartesian_ictd_layers_full import PureCartesianICTDTransformerLayer
 
         m = PureCartesianICTDTransformerLayer(lmax=2, internal_compute_dtype=torch.float32, **kw)
+    elif w["model"] == "o3":
+        from molecular_force_field.models.pure_cartesian_ictd_layers_o3 import PureCartesianICTDO3TransformerLayer
+
+        m = PureCartesianICTDO3TransformerLayer(lmax=2, internal_compute_dtype=torch.float32, external_tensor_rank=1,
+                                                external_tensor_irrep="1o", physical_tensor_outputs=O3_HEADS,
+                                                o3_active_irreps=["0e", "1e", "1o", "2e"], **kw)
     else:
         from molecular_force_field.models.pure_cartesian_sparse_layers import PureCartesianSparseTransformerLayer
 
@@ -516,9 +624,14 @@ def cpu_reference(workload, steps, warmup):
     w = WORKLOADS[workload]
     sparse = w["model"] == "sparse"
     cfg = sparse_cfg(w) if sparse else model_cfg(w)
+    stress = sparse or w.get("system") == "frames"  # the GPU step's virial / stress
     sd = sparse_weights(cfg) if sparse else seeded_weights(cfg)
     sysd, what = cpu_sample(workload)
-    src, dst, S = ON.neighbor_list(sysd["pos"], sysd["cell"][0], 5.0)
+    batched = w.get("system") in BATCHED
+    if batched:
+        src, dst, S = ON.batched_neighbor_list(sysd["pos"], sysd["batch"], sysd["cell"], 5.0, sysd["pbc"])
+    else:
+        src, dst, S = ON.neighbor_list(sysd["pos"], sysd["cell"][0], 5.0)
     pos0 = torch.tensor(sysd["pos"], dtype=torch.float32)
     Z, b = torch.tensor(sysd["Z"]).long(), torch.tensor(sysd["batch"]).long()
     src_t, dst_t, S_t = torch.tensor(src).long(), torch.tensor(dst).long(), torch.tensor(S, dtype=torch.float32)
@@ -527,15 +640,21 @@ def cpu_reference(workload, steps, warmup):
     if kind == "reference":
         model = _reference_model(w, sd)
 
+        kw = {}
+        if "field" in sysd:
+            kw = {"external_tensor": torch.tensor(sysd["field"], dtype=torch.float32), "return_physical_tensors": True}
+
         def step():
             pos = pos0.clone().requires_grad_(True)
-            if sparse:  # virial through the strain derivative (trainer convention)
-                strain = torch.zeros(1, 3, 3, requires_grad=True)
+            if stress:  # virial through the strain derivative (trainer convention)
+                nb = cell.shape[0]
+                strain = torch.zeros(nb, 3, 3, requires_grad=True)
                 D = torch.eye(3) + 0.5 * (strain + strain.transpose(-1, -2))
-                e = model(pos @ D[0], Z, b, src_t, dst_t, S_t, torch.bmm(cell, D))
+                e = model(torch.einsum("ni,nij->nj", pos, D[b]), Z, b, src_t, dst_t, S_t, torch.bmm(cell, D))
                 torch.autograd.grad(e.sum(), [pos, strain])
             else:
-                e = model(pos, Z, b, src_t, dst_t, S_t, cell)
+                out = model(pos, Z, b, src_t, dst_t, S_t, cell, **kw)
+                e = out[0] if isinstance(out, tuple) else out
                 torch.autograd.grad(e.sum(), [pos])
         how = "the reference's own PyTorch modules (baseline/_ref, unmodified; import shims: bare models package, " \
               "torch_scatter -> its utils/scatter fallback, e3nn soft_one_hot_linspace restated)"
@@ -545,16 +664,18 @@ def cpu_reference(workload, steps, warmup):
 
         sd32 = {k: v.float() for k, v in sd.items()}
         args = (pos0, Z, b, src_t, dst_t, S_t, cell)
+        if w["model"] == "o3":
+            raise SystemExit("the o3 workload's CPU leg needs the reference installed under baseline/_ref")
         if sparse:
             def step():
                 OS.sparse_energy_forces_stress(sd32, cfg, *args, want_stress=True)
         else:
-            ocfg = OM.ICTDConfig(channels=cfg.channels, num_interaction=cfg.num_interaction, function_type="gaussian",
-                                 max_atomvalue=cfg.max_atomvalue)
+            ocfg = OM.ICTDConfig(channels=cfg.channels, num_interaction=cfg.num_interaction,
+                                 function_type=cfg.function_type, max_atomvalue=cfg.max_atomvalue)
             tabs = OM._TPTables(2, torch.float32)
 
             def step():
-                OM.energy_forces_stress(sd32, ocfg, *args, want_stress=False, tabs=tabs)
+                OM.energy_forces_stress(sd32, ocfg, *args, want_stress=stress, tabs=tabs)
         how = "the oracle port of the reference CPU path (the reference is not installed under baseline/_ref)"
     for _ in range(warmup):
         step()
@@ -572,7 +693,8 @@ def cpu_reference(workload, steps, warmup):
         cpu_model = "unknown"
     return {"value": n / med, "unit": "atom-steps/s", "cores": threads, "kind": kind,
             "sample": f"{what}, {len(src)} edges; fp32 PyTorch eager, energy + forces"
-                      + (" + virial" if sparse else "") + f", neighbour list excluded; {how}",
+                      + (" + virial" if stress else "") + (" + field and heads" if "field" in sysd else "")
+                      + f", neighbour list excluded; {how}",
             "steps": steps, "warmup": warmup, "statistic": "median", "cpu_model": cpu_model,
             "seconds_per_step": med}
 
@@ -603,9 +725,12 @@ def main():
     metric = "atom-steps/s (E+F)"
     w = WORKLOADS[args.workload]
     sparse = w["model"] == "sparse"
+    batched = w.get("system") in BATCHED
+    if batched and (world > 1 or args.gpus > 1):
+        raise SystemExit(f"--workload {args.workload}: runs on one GPU")
     if sparse and w["system"] != "fcc" and (world > 1 or args.gpus > 1):
         raise SystemExit(f"--workload {args.workload}: runs on one GPU (the FCC workloads decompose over GPUs)")
-    n_atoms = int(np.prod(w["cells"])) * 8 if not sparse else None
+    n_atoms = int(np.prod(w["cells"])) * 8 if not (sparse or batched) else None
     config = {"workload": f"{args.workload}: pure-cartesian-ictd diamond Si {n_atoms} atoms (config 4)",
               "model": "pure-cartesian-ictd", "channels": w["channels"], "num_interaction": w["num_interaction"],
               "lmax": 2, "cutoff": 5.0, "radial_basis": "gaussian x8", "atoms_per_gpu": n_atoms if args.scaling == "weak" else n_atoms // max(args.gpus, 1),
@@ -648,6 +773,21 @@ def main():
                   "l2": "inputs smaller than L2 for water3k (re-read from L2 between steps); "
                         "per-layer aggregation buffers larger than L2 for the FCC workloads"}
 
+    if batched:
+        cfgb = model_cfg(w)
+        if w["system"] == "frames":
+            what = (f"config 1: {w['n_frames']} periodic frames of {w['n_atoms']} atoms, uniform in a {w['box']} A "
+                    "cube (0.9 A rejection), 3 species; pure-cartesian-ictd C 32, 2 layers, 8 bessel; E + F + stress")
+        else:
+            what = (f"config 3: {w['n_mol']} non-periodic organic-like molecules of 10-30 atoms (C:H:N:O 3:5:1:1, "
+                    "bonded chains 1.1-1.5 A); pure-cartesian-ictd-o3 irreps 0e,1e,1o,2e, C 64, 3 layers, external "
+                    "1o field N(0, 0.05) per molecule, dipole + polarizability heads; E + F")
+        config = {"workload": f"{args.workload}: {what}", "model": "pure-cartesian-ictd" + ("-o3" if cfgb.o3 else ""),
+                  "channels": w["channels"], "num_interaction": w["num_interaction"], "lmax": 2, "cutoff": 5.0,
+                  "radial_basis": f"{w['basis']} x8", "parallelism": "single",
+                  "step": "batched neighbour list + forward" + (" + heads" if cfgb.o3 else "") + " + backward",
+                  "l2": "inputs smaller than L2 (re-read from L2 between steps)"}
+
     if args.impl == "reference":
         if rank != 0:
             return
@@ -666,7 +806,10 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300))
     device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(device)
-    res = run_sparse(args, rank, world, device) if sparse else run_native(args, rank, world, device)
+    if batched:
+        res = run_batched(args, rank, world, device)
+    else:
+        res = run_sparse(args, rank, world, device) if sparse else run_native(args, rank, world, device)
     n, E = res["n"], res["E"]
     n_total = n
     if world > 1:  # atoms of all ranks (blocks of a strong-scaling crystal differ slightly)

@@ -53,3 +53,24 @@ def test_fp32_context():
     assert bench.fp32_context(roof, {"sm_mhz": None, "reasons": ["no samples"]})["sm_mhz"] == 1965.0
     assert bench.fp32_context({"bound": "tensor", "algorithmic_tflops": 300.0}, {"sm_mhz": 1965.0}) is None
     assert bench.fp32_context(None, None) is None
+
+
+def test_batched_workloads_match_configs_1_and_3():
+    """frames8 = config 1 (8 periodic frames of 96 atoms in a 10 A box, ictd C 32, 2 layers,
+    8 bessel); mol256 = config 3 (256 molecules of 10-30 atoms, o3 C 64, 3 layers, one field
+    vector per molecule)."""
+    w = bench.WORKLOADS["frames8"]
+    s = bench.batched_system(w)
+    assert s["pos"].shape == (8 * 96, 3) and s["cell"].shape == (8, 3, 3) and tuple(s["pbc"]) == (True,) * 3
+    assert len(set(s["Z"].tolist())) == 3
+    cfg = bench.model_cfg(w)
+    assert (cfg.channels, cfg.num_interaction, cfg.function_type, cfg.o3) == (32, 2, "bessel", False)
+    assert list(s["frame_ptr"]) == list(range(0, 8 * 96 + 1, 96))
+    w = bench.WORKLOADS["mol256"]
+    s = bench.batched_system(w)
+    sizes = s["frame_ptr"][1:] - s["frame_ptr"][:-1]
+    assert len(sizes) == 256 and sizes.min() >= 10 and sizes.max() <= 30 and s["field"].shape == (256, 3)
+    cfg = bench.model_cfg(w)
+    assert (cfg.channels, cfg.num_interaction, cfg.o3) == (64, 3, True)
+    sd = bench.seeded_weights(cfg)
+    assert any(k.startswith("physical_tensor_heads.") for k in sd)
