@@ -239,17 +239,51 @@ TRAFFIC_PER_NODE = {
 }
 
 
-def fp32_context(roofline, clocks, sms=148):
-    """The dominant kernel's FP32 rate against the nominal CUDA-core FP32 peak (sms x 128 lanes x 2
-    FLOP x the median SM clock sampled during the timed region; no measured FP32 peak exists for
-    this pool).  Only for the CUDA-core kernels, which the HBM roofline undersells."""
+def fp32_context(roofline, clocks, sms=148, measured=None):
+    """The dominant kernel's FP32 rate against the CUDA-core FP32 peak: ``measured`` (the FMA probe
+    of this run, :func:`measure_fp32_peak`) when given, else the nominal sms x 128 lanes x 2 FLOP x
+    the median SM clock sampled during the timed region.  Only for the CUDA-core kernels, which the
+    HBM roofline undersells."""
     if not roofline or roofline.get("bound") != "hbm" or roofline.get("algorithmic_tflops") is None:
         return None
     mhz = (clocks or {}).get("sm_mhz") or (clocks or {}).get("sm_max_mhz") or 1965.0
-    peak = sms * 128 * 2 * float(mhz) * 1e6 / 1e12
     ach = float(roofline["algorithmic_tflops"])
-    return {"achieved_tflops": ach, "peak_tflops": peak, "frac": ach / peak, "sm_mhz": float(mhz),
+    nominal = sms * 128 * 2 * float(mhz) * 1e6 / 1e12
+    if measured:
+        return {"achieved_tflops": ach, "peak_tflops": measured["tflops"], "frac": ach / measured["tflops"],
+                "sm_mhz": float(mhz), "nominal_tflops": nominal,
+                "peak_source": "measured: " + measured["how"]}
+    return {"achieved_tflops": ach, "peak_tflops": nominal, "frac": ach / nominal, "sm_mhz": float(mhz),
             "peak_source": f"nominal: {sms} SMs x 128 FP32 lanes x 2 FLOP x SM clock"}
+
+
+def measure_fp32_peak(device, reps=5):
+    """FP32 CUDA-core throughput of this GPU: the library's FMA probe (8 independent chains per
+    thread, 8 blocks of 256 threads per SM), scalar and packed two-lane FMAs, best of ``reps``
+    CUDA-event-timed launches after a warm-up; the faster form is the peak."""
+    from fsctep_b200 import _native as NAT
+
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    blocks = 8 * sms
+    out = torch.empty(blocks * 256, dtype=torch.float32, device=device)
+    flops = NAT.C.c_double(0.0)
+    best = {}
+    for packed in (0, 1):
+        times = []
+        for r in range(reps + 1):
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record()
+            NAT.check(NAT.lib().fsc_fp32_fma_probe(packed, blocks, 4096, NAT.ptr(out), NAT.C.byref(flops),
+                                                   NAT.stream_ptr(device)), "fsc_fp32_fma_probe")
+            t1.record()
+            torch.cuda.synchronize()
+            if r:
+                times.append(t0.elapsed_time(t1))
+        best["packed" if packed else "scalar"] = flops.value / (min(times) / 1e3) / 1e12
+    form = max(best, key=best.get)
+    return {"tflops": best[form], "scalar_tflops": best["scalar"], "packed_tflops": best["packed"],
+            "how": f"FMA probe (fsc_fp32_fma_probe, {form} FMAs, {blocks} x 256 threads, best of {reps}, "
+                   "CUDA events)"}
 
 
 def timed_steps(args, world, step):
@@ -852,7 +886,8 @@ def main():
                                 peak_source=pk["source"] + " bf16 dense (" + how + ")")
     if roofline is not None:
         try:
-            ctx = fp32_context(roofline, res["clocks"], torch.cuda.get_device_properties(device).multi_processor_count)
+            ctx = fp32_context(roofline, res["clocks"], torch.cuda.get_device_properties(device).multi_processor_count,
+                               measure_fp32_peak(device))
         except Exception:  # reporting context only: never block the line
             ctx = None
         if ctx is not None:

@@ -42,6 +42,12 @@ int fsc_version(void);
 /* 1 when the library was built with its CUDA kernels (always, for this build).
  * Replaces `_C_ictd_tp.has_cuda()` (csrc/ictd_tp.cpp:516-522). */
 int fsc_has_cuda(void);
+/* FP32 CUDA-core throughput probe: launches `blocks` x 256 threads, each running 8 independent
+ * fp32 FMA chains of 16 * iters steps (packed != 0: two-lane packed FMAs), and writes the launch's
+ * FLOP count to *flops; the caller times it with events on `stream`.  `out`: a device buffer of
+ * blocks * 256 floats (written only to keep the chains live).  No reference counterpart: the
+ * measured denominator of the CUDA-core kernels' FP32 roofline. */
+int fsc_fp32_fma_probe(int packed, int blocks, int iters, float* out, double* flops, void* stream);
 
 /* ---- `_C_ictd_tp` operator family (csrc/ictd_tp.cpp:137-497) -------------
  * Shapes follow the reference TORCH_CHECKs (csrc/ictd_tp.cpp:78-108):

@@ -74,3 +74,10 @@ def test_batched_workloads_match_configs_1_and_3():
     assert (cfg.channels, cfg.num_interaction, cfg.o3) == (64, 3, True)
     sd = bench.seeded_weights(cfg)
     assert any(k.startswith("physical_tensor_heads.") for k in sd)
+
+
+def test_fp32_context_uses_the_measured_peak():
+    roof = {"bound": "hbm", "algorithmic_tflops": 20.0}
+    ctx = bench.fp32_context(roof, {"sm_mhz": 1965.0}, measured={"tflops": 80.0, "how": "probe"})
+    assert ctx["peak_tflops"] == 80.0 and ctx["frac"] == 0.25 and ctx["peak_source"] == "measured: probe"
+    assert ctx["nominal_tflops"] == pytest.approx(148 * 128 * 2 * 1965e6 / 1e12)
