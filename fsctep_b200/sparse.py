@@ -315,3 +315,36 @@ class SparseEngine:
             v = out["virial"]
             out["stress"] = 0.5 * (v + v.transpose(1, 2)) / vol.view(-1, 1, 1)
         return out
+
+
+# Field order of the core.pt weight blob of fsctep::sparse_atom_energy (torch_ops/ictd_op.cpp).
+SPARSE_BLOB_FIELDS = (["rad_w1", "rad_b1", "rad_w2", "rad_b2", "pair_k", "mix", "mixT", "wread_p", "wread_s", "pairs",
+                       "mn_in_g", "mn_in_b"] + [f"mn_w{k}" for k in range(4)] + [f"mn_b{k}" for k in range(4)]
+                      + [f"mn_g{k}" for k in range(4)] + [f"mn_beta{k}" for k in range(4)] + ["out_v"])
+
+
+def sparse_weight_blob(packed: "PackedSparseWeights", cfg: SparseConfig):
+    """One float32 device tensor holding every packed sparse weight array (int32 arrays
+    bit-cast), each field 256-byte aligned, plus the integer / float configuration lists of the
+    core.pt op."""
+    parts, offs, cur = [], [], 0
+    for name in SPARSE_BLOB_FIELDS:
+        t = packed.tensors.get(name)
+        if t is None:
+            offs.append(-1)
+            continue
+        flat = t.reshape(-1)
+        flat = flat.view(torch.float32) if flat.dtype == torch.int32 else flat.to(torch.float32)
+        pad = (-cur) % 64
+        if pad:
+            parts.append(torch.zeros(pad, dtype=torch.float32, device=flat.device))
+            cur += pad
+        offs.append(cur)
+        parts.append(flat)
+        cur += flat.numel()
+    blob = torch.cat(parts).contiguous()
+    nc = cfg.native()
+    icfg = [nc.channels, nc.lmax, nc.num_interaction, nc.number_of_basis, nc.basis_kind, nc.num_species,
+            nc.invariant_channels, nc.n_hidden] + [int(nc.hidden[k]) for k in range(4)] + [nc.n_out] + offs
+    fcfg = [float(cfg.max_radius), float(packed.out_c0)]
+    return blob, icfg, fcfg

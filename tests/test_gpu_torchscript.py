@@ -72,3 +72,67 @@ def test_double_backward_is_refused(tmp_path):
     e = core(*args[:7], ev, args[8]).sum()
     with pytest.raises(RuntimeError, match="double backward"):
         torch.autograd.grad(e, ev, create_graph=True)
+
+
+def _one_graph(c, b=0):
+    """Graph b of a batched fixture as a one-graph case (atoms renumbered from 0)."""
+    idx = np.nonzero(c["batch"] == b)[0]
+    n0 = idx[0]
+    e = np.nonzero(c["batch"][c["edge_dst"]] == b)[0]
+    return {"pos": c["pos"][idx], "Z": c["Z"][idx], "edge_src": c["edge_src"][e] - n0,
+            "edge_dst": c["edge_dst"][e] - n0, "edge_shifts": c["edge_shifts"][e], "cell": c["cell"][b:b + 1]}
+
+
+def _lammps_like_field(core, c, nlocal, field):
+    dev = torch.device("cuda")
+    pos = torch.tensor(c["pos"], device=dev, dtype=torch.float32).requires_grad_(True)
+    A = torch.tensor(c["Z"], device=dev).long()
+    batch = torch.zeros(pos.shape[0], dtype=torch.long, device=dev)
+    src = torch.tensor(c["edge_src"], device=dev).long()
+    dst = torch.tensor(c["edge_dst"], device=dev).long()
+    shifts = torch.tensor(c["edge_shifts"], device=dev, dtype=torch.float32)
+    cell = torch.tensor(c["cell"], device=dev, dtype=torch.float32)[:1]
+    edge_vec = pos[dst] - pos[src] + torch.einsum("ni,nij->nj", shifts, cell[batch[src]])
+    atom_e = core(pos, A, batch, src, dst, shifts, cell, edge_vec, field)
+    (gpos,) = torch.autograd.grad(atom_e.view(-1)[:nlocal].sum(), [pos])
+    return atom_e.detach().view(-1).cpu().numpy(), -gpos.cpu().numpy()
+
+
+def test_o3_core_pt_with_field_matches_reference(tmp_path):
+    """pure-cartesian-ictd-o3 core.pt with its external field as the traced core's external_tensor."""
+    import golden_io
+    from fsctep_b200.ictd import ICTDConfig
+
+    cfg, sd, c = golden_io.o3_case("a")
+    icfg = ICTDConfig(channels=int(cfg["channels"]), lmax=2, num_interaction=int(cfg["num_interaction"]),
+                      number_of_basis=int(cfg["number_of_basis"]), max_radius=float(cfg["max_radius"]),
+                      function_type=str(cfg["function_type"]), max_atomvalue=int(cfg["max_atomvalue"]), o3=True)
+    path = str(tmp_path / "core_o3.pt")
+    TS.export_core(sd, icfg, path)
+    core = torch.jit.load(path, map_location="cuda")
+    c1 = _one_graph(c, 0)
+    field = torch.tensor(c["field"][0], device="cuda", dtype=torch.float32)
+    n = c1["pos"].shape[0]
+    ae, F = _lammps_like_field(core, c1, n, field)
+    assert abs(ae.sum() - c["ref64_energy"][0]) <= U.E_RTOL * np.abs(c["ref64_energy"]).max()
+    ref_f = c["ref64_forces"][c["batch"] == 0]
+    assert U.rel_max(F, ref_f) <= U.F_RTOL
+    np.testing.assert_allclose(ae, c["ref64_atom_energy"][c["batch"] == 0], rtol=1e-4, atol=1e-4)
+
+
+def test_sparse_core_pt_matches_reference(tmp_path):
+    import golden_io
+    from fsctep_b200.sparse import SparseConfig
+
+    cfg, sd, c = golden_io.sparse_case("a")
+    scfg = SparseConfig(channels=int(cfg["channels"]), lmax=int(cfg["lmax"]),
+                        num_interaction=int(cfg["num_interaction"]), number_of_basis=int(cfg["number_of_basis"]),
+                        max_radius=float(cfg["max_radius"]), function_type=str(cfg["function_type"]),
+                        max_atomvalue=int(cfg["max_atomvalue"]))
+    path = str(tmp_path / "core_sparse.pt")
+    TS.export_core(sd, scfg, path)
+    core = torch.jit.freeze(torch.jit.load(path, map_location="cuda").eval())
+    n = c["pos"].shape[0]
+    ae, F, _ = _lammps_like(core, c, n)
+    assert abs(ae.sum() - c["ref64_energy"].sum()) <= U.E_RTOL * abs(c["ref64_energy"].sum())
+    assert U.rel_max(F, c["ref64_forces"]) <= U.F_RTOL

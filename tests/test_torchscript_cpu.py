@@ -29,3 +29,13 @@ def test_cpu_tensors_are_rejected():
     with pytest.raises((RuntimeError, NotImplementedError)):
         torch.ops.fsctep.ictd_atom_energy(z, torch.zeros(2, dtype=torch.long), torch.zeros(2, dtype=torch.long),
                                           torch.zeros(2, dtype=torch.long), torch.zeros(4), [0] * 53, [5.0, 0.0])
+
+
+def test_o3_and_sparse_ops_are_registered():
+    TS.load_ops()
+    o3 = str(torch.ops.fsctep.ictd_o3_atom_energy.default._schema)
+    assert o3.startswith("fsctep::ictd_o3_atom_energy(Tensor edge_vec, Tensor species, Tensor edge_src, "
+                         "Tensor edge_dst, Tensor field, Tensor blob, int[] icfg, float[] fcfg) -> Tensor"), o3
+    sp = str(torch.ops.fsctep.sparse_atom_energy.default._schema)
+    assert sp.startswith("fsctep::sparse_atom_energy(Tensor edge_vec, Tensor species, Tensor edge_src, "
+                         "Tensor edge_dst, Tensor blob, int[] icfg, float[] fcfg) -> Tensor"), sp
