@@ -231,8 +231,12 @@ fsc_graph engine_graph(const Graph& g, const float* energy_weight, const at::Ten
   s.tr_ptr = g.tr_ptr.data_ptr<int32_t>();
   s.tr_eid = g.tr_eid.data_ptr<int32_t>();
   s.energy_weight = energy_weight;
-  s.field = field.defined() ? field.data_ptr<float>() : nullptr;
+  s.field = (field.defined() && field.numel() > 0) ? field.data_ptr<float>() : nullptr;
   return s;
+}
+
+at::Tensor no_field(const at::Tensor& edge_vec) {
+  return at::empty({0}, edge_vec.options().dtype(at::kFloat));
 }
 
 // (1, 3) float32 field of the o3 op on the edge vectors' device (the engine's l = 1 conv1 term)
@@ -303,7 +307,8 @@ at::Tensor sparse_atom_energy_cuda(const at::Tensor& edge_vec, const at::Tensor&
 }
 
 // Autograd: the backward is the engine's reverse pass with the upstream gradient as per-atom
-// energy weights; dE/d(edge_vec) is its per-edge dE/dr.  The field (o3) is not differentiated.
+// energy weights; dE/d(edge_vec) is its per-edge dE/dr.  The field (o3) is not differentiated;
+// ops without one pass an empty tensor (custom autograd functions take defined tensors only).
 class AtomEnergy : public torch::autograd::Function<AtomEnergy> {
  public:
   static at::Tensor forward(AutogradContext* ctx, const at::Tensor& edge_vec, const at::Tensor& species,
@@ -314,8 +319,7 @@ class AtomEnergy : public torch::autograd::Function<AtomEnergy> {
     Graph g = make_graph(edge_vec, species, edge_src, edge_dst, st);
     auto out = forward_impl(kind, blob, icfg, fcfg, g, field, st);
     ctx->saved_data["kind"] = kind;
-    ctx->saved_data["has_field"] = field.defined();
-    if (field.defined()) ctx->saved_data["field"] = field;
+    ctx->saved_data["field"] = field;
     ctx->saved_data["ws"] = out.second;
     ctx->saved_data["order"] = g.order;
     ctx->saved_data["row_ptr"] = g.row_ptr;
@@ -356,7 +360,7 @@ class AtomEnergy : public torch::autograd::Function<AtomEnergy> {
     const auto fcfg = sd["fcfg"].toDoubleVector();
     at::Tensor blob = sd["blob"].toTensor();
     const int64_t kind = sd["kind"].toInt();
-    at::Tensor field = sd["has_field"].toBool() ? sd["field"].toTensor() : at::Tensor();
+    at::Tensor field = sd["field"].toTensor();
     at::Tensor ws = sd["ws"].toTensor();
     cudaStream_t st = current_stream(g.shift);
     auto dev = g.shift.device();
@@ -384,7 +388,8 @@ class AtomEnergy : public torch::autograd::Function<AtomEnergy> {
 at::Tensor ictd_atom_energy_autograd(const at::Tensor& edge_vec, const at::Tensor& species, const at::Tensor& edge_src,
                                      const at::Tensor& edge_dst, const at::Tensor& blob, c10::IntArrayRef icfg,
                                      c10::ArrayRef<double> fcfg) {
-  return AtomEnergy::apply(edge_vec, species, edge_src, edge_dst, at::Tensor(), blob, icfg, fcfg, (int64_t)kIctd);
+  return AtomEnergy::apply(edge_vec, species, edge_src, edge_dst, no_field(edge_vec), blob, icfg, fcfg,
+                           (int64_t)kIctd);
 }
 
 at::Tensor ictd_o3_atom_energy_autograd(const at::Tensor& edge_vec, const at::Tensor& species,
@@ -398,7 +403,8 @@ at::Tensor ictd_o3_atom_energy_autograd(const at::Tensor& edge_vec, const at::Te
 at::Tensor sparse_atom_energy_autograd(const at::Tensor& edge_vec, const at::Tensor& species,
                                        const at::Tensor& edge_src, const at::Tensor& edge_dst, const at::Tensor& blob,
                                        c10::IntArrayRef icfg, c10::ArrayRef<double> fcfg) {
-  return AtomEnergy::apply(edge_vec, species, edge_src, edge_dst, at::Tensor(), blob, icfg, fcfg, (int64_t)kSparse);
+  return AtomEnergy::apply(edge_vec, species, edge_src, edge_dst, no_field(edge_vec), blob, icfg, fcfg,
+                           (int64_t)kSparse);
 }
 
 }  // namespace
