@@ -320,19 +320,17 @@ __global__ void __launch_bounds__(CONV_WARPS * 32, 3) conv2_r_kernel(ConvArgs a,
 // (dZ already carries 1/deg), then
 //   dgate[p]         = sum_{q in p} Q[q] * Yt0[q],     Yt0[q] = sum_m2 CG_p[m1,m2,kk] Y[KB(l2)+m2]
 //   dY[KB(l2)+m2]   += sum_{q in p} Q[q] * gate[p] * CG_p[m1,m2,kk]
-// Every reduction runs inside one thread: no cross-lane traffic.  The paths are taken in four units
-// (paths 0-2, 3-6, 7-8, 9-10: the l1 = 2 group in two halves, so that no unit holds more than 40
-// Q entries in registers).  The sender rows of the warp's 32 edges are staged in shared memory one
-// (unit, 8-channel chunk) step at a time by 16-byte asynchronous copies (two lanes per 32-byte row
-// chunk, a full sector), double-buffered so that the next step's copies run under this step's
-// arithmetic; each lane then reads its own edge's rows from there, and the dZ rows of the step
-// (same node for all lanes) as broadcasts.  Q is accumulated as even / odd channel partial sums
-// with packed fp32 FMAs (two channels per instruction).
-constexpr int QCH = 8;                        // channels per staged chunk
-constexpr int QF4 = QCH / 4;                  // float4 per staged row
-constexpr int QES = QF4 * 5 + 1;              // float4 slots per edge in a chunk (odd: no bank conflicts)
-constexpr int QZR = 12;                       // dZ rows of the largest unit
-constexpr int QBUF_F4 = 32 * QES + QF4 * QZR; // one step: sender rows, then dZ rows
+// Every reduction runs inside one thread: no cross-lane traffic.  The sender rows of the warp's 32
+// edges are staged in shared memory one (l1 group, 16-channel chunk) step at a time by coalesced
+// 16-byte asynchronous copies (four lanes per 64-byte row chunk), double-buffered so that the
+// next step's copies run under this step's arithmetic; each lane then reads its own edge's rows
+// from there, and the dZ rows of the step (same node for all lanes) as broadcasts.  Q is
+// accumulated as even / odd channel partial sums with packed fp32 FMAs (two channels per
+// instruction).
+constexpr int QCH = 16;                       // channels per staged chunk
+constexpr int QES = 4 * 5 + 1;                // float4 slots per edge in a chunk (odd: no bank conflicts)
+constexpr int QZR = 14;                       // dZ rows of the largest l1 group
+constexpr int QBUF_F4 = 32 * QES + 4 * QZR;   // one step: sender rows, then dZ rows
 constexpr int QTAB_F4 = (NQ * 5 + 3) / 4 + 9; // cg2, then the dZ row list of every group (35 ints)
 constexpr uint32_t QSMEM = 16u * (QTAB_F4 + CONV_WARPS * 2 * QBUF_F4);
 
@@ -345,20 +343,6 @@ __host__ __device__ constexpr int zlocal(int p, int kk) {
 __host__ __device__ constexpr int zcount(int G) { return zlocal(P_HI(G) - 1, 2 * L3(P_HI(G) - 1)) + 1; }
 __host__ __device__ constexpr int zbase(int G) { return G == 0 ? 0 : (G == 1 ? zcount(0) : zcount(0) + zcount(1)); }
 
-// Units of conv2_q: paths [UPLO, UPHI) of l1 group UG.
-constexpr int QUNITS = 4;
-__host__ __device__ constexpr int UG(int U) { return U == 0 ? 0 : (U == 1 ? 1 : 2); }
-__host__ __device__ constexpr int UPLO(int U) { return U == 0 ? 0 : (U == 1 ? 3 : (U == 2 ? 7 : 9)); }
-__host__ __device__ constexpr int UPHI(int U) { return U == 0 ? 3 : (U == 1 ? 7 : (U == 2 ? 9 : 11)); }
-__host__ __device__ constexpr int UZ0(int U) { return zbase(UG(U)) + zlocal(UPLO(U), 0); }  // first zlist row
-__host__ __device__ constexpr int UZN(int U) {
-  int n = 0;
-  for (int p = UPLO(U); p < UPHI(U); ++p) n += 2 * L3(p) + 1;
-  return n;
-}
-__host__ __device__ constexpr int UQ0(int U) { return QOFF(UPLO(U)); }
-__host__ __device__ constexpr int UQ1(int U) { return UPHI(U) == NP ? NQ : QOFF(UPHI(U)); }
-
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
                "l"(gmem_src)
@@ -368,23 +352,23 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Issues the copies of step (U, cc) into `buf` as one group: 32 edges x (2G+1) rows x QF4 float4
-// (lane copies slots f = lane + 32 i, f = (edge, m1, c4)), then the unit's dZ rows.
-template <int U, int C>
+// Issues the copies of step (G, cc) into `buf` as one group: 32 edges x (2G+1) rows x 4 float4
+// (lane copies slots f = lane + 32 i, f = (edge, m1, c4)), then the group's dZ rows.
+template <int G, int C>
 __device__ __forceinline__ void q_stage(float4* __restrict__ buf, const int* __restrict__ zlist,
                                         const float* __restrict__ x, int64_t src_row,
                                         const float* __restrict__ dzn, int cc, int lane) {
-  constexpr int G = UG(U), M1 = 2 * G + 1, NZG = UZN(U);
+  constexpr int M1 = 2 * G + 1, NZG = zcount(G);
   static_assert(NZG <= QZR, "dZ row buffer");
 #pragma unroll 1
-  for (int i = 0; i < QF4 * M1; ++i) {
-    const int f = lane + 32 * i, e = f / (QF4 * M1), r = f - e * (QF4 * M1);
+  for (int i = 0; i < 4 * M1; ++i) {
+    const int f = lane + 32 * i, e = f / (4 * M1), r = f - e * (4 * M1);
     const int64_t row = __shfl_sync(0xffffffffu, src_row, e);
-    cp_async16(buf + e * QES + r, x + (row + KB(G) + r / QF4) * C + cc * QCH + 4 * (r % QF4));
+    cp_async16(buf + e * QES + r, x + (row + KB(G) + (r >> 2)) * C + cc * QCH + 4 * (r & 3));
   }
   float4* zb = buf + 32 * QES;
-  for (int f = lane; f < QF4 * NZG; f += 32)
-    cp_async16(zb + f, dzn + zlist[UZ0(U) + f / QF4] * C + cc * QCH + 4 * (f % QF4));
+  for (int f = lane; f < 4 * NZG; f += 32)
+    cp_async16(zb + f, dzn + zlist[zbase(G) + (f >> 2)] * C + cc * QCH + 4 * (f & 3));
   cp_async_commit();
 }
 
@@ -392,17 +376,16 @@ __device__ __forceinline__ float2 ffma2(float a0, float a1, float b0, float b1, 
   return __ffma2_rn(make_float2(a0, a1), make_float2(b0, b1), c);
 }
 
-// Unit U: its Q partial sums over all chunks, then its share of dgate / dY.  On entry step
-// (U, 0) is staged (or in flight) in bufs[0]; the unit stages every following step, the first
-// step of unit U + 1 included, one step ahead.
-template <int U, int C>
-__device__ __forceinline__ void q_unit(float4* __restrict__ bufs, const int* __restrict__ zlist,
-                                       const float* __restrict__ x, int64_t src_row, const float* __restrict__ dzn,
-                                       const float* __restrict__ cg2, const float4* __restrict__ ey4,
-                                       const float4* __restrict__ eg4, float* dg, float* dy) {
-  constexpr int G = UG(U), Q0 = UQ0(U), NQG = UQ1(U) - Q0, M1 = 2 * G + 1, NCH = C / QCH;
-  constexpr int ZL0 = zlocal(UPLO(U), 0);  // the unit's first dZ row within its group
-  static_assert(NCH % 2 == 0, "every unit starts in buffer 0");
+// Group G: its Q partial sums over all chunks, then its share of dgate / dY.  On entry step
+// (G, 0) is staged (or in flight) in bufs[0]; the group stages every following step, the first
+// step of group G + 1 included, one step ahead.
+template <int G, int C>
+__device__ __forceinline__ void q_group(float4* __restrict__ bufs, const int* __restrict__ zlist,
+                                        const float* __restrict__ x, int64_t src_row, const float* __restrict__ dzn,
+                                        const float* __restrict__ cg2, const float4* __restrict__ ey4,
+                                        const float4* __restrict__ eg4, float* dg, float* dy) {
+  constexpr int Q0 = QOFF(P_LO(G)), NQG = Q_END(G) - Q0, M1 = 2 * G + 1, NCH = C / QCH;
+  static_assert(NCH % 2 == 0, "every group starts in buffer 0");
   const int lane = threadIdx.x & 31;
   float2 Q[NQG];
 #pragma unroll
@@ -412,10 +395,10 @@ __device__ __forceinline__ void q_unit(float4* __restrict__ bufs, const int* __r
     float4* cur = bufs + (cc & 1) * QBUF_F4;
     float4* nxt = bufs + ((cc + 1) & 1) * QBUF_F4;
     if (cc + 1 < NCH) {
-      q_stage<U, C>(nxt, zlist, x, src_row, dzn, cc + 1, lane);
+      q_stage<G, C>(nxt, zlist, x, src_row, dzn, cc + 1, lane);
       cp_async_wait<1>();
-    } else if (U + 1 < QUNITS) {
-      q_stage<(U + 1 < QUNITS ? U + 1 : U), C>(nxt, zlist, x, src_row, dzn, 0, lane);
+    } else if (G < 2) {
+      q_stage<(G < 2 ? G + 1 : 2), C>(nxt, zlist, x, src_row, dzn, 0, lane);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
@@ -423,15 +406,15 @@ __device__ __forceinline__ void q_unit(float4* __restrict__ bufs, const int* __r
     __syncwarp();
     const float4* zb = cur + 32 * QES;
 #pragma unroll 1
-    for (int c4 = 0; c4 < QF4; ++c4) {
+    for (int c4 = 0; c4 < QCH / 4; ++c4) {
       float4 xv[M1];
 #pragma unroll
-      for (int m1 = 0; m1 < M1; ++m1) xv[m1] = cur[lane * QES + QF4 * m1 + c4];
+      for (int m1 = 0; m1 < M1; ++m1) xv[m1] = cur[lane * QES + 4 * m1 + c4];
 #pragma unroll
-      for (int p = UPLO(U); p < UPHI(U); ++p)
+      for (int p = P_LO(G); p < P_HI(G); ++p)
 #pragma unroll
         for (int kk = 0; kk < 2 * L3(p) + 1; ++kk) {
-          const float4 d = zb[QF4 * (zlocal(p, kk) - ZL0) + c4];
+          const float4 d = zb[4 * zlocal(p, kk) + c4];
 #pragma unroll
           for (int m1 = 0; m1 < M1; ++m1) {
             float2 acc = Q[qidx(p, m1, kk) - Q0];
@@ -451,7 +434,7 @@ __device__ __forceinline__ void q_unit(float4* __restrict__ bufs, const int* __r
     g[4 * i] = v.x; g[4 * i + 1] = v.y; g[4 * i + 2] = v.z; g[4 * i + 3] = v.w;
   }
 #pragma unroll
-  for (int p = UPLO(U); p < UPHI(U); ++p)
+  for (int p = P_LO(G); p < P_HI(G); ++p)
 #pragma unroll
     for (int m1 = 0; m1 < M1; ++m1)
 #pragma unroll
@@ -470,7 +453,7 @@ __device__ __forceinline__ void q_unit(float4* __restrict__ bufs, const int* __r
 }
 
 template <int CPL>
-__global__ void __launch_bounds__(CONV_WARPS * 32, 4) conv2_q_kernel(ConvArgs a, const float* __restrict__ x,
+__global__ void __launch_bounds__(CONV_WARPS * 32, 2) conv2_q_kernel(ConvArgs a, const float* __restrict__ x,
                                                                      const float* __restrict__ dZ,
                                                                      float* __restrict__ dgates,
                                                                      float* __restrict__ dY) {
@@ -509,10 +492,9 @@ __global__ void __launch_bounds__(CONV_WARPS * 32, 4) conv2_q_kernel(ConvArgs a,
 #pragma unroll
       for (int p = 0; p < NP; ++p) dg[p] = 0.f;
       q_stage<0, C>(bufs, zlist, x, src_row, dzn, 0, lane);
-      q_unit<0, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
-      q_unit<1, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
-      q_unit<2, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
-      q_unit<3, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
+      q_group<0, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
+      q_group<1, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
+      q_group<2, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
       if (!active) continue;
       float4* dgo = reinterpret_cast<float4*>(dgates + 12 * (int64_t)e);
       dgo[0] = make_float4(dg[0], dg[1], dg[2], dg[3]);
