@@ -308,7 +308,7 @@ def stage_pass(args, world, step):
         torch.distributed.barrier()
     stage_ms = {}
     NAT.profile_enable(True)
-    for _ in range(args.steps):
+    for _ in range(args.stage_steps if args.stage_steps is not None else args.steps):
         step()
         for name, ms in NAT.profile_read():
             stage_ms.setdefault(name, []).append(ms)
@@ -750,6 +750,8 @@ def main():
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                     help="N > 1, pure-cartesian-ictd: a fixed crystal per GPU (weak, default) or one fixed "
                          "crystal cut over the GPUs (strong)")
+    ap.add_argument("--stage-steps", type=int, default=None,
+                    help="steps of the untimed per-stage pass (default: --steps)")
     ap.add_argument("--clocks-csv", default=None, help="where to write the nvidia-smi clock samples (default: a "
                                                         "temporary directory)")
     args = ap.parse_args()
@@ -854,8 +856,9 @@ def main():
     e2e_value = n_total / (res["ms_e2e"] / 1e3)
     # dominant stage and its roofline
     stage_avg = {}
+    nst = args.stage_steps if args.stage_steps is not None else args.steps
     for name, lst in res["stage_ms"].items():
-        stage_avg[name] = (sum(lst) / args.steps, len(lst) / args.steps)
+        stage_avg[name] = (sum(lst) / nst, len(lst) / nst)
     dom = max(stage_avg, key=lambda k: stage_avg[k][0]) if stage_avg else None
     pk = peaks()
     roofline = None
