@@ -35,6 +35,7 @@ constexpr int64_t kMaxGraphs = 4096;
 // Aggregation buffer budget, 16 GB: the per-rank fc.4 GEMMs over one node chunk have
 // chunk x 3^Lout rows, and the low ranks need large chunks to fill the GPU.
 constexpr int64_t kZBudgetFloats = (int64_t)1 << 32;
+constexpr int64_t kDmBudgetFloats = (int64_t)1 << 31;  // 8 GB of dm rows per conv2-backward sub-chunk
 constexpr int64_t kGramChunk = 16384;
 
 __host__ __device__ constexpr int pow3(int L) { return L == 0 ? 1 : 3 * pow3(L - 1); }
@@ -592,27 +593,22 @@ int launch_z_tc(const Args& a, const Rows& rows, const float* x, const float* h2
 // ---------------------------------------------------------------- conv2 backward
 // Both kernels take one receiving node per block and read its dZ block once.
 // dm_kernel: thread = column (row r, channel a) holding dZ[n][r][:][a] in registers; per edge
-//   dm = sum_j dZ[n][r][j][a] h2'_e[j]
-//   dE/dx1[src][c1(r)][a]   += dm * n^{(x)L2}[c2(r)]     (atomic: sources are shared)
-//   dE/dn^{(x)L2}[c2(r)]    += sum_a dm * x1[src][c1(r)][a]
-__global__ void __launch_bounds__(256) bwd_dm_kernel(Args a, Rows rows, const float* __restrict__ x,
-                                                     const float* __restrict__ h2, const float* __restrict__ dZ,
-                                                     int64_t n0, float* __restrict__ gx, float* __restrict__ dnp) {
+//   dm = sum_j dZ[n][r][j][a] h2'_e[j],  written to the chunk's dm rows dmbuf[e - e_base][r][a].
+// The two contractions of dm (dE/dx1 of the sources and dE/dn^{(x)L2} of the edges) are
+// dm_gx_kernel and dm_dn_kernel below: reductions in a fixed order, no atomics.
+__global__ void __launch_bounds__(256) bwd_dm_kernel(Args a, Rows rows, const float* __restrict__ h2,
+                                                     const float* __restrict__ dZ, int64_t n0,
+                                                     float* __restrict__ dmbuf, int64_t e_base) {
   __shared__ __align__(16) float hs[ZEB][RH];
-  __shared__ float np[ZEB][MAXR];
-  __shared__ float sdn[ZEB][MAXR];
-  __shared__ int srcs[ZEB];
   const int64_t n = n0 + blockIdx.x;
-  const int C = a.C, R = a.R;
+  const int C = a.C;
   const int e0 = a.row_ptr[n], e1 = a.row_ptr[n + 1];
   const int cols = rows.nrows * C;
-  const int lane = threadIdx.x & 31;
   const float* dzn = dZ + (int64_t)blockIdx.x * rows.nrows * J * C;
   for (int base = 0; base < cols; base += blockDim.x) {
     const int col = base + threadIdx.x;
     const bool valid = col < cols;  // warp-uniform: cols and blockDim are multiples of 32
     const int r = valid ? col / C : 0, ch = valid ? col - r * C : 0;
-    const int c1 = rows.c1[r], c2 = rows.c2[r];
     float dz[RH];
     float dzb = 0.f;
     if (valid) {
@@ -628,13 +624,6 @@ __global__ void __launch_bounds__(256) bwd_dm_kernel(Args a, Rows rows, const fl
       const int ne = min(ZEB, e1 - eb);
       __syncthreads();
       for (int t = threadIdx.x; t < ne * RH; t += blockDim.x) hs[t / RH][t % RH] = h2[(int64_t)(eb + t / RH) * RH + t % RH];
-      for (int t = threadIdx.x; t < ZEB * MAXR; t += blockDim.x) sdn[t / MAXR][t % MAXR] = 0.f;
-      if (threadIdx.x < ne) {
-        const int e = eb + threadIdx.x;
-        srcs[threadIdx.x] = a.src[e];
-        const float* y = a.edge_y + 12 * (int64_t)e;
-        npow_all(a.lmax, y[0], y[1], y[2], np[threadIdx.x]);
-      }
       __syncthreads();
       if (valid) {
         for (int k = 0; k < ne; ++k) {
@@ -648,20 +637,100 @@ __global__ void __launch_bounds__(256) bwd_dm_kernel(Args a, Rows rows, const fl
             d2 = fmaf(dz[4 * j4 + 2], h.z, d2);
             d3 = fmaf(dz[4 * j4 + 3], h.w, d3);
           }
-          const float dm = (d0 + d1) + (d2 + d3);
-          const int s = srcs[k];
-          const float xv = x[((int64_t)s * R + c1) * C + ch];
-          atomicAdd(gx + ((int64_t)s * R + c1) * C + ch, dm * np[k][c2]);
-          const float t = warp_sum(dm * xv);
-          if (lane == 0) atomicAdd(&sdn[k][c2], t);
+          dmbuf[((int64_t)(eb + k - e_base) * rows.nrows + r) * C + ch] = (d0 + d1) + (d2 + d3);
         }
       }
-      __syncthreads();
-      for (int t = threadIdx.x; t < ne * R; t += blockDim.x) {
-        const int k = t / R, c = t - k * R;
-        dnp[(int64_t)(eb + k) * MAXR + c] += sdn[k][c];
-      }
     }
+  }
+}
+
+// dE/dx1 of the sources, warp per source atom s: its out-edges in [e_base, e_end) taken in
+// increasing edge order (the transpose CSR rows are sorted), 32 at a time with their
+// n^{(x)L2} in shared memory; per x1 component c1 (lanes over channels)
+//   gx[s][c1][a] += sum_e sum_{r: c1(r) = c1} dm_e[r][a] n_e^{(x)L2}[c2(r)]
+// with the rows of c1 in rows.rlist order: a fixed summation order, so the result repeats bit for
+// bit.  A source with no out-edge in the range returns after one binary search.
+template <int CPL>
+__global__ void __launch_bounds__(256) dm_gx_kernel(Args a, Rows rows, const int32_t* __restrict__ tr_ptr,
+                                                    const int32_t* __restrict__ tr_eid, const float* __restrict__ dmbuf,
+                                                    int64_t e_base, int64_t e_end, float* __restrict__ gx) {
+  __shared__ float nps[8][32][MAXR];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int C = 32 * CPL;
+  const int R = a.R, NR = rows.nrows;
+  for (int64_t s = (int64_t)blockIdx.x * 8 + warp; s < a.N; s += (int64_t)gridDim.x * 8) {
+    const int t0 = tr_ptr[s], t1 = tr_ptr[s + 1];
+    int lo = t0, hi = t1;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (tr_eid[mid] < e_base) lo = mid + 1;
+      else hi = mid;
+    }
+    for (int t = lo; t < t1; t += 32) {
+      const int me = t + lane < t1 ? tr_eid[t + lane] : (int)e_end;
+      const unsigned in = __ballot_sync(0xffffffffu, me < e_end);
+      const int nb = __popc(in);  // edges sorted: the ones in the range are a prefix
+      if (nb == 0) break;
+      if (lane < nb) {
+        const float* y = a.edge_y + 12 * (int64_t)me;
+        npow_all(a.lmax, y[0], y[1], y[2], nps[warp][lane]);
+      }
+      __syncwarp();
+      for (int c1 = 0; c1 < R; ++c1) {
+        float acc[CPL];
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) acc[j] = 0.f;
+        for (int i = 0; i < nb; ++i) {
+          const int64_t e = __shfl_sync(0xffffffffu, me, i);
+          const float* dme = dmbuf + (e - e_base) * NR * C + lane;
+          for (int qq = rows.c1off[c1]; qq < rows.c1off[c1 + 1]; ++qq) {
+            const int r = rows.rlist[qq];
+            const float w = nps[warp][i][rows.c2[r]];
+#pragma unroll
+            for (int j = 0; j < CPL; ++j) acc[j] = fmaf(dme[(int64_t)r * C + 32 * j], w, acc[j]);
+          }
+        }
+        float* g = gx + (s * R + c1) * C + lane;
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) g[32 * j] += acc[j];
+      }
+      __syncwarp();
+      if (nb < 32) break;
+    }
+  }
+}
+
+// dE/dn^{(x)L2} of the edges, warp per edge e in [e_base, e_base + count): lanes over channels,
+//   dnp[e][c2] += sum_{r: c2(r) = c2} sum_a dm_e[r][a] x1[src_e][c1(r)][a]
+// each lane's partial sums per c2 kept in shared memory, then summed over the lanes in order.
+template <int CPL>
+__global__ void __launch_bounds__(256) dm_dn_kernel(Args a, Rows rows, const float* __restrict__ x,
+                                                    const float* __restrict__ dmbuf, int64_t e_base, int64_t count,
+                                                    float* __restrict__ dnp) {
+  __shared__ float part[8][MAXR][33];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int C = 32 * CPL;
+  const int R = a.R, NR = rows.nrows;
+  for (int64_t w = (int64_t)blockIdx.x * 8 + warp; w < count; w += (int64_t)gridDim.x * 8) {
+    const int64_t e = e_base + w;
+    const int64_t s = a.src[e];
+    for (int c = 0; c < R; ++c) part[warp][c][lane] = 0.f;
+    const float* dme = dmbuf + w * NR * C + lane;
+    const float* xs = x + s * R * C + lane;
+    for (int r = 0; r < NR; ++r) {
+      const int c1 = rows.c1[r];
+      float t = 0.f;
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) t = fmaf(dme[(int64_t)r * C + 32 * j], xs[(int64_t)c1 * C + 32 * j], t);
+      part[warp][rows.c2[r]][lane] += t;
+    }
+    __syncwarp();
+    if (lane < R) {
+      float v = 0.f;
+      for (int l = 0; l < 32; ++l) v += part[warp][lane][l];
+      dnp[e * MAXR + lane] += v;
+    }
+    __syncwarp();
   }
 }
 
@@ -669,9 +738,8 @@ __global__ void __launch_bounds__(256) bwd_dm_kernel(Args a, Rows rows, const fl
 //   D[(r, a)][e] = sum_{j < 64} dZ[n][r][j][a] h2_e[j]      (M = 128, N = 64 edges, K = 64, 3xTF32)
 //   dm = D + dZ[n][r][64][a]                                (the bias row of h2' = [h2, 1])
 // A (the dZ rows) is written to TMEM by the CUDA cores, B is the node's h2 rows as a K-major image
-// in shared memory (up to two 64-edge chunks).  The epilogue is bwd_dm_kernel's: the source
-// feature gradients by atomics, dE/dn^{(x)L2} reduced over the warp's 32 channels by a transpose
-// reduction (lane i ends with edge i's sum) into per-edge shared-memory rows.
+// in shared memory (up to two 64-edge chunks).  The epilogue writes dm to the sub-chunk's dm rows
+// (as bwd_dm_kernel); dm_gx_kernel and dm_dn_kernel reduce them.
 constexpr int DTC_NE = 64;
 struct DtcSmem {
   static constexpr uint32_t IMG = 4u * DTC_NE * 64u * 2u;        // one hi or lo image, two edge chunks
@@ -687,20 +755,16 @@ static_assert(3 * DtcSmem::TOTAL > 228u * 1024u, "at most two CTAs per SM (256 T
 
 __device__ __forceinline__ int dimg(int n, int k) { return (k >> 2) * 4 * DTC_NE + 4 * n + (k & 3); }
 
-__global__ void __launch_bounds__(ZTC_THREADS, 2) dm_tc_kernel(Args a, Rows rows, const float* __restrict__ x,
-                                                               const float* __restrict__ h2, const float* __restrict__ dZ,
-                                                               int64_t n0, int64_t nc, float* __restrict__ gx,
-                                                               float* __restrict__ dnp, int* err) {
+__global__ void __launch_bounds__(ZTC_THREADS, 2) dm_tc_kernel(Args a, Rows rows, const float* __restrict__ h2,
+                                                               const float* __restrict__ dZ, int64_t n0, int64_t nc,
+                                                               float* __restrict__ dmbuf, int64_t e_base, int* err) {
   extern __shared__ __align__(1024) uint8_t smem[];
   float* bhi = reinterpret_cast<float*>(smem + DtcSmem::BHI);
   float* blo = reinterpret_cast<float*>(smem + DtcSmem::BLO);
-  float* np = reinterpret_cast<float*>(smem + DtcSmem::NP);
-  float* sdn = reinterpret_cast<float*>(smem + DtcSmem::SDN);
-  int64_t* xoff = reinterpret_cast<int64_t*>(smem + DtcSmem::XOFF);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + DtcSmem::BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + DtcSmem::BAR + 8);
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, half = tid / ZTC_M, row = tid % ZTC_M;
+  const int tid = threadIdx.x, warp = tid >> 5, half = tid / ZTC_M, row = tid % ZTC_M;
   if (warp == 0) {
     tc::tmem_alloc(tmem_slot, 256);
     tc::tmem_relinquish();
@@ -717,7 +781,7 @@ __global__ void __launch_bounds__(ZTC_THREADS, 2) dm_tc_kernel(Args a, Rows rows
   const uint32_t tD = tbase, tAhi = tbase + 128u, tAlo = tbase + 192u;  // D: 64 columns, A: 64 + 64
   const uint32_t s_hi = tc::smem_u32(bhi), s_lo = tc::smem_u32(blo);
   constexpr uint32_t idesc = tc::idesc_tf32(ZTC_M, DTC_NE);
-  const int C = a.C, R = a.R, S = ZTC_M / C, slot = row / C, ch = row - slot * C;
+  const int C = a.C, S = ZTC_M / C, slot = row / C, ch = row - slot * C;
   const int ntiles = (rows.nrows + S - 1) / S;
   uint32_t phase = 0;
   bool ok = true;
@@ -730,18 +794,6 @@ __global__ void __launch_bounds__(ZTC_THREADS, 2) dm_tc_kernel(Args a, Rows rows
       const int kg = min(ZTC_KMAX, e1 - g0);
       const int nch = (kg + DTC_NE - 1) / DTC_NE;
       __syncthreads();
-      if (tid < ZTC_KMAX) {
-        if (tid < kg) {
-          const int e = g0 + tid;
-          xoff[tid] = (int64_t)a.src[e] * R * C;
-          const float* y = a.edge_y + 12 * (int64_t)e;
-          npow_all(a.lmax, y[0], y[1], y[2], np + tid * MAXR);
-        } else {
-          xoff[tid] = 0;
-        }
-#pragma unroll 8
-        for (int c = 0; c < MAXR; ++c) sdn[tid * MAXR + c] = 0.f;
-      }
       for (int i = tid; i < nch * DTC_NE * 64; i += ZTC_THREADS) {
         const int k = i >> 6, j = i & 63;  // edge of the group, hidden unit
         const float v = k < kg ? h2[(int64_t)(g0 + k) * RH + j] : 0.f;
@@ -753,13 +805,10 @@ __global__ void __launch_bounds__(ZTC_THREADS, 2) dm_tc_kernel(Args a, Rows rows
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncthreads();
-      int cached_c1 = -1;
-      float xv[32];
       for (int tile = 0; tile < ntiles && ok; ++tile) {
         const int q = tile * S + slot;
         const bool valid = q < rows.nrows;
         const int r = valid ? rows.rlist[q] : 0;
-        const int c1 = rows.c1[r], c2 = rows.c2[r];
         const float* dzc = dzn + (int64_t)r * J * C + ch;
         // ---- A = dZ[n][r][j][a], columns j in [32 half, 32 half + 32)
         {
@@ -802,36 +851,19 @@ __global__ void __launch_bounds__(ZTC_THREADS, 2) dm_tc_kernel(Args a, Rows rows
             ok = false;
             break;
           }
-          // ---- epilogue: this thread's 32 edges kb .. kb + 31 of the group
+          // ---- epilogue: dm of this thread's 32 edges kb .. kb + 31 of the group, written to the
+          // chunk's dm rows (a warp writes 32 consecutive channels of one row: 128-byte runs)
           const int kb = cc * DTC_NE + 32 * half;
           uint32_t u[32];
           tc::tmem_ld32(tD + lane_off + 32u * half, u);
           tc::tmem_wait_ld();
-          if (nch > 1 || c1 != cached_c1) {  // warp-uniform
-            const float* xc = x + (int64_t)c1 * C + ch;
+          if (valid) {
+            float* out = dmbuf + ((int64_t)(g0 - e_base) * rows.nrows + r) * C + ch;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) xv[i] = (valid && kb + i < kg) ? xc[xoff[kb + i]] : 0.f;
-            cached_c1 = nch == 1 ? c1 : -1;
+            for (int i = 0; i < 32; ++i)
+              if (kb + i < kg) out[(int64_t)(kb + i) * rows.nrows * C] = __uint_as_float(u[i]) + bias;
           }
-          float t[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int k = kb + i;
-            const float dm = __uint_as_float(u[i]) + bias;
-            t[i] = 0.f;
-            if (valid && k < kg) {
-              atomicAdd(gx + xoff[k] + (int64_t)c1 * C + ch, dm * np[k * MAXR + c2]);
-              t[i] = dm * xv[i];
-            }
-          }
-          const float tsum = transpose_reduce32(t, lane);  // lane i: edge kb + i, summed over the warp's channels
-          if (valid && kb + lane < kg) atomicAdd(&sdn[(kb + lane) * MAXR + c2], tsum);
         }
-      }
-      __syncthreads();
-      for (int i = tid; i < kg * R; i += ZTC_THREADS) {
-        const int k = i / R, c = i - k * R;
-        dnp[(int64_t)(g0 + k) * MAXR + c] += sdn[k * MAXR + c];
       }
     }
   }
@@ -845,8 +877,8 @@ __global__ void __launch_bounds__(ZTC_THREADS, 2) dm_tc_kernel(Args a, Rows rows
   if (warp == 0) tc::tmem_dealloc(tbase, 256);
 }
 
-int launch_dm_tc(const Args& a, const Rows& rows, const float* x, const float* h2, const float* dZ, int64_t n0,
-                 int64_t nc, float* gx, float* dnp, int* err, cudaStream_t st) {
+int launch_dm_tc(const Args& a, const Rows& rows, const float* h2, const float* dZ, int64_t n0, int64_t nc,
+                 float* dmbuf, int64_t e_base, int* err, cudaStream_t st) {
   if (nc <= 0) return FSC_OK;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -854,8 +886,28 @@ int launch_dm_tc(const Args& a, const Rows& rows, const float* x, const float* h
   if (cudaFuncSetAttribute(dm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DtcSmem::TOTAL) != cudaSuccess)
     return fail(FSC_ERR_CUDA, "dm_tc_kernel: shared memory attribute");
   const unsigned blocks = (unsigned)std::min<int64_t>(nc, 2 * (int64_t)sms);
-  dm_tc_kernel<<<blocks, ZTC_THREADS, DtcSmem::TOTAL, st>>>(a, rows, x, h2, dZ, n0, nc, gx, dnp, err);
+  dm_tc_kernel<<<blocks, ZTC_THREADS, DtcSmem::TOTAL, st>>>(a, rows, h2, dZ, n0, nc, dmbuf, e_base, err);
   return check_launch("sparse dm_tc_kernel");
+}
+
+// The fixed-order reductions of a sub-chunk's dm rows (edges [e_base, e_end)).
+int launch_dm_reduce(const Args& a, const Rows& rows, const int32_t* tr_ptr, const int32_t* tr_eid, const float* x,
+                     const float* dmbuf, int64_t e_base, int64_t e_end, float* gx, float* dnp, cudaStream_t st) {
+  if (e_end <= e_base) return FSC_OK;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const unsigned gs = (unsigned)std::min<int64_t>(ceil_div(a.N, 8), 16 * (int64_t)sms);
+  const unsigned ge = (unsigned)std::min<int64_t>(ceil_div(e_end - e_base, 8), 16 * (int64_t)sms);
+  auto go = [&](auto cpl) {
+    constexpr int CPL = decltype(cpl)::value;
+    dm_gx_kernel<CPL><<<gs, 256, 0, st>>>(a, rows, tr_ptr, tr_eid, dmbuf, e_base, e_end, gx);
+    dm_dn_kernel<CPL><<<ge, 256, 0, st>>>(a, rows, x, dmbuf, e_base, e_end - e_base, dnp);
+    return check_launch("sparse dm_gx / dm_dn kernels");
+  };
+  if (a.C == 32) return go(std::integral_constant<int, 1>{});
+  if (a.C == 64) return go(std::integral_constant<int, 2>{});
+  return go(std::integral_constant<int, 4>{});
 }
 
 // dh_kernel: dE/dh2_e[j] = sum_{(r, a)} dZ[n][r][j][a] * x1[src_e][c1(r)][a] * n_e^{(x)L2}[c2(r)],
@@ -1256,6 +1308,8 @@ struct Plan {
   float* dxb;
   float* dh2;
   float* dnp;
+  float* dmbuf;    // [dmcap][nrows][C] dm rows of one sub-chunk of receivers (conv2 backward)
+  int64_t dmcap;   // edges of a sub-chunk
   float* edge_grad;
   float* gbuf;
   int* err;
@@ -1328,6 +1382,8 @@ void layout(Plan& p, Arena& ar, const fsc_sparse_config* cfg, int64_t N, int64_t
   p.dxb = ar.take<float>(N * maxw);
   p.dh2 = ar.take<float>((int64_t)p.nint * E * RH);
   p.dnp = ar.take<float>(E * MAXR);
+  p.dmcap = std::max<int64_t>(1, std::min<int64_t>(std::max<int64_t>(E, 1), kDmBudgetFloats / ((int64_t)p.rows.nrows * p.C)));
+  p.dmbuf = ar.take<float>(p.dmcap * p.rows.nrows * p.C);
   p.edge_grad = ar.take<float>(E * 3);
   p.gbuf = ar.take<float>(p.gchunk * std::max<int64_t>(p.npairs, (int64_t)p.nC * p.nC));
   p.err = ar.take<int>(64);
@@ -1364,6 +1420,7 @@ struct Ctx {
   const fsc_graph* g;
   Plan p;
   cudaStream_t st;
+  std::vector<int32_t> row_ptr_host;  // conv2 backward: sub-chunks of at most p.dmcap edges
 };
 
 Args args(const Ctx& c) {
@@ -1610,6 +1667,13 @@ int backward_conv2(Ctx& c, int k) {
   cudaStream_t st = c.st;
   Args a = args(c);
   const float avg = conv2_norm(c);
+  if ((int64_t)c.row_ptr_host.size() != p.N + 1) {  // once per call: the sub-chunk boundaries
+    c.row_ptr_host.resize(p.N + 1);
+    if (cudaMemcpyAsync(c.row_ptr_host.data(), c.g->row_ptr, sizeof(int32_t) * (p.N + 1), cudaMemcpyDeviceToHost,
+                        st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+      return fail(FSC_ERR_CUDA, "row_ptr readback");
+  }
   {
     for (int64_t n0 = 0; n0 < p.N; n0 += p.chunk) {
       const int64_t nc = std::min(p.chunk, p.N - n0);
@@ -1621,13 +1685,25 @@ int backward_conv2(Ctx& c, int k) {
         ga.alpha = 1.f / avg;
         FSC_TRY(run_gemm(ga, p.img_mixT[k][Lo], p.err, st));
       }
-      if (p.atc) {
-        FSC_TRY(launch_dm_tc(a, p.rows, p.feats[k - 1], p.h2 + (int64_t)k * p.E * RH, p.zbuf, n0, nc, p.grads[k - 1],
-                             p.dnp, p.err, st));
-      } else {
-        bwd_dm_kernel<<<(unsigned)nc, 256, 0, st>>>(a, p.rows, p.feats[k - 1], p.h2 + (int64_t)k * p.E * RH, p.zbuf,
-                                                     n0, p.grads[k - 1], p.dnp);
-        FSC_TRY(check_launch("sparse bwd_dm_kernel"));
+      // dm rows of sub-chunks of at most dmcap edges, each reduced in a fixed order (no atomics)
+      for (int64_t m0 = n0; m0 < n0 + nc;) {
+        const int64_t eb = c.row_ptr_host[m0];
+        int64_t m1 = m0 + 1;
+        while (m1 < n0 + nc && c.row_ptr_host[m1 + 1] - eb <= p.dmcap) ++m1;
+        const int64_t ee = c.row_ptr_host[m1];
+        if (ee - eb > p.dmcap) return fail(FSC_ERR_CAPACITY, "sparse conv2 backward: a receiver has more edges "
+                                                           "than the dm buffer holds");
+        const float* dz = p.zbuf + (m0 - n0) * p.zstride;
+        if (p.atc) {
+          FSC_TRY(launch_dm_tc(a, p.rows, p.h2 + (int64_t)k * p.E * RH, dz, m0, m1 - m0, p.dmbuf, eb, p.err, st));
+        } else if (m1 > m0) {
+          bwd_dm_kernel<<<(unsigned)(m1 - m0), 256, 0, st>>>(a, p.rows, p.h2 + (int64_t)k * p.E * RH, dz, m0,
+                                                              p.dmbuf, eb);
+          FSC_TRY(check_launch("sparse bwd_dm_kernel"));
+        }
+        FSC_TRY(launch_dm_reduce(a, p.rows, c.g->tr_ptr, c.g->tr_eid, p.feats[k - 1], p.dmbuf, eb, ee,
+                                 p.grads[k - 1], p.dnp, st));
+        m0 = m1;
       }
       if (p.atc) {
         FSC_TRY(launch_dh_tc(a, p.rows, p.feats[k - 1], p.zbuf, n0, nc, p.dh2 + (int64_t)k * p.E * RH, p.err, st));

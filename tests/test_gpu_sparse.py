@@ -41,15 +41,28 @@ def test_sparse_energy_forces_stress_match_reference(tag):
     np.testing.assert_allclose(out["atom_energy"].cpu().numpy(), c["ref64_atom_energy"], rtol=1e-4, atol=1e-4)
 
 
-def test_sparse_forces_sum_to_zero_and_repeatable():
-    eng, g, (pos, Z, batch, cell), c = sparse_engine("a")
-    o1 = eng.energy_forces(pos, Z, batch, cell, g)
-    e1 = o1["energy"].clone()
-    o2 = eng.energy_forces(pos, Z, batch, cell, g)
-    torch.cuda.synchronize()
-    F = o1["forces"].double()
+@pytest.mark.parametrize("gemm_path", [0, 1])
+@pytest.mark.parametrize("tag", ["a", "d"])
+def test_sparse_forces_sum_to_zero_and_repeat_bit_for_bit(tag, gemm_path):
+    """The reverse pass has no floating-point atomics (dm rows reduced in a fixed order through the
+    transpose CSR): energies, forces and the virial repeat bit for bit."""
+    from fsctep_b200 import _native as NAT
+
+    eng, g, (pos, Z, batch, cell), c = sparse_engine(tag)
+    NAT.lib().fsc_ictd_set_gemm_path(gemm_path)
+    try:
+        outs = []
+        for _ in range(3):
+            o = eng.energy_forces(pos, Z, batch, cell, g)
+            outs.append({k: o[k].clone() for k in ("energy", "forces", "virial")})
+        torch.cuda.synchronize()
+    finally:
+        NAT.lib().fsc_ictd_set_gemm_path(0)
+    F = outs[0]["forces"].double()
     assert F.sum(0).abs().max().item() < 1e-3 * F.abs().max().item()
-    assert torch.equal(e1, o2["energy"])
+    for o in outs[1:]:
+        for k in ("energy", "forces", "virial"):
+            assert torch.equal(outs[0][k], o[k]), k
 
 
 def _dense_case(n_atoms=64, box=6.0, seed=11):
