@@ -725,10 +725,10 @@ __global__ void __launch_bounds__(256) dm_dn_kernel(Args a, Rows rows, const flo
       part[warp][rows.c2[r]][lane] += t;
     }
     __syncwarp();
-    if (lane < R) {
+    for (int c = lane; c < R; c += 32) {  // R = 40 components at lmax 3
       float v = 0.f;
-      for (int l = 0; l < 32; ++l) v += part[warp][lane][l];
-      dnp[e * MAXR + lane] += v;
+      for (int l = 0; l < 32; ++l) v += part[warp][c][l];
+      dnp[e * MAXR + c] += v;
     }
     __syncwarp();
   }
