@@ -88,6 +88,8 @@ _PROTOS = {
     "fsc_csr_transpose_workspace_bytes": (C.c_size_t, [I64, I64]),
     "fsc_csr_transpose": (C.c_int, [P, P, I64, I64, P, P, P, C.c_size_t, P]),
     "fsc_csr_transpose_static": (C.c_int, [P, P, I64, I64, P, P, P]),
+    "fsc_neighbor_cap_workspace_bytes": (C.c_size_t, [I64, I64]),
+    "fsc_neighbor_cap": (C.c_int, [P, P, P, I64, I64, P, P, C.c_int, P, P, P, P, P, C.c_size_t, P]),
     "fsc_ictd_tables_floats": (I64, []),
     "fsc_ictd_workspace_bytes": (C.c_size_t, [C.POINTER(IctdConfig), I64, I64]),
     "fsc_ictd_energy_forces": (C.c_int, [C.POINTER(IctdConfig), C.POINTER(IctdWeights), C.POINTER(Graph),

@@ -97,7 +97,8 @@ class NativeCalculator(_Base):
 
     def __init__(self, model, atomic_energies_dict: Dict[int, float], device, max_radius: float,
                  external_tensor: Optional[torch.Tensor] = None, fidelity_id: Optional[int] = None,
-                 return_physical_tensors: bool = False, graph_builder: Optional[Callable] = None, **kwargs: Any):
+                 return_physical_tensors: bool = False, graph_builder: Optional[Callable] = None,
+                 max_num_neighbors: Optional[int] = 100, **kwargs: Any):
         if fidelity_id is not None or return_physical_tensors:
             raise NotImplementedError("fsctep_b200 calculator: multi-fidelity and physical-tensor outputs are "
                                       "not covered by the native engines")
@@ -107,6 +108,9 @@ class NativeCalculator(_Base):
         self.max_radius = float(max_radius)
         self.atomic_energies = {int(k): float(v) for k, v in atomic_energies_dict.items()}
         self.external_tensor = external_tensor
+        # the reference's graph builder caps each source at 100 candidates per image shift
+        # (radius_graph_pbc_gpu's default, utils/graph_utils.py:192); None lifts the cap
+        self.max_num_neighbors = max_num_neighbors
         self.native = graph_builder is None  # the GPU cell list and a native engine
         if graph_builder is None:
             from .neighbors import build_graph as graph_builder
@@ -135,7 +139,7 @@ class NativeCalculator(_Base):
         cell_t = torch.tensor(cell, device=dev).reshape(1, 3, 3)
         species = torch.tensor(numbers, device=dev, dtype=torch.int32)
         batch = torch.zeros(len(numbers), device=dev, dtype=torch.int32)
-        graph = self.graph_builder(pos, cell_t, self.max_radius, pbc=pbc)
+        graph = self.graph_builder(pos, cell_t, self.max_radius, pbc=pbc, max_num_neighbors=self.max_num_neighbors)
         kwargs = {}
         if self.external_tensor is not None:
             kwargs["field"] = torch.as_tensor(self.external_tensor, device=dev).reshape(1, 3)

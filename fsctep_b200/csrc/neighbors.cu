@@ -300,6 +300,65 @@ __global__ void tr_sort_kernel(const int32_t* __restrict__ tr_ptr, int64_t N, in
   for (int e = e0 + lane; e < e1; e += 32) tr_eid[e] = tmp[e];
 }
 
+// Per-source neighbour cap (max_num_neighbors of radius_graph_pbc_gpu, utils/graph_utils.py:192,
+// 240): the reference runs one torch_cluster radius search per image shift S, and that search
+// keeps, for every source i, the first `cap` candidates j in ascending index order with
+// |pos[j] + S@cell - pos[i]| < cutoff; the self pair (j == i at S == 0) takes a slot before it is
+// removed.  One thread per source walks its out-edges in the transpose CSR (ascending edge id =
+// ascending dst, then shift) with one counter per shift.
+__device__ __forceinline__ int64_t row_of(const int32_t* __restrict__ row_ptr, int64_t N, int64_t e) {
+  int64_t lo = 0, hi = N;  // row_ptr[lo] <= e < row_ptr[hi]
+  while (hi - lo > 1) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (row_ptr[mid] <= e) lo = mid;
+    else hi = mid;
+  }
+  return lo;
+}
+__global__ void cap_mark_kernel(const int32_t* __restrict__ row_ptr, int64_t N, const int8_t* __restrict__ sidx,
+                                const int32_t* __restrict__ tr_ptr, const int32_t* __restrict__ tr_eid, int cap,
+                                uint8_t* __restrict__ keep) {
+  const int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= N) return;
+  int cnt[27];
+#pragma unroll
+  for (int k = 0; k < 27; ++k) cnt[k] = 0;
+  bool self_counted = false;
+  for (int t = tr_ptr[s]; t < tr_ptr[s + 1]; ++t) {
+    const int e = tr_eid[t];
+    const int k = min(max((int)sidx[e], 0), 26);
+    if (k == 13 && !self_counted && row_of(row_ptr, N, e) > s) {  // past j == i in the S == 0 search
+      ++cnt[13];
+      self_counted = true;
+    }
+    keep[e] = cnt[k] < cap ? 1 : 0;
+    ++cnt[k];
+  }
+}
+__global__ void cap_count_kernel(const int32_t* __restrict__ row_ptr, int64_t N, const uint8_t* __restrict__ keep,
+                                 int32_t* __restrict__ counts) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r > N) return;
+  int n = 0;
+  if (r < N)
+    for (int e = row_ptr[r]; e < row_ptr[r + 1]; ++e) n += keep[e];
+  counts[r] = n;
+}
+__global__ void cap_fill_kernel(const int32_t* __restrict__ row_ptr, int64_t N, const uint8_t* __restrict__ keep,
+                                const int32_t* __restrict__ src, const int8_t* __restrict__ sidx,
+                                const int32_t* __restrict__ out_ptr, int32_t* __restrict__ out_src,
+                                int8_t* __restrict__ out_sidx) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= N) return;
+  int o = out_ptr[r];
+  for (int e = row_ptr[r]; e < row_ptr[r + 1]; ++e)
+    if (keep[e]) {
+      out_src[o] = src[e];
+      out_sidx[o] = sidx[e];
+      ++o;
+    }
+}
+
 size_t scan_temp_bytes(int64_t n) {
   size_t bytes = 0;
   cub::DeviceScan::ExclusiveSum(nullptr, bytes, (int32_t*)nullptr, (int32_t*)nullptr, (int)n);
@@ -629,6 +688,55 @@ size_t fsc_csr_transpose_workspace_bytes(int64_t num_atoms, int64_t num_edges) {
   ar.take<int32_t>(num_edges + 1);
   ar.take<char>((int64_t)scan_temp_bytes(num_atoms + 1) + 16);
   return ar.off;
+}
+
+size_t fsc_neighbor_cap_workspace_bytes(int64_t num_atoms, int64_t num_edges) {
+  Arena ar(nullptr, 0);
+  ar.take<uint8_t>(num_edges + 1);
+  ar.take<int32_t>(num_atoms + 1);
+  ar.take<char>((int64_t)scan_temp_bytes(num_atoms + 1) + 16);
+  return ar.off;
+}
+
+int fsc_neighbor_cap(const int32_t* row_ptr, const int32_t* src, const int8_t* sidx, int64_t num_atoms,
+                     int64_t num_edges, const int32_t* tr_ptr, const int32_t* tr_eid, int max_num_neighbors,
+                     int32_t* out_row_ptr, int32_t* out_src, int8_t* out_sidx, int64_t* out_num_edges_host,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  FSC_REQUIRE(row_ptr && out_row_ptr && out_num_edges_host, "null pointer");
+  FSC_REQUIRE(num_atoms >= 0 && num_edges >= 0, "negative size");
+  FSC_REQUIRE(num_edges == 0 || (src && sidx && tr_ptr && tr_eid && out_src && out_sidx), "null edge arrays");
+  FSC_REQUIRE(max_num_neighbors >= 1, "max_num_neighbors must be >= 1");
+  FSC_REQUIRE(num_atoms < (int64_t)INT32_MAX && num_edges < (int64_t)INT32_MAX, "graph too large");
+  cudaStream_t st = as_stream(stream);
+  const int64_t N = num_atoms, E = num_edges;
+  Arena ar(workspace, workspace_bytes);
+  uint8_t* keep = ar.take<uint8_t>(E + 1);
+  int32_t* counts = ar.take<int32_t>(N + 1);
+  const size_t sbytes = scan_temp_bytes(N + 1);
+  void* stmp = ar.take<char>((int64_t)sbytes + 16);
+  if (!ar.ok() || workspace == nullptr)
+    return fail(FSC_ERR_CAPACITY, "neighbour cap workspace too small; size it with fsc_neighbor_cap_workspace_bytes");
+  if (E > 0 && N > 0) {
+    cap_mark_kernel<<<(unsigned)ceil_div(N, 128), 128, 0, st>>>(row_ptr, N, sidx, tr_ptr, tr_eid, max_num_neighbors,
+                                                                keep);
+    FSC_TRY(check_launch("cap_mark_kernel"));
+  }
+  cap_count_kernel<<<(unsigned)ceil_div(N + 1, 256), 256, 0, st>>>(row_ptr, N, keep, counts);
+  FSC_TRY(check_launch("cap_count_kernel"));
+  size_t sb = sbytes;
+  if (cub::DeviceScan::ExclusiveSum(stmp, sb, counts, out_row_ptr, (int)(N + 1), st) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "neighbour cap scan");
+  if (E > 0 && N > 0) {
+    cap_fill_kernel<<<(unsigned)ceil_div(N, 256), 256, 0, st>>>(row_ptr, N, keep, src, sidx, out_row_ptr, out_src,
+                                                                out_sidx);
+    FSC_TRY(check_launch("cap_fill_kernel"));
+  }
+  int32_t total = 0;
+  if (cudaMemcpyAsync(&total, out_row_ptr + N, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return fail(FSC_ERR_CUDA, "capped edge count readback");
+  *out_num_edges_host = total;
+  return FSC_OK;
 }
 
 }  // extern "C"

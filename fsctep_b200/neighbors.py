@@ -5,6 +5,11 @@ frames, all-pairs otherwise; identical edge sets, float64 distance test in a fix
 and the transpose CSR, returning a ``GraphCSR`` ready for ``ICTDEngine``.
 ``radius_graph_pbc`` returns the flat ``(edge_src, edge_dst, edge_shifts)`` triple of the
 reference function (canonical order: dst, then src, then shift).
+
+``max_num_neighbors`` applies the reference's per-source cap (``graph_utils.py:192, 240``): its
+torch_cluster search runs once per image shift and keeps, for every source atom, the first
+``max_num_neighbors`` candidates in ascending index order, the self pair at zero shift taking a
+slot.  ``radius_graph_pbc`` defaults to the reference's 100; ``build_graph`` to no cap.
 """
 
 from __future__ import annotations
@@ -24,7 +29,7 @@ def _sidx_to_shift(sidx: torch.Tensor) -> torch.Tensor:
 
 
 def build_graph(pos: torch.Tensor, cell: torch.Tensor, cutoff: float, frame_ptr: Sequence[int] = None,
-                pbc=(True, True, True)) -> GraphCSR:
+                pbc=(True, True, True), max_num_neighbors: int = None) -> GraphCSR:
     """pos (N,3) and cell (F,3,3) on the GPU (float64 used for the distance test)."""
     dev = pos.device
     pos64 = pos.detach().to(torch.float64).contiguous()
@@ -55,18 +60,39 @@ def build_graph(pos: torch.Tensor, cell: torch.Tensor, cutoff: float, frame_ptr:
                                 pbc_h.ctypes.data_as(N.P), float(cutoff), N.ptr(row_ptr), N.ptr(src), N.ptr(sidx), E,
                                 N.ptr(ws), ws.numel(), st), "fsc_neighbor_fill")
     src, sidx = src[:E], sidx[:E]
-    shift = _sidx_to_shift(sidx).to(torch.float32).contiguous()
     tr_ptr, tr_eid = GraphCSR.transpose(row_ptr, src, n)
+    if max_num_neighbors is not None:
+        row_ptr, src, sidx = _cap(row_ptr, src, sidx, tr_ptr, tr_eid, n, int(max_num_neighbors))
+        tr_ptr, tr_eid = GraphCSR.transpose(row_ptr, src, n)
+    shift = _sidx_to_shift(sidx).to(torch.float32).contiguous()
     g = GraphCSR(n, row_ptr, src, shift, tr_ptr, tr_eid)
     g.sidx = sidx
     return g
 
 
-def radius_graph_pbc(pos: torch.Tensor, r: float, cell: torch.Tensor, pbc=None, frame_ptr=None):
-    """(edge_src, edge_dst, edge_shifts) like the reference, canonical order, int64 / float64."""
+def _cap(row_ptr, src, sidx, tr_ptr, tr_eid, n: int, cap: int):
+    L = N.lib()
+    dev = src.device
+    E = int(src.shape[0])
+    out_ptr = torch.empty(n + 1, dtype=torch.int32, device=dev)
+    out_src = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
+    out_sidx = torch.empty(max(E, 1), dtype=torch.int8, device=dev)
+    ws = torch.empty(L.fsc_neighbor_cap_workspace_bytes(n, E), dtype=torch.uint8, device=dev)
+    ne = N.I64(0)
+    N.check(L.fsc_neighbor_cap(N.ptr(row_ptr), N.ptr(src), N.ptr(sidx), n, E, N.ptr(tr_ptr), N.ptr(tr_eid), cap,
+                               N.ptr(out_ptr), N.ptr(out_src), N.ptr(out_sidx), N.C.byref(ne), N.ptr(ws), ws.numel(),
+                               N.stream_ptr(dev)), "fsc_neighbor_cap")
+    E2 = int(ne.value)
+    return out_ptr, out_src[:E2], out_sidx[:E2]
+
+
+def radius_graph_pbc(pos: torch.Tensor, r: float, cell: torch.Tensor, max_num_neighbors: int = 100, pbc=None,
+                     frame_ptr=None):
+    """(edge_src, edge_dst, edge_shifts) like the reference, canonical order, int64 / float64;
+    the argument order of ``radius_graph_pbc_gpu(pos, r, cell, max_num_neighbors=100, pbc=None)``."""
     if pbc is None:
         pbc = (True, True, True)
-    g = build_graph(pos, cell, r, frame_ptr, pbc)
+    g = build_graph(pos, cell, r, frame_ptr, pbc, max_num_neighbors)
     dev = pos.device
     counts = (g.row_ptr[1:] - g.row_ptr[:-1]).to(torch.int64)
     dst = torch.repeat_interleave(torch.arange(g.num_atoms, device=dev), counts)

@@ -151,6 +151,19 @@ size_t fsc_csr_transpose_workspace_bytes(int64_t num_atoms, int64_t num_edges);
 int fsc_csr_transpose(const int32_t* row_ptr, const int32_t* src, int64_t num_atoms,
                       int64_t num_edges, int32_t* tr_ptr, int32_t* tr_eid, void* workspace,
                       size_t workspace_bytes, void* stream);
+/* Per-source cap of radius_graph_pbc_gpu's max_num_neighbors (utils/graph_utils.py:192, 240):
+ * the reference runs one torch_cluster radius search per image shift, which keeps for every
+ * source i the first max_num_neighbors candidates j (ascending j) inside the cutoff, the self
+ * pair at S = 0 taking a slot before it is dropped.  Input: a CSR from fsc_neighbor_fill and
+ * its transpose; output: the capped CSR (out_row_ptr[N+1], out_src / out_sidx with room for
+ * num_edges entries, rows in the input order) and its edge count (host).  Synchronises
+ * `stream`.  Workspace >= fsc_neighbor_cap_workspace_bytes(N, E).                            */
+size_t fsc_neighbor_cap_workspace_bytes(int64_t num_atoms, int64_t num_edges);
+int fsc_neighbor_cap(const int32_t* row_ptr, const int32_t* src, const int8_t* sidx,
+                     int64_t num_atoms, int64_t num_edges, const int32_t* tr_ptr,
+                     const int32_t* tr_eid, int max_num_neighbors, int32_t* out_row_ptr,
+                     int32_t* out_src, int8_t* out_sidx, int64_t* out_num_edges_host,
+                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* Allocation-free transpose, for callers that cannot call cudaMalloc (a CUDA-graph-captured
  * MD step, a host that hands all device memory to a fixed pool, an FFI binding without a

@@ -96,7 +96,7 @@ def _split(x, C, lmax):
 
 
 def _merge(blocks, lmax):
-    return torch.cat([blocks[l].reshape(blocks[l].shape[0], -1) for l in range(lmax + 1)], dim=-1)
+    return torch.cat([blocks[l].flatten(1) for l in range(lmax + 1)], dim=-1)
 
 
 def _scatter_sum(x, index, n):

@@ -72,7 +72,7 @@ def split_o3(x, C, active):
 
 
 def merge_o3(blocks, active):
-    return torch.cat([blocks[k].reshape(blocks[k].shape[0], -1) for k in active], dim=-1)
+    return torch.cat([blocks[k].flatten(1) for k in active], dim=-1)
 
 
 def field_harmonic(field: torch.Tensor) -> torch.Tensor:

@@ -9,8 +9,11 @@ Restates the semantics of ``radius_graph_pbc_gpu`` (``utils/graph_utils.py:192-2
   (torch_cluster ``radius(pos + S@cell, pos, r)``: query ``i`` in ``pos``, neighbour
   ``j`` in the shifted copy, ``:240-242``), excluding ``i == j`` at ``S == 0``
   (``:244-246``);
-* the reference's per-query cap ``max_num_neighbors=100`` per image is reported,
-  not applied (the builder raises when a query exceeds it).
+* with ``max_num_neighbors`` given, the reference's per-query cap (``:192, 240``): the
+  published algorithm of torch_cluster's CUDA ``radius`` kernel (torch_cluster is a dependency
+  that is not vendored) visits the candidates ``j`` of query ``i`` in ascending index order and
+  stops after ``max_num_neighbors`` hits, so per image shift only the first hits survive; the
+  self pair at ``S == 0`` is one of them and is removed afterwards.
 
 Arithmetic is float64 in one fixed order, which the CUDA builder reproduces without
 FMA contraction so that both produce the same edge set bit for bit:
@@ -39,7 +42,7 @@ def shift_vectors(shifts: np.ndarray, cell: np.ndarray) -> np.ndarray:
 
 
 def neighbor_list(pos: np.ndarray, cell: np.ndarray, r: float, pbc=(True, True, True),
-                  chunk: int = 2048):
+                  chunk: int = 2048, max_num_neighbors: int = None):
     """Brute-force O(27 N^2) neighbour list; returns (src, dst, shifts) int64, canonical order."""
     pos = np.asarray(pos, dtype=np.float64)
     n = pos.shape[0]
@@ -50,11 +53,17 @@ def neighbor_list(pos: np.ndarray, cell: np.ndarray, r: float, pbc=(True, True, 
     for k in range(S.shape[0]):
         shifted = pos + sv[k][None, :]
         zero = not S[k].any()
+        hits = np.zeros(n, dtype=np.int64)  # hits of each query so far in this image (self included)
         for j0 in range(0, n, chunk):
             pj = shifted[j0:j0 + chunk]                     # neighbours j
             d = pj[None, :, :] - pos[:, None, :]            # (i, j, 3)
             r2 = (d[..., 0] * d[..., 0] + d[..., 1] * d[..., 1]) + d[..., 2] * d[..., 2]
-            ii, jj = np.nonzero(r2 < r2max)
+            m = r2 < r2max
+            if max_num_neighbors is not None:
+                rank = hits[:, None] + np.cumsum(m, axis=1)  # 1-based hit number of (i, j)
+                hits += m.sum(axis=1)
+                m &= rank <= max_num_neighbors
+            ii, jj = np.nonzero(m)
             jj = jj + j0
             if zero:
                 keep = ii != jj
@@ -70,12 +79,12 @@ def neighbor_list(pos: np.ndarray, cell: np.ndarray, r: float, pbc=(True, True, 
 
 
 def batched_neighbor_list(pos: np.ndarray, batch: np.ndarray, cells: np.ndarray, r: float,
-                          pbc=(True, True, True)):
+                          pbc=(True, True, True), max_num_neighbors: int = None):
     """Per-frame lists concatenated with global atom indices (frames independent)."""
     out_s, out_d, out_S = [], [], []
     for g in range(cells.shape[0]):
         idx = np.nonzero(batch == g)[0]
-        s, d, S = neighbor_list(pos[idx], cells[g], r, pbc)
+        s, d, S = neighbor_list(pos[idx], cells[g], r, pbc, max_num_neighbors=max_num_neighbors)
         out_s.append(idx[s])
         out_d.append(idx[d])
         out_S.append(S)

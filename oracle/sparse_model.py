@@ -41,7 +41,7 @@ def rank_powers(n: torch.Tensor, lmax: int) -> List[torch.Tensor]:
     E = n.shape[0]
     out = [torch.ones(E, 1, dtype=n.dtype)]
     for L in range(1, lmax + 1):
-        out.append((out[-1].unsqueeze(-1) * n.unsqueeze(-2)).reshape(E, -1))
+        out.append((out[-1].unsqueeze(-1) * n.unsqueeze(-2)).flatten(1))
     return out
 
 

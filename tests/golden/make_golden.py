@@ -27,6 +27,12 @@ Fixtures:
 * ``ictd_hook.npz`` / ``ictd_o3_hook.npz`` -- an ictd and an o3 model evaluated with a seeded,
   differentiable ``sync_after_scatter`` (per-node scale, then ghost rows overwritten by owner
   rows): energies and forces.
+* ``ictd_model_e.npz`` / ``ictd_o3_e.npz`` / ``sparse_e.npz`` -- the three models on frames with a
+  receiver that has no neighbours (a bonded chain plus one atom 30 A away, a lone-atom frame, a
+  dimer); ``ictd_model_z.npz`` / ``sparse_z.npz`` -- a system with no edges at all.  The reference
+  clamps the neighbour count at 1 (``pure_cartesian_ictd_layers_full.py:471,929``,
+  ``pure_cartesian_sparse_layers.py:328``) and averages E/N over the whole system
+  (``pure_cartesian_sparse_layers.py:419``).
 * ``tp_ops.npz`` -- the ``_C_ictd_tp`` operator family evaluated by the reference's
   einsum references (``models/ictd_irreps_cuda.py:169-311``) on the shapes of
   ``test/test_ictd_tp_backend.py``.
@@ -248,6 +254,36 @@ def sparse_widths():
     sparse_case("d", systems.fcc_crystal(n_cells=(2, 2, 2), seed=21), cfg5, seed=9)
 
 
+def isolated_frames(seed):
+    """Three non-periodic frames: a 12-atom bonded chain with one O atom 30 A from its centre, a
+    lone C atom, and an H-O dimer at 1.2 A."""
+    m = systems.organic_molecules(n_mol=1, min_atoms=12, max_atoms=12, seed=seed)
+    far = m["pos"].mean(axis=0) + np.array([30.0, 0.0, 0.0])
+    pos = np.vstack([m["pos"], far, [[50.0, 50.0, 50.0]], [[50.0, 50.0, 50.0], [51.2, 50.1, 49.9]]])
+    Z = np.concatenate([m["Z"], [8, 6, 1, 8]])
+    batch = np.concatenate([np.zeros(13, dtype=np.int64), [1, 2, 2]])
+    cells = np.stack([np.eye(3) * 100.0] * 3)
+    return systems._system(pos, Z, batch, cells, pbc=(False, False, False))
+
+
+def no_edge_frames():
+    """Two non-periodic frames of three atoms each, 8 A apart: no pair within the 5 A cutoff."""
+    pos = np.array([[10.0, 10.0, 10.0], [18.0, 10.0, 10.0], [10.0, 18.0, 10.0],
+                    [10.0, 10.0, 10.0], [10.0, 10.0, 18.0], [18.0, 18.0, 18.0]])
+    return systems._system(pos, [1, 6, 8, 8, 7, 1], [0, 0, 0, 1, 1, 1], np.stack([np.eye(3) * 40.0] * 2),
+                           pbc=(False, False, False))
+
+
+def edge_cases():
+    cfg = dict(channels=32, lmax=2, num_interaction=3, number_of_basis=8, max_radius=5.0,
+               function_type="gaussian", max_atomvalue=10)
+    model_case("e", isolated_frames(seed=30), cfg, seed=31)
+    o3_case("e", isolated_frames(seed=30), cfg, seed=32, field_seed=33)
+    sparse_case("e", isolated_frames(seed=30), cfg, seed=34)
+    model_case("z", no_edge_frames(), cfg, seed=35)
+    sparse_case("z", no_edge_frames(), cfg, seed=36)
+
+
 def tp_ops():
     from molecular_force_field.models import ictd_irreps_cuda as RC
 
@@ -360,6 +396,7 @@ def main():
     sparse()
     sparse_widths()
     hook_cases()
+    edge_cases()
 
 
 def o3():
@@ -379,5 +416,7 @@ if __name__ == "__main__":
         sparse_widths()
     elif len(sys.argv) > 1 and sys.argv[1] == "hooks":
         hook_cases()
+    elif len(sys.argv) > 1 and sys.argv[1] == "edge_cases":
+        edge_cases()
     else:
         main()

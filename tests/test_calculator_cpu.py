@@ -40,7 +40,8 @@ class _Engine:
 
 
 def _graph_builder(log):
-    def build(pos, cell, cutoff, pbc=(True, True, True)):
+    def build(pos, cell, cutoff, pbc=(True, True, True), max_num_neighbors=None):
+        assert max_num_neighbors == 100  # the reference builder's default cap
         log.append((cell.clone(), cutoff, pbc))
         return "graph"
     return build

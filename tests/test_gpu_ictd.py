@@ -9,7 +9,7 @@ import gpu_util as U
 pytestmark = [pytest.mark.gpu, U.needs_gpu]
 
 
-@pytest.mark.parametrize("tag", ["a", "b", "c"])
+@pytest.mark.parametrize("tag", ["a", "b", "c", "e", "z"])
 def test_energy_forces_stress_match_reference(tag):
     eng, g, (pos, Z, batch, cell), c, _, _ = U.golden_engine(tag)
     out = eng.energy_forces(pos, Z, batch, cell, g)

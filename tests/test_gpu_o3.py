@@ -27,7 +27,7 @@ def _engine(tag):
 
 
 @pytest.mark.parametrize("readout_path", [0, 1])
-@pytest.mark.parametrize("tag", ["a", "b"])
+@pytest.mark.parametrize("tag", ["a", "b", "e"])
 def test_o3_energy_forces_heads_match_reference(tag, readout_path):
     from fsctep_b200 import _native as NAT
 

@@ -27,7 +27,7 @@ def sparse_engine(tag):
     return eng, g, inputs, c
 
 
-@pytest.mark.parametrize("tag", ["a", "b"])
+@pytest.mark.parametrize("tag", ["a", "b", "e", "z"])
 def test_sparse_energy_forces_stress_match_reference(tag):
     eng, g, (pos, Z, batch, cell), c = sparse_engine(tag)
     out = eng.energy_forces(pos, Z, batch, cell, g)

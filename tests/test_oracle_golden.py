@@ -39,7 +39,7 @@ def test_high_lmax_basis_orthonormal():
         np.testing.assert_allclose((B.T @ G @ B).numpy(), np.eye(2 * L + 1), atol=1e-10)
 
 
-@pytest.mark.parametrize("tag", ["a", "b", "c"])
+@pytest.mark.parametrize("tag", ["a", "b", "c", "e", "z"])
 def test_oracle_energy_forces_stress_match_reference(tag):
     cfg, sd, c = golden_io.model_case(tag)
     ocfg = OM.ICTDConfig(**cfg)
@@ -52,7 +52,7 @@ def test_oracle_energy_forces_stress_match_reference(tag):
     np.testing.assert_allclose(out["stress"].numpy(), c["ref64_stress"], rtol=1e-9, atol=1e-11)
 
 
-@pytest.mark.parametrize("tag", ["a", "b", "c"])
+@pytest.mark.parametrize("tag", ["a", "b", "c", "e", "z"])
 def test_neighbor_oracle_reproduces_fixture(tag):
     _, _, c = golden_io.model_case(tag)
     src, dst, S = ON.batched_neighbor_list(c["pos"], c["batch"], c["cell"], 5.0, tuple(c["pbc"]))

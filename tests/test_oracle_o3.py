@@ -9,7 +9,7 @@ from oracle import ictd_o3 as O3
 from oracle.ictd_model import ICTDConfig
 
 
-@pytest.mark.parametrize("tag", ["a", "b"])
+@pytest.mark.parametrize("tag", ["a", "b", "e"])
 def test_o3_oracle_matches_reference(tag):
     cfg, sd, c = golden_io.o3_case(tag)
     ocfg = ICTDConfig(channels=int(cfg["channels"]), num_interaction=int(cfg["num_interaction"]),

@@ -15,7 +15,7 @@ def _cfg(cfg):
                       max_atomvalue=int(cfg["max_atomvalue"]))
 
 
-@pytest.mark.parametrize("tag", ["a", "b", "c", "d"])
+@pytest.mark.parametrize("tag", ["a", "b", "c", "d", "e", "z"])
 def test_sparse_oracle_matches_reference(tag):
     cfg, sd, c = golden_io.sparse_case(tag)
     r = SP.sparse_energy_forces_stress(sd, _cfg(cfg), torch.tensor(c["pos"]), torch.tensor(c["Z"]),
