@@ -754,7 +754,14 @@ def main():
                     help="steps of the untimed per-stage pass (default: --steps)")
     ap.add_argument("--clocks-csv", default=None, help="where to write the nvidia-smi clock samples (default: a "
                                                         "temporary directory)")
+    ap.add_argument("--conv2-tc", action="store_true",
+                    help="pure-cartesian-ictd: the conv2 gate gradients on the tensor-core kernel instead of the "
+                         "(faster, default) CUDA-core one")
     args = ap.parse_args()
+    if args.conv2_tc and args.impl == "native":
+        from fsctep_b200 import _native as NAT
+
+        NAT.lib().fsc_ictd_set_conv2_path(1)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

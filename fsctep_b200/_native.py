@@ -121,6 +121,7 @@ _PROTOS = {
     "fsc_ictd_heads": (C.c_int, [P, P, P, C.c_int, P, P, P, P, C.c_size_t, P]),
     "fsc_ictd_set_radial_path": (None, [C.c_int]),
     "fsc_ictd_set_gemm_path": (None, [C.c_int]),
+    "fsc_ictd_set_conv2_path": (None, [C.c_int]),
     "fsc_fp32_fma_probe": (C.c_int, [C.c_int, C.c_int, C.c_int, P, C.POINTER(C.c_double), P]),
     "fsc_gemm_tc_plan": (C.c_int, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "fsc_profile_enable": (None, [C.c_int]),

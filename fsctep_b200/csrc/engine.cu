@@ -98,6 +98,7 @@ struct Plan {
 int g_readout_path = 0;  // 0: tensor cores where supported, 1: CUDA cores
 int g_radial_path = 0;   // 0: tensor cores where supported, 1: CUDA cores
 int g_gemm_path = 0;     // 0: tensor cores where supported, 1: CUDA cores
+int g_conv2_path = 0;    // conv2 gate gradients: 0 CUDA cores (faster), 1 tensor cores
 
 int validate(const fsc_ictd_config* cfg) {
   FSC_REQUIRE(cfg != nullptr, "config is null");
@@ -516,7 +517,10 @@ int backward_conv2(Ctx& c, int k) {
     prof::mark("conv2_mix_backward_dz", st);
     ConvArgs cq = ca;
     cq.N = p.N;  // every receiver: the ones not evaluated zero their gate gradients
-    FSC_TRY(launch_conv2_q(cq, p.feats[k - 1], p.zbuf, p.dgates + (int64_t)k * p.E * 12, p.dY, st));
+    if (g_conv2_path == 1)
+      FSC_TRY(launch_conv2_q_tc(cq, p.feats[k - 1], p.zbuf, p.dgates + (int64_t)k * p.E * 12, p.dY, st));
+    else
+      FSC_TRY(launch_conv2_q(cq, p.feats[k - 1], p.zbuf, p.dgates + (int64_t)k * p.E * 12, p.dY, st));
     prof::mark("conv2_edge_backward_gates", st);
     ConvArgs cr = ca;
     cr.N = p.nk[k - 1];  // senders whose layer k-1 features were evaluated
@@ -842,6 +846,7 @@ int fsc_ictd_status(const fsc_ictd_config* cfg, int64_t num_atoms, int64_t num_e
 void fsc_ictd_set_readout_path(int path) { fsc::g_readout_path = path; }
 void fsc_ictd_set_radial_path(int path) { fsc::g_radial_path = path; }
 void fsc_ictd_set_gemm_path(int path) { fsc::g_gemm_path = path; }
+void fsc_ictd_set_conv2_path(int path) { fsc::g_conv2_path = path; }
 
 void fsc_profile_enable(int enable) {
   fsc::prof::enabled = enable != 0;

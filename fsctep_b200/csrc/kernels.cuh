@@ -107,6 +107,9 @@ int launch_conv2_r(const ConvArgs& a, const float* G, float* R, cudaStream_t st)
 // conv2 backward, dst-centric: dgates[e][p], dY[e][k] += from x[src] and dZ[dst]
 int launch_conv2_q(const ConvArgs& a, const float* x, const float* dZ, float* dgates, float* dY,
                    cudaStream_t st);
+// the same on the tensor cores (conv2_q_tc.cu); needs a.work
+int launch_conv2_q_tc(const ConvArgs& a, const float* x, const float* dZ, float* dgates, float* dY,
+                      cudaStream_t st);
 
 // Generic fp32 GEMM with two-level row addressing:
 //   row (g, r), g < G, r < R:  A + g*a_gs + r*a_rs (K contiguous), C + g*c_gs + r*c_rs (N contiguous)

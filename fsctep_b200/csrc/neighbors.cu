@@ -604,7 +604,7 @@ int fsc_csr_transpose(const int32_t* row_ptr, const int32_t* src, int64_t num_at
                       int32_t* tr_ptr, int32_t* tr_eid, void* workspace, size_t workspace_bytes, void* stream) {
   cudaStream_t st = as_stream(stream);
   const int64_t N = num_atoms, E = num_edges;
-  FSC_REQUIRE(tr_ptr && tr_eid && row_ptr && src, "null pointer");
+  FSC_REQUIRE(tr_ptr && row_ptr && (E == 0 || (tr_eid && src)), "null pointer");
   Arena ar(workspace, workspace_bytes);
   int32_t* cnt = ar.take<int32_t>(N + 1);
   int32_t* cursor = ar.take<int32_t>(N + 1);

@@ -227,5 +227,17 @@ __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) 
   lo = l;
 }
 
+// The same split by bit operations on the ALU / FMA pipes (no conversion instructions):
+// hi = x with the 13 low mantissa bits cleared, the exact remainder x - hi rounded to tf32 by
+// adding half a tf32 unit before clearing them (round half away from zero in magnitude; a carry
+// into the exponent is the correct rounding).  Both halves are exact tf32 values and
+// |x - hi - lo| <= 2^-22 |x|, like split_tf32.
+__device__ __forceinline__ void split_tf32_bits(float x, uint32_t& hi, uint32_t& lo) {
+  const uint32_t h = __float_as_uint(x) & 0xFFFFE000u;
+  const float r = x - __uint_as_float(h);
+  hi = h;
+  lo = (__float_as_uint(r) + 0x1000u) & 0xFFFFE000u;
+}
+
 }  // namespace tc
 }  // namespace fsc

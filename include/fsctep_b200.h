@@ -353,6 +353,10 @@ void fsc_ictd_set_radial_path(int path);
  * shape qualifies (default), 1 = CUDA-core kernels, 2 = tensor-core aggregation with CUDA-core
  * GEMMs, 3 = CUDA-core aggregation with tensor-core GEMMs.  Process-wide. */
 void fsc_ictd_set_gemm_path(int path);
+/* conv2 gate / harmonic gradients (the reverse of the per-edge contraction with the sender
+ * rows): 0 = CUDA-core kernel (default, the faster one), 1 = tensor cores (tcgen05, 3xTF32,
+ * one 128 x 48 product per 14 edges of a receiver, warp-specialised pipeline).  Process-wide. */
+void fsc_ictd_set_conv2_path(int path);
 /* Plan of the tensor-core GEMM for a K x N product (host arithmetic, no device work): the output
  * tile width and the longest chain of tcgen05.mma instructions that accumulate into one TMEM
  * accumulator before the partial sum moves to fp32 registers (tensor-core accumulation rounds

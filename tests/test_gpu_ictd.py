@@ -145,3 +145,47 @@ def test_tensor_core_gemms_match_cuda_core(channels, n_cells):
     assert U.rel_max(out["forces"].cpu().numpy(), ref["forces"].cpu().numpy()) <= 1e-4
     assert U.rel_max(out["atom_energy"].cpu().numpy(), ref["atom_energy"].cpu().numpy()) <= 1e-4
     assert U.rel_max(out["stress"].cpu().numpy(), ref["stress"].cpu().numpy()) <= 1e-4
+
+
+@pytest.mark.parametrize("channels,kind", [(64, "diamond"), (32, "diamond"), (64, "frames")])
+def test_tensor_core_conv2_gates_match_cuda_core(channels, kind):
+    """tcgen05 conv2 gate / harmonic gradients (conv2 path 1; 14 edges of a receiver per
+    128 x 48 product) vs the CUDA-core kernel (the default): degrees of 28 (two full tiles) and
+    of 30-70 (partial tiles).  Energies are the same bits (forward unchanged); forces and stress
+    agree to fp32 accuracy; the tensor-core reverse pass repeats bit for bit."""
+    from fsctep_b200 import _native as NAT
+    from fsctep_b200 import systems
+    from fsctep_b200.ictd import ICTDConfig, ICTDEngine
+    from fsctep_b200.models import reference_state_dict_shapes
+    from fsctep_b200.neighbors import build_graph
+    from fsctep_b200.weights import seeded_state_dict
+
+    cfg = ICTDConfig(channels=channels, num_interaction=3, number_of_basis=8, max_radius=5.0,
+                     function_type="gaussian", max_atomvalue=16)
+    eng = ICTDEngine(seeded_state_dict(reference_state_dict_shapes(cfg), 13), cfg, "cuda")
+    if kind == "diamond":
+        s = systems.diamond_crystal(n_cells=(4, 4, 3), seed=29)
+    else:
+        s = systems.random_frames(n_frames=3, n_atoms=96, box=9.0, seed=30)
+    dev = torch.device("cuda")
+    pos, cell = torch.tensor(s["pos"], device=dev), torch.tensor(s["cell"], device=dev)
+    b_np = s["batch"]
+    fp = np.concatenate([[0], np.cumsum(np.bincount(b_np, minlength=s["cell"].shape[0]))])
+    g = build_graph(pos, cell, 5.0, frame_ptr=fp)
+    deg = (g.row_ptr[1:] - g.row_ptr[:-1]).cpu().numpy()
+    assert deg.min() > 0 and (kind == "diamond" or (deg % 14 != 0).any())
+    Z, b = torch.tensor(s["Z"], device=dev), torch.tensor(b_np, device=dev)
+    try:
+        ref = eng.energy_forces(pos, Z, b, cell, g)
+        torch.cuda.synchronize()
+        NAT.lib().fsc_ictd_set_conv2_path(1)
+        out = eng.energy_forces(pos, Z, b, cell, g)
+        again = eng.energy_forces(pos, Z, b, cell, g)
+        torch.cuda.synchronize()
+        assert eng.status() == 0
+    finally:
+        NAT.lib().fsc_ictd_set_conv2_path(0)
+    assert torch.equal(out["energy"], ref["energy"])
+    assert U.rel_max(out["forces"].cpu().numpy(), ref["forces"].cpu().numpy()) <= 2e-5
+    assert U.rel_max(out["stress"].cpu().numpy(), ref["stress"].cpu().numpy()) <= 2e-5
+    assert torch.equal(out["forces"], again["forces"]) and torch.equal(out["virial"], again["virial"])
