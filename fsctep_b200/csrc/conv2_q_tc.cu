@@ -344,10 +344,10 @@ __global__ void __launch_bounds__(QT_THREADS, 1)
           if (row < NZ) {
             const float4 v = reinterpret_cast<const float4*>(zsrc + row * C)[kc];
             uint4 h, l;
-            tc::split_tf32_bits(v.x, h.x, l.x);
-            tc::split_tf32_bits(v.y, h.y, l.y);
-            tc::split_tf32_bits(v.z, h.z, l.z);
-            tc::split_tf32_bits(v.w, h.w, l.w);
+            tc::split_tf32(v.x, h.x, l.x);
+            tc::split_tf32(v.y, h.y, l.y);
+            tc::split_tf32(v.z, h.z, l.z);
+            tc::split_tf32(v.w, h.w, l.w);
             reinterpret_cast<uint4*>(bhi)[kc * QT_N + row] = h;
             reinterpret_cast<uint4*>(blo)[kc * QT_N + row] = l;
           }
@@ -369,10 +369,10 @@ __global__ void __launch_bounds__(QT_THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const float4 v = valid ? reinterpret_cast<const float4*>(xr)[4 * h + i] : make_float4(0.f, 0.f, 0.f, 0.f);
-            tc::split_tf32_bits(v.x, hi[4 * i], lo[4 * i]);
-            tc::split_tf32_bits(v.y, hi[4 * i + 1], lo[4 * i + 1]);
-            tc::split_tf32_bits(v.z, hi[4 * i + 2], lo[4 * i + 2]);
-            tc::split_tf32_bits(v.w, hi[4 * i + 3], lo[4 * i + 3]);
+            tc::split_tf32(v.x, hi[4 * i], lo[4 * i]);
+            tc::split_tf32(v.y, hi[4 * i + 1], lo[4 * i + 1]);
+            tc::split_tf32(v.z, hi[4 * i + 2], lo[4 * i + 2]);
+            tc::split_tf32(v.w, hi[4 * i + 3], lo[4 * i + 3]);
           }
           tc::tmem_st16(tA + 16u * h, hi);
           tc::tmem_st16(tA + (uint32_t)C + 16u * h, lo);

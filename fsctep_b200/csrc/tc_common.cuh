@@ -218,25 +218,14 @@ __device__ __forceinline__ float f16_range_scale(float bound) {
 
 // tf32 split: hi = round_tf32(x) (exactly representable, |x - hi| <= 2^-11 |x|),
 // lo = round_tf32(x - hi); hi*hi + hi*lo + lo*hi then misses at most ~2^-22 of each product.
+// Rounding to nearest with ties away from zero (the cvt.rna.tf32.f32 rule) by bit operations on
+// the ALU / FMA pipes: add half a tf32 unit (bit 12) to the magnitude bits and clear the 13 low
+// mantissa bits (a carry into the exponent is the correct rounding; denormals round the same way).
+__device__ __forceinline__ uint32_t round_tf32_bits(uint32_t b) { return (b + 0x1000u) & 0xFFFFE000u; }
 __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
-  uint32_t h, l;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
-  const float r = x - __uint_as_float(h);
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(r));
+  const uint32_t h = round_tf32_bits(__float_as_uint(x));
   hi = h;
-  lo = l;
-}
-
-// The same split by bit operations on the ALU / FMA pipes (no conversion instructions):
-// hi = x with the 13 low mantissa bits cleared, the exact remainder x - hi rounded to tf32 by
-// adding half a tf32 unit before clearing them (round half away from zero in magnitude; a carry
-// into the exponent is the correct rounding).  Both halves are exact tf32 values and
-// |x - hi - lo| <= 2^-22 |x|, like split_tf32.
-__device__ __forceinline__ void split_tf32_bits(float x, uint32_t& hi, uint32_t& lo) {
-  const uint32_t h = __float_as_uint(x) & 0xFFFFE000u;
-  const float r = x - __uint_as_float(h);
-  hi = h;
-  lo = (__float_as_uint(r) + 0x1000u) & 0xFFFFE000u;
+  lo = round_tf32_bits(__float_as_uint(x - __uint_as_float(h)));
 }
 
 }  // namespace tc
