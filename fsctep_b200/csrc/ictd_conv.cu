@@ -328,7 +328,8 @@ __global__ void __launch_bounds__(CONV_WARPS * 32, 3) conv2_r_kernel(ConvArgs a,
 // accumulated as even / odd channel partial sums with packed fp32 FMAs (two channels per
 // instruction).
 constexpr int QCH = 16;                       // channels per staged chunk
-constexpr int QES = 4 * 5 + 1;                // float4 slots per edge in a chunk (odd: no bank conflicts)
+constexpr int QRMAX = 3;                      // sender rows per pass (the l1 = 2 group in two passes)
+constexpr int QES = 4 * QRMAX + 1;            // float4 slots per edge in a chunk (odd: no bank conflicts)
 constexpr int QZR = 14;                       // dZ rows of the largest l1 group
 constexpr int QBUF_F4 = 32 * QES + 4 * QZR;   // one step: sender rows, then dZ rows
 constexpr int QTAB_F4 = (NQ * 5 + 3) / 4 + 9; // cg2, then the dZ row list of every group (35 ints)
@@ -343,6 +344,19 @@ __host__ __device__ constexpr int zlocal(int p, int kk) {
 __host__ __device__ constexpr int zcount(int G) { return zlocal(P_HI(G) - 1, 2 * L3(P_HI(G) - 1)) + 1; }
 __host__ __device__ constexpr int zbase(int G) { return G == 0 ? 0 : (G == 1 ? zcount(0) : zcount(0) + zcount(1)); }
 
+// A pass covers the sender rows m1 in [R0, R1) of l1 group G; its Q entries (p, m1, kk) are held
+// path by path, then row by row.
+template <int G, int R0, int R1>
+__host__ __device__ constexpr int qloc(int p, int m1, int kk) {
+  int j = 0;
+  for (int pp = P_LO(G); pp < p; ++pp) j += (R1 - R0) * (2 * L3(pp) + 1);
+  return j + (m1 - R0) * (2 * L3(p) + 1) + kk;
+}
+template <int G, int R0, int R1>
+__host__ __device__ constexpr int qcount() {
+  return qloc<G, R0, R1>(P_HI(G) - 1, R1 - 1, 2 * L3(P_HI(G) - 1)) + 1;
+}
+
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
                "l"(gmem_src)
@@ -352,19 +366,19 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Issues the copies of step (G, cc) into `buf` as one group: 32 edges x (2G+1) rows x 4 float4
-// (lane copies slots f = lane + 32 i, f = (edge, m1, c4)), then the group's dZ rows.
-template <int G, int C>
+// Issues the copies of step (pass, cc) into `buf` as one group: 32 edges x (R1 - R0) rows x 4
+// float4 (lane copies slots f = lane + 32 i, f = (edge, row, c4)), then the group's dZ rows.
+template <int G, int R0, int R1, int C>
 __device__ __forceinline__ void q_stage(float4* __restrict__ buf, const int* __restrict__ zlist,
                                         const float* __restrict__ x, int64_t src_row,
                                         const float* __restrict__ dzn, int cc, int lane) {
-  constexpr int M1 = 2 * G + 1, NZG = zcount(G);
-  static_assert(NZG <= QZR, "dZ row buffer");
+  constexpr int NR = R1 - R0, NZG = zcount(G);
+  static_assert(NR <= QRMAX && NZG <= QZR, "staging buffer");
 #pragma unroll 1
-  for (int i = 0; i < 4 * M1; ++i) {
-    const int f = lane + 32 * i, e = f / (4 * M1), r = f - e * (4 * M1);
+  for (int i = 0; i < 4 * NR; ++i) {
+    const int f = lane + 32 * i, e = f / (4 * NR), r = f - e * (4 * NR);
     const int64_t row = __shfl_sync(0xffffffffu, src_row, e);
-    cp_async16(buf + e * QES + r, x + (row + KB(G) + (r >> 2)) * C + cc * QCH + 4 * (r & 3));
+    cp_async16(buf + e * QES + r, x + (row + KB(G) + R0 + (r >> 2)) * C + cc * QCH + 4 * (r & 3));
   }
   float4* zb = buf + 32 * QES;
   for (int f = lane; f < 4 * NZG; f += 32)
@@ -376,29 +390,29 @@ __device__ __forceinline__ float2 ffma2(float a0, float a1, float b0, float b1, 
   return __ffma2_rn(make_float2(a0, a1), make_float2(b0, b1), c);
 }
 
-// Group G: its Q partial sums over all chunks, then its share of dgate / dY.  On entry step
-// (G, 0) is staged (or in flight) in bufs[0]; the group stages every following step, the first
-// step of group G + 1 included, one step ahead.
-template <int G, int C>
-__device__ __forceinline__ void q_group(float4* __restrict__ bufs, const int* __restrict__ zlist,
-                                        const float* __restrict__ x, int64_t src_row, const float* __restrict__ dzn,
-                                        const float* __restrict__ cg2, const float4* __restrict__ ey4,
-                                        const float4* __restrict__ eg4, float* dg, float* dy) {
-  constexpr int Q0 = QOFF(P_LO(G)), NQG = Q_END(G) - Q0, M1 = 2 * G + 1, NCH = C / QCH;
-  static_assert(NCH % 2 == 0, "every group starts in buffer 0");
+// Pass (G, R0, R1): its Q partial sums over all chunks, then its share of dgate / dY.  On entry
+// step (pass, 0) is staged (or in flight) in bufs[0]; the pass stages every following step, the
+// first step of the next pass (NG, NR0, NR1; NG < 0: none) included, one step ahead.
+template <int G, int R0, int R1, int NG, int NR0, int NR1, int C>
+__device__ __forceinline__ void q_pass(float4* __restrict__ bufs, const int* __restrict__ zlist,
+                                       const float* __restrict__ x, int64_t src_row, const float* __restrict__ dzn,
+                                       const float* __restrict__ cg2, const float4* __restrict__ ey4,
+                                       const float4* __restrict__ eg4, float* dg, float* dy) {
+  constexpr int NQP = qcount<G, R0, R1>(), NCH = C / QCH;
+  static_assert(NCH % 2 == 0, "every pass starts in buffer 0");
   const int lane = threadIdx.x & 31;
-  float2 Q[NQG];
+  float2 Q[NQP];
 #pragma unroll
-  for (int i = 0; i < NQG; ++i) Q[i] = make_float2(0.f, 0.f);
+  for (int i = 0; i < NQP; ++i) Q[i] = make_float2(0.f, 0.f);
 #pragma unroll 1
   for (int cc = 0; cc < NCH; ++cc) {
     float4* cur = bufs + (cc & 1) * QBUF_F4;
     float4* nxt = bufs + ((cc + 1) & 1) * QBUF_F4;
     if (cc + 1 < NCH) {
-      q_stage<G, C>(nxt, zlist, x, src_row, dzn, cc + 1, lane);
+      q_stage<G, R0, R1, C>(nxt, zlist, x, src_row, dzn, cc + 1, lane);
       cp_async_wait<1>();
-    } else if (G < 2) {
-      q_stage<(G < 2 ? G + 1 : 2), C>(nxt, zlist, x, src_row, dzn, 0, lane);
+    } else if constexpr (NG >= 0) {
+      q_stage<NG, NR0, NR1, C>(nxt, zlist, x, src_row, dzn, 0, lane);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
@@ -407,20 +421,20 @@ __device__ __forceinline__ void q_group(float4* __restrict__ bufs, const int* __
     const float4* zb = cur + 32 * QES;
 #pragma unroll 1
     for (int c4 = 0; c4 < QCH / 4; ++c4) {
-      float4 xv[M1];
+      float4 xv[R1 - R0];
 #pragma unroll
-      for (int m1 = 0; m1 < M1; ++m1) xv[m1] = cur[lane * QES + 4 * m1 + c4];
+      for (int m1 = R0; m1 < R1; ++m1) xv[m1 - R0] = cur[lane * QES + 4 * (m1 - R0) + c4];
 #pragma unroll
       for (int p = P_LO(G); p < P_HI(G); ++p)
 #pragma unroll
         for (int kk = 0; kk < 2 * L3(p) + 1; ++kk) {
           const float4 d = zb[4 * zlocal(p, kk) + c4];
 #pragma unroll
-          for (int m1 = 0; m1 < M1; ++m1) {
-            float2 acc = Q[qidx(p, m1, kk) - Q0];
-            acc = ffma2(xv[m1].x, xv[m1].y, d.x, d.y, acc);
-            acc = ffma2(xv[m1].z, xv[m1].w, d.z, d.w, acc);
-            Q[qidx(p, m1, kk) - Q0] = acc;
+          for (int m1 = R0; m1 < R1; ++m1) {
+            float2 acc = Q[qloc<G, R0, R1>(p, m1, kk)];
+            acc = ffma2(xv[m1 - R0].x, xv[m1 - R0].y, d.x, d.y, acc);
+            acc = ffma2(xv[m1 - R0].z, xv[m1 - R0].w, d.z, d.w, acc);
+            Q[qloc<G, R0, R1>(p, m1, kk)] = acc;
           }
         }
     }
@@ -436,11 +450,12 @@ __device__ __forceinline__ void q_group(float4* __restrict__ bufs, const int* __
 #pragma unroll
   for (int p = P_LO(G); p < P_HI(G); ++p)
 #pragma unroll
-    for (int m1 = 0; m1 < M1; ++m1)
+    for (int m1 = R0; m1 < R1; ++m1)
 #pragma unroll
       for (int kk = 0; kk < 2 * L3(p) + 1; ++kk) {
         const int q = qidx(p, m1, kk);
-        const float Qv = Q[q - Q0].x + Q[q - Q0].y;
+        const float2 qq = Q[qloc<G, R0, R1>(p, m1, kk)];
+        const float Qv = qq.x + qq.y;
         float y0 = 0.f;
 #pragma unroll
         for (int m2 = 0; m2 < 2 * L2(p) + 1; ++m2) y0 = fmaf(cg2[5 * q + m2], Y[KB(L2(p)) + m2], y0);
@@ -453,7 +468,7 @@ __device__ __forceinline__ void q_group(float4* __restrict__ bufs, const int* __
 }
 
 template <int CPL>
-__global__ void __launch_bounds__(CONV_WARPS * 32, 2) conv2_q_kernel(ConvArgs a, const float* __restrict__ x,
+__global__ void __launch_bounds__(CONV_WARPS * 32, 3) conv2_q_kernel(ConvArgs a, const float* __restrict__ x,
                                                                      const float* __restrict__ dZ,
                                                                      float* __restrict__ dgates,
                                                                      float* __restrict__ dY) {
@@ -491,10 +506,11 @@ __global__ void __launch_bounds__(CONV_WARPS * 32, 2) conv2_q_kernel(ConvArgs a,
       for (int k = 0; k < NK; ++k) dy[k] = 0.f;
 #pragma unroll
       for (int p = 0; p < NP; ++p) dg[p] = 0.f;
-      q_stage<0, C>(bufs, zlist, x, src_row, dzn, 0, lane);
-      q_group<0, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
-      q_group<1, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
-      q_group<2, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
+      q_stage<0, 0, 1, C>(bufs, zlist, x, src_row, dzn, 0, lane);
+      q_pass<0, 0, 1, 1, 0, 3, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
+      q_pass<1, 0, 3, 2, 0, 3, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
+      q_pass<2, 0, 3, 2, 3, 5, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
+      q_pass<2, 3, 5, -1, 0, 0, C>(bufs, zlist, x, src_row, dzn, cg2, ey4, eg4, dg, dy);
       if (!active) continue;
       float4* dgo = reinterpret_cast<float4*>(dgates + 12 * (int64_t)e);
       dgo[0] = make_float4(dg[0], dg[1], dg[2], dg[3]);
