@@ -215,39 +215,51 @@ class HaloPlan:
     ghost_species: torch.Tensor     # (G,)
 
 
-def select_ghosts(dec: Decomposition, rank: int, pos: torch.Tensor, bboxes: torch.Tensor):
+def select_ghosts(dec: Decomposition, rank: int, pos: torch.Tensor, bboxes: torch.Tensor, chunk: int = 1 << 18):
     """Rows this rank sends: (send_idx, send_image, send_counts) grouped by destination rank.
 
     ``bboxes`` (world, 2, 3) are the owned-atom bounding boxes of all ranks; an image
     x + S.cell is sent to rank d if it lies inside d's box grown by the halo along every split
     axis (the unsplit axes are periodic in d's local system), except the atom itself
-    (S = 0) for its own rank."""
+    (S = 0) for its own rank.  Rows are ordered by destination, then image, then atom.
+
+    The owned boxes are disjoint blocks along every split axis, so only an atom within one halo
+    of its own box's faces along a split axis can lie in another rank's grown box in any image:
+    those candidates (one host synchronisation) are tested against all images and ranks at once
+    (a second one), in chunks that bound the temporaries."""
     dev = pos.device
+    world = bboxes.shape[0]
+    images = dec.images()
+    if pos.shape[0] == 0:
+        z = torch.zeros(0, dtype=torch.int64, device=dev)
+        return z, z, [0] * world
     cell = torch.tensor(dec.cell, dtype=torch.float64, device=dev)
     split = torch.tensor(dec.split, device=dev)
     lo = bboxes[:, 0, :] - dec.halo
     hi = bboxes[:, 1, :] + dec.halo
-    rows_d, rows_i, rows_s = [], [], []
-    for si, S in enumerate(dec.images()):
-        shift = torch.tensor(S, dtype=torch.float64, device=dev) @ cell
-        x = pos + shift
-        inside = ((x[:, None, :] >= lo[None]) & (x[:, None, :] <= hi[None])) | ~split[None, None, :]
-        inside = inside.all(-1)                       # (n, world)
-        if S == (0, 0, 0):
-            inside[:, rank] = False
-        nz = inside.nonzero()
-        if nz.numel():
-            rows_i.append(nz[:, 0])
-            rows_d.append(nz[:, 1])
-            rows_s.append(torch.full_like(nz[:, 0], si))
-    world = bboxes.shape[0]
+    margin = dec.halo * (1.0 + 1e-9) + 1e-9
+    near = ((pos - bboxes[rank, 0]) <= margin) | ((bboxes[rank, 1] - pos) <= margin)
+    cand = (near & split).any(1).nonzero().squeeze(1)
+    shifts = torch.tensor(images, dtype=torch.float64, device=dev) @ cell          # (I, 3)
+    zero = images.index((0, 0, 0))
+    rows_s, rows_i, rows_d = [], [], []
+    for c0 in range(0, cand.shape[0], chunk):
+        cc = cand[c0:c0 + chunk]
+        x = pos[cc][None, :, :] + shifts[:, None, :]                               # (I, nc, 3)
+        inside = ((x[:, :, None, :] >= lo[None, None]) & (x[:, :, None, :] <= hi[None, None])) | ~split
+        inside = inside.all(-1)                                                    # (I, nc, world)
+        inside[zero, :, rank] = False
+        nz = inside.nonzero()                                                      # (image, atom, rank)
+        rows_s.append(nz[:, 0])
+        rows_i.append(cc[nz[:, 1]])
+        rows_d.append(nz[:, 2])
     if not rows_d:
         z = torch.zeros(0, dtype=torch.int64, device=dev)
         return z, z, [0] * world
     d = torch.cat(rows_d)
     i = torch.cat(rows_i)
     s = torch.cat(rows_s)
-    order = torch.sort(d * (len(dec.images()) + 1) + s, stable=True).indices
+    order = torch.sort((d * (len(images) + 1) + s) * (pos.shape[0] + 1) + i, stable=True).indices
     d, i, s = d[order], i[order], s[order]
     counts = torch.bincount(d, minlength=world).tolist()
     return i, s, counts
@@ -375,7 +387,7 @@ def layer_exchange_step(dec: Decomposition, rank: int, pos: torch.Tensor, specie
     spec_l = torch.cat([species, plan.ghost_species.to(species.dtype)])
     n_all = int(pos_l.shape[0])
     cell_t = torch.as_tensor(dec.cell, dtype=torch.float64, device=dev).reshape(1, 3, 3)
-    g = owned_receiver_graph(build_graph(pos_l, cell_t, cutoff, pbc=dec.local_pbc), n)
+    g = owned_receiver_graph(build_graph(pos_l, cell_t, cutoff, pbc=dec.local_pbc, transpose=False), n)
     batch = torch.zeros(n_all, dtype=torch.int32, device=dev)
     if isinstance(engine, SparseEngine):
         counts = torch.stack([g.row_ptr[n].to(torch.float64),

@@ -29,8 +29,10 @@ def _sidx_to_shift(sidx: torch.Tensor) -> torch.Tensor:
 
 
 def build_graph(pos: torch.Tensor, cell: torch.Tensor, cutoff: float, frame_ptr: Sequence[int] = None,
-                pbc=(True, True, True), max_num_neighbors: int = None) -> GraphCSR:
-    """pos (N,3) and cell (F,3,3) on the GPU (float64 used for the distance test)."""
+                pbc=(True, True, True), max_num_neighbors: int = None, transpose: bool = True) -> GraphCSR:
+    """pos (N,3) and cell (F,3,3) on the GPU (float64 used for the distance test).  With
+    ``transpose=False`` the transpose CSR is left out (``tr_ptr`` / ``tr_eid`` None), for a caller
+    that restricts the graph first."""
     dev = pos.device
     pos64 = pos.detach().to(torch.float64).contiguous()
     cell64 = cell.detach().to(device=dev, dtype=torch.float64).reshape(-1, 3, 3).contiguous()
@@ -60,9 +62,11 @@ def build_graph(pos: torch.Tensor, cell: torch.Tensor, cutoff: float, frame_ptr:
                                 pbc_h.ctypes.data_as(N.P), float(cutoff), N.ptr(row_ptr), N.ptr(src), N.ptr(sidx), E,
                                 N.ptr(ws), ws.numel(), st), "fsc_neighbor_fill")
     src, sidx = src[:E], sidx[:E]
-    tr_ptr, tr_eid = GraphCSR.transpose(row_ptr, src, n)
+    tr_ptr = tr_eid = None
     if max_num_neighbors is not None:
-        row_ptr, src, sidx = _cap(row_ptr, src, sidx, tr_ptr, tr_eid, n, int(max_num_neighbors))
+        t_ptr, t_eid = GraphCSR.transpose(row_ptr, src, n)
+        row_ptr, src, sidx = _cap(row_ptr, src, sidx, t_ptr, t_eid, n, int(max_num_neighbors))
+    if transpose:
         tr_ptr, tr_eid = GraphCSR.transpose(row_ptr, src, n)
     shift = _sidx_to_shift(sidx).to(torch.float32).contiguous()
     g = GraphCSR(n, row_ptr, src, shift, tr_ptr, tr_eid)

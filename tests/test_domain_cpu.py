@@ -334,3 +334,43 @@ def test_gloo_ghost_row_exchange():
     import torch.multiprocessing as mp
 
     mp.spawn(_gloo_exchange_rank, args=(2, _free_port(), (2, 1, 1)), nprocs=2, join=True)
+
+
+def _select_ghosts_brute(dec, rank, pos, bboxes):
+    """Every owned atom, every image, every rank: the definition the vectorised selection follows."""
+    cell = torch.tensor(dec.cell, dtype=torch.float64)
+    split = torch.tensor(dec.split)
+    lo, hi = bboxes[:, 0, :] - dec.halo, bboxes[:, 1, :] + dec.halo
+    rows = []
+    for si, S in enumerate(dec.images()):
+        x = pos + torch.tensor(S, dtype=torch.float64) @ cell
+        inside = (((x[:, None, :] >= lo[None]) & (x[:, None, :] <= hi[None])) | ~split[None, None, :]).all(-1)
+        if S == (0, 0, 0):
+            inside[:, rank] = False
+        for i, d in inside.nonzero().tolist():
+            rows.append((d, si, i))
+    rows.sort()
+    counts = [sum(1 for r in rows if r[0] == d) for d in range(bboxes.shape[0])]
+    return [r[2] for r in rows], [r[1] for r in rows], counts
+
+
+@pytest.mark.parametrize("dims", [(2, 1, 1), (2, 2, 1), (2, 2, 2), (3, 1, 2)])
+def test_vectorised_ghost_selection_matches_definition(dims):
+    s = systems.diamond_crystal(n_cells=(6, 6, 6), seed=17)
+    cell = s["cell"][0]
+    dec = D.Decomposition(cell, dims, 5.0)
+    pos = torch.tensor(s["pos"])
+    frac = s["pos"] @ np.linalg.inv(cell)
+    frac -= np.floor(frac)
+    owner = np.zeros(len(frac), dtype=np.int64)
+    for k in range(3):
+        owner = owner * dims[k] + np.floor(frac[:, k] * dims[k]).astype(np.int64)
+    owned = [np.nonzero(owner == r)[0] for r in range(dec.world)]
+    # the rank numbering of block_of: check the owned blocks against it, then build the boxes
+    bb = torch.stack([torch.stack([pos[o].min(0).values, pos[o].max(0).values]) for o in owned])
+    for r in range(dec.world):
+        p = pos[owned[r]]
+        got_i, got_s, got_c = D.select_ghosts(dec, r, p, bb, chunk=37)
+        ref_i, ref_s, ref_c = _select_ghosts_brute(dec, r, p, bb)
+        assert got_c == ref_c
+        assert got_i.tolist() == ref_i and got_s.tolist() == ref_s
