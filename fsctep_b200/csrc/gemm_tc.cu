@@ -45,7 +45,9 @@ struct GCfg {
   static constexpr bool FLUSH = NT <= 128;
   static constexpr int GC = PRECISE ? 1 : 2;
   static constexpr int NACC = FLUSH ? 2 : 2;
-  static constexpr int NST = 2;
+  // shared-memory ring depth: NT = 128 runs one CTA per SM and has room for a third stage;
+  // NT = 64 keeps two stages so that two CTAs share an SM
+  static constexpr int NST = NT == 128 ? 3 : 2;
   static constexpr uint32_t BBYTES = 2u * KC * NT * 4u;  // hi + lo planes of one chunk
   static constexpr uint32_t ALO_OFF = NST * ABYTES;
   static constexpr uint32_t B_OFF = 2 * NST * ABYTES;
