@@ -312,6 +312,238 @@ __global__ void __launch_bounds__(GT_THREADS) gemm_tc_kernel(const __grid_consta
   }
 }
 
+// ------------------------------------------------------------------ streaming, A split into TMEM
+// The same product for NT <= 128 with the A operand in tensor memory: the math warps read the
+// staged A tile (thread = tile row = TMEM lane; the 128-byte swizzle is undone by XOR-ing the
+// 16-byte chunk index with the row), split it into tf32 hi / lo straight into one of NAB TMEM
+// A buffers (64 columns each), and the MMAs read A from TMEM and B from shared memory.  No hi / lo
+// copy of A is written back to shared memory, so a stage holds only the raw A tile and the B
+// chunk: four stages for NT = 128 (one CTA per SM, all 512 TMEM columns), three for NT = 64 (two
+// CTAs per SM, 256 columns each).  Accumulation as in gemm_tc_kernel (FLUSH groups of GC chunks).
+template <int NT, bool PRECISE = false>
+struct GmCfg {
+  static_assert(NT == 64 || NT == 128, "A-in-TMEM tiles");
+  static constexpr int GC = PRECISE ? 1 : 2;
+  static constexpr int NST = NT == 128 ? 4 : 3;
+  static constexpr int NAB = NT == 128 ? 4 : 2;
+  static constexpr uint32_t TCOLS = NT == 128 ? 512 : 256;
+  static constexpr uint32_t ACOL = 2 * NT;                 // A buffers after the two D slots
+  static constexpr uint32_t BBYTES = 2u * KC * NT * 4u;
+  static constexpr uint32_t B_OFF = NST * ABYTES;
+  static constexpr uint32_t BAR_OFF = B_OFF + NST * BBYTES;
+  static constexpr uint32_t TOTAL = BAR_OFF + 256 + 1024;  // + slack for 1024-byte alignment
+};
+static_assert(GmCfg<128>::ACOL + 64 * GmCfg<128>::NAB <= GmCfg<128>::TCOLS, "TMEM plan");
+static_assert(GmCfg<64>::ACOL + 64 * GmCfg<64>::NAB <= GmCfg<64>::TCOLS, "TMEM plan");
+static_assert(GmCfg<128>::TOTAL <= 227u * 1024u && GmCfg<128>::TOTAL > 114u * 1024u, "one CTA per SM at NT = 128");
+static_assert(2u * (GmCfg<64>::TOTAL + 1024u) <= 228u * 1024u, "two CTAs per SM at NT = 64");
+static_assert(2 * GmCfg<64, true>::NST + 2 * GmCfg<64, true>::NAB + 5 <= 31, "barrier space");
+
+template <int NT, bool PRECISE>
+__global__ void __launch_bounds__(GT_THREADS) gemm_tcm_kernel(const __grid_constant__ CUtensorMap tmA, GemmTcArgs a) {
+  using CF = GmCfg<NT, PRECISE>;
+  constexpr int NST = CF::NST, NAB = CF::NAB, GC = CF::GC;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + CF::B_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + CF::BAR_OFF);
+  uint64_t* full = bars;                         // [NST] TMA + bulk bytes landed
+  uint64_t* empty = bars + NST;                  // [NST] MMAs done with the stage
+  uint64_t* a_ready = bars + 2 * NST;            // [NAB] math warps split the chunk into the buffer
+  uint64_t* a_free = bars + 2 * NST + NAB;       // [NAB] MMAs done with the buffer
+  uint64_t* d_ready = bars + 2 * NST + 2 * NAB;  // all MMAs done
+  uint64_t* grp_full = d_ready + 1;              // [2] a group's MMAs done
+  uint64_t* grp_empty = d_ready + 3;             // [2] math warps read the slot
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_ready + 5);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nchunks = (a.K + KC - 1) / KC;  // a K tail reads TMA zero fill and zero image rows
+  const int64_t g0 = (int64_t)blockIdx.x * a.Gb;
+
+  if (warp == 4) {
+    tc::tmem_alloc(tmem_slot, CF::TCOLS);
+    tc::tmem_relinquish();
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NST; ++i) {
+      tc::mbar_init(full + i, 1);
+      tc::mbar_init(empty + i, 1);
+    }
+    for (int i = 0; i < NAB; ++i) {
+      tc::mbar_init(a_ready + i, 4);
+      tc::mbar_init(a_free + i, 1);
+    }
+    tc::mbar_init(d_ready, 1);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(grp_full + i, 1);
+      tc::mbar_init(grp_empty + i, 4);
+    }
+    tc::fence_mbar_init();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const int ngroups = (nchunks + GC - 1) / GC;
+
+  if (warp < 4) {
+    // ---------------- split the staged A rows into TMEM (thread = row = lane), flush groups
+    bool ok = true;
+    const int t = warp * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    float sum[NT];
+#pragma unroll
+    for (int i = 0; i < NT; ++i) sum[i] = 0.f;
+    auto flush = [&](int g) {  // add group g's slot to the fp32 sums and free it
+      const int slot = g & 1;
+      if (!(ok = tc::mbar_wait(grp_full + slot, (g >> 1) & 1, a.err, 86))) return;
+      tc::tc_fence_after();
+#pragma unroll
+      for (int cb = 0; cb < NT / 16; ++cb) {
+        uint32_t u[16];
+        tc::tmem_ld16(tbase + (uint32_t)(slot * NT) + lane_off + 16u * cb, u);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sum[16 * cb + i] += __uint_as_float(u[i]);
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(grp_empty + slot);
+    };
+    for (int c = 0; c < nchunks && ok; ++c) {
+      const int st = c % NST, ab = c % NAB;
+      if (!(ok = tc::mbar_wait(full + st, (c / NST) & 1, a.err, 81))) break;
+      if (c >= NAB && !(ok = tc::mbar_wait(a_free + ab, ((c / NAB) - 1) & 1, a.err, 88))) break;
+      const uint8_t* row = sA + st * ABYTES + t * 128;
+      const uint32_t tA = tbase + CF::ACOL + 64u * (uint32_t)ab + lane_off;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int j = 4 * h + q;  // 16-byte chunk of the 128-byte row (4 K values)
+          const float4 v = *reinterpret_cast<const float4*>(row + ((j ^ (t & 7)) << 4));
+          tc::split_tf32(v.x, hi[4 * q], lo[4 * q]);
+          tc::split_tf32(v.y, hi[4 * q + 1], lo[4 * q + 1]);
+          tc::split_tf32(v.z, hi[4 * q + 2], lo[4 * q + 2]);
+          tc::split_tf32(v.w, hi[4 * q + 3], lo[4 * q + 3]);
+        }
+        tc::tmem_st16(tA + 16u * h, hi);
+        tc::tmem_st16(tA + 32u + 16u * h, lo);
+      }
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(a_ready + ab);
+      if ((c % GC == GC - 1 || c == nchunks - 1) && c / GC >= 1) flush(c / GC - 1);
+    }
+    if (ok) flush(ngroups - 1);
+    // ---------------- epilogue: thread = tile row = TMEM lane
+    if (ok) ok = tc::mbar_wait(d_ready, 0, a.err, 82);
+    tc::tc_fence_after();
+    const int64_t g = g0 + t / a.R;
+    const int r = t % a.R;
+    const bool valid = ok && t < a.R * a.Gb && g < a.G;
+    float scale = a.alpha != 0.f ? a.alpha : 1.f;
+    if (valid && a.deg_rowptr) {
+      const int d = a.deg_rowptr[g + 1] - a.deg_rowptr[g];
+      scale *= 1.f / (float)(d > 1 ? d : 1);
+    }
+    float* crow = valid ? a.C + g * a.c_gs + r * a.c_rs : nullptr;
+    const int n0 = blockIdx.y * NT;
+#pragma unroll
+    for (int cb = 0; cb < NT / 16; ++cb) {
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = sum[16 * cb + i];
+      const int nc = n0 + 16 * cb;
+      if (crow && nc < a.N) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          v[i] *= scale;
+          if (a.bias && nc + i < a.N) v[i] += a.bias[nc + i];
+        }
+        float* cp = crow + nc;
+        if (nc + 16 <= a.N && (reinterpret_cast<uintptr_t>(cp) & 15) == 0) {
+          float4* c4 = reinterpret_cast<float4*>(cp);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float4 o = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            if (a.accumulate) {
+              const float4 p = c4[i];
+              o.x += p.x;
+              o.y += p.y;
+              o.z += p.z;
+              o.w += p.w;
+            }
+            c4[i] = o;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (nc + i < a.N) cp[i] = a.accumulate ? cp[i] + v[i] : v[i];
+        }
+      }
+    }
+  } else if (warp == 4) {
+    // ---------------- producer
+    if (lane == 0) {
+      const uint8_t* bsrc = reinterpret_cast<const uint8_t*>(a.bimg) + (size_t)blockIdx.y * nchunks * CF::BBYTES;
+      for (int c = 0; c < nchunks; ++c) {
+        const int st = c % NST;
+        if (c >= NST && !tc::mbar_wait(empty + st, ((c / NST) - 1) & 1, a.err, 83)) break;
+        tc::mbar_arrive_expect_tx(full + st, a.abox + CF::BBYTES);
+        tma_load_3d(sA + st * ABYTES, &tmA, c * KC, 0, (int)g0, full + st);
+        tc::bulk_g2s(sB + st * CF::BBYTES, bsrc + (size_t)c * CF::BBYTES, CF::BBYTES, full + st);
+      }
+    }
+  } else {
+    // ---------------- MMA issuer: A from TMEM, B from shared memory
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_tf32(MT, NT);
+      const uint32_t b0 = tc::smem_u32(sB);
+      bool ok = true;
+      for (int c = 0; c < nchunks; ++c) {
+        const int st = c % NST, ab = c % NAB;
+        if (!(ok = tc::mbar_wait(a_ready + ab, (c / NAB) & 1, a.err, 84))) break;
+        const int g = c / GC;
+        const bool first = c % GC == 0;
+        if (first && g >= 2 && !(ok = tc::mbar_wait(grp_empty + (g & 1), ((g >> 1) - 1) & 1, a.err, 87))) break;
+        tc::tc_fence_after();
+        const uint32_t d = tbase + (uint32_t)((g & 1) * NT);
+        const uint32_t tA = tbase + CF::ACOL + 64u * (uint32_t)ab;
+#pragma unroll
+        for (int j = 0; j < KC / 8; ++j) {  // small products first
+          const uint32_t bh_addr = b0 + st * CF::BBYTES + j * 2 * 16 * NT;
+          const uint64_t bh = tc::smem_desc_kmajor(bh_addr, 16 * NT, 128);
+          const uint64_t bl = tc::smem_desc_kmajor(bh_addr + CF::BBYTES / 2, 16 * NT, 128);
+          tc::mma_tf32_ts(d, tA + 8u * j, bl, idesc, (!first || j > 0) ? 1u : 0u);
+          tc::mma_tf32_ts(d, tA + 32u + 8u * j, bh, idesc, 1u);
+        }
+#pragma unroll
+        for (int j = 0; j < KC / 8; ++j) {
+          const uint64_t bh = tc::smem_desc_kmajor(b0 + st * CF::BBYTES + j * 2 * 16 * NT, 16 * NT, 128);
+          tc::mma_tf32_ts(d, tA + 8u * j, bh, idesc, 1u);
+        }
+        tc::mma_commit(empty + st);
+        tc::mma_commit(a_free + ab);
+        if (c % GC == GC - 1 || c == nchunks - 1) tc::mma_commit(grp_full + (g & 1));
+      }
+      tc::mma_commit(d_ready);  // also when a wait failed: whatever was issued completes first
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    // the MMA warp commits d_ready on every path: wait (bounded) until no MMA still writes TMEM
+    if (lane == 0) tc::mbar_wait(d_ready, 0, a.err, 85);
+    __syncwarp();
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tbase, CF::TCOLS);
+  }
+}
+
 // ------------------------------------------------------------------ persistent, B resident
 // For short K and N <= 256 (the dZ channel mix and the MainNet layers here) the whole B image
 // fits in shared memory: one CTA per SM loads it once and walks row tiles.  Roles: producer warp (B once,
@@ -585,11 +817,18 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 template <int NT, bool PRECISE>
 int launch_nt(const GemmArgs& g, const CUtensorMap& map, GemmTcArgs t, cudaStream_t st) {
-  const int sm = (int)GCfg<NT, PRECISE>::TOTAL;
-  cudaFuncSetAttribute(gemm_tc_kernel<NT, PRECISE>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
   dim3 grid((unsigned)ceil_div(g.G, (int64_t)t.Gb), (unsigned)ceil_div(g.N, NT));
-  gemm_tc_kernel<NT, PRECISE><<<grid, GT_THREADS, sm, st>>>(map, t);
-  return check_launch("gemm_tc_kernel");
+  if constexpr (NT <= 128) {  // A split into TMEM
+    const int sm = (int)GmCfg<NT, PRECISE>::TOTAL;
+    cudaFuncSetAttribute(gemm_tcm_kernel<NT, PRECISE>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    gemm_tcm_kernel<NT, PRECISE><<<grid, GT_THREADS, sm, st>>>(map, t);
+    return check_launch("gemm_tcm_kernel");
+  } else {
+    const int sm = (int)GCfg<NT, PRECISE>::TOTAL;
+    cudaFuncSetAttribute(gemm_tc_kernel<NT, PRECISE>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    gemm_tc_kernel<NT, PRECISE><<<grid, GT_THREADS, sm, st>>>(map, t);
+    return check_launch("gemm_tc_kernel");
+  }
 }
 
 // The persistent kernel holds B (whole K) in shared memory and keeps every chunk group at <= 2
