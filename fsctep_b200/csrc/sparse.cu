@@ -1198,43 +1198,156 @@ struct RdArgs {
 };
 
 // Gp[nl][j] = sum_m t_L[c][m] t_L[d][m], (c, d) = pairs[j]; grid (pair blocks, nodes)
-__global__ void gram_pack_kernel(RdArgs a, int L, int64_t n0, int64_t nn, const int32_t* __restrict__ pairs,
-                                 int64_t npairs, float* __restrict__ Gp) {
-  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t nl = blockIdx.y;
-  if (j >= npairs || nl >= nn) return;
+// Gram operand of one node for Lout = L (M = 3^L components): Gp[n][j(c, d)] = sum_m t[c][m] t[d][m]
+// over the packed upper triangle c <= d of the nC = C * nint concatenated channels, pair j(c, d) =
+// c nC - c (c - 1) / 2 + d - c (the order of the W_read image).  One CTA per node holds the node's
+// t as [M][nC] in shared memory; each warp walks triangle rows c, its lanes taking aligned quads
+// d4 .. d4 + 3 (one float4 read per component), and a row's results leave through a per-warp
+// staging buffer as coalesced runs.
+template <int M>
+__global__ void __launch_bounds__(256) gram_pack_kernel(RdArgs a, int L, int64_t n0, int64_t nn, int64_t npairs,
+                                                        float* __restrict__ Gp) {
+  extern __shared__ float4 gp_smem4[];
+  float* ts = reinterpret_cast<float*>(gp_smem4);  // [M][nC], then [8 warps][128] staging
+  const int nC = a.C * a.nint;
+  const int64_t nl = blockIdx.x;
   const int64_t n = n0 + nl;
-  const int32_t pr = pairs[j];
-  const int cp = pr & 0xffff, dp = pr >> 16;
-  const int kc = cp / a.C, c = cp - kc * a.C, kd = dp / a.C, d = dp - kd * a.C;
-  const float* fc = a.feats[kc] + (n * a.R + roff(L)) * a.C + c;
-  const float* fd = a.feats[kd] + (n * a.R + roff(L)) * a.C + d;
-  float acc = 0.f;
-  for (int m = 0; m < pow3(L); ++m) acc = fmaf(fc[m * a.C], fd[m * a.C], acc);
-  Gp[nl * npairs + j] = acc;
+  for (int i = threadIdx.x; i < M * nC; i += blockDim.x) {
+    const int m = i / nC, cp = i - m * nC, k = cp / a.C, c = cp - k * a.C;
+    ts[i] = a.feats[k][(n * a.R + roff(L) + m) * a.C + c];
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  float* stage = ts + M * nC + warp * 128;
+  float* gout = Gp + nl * npairs;
+  for (int c = warp; c < nC; c += nw) {
+    const int64_t j0 = (int64_t)c * nC - (int64_t)c * (c - 1) / 2 - c;  // pair index of (c, d) = j0 + d
+    float tc[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) tc[m] = ts[m * nC + c];
+    for (int base = c & ~3; base < nC; base += 128) {
+      const int d4 = base + 4 * lane;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (d4 < nC) {
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          const float4 t4 = reinterpret_cast<const float4*>(ts + m * nC)[d4 >> 2];
+          acc.x = fmaf(tc[m], t4.x, acc.x);
+          acc.y = fmaf(tc[m], t4.y, acc.y);
+          acc.z = fmaf(tc[m], t4.z, acc.z);
+          acc.w = fmaf(tc[m], t4.w, acc.w);
+        }
+      }
+      reinterpret_cast<float4*>(stage)[lane] = acc;
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int d = base + lane + 32 * i;
+        if (d >= c && d < nC) gout[j0 + d] = stage[lane + 32 * i];
+      }
+      __syncwarp();
+    }
+  }
 }
 
-// grads at t_L[c'][m] += 2 sum_d H[n][c'][d] t_L[d][m]; grid (channel blocks, nodes).  H is
-// symmetric (ds times the symmetrised W_read), so H[n][d][c'] is read: coalesced over c'.
-__global__ void gram_apply_kernel(RdArgs a, GradList g, int L, int64_t n0, int64_t nn, const float* __restrict__ H) {
+// grads at t_L[c'][m] += 2 sum_d H[n][c'][d] t_L[d][m]; one CTA per node, two channels c' per
+// thread.  t is held as [nC][M] in shared memory (a row of M values read as float4 broadcasts); H
+// is symmetric (ds times the symmetrised W_read), so H[n][d][c'] is read: coalesced over c'.
+template <int M>
+__global__ void __launch_bounds__(192) gram_apply_kernel(RdArgs a, GradList g, int L, int64_t n0, int64_t nn,
+                                                         const float* __restrict__ H) {
+  constexpr int MP = (M + 3) / 4 * 4;
+  extern __shared__ float4 ga_smem4[];
+  float* ts = reinterpret_cast<float*>(ga_smem4);  // [nC][MP]
   const int nC = a.C * a.nint;
-  const int cp = blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t nl = blockIdx.y;
-  if (cp >= nC || nl >= nn) return;
+  const int64_t nl = blockIdx.x;
   const int64_t n = n0 + nl;
-  const int M = pow3(L);
-  const float* h = H + nl * (int64_t)nC * nC + cp;
-  float acc[27];
-  for (int m = 0; m < M; ++m) acc[m] = 0.f;
-  for (int d = 0; d < nC; ++d) {
-    const float hv = h[(int64_t)d * nC];
-    const int kd = d / a.C, dd = d - kd * a.C;
-    const float* fd = a.feats[kd] + (n * a.R + roff(L)) * a.C + dd;
-    for (int m = 0; m < M; ++m) acc[m] = fmaf(hv, fd[m * a.C], acc[m]);
+  for (int i = threadIdx.x; i < nC * MP; i += blockDim.x) {
+    const int d = i / MP, m = i - d * MP, k = d / a.C, dd = d - k * a.C;
+    ts[i] = m < M ? a.feats[k][(n * a.R + roff(L) + m) * a.C + dd] : 0.f;
   }
-  const int kc = cp / a.C, c = cp - kc * a.C;
-  float* gp = g.p[kc] + (n * a.R + roff(L)) * a.C + c;
-  for (int m = 0; m < M; ++m) gp[m * a.C] += 2.f * acc[m];
+  __syncthreads();
+  const int half = (nC + 1) / 2;
+  const int c0 = threadIdx.x, c1 = threadIdx.x + half;
+  const bool v0 = c0 < half, v1 = c1 < nC && v0;
+  float acc0[MP], acc1[MP];
+#pragma unroll
+  for (int m = 0; m < MP; ++m) acc0[m] = acc1[m] = 0.f;
+  const float* h = H + nl * (int64_t)nC * nC;
+  if (v0) {
+    for (int d = 0; d < nC; ++d) {
+      const float h0 = h[(int64_t)d * nC + c0];
+      const float h1 = v1 ? h[(int64_t)d * nC + c1] : 0.f;
+      const float4* t4 = reinterpret_cast<const float4*>(ts + d * MP);
+#pragma unroll
+      for (int q = 0; q < MP / 4; ++q) {
+        const float4 t = t4[q];
+        acc0[4 * q] = fmaf(h0, t.x, acc0[4 * q]);
+        acc0[4 * q + 1] = fmaf(h0, t.y, acc0[4 * q + 1]);
+        acc0[4 * q + 2] = fmaf(h0, t.z, acc0[4 * q + 2]);
+        acc0[4 * q + 3] = fmaf(h0, t.w, acc0[4 * q + 3]);
+        acc1[4 * q] = fmaf(h1, t.x, acc1[4 * q]);
+        acc1[4 * q + 1] = fmaf(h1, t.y, acc1[4 * q + 1]);
+        acc1[4 * q + 2] = fmaf(h1, t.z, acc1[4 * q + 2]);
+        acc1[4 * q + 3] = fmaf(h1, t.w, acc1[4 * q + 3]);
+      }
+    }
+  }
+  if (v0) {
+    const int k = c0 / a.C, c = c0 - k * a.C;
+    float* gp = g.p[k] + (n * a.R + roff(L)) * a.C + c;
+#pragma unroll
+    for (int m = 0; m < M; ++m) gp[m * a.C] += 2.f * acc0[m];
+  }
+  if (v1) {
+    const int k = c1 / a.C, c = c1 - k * a.C;
+    float* gp = g.p[k] + (n * a.R + roff(L)) * a.C + c;
+#pragma unroll
+    for (int m = 0; m < M; ++m) gp[m * a.C] += 2.f * acc1[m];
+  }
+}
+
+int launch_gram_pack(const RdArgs& a, int L, int nC, int64_t n0, int64_t nn, int64_t npairs, float* Gp,
+                     cudaStream_t st) {
+  if (nn <= 0) return FSC_OK;
+  const int M = pow3(L);
+  const size_t smem = sizeof(float) * ((size_t)M * nC + 8 * 128);
+  if (nC % 4 || smem > 227u * 1024u) return fail(FSC_ERR_UNSUPPORTED, "sparse gram_pack: channel count");
+  auto go = [&](auto kernel) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return fail(FSC_ERR_CUDA, "sparse gram_pack: shared memory attribute");
+    kernel<<<(unsigned)nn, 256, smem, st>>>(a, L, n0, nn, npairs, Gp);
+    return check_launch("sparse gram_pack_kernel");
+  };
+  switch (L) {
+    case 0: return go(gram_pack_kernel<1>);
+    case 1: return go(gram_pack_kernel<3>);
+    case 2: return go(gram_pack_kernel<9>);
+    case 3: return go(gram_pack_kernel<27>);
+    default: return fail(FSC_ERR_UNSUPPORTED, "sparse gram_pack: lmax <= 3");
+  }
+}
+
+int launch_gram_apply(const RdArgs& a, const GradList& g, int L, int nC, int64_t n0, int64_t nn, const float* H,
+                      cudaStream_t st) {
+  if (nn <= 0) return FSC_OK;
+  const int M = pow3(L), MP = (M + 3) / 4 * 4;
+  const int threads = (int)ceil_div((nC + 1) / 2, 32) * 32;
+  const size_t smem = sizeof(float) * (size_t)nC * MP;
+  if (threads > 192 || smem > 227u * 1024u) return fail(FSC_ERR_UNSUPPORTED, "sparse gram_apply: channel count");
+  auto go = [&](auto kernel) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return fail(FSC_ERR_CUDA, "sparse gram_apply: shared memory attribute");
+    kernel<<<(unsigned)nn, threads, smem, st>>>(a, g, L, n0, nn, H);
+    return check_launch("sparse gram_apply_kernel");
+  };
+  switch (L) {
+    case 0: return go(gram_apply_kernel<1>);
+    case 1: return go(gram_apply_kernel<3>);
+    case 2: return go(gram_apply_kernel<9>);
+    case 3: return go(gram_apply_kernel<27>);
+    default: return fail(FSC_ERR_UNSUPPORTED, "sparse gram_apply: lmax <= 3");
+  }
 }
 
 // MainNet input [layer k: L = 0..lmax: C] x nint | scalars^2 (S)
@@ -1590,9 +1703,7 @@ int forward_readout(Ctx& c) {
     const float* Wp = w->wread_p + (int64_t)L * p.S * p.npairs;
     for (int64_t n0 = 0; n0 < p.N; n0 += p.gchunk) {
       const int64_t nn = std::min(p.gchunk, p.N - n0);
-      const dim3 grid((unsigned)ceil_div(p.npairs, 256), (unsigned)nn);
-      gram_pack_kernel<<<grid, 256, 0, st>>>(rd, L, n0, nn, w->pairs, p.npairs, p.gbuf);
-      FSC_TRY(check_launch("sparse gram_pack_kernel"));
+      FSC_TRY(launch_gram_pack(rd, L, p.C * p.nint, n0, nn, p.npairs, p.gbuf, st));
       GemmArgs ga = gemm(p.gbuf, p.npairs, 0, Wp, p.npairs, 1, p.scalars + n0 * p.S, p.S, 0, nn, 1, (int)p.npairs, p.S);
       ga.accumulate = 1;
       ga.precise = 1;  // K = nC (nC + 1) / 2 Gram pairs whose terms cancel heavily
@@ -1652,8 +1763,7 @@ int backward_readout(Ctx& c) {
       GemmArgs ga = gemm(p.dscalars + n0 * p.S, p.S, 0, Ws, (int64_t)p.nC * p.nC, 0, p.gbuf, (int64_t)p.nC * p.nC, 0,
                          nn, 1, p.S, p.nC * p.nC);
       FSC_TRY(run_gemm(ga, p.img_gb[L], p.err, st));
-      gram_apply_kernel<<<dim3((unsigned)ceil_div(p.nC, 128), (unsigned)nn), 128, 0, st>>>(rd, gl, L, n0, nn, p.gbuf);
-      FSC_TRY(check_launch("sparse gram_apply_kernel"));
+      FSC_TRY(launch_gram_apply(rd, gl, L, p.C * p.nint, n0, nn, p.gbuf, st));
     }
   }
   prof::mark("sparse_readout_gram_backward", st);
