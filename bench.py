@@ -301,17 +301,37 @@ def timed_steps(args, world, step):
 
 
 def stage_pass(args, world, step):
-    """Per-stage CUDA-event times from a separate, untimed pass of the same steps."""
+    """Per-stage CUDA-event times from a separate, untimed pass of the same steps.  Two extra
+    entries: ``__step__`` (each step's time, for the time outside the stage marks) and, at N > 1,
+    ``__halo__`` (each step's time inside its halo phases: the halo plan with its position
+    exchange, the per-layer feature and gradient exchanges, the reverse force exchange)."""
     from fsctep_b200 import _native as NAT
+    from fsctep_b200 import domain as D
 
     if world > 1:
         torch.distributed.barrier()
     stage_ms = {}
     NAT.profile_enable(True)
     for _ in range(args.stage_steps if args.stage_steps is not None else args.steps):
+        D.HALO_TIMER = [] if world > 1 else None
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
         step()
+        t1.record()
         for name, ms in NAT.profile_read():
             stage_ms.setdefault(name, []).append(ms)
+        torch.cuda.synchronize()
+        stage_ms.setdefault("__step__", []).append(t0.elapsed_time(t1))
+        if D.HALO_TIMER is not None:
+            marks, halo, begin = D.HALO_TIMER, 0.0, None
+            for which, ev in marks:
+                if which == "begin":
+                    begin = ev
+                elif begin is not None:
+                    halo += begin.elapsed_time(ev)
+                    begin = None
+            stage_ms.setdefault("__halo__", []).append(halo)
+        D.HALO_TIMER = None
     NAT.profile_enable(False)
     torch.cuda.synchronize()
     return stage_ms
@@ -864,6 +884,8 @@ def main():
     # dominant stage and its roofline
     stage_avg = {}
     nst = args.stage_steps if args.stage_steps is not None else args.steps
+    step_ms = res["stage_ms"].pop("__step__", None)
+    halo_ms = res["stage_ms"].pop("__halo__", None)
     for name, lst in res["stage_ms"].items():
         stage_avg[name] = (sum(lst) / nst, len(lst) / nst)
     dom = max(stage_avg, key=lambda k: stage_avg[k][0]) if stage_avg else None
@@ -912,6 +934,10 @@ def main():
             "e2e": {"value": e2e_value, "unit": "atom-steps/s", "h2d_bytes_per_step": n * 3 * 8,
                     "d2h_bytes_per_step": n * 3 * 4 + 4},
             "stages_ms": {k: round(v[0], 3) for k, v in sorted(stage_avg.items(), key=lambda kv: -kv[1][0])}}
+    if step_ms:  # time of a stage-pass step outside the engine's stage marks (neighbour list, halo work)
+        line["unstaged_ms"] = round(sum(step_ms) / len(step_ms) - sum(v[0] for v in stage_avg.values()), 3)
+    if halo_ms:
+        line["halo_ms"] = round(sum(halo_ms) / len(halo_ms), 3)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r = cpu_reference(args.workload, 3, 1)
         line["cpu_baseline"] = {k: r[k] for k in CPU_KEYS}

@@ -24,7 +24,11 @@ A step is written once, as a generator that yields its collectives as requests
 (``("all_gather", t)``, ``("all_reduce_sum", t)``, ``("all_to_all", (rows, counts, recv_counts))``);
 :func:`run_dist` serves them with ``torch.distributed`` (NCCL on GPUs, gloo on CPU; variable
 lengths through ``all_to_all_single``) and :func:`run_local` serves all ranks of a decomposition
-in one process, which is how one device tests the whole multi-rank path.
+in one process, which is how one device tests the whole multi-rank path.  The steps also yield
+``("mark", "begin" | "end")`` around their halo phases (the halo plan with its position exchange,
+the per-layer feature and gradient exchanges, the reverse force exchange): with ``HALO_TIMER``
+set to a list, :func:`run_dist` records a CUDA event at each mark into it (``halo_ms`` of
+``bench.py``); otherwise marks cost nothing.
 """
 
 from __future__ import annotations
@@ -124,6 +128,13 @@ def all_to_all(rows: torch.Tensor, counts: List[int], recv_counts: Optional[List
     return (yield ("all_to_all", (rows, list(counts), recv_counts)))
 
 
+HALO_TIMER: Optional[list] = None  # (mark, torch.cuda.Event) pairs recorded by run_dist when a list
+
+
+def halo_mark(which: str):
+    yield ("mark", which)
+
+
 def run_dist(gen):
     """Drive a step generator with torch.distributed collectives (this process = one rank)."""
     import torch.distributed as dist
@@ -135,7 +146,13 @@ def run_dist(gen):
             kind, arg = gen.send(reply)
         except StopIteration as e:
             return e.value
-        if kind == "all_gather":
+        if kind == "mark":
+            if HALO_TIMER is not None and torch.cuda.is_available():
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                HALO_TIMER.append((arg, ev))
+            reply = None
+        elif kind == "all_gather":
             out = [torch.empty_like(arg) for _ in range(world)]
             dist.all_gather(out, arg.contiguous())
             reply = torch.stack(out)
@@ -181,7 +198,9 @@ def run_local(gens: List):
             raise RuntimeError(f"collective mismatch across ranks: {sorted(kinds)}")
         kind = pending[0][0]
         args = [p[1] for p in pending]
-        if kind == "all_gather":
+        if kind == "mark":
+            replies = [None] * world
+        elif kind == "all_gather":
             t = torch.stack(args)
             replies = [t.clone() for _ in range(world)]
         elif kind == "all_reduce_sum":
@@ -304,7 +323,9 @@ def decomposed_step(dec: Decomposition, rank: int, pos: torch.Tensor, species: t
     Returns the total energy (all ranks), the owned atoms' forces and energies, and the total
     virial when asked."""
     n = pos.shape[0]
+    yield from halo_mark("begin")
     plan = yield from halo_exchange(dec, rank, pos, species)
+    yield from halo_mark("end")
     pos_l = torch.cat([pos, plan.ghost_pos.to(pos.dtype)])
     spec_l = torch.cat([species, plan.ghost_species.to(species.dtype)])
     counts = getattr(evaluate, "local_counts", None)
@@ -314,7 +335,9 @@ def decomposed_step(dec: Decomposition, rank: int, pos: torch.Tensor, species: t
     else:
         out = evaluate(pos_l, spec_l, n, dec.local_pbc)
     f = out["forces"]
+    yield from halo_mark("begin")
     forces = yield from return_ghost_forces(plan, f[:n], f[n:])
+    yield from halo_mark("end")
     red = [out["energy"].reshape(1).to(torch.float64)]
     if want_virial:
         red.append(out["virial"].reshape(9).to(torch.float64))
@@ -382,7 +405,9 @@ def layer_exchange_step(dec: Decomposition, rank: int, pos: torch.Tensor, specie
     n = pos.shape[0]
     dev = pos.device
     nint = engine.cfg.num_interaction
+    yield from halo_mark("begin")
     plan = yield from halo_exchange(dec, rank, pos, species)
+    yield from halo_mark("end")
     pos_l = torch.cat([pos, plan.ghost_pos.to(pos.dtype)])
     spec_l = torch.cat([species, plan.ghost_species.to(species.dtype)])
     n_all = int(pos_l.shape[0])
@@ -400,17 +425,23 @@ def layer_exchange_step(dec: Decomposition, rank: int, pos: torch.Tensor, specie
         engine.begin_steps(pos_l, spec_l, batch, cell_t, g, num_local=n, layer_atoms=[n_all] * (nint - 1) + [n])
     for k in range(nint - 1):
         feats = engine.forward_step(k)
+        yield from halo_mark("begin")
         yield from exchange_ghost_rows(plan, feats, n)
+        yield from halo_mark("end")
     engine.forward_step(nint - 1)  # read by the readout only
     energy, atom_e = engine.forward_step(nint)
     out = engine.begin_backward(want_virial=want_virial)
     engine.backward_step(nint)
     for k in range(nint - 1, -1, -1):
         if k < nint - 1:
+            yield from halo_mark("begin")
             yield from return_ghost_rows(plan, engine.feature_buffer(1, k), n)
+            yield from halo_mark("end")
         engine.backward_step(k)
     f = out["forces"]
+    yield from halo_mark("begin")
     forces = yield from return_ghost_forces(plan, f[:n], f[n:])
+    yield from halo_mark("end")
     red = [energy.reshape(1).to(torch.float64)]
     if want_virial:
         red.append(out["virial"].reshape(9).to(torch.float64))
