@@ -627,8 +627,8 @@ int fsc_csr_transpose(const int32_t* row_ptr, const int32_t* src, int64_t num_at
 }
 
 // ---- allocation-free transpose ----------------------------------------------------------
-// For callers that cannot allocate device memory (a CUDA-graph-captured MD step, a host
-// program bound to a fixed memory pool, an FFI binding with no allocator): the scratch lives
+// For callers that cannot allocate device memory (a host program bound to its own fixed
+// memory pool, an FFI binding with no allocator): the scratch lives
 // in a file-scope __device__ array that every GPU loading this library keeps until exit.
 namespace {
 constexpr int64_t kStaticMaxAtoms = 262144;       // rows of the CSR

@@ -165,9 +165,9 @@ int fsc_neighbor_cap(const int32_t* row_ptr, const int32_t* src, const int8_t* s
                      int32_t* out_src, int8_t* out_sidx, int64_t* out_num_edges_host,
                      void* workspace, size_t workspace_bytes, void* stream);
 
-/* Allocation-free transpose, for callers that cannot call cudaMalloc (a CUDA-graph-captured
- * MD step, a host that hands all device memory to a fixed pool, an FFI binding without a
- * device allocator).  No counterpart in the reference.  Same result as fsc_csr_transpose,
+/* Allocation-free transpose, for callers that cannot call cudaMalloc (a host program that
+ * hands all device memory to its own fixed pool, an FFI binding without a device allocator,
+ * a plugin inside another program that owns the device's memory).  No counterpart in the reference.  Same result as fsc_csr_transpose,
  * but its scratch is a file-scope __device__ array of this library (about 19 MiB, held on
  * every GPU that loads the library until exit), so it accepts at most 262,144 atoms and
  * 4,194,304 edges and returns FSC_ERR_CAPACITY beyond that.  It allocates nothing.  The

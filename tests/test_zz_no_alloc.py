@@ -1,8 +1,9 @@
 """Allocation-free CSR transpose (fsc_csr_transpose_static) against the workspace version.
 
-The static entry point exists for callers that cannot allocate device memory, for example an
-MD step captured into a CUDA graph or a host program that gives all device memory to a fixed
-pool: its scratch is a file-scope device array of the library instead of a caller buffer.
+The static entry point exists for callers that cannot allocate device memory, for example a
+host program that gives all device memory to its own fixed pool or an FFI binding without a
+device allocator: its scratch is a file-scope device array of the library instead of a caller
+buffer.
 This file is collected last so that a failure here never hides the other tests.
 """
 
