@@ -10,11 +10,15 @@ reference semantics) + forward + hand-written backward (energy, forces).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
 
 ``--impl reference`` times the reference's own CPU path (its PyTorch modules, installed unmodified
-under baseline/_ref, fp32, all host threads) on a bounded replica of the same workload.  Under torchrun (N > 1) the crystal grows with N (weak scaling, 1,000,000 owned atoms
-per GPU) and is cut into a (2, 1, 1) / (2, 2, 1) / (2, 2, 2) grid of blocks, one per rank: each
-step exchanges a 15 A halo of ghost positions, evaluates the owned atoms' energies and forces
-on the local system, returns the ghost forces to their owners and sums the energy
-(fsctep_b200.domain); the reported value is all owned atoms / the slowest rank's time.
+under baseline/_ref, fp32, all host threads) on a bounded replica of the same workload.  Under
+torchrun (N > 1) the crystal grows with N (weak scaling, 1,000,000 owned atoms per GPU; or
+``--scaling strong``: one fixed crystal) and is cut into a (2, 1, 1) / (2, 2, 1) / (2, 2, 2) grid
+of blocks, one per rank: each step exchanges a one-cutoff (5 A) halo of ghost positions,
+overwrites the ghost feature rows after every interaction layer that a later layer reads (and
+returns their gradients in the reverse pass), returns the ghost forces to their owners and sums
+the energy (fsctep_b200.domain; ``--halo recompute``: a 15 A halo of recomputed ghosts and no
+per-layer exchange); the reported value is all owned atoms / the slowest rank's time, and the
+clock record covers every GPU of the job.
 """
 
 from __future__ import annotations
@@ -151,6 +155,30 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(max(smax)), "reasons": sorted(reasons),
                 "samples": len(sm)}
+
+
+def combine_clocks(summaries):
+    """One clocks record for a job of several GPUs from every rank's ClockSampler.summary():
+    the slowest GPU's median SM clock, the highest max clock, the union of the throttle reasons
+    seen on any GPU, and each rank's median and reasons."""
+    if len(summaries) == 1:
+        return summaries[0]
+    meds = [c.get("sm_mhz") for c in summaries]
+    known = [m for m in meds if m is not None]
+    maxes = [c.get("sm_max_mhz") for c in summaries if c.get("sm_max_mhz") is not None]
+    reasons = sorted({r for c in summaries for r in c.get("reasons", [])})
+    return {"sm_mhz": min(known) if known else None, "sm_max_mhz": max(maxes) if maxes else None,
+            "reasons": reasons, "samples": sum(c.get("samples", 0) for c in summaries),
+            "per_rank": [{"sm_mhz": c.get("sm_mhz"), "reasons": c.get("reasons", [])} for c in summaries],
+            "statistic": "sm_mhz: lowest per-GPU median over the ranks"}
+
+
+def rank_path(path, rank, world):
+    """A clock CSV path of its own for every rank of a multi-GPU run."""
+    if path is None or world <= 1:
+        return path
+    root, ext = os.path.splitext(path)
+    return f"{root}_rank{rank}{ext or '.csv'}"
 
 
 def sparse_cfg(w):
@@ -291,13 +319,18 @@ def timed_steps(args, world, step):
     no stage profiling inside."""
     dev = torch.cuda.current_device() if world == 1 else int(os.environ.get("LOCAL_RANK", 0))
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev, args.clocks_csv) as clk:
+    with ClockSampler(dev, rank_path(args.clocks_csv, int(os.environ.get("RANK", 0)), world)) as clk:
         t0.record()
         for _ in range(args.steps):
             step()
         t1.record()
         torch.cuda.synchronize()
-    return t0.elapsed_time(t1), clk.summary()
+    summary = clk.summary()
+    if world > 1:  # every GPU of the job, not only rank 0's
+        gathered = [None] * world
+        torch.distributed.all_gather_object(gathered, summary)
+        summary = combine_clocks(gathered)
+    return t0.elapsed_time(t1), summary
 
 
 def stage_pass(args, world, step):

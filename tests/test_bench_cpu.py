@@ -81,3 +81,21 @@ def test_fp32_context_uses_the_measured_peak():
     ctx = bench.fp32_context(roof, {"sm_mhz": 1965.0}, measured={"tflops": 80.0, "how": "probe"})
     assert ctx["peak_tflops"] == 80.0 and ctx["frac"] == 0.25 and ctx["peak_source"] == "measured: probe"
     assert ctx["nominal_tflops"] == pytest.approx(148 * 128 * 2 * 1965e6 / 1e12)
+
+
+def test_clock_records_of_several_gpus_combine_conservatively():
+    one = {"sm_mhz": 1950.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"], "samples": 6}
+    assert bench.combine_clocks([one]) is one
+    two = {"sm_mhz": 1792.5, "sm_max_mhz": 1965.0, "reasons": ["hw_slowdown", "sw_power_cap"], "samples": 5}
+    none = {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+    c = bench.combine_clocks([one, two, none])
+    assert c["sm_mhz"] == 1792.5 and c["sm_max_mhz"] == 1965.0
+    assert c["reasons"] == ["hw_slowdown", "no samples", "sw_power_cap"]
+    assert c["samples"] == 11 and [r["sm_mhz"] for r in c["per_rank"]] == [1950.0, 1792.5, None]
+
+
+def test_each_rank_writes_its_own_clock_file():
+    assert bench.rank_path(None, 3, 8) is None
+    assert bench.rank_path("/tmp/c.csv", 0, 1) == "/tmp/c.csv"
+    assert bench.rank_path("/tmp/c.csv", 3, 8) == "/tmp/c_rank3.csv"
+    assert bench.rank_path("/tmp/c", 1, 2) == "/tmp/c_rank1.csv"
