@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(CONV_WARPS * 32, 3) conv2_z_kernel(ConvArgs a,
 #pragma unroll
         for (int k = 0; k < NK; ++k)
 #pragma unroll
-          for (int c = 0; c < CPL; ++c) xd[k][c] = ok ? x[(s * NK + k) * C + lane + 32 * c] : 0.f;
+          for (int c = 0; c < CPL; ++c) xd[k][c] = ok ? __ldcg(x + (s * NK + k) * C + lane + 32 * c) : 0.f;
         return ok;
       };
       float xv[NK][CPL];
@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(CONV_WARPS * 32, 3) conv2_r_kernel(ConvArgs a,
 #pragma unroll
         for (int k = 0; k < NK; ++k)
 #pragma unroll
-          for (int c = 0; c < CPL; ++c) gd[k][c] = on ? G[(d * NK + k) * C + lane + 32 * c] * inv : 0.f;
+          for (int c = 0; c < CPL; ++c) gd[k][c] = on ? __ldcg(G + (d * NK + k) * C + lane + 32 * c) * inv : 0.f;
         return on;
       };
       float gv[NK][CPL];
@@ -358,7 +358,7 @@ __host__ __device__ constexpr int qcount() {
 }
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
                "l"(gmem_src)
                : "memory");
 }
