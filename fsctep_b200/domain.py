@@ -34,6 +34,7 @@ set to a list, :func:`run_dist` records a CUDA event at each mark into it (``hal
 from __future__ import annotations
 
 import itertools
+import time
 from dataclasses import dataclass, field
 from typing import Callable, Dict, List, Optional, Sequence
 
@@ -135,8 +136,95 @@ def halo_mark(which: str):
     yield ("mark", which)
 
 
-def run_dist(gen):
-    """Drive a step generator with torch.distributed collectives (this process = one rank)."""
+class RankFailure(RuntimeError):
+    """Another rank of the decomposition failed, or never arrived at a step: raised by
+    :meth:`StepGuard.begin` before this rank enters the step's first collective."""
+
+
+class StepGuard:
+    """Failure detection between steps through a key-value store shared by the ranks (a
+    ``torch.distributed`` store, e.g. the ``TCPStore`` of the job), independent of the process
+    group whose collectives it protects.
+
+    :meth:`begin` starts a step: the rank adds itself to the step's arrival count and waits until
+    all ``world`` ranks have arrived, a rank has posted a failure, or ``timeout`` seconds pass.  A
+    rank whose step raises posts the reason (:meth:`fail`; :func:`run_dist` does it), so the other
+    ranks learn of it on the host before their next step's first collective instead of waiting in
+    that collective until the process group's own timeout; a rank that stops without posting shows
+    up as a missing arrival.  A rank that fails between two collectives of a step leaves its peers
+    in the collective in flight: the process group's timeout (set it short) ends that one with an
+    error, and the posted reason tells the peers which rank failed and why.  The first failure
+    posted is the one kept.  Rank 0 deletes a step's arrival key once every rank has passed the
+    next step's arrival."""
+
+    def __init__(self, store, rank: int, world: int, timeout: float = 60.0, prefix: str = "fsctep_step_guard",
+                 poll: float = 1e-3):
+        self.store, self.rank, self.world = store, int(rank), int(world)
+        self.timeout, self.prefix, self.poll = float(timeout), prefix, float(poll)
+        self.step = 0
+
+    def _fail_key(self) -> str:
+        return f"{self.prefix}/failed"
+
+    def failure(self) -> Optional[str]:
+        """The failure posted by any rank, or None."""
+        key = self._fail_key()
+        if not self.store.check([key]):
+            return None
+        msg = self.store.get(key)
+        msg = msg.decode() if isinstance(msg, (bytes, bytearray)) else str(msg)
+        return msg or None
+
+    def fail(self, reason: str) -> None:
+        """Post this rank's failure (kept only if no rank posted one before)."""
+        self.store.compare_set(self._fail_key(), "", f"rank {self.rank}: {reason}")
+
+    def begin(self) -> None:
+        """Arrival at the next step; raises RankFailure if a rank failed or did not arrive."""
+        msg = self.failure()
+        if msg:
+            raise RankFailure(msg)
+        self.step += 1
+        key = f"{self.prefix}/arrived/{self.step}"
+        self.store.add(key, 1)
+        t0 = time.monotonic()
+        while True:
+            n = self.store.add(key, 0)
+            if n >= self.world:
+                break
+            msg = self.failure()
+            if msg:
+                raise RankFailure(msg)
+            if time.monotonic() - t0 > self.timeout:
+                msg = (f"step {self.step}: {self.world - n} of {self.world} ranks did not arrive within "
+                       f"{self.timeout:g} s")
+                self.fail(msg)
+                raise RankFailure(self.failure() or msg)
+            time.sleep(self.poll)
+        if self.rank == 0 and self.step > 1:
+            self.store.delete_key(f"{self.prefix}/arrived/{self.step - 1}")
+
+
+def run_dist(gen, guard: Optional[StepGuard] = None):
+    """Drive a step generator with torch.distributed collectives (this process = one rank).
+    With a :class:`StepGuard`, the step starts with its arrival check and an exception raised
+    while the step runs is posted to the other ranks before it propagates."""
+    if guard is None:
+        return _serve_dist(gen)
+    try:
+        guard.begin()
+    except BaseException:
+        gen.close()
+        raise
+    try:
+        return _serve_dist(gen)
+    except BaseException as e:
+        if not isinstance(e, RankFailure):
+            guard.fail(f"{type(e).__name__}: {e}")
+        raise
+
+
+def _serve_dist(gen):
     import torch.distributed as dist
 
     world = dist.get_world_size()
