@@ -123,6 +123,7 @@ _PROTOS = {
     "fsc_ictd_set_gemm_path": (None, [C.c_int]),
     "fsc_ictd_set_conv2_path": (None, [C.c_int]),
     "fsc_fp32_fma_probe": (C.c_int, [C.c_int, C.c_int, C.c_int, P, C.POINTER(C.c_double), P]),
+    "fsc_bounded_wait_probe": (C.c_int, [C.c_int, C.c_int, P, P]),
     "fsc_gemm_tc_plan": (C.c_int, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "fsc_profile_enable": (None, [C.c_int]),
     "fsc_profile_read": (C.c_int, [C.POINTER(C.c_char_p), C.POINTER(C.c_float), C.c_int]),

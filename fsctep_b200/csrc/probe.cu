@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace fsc {
 namespace {
@@ -41,6 +42,18 @@ __global__ void __launch_bounds__(PROBE_THREADS) fma_probe_kernel(float* __restr
   if (s == 12345.678f) out[blockIdx.x * blockDim.x + threadIdx.x] = s;  // keeps the chains live
 }
 
+// One mbarrier of arrival count 1 that nothing arrives at; thread 0 waits for phase `parity` with
+// the bounded wait of the tensor-core kernels (tc::mbar_wait), which records `where` in *err when
+// it gives up.
+__global__ void bounded_wait_probe_kernel(uint32_t parity, int where, int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    tc::fence_mbar_init();
+    tc::mbar_wait(&bar, parity, err, where);
+  }
+}
+
 }  // namespace
 }  // namespace fsc
 
@@ -55,4 +68,11 @@ extern "C" int fsc_fp32_fma_probe(int packed, int blocks, int iters, float* out,
     fma_probe_kernel<false><<<blocks, PROBE_THREADS, 0, st>>>(out, iters, 0.999f, 1e-4f);
   *flops = 2.0 * (packed ? 2.0 : 1.0) * PROBE_CHAINS * 16.0 * (double)iters * (double)blocks * PROBE_THREADS;
   return check_launch("fma_probe_kernel");
+}
+
+extern "C" int fsc_bounded_wait_probe(int parity, int where, int* err_dev, void* stream) {
+  using namespace fsc;
+  FSC_REQUIRE(err_dev && (parity == 0 || parity == 1) && where != 0, "fsc_bounded_wait_probe: bad arguments");
+  bounded_wait_probe_kernel<<<1, 32, 0, as_stream(stream)>>>((uint32_t)parity, where, err_dev);
+  return check_launch("bounded_wait_probe_kernel");
 }

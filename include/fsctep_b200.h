@@ -48,6 +48,14 @@ int fsc_has_cuda(void);
  * blocks * 256 floats (written only to keep the chains live).  No reference counterpart: the
  * measured denominator of the CUDA-core kernels' FP32 roofline. */
 int fsc_fp32_fma_probe(int packed, int blocks, int iters, float* out, double* flops, void* stream);
+/* Bounded-wait check: one thread of one block runs the mbarrier wait that every tensor-core
+ * kernel of this library uses on a fresh barrier of arrival count 1 that nothing arrives at,
+ * waiting for phase `parity`.  Parity 0 is never completed: the wait gives up after its limit
+ * (about 2e9 SM clock cycles, ~1 s), writes `where` to *err_dev (a device int, if it was 0) and
+ * the kernel returns; parity 1 counts as the completed previous phase and returns at once.  No
+ * reference counterpart: it shows that a stalled pipeline ends with an error status that the host
+ * reads, leaving the context usable. */
+int fsc_bounded_wait_probe(int parity, int where, int* err_dev, void* stream);
 
 /* ---- `_C_ictd_tp` operator family (csrc/ictd_tp.cpp:137-497) -------------
  * Shapes follow the reference TORCH_CHECKs (csrc/ictd_tp.cpp:78-108):
